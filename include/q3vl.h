@@ -1,0 +1,157 @@
+/*
+ * q3vl.h -- C ABI of the B200 (sm_100a) Qwen3-VL tensor-parallel decoder path.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * densely packed row-major data unless a stride argument says otherwise.
+ * Every call is asynchronous on the given stream (a cudaStream_t passed as
+ * void*; NULL means the legacy default stream), never throws, and returns an
+ * int status (Q3_OK on success).  q3_last_error() gives the reason for the
+ * last non-zero status on the calling host thread.
+ *
+ * The reference implements this path in Python (PyTorch eager + NKI); each
+ * declaration names the reference function it replaces as file:line within
+ * the yahavb/qwen3-vl project.  Weights follow the reference convention of
+ * the public Python API ([in, out], x @ W) at the module level; at this ABI
+ * level they are stored [out, in] (K-major) so the tensor-core loads read
+ * contiguous K.
+ */
+#ifndef Q3VL_H_
+#define Q3VL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q3_API __attribute__((visibility("default")))
+#else
+#define Q3_API
+#endif
+
+typedef void* q3_stream_t; /* cudaStream_t */
+
+enum q3_status {
+  Q3_OK = 0,
+  Q3_ERR_INVALID = 1,     /* bad shape, pointer alignment or argument     */
+  Q3_ERR_UNSUPPORTED = 2, /* valid request this build does not implement  */
+  Q3_ERR_CUDA = 3,        /* CUDA runtime/driver error                    */
+  Q3_ERR_TIMEOUT = 4,     /* a bounded in-kernel wait gave up             */
+  Q3_ERR_COMM = 5         /* peer setup / exchange failure                */
+};
+
+enum q3_dtype { Q3_F32 = 0, Q3_BF16 = 1 };
+
+enum q3_epilogue {
+  Q3_EPI_NONE = 0,     /* C = A W^T                                          */
+  Q3_EPI_RESIDUAL = 1, /* C = bf16(R + bf16(A W^T)); R = aux [M,N]           */
+  Q3_EPI_SWIGLU = 2    /* W rows interleaved gate/up in blocks of 128;
+                          C[M, N/2] = silu(gate) * up                          */
+};
+
+/* ---- library ---------------------------------------------------------- */
+Q3_API int q3_version(void);
+Q3_API const char* q3_last_error(void);
+/* Reads (and with clear!=0 resets) the device error word that kernels set
+ * when a bounded wait times out; 0 means no error was recorded. */
+Q3_API int q3_device_error(int clear);
+
+/* ---- a1: RMSNorm -------------------------------------------------------
+ * Replaces RMSNorm.forward (model_fused.py:37-40; model.py:44-47) and the
+ * inlined norms of AttentionBlock (model_fused.py:97-100) and MLPBlock
+ * (model_fused.py:159-162).  y = bf16(bf16(h * rsqrt(mean(h^2)+eps)) * w).
+ * If `add` is non-NULL, h = bf16(x + add) (the residual add of
+ * model_fused.py:269/275) and h is written to `h_out` when that is non-NULL;
+ * otherwise h = x.  x, add, h_out, y: bf16 [rows, hidden]; w: bf16 [hidden]. */
+Q3_API int q3_rmsnorm(const void* x, const void* add, void* h_out, const void* w, void* y, int64_t rows,
+               int64_t hidden, float eps, q3_stream_t stream);
+
+/* ---- a9: standalone RoPE -----------------------------------------------
+ * Replaces qwen3_rope (kernels/rope.py:24-96).  x bf16 [seq, heads, head_dim];
+ * cos_sin f32 [seq, head_dim] (cos in [0, D/2), sin in [D/2, D));
+ * out = x*cat(cos,cos) + rotate_half(x)*cat(sin,sin), fp32 math, bf16 out. */
+Q3_API int q3_rope(const void* x, const float* cos_sin, void* out, int64_t seq, int heads, int head_dim,
+            q3_stream_t stream);
+
+/* ---- a4: interleaved M-RoPE angle tables --------------------------------
+ * Replaces Qwen3VLTextRotaryEmbedding.forward + apply_interleaved_mrope
+ * (transformers 5.5.0 modeling_qwen3_vl.py:352-386).  pos int64 [3, n_tok]
+ * (t, h, w rows); inv_freq f32 [head_dim/2]; frequency j takes axis h when
+ * j%3==1 and j<3*sec_h, axis w when j%3==2 and j<3*sec_w, else t.
+ * cos_out/sin_out f32 [n_tok, head_dim/2]. */
+Q3_API int q3_mrope_cos_sin(const int64_t* pos, const float* inv_freq, int64_t n_tok, int head_dim,
+                     int sec_h, int sec_w, float* cos_out, float* sin_out, q3_stream_t stream);
+
+/* ---- a3 epilogue + a5: per-head QK-RMSNorm, RoPE, KV-cache write ---------
+ * Replaces AttentionBlock.forward after the QKV matmul (model_fused.py:107-129)
+ * and the cache slice assignment (model_fused.py:244-246).
+ * qkv bf16 [B*S, (Hq+2*Hkv)*D] laid out [q | k | v] per token.
+ * RoPE row for token (b, s): cs + (cs_use_pos*pos + cs_offset + b*cs_stride_b
+ * + s) * D/2, where pos = *pos_dev if pos_dev != NULL else start_pos (the
+ * cache position); cs dtype = cs_dtype (bf16 tables as RotaryEmbedding builds
+ * them, or f32 M-RoPE rows).  cs_offset shifts text positions after an image
+ * (the M-RoPE rope delta) without moving the cache position.
+ * Outputs (each may be NULL): q_out bf16 [B, Hq, S, D]; k_out, v_out bf16
+ * [B, Hkv, S, D]; k_cache, v_cache bf16 [B, Hkv, max_seq, D] written at
+ * positions pos..pos+S-1. */
+Q3_API int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
+                     const void* sin, int cs_dtype, int cs_use_pos, int64_t cs_offset,
+                     int64_t cs_stride_b, void* q_out, void* k_out, void* v_out, void* k_cache, void* v_cache, int B,
+                     int S, int Hq, int Hkv, int head_dim, int64_t start_pos,
+                     const int32_t* pos_dev, int64_t max_seq, float eps, q3_stream_t stream);
+
+/* ---- a6/a8: GQA decode attention (one query token) -----------------------
+ * Replaces the S=1 case of the eager attention in forward_layer
+ * (model_fused.py:248-262) and the unfinished decode_attention_simple
+ * (kernels/decode_attention.py:56-134).  q [B, Hq, D]; caches [B, Hkv,
+ * max_seq, D]; out [B, Hq, D]; all of dtype `dtype` (Q3_F32 or Q3_BF16).
+ * Attends to cache positions [0, kv_len) where kv_len = *kv_len_dev if that
+ * is non-NULL, else kv_len; head h reads KV head h / (Hq/Hkv).  Split-K over
+ * SMs: workspace must hold q3_attn_decode_workspace_bytes(...) bytes. */
+Q3_API size_t q3_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int head_dim, int64_t max_kv_len);
+Q3_API int q3_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
+                   int Hq, int Hkv, int head_dim, int64_t kv_len, const int32_t* kv_len_dev,
+                   int64_t max_seq, float scale, int dtype, void* workspace,
+                   size_t workspace_bytes, q3_stream_t stream);
+
+/* ---- a6/a7: causal GQA prefill attention ---------------------------------
+ * Replaces the S>1 eager attention of forward_layer (model_fused.py:248-262)
+ * and prefill_gqa_flash_attention (kernels/prefill_attention.py:28-149).
+ * bf16 throughout; head_dim 128.  Element (b, h, s, d) of q/k/v/out lives at
+ * base + b*stride_b + h*stride_h + s*stride_s + d.  Query row s has absolute
+ * position start_pos + s and (when causal) attends to keys 0..start_pos+s;
+ * keys 0..start_pos+S-1 must be present in k/v. */
+Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* out, int B, int Hq,
+                    int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
+                    const int64_t* q_strides, const int64_t* kv_strides, const int64_t* o_strides,
+                    q3_stream_t stream);
+
+/* ---- a3/a10/a11: bf16 GEMM with fused epilogues ---------------------------
+ * Replaces the projections h @ Wqkv (model_fused.py:103), x @ Wo (:141),
+ * h @ Wgate_up + SiLU*up (:165-169), h @ Wdown (:172) and lm_head (:183).
+ * A bf16 [M, K]; W bf16 [N, K] (K-major); C bf16 [M, N] (or [M, N/2] for
+ * Q3_EPI_SWIGLU); aux = residual R [M, N] for Q3_EPI_RESIDUAL.  M <= 16 runs
+ * the HBM-streaming decode kernel, larger M the tcgen05/TMEM kernel. */
+Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
+            const void* aux, q3_stream_t stream);
+
+/* ---- a13: embedding gather and greedy argmax -----------------------------
+ * Replaces embed_tokens(input_ids) (model_fused.py:281) and
+ * logits.argmax(-1) (model_fused.py:310,320).  ids int64 [n]; table bf16
+ * [vocab, hidden]; out bf16 [n, hidden].  Out-of-range ids are an error
+ * recorded in the device error word and produce zero rows. */
+Q3_API int q3_embed(const int64_t* ids, const void* table, void* out, int64_t n, int64_t hidden,
+             int64_t vocab, q3_stream_t stream);
+/* out = bf16(a + b) elementwise over n bf16 values (n % 8 == 0): the residual
+ * add `residual + mlp_out` of forward_layer (model_fused.py:275). */
+Q3_API int q3_add(const void* a, const void* b, void* out, int64_t n, q3_stream_t stream);
+/* Row-wise argmax of bf16 logits [rows, V] (first index on ties), int64 out. */
+Q3_API int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* out_idx, q3_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q3VL_H_ */

@@ -1,0 +1,138 @@
+// a13: embedding gather (model_fused.py:281) and greedy argmax
+// (model_fused.py:310,320).  Both are HBM-bound copies/scans with 16-byte loads.
+#include <float.h>
+
+#include "common.cuh"
+
+namespace q3 {
+
+__global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                             __nv_bfloat16* __restrict__ out, int64_t n, int64_t hidden,
+                             int64_t vocab, int* err) {
+  const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (tok >= n) return;
+  const int64_t id = ids[tok];
+  uint4* dst = reinterpret_cast<uint4*>(out + tok * hidden);
+  const int64_t nvec = hidden >> 3;
+  if (id < 0 || id >= vocab) {
+    if (lane == 0 && err) atomicCAS(err, 0, 0x201);
+    for (int64_t v = lane; v < nvec; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * hidden);
+  for (int64_t v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
+}
+
+// One CTA per row; ties resolve to the lowest index like torch.argmax.
+__global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                     int64_t V, int64_t* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* x = logits + row * V;
+  float best = -INFINITY;
+  int64_t bi = INT64_MAX;
+  const int64_t nvec = V >> 3;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    const uint4 u = __ldg(xv + v);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(w[i]);
+      const int64_t j = v * 8 + 2 * i;
+      if (f.x > best) { best = f.x; bi = j; }
+      if (f.y > best) { best = f.y; bi = j + 1; }
+    }
+  }
+  for (int64_t j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {
+    const float f = bf2f(x[j]);
+    if (f > best) { best = f; bi = j; }
+  }
+  // warp then block reduction of (best, index)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+  }
+  __shared__ float sb[16];
+  __shared__ int64_t si[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sb[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : INT64_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) out[row] = (bi == INT64_MAX) ? 0 : bi;
+  }
+}
+
+// out = bf16(a + b), the bf16 residual add of model_fused.py:269/275.
+__global__ void add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                           uint4* __restrict__ out, int64_t nvec) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 x = a[i], y = b[i];
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fx = unpack_bf16x2(xs[j]), fy = unpack_bf16x2(ys[j]);
+      o[j] = pack_bf16x2(fx.x + fy.x, fx.y + fy.y);
+    }
+    out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+}  // namespace q3
+
+extern "C" int q3_add(const void* a, const void* b, void* out, int64_t n, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(a && b && out, "q3_add: null pointer");
+  Q3_REQUIRE(n >= 0 && n % 8 == 0, "q3_add: n=%lld must be a multiple of 8", (long long)n);
+  Q3_REQUIRE(aligned(a, 16) && aligned(b, 16) && aligned(out, 16), "q3_add: misaligned");
+  if (n == 0) return Q3_OK;
+  const int64_t nvec = n / 8;
+  int64_t blocks = (nvec + 255) / 256;
+  const int64_t cap = (int64_t)num_sms() * 8;
+  if (blocks > cap) blocks = cap;
+  add_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      (const uint4*)a, (const uint4*)b, (uint4*)out, nvec);
+  Q3_LAUNCH_CHECK();
+  return Q3_OK;
+}
+
+extern "C" int q3_embed(const int64_t* ids, const void* table, void* out, int64_t n,
+                        int64_t hidden, int64_t vocab, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(ids && table && out, "q3_embed: null pointer");
+  Q3_REQUIRE(n >= 0 && hidden > 0 && hidden % 8 == 0 && vocab > 0, "q3_embed: bad shape");
+  Q3_REQUIRE(aligned(table, 16) && aligned(out, 16) && aligned(ids, 8), "q3_embed: misaligned");
+  if (n == 0) return Q3_OK;
+  embed_kernel<<<(unsigned)((n + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
+      ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, n, hidden, vocab,
+      device_error_word());
+  Q3_LAUNCH_CHECK();
+  return Q3_OK;
+}
+
+extern "C" int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* out_idx,
+                         q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(logits && out_idx, "q3_argmax: null pointer");
+  Q3_REQUIRE(rows >= 0 && V > 0 && V % 8 == 0, "q3_argmax: V=%lld must be a multiple of 8",
+             (long long)V);
+  Q3_REQUIRE(aligned(logits, 16), "q3_argmax: misaligned logits");
+  if (rows == 0) return Q3_OK;
+  argmax_kernel<<<(unsigned)rows, 512, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)logits, V,
+                                                                  out_idx);
+  Q3_LAUNCH_CHECK();
+  return Q3_OK;
+}

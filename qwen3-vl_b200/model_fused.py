@@ -1,0 +1,522 @@
+"""Qwen3-VL-8B text decoder on B200 -- drop-in for the reference model_fused.py.
+
+Same module/class names and signatures as the reference
+(model_fused.py:31-362): RMSNorm, RotaryEmbedding, AttentionBlock,
+OProjection, MLPBlock, FusedLinear, DecoderLayer, Qwen3VLDecoderFused.  Weights
+arrive in the reference's [in, out] convention; each module keeps one K-major
+[out, in] copy for the kernels and exposes the [in, out] view under the
+reference's attribute name.  Every op runs on the q3vl sm_100a kernels
+(q3vl.ops); CPU tensors raise instead of falling back.
+
+Per layer (forward_layer) the kernels are:
+  rmsnorm -> QKV GEMM -> QK-norm+RoPE+KV-write -> prefill/decode attention ->
+  o_proj GEMM (+residual) -> [TP all-reduce + fused add+rmsnorm | rmsnorm] ->
+  gate_up GEMM with SwiGLU epilogue -> down GEMM (+residual) [-> all-reduce].
+Decode runs as a captured CUDA graph per (batch, KV bucket) with the token
+and position kept on the device (no per-token host sync).
+"""
+from __future__ import annotations
+
+import math
+import os
+import time
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from q3vl import layout, ops
+
+KV_BUCKETS = (2048, 4096, 8192)
+
+
+def _param(t: torch.Tensor) -> nn.Parameter:
+    return nn.Parameter(t, requires_grad=False)
+
+
+class RMSNorm(nn.Module):
+    """model_fused.py:31-40."""
+
+    def __init__(self, weight, eps=1e-6):
+        super().__init__()
+        self.weight = _param(weight)
+        self.eps = eps
+
+    def forward(self, x):
+        return ops.rmsnorm(x.contiguous(), self.weight, self.eps)
+
+
+class RotaryEmbedding:
+    """model_fused.py:43-58: bf16 cos/sin tables built on the host exactly as the
+    reference builds them; device copies stay resident, so `get` slices HBM
+    instead of copying from the host every layer."""
+
+    def __init__(self, head_dim, max_seq_len=8192, base=1000000.0):
+        inv_freq = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+        t = torch.arange(max_seq_len, dtype=torch.float32)
+        freqs = torch.outer(t, inv_freq)
+        self.cos_cached = freqs.cos().to(torch.bfloat16)
+        self.sin_cached = freqs.sin().to(torch.bfloat16)
+        self.inv_freq = inv_freq
+        self.head_dim = head_dim
+        self.max_seq_len = max_seq_len
+        self.base = base
+        self._dev = {}
+
+    def tables(self, device):
+        key = str(torch.device(device))
+        if key not in self._dev:
+            self._dev[key] = (self.cos_cached.to(device), self.sin_cached.to(device),
+                              self.inv_freq.to(device))
+        return self._dev[key]
+
+    def get(self, seq_len, offset=0, device=None):
+        if device is None:
+            return (self.cos_cached[offset:offset + seq_len],
+                    self.sin_cached[offset:offset + seq_len])
+        cos, sin, _ = self.tables(device)
+        return cos[offset:offset + seq_len], sin[offset:offset + seq_len]
+
+
+class AttentionBlock(nn.Module):
+    """model_fused.py:61-131: norm -> QKV -> per-head QK-norm -> RoPE."""
+
+    def __init__(self, qkv_weight, qkv_bias, o_proj_weight, input_norm_weight, q_norm_weight,
+                 k_norm_weight, num_q_heads, num_kv_heads, head_dim, eps=1e-6):
+        super().__init__()
+        if head_dim != ops.HEAD_DIM:
+            raise ValueError(f"head_dim {head_dim} unsupported (kernels are built for 128)")
+        self.qkv_weight_km = _param(layout.k_major(qkv_weight))
+        self.qkv_bias = _param(qkv_bias) if qkv_bias is not None else None
+        self.input_norm_weight = _param(input_norm_weight)
+        self.q_norm_weight = _param(q_norm_weight)
+        self.k_norm_weight = _param(k_norm_weight)
+        self.o_proj_weight_km = _param(layout.k_major(o_proj_weight))
+        self.num_q_heads = num_q_heads
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.q_dim = num_q_heads * head_dim
+        self.kv_dim = num_kv_heads * head_dim
+        self.eps = eps
+
+    @property
+    def qkv_weight(self):
+        return self.qkv_weight_km.t()
+
+    @property
+    def o_proj_weight(self):
+        return self.o_proj_weight_km.t()
+
+    def qkv(self, h2d: torch.Tensor) -> torch.Tensor:
+        out = ops.gemm(h2d, self.qkv_weight_km)
+        if self.qkv_bias is not None:
+            out = ops.add(out, self.qkv_bias.expand_as(out).contiguous())
+        return out
+
+    def forward(self, hidden, cos, sin):
+        """hidden [B, S, H]; cos/sin [S, D/2] -> q [B,Hq,S,D], k/v [B,Hkv,S,D]."""
+        B, S, H = hidden.shape
+        h = ops.rmsnorm(hidden.reshape(B * S, H).contiguous(), self.input_norm_weight, self.eps)
+        qkv = self.qkv(h)
+        return ops.qkv_norm_rope(qkv, self.q_norm_weight, self.k_norm_weight,
+                                 cos.contiguous(), sin.contiguous(), B=B, S=S,
+                                 Hq=self.num_q_heads, Hkv=self.num_kv_heads, cs_use_pos=False,
+                                 want_kv=True, eps=self.eps)
+
+
+class OProjection(nn.Module):
+    """model_fused.py:134-141."""
+
+    def __init__(self, weight):
+        super().__init__()
+        self.weight_km = _param(layout.k_major(weight))
+
+    @property
+    def weight(self):
+        return self.weight_km.t()
+
+    def forward(self, x):
+        return ops.gemm(x.contiguous(), self.weight_km)
+
+
+class MLPBlock(nn.Module):
+    """model_fused.py:144-172: norm -> gate_up -> SiLU*up -> down (partial sum)."""
+
+    def __init__(self, gate_up_weight, down_weight, post_norm_weight, eps=1e-6):
+        super().__init__()
+        self.gate_up_weight_il = _param(layout.gate_up_from_fused(gate_up_weight))
+        self.down_weight_km = _param(layout.k_major(down_weight))
+        self.post_norm_weight = _param(post_norm_weight)
+        self.eps = eps
+
+    @property
+    def gate_up_weight(self):
+        return layout.fused_from_gate_up(self.gate_up_weight_il)
+
+    @property
+    def down_weight(self):
+        return self.down_weight_km.t()
+
+    def forward(self, hidden):
+        shp = hidden.shape
+        x = hidden.reshape(-1, shp[-1]).contiguous()
+        h = ops.rmsnorm(x, self.post_norm_weight, self.eps)
+        act = ops.gemm(h, self.gate_up_weight_il, "swiglu")
+        return ops.gemm(act, self.down_weight_km).view(*shp[:-1], -1)
+
+
+class FusedLinear(nn.Module):
+    """model_fused.py:175-186 (lm_head)."""
+
+    def __init__(self, weight, bias=None):
+        super().__init__()
+        self.weight_km = _param(layout.k_major(weight))
+        self.bias = _param(bias) if bias is not None else None
+
+    @property
+    def weight(self):
+        return self.weight_km.t()
+
+    def forward(self, x):
+        shp = x.shape
+        out = ops.gemm(x.reshape(-1, shp[-1]).contiguous(), self.weight_km)
+        if self.bias is not None:
+            out = ops.add(out, self.bias.expand_as(out).contiguous())
+        return out.view(*shp[:-1], -1)
+
+
+class DecoderLayer:
+    """model_fused.py:189-194."""
+
+    def __init__(self, attn_block, o_proj, mlp_block):
+        self.attn_block = attn_block
+        self.o_proj = o_proj
+        self.mlp_block = mlp_block
+
+
+class _DecodeGraph:
+    """One captured decode step for a fixed batch, KV bucket and cache storage."""
+
+    def __init__(self, graph, tok, pos, kv_len, logits):
+        self.graph, self.tok, self.pos, self.kv_len, self.logits = graph, tok, pos, kv_len, logits
+
+
+class Qwen3VLDecoderFused:
+    """model_fused.py:197-362 on the q3vl kernels."""
+
+    def __init__(self, layers, lm_head, embed_tokens, final_norm, rotary, tp_size, num_q_heads,
+                 num_kv_heads, head_dim, max_seq_len, device):
+        self.layers = layers
+        self.lm_head = lm_head
+        self.embed_tokens = embed_tokens
+        self.final_norm = final_norm
+        self.rotary = rotary
+        self.tp_size = tp_size
+        self.num_q_heads = num_q_heads
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.max_seq_len = max_seq_len
+        self.device = torch.device(device)
+        self.num_layers = len(layers)
+        self.q_dim = num_q_heads * head_dim
+        self.scale = 1.0 / math.sqrt(head_dim)
+        self.comm = None            # optional in-kernel all-reduce (q3vl.comm)
+        self._graphs = {}
+        self._kv_pool = {}
+        self.use_graphs = os.environ.get("Q3VL_DECODE_GRAPHS", "1") != "0"
+
+    # ------------------------------------------------------------------ cache
+    def init_kv_cache(self, batch_size=1):
+        """model_fused.py:224-232: per layer (k, v) [B, Hkv, max_seq_len, D] bf16."""
+        cache = []
+        for _ in range(self.num_layers):
+            k = torch.zeros(batch_size, self.num_kv_heads, self.max_seq_len, self.head_dim,
+                            dtype=torch.bfloat16, device=self.device)
+            cache.append((k, torch.zeros_like(k)))
+        return cache
+
+    # ----------------------------------------------------------------- comm
+    def _all_reduce(self, t: torch.Tensor):
+        if self.tp_size > 1:
+            if self.comm is not None:
+                self.comm.all_reduce(t)
+            else:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM)
+
+    @property
+    def _eps(self):
+        return self.layers[0].attn_block.eps
+
+    # ----------------------------------------------------------------- layer
+    def _layer(self, x, pend, layer_idx, kv_cache, start_pos, S, B, rope=None, pos_dev=None,
+               kv_len_dev=None, kv_bound=None, rope_delta=0):
+        """One decoder layer on the residual stream x [T, H].  `pend` is a partial
+        sum still to be added to x (TP>1 keeps the add fused with the next norm).
+        Returns (x, pend) in the same convention."""
+        L = self.layers[layer_idx]
+        ab, mlp = L.attn_block, L.mlp_block
+        H = x.shape[-1]
+        T = B * S
+        if pend is not None:
+            xn = torch.empty_like(x)
+            h = ops.rmsnorm(pend, ab.input_norm_weight, ab.eps, add=x, h_out=xn)
+            x = xn
+        else:
+            h = ops.rmsnorm(x, ab.input_norm_weight, ab.eps)
+        qkv = ab.qkv(h)
+        kc, vc = kv_cache[layer_idx]
+        if rope is None:
+            cos, sin, _ = self.rotary.tables(self.device)
+            cs_use_pos, cs_stride_b, cs_offset = True, 0, rope_delta
+        else:
+            cos, sin = rope
+            cs_use_pos, cs_stride_b, cs_offset = False, S, 0
+        q, _, _ = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B, S=S,
+                                    Hq=ab.num_q_heads, Hkv=ab.num_kv_heads, start_pos=start_pos,
+                                    pos_dev=pos_dev, cs_use_pos=cs_use_pos, cs_offset=cs_offset,
+                                    cs_stride_b=cs_stride_b, k_cache=kc, v_cache=vc, eps=ab.eps)
+        if S == 1:
+            bound = kv_bound if kv_bound is not None else start_pos + 1
+            attn = ops.attn_decode(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
+                                   kv_len=bound, kv_len_dev=kv_len_dev, scale=self.scale)
+            attn = attn.view(T, ab.q_dim)
+        else:
+            attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,
+                               device=x.device)
+            ops.attn_prefill(q, kc, vc, start_pos=start_pos, causal=True, scale=self.scale,
+                             out=attn.transpose(1, 2))
+            attn = attn.view(T, ab.q_dim)
+        if self.tp_size == 1:
+            x2 = ops.gemm(attn, L.o_proj.weight_km, "residual", residual=x)
+            h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
+        else:
+            part = ops.gemm(attn, L.o_proj.weight_km)
+            self._all_reduce(part)
+            x2 = torch.empty_like(x)
+            h2 = ops.rmsnorm(part, mlp.post_norm_weight, mlp.eps, add=x, h_out=x2)
+        act = ops.gemm(h2, mlp.gate_up_weight_il, "swiglu")
+        if self.tp_size == 1:
+            return ops.gemm(act, mlp.down_weight_km, "residual", residual=x2), None
+        part2 = ops.gemm(act, mlp.down_weight_km)
+        self._all_reduce(part2)
+        return x2, part2
+
+    def forward_layer(self, hidden, layer_idx, kv_cache, start_pos, seq_len, position_ids=None):
+        """model_fused.py:234-277.  position_ids [3, B, S] switches to M-RoPE."""
+        B = hidden.shape[0]
+        H = hidden.shape[-1]
+        x = hidden.reshape(B * seq_len, H).contiguous()
+        rope = self._mrope(position_ids) if position_ids is not None else None
+        x, pend = self._layer(x, None, layer_idx, kv_cache, start_pos, seq_len, B, rope=rope)
+        if pend is not None:
+            x = ops.add(x, pend)
+        return x.view(B, seq_len, H)
+
+    def _mrope(self, position_ids):
+        _, _, inv = self.rotary.tables(self.device)
+        pos = position_ids.to(self.device, torch.int64)
+        return ops.mrope_cos_sin(pos, inv)
+
+    # --------------------------------------------------------------- logits
+    def _logits(self, x, pend, B, S, logits_out=None):
+        H = x.shape[-1]
+        if S > 1:
+            x = x.view(B, S, H)[:, -1].contiguous()
+            pend = pend.view(B, S, H)[:, -1].contiguous() if pend is not None else None
+        if pend is not None:
+            h = ops.rmsnorm(pend, self.final_norm.weight, self.final_norm.eps, add=x)
+        else:
+            h = ops.rmsnorm(x, self.final_norm.weight, self.final_norm.eps)
+        local = ops.gemm(h, self.lm_head.weight_km)           # [B, V/tp]
+        if self.tp_size == 1:
+            return local.view(B, 1, -1)
+        gathered = torch.empty(self.tp_size, B, local.shape[-1], dtype=local.dtype,
+                               device=local.device)
+        dist.all_gather_into_tensor(gathered, local)
+        return gathered.permute(1, 0, 2).reshape(B, 1, -1)
+
+    def _embed(self, input_ids):
+        table = self.embed_tokens.weight if hasattr(self.embed_tokens, "weight") \
+            else self.embed_tokens
+        return ops.embed(input_ids.to(self.device), table)
+
+    def _run(self, hidden2d, B, S, start_pos, kv_cache, rope=None, deepstack=None,
+             visual_mask=None, pos_dev=None, kv_len_dev=None, kv_bound=None, rope_delta=0):
+        x, pend = hidden2d, None
+        for i in range(self.num_layers):
+            x, pend = self._layer(x, pend, i, kv_cache, start_pos, S, B, rope=rope,
+                                  pos_dev=pos_dev, kv_len_dev=kv_len_dev, kv_bound=kv_bound,
+                                  rope_delta=rope_delta)
+            if deepstack is not None and i < len(deepstack):
+                if pend is not None:
+                    x = ops.add(x, pend)
+                    pend = None
+                x = self._deepstack_add(x, B, S, deepstack[i], visual_mask)
+        return x, pend
+
+    def _deepstack_add(self, x, B, S, feats, visual_mask):
+        """model_fused.py:339-341 (batch row 0, as the reference)."""
+        H = x.shape[-1]
+        xv = x.view(B, S, H)
+        idx = torch.nonzero(visual_mask.to(self.device).reshape(-1)).flatten()
+        rows = xv[0].index_select(0, idx).contiguous()
+        upd = ops.add(rows, feats.to(self.device, torch.bfloat16).contiguous())
+        xv[0].index_copy_(0, idx, upd)
+        return x
+
+    def forward(self, input_ids, start_pos, kv_cache, position_ids=None):
+        """model_fused.py:279-293 -> logits [B, 1, V]."""
+        B, S = input_ids.shape
+        x = self._embed(input_ids).view(B * S, -1)
+        rope = self._mrope(position_ids) if position_ids is not None else None
+        x, pend = self._run(x, B, S, start_pos, kv_cache, rope=rope)
+        return self._logits(x, pend, B, S)
+
+    def prefill(self, input_ids, kv_cache):
+        return self.forward(input_ids, start_pos=0, kv_cache=kv_cache)
+
+    def decode_step(self, token_id, pos, kv_cache):
+        return self.forward(token_id.view(-1, 1), start_pos=pos, kv_cache=kv_cache)
+
+    # ------------------------------------------------------------- generate
+    def _bucket(self, need: int) -> int:
+        for b in KV_BUCKETS:
+            if need <= b and b <= self.max_seq_len:
+                return b
+        return self.max_seq_len
+
+    def _capture_decode(self, B, kv_cache, bucket, rope_delta=0):
+        """Capture one decode step.  Must run before the prefill that fills this
+        cache: the warm-up step writes KV slot 0, which the prefill overwrites."""
+        key = (B, bucket, kv_cache[0][0].data_ptr(), rope_delta)
+        g = self._graphs.get(key)
+        if g is not None:
+            return g
+        dev = self.device
+        tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        kv_len = torch.ones(1, dtype=torch.int32, device=dev)
+        ops.decode_workspace(B, self.num_q_heads, self.num_kv_heads, dev)
+
+        def step():
+            x = self._embed(tok.view(B, 1)).view(B, -1)
+            x, pend = self._run(x, B, 1, 0, kv_cache, pos_dev=pos, kv_len_dev=kv_len,
+                                kv_bound=bucket, rope_delta=rope_delta)
+            return self._logits(x, pend, B, 1)
+
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            step()                                  # warm up allocator + tensor maps
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = step()
+            ops.argmax(logits.view(B, -1), out=tok)
+        g = _DecodeGraph(graph, tok, pos, kv_len, logits)
+        self._graphs[key] = g
+        return g
+
+    def _kv_for(self, B, bucket):
+        key = (B, bucket)
+        kv = self._kv_pool.get(key)
+        if kv is None:
+            kv = []
+            for _ in range(self.num_layers):
+                k = torch.zeros(B, self.num_kv_heads, bucket, self.head_dim,
+                                dtype=torch.bfloat16, device=self.device)
+                kv.append((k, torch.zeros_like(k)))
+            self._kv_pool[key] = kv
+        return kv
+
+    @torch.no_grad()
+    def generate_tokens(self, input_ids=None, max_new_tokens=256, eos_token_id=151645,
+                        inputs_embeds=None, position_ids=None, deepstack_embeds=None,
+                        visual_mask=None, rope_delta=0, eos_check_every=32):
+        """Batched greedy generation with a device-resident decode loop.
+
+        Returns int64 [B, T] (T <= max_new_tokens): generation stops once every row
+        has produced EOS; rows that stop early keep producing tokens after their
+        EOS, which callers cut (see generate)."""
+        if inputs_embeds is not None:
+            B, P, _ = inputs_embeds.shape
+        else:
+            B, P = input_ids.shape
+        need = P + max_new_tokens
+        if need > self.max_seq_len:
+            raise ValueError(f"prompt {P} + {max_new_tokens} new tokens exceeds max_seq_len "
+                             f"{self.max_seq_len}")
+        bucket = self._bucket(need)
+        kv = self._kv_for(B, bucket)
+        g = None
+        if self.use_graphs and max_new_tokens > 1:
+            g = self._capture_decode(B, kv, bucket, rope_delta)
+        if inputs_embeds is not None:
+            x = inputs_embeds.to(self.device, torch.bfloat16).reshape(B * P, -1).contiguous()
+        else:
+            x = self._embed(input_ids).view(B * P, -1)
+        rope = self._mrope(position_ids) if position_ids is not None else None
+        x, pend = self._run(x, B, P, 0, kv, rope=rope, deepstack=deepstack_embeds,
+                            visual_mask=visual_mask)
+        logits = self._logits(x, pend, B, P)
+        out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
+        out[:, 0] = ops.argmax(logits.view(B, -1))
+        if max_new_tokens == 1:
+            return out
+        # cache positions continue at P; RoPE rows at P + rope_delta (M-RoPE text)
+        if g is not None:
+            g.tok.copy_(out[:, 0])
+            g.pos.fill_(P)
+            g.kv_len.fill_(P + 1)
+            done_at = max_new_tokens
+            for i in range(1, max_new_tokens):
+                g.graph.replay()
+                out[:, i].copy_(g.tok)
+                g.pos.add_(1)
+                g.kv_len.add_(1)
+                if eos_token_id is not None and i % eos_check_every == 0:
+                    if bool((out[:, :i + 1] == eos_token_id).any(dim=1).all()):
+                        done_at = i + 1
+                        break
+            return out[:, :done_at]
+        tok = out[:, 0]
+        for i in range(1, max_new_tokens):
+            pos = P + i - 1
+            x = self._embed(tok.view(B, 1)).view(B, -1)
+            x, pend = self._run(x, B, 1, pos, kv, rope_delta=rope_delta)
+            tok = ops.argmax(self._logits(x, pend, B, 1).view(B, -1))
+            out[:, i] = tok
+        return out
+
+    @staticmethod
+    def _cut_at_eos(row, eos):
+        toks = []
+        for t in row:
+            if t == eos:
+                break
+            toks.append(t)
+        return toks
+
+    @torch.no_grad()
+    def generate(self, input_ids, max_new_tokens=256, eos_token_id=151645, verbose=False):
+        """model_fused.py:302-328: greedy, returns list[int] for batch 1 (a list
+        of lists for batch > 1).  The first token is always kept; later tokens
+        stop before the first EOS, as in the reference."""
+        t0 = time.time()
+        toks = self.generate_tokens(input_ids, max_new_tokens, eos_token_id).tolist()
+        if verbose and (not dist.is_initialized() or dist.get_rank() == 0):
+            print(f"    generate: {time.time() - t0:.3f}s for {len(toks[0])} tokens")
+        rows = [[r[0]] + self._cut_at_eos(r[1:], eos_token_id) for r in toks]
+        return rows[0] if len(rows) == 1 else rows
+
+    @torch.no_grad()
+    def generate_with_embeds(self, inputs_embeds, max_new_tokens=256, eos_token_id=151645,
+                             deepstack_embeds=None, visual_mask=None, position_ids=None,
+                             rope_delta=0):
+        """model_fused.py:330-362 (+ optional 3-axis M-RoPE position_ids)."""
+        toks = self.generate_tokens(None, max_new_tokens, eos_token_id,
+                                    inputs_embeds=inputs_embeds, position_ids=position_ids,
+                                    deepstack_embeds=deepstack_embeds, visual_mask=visual_mask,
+                                    rope_delta=rope_delta).tolist()
+        rows = [[r[0]] + self._cut_at_eos(r[1:], eos_token_id) for r in toks]
+        return rows[0] if len(rows) == 1 else rows

@@ -1,0 +1,294 @@
+"""Torch-facing wrappers around the q3vl C ABI.
+
+Every wrapper validates device, dtype, shape and contiguity, then launches on
+torch's current CUDA stream.  Tensors must already live on a CUDA device: the
+path has no CPU fallback and raises instead.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import (Q3_BF16, Q3_EPI_NONE, Q3_EPI_RESIDUAL, Q3_EPI_SWIGLU, Q3_F32, call)
+
+HEAD_DIM = 128
+_EPI = {"none": Q3_EPI_NONE, "residual": Q3_EPI_RESIDUAL, "swiglu": Q3_EPI_SWIGLU}
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(name: str, *ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name}: tensors must be on a CUDA device (no CPU fallback); "
+                               f"got {t.device}")
+
+
+def _bf16(name: str, *ts):
+    for t in ts:
+        if t is not None and t.dtype != torch.bfloat16:
+            raise TypeError(f"{name}: expected bfloat16, got {t.dtype}")
+
+
+def _contig(name: str, *ts):
+    for t in ts:
+        if t is not None and not t.is_contiguous():
+            raise ValueError(f"{name}: tensors must be contiguous")
+
+
+# ----------------------------------------------------------------------------
+# a1: RMSNorm (+ fused residual add)
+# ----------------------------------------------------------------------------
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, add: torch.Tensor = None,
+            h_out: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+    """y = bf16(bf16(h*rsqrt(mean(h^2)+eps))*w) with h = x (+ add, written to h_out)."""
+    _cuda("rmsnorm", x, weight, add, h_out, out)
+    _bf16("rmsnorm", x, weight, add, h_out, out)
+    _contig("rmsnorm", x, weight, add, h_out, out)
+    hidden = x.shape[-1]
+    if weight.numel() != hidden:
+        raise ValueError(f"rmsnorm: weight has {weight.numel()} elements, hidden is {hidden}")
+    if add is not None and add.shape != x.shape:
+        raise ValueError("rmsnorm: add must match x")
+    y = torch.empty_like(x) if out is None else out
+    call("q3_rmsnorm", _p(x), _p(add), _p(h_out), _p(weight), _p(y), x.numel() // hidden,
+         hidden, float(eps), _stream())
+    return y
+
+
+# ----------------------------------------------------------------------------
+# a9 / a4: RoPE and M-RoPE tables
+# ----------------------------------------------------------------------------
+def rope(x: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """x bf16 [S, N, 128], cos_sin f32 [S, 128] -> rotate_half RoPE (bf16)."""
+    _cuda("rope", x, cos_sin)
+    _bf16("rope", x)
+    _contig("rope", x, cos_sin)
+    if cos_sin.dtype != torch.float32:
+        raise TypeError("rope: cos_sin must be float32")
+    S, N, D = x.shape
+    if cos_sin.shape != (S, D):
+        raise ValueError(f"rope: cos_sin shape {tuple(cos_sin.shape)} != {(S, D)}")
+    out = torch.empty_like(x)
+    call("q3_rope", _p(x), _p(cos_sin), _p(out), S, N, D, _stream())
+    return out
+
+
+def mrope_cos_sin(position_ids: torch.Tensor, inv_freq: torch.Tensor,
+                  mrope_section=(24, 20, 20)):
+    """position_ids int64 [3, n] -> (cos, sin) f32 [n, D/2] (interleaved M-RoPE)."""
+    _cuda("mrope_cos_sin", position_ids, inv_freq)
+    if position_ids.dtype != torch.int64 or inv_freq.dtype != torch.float32:
+        raise TypeError("mrope_cos_sin: position_ids int64, inv_freq float32")
+    pos = position_ids.reshape(3, -1).contiguous()
+    n = pos.shape[1]
+    half = inv_freq.numel()
+    cos = torch.empty(n, half, dtype=torch.float32, device=pos.device)
+    sin = torch.empty_like(cos)
+    call("q3_mrope_cos_sin", _p(pos), _p(inv_freq.contiguous()), n, 2 * half,
+         int(mrope_section[1]), int(mrope_section[2]), _p(cos), _p(sin), _stream())
+    return cos, sin
+
+
+# ----------------------------------------------------------------------------
+# a3 epilogue + a5: QK-norm, RoPE, KV write
+# ----------------------------------------------------------------------------
+def qkv_norm_rope(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *, B: int, S: int, Hq: int,
+                  Hkv: int, start_pos: int = 0, pos_dev: torch.Tensor = None,
+                  cs_use_pos: bool = True, cs_offset: int = 0, cs_stride_b: int = 0,
+                  k_cache=None, v_cache=None, want_q: bool = True, want_kv: bool = False,
+                  eps: float = 1e-6):
+    """Per-head QK-RMSNorm + RoPE on a fused qkv [B*S, (Hq+2Hkv)*128]; writes the
+    rotated k and v into the caches at the cache position (start_pos or
+    *pos_dev).  RoPE row of token (b, s) = cs_use_pos*pos + cs_offset +
+    b*cs_stride_b + s."""
+    _cuda("qkv_norm_rope", qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, pos_dev)
+    _bf16("qkv_norm_rope", qkv, q_norm_w, k_norm_w, k_cache, v_cache)
+    _contig("qkv_norm_rope", qkv, cos, sin, k_cache, v_cache)
+    if qkv.numel() != B * S * (Hq + 2 * Hkv) * HEAD_DIM:
+        raise ValueError("qkv_norm_rope: qkv size does not match B,S,Hq,Hkv")
+    if cos.dtype == torch.bfloat16:
+        cs_dtype = Q3_BF16
+    elif cos.dtype == torch.float32:
+        cs_dtype = Q3_F32
+    else:
+        raise TypeError("qkv_norm_rope: cos/sin must be bf16 or f32")
+    dev = qkv.device
+    q = torch.empty(B, Hq, S, HEAD_DIM, dtype=torch.bfloat16, device=dev) if want_q else None
+    k = v = None
+    if want_kv:
+        k = torch.empty(B, Hkv, S, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        v = torch.empty_like(k)
+    max_seq = k_cache.shape[2] if k_cache is not None else 0
+    if pos_dev is not None and pos_dev.dtype != torch.int32:
+        raise TypeError("qkv_norm_rope: pos_dev must be int32")
+    call("q3_qkv_norm_rope", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin), cs_dtype,
+         1 if cs_use_pos else 0, int(cs_offset), int(cs_stride_b), _p(q), _p(k), _p(v),
+         _p(k_cache),
+         _p(v_cache), B, S, Hq, Hkv, HEAD_DIM, int(start_pos), _p(pos_dev), int(max_seq),
+         float(eps), _stream())
+    return q, k, v
+
+
+# ----------------------------------------------------------------------------
+# a6/a8: decode attention
+# ----------------------------------------------------------------------------
+# Split-K workspaces, one per (device, shape); never freed, because captured
+# decode graphs keep their addresses.
+_ws_cache: dict = {}
+
+
+def decode_workspace(B: int, Hq: int, Hkv: int, device) -> torch.Tensor | None:
+    """Workspace large enough for any KV length (the split count saturates at
+    about two CTAs per SM, so the size is bounded)."""
+    nbytes = _lib.raw("q3_attn_decode_workspace_bytes")(B, Hq, Hkv, HEAD_DIM, 1 << 30)
+    if nbytes == 0:
+        return None
+    key = (str(torch.device(device)), B, Hq, Hkv)
+    ws = _ws_cache.get(key)
+    if ws is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("decode workspace must be allocated before graph capture")
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _ws_cache[key] = ws
+    return ws
+
+
+def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: int,
+                scale: float = None, kv_len_dev: torch.Tensor = None, out: torch.Tensor = None,
+                workspace: torch.Tensor = None) -> torch.Tensor:
+    """q [B, Hq, 128]; caches [B, Hkv, max_seq, 128]; attends to [0, kv_len).
+
+    With kv_len_dev (int32 device scalar), kv_len is the upper bound used to
+    size the split-K grid and the actual length is read on the device."""
+    _cuda("attn_decode", q, k_cache, v_cache, kv_len_dev)
+    _contig("attn_decode", q, k_cache, v_cache)
+    if q.dtype == torch.float32:
+        dt = Q3_F32
+    elif q.dtype == torch.bfloat16:
+        dt = Q3_BF16
+    else:
+        raise TypeError("attn_decode: q must be float32 or bfloat16")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise TypeError("attn_decode: q, k_cache, v_cache must share a dtype")
+    B, Hq, D = q.shape
+    _, Hkv, max_seq, _ = k_cache.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = torch.empty_like(q) if out is None else out
+    ws = workspace if workspace is not None else decode_workspace(B, Hq, Hkv, q.device)
+    call("q3_attn_decode", _p(q), _p(k_cache), _p(v_cache), _p(o), B, Hq, Hkv, D, int(kv_len),
+         _p(kv_len_dev), max_seq, float(scale), dt, _p(ws), 0 if ws is None else ws.numel(),
+         _stream())
+    return o
+
+
+# ----------------------------------------------------------------------------
+# a6/a7: prefill attention
+# ----------------------------------------------------------------------------
+def _strides_bhs(t: torch.Tensor, name: str):
+    """(b, h, s) element strides of a [B, H, S, D] view with unit d stride."""
+    if t.stride(3) != 1:
+        raise ValueError(f"attn_prefill: {name} must have a contiguous head_dim")
+    return (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+
+
+def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_pos: int = 0,
+                 causal: bool = True, scale: float = None, out: torch.Tensor = None):
+    """q [B, Hq, S, 128] (any strides with unit d), k/v [B, Hkv, >=start+S, 128].
+
+    Returns out as a [B, Hq, S, 128] view (pass `out` to choose the layout)."""
+    _cuda("attn_prefill", q, k, v, out)
+    _bf16("attn_prefill", q, k, v, out)
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    if k.shape[2] < start_pos + S or v.shape != k.shape:
+        raise ValueError("attn_prefill: k/v must hold start_pos + S positions")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device=q.device)
+    if v.stride() != k.stride():
+        raise ValueError("attn_prefill: k and v must share strides")
+    call("q3_attn_prefill", _p(q), _p(k), _p(v), _p(out), B, Hq, Hkv, S, D, int(start_pos),
+         1 if causal else 0, float(scale), _strides_bhs(q, "q"), _strides_bhs(k, "k"),
+         _strides_bhs(out, "out"), _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------
+# GEMM
+# ----------------------------------------------------------------------------
+def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none", residual: torch.Tensor = None,
+         out: torch.Tensor = None) -> torch.Tensor:
+    """C = a @ w.T for a [..., K] and K-major weights w [N, K] (bf16)."""
+    _cuda("gemm", a, w, residual, out)
+    _bf16("gemm", a, w, residual, out)
+    _contig("gemm", a, w, residual, out)
+    K = a.shape[-1]
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"gemm: weight [N={N}, K={w.shape[1]}] does not match K={K}")
+    M = a.numel() // K
+    epi = _EPI[epilogue]
+    n_out = N // 2 if epi == Q3_EPI_SWIGLU else N
+    if out is None:
+        out = torch.empty(*a.shape[:-1], n_out, dtype=torch.bfloat16, device=a.device)
+    if epi == Q3_EPI_RESIDUAL and (residual is None or residual.numel() != M * N):
+        raise ValueError("gemm: residual epilogue needs residual [M, N]")
+    call("q3_gemm", _p(a), _p(w), _p(out), M, N, K, epi, _p(residual), _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------
+# embedding / argmax
+# ----------------------------------------------------------------------------
+def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    _cuda("embed", ids, table, out)
+    _bf16("embed", table, out)
+    ids_c = ids.contiguous()
+    if ids_c.dtype != torch.int64:
+        ids_c = ids_c.to(torch.int64)
+    V, H = table.shape
+    if out is None:
+        out = torch.empty(*ids.shape, H, dtype=torch.bfloat16, device=table.device)
+    call("q3_embed", _p(ids_c), _p(table), _p(out), ids_c.numel(), H, V, _stream())
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """bf16(a + b)."""
+    _cuda("add", a, b, out)
+    _bf16("add", a, b, out)
+    _contig("add", a, b, out)
+    if a.shape != b.shape:
+        raise ValueError("add: shapes differ")
+    out = torch.empty_like(a) if out is None else out
+    call("q3_add", _p(a), _p(b), _p(out), a.numel(), _stream())
+    return out
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    _cuda("argmax", logits, out)
+    _bf16("argmax", logits)
+    _contig("argmax", logits)
+    V = logits.shape[-1]
+    rows = logits.numel() // V
+    if out is None:
+        out = torch.empty(logits.shape[:-1], dtype=torch.int64, device=logits.device)
+    call("q3_argmax", _p(logits), rows, V, _p(out), _stream())
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    """Error code recorded by a kernel whose bounded wait timed out (0 = none)."""
+    return int(_lib.raw("q3_device_error")(1 if clear else 0))

@@ -1,0 +1,139 @@
+"""Seeded inputs shared by the fixture generator and the tests.
+
+Everything here is regenerated deterministically from CPU torch RNG seeds, so
+the fixtures only need to store outputs (and input checksums).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from oracle import decoder as odec
+from oracle import ref as oref
+
+BF16 = torch.bfloat16
+
+
+# ---- test_kernels.py:34,113-123,171-175: seed 42, S=256, 4 q heads, 1 kv head ----
+def kernels_kat_inputs():
+    g = torch.Generator().manual_seed(42)
+    x = torch.randn(256, 4, 128, dtype=BF16, generator=g)
+    inv = 1.0 / (1000000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    freqs = torch.outer(torch.arange(256, dtype=torch.float32), inv)
+    cos, sin = freqs.cos(), freqs.sin()
+    q = torch.randn(4, 128, 256, dtype=BF16, generator=g)
+    k = torch.randn(1, 128, 256, dtype=BF16, generator=g)
+    v = torch.randn(1, 256, 128, dtype=BF16, generator=g)
+    return x, cos, sin, q, k, v
+
+
+# ---- config 1: B1, 32 q heads, 8 kv heads, D128, L1024, fp32, N(0,1) ----
+def decode_cfg1_inputs(seed: int = 0, B: int = 1, Hq: int = 32, Hkv: int = 8, L: int = 1024):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, 128, generator=g)
+    k = torch.randn(B, Hkv, L, 128, generator=g)
+    v = torch.randn(B, Hkv, L, 128, generator=g)
+    return q, k, v
+
+
+# ---- a3: AttentionBlock on small shapes (TP8-like 4:1 GQA, nonzero offset) ----
+def attn_block_case(seed: int = 3):
+    g = torch.Generator().manual_seed(seed)
+    H, Hq, Hkv, S, B = 512, 4, 1, 32, 2
+
+    def rn(*s, std=0.02):
+        return (torch.randn(*s, generator=g) * std).to(BF16)
+
+    return dict(
+        H=H, Hq=Hq, Hkv=Hkv, S=S, B=B, start=16, max_seq=128,
+        qkv_w=rn(H, (Hq + 2 * Hkv) * 128), o_w=rn(Hq * 128, H),
+        in_norm=(1 + torch.randn(H, generator=g) * 0.1).to(BF16),
+        q_norm=(1 + torch.randn(128, generator=g) * 0.1).to(BF16),
+        k_norm=(1 + torch.randn(128, generator=g) * 0.1).to(BF16),
+        hidden=torch.randn(B, S, H, generator=g).to(BF16))
+
+
+# ---- one Qwen3-VL-8B-shape layer at TP1 ----
+def layer8b_case(seed: int = 1):
+    spec = odec.Spec(layers=1, vocab=16, max_seq=64)
+    w = odec.make_weights(spec, seed=seed, random_norms=True)
+    g = torch.Generator().manual_seed(seed + 100)
+    hidden = torch.randn(1, 8, 4096, generator=g).to(BF16)
+    hidden_dec = torch.randn(1, 1, 4096, generator=g).to(BF16)
+    return dict(spec=spec, weights=w, hidden=hidden, hidden_dec=hidden_dec, S=8, max_seq=64)
+
+
+# ---- tiny full decoders (reference generate), TP1 and TP2 ----
+DECODER_CASES = {
+    "decoder_tiny_tp1": dict(
+        spec=odec.Spec(hidden=512, q_heads=4, kv_heads=1, inter=1024, vocab=1024, layers=2,
+                       max_seq=256),
+        tp=1, seed=11, prompt_len=40, new_tokens=32, max_seq=256),
+    "decoder_tiny_tp2": dict(
+        spec=odec.Spec(hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=1024, layers=2,
+                       max_seq=256),
+        tp=2, seed=12, prompt_len=40, new_tokens=32, max_seq=256),
+}
+
+
+def peaky(lm_head: torch.Tensor, seed: int) -> torch.Tensor:
+    """Scale lm_head rows by lognormal factors so greedy argmax has clear margins
+    (random-init logits otherwise sit within bf16 rounding of each other)."""
+    g = torch.Generator().manual_seed(seed + 7)
+    f = torch.exp(torch.randn(lm_head.shape[0], 1, generator=g) * 1.0)
+    return (lm_head.float() * f).to(BF16)
+
+
+def decoder_weights(name: str):
+    c = DECODER_CASES[name]
+    w = odec.make_weights(c["spec"], seed=c["seed"], random_norms=True)
+    w["lm_head"] = peaky(w["lm_head"], c["seed"])
+    return w
+
+
+def decoder_prompt(name: str) -> torch.Tensor:
+    c = DECODER_CASES[name]
+    g = torch.Generator().manual_seed(c["seed"] + 1)
+    return torch.randint(0, c["spec"].vocab, (1, c["prompt_len"]), generator=g)
+
+
+def weights_checksum(w: dict) -> float:
+    s = 0.0
+    for lw in w["layers"]:
+        for t in lw.values():
+            s += float(t.double().abs().sum())
+    for k in ("embed", "final_norm", "lm_head"):
+        s += float(w[k].double().abs().sum())
+    return s
+
+
+# ---- config 2 M-RoPE: HF rotary on the 3-axis positions (first 512 tokens) ----
+MROPE_ROWS = 512
+
+
+def mrope_q_input(seed: int = 5):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(1, 1, MROPE_ROWS, 128, generator=g).to(BF16)
+
+
+def hf_mrope_reference():
+    """transformers 5.5.0 Qwen3VLTextRotaryEmbedding + apply_rotary_pos_emb."""
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import (Qwen3VLTextRotaryEmbedding,
+                                                                apply_rotary_pos_emb)
+    cfg = Qwen3VLTextConfig(hidden_size=4096, num_attention_heads=32, num_key_value_heads=8,
+                            head_dim=128,
+                            rope_parameters={"rope_type": "default", "rope_theta": 5e6,
+                                             "mrope_section": [24, 20, 20],
+                                             "mrope_interleaved": True})
+    rot = Qwen3VLTextRotaryEmbedding(cfg)
+    pos = oref.config2_position_ids()            # [3, 1, 2048]
+    q = mrope_q_input()
+    cos, sin = rot(q, pos[:, :, :MROPE_ROWS])     # [1, S, 128] bf16
+    qe, _ = apply_rotary_pos_emb(q, q, cos, sin)
+    return cos[0, :, :64].contiguous(), sin[0, :, :64].contiguous(), qe
+
+
+def attention_scale() -> float:
+    return 1.0 / math.sqrt(128)

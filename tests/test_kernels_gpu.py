@@ -1,0 +1,257 @@
+"""Kernel parity: the CUDA path (through the C ABI) vs the CPU oracle and the
+golden fixtures made from the reference.  Tolerances are stated per test:
+bf16 outputs are compared by max-abs and cosine; the fp32 decode attention of
+config 1 by max-abs <= 1e-5."""
+import math
+
+import pytest
+import torch
+
+from oracle import ref as oref
+from q3vl import layout, ops
+from tests.golden import cases
+from tests.helpers import as_tensor, compare, load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+BF16 = torch.bfloat16
+
+
+def rnd(*shape, seed=0, dtype=BF16, std=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * std).to(dtype)
+
+
+# --------------------------------------------------------------------------- a1
+@pytest.mark.parametrize("rows,hidden", [(1, 4096), (37, 4096), (8, 2048), (5, 520), (3, 1024)])
+def test_rmsnorm(rows, hidden):
+    x, w = rnd(rows, hidden, seed=1), (1 + rnd(hidden, seed=2, std=0.1)).to(BF16)
+    y = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6).cpu()
+    compare("rmsnorm", y, oref.rmsnorm(x, w), max_abs=1.6e-2, min_cos=0.99999)
+    mism = (y.view(torch.int16) != oref.rmsnorm(x, w).view(torch.int16)).float().mean().item()
+    assert mism < 1e-3, f"rmsnorm: {mism:.4%} of elements differ from the oracle bit pattern"
+
+
+def test_rmsnorm_fused_residual():
+    x, a = rnd(9, 4096, seed=3), rnd(9, 4096, seed=4)
+    w = (1 + rnd(4096, seed=5, std=0.1)).to(BF16)
+    h = torch.empty(9, 4096, dtype=BF16, device=DEV)
+    y = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6, add=a.to(DEV), h_out=h)
+    assert torch.equal(h.cpu(), x + a)
+    compare("add+rmsnorm", y.cpu(), oref.rmsnorm(x + a, w), max_abs=1.6e-2, min_cos=0.99999)
+
+
+# --------------------------------------------------------------------------- a9
+def test_rope_kat_bit_exact():
+    """kernels/rope.py semantics on the reference test's seed-42 inputs (S=256, N=4)."""
+    g = load_golden("kernels_kat")
+    x, cos, sin, *_ = cases.kernels_kat_inputs()
+    cs = torch.cat([cos, sin], dim=-1).float()
+    out = ops.rope(x.to(DEV), cs.to(DEV)).cpu()
+    assert torch.equal(out, as_tensor(g["rope"]))
+
+
+# --------------------------------------------------------------------------- a4
+def test_mrope_tables_config2():
+    pos = oref.config2_position_ids()             # [3, 1, 2048]
+    inv = oref.inv_freq(128, 5e6)
+    cos, sin = ops.mrope_cos_sin(pos.to(DEV), inv.to(DEV))
+    f = oref.mrope_freqs(pos, inv)[0]             # [2048, 64] fp32 angles
+    compare("mrope cos", cos.cpu(), f.cos(), max_abs=2e-6)
+    compare("mrope sin", sin.cpu(), f.sin(), max_abs=2e-6)
+    g = load_golden("mrope_cfg2")                 # HF tables (bf16) for the first 512 rows
+    compare("mrope vs HF", cos[:cases.MROPE_ROWS].cpu().to(BF16), as_tensor(g["cos"]),
+            max_abs=8e-3)
+
+
+# --------------------------------------------------------------------------- a3 epilogue
+def _attn_block_qkv(c):
+    h = oref.rmsnorm(c["hidden"], c["in_norm"])
+    return h @ c["qkv_w"]                         # bf16 [B, S, (Hq+2Hkv)*D]
+
+
+def test_qkv_norm_rope_matches_reference_attention_block():
+    """Epilogue on the reference AttentionBlock's own QKV product (1-D bf16 tables)."""
+    g = load_golden("attn_block")
+    c = cases.attn_block_case()
+    qkv = _attn_block_qkv(c)
+    cos, sin = oref.rotary_tables(128, c["max_seq"], 5e6)
+    B, S, Hq, Hkv = c["B"], c["S"], c["Hq"], c["Hkv"]
+    kc = torch.zeros(B, Hkv, c["max_seq"], 128, dtype=BF16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q, k, v = ops.qkv_norm_rope(qkv.to(DEV).contiguous(), c["q_norm"].to(DEV),
+                                c["k_norm"].to(DEV), cos.to(DEV), sin.to(DEV), B=B, S=S,
+                                Hq=Hq, Hkv=Hkv, start_pos=c["start"], k_cache=kc, v_cache=vc,
+                                want_kv=True)
+    for name, got in (("q", q), ("k", k), ("v", v)):
+        want = as_tensor(g[name])
+        compare(f"qkv epilogue {name}", got.cpu(), want, max_abs=3.2e-2, min_cos=0.99999)
+        mism = (got.cpu().view(torch.int16) != want.view(torch.int16)).float().mean().item()
+        assert mism < 2e-3, f"{name}: {mism:.4%} differ bitwise from the reference"
+    st = c["start"]
+    assert torch.equal(kc[:, :, st:st + S].cpu(), k.cpu())
+    assert torch.equal(vc[:, :, st:st + S].cpu(), v.cpu())
+    assert kc[:, :, :st].abs().sum().item() == 0 and kc[:, :, st + S:].abs().sum().item() == 0
+
+
+def test_qkv_norm_rope_device_position_and_mrope():
+    c = cases.attn_block_case()
+    qkv = _attn_block_qkv(c)
+    B, S, Hq, Hkv = c["B"], c["S"], c["Hq"], c["Hkv"]
+    # per-token f32 M-RoPE rows (b-stride S), positions from the config-2 layout
+    pos = oref.config2_position_ids(seq=S + 100)[:, :, 100:100 + S].expand(3, B, S)
+    inv = oref.inv_freq(128, 5e6)
+    cosf, sinf = ops.mrope_cos_sin(pos.contiguous().to(DEV), inv.to(DEV))
+    q, k, v = ops.qkv_norm_rope(qkv.to(DEV).contiguous(), c["q_norm"].to(DEV),
+                                c["k_norm"].to(DEV), cosf, sinf, B=B, S=S, Hq=Hq, Hkv=Hkv,
+                                cs_use_pos=False, cs_stride_b=S, want_kv=True)
+    hc, hs = oref.mrope_cos_sin(pos, inv)          # bf16 [B, S, 128]
+    rq, rk, rv = oref.attention_block(c["hidden"], c["qkv_w"], None, c["in_norm"], c["q_norm"],
+                                      c["k_norm"], hc[:, None], hs[:, None], Hq, Hkv)
+    compare("mrope q", q.cpu(), rq, max_abs=3.2e-2, min_cos=0.99999)
+    compare("mrope k", k.cpu(), rk, max_abs=3.2e-2, min_cos=0.99999)
+    # device-resident position (graph replay path) == host position
+    pos_dev = torch.tensor([c["start"]], dtype=torch.int32, device=DEV)
+    cos, sin = oref.rotary_tables(128, c["max_seq"], 5e6)
+    q1, _, _ = ops.qkv_norm_rope(qkv.to(DEV).contiguous(), c["q_norm"].to(DEV),
+                                 c["k_norm"].to(DEV), cos.to(DEV), sin.to(DEV), B=B, S=S, Hq=Hq,
+                                 Hkv=Hkv, start_pos=c["start"])
+    q2, _, _ = ops.qkv_norm_rope(qkv.to(DEV).contiguous(), c["q_norm"].to(DEV),
+                                 c["k_norm"].to(DEV), cos.to(DEV), sin.to(DEV), B=B, S=S, Hq=Hq,
+                                 Hkv=Hkv, start_pos=0, pos_dev=pos_dev)
+    assert torch.equal(q1, q2)
+
+
+# --------------------------------------------------------------------------- a6/a8 decode
+def test_decode_attention_config1_fp32_vs_reference():
+    """Config 1 (B1, Hq32, Hkv8, D128, L1024, fp32): max-abs <= 1e-5 vs the
+    reference forward_layer's eager attention (golden)."""
+    g = load_golden("decode_cfg1")
+    q, k, v = cases.decode_cfg1_inputs()
+    out = ops.attn_decode(q.to(DEV), k.to(DEV), v.to(DEV), kv_len=1024).cpu()
+    compare("decode cfg1", out, as_tensor(g["out"]), max_abs=1e-5, min_cos=0.999999)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,maxS", [(3, 8, 2, 777, 1024), (8, 32, 8, 1100, 2048),
+                                            (2, 4, 1, 1, 64), (1, 4, 1, 64, 64),
+                                            (2, 16, 16, 300, 512), (1, 16, 2, 4096, 4096)])
+def test_decode_attention_bf16(B, Hq, Hkv, L, maxS):
+    q = rnd(B, Hq, 128, seed=7)
+    kc = rnd(B, Hkv, maxS, 128, seed=8)
+    vc = rnd(B, Hkv, maxS, 128, seed=9)
+    out = ops.attn_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), kv_len=L).cpu()
+    want = oref.decode_attention_fp32(q.float(), kc[:, :, :L].float(), vc[:, :, :L].float())
+    compare("decode bf16", out, want, max_abs=1e-2, min_cos=0.9999)
+    # the reference's own bf16 eager path (rounded scores/probabilities)
+    eager = oref.eager_attention(q[:, :, None], kc[:, :, :L], vc[:, :, :L], L - 1)[:, :, 0]
+    compare("decode vs eager bf16", out, eager, max_abs=2e-2, min_cos=0.9999)
+
+
+def test_decode_attention_device_length():
+    q = rnd(2, 8, 128, seed=10)
+    kc, vc = rnd(2, 2, 2048, 128, seed=11), rnd(2, 2, 2048, 128, seed=12)
+    qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
+    for L in (1, 513, 2048):
+        Ld = torch.tensor([L], dtype=torch.int32, device=DEV)
+        a = ops.attn_decode(qd, kd, vd, kv_len=2048, kv_len_dev=Ld).cpu()
+        b = ops.attn_decode(qd, kd, vd, kv_len=L).cpu()
+        compare(f"decode dev len {L}", a, b, max_abs=2e-3, min_cos=0.99999)
+
+
+# --------------------------------------------------------------------------- a6/a7 prefill
+def test_prefill_kat_vs_reference_attention_ref():
+    """kernels/prefill_attention.py layouts (q [Hq,D,S], k [Hkv,D,S], v [Hkv,S,D])."""
+    g = load_golden("kernels_kat")
+    _, _, _, q, k, v = cases.kernels_kat_inputs()
+    qd = q.transpose(1, 2)[None].to(DEV)          # strided views with unit d stride
+    kd = k.transpose(1, 2).contiguous()[None].to(DEV)
+    vd = v[None].contiguous().to(DEV)
+    out = ops.attn_prefill(qd.contiguous(), kd, vd, causal=True)[0].cpu()
+    compare("prefill KAT", out, as_tensor(g["attn"]), max_abs=2e-2, min_cos=0.9999)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,start,causal", [(1, 32, 8, 2048, 0, True),
+                                                     (2, 8, 2, 200, 0, True),
+                                                     (1, 4, 1, 130, 70, True),
+                                                     (1, 8, 8, 96, 0, False),
+                                                     (3, 4, 4, 1, 37, True)])
+def test_prefill_attention(B, Hq, Hkv, S, start, causal):
+    q = rnd(B, Hq, S, 128, seed=20)
+    k = rnd(B, Hkv, start + S, 128, seed=21)
+    v = rnd(B, Hkv, start + S, 128, seed=22)
+    out = ops.attn_prefill(q.to(DEV), k.to(DEV), v.to(DEV), start_pos=start, causal=causal).cpu()
+    if causal:
+        want = oref.causal_attention_fp32(q, k, v, start)
+    else:
+        rep = Hq // Hkv
+        s = q.float() @ k.float().repeat_interleave(rep, 1).transpose(-2, -1) / math.sqrt(128)
+        want = torch.softmax(s, -1) @ v.float().repeat_interleave(rep, 1)
+    compare("prefill", out, want, max_abs=2e-2, min_cos=0.9999)
+
+
+def test_prefill_attention_output_layout_bshd():
+    """Writing straight into the [B, S, Hq*D] layout o_proj consumes."""
+    B, Hq, Hkv, S = 2, 8, 2, 160
+    q, k, v = rnd(B, Hq, S, 128, seed=23), rnd(B, Hkv, S, 128, seed=24), rnd(B, Hkv, S, 128, seed=25)
+    o = torch.empty(B, S, Hq, 128, dtype=BF16, device=DEV)
+    ops.attn_prefill(q.to(DEV), k.to(DEV), v.to(DEV), out=o.transpose(1, 2))
+    want = oref.causal_attention_fp32(q, k, v).transpose(1, 2)
+    compare("prefill bshd", o.cpu(), want, max_abs=2e-2, min_cos=0.9999)
+
+
+# --------------------------------------------------------------------------- GEMMs
+def _mm_ref(a, w):
+    return (a.float() @ w.float().t()).to(BF16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (5, 768, 4096), (8, 6144, 4096),
+                                   (16, 4096, 1536), (9, 18992, 512), (17, 768, 4096),
+                                   (128, 512, 512), (300, 1024, 4096), (1024, 3072, 4096),
+                                   (2048, 4096, 1536), (256, 272, 256)])
+def test_gemm_plain(M, N, K):
+    a = rnd(M, K, seed=30)
+    w = rnd(N, K, seed=31, std=0.02)
+    c = ops.gemm(a.to(DEV), w.to(DEV)).cpu()
+    compare(f"gemm {M}x{N}x{K}", c, _mm_ref(a, w), max_abs=1e-2, rel_scale=True,
+            min_cos=0.99999)
+
+
+@pytest.mark.parametrize("M", [4, 200])
+def test_gemm_residual(M):
+    N, K = 4096, 1536
+    a, w, r = rnd(M, K, seed=32), rnd(N, K, seed=33, std=0.02), rnd(M, N, seed=34)
+    c = ops.gemm(a.to(DEV), w.to(DEV), "residual", residual=r.to(DEV)).cpu()
+    compare("gemm+residual", c, r + _mm_ref(a, w), max_abs=1e-2, rel_scale=True,
+            min_cos=0.99999)
+
+
+@pytest.mark.parametrize("M", [3, 16, 130, 512])
+def test_gemm_swiglu(M):
+    I, H = 1536, 4096
+    a = rnd(M, H, seed=35)
+    gate, up = rnd(I, H, seed=36, std=0.02), rnd(I, H, seed=37, std=0.02)
+    w = layout.interleave_gate_up(gate, up)
+    c = ops.gemm(a.to(DEV), w.to(DEV), "swiglu").cpu()
+    gu = a @ torch.cat([gate, up], 0).t()        # reference: fused [gate | up] product
+    g_, u_ = gu.chunk(2, dim=-1)
+    want = torch.nn.functional.silu(g_) * u_
+    compare("gemm+swiglu", c, want, max_abs=2e-2, rel_scale=True, min_cos=0.9999)
+
+
+# --------------------------------------------------------------------------- a13
+def test_embed_and_argmax():
+    V, H = 1000, 512
+    table = rnd(V, H, seed=40)
+    ids = torch.tensor([[0, 5, 999], [17, 17, 3]])
+    out = ops.embed(ids.to(DEV), table.to(DEV)).cpu()
+    assert torch.equal(out, table[ids])
+    logits = rnd(4, 151936, seed=41)
+    logits[2, 77] = 100.0
+    logits[2, 9000] = 100.0  # tie -> first index
+    idx = ops.argmax(logits.to(DEV)).cpu()
+    assert idx.tolist() == logits.float().argmax(-1).tolist()
+    assert idx[2].item() == 77
+
+
+def test_device_error_word_clear():
+    assert ops.device_error(clear=True) == 0

@@ -1,0 +1,76 @@
+"""Host-side checks of the C-ABI library (no GPU needed, no kernel launches):
+it loads, exports every entry point include/q3vl.h declares, and rejects bad
+arguments with a status and a message before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from q3vl import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(REPO, "include", f) for f in os.listdir(os.path.join(REPO, "include"))
+           if f.endswith(".h")]
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        names.update(re.findall(r"^Q3_API\s+[\w\s\*]+?\b(q3_\w+)\s*\(", src, flags=re.M))
+    return names
+
+
+def test_library_loads_and_reports_version():
+    lib = _lib.load()
+    assert lib.q3_version() >= 100
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    lib = _lib.load()
+    decl = declared_symbols()
+    assert decl, "no declarations found in include/*.h"
+    for name in sorted(decl):
+        assert hasattr(lib, name), f"{name} declared but not exported"
+    assert decl == set(_lib.SIGNATURES) - set(), (
+        f"ctypes table and header differ: {sorted(decl ^ set(_lib.SIGNATURES))}")
+
+
+def test_invalid_arguments_are_rejected_on_the_host():
+    lib = _lib.load()
+    rc = lib.q3_gemm(None, None, None, 4, 16, 32, 0, None, None)
+    assert rc == _lib.Q3_ERR_INVALID
+    assert b"null" in lib.q3_last_error()
+    one = ctypes.c_void_p(16)
+    rc = lib.q3_gemm(one, one, one, 4, 10, 32, 0, None, None)          # N % 16 != 0
+    assert rc == _lib.Q3_ERR_INVALID
+    rc = lib.q3_attn_decode(one, one, one, one, 1, 6, 4, 128, 8, None, 16, 0.1, 1, None, 0,
+                            None)                                       # Hq % Hkv != 0
+    assert rc == _lib.Q3_ERR_INVALID
+    rc = lib.q3_rope(one, one, one, 4, 2, 64, None)                      # head_dim != 128
+    assert rc == _lib.Q3_ERR_INVALID
+    rc = lib.q3_qkv_norm_rope(one, one, one, one, one, 1, 1, 0, 0, None, None, None, one, one,
+                              1, 8, 4, 1, 128, 60, None, 64, 1e-6, None)  # cache overflow
+    assert rc == _lib.Q3_ERR_INVALID
+    assert b"max_seq" in lib.q3_last_error()
+
+
+def test_error_raises_q3error():
+    with pytest.raises(_lib.Q3Error) as e:
+        _lib.call("q3_rmsnorm", None, None, None, None, None, 1, 8, 1e-6, None)
+    assert e.value.status == _lib.Q3_ERR_INVALID
+
+
+def test_decode_workspace_sizing_is_host_only():
+    f = _lib.raw("q3_attn_decode_workspace_bytes")
+    assert f(1, 32, 8, 128, 1024) > 0
+    assert f(0, 32, 8, 128, 1024) == 0
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from q3vl import ops
+    x = torch.zeros(2, 4096, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.rmsnorm(x, torch.ones(4096, dtype=torch.bfloat16))
