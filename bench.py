@@ -1,0 +1,379 @@
+"""Benchmark: Qwen3-VL-8B-shape text decoder, greedy generation at TP = N.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1 under: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+Workload (the full 36-layer decoder of the 8B shape, random-init bf16 weights
+N(0, 0.02)): batch 8, prompts of 1024 uniformly random token ids, greedy
+generation of 256 new tokens, KV bucket 2048.  One step = one generate():
+prefill of 8x1024 tokens + 255 CUDA-graph decode steps.  Tensor parallelism
+splits every layer over the N GPUs (strong scaling: total work is fixed).
+
+value  = generated tokens per second over the whole step (8 x 256 / step time);
+         prefill and decode rates are reported beside it.
+e2e    = the same metric through the public API (decoder.generate_tokens) with
+         the prompt copied from pinned host memory and the tokens read back
+         every step.
+The reference arm (--impl reference) times the CPU oracle -- a restatement of
+the reference's own PyTorch decoder -- on a bounded sample of the same
+workload on the host cores and scales it to the full workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "qwen3-vl_b200")
+for _p in (PKG, REPO):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode & prefill tok/s at TP1/2/4/8 (8B shape); attention HBM GB/s vs peak"
+BATCH, PROMPT, NEW_TOKENS, BUCKET = 8, 1024, 256, 2048
+WORKLOAD = (f"Qwen3-VL-8B-shape text decoder (36 layers, hidden 4096, 32/8 heads, inter "
+            f"12288, vocab 151936), batch {BATCH}, prompt {PROMPT} random ids, "
+            f"{NEW_TOKENS} greedy tokens, KV bucket {BUCKET}")
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import loader_fused
+    from q3vl import _lib, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=300), device_id=dev)
+    torch.manual_seed(0)
+    dec = loader_fused.random_decoder(loader_fused.QWEN3_VL_8B, rank, world, dev, seed=0,
+                                      max_seq=BUCKET)
+    g = torch.Generator().manual_seed(1234)
+    prompt_host = torch.randint(0, 151936, (BATCH, PROMPT), generator=g).pin_memory()
+    prompt = prompt_host.to(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up (includes CUDA-graph capture of the decode step)
+    for _ in range(args.warmup):
+        dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
+
+    # launch accounting: one step run eagerly (graphs replay exactly these kernels);
+    # q3_attn_decode launches a split-K combine kernel as well
+    import q3vl.ops as ops_mod
+    counts = {"n": 0}
+    orig_call = ops_mod.call
+
+    def counting_call(name, *a):
+        counts["n"] += 2 if name == "q3_attn_decode" else 1
+        return orig_call(name, *a)
+
+    ops_mod.call = counting_call
+    dec.use_graphs = False
+    dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
+    dec.use_graphs = True
+    ops_mod.call = orig_call
+    launches_per_step = counts["n"]
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, prefill_done=ev[i][1])
+            ev[i][2].record(stream)
+        barrier()
+    tot = sum(e[0].elapsed_time(e[2]) for e in ev)
+    pre = sum(e[0].elapsed_time(e[1]) for e in ev)
+    t = torch.tensor([tot, pre], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tot_ms, pre_ms = float(t[0]), float(t[1])
+    dec_ms = tot_ms - pre_ms
+    K = args.steps
+    gen_tok = BATCH * NEW_TOKENS * K
+    value = gen_tok / (tot_ms / 1e3)
+    prefill_tps = BATCH * PROMPT * K / (pre_ms / 1e3)
+    decode_tps = BATCH * (NEW_TOKENS - 1) * K / (dec_ms / 1e3)
+
+    # ---- e2e through the public API: H2D prompt, D2H tokens each step ----
+    e2e_ms = []
+    for _ in range(max(2, min(3, K))):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        p = prompt_host.to(dev, non_blocking=True)
+        toks = dec.generate_tokens(p, NEW_TOKENS, eos_token_id=None).cpu()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+    te = torch.tensor([sum(e2e_ms) / len(e2e_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = BATCH * NEW_TOKENS / (float(te[0]) / 1e3)
+
+    # ---- dominant kernel: decode GEMV over the largest per-layer weight ----
+    hbm, tflops, peak_kind = peaks()
+    mlp = dec.layers[0].mlp_block
+    x = torch.randn(BATCH, 4096, device=dev).to(torch.bfloat16)
+    w = mlp.gate_up_weight_il
+    for _ in range(5):
+        ops.gemm(x, w, "swiglu")
+    n_it = 50
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n_it):
+        ops.gemm(x, w, "swiglu")
+    b.record(stream)
+    torch.cuda.synchronize()
+    gemv_ms = a.elapsed_time(b) / n_it
+    gemv_bytes = w.numel() * 2 + x.numel() * 2 + BATCH * w.shape[0] // 2 * 2
+    gemv_gbs = gemv_bytes / (gemv_ms / 1e3) / 1e9
+
+    # ---- decode attention HBM GB/s at the workload's mid-generation length ----
+    L = PROMPT + NEW_TOKENS // 2
+    ab = dec.layers[0].attn_block
+    kc = torch.randn(BATCH, ab.num_kv_heads, BUCKET, 128, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(BATCH, ab.num_q_heads, 128, device=dev).to(torch.bfloat16)
+    for _ in range(5):
+        ops.attn_decode(q, kc, vc, kv_len=L)
+    a.record(stream)
+    for _ in range(n_it):
+        ops.attn_decode(q, kc, vc, kv_len=L)
+    b.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = a.elapsed_time(b) / n_it
+    attn_bytes = BATCH * ab.num_kv_heads * L * 128 * 2 * 2 + 2 * q.numel() * 2
+    attn_gbs = attn_bytes / (attn_ms / 1e3) / 1e9
+
+    # decode-step bytes (weights + KV) for the whole-step HBM fraction
+    n_params = sum(p.numel() for lyr in dec.layers for p in
+                   (lyr.attn_block.qkv_weight_km, lyr.o_proj.weight_km,
+                    lyr.mlp_block.gate_up_weight_il, lyr.mlp_block.down_weight_km))
+    n_params += dec.lm_head.weight_km.numel()
+    kv_step = 36 * BATCH * ab.num_kv_heads * (PROMPT + NEW_TOKENS // 2) * 128 * 2 * 2
+    step_bytes = n_params * 2 + kv_step
+    dec_step_ms = dec_ms / K / (NEW_TOKENS - 1)
+    step_gbs = step_bytes / (dec_step_ms / 1e3) / 1e9
+
+    clocks = clk.summary()
+    if rank == 0:
+        cpu = cpu_baseline(budget_s=args.cpu_budget) if args.cpu_budget > 0 else None
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s",
+            "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": round(tot_ms / K, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) bf16 weights, uniform random prompt ids)",
+            "config": {"workload": WORKLOAD, "model": "Qwen3-VL-8B text decoder shape",
+                       "global_batch": BATCH, "seq_len": PROMPT, "new_tokens": NEW_TOKENS,
+                       "parallelism": f"tp{world}", "l2": "weights > L2 (126 MB) every step"},
+            "prefill_tok_s": round(prefill_tps, 1), "decode_tok_s": round(decode_tps, 1),
+            "decode_step_ms": round(dec_step_ms, 4),
+            "decode_step_hbm": {"bytes": step_bytes, "achieved_gbs": round(step_gbs, 1),
+                                "frac": round(step_gbs / hbm, 4)},
+            "attention_hbm_gbs": round(attn_gbs, 1),
+            "attention_hbm_frac": round(attn_gbs / hbm, 4),
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<1,SWIGLU> (gate_up, M=8)",
+                         "achieved": round(gemv_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gemv_gbs / hbm, 4), "traffic": None,
+                         "peak_source": peak_kind,
+                         "bytes_per_launch": gemv_bytes, "launch_ms": round(gemv_ms, 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": BATCH * PROMPT * 8,
+                    "d2h_bytes_per_step": BATCH * NEW_TOKENS * 8},
+            "gpu_launches": launches_per_step * K,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dec._graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle (restated reference decoder)
+# ---------------------------------------------------------------------------
+def cpu_baseline(budget_s: float = 20.0):
+    """Time the CPU oracle on one 8B-shape layer: prefill of a bounded prompt
+    slice and a few decode steps, then scale to the full workload (36 layers,
+    batch 8, 1024-token prompt, 256 tokens).  Returns the cpu_baseline object."""
+    import torch
+
+    from oracle import decoder as odec
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    spec = odec.Spec(layers=1, vocab=16, max_seq=PROMPT + NEW_TOKENS)
+    w = odec.make_weights(spec, seed=0)
+    o = odec.OracleDecoder(spec, w, tp=1)
+    g = torch.Generator().manual_seed(0)
+    # prefill sample: B=8 x p tokens, p shrinks until one layer takes < budget/3
+    p = 256
+    hid = torch.randn(BATCH, p, 4096, generator=g).to(torch.bfloat16)
+    kv = o.init_kv_cache(BATCH, PROMPT + NEW_TOKENS)
+    t0 = time.perf_counter()
+    o.forward_layer(hid, 0, kv, 0)
+    t_pf = time.perf_counter() - t0
+    pf_per_tok = t_pf / (BATCH * p)
+    # decode sample at context ~ the mid-generation length (KV filled with noise)
+    for kc, vc in kv[0]:
+        kc.normal_()
+        vc.normal_()
+    n_dec, t_dec = 0, 0.0
+    L0 = PROMPT + NEW_TOKENS // 2
+    while n_dec < 8 and t_dec < budget_s / 2:
+        x = torch.randn(BATCH, 1, 4096, generator=g).to(torch.bfloat16)
+        t0 = time.perf_counter()
+        o.forward_layer(x, 0, kv, L0 + n_dec)
+        t_dec += time.perf_counter() - t0
+        n_dec += 1
+    dec_per_step = t_dec / n_dec
+    # lm_head GEMV on the last token, measured once
+    lm = (torch.randn(151936 // 8, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    _ = torch.randn(BATCH, 4096).to(torch.bfloat16) @ lm.t()
+    t_lm = (time.perf_counter() - t0) * 8
+    total = 36 * (pf_per_tok * BATCH * PROMPT + (NEW_TOKENS - 1) * dec_per_step) + \
+        NEW_TOKENS * t_lm
+    value = BATCH * NEW_TOKENS / total
+    return {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"oracle (restated model_fused.py decoder, bf16) on one 8B-shape layer: "
+                       f"prefill {BATCH}x{p} tokens ({t_pf:.2f}s) and {n_dec} decode steps at "
+                       f"context {L0} ({dec_per_step:.3f}s/step), lm_head {t_lm:.3f}s/token; "
+                       f"scaled to 36 layers x ({BATCH}x{PROMPT} prefill + "
+                       f"{NEW_TOKENS - 1} decode steps)"),
+            "prefill_tok_s": round(1.0 / (36 * pf_per_tok), 3),
+            "decode_tok_s": round(BATCH / (36 * dec_per_step + t_lm), 4)}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(budget_s=6.0)
+    info = None
+    for _ in range(args.steps):
+        info = cpu_baseline(budget_s=6.0)
+        vals.append(info["value"])
+    value = statistics.mean(vals)
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "model": "Qwen3-VL-8B text decoder shape",
+                       "global_batch": BATCH, "seq_len": PROMPT, "new_tokens": NEW_TOKENS,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": info["cores"],
+                             "kind": "port", "sample": info["sample"]},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=20.0,
+                    help="seconds of CPU-oracle work for the cpu_baseline (0 = skip)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

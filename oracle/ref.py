@@ -86,8 +86,9 @@ def config2_position_ids(seq: int = 2048, text0: int = 100, grid: int = 16) -> t
     (t=h=w=index), then a grid x grid image at t=text0, h=text0+row,
     w=text0+col, then text continuing from text0 + grid (the convention of
     get_vision_position_ids / get_rope_index, modeling_qwen3_vl.py:975-1122)."""
-    pos = torch.zeros(3, seq, dtype=torch.int64)
     n_img = grid * grid
+    full = max(seq, text0 + n_img)
+    pos = torch.zeros(3, full, dtype=torch.int64)
     t = torch.arange(text0)
     pos[:, :text0] = t
     r = torch.arange(n_img) // grid
@@ -95,10 +96,10 @@ def config2_position_ids(seq: int = 2048, text0: int = 100, grid: int = 16) -> t
     pos[0, text0:text0 + n_img] = text0
     pos[1, text0:text0 + n_img] = text0 + r
     pos[2, text0:text0 + n_img] = text0 + c
-    rest = seq - text0 - n_img
+    rest = full - text0 - n_img
     if rest > 0:
         pos[:, text0 + n_img:] = text0 + grid + torch.arange(rest)
-    return pos[:, None, :]   # [3, 1, S]
+    return pos[:, None, :seq]   # [3, 1, S]
 
 
 # ---------------------------------------------------------------------------

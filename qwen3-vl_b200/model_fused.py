@@ -432,12 +432,14 @@ class Qwen3VLDecoderFused:
     @torch.no_grad()
     def generate_tokens(self, input_ids=None, max_new_tokens=256, eos_token_id=151645,
                         inputs_embeds=None, position_ids=None, deepstack_embeds=None,
-                        visual_mask=None, rope_delta=0, eos_check_every=32):
+                        visual_mask=None, rope_delta=0, eos_check_every=32,
+                        prefill_done=None):
         """Batched greedy generation with a device-resident decode loop.
 
         Returns int64 [B, T] (T <= max_new_tokens): generation stops once every row
         has produced EOS; rows that stop early keep producing tokens after their
-        EOS, which callers cut (see generate)."""
+        EOS, which callers cut (see generate).  `prefill_done` (a CUDA event) is
+        recorded on the current stream between prefill and decode."""
         if inputs_embeds is not None:
             B, P, _ = inputs_embeds.shape
         else:
@@ -461,6 +463,8 @@ class Qwen3VLDecoderFused:
         logits = self._logits(x, pend, B, P)
         out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
         out[:, 0] = ops.argmax(logits.view(B, -1))
+        if prefill_done is not None:
+            prefill_done.record(torch.cuda.current_stream(self.device))
         if max_new_tokens == 1:
             return out
         # cache positions continue at P; RoPE rows at P + rope_delta (M-RoPE text)
