@@ -116,6 +116,20 @@ Q3_API int q3_attn_decode(const void* q, const void* k_cache, const void* v_cach
                    int64_t max_seq, float scale, int dtype, void* workspace,
                    size_t workspace_bytes, q3_stream_t stream);
 
+/* Same computation as q3_attn_decode, for callers that cannot allocate device
+ * memory at call time (a runtime whose free HBM is already committed to its
+ * own pools, or a binding that owns only these buffers).  No counterpart in
+ * the reference.  Needs no workspace: split-K partials go to a 4 MiB array
+ * built into the library (held by every GPU that loads it until exit);
+ * requests needing more are rejected with Q3_ERR_INVALID.  All calls on a
+ * device share that array, so calls that overlap on the GPU race; order them
+ * on one stream.  The first call on a device looks up the array's address:
+ * make it before any stream capture.  Allocates nothing. */
+Q3_API int q3_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                  void* out, int B, int Hq, int Hkv, int head_dim,
+                                  int64_t kv_len, const int32_t* kv_len_dev, int64_t max_seq,
+                                  float scale, int dtype, q3_stream_t stream);
+
 /* ---- a6/a7: causal GQA prefill attention ---------------------------------
  * Replaces the S>1 eager attention of forward_layer (model_fused.py:248-262)
  * and prefill_gqa_flash_attention (kernels/prefill_attention.py:28-149).

@@ -354,3 +354,94 @@ extern "C" int q3_attn_decode(const void* q, const void* k_cache, const void* v_
   cudaStream_t s = (cudaStream_t)stream;
   return dtype == Q3_F32 ? launch_decode<float>(p, G, s) : launch_decode<__nv_bfloat16>(p, G, s);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of q3_attn_decode.
+//
+// Some callers cannot allocate device memory when they call this kernel: a
+// serving runtime that has already handed all free HBM to its own KV-cache
+// pool, or a foreign-language binding that only owns the q/cache/out buffers
+// and has no allocator to create a split-K workspace with.  This entry point
+// takes no workspace.  Its split-K partial sums live in the fixed array below,
+// which every GPU that loads this library keeps for the life of the process.
+//
+// Limits and sharing rules:
+//  * the array holds kNoAllocScratchBytes (4 MiB); a request whose split-K
+//    partials would need more is rejected with Q3_ERR_INVALID before launch;
+//  * all calls on a device share the one array, and it keeps whatever the
+//    last call wrote.  Each call writes every partial slot it later reads, so
+//    nothing needs clearing between calls, but two calls that run at the same
+//    time on the GPU (different streams, or different host threads) overwrite
+//    each other's partials: order them on one stream;
+//  * the first call on each device looks up the array's device address with
+//    cudaGetSymbolAddress (with that device current).  Make that first call
+//    before any stream capture on the device.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace q3 {
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_decode_scratch on the current device (looked up once per
+// device); nullptr with the error recorded if the lookup fails.
+static float* decode_scratch_address() {
+  static float* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("q3_attn_decode_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess) {
+      set_error("q3_attn_decode_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  return addr[dev];
+}
+}  // namespace q3
+
+extern "C" int q3_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                      void* out, int B, int Hq, int Hkv, int head_dim,
+                                      int64_t kv_len, const int32_t* kv_len_dev, int64_t max_seq,
+                                      float scale, int dtype, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(q && k_cache && v_cache && out, "q3_attn_decode_noalloc: null pointer");
+  Q3_REQUIRE(head_dim == kHD, "q3_attn_decode_noalloc: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+             "q3_attn_decode_noalloc: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  Q3_REQUIRE(kv_len >= 1 && kv_len <= max_seq,
+             "q3_attn_decode_noalloc: kv_len=%lld outside [1, max_seq=%lld]",
+             (long long)kv_len, (long long)max_seq);
+  Q3_REQUIRE(dtype == Q3_F32 || dtype == Q3_BF16,
+             "q3_attn_decode_noalloc: dtype must be f32 or bf16");
+  const size_t align = dtype == Q3_F32 ? 16 : 8;
+  Q3_REQUIRE(aligned(q, align) && aligned(k_cache, align) && aligned(v_cache, align) &&
+                 aligned(out, align),
+             "q3_attn_decode_noalloc: misaligned pointer");
+  DecodeParams p{};
+  p.q = q; p.k = k_cache; p.v = v_cache; p.out = out;
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv;
+  p.kv_len = kv_len; p.kv_len_dev = kv_len_dev; p.max_seq = max_seq; p.scale = scale;
+  decode_split_plan(B, Hkv, kv_len, &p.splits, &p.chunk);
+  if (p.splits > 1) {
+    const size_t need = (size_t)B * Hq * p.splits * (kHD + 2) * sizeof(float);
+    Q3_REQUIRE(need <= kNoAllocScratchBytes,
+               "q3_attn_decode_noalloc: split-K partials need %zu bytes, more than the %zu-byte "
+               "built-in scratch (use q3_attn_decode with a caller workspace)",
+               need, kNoAllocScratchBytes);
+    float* scratch = decode_scratch_address();
+    if (!scratch) return Q3_ERR_CUDA;
+    p.ws_acc = scratch;
+    p.ws_ml = p.ws_acc + (size_t)B * Hq * p.splits * kHD;
+  }
+  const int G = Hq / Hkv;
+  cudaStream_t s = (cudaStream_t)stream;
+  return dtype == Q3_F32 ? launch_decode<float>(p, G, s) : launch_decode<__nv_bfloat16>(p, G, s);
+}

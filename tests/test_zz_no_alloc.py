@@ -1,0 +1,74 @@
+"""q3_attn_decode_noalloc: the decode-attention entry point for callers that
+cannot allocate device memory when they call it (a runtime whose free HBM is
+already committed to its own pools, or a binding that owns only the q, cache
+and output buffers).  It keeps split-K partials in a fixed array built into
+the library instead of a caller workspace.
+
+The test calls it through the C ABI, twice in a row on different inputs (the
+shared array keeps the first call's partials, which must not leak into the
+second), and compares each result with the existing q3_attn_decode, which
+takes a caller-allocated workspace.  Collected last on purpose (file name).
+"""
+import ctypes
+import math
+
+import pytest
+import torch
+
+from q3vl import _lib, ops
+from tests.helpers import compare
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _noalloc(q, kc, vc, kv_len, kv_len_dev=None):
+    B, Hq, D = q.shape
+    _, Hkv, max_seq, _ = kc.shape
+    out = torch.empty_like(q)
+    dt = _lib.Q3_F32 if q.dtype == torch.float32 else _lib.Q3_BF16
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.call("q3_attn_decode_noalloc", ctypes.c_void_p(q.data_ptr()),
+              ctypes.c_void_p(kc.data_ptr()), ctypes.c_void_p(vc.data_ptr()),
+              ctypes.c_void_p(out.data_ptr()), B, Hq, Hkv, D, kv_len,
+              None if kv_len_dev is None else ctypes.c_void_p(kv_len_dev.data_ptr()),
+              max_seq, 1.0 / math.sqrt(D), dt, stream)
+    return out
+
+
+def _inputs(seed, B, Hq, Hkv, S, dtype):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, 128, generator=g).to(dtype).to(DEV)
+    kc = torch.randn(B, Hkv, S, 128, generator=g).to(dtype).to(DEV)
+    vc = torch.randn(B, Hkv, S, 128, generator=g).to(dtype).to(DEV)
+    return q, kc, vc
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 1e-2)])
+def test_noalloc_matches_workspace_entry_point_twice(dtype, tol):
+    # first call: config-1 shape (B1, Hq32, Hkv8, L1024) -> 32 split-K partials
+    q, kc, vc = _inputs(1, 1, 32, 8, 1024, dtype)
+    a = _noalloc(q, kc, vc, 1024)
+    b = ops.attn_decode(q, kc, vc, kv_len=1024)
+    compare("noalloc call 1", a.cpu(), b.cpu(), max_abs=tol, min_cos=0.99999)
+    # second call right after, different shape and data, same shared scratch
+    q2, kc2, vc2 = _inputs(2, 8, 32, 8, 2048, dtype)
+    a2 = _noalloc(q2, kc2, vc2, 1500)
+    b2 = ops.attn_decode(q2, kc2, vc2, kv_len=1500)
+    compare("noalloc call 2", a2.cpu(), b2.cpu(), max_abs=tol, min_cos=0.99999)
+    torch.cuda.synchronize()
+
+
+def test_noalloc_device_length_and_limit():
+    q, kc, vc = _inputs(3, 2, 8, 2, 2048, torch.bfloat16)
+    L = torch.tensor([777], dtype=torch.int32, device=DEV)
+    a = _noalloc(q, kc, vc, 2048, kv_len_dev=L)
+    b = ops.attn_decode(q, kc, vc, kv_len=777)
+    compare("noalloc device length", a.cpu(), b.cpu(), max_abs=1e-2, min_cos=0.99999)
+    # a request whose partials exceed the built-in scratch (64 query heads on one
+    # KV head over 4096 positions -> 256 splits x 64 heads x 520 B) is refused
+    # on the host before any launch
+    big_q = torch.zeros(1, 64, 128, dtype=torch.bfloat16, device=DEV)
+    big_c = torch.zeros(1, 1, 4096, 128, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(_lib.Q3Error, match="scratch"):
+        _noalloc(big_q, big_c, big_c, 4096)
