@@ -135,6 +135,20 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    if args.profile:
+        # profiling mode (for ncu launch lists): the same generate step with
+        # --new-tokens decode tokens, no side measurements
+        for _ in range(args.warmup + args.steps):
+            dec.generate_tokens(prompt, args.new_tokens, eos_token_id=None)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"profile": True, "new_tokens": args.new_tokens,
+                              "steps": args.warmup + args.steps}), flush=True)
+        if world > 1:
+            dec._graphs.clear()
+            dist.destroy_process_group()
+        return
+
     # warm-up (includes CUDA-graph capture of the decode step)
     for _ in range(args.warmup):
         dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
@@ -368,6 +382,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=20.0,
                     help="seconds of CPU-oracle work for the cpu_baseline (0 = skip)")
+    ap.add_argument("--profile", action="store_true",
+                    help="run warmup+steps generate steps only (for ncu); prints no bench line")
+    ap.add_argument("--new-tokens", type=int, default=NEW_TOKENS,
+                    help="decode tokens per step in --profile mode")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

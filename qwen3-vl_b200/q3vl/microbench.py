@@ -1,0 +1,107 @@
+"""Per-kernel timing on chosen shapes (CUDA events, warm-up, L2 flush between
+iterations), printing achieved GB/s or TFLOP/s.  Also the small-case driver
+for ncu captures of a single kernel.
+
+    python qwen3-vl_b200/q3vl/microbench.py gemv   --M 8 --N 24576 --K 4096 --epi swiglu
+    python qwen3-vl_b200/q3vl/microbench.py gemm   --M 8192 --N 6144 --K 4096
+    python qwen3-vl_b200/q3vl/microbench.py decode --B 8 --Hq 32 --Hkv 8 --L 1152
+    python qwen3-vl_b200/q3vl/microbench.py prefill --B 1 --Hq 32 --Hkv 8 --S 2048
+    python qwen3-vl_b200/q3vl/microbench.py rmsnorm --rows 8192 --hidden 4096
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if _PKG not in sys.path:
+    sys.path.insert(0, _PKG)
+
+import torch  # noqa: E402
+
+from q3vl import ops  # noqa: E402
+
+
+def _time(fn, iters, warmup, flush):
+    for _ in range(warmup):
+        fn()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(iters)]
+    for a, b in evs:
+        if flush is not None:
+            flush.zero_()
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    ts = sorted(a.elapsed_time(b) for a, b in evs)
+    return ts[len(ts) // 2]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm"])
+    ap.add_argument("--M", type=int, default=8)
+    ap.add_argument("--N", type=int, default=24576)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--epi", default="none", choices=["none", "residual", "swiglu"])
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--Hq", type=int, default=32)
+    ap.add_argument("--Hkv", type=int, default=8)
+    ap.add_argument("--L", type=int, default=1152)
+    ap.add_argument("--S", type=int, default=2048)
+    ap.add_argument("--rows", type=int, default=8192)
+    ap.add_argument("--hidden", type=int, default=4096)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--no-flush", action="store_true", help="keep L2 warm between iterations")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    flush = None if a.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    bf = torch.bfloat16
+    res = {"kernel": a.kernel}
+    if a.kernel in ("gemv", "gemm"):
+        x = torch.randn(a.M, a.K, device=dev).to(bf)
+        w = (torch.randn(a.N, a.K, device=dev) * 0.02).to(bf)
+        r = torch.randn(a.M, a.N, device=dev).to(bf) if a.epi == "residual" else None
+        out_n = a.N // 2 if a.epi == "swiglu" else a.N
+        out = torch.empty(a.M, out_n, dtype=bf, device=dev)
+        ms = _time(lambda: ops.gemm(x, w, a.epi, residual=r, out=out), a.iters, a.warmup, flush)
+        nbytes = (w.numel() + x.numel() + out.numel() + (r.numel() if r is not None else 0)) * 2
+        flops = 2.0 * a.M * a.N * a.K
+        res.update(M=a.M, N=a.N, K=a.K, epi=a.epi, ms=ms, gbs=nbytes / ms / 1e6,
+                   tflops=flops / ms / 1e9)
+    elif a.kernel == "decode":
+        dt = torch.float32 if a.dtype == "f32" else bf
+        q = torch.randn(a.B, a.Hq, 128, device=dev).to(dt)
+        kc = torch.randn(a.B, a.Hkv, a.L, 128, device=dev).to(dt)
+        vc = torch.randn_like(kc)
+        out = torch.empty_like(q)
+        ms = _time(lambda: ops.attn_decode(q, kc, vc, kv_len=a.L, out=out), a.iters, a.warmup,
+                   flush)
+        nbytes = 2 * kc.numel() * kc.element_size() + 2 * q.numel() * q.element_size()
+        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, L=a.L, dtype=a.dtype, ms=ms,
+                   gbs=nbytes / ms / 1e6)
+    elif a.kernel == "prefill":
+        q = torch.randn(a.B, a.Hq, a.S, 128, device=dev).to(bf)
+        k = torch.randn(a.B, a.Hkv, a.S, 128, device=dev).to(bf)
+        v = torch.randn_like(k)
+        out = torch.empty_like(q)
+        ms = _time(lambda: ops.attn_prefill(q, k, v, out=out), a.iters, a.warmup, flush)
+        flops = 4.0 * a.B * a.Hq * a.S * a.S * 128 / 2
+        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, S=a.S, ms=ms, tflops=flops / ms / 1e9)
+    else:
+        x = torch.randn(a.rows, a.hidden, device=dev).to(bf)
+        w = torch.ones(a.hidden, dtype=bf, device=dev)
+        y = torch.empty_like(x)
+        ms = _time(lambda: ops.rmsnorm(x, w, out=y), a.iters, a.warmup, flush)
+        res.update(rows=a.rows, hidden=a.hidden, ms=ms, gbs=2 * x.numel() * 2 / ms / 1e6)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
