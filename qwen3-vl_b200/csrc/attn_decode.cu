@@ -113,6 +113,8 @@ struct DecodeParams {
 
 template <typename T, int G>
 __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(DecodeParams p) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -248,6 +250,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(DecodeParam
 // One warp per (b, h): merge the split partials.
 template <typename T>
 __global__ void attn_decode_combine(DecodeParams p) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int64_t bh = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (bh >= (int64_t)p.B * p.Hq) return;
@@ -276,36 +280,338 @@ __global__ void attn_decode_combine(DecodeParams p) {
   Vec4<T>::store(reinterpret_cast<T*>(p.out) + bh * kHD + d0, o);
 }
 
-static void decode_split_plan(int B, int Hkv, int64_t max_kv_len, int* splits, int* chunk) {
+// Split the valid prefix [0, L) into chunks (multiples of `step`) so that the
+// grid covers about two CTAs per SM.  A larger step never yields more splits,
+// so the plan with the smallest step bounds the workspace of every kernel.
+static void decode_split_plan_step(int B, int Hkv, int64_t max_kv_len, int step, int* splits,
+                                   int* chunk) {
   const int64_t L = max_kv_len < 1 ? 1 : max_kv_len;
   const int target = 2 * num_sms();
   int64_t sp = (target + (int64_t)B * Hkv - 1) / ((int64_t)B * Hkv);
-  const int64_t max_sp = (L + kDecStep - 1) / kDecStep;
+  const int64_t max_sp = (L + step - 1) / step;
   if (sp > max_sp) sp = max_sp;
   if (sp < 1) sp = 1;
   int64_t ch = (L + sp - 1) / sp;
-  ch = (ch + kDecStep - 1) / kDecStep * kDecStep;
+  ch = (ch + step - 1) / step * step;
   sp = (L + ch - 1) / ch;
   *splits = (int)sp;
   *chunk = (int)ch;
 }
 
-template <typename T>
-static int launch_decode(DecodeParams& p, int G, cudaStream_t s) {
-  dim3 grid(p.splits, p.Hkv, p.B), block(kDecWarps * 32);
+static void decode_split_plan(int B, int Hkv, int64_t max_kv_len, int* splits, int* chunk) {
+  decode_split_plan_step(B, Hkv, max_kv_len, kDecStep, splits, chunk);
+}
+
+// ---------------------------------------------------------------------------
+// bf16 tensor-core variant.  The fp32 kernel above keeps the exact fp32
+// arithmetic config 1 needs; for bf16 caches the work per position (G query
+// heads x 128 dims, twice) moves to mma.sync so the kernel is HBM-bound:
+//   * a producer warp streams 64-position K and V tiles of the split's chunk
+//     with TMA (two 64-dim boxes each, 128-byte swizzle) into a 3-stage ring
+//     (32 KB per stage, full/empty mbarriers);
+//   * four consumer warps take 16 positions of each tile: S = Q K^T with the
+//     G query heads as rows 0..G-1 of the 16-row A operand (Q fragments stay
+//     in registers), online softmax per head row in fp32, then O += P V with
+//     V read by ldmatrix.trans; K is read by ldmatrix from the swizzled tile;
+//   * the warps merge (m, l, O) in shared memory and write one split-K
+//     partial (or the output when there is a single split).
+// ---------------------------------------------------------------------------
+constexpr int kTcTile = 64;                       // positions per stage
+constexpr int kTcStages = 3;
+constexpr int kTcHalfBytes = kTcTile * 128;       // one 64x64 bf16 box (8 KB)
+constexpr int kTcStageBytes = 4 * kTcHalfBytes;   // K lo/hi + V lo/hi = 32 KB
+constexpr int kTcConsumers = 4;
+constexpr int kTcThreads = (kTcConsumers + 1) * 32;
+constexpr int kTcSmem = kTcStages * kTcStageBytes + 1024 + 256;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// Byte offset of 16-byte chunk c (0..15 across the 128 dims) of row r in a
+// stage's K or V region (two 64-dim boxes, each with the 128-byte swizzle).
+__device__ __forceinline__ uint32_t kv_off(int r, int c) {
+  return (c >> 3) * kTcHalfBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+struct DecodeTcParams {
+  DecodeParams p;
+  int* err;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    DecodeTcParams prm) {
+  pdl_wait();
+  pdl_launch();
+  const DecodeParams& p = prm.p;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kTcStages * kTcStageBytes);
+  uint64_t* empty = full + kTcStages;
+  __shared__ float sm_o[kTcConsumers][G][kHD];
+  __shared__ float sm_ml[kTcConsumers][G][2];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int64_t L = p.kv_len_dev ? (int64_t)(*p.kv_len_dev) : p.kv_len;
+  const int64_t start = (int64_t)split * p.chunk;
+  const int64_t end = min64(start + p.chunk, L);
+  const int ntiles = end > start ? (int)((end - start + kTcTile - 1) / kTcTile) : 0;
+  const int64_t row_base = ((int64_t)b * p.Hkv + kvh) * p.max_seq + start;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kTcConsumers);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  __syncthreads();
+
+  if (warp == kTcConsumers) {
+    if (lane == 0) {
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % kTcStages;
+        const uint32_t ph = (i / kTcStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, prm.err, 0x401)) break;
+        uint8_t* st = ring + s * kTcStageBytes;
+        const int y = (int)(row_base + (int64_t)i * kTcTile);
+        mbar_arrive_expect_tx(&full[s], kTcStageBytes);
+        tma_load_2d(st, &tmK, &full[s], 0, y, kCacheEvictFirst);
+        tma_load_2d(st + kTcHalfBytes, &tmK, &full[s], 64, y, kCacheEvictFirst);
+        tma_load_2d(st + 2 * kTcHalfBytes, &tmV, &full[s], 0, y, kCacheEvictFirst);
+        tma_load_2d(st + 3 * kTcHalfBytes, &tmV, &full[s], 64, y, kCacheEvictFirst);
+      }
+    }
+  } else {
+    const int g = lane >> 2, t = lane & 3;
+    // Q as the A operand: row g = query head kvh*G + g (rows >= G are zero)
+    uint32_t qf[8][2];
+    {
+      const __nv_bfloat16* qh =
+          reinterpret_cast<const __nv_bfloat16*>(p.q) + ((int64_t)b * p.Hq + kvh * G + g) * kHD;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        if (g < G) {
+          qf[ks][0] = *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t);
+          qf[ks][1] = *reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t);
+        } else {
+          qf[ks][0] = qf[ks][1] = 0u;
+        }
+      }
+    }
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float o[16][2];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = 0.f;
+    float m_r = -INFINITY, l_r = 0.f;
+    const uint32_t ring_base = smem_u32(ring);
+
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % kTcStages;
+      const uint32_t ph = (i / kTcStages) & 1;
+      if (!mbar_wait(&full[s], ph, prm.err, 0x402)) break;
+      const uint32_t sK = ring_base + s * kTcStageBytes;
+      const uint32_t sV = sK + 2 * kTcHalfBytes;
+      // ---- S = Q K^T: 16 rows x 16 positions (two n-tiles of 8) ----
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t kf[4];
+        const int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = ks * 2 + ((lane >> 3) & 1);
+        ldsm_x4(kf, sK + kv_off(r, c));
+        mma_bf16_16816(sc[0], qf[ks][0], 0u, qf[ks][1], 0u, kf[0], kf[1]);
+        mma_bf16_16816(sc[1], qf[ks][0], 0u, qf[ks][1], 0u, kf[2], kf[3]);
+      }
+      // ---- mask + online softmax for row g (c0, c1 of each n-tile) ----
+      const int64_t pos0 = start + (int64_t)i * kTcTile + warp * 16;
+      float x[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int64_t pos = pos0 + j * 8 + 2 * t + e;
+          x[j * 2 + e] = (pos < end) ? sc[j][e] * sl2 : -INFINITY;
+        }
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_r, mx);
+      const float base = (m_new == -INFINITY) ? 0.f : m_new;
+      const float corr = exp2f(m_r - base);
+      float pr[4], rs = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        pr[e] = exp2f(x[e] - base);
+        rs += pr[e];
+      }
+      l_r = l_r * corr + rs;
+      m_r = m_new;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        o[d][0] *= corr;
+        o[d][1] *= corr;
+      }
+      // P as A (rows g; rows g+8 are zero): k = 16 positions of this warp
+      const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]);
+      const uint32_t pa2 = pack_bf16x2(pr[2], pr[3]);
+      // ---- O += P V ----
+#pragma unroll
+      for (int ip = 0; ip < 8; ++ip) {
+        uint32_t vf[4];
+        const int r = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int c = ip * 2 + (lane >> 4);
+        ldsm_x4_t(vf, sV + kv_off(r, c));
+        float d0[4] = {o[2 * ip][0], o[2 * ip][1], 0.f, 0.f};
+        float d1[4] = {o[2 * ip + 1][0], o[2 * ip + 1][1], 0.f, 0.f};
+        mma_bf16_16816(d0, pa0, 0u, pa2, 0u, vf[0], vf[1]);
+        mma_bf16_16816(d1, pa0, 0u, pa2, 0u, vf[2], vf[3]);
+        o[2 * ip][0] = d0[0]; o[2 * ip][1] = d0[1];
+        o[2 * ip + 1][0] = d1[0]; o[2 * ip + 1][1] = d1[1];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // row sums across the 4 lanes of a row
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
+    if (g < G) {
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        sm_o[warp][g][d * 8 + 2 * t] = o[d][0];
+        sm_o[warp][g][d * 8 + 2 * t + 1] = o[d][1];
+      }
+      if (t == 0) {
+        sm_ml[warp][g][0] = m_r;  // in log2 units
+        sm_ml[warp][g][1] = l_r;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- merge the consumer warps; write the partial or the output ----
+  for (int idx = threadIdx.x; idx < G * kHD; idx += blockDim.x) {
+    const int gg = idx / kHD, d = idx % kHD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kTcConsumers; ++w) M = fmaxf(M, sm_ml[w][gg][0]);
+    float a = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTcConsumers; ++w) {
+      const float mw = sm_ml[w][gg][0];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      a = fmaf(f, sm_o[w][gg][d], a);
+      l = fmaf(f, sm_ml[w][gg][1], l);
+    }
+    const int h = kvh * G + gg;
+    if (p.splits == 1) {
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + ((int64_t)b * p.Hq + h) * kHD;
+      out[d] = f2bf(l > 0.f ? a / l : 0.f);
+    } else {
+      const int64_t slot = ((int64_t)b * p.Hq + h) * p.splits + split;
+      p.ws_acc[slot * kHD + d] = a;
+      if (d == 0) {
+        // the combine kernel works in natural-log units
+        p.ws_ml[slot * 2 + 0] = (M == -INFINITY) ? -INFINITY : M * 0.6931471805599453f;
+        p.ws_ml[slot * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+static void decode_split_plan_step(int B, int Hkv, int64_t max_kv_len, int step, int* splits,
+                                   int* chunk);
+
+static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s) {
+  void (*kern)(const CUtensorMap, const CUtensorMap, DecodeTcParams) = nullptr;
+  int gi = 0;
   switch (G) {
-    case 1: attn_decode_kernel<T, 1><<<grid, block, 0, s>>>(p); break;
-    case 2: attn_decode_kernel<T, 2><<<grid, block, 0, s>>>(p); break;
-    case 4: attn_decode_kernel<T, 4><<<grid, block, 0, s>>>(p); break;
-    case 8: attn_decode_kernel<T, 8><<<grid, block, 0, s>>>(p); break;
+    case 1: kern = attn_decode_tc_kernel<1>; gi = 0; break;
+    case 2: kern = attn_decode_tc_kernel<2>; gi = 1; break;
+    case 4: kern = attn_decode_tc_kernel<4>; gi = 2; break;
+    case 8: kern = attn_decode_tc_kernel<8>; gi = 3; break;
     default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
   }
-  Q3_LAUNCH_CHECK();
+  static int per_sm_cache[64][4] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool cacheable = dev >= 0 && dev < 64;
+  if (!cacheable || per_sm_cache[dev][gi] == 0) {
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kTcSmem));
+    int per_sm = 0;
+    Q3_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTcThreads,
+                                                                kTcSmem));
+    if (cacheable) per_sm_cache[dev][gi] = per_sm > 0 ? per_sm : 1;
+  }
+  const int per_sm = cacheable ? per_sm_cache[dev][gi] : 1;
+  // One wave: at most (resident CTAs per SM x SMs) CTAs, and never more splits
+  // than the workspace was sized for (two CTAs per SM, 16-position chunks).
+  int64_t slots = (int64_t)per_sm * num_sms();
+  if (slots > 2 * (int64_t)num_sms()) slots = 2 * (int64_t)num_sms();
+  const int64_t pairs = (int64_t)p.B * p.Hkv;
+  const int64_t L = p.kv_len < 1 ? 1 : p.kv_len;
+  int64_t sp = slots / pairs;
+  const int64_t max_sp = (L + kTcTile - 1) / kTcTile;
+  if (sp > max_sp) sp = max_sp;
+  if (sp < 1) sp = 1;
+  int64_t ch = (L + sp - 1) / sp;
+  ch = (ch + kTcTile - 1) / kTcTile * kTcTile;
+  sp = (L + ch - 1) / ch;
+  if (sp > 1 && (p.splits <= 1 || sp > p.splits))
+    return fail(Q3_ERR_INVALID, "q3_attn_decode: internal split plan mismatch");
+  p.splits = (int)sp;
+  p.chunk = (int)ch;
+  if (sp > 1) p.ws_ml = p.ws_acc + (size_t)p.B * p.Hq * sp * kHD;
+  CUtensorMap tk, tv;
+  const int64_t rows = (int64_t)p.B * p.Hkv * p.max_seq;
+  int rc = cached_tmap_2d(&tk, p.k, rows, kHD, kTcTile, 64);
+  if (rc) return rc;
+  rc = cached_tmap_2d(&tv, p.v, rows, kHD, kTcTile, 64);
+  if (rc) return rc;
+  DecodeTcParams prm{p, device_error_word()};
+  rc = launch_ex(kern, dim3(p.splits, p.Hkv, p.B), dim3(kTcThreads), kTcSmem, s, 1, tk, tv, prm);
+  if (rc) return rc;
   if (p.splits > 1) {
     const int warps = 4;
     const int64_t n = (int64_t)p.B * p.Hq;
-    attn_decode_combine<T><<<(unsigned)((n + warps - 1) / warps), warps * 32, 0, s>>>(p);
-    Q3_LAUNCH_CHECK();
+    rc = launch_ex(attn_decode_combine<__nv_bfloat16>, dim3((unsigned)((n + warps - 1) / warps)),
+                   dim3(warps * 32), 0, s, 1, p);
+    if (rc) return rc;
+  }
+  return Q3_OK;
+}
+
+template <typename T>
+static int launch_decode(DecodeParams& p, int G, cudaStream_t s) {
+  if constexpr (sizeof(T) == 2) return launch_decode_tc(p, G, s);
+  dim3 grid(p.splits, p.Hkv, p.B), block(kDecWarps * 32);
+  int rc = Q3_OK;
+  switch (G) {
+    case 1: rc = launch_ex(attn_decode_kernel<T, 1>, grid, block, 0, s, 1, p); break;
+    case 2: rc = launch_ex(attn_decode_kernel<T, 2>, grid, block, 0, s, 1, p); break;
+    case 4: rc = launch_ex(attn_decode_kernel<T, 4>, grid, block, 0, s, 1, p); break;
+    case 8: rc = launch_ex(attn_decode_kernel<T, 8>, grid, block, 0, s, 1, p); break;
+    default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
+  }
+  if (rc) return rc;
+  if (p.splits > 1) {
+    const int warps = 4;
+    const int64_t n = (int64_t)p.B * p.Hq;
+    rc = launch_ex(attn_decode_combine<T>, dim3((unsigned)((n + warps - 1) / warps)),
+                   dim3(warps * 32), 0, s, 1, p);
+    if (rc) return rc;
   }
   return Q3_OK;
 }

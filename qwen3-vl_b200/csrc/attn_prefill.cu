@@ -83,6 +83,8 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* g,
 }
 
 __global__ void __launch_bounds__(kPThreads, 1) attn_prefill_kernel(PrefillParams p) {
+  pdl_wait();
+  pdl_launch();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t sQ = smem_u32(smem_raw);
   const uint32_t sK0 = sQ + kPBM * kPD * 2;
@@ -296,7 +298,6 @@ extern "C" int q3_attn_prefill(const void* q, const void* k, const void* v, void
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((S + kPBM - 1) / kPBM, Hq, B);
-  attn_prefill_kernel<<<grid, kPThreads, kPSmem, (cudaStream_t)stream>>>(p);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(attn_prefill_kernel, grid, dim3(kPThreads), kPSmem, (cudaStream_t)stream, 1,
+                   p);
 }

@@ -37,21 +37,31 @@ int num_sms() {
   return cached[dev];
 }
 
-// One error word per device, allocated on first use with that device current.
+// The error word is a static device variable (one per device that loads the
+// library, zero-initialised at module load); host code looks its address up
+// once per device, so no entry point ever allocates device memory for it.
+static __device__ int g_error_word = 0;
+
 int* device_error_word() {
   static int* words[64] = {nullptr};
   static std::mutex mu;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
   if (!words[dev]) {
-    int* p = nullptr;
-    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
-    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) return nullptr;
-    words[dev] = p;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) return nullptr;
+    words[dev] = static_cast<int*>(p);
   }
   return words[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("Q3VL_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 }  // namespace q3

@@ -55,6 +55,58 @@ int num_sms();  // cached SM count of the current device
 // cleared by q3_device_error().
 int* device_error_word();
 
+// 2-D bf16 row-major [rows, cols] tensor map, box of box_rows x box_cols
+// elements, 128-byte swizzle (box_cols * 2 must be 128).  The cached variant
+// keeps one map per (pointer, shape, box) for weights, whose addresses are
+// stable; activation maps are rebuilt per call.
+int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                 int box_cols);
+int cached_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                   int box_cols);
+
+// Programmatic dependent launch: when enabled (default; Q3VL_PDL=0 disables),
+// every kernel is launched with programmatic stream serialization so it can
+// be scheduled while its predecessor drains.  Kernels call pdl_wait() before
+// touching memory an earlier kernel produced (the wait returns once the
+// preceding grid has completed and its writes are visible; because every
+// kernel waits before it completes, completion is transitive along the
+// stream), and pdl_launch() to let the next kernel start its prologue.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+              int cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+  if (e != cudaSuccess)
+    return fail(Q3_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  return Q3_OK;
+}
+
+// Decode-shaped (M <= 16) projection, defined in gemv.cu.
+int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
+                int epilogue, cudaStream_t s);
+
 // ---------------------------------------------------------------------------
 // Device helpers
 // ---------------------------------------------------------------------------
@@ -85,6 +137,11 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ void report_timeout(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -227,6 +284,54 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
          | (1u << 10)                   // B format bf16
          | ((uint32_t)(n >> 3) << 17)   // N / 8
          | ((uint32_t)(m >> 4) << 24);  // M / 16
+}
+
+// F.silu on a bf16 tensor (model_fused.py:169): computed in fp32, rounded to bf16.
+__device__ __forceinline__ float silu_ref(float g) { return rbf(g / (1.0f + expf(-g))); }
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(addr));
+  return r;
+}
+
+// Thread-block-cluster helpers (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+__device__ __forceinline__ uint32_t map_shared_rank(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float x;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(addr));
+  return x;
 }
 
 // --------------------------- warp reductions -------------------------------

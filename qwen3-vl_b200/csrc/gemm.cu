@@ -29,194 +29,6 @@
 namespace q3 {
 
 // ===========================================================================
-// Epilogue helpers (shared by both kernels)
-// ===========================================================================
-__device__ __forceinline__ float silu_ref(float g) {
-  // F.silu on a bf16 tensor: computed in fp32, rounded to bf16
-  return rbf(g / (1.0f + expf(-g)));
-}
-
-// ===========================================================================
-// Decode kernel (M <= 16)
-// ===========================================================================
-constexpr int kGvWarps = 8;
-
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
-                                               uint32_t a2, uint32_t a3, uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-
-// Each lane (g = lane/4, t = lane%4) loads W rows g and g+8 and activation row
-// g at K offsets 8t..8t+7 of a 32-wide step.  The two mma.sync of the step use
-// elements 0-3 and 4-7 of those vectors; A and B share the same permutation
-// of K, so the dot products are unchanged.
-template <int NT, int EPI>
-__global__ void __launch_bounds__(kGvWarps * 32) gemv_kernel(
-    const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ W,
-    __nv_bfloat16* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K,
-    int k_per_cta, int ldc) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int rb = blockIdx.x;                 // 16-row block of W
-  const int kslice = blockIdx.y;
-  const int k_begin = kslice * k_per_cta;
-  const int k_end = min(K, k_begin + k_per_cta);
-  const int n_steps = (k_end - k_begin + 31) / 32;
-
-  const __nv_bfloat16* w0 = W + (int64_t)(rb * 16 + g) * K + 8 * t;
-  const __nv_bfloat16* w1 = w0 + (int64_t)8 * K;
-  const bool row0_ok = rb * 16 + g < N, row1_ok = rb * 16 + g + 8 < N;
-
-  float acc[NT][4];
-#pragma unroll
-  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-
-  constexpr int U = 4;
-  for (int s0 = warp; s0 < n_steps; s0 += kGvWarps * U) {
-    uint4 wa[U], wb[U], xa[U][NT];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int s = s0 + u * kGvWarps;
-      const int k = k_begin + s * 32;
-      const bool ok = s < n_steps && k + 8 * t < k_end;
-      wa[u] = (ok && row0_ok) ? ldg_stream(w0 + k) : make_uint4(0, 0, 0, 0);
-      wb[u] = (ok && row1_ok) ? ldg_stream(w1 + k) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int tok = n * 8 + g;
-        xa[u][n] = (ok && tok < M)
-                       ? __ldg(reinterpret_cast<const uint4*>(A + (int64_t)tok * K + k + 8 * t))
-                       : make_uint4(0, 0, 0, 0);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-#pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        mma_bf16_16816(acc[n], wa[u].x, wb[u].x, wa[u].y, wb[u].y, xa[u][n].x, xa[u][n].y);
-        mma_bf16_16816(acc[n], wa[u].z, wb[u].z, wa[u].w, wb[u].w, xa[u][n].z, xa[u][n].w);
-      }
-    }
-  }
-
-  // ---- reduce the 8 warps of the CTA ----
-  __shared__ float red[kGvWarps][NT * 4][32];
-#pragma unroll
-  for (int n = 0; n < NT; ++n)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) red[warp][n * 4 + e][lane] = acc[n][e];
-  __syncthreads();
-  __shared__ float part[NT * 4][32];
-  if (warp == 0) {
-#pragma unroll
-    for (int i = 0; i < NT * 4; ++i) {
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kGvWarps; ++w) v += red[w][i][lane];
-      part[i][lane] = v;
-    }
-  }
-  // ---- reduce across the cluster (K slices) through distributed smem ----
-  uint32_t csize = 1, crank = 0;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
-  if (csize > 1) {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                     : "memory");
-  } else {
-    __syncthreads();
-  }
-  if (crank == 0 && warp == 0) {
-    float v[NT * 4];
-#pragma unroll
-    for (int i = 0; i < NT * 4; ++i) v[i] = part[i][lane];
-    for (uint32_t r = 1; r < csize; ++r) {
-      const uint32_t local = smem_u32(&part[0][lane]);
-      uint32_t remote;
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(r));
-#pragma unroll
-      for (int i = 0; i < NT * 4; ++i) {
-        float x;
-        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(remote + i * 32 * 4));
-        v[i] += x;
-      }
-    }
-    // ---- epilogue: c0,c1 = (row g, tokens 2t,2t+1); c2,c3 = (row g+8, ...) ----
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int tok0 = n * 8 + 2 * t;
-      if (EPI == Q3_EPI_SWIGLU) {
-        // rows g and g+8 of the block are gate and up of feature rb*8+g
-        const int f = rb * 8 + g;
-        if (f < N / 2) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int tok = tok0 + e;
-            if (tok < M) {
-              const float gt = rbf(v[n * 4 + e]), up = rbf(v[n * 4 + 2 + e]);
-              C[(int64_t)tok * ldc + f] = f2bf(silu_ref(gt) * up);
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = rb * 16 + g + (e >= 2 ? 8 : 0);
-          const int tok = tok0 + (e & 1);
-          if (tok < M && row < N) {
-            float val = rbf(v[n * 4 + e]);
-            if (EPI == Q3_EPI_RESIDUAL) val = bf2f(R[(int64_t)tok * ldc + row]) + val;
-            C[(int64_t)tok * ldc + row] = f2bf(val);
-          }
-        }
-      }
-    }
-  }
-  if (csize > 1) {
-    // keep this CTA's shared memory alive until rank 0 has read it
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                     : "memory");
-  }
-}
-
-template <int NT, int EPI>
-static int launch_gemv(const __nv_bfloat16* A, const __nv_bfloat16* W, __nv_bfloat16* C,
-                       const __nv_bfloat16* R, int M, int N, int K, cudaStream_t s) {
-  const int nrb = (N + 15) / 16;
-  const int target = 2 * num_sms();
-  int ks = 1;
-  while (ks < 8 && nrb * ks < target && K / (ks * 2) >= 256) ks *= 2;
-  int kpc = (K + ks - 1) / ks;
-  kpc = (kpc + 31) / 32 * 32;
-  const int ldc = (EPI == Q3_EPI_SWIGLU) ? N / 2 : N;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nrb, ks, 1);
-  cfg.blockDim = dim3(kGvWarps * 32, 1, 1);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = ks;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  Q3_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemv_kernel<NT, EPI>, A, W, C, R, M, N, K, kpc, ldc));
-  return Q3_OK;
-}
-
 // ===========================================================================
 // tcgen05 kernel (M > 16)
 // ===========================================================================
@@ -246,6 +58,8 @@ template <int BN, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    TcParams p) {
+  pdl_wait();
+  pdl_launch();
   using Cfg = TcCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -427,85 +241,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Host side: tensor maps (cached) and launch
+// Host side: launch
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// 2-D bf16 [rows, cols] row-major tensor map with a box of box_rows x 64 and
-// the 128-byte swizzle.
-static int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
-                     int box_rows) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return Q3_OK;
-}
-
-struct TmapKey {
-  const void* p;
-  int64_t rows, cols;
-  int box;
-  bool operator==(const TmapKey& o) const {
-    return p == o.p && rows == o.rows && cols == o.cols && box == o.box;
-  }
-};
-struct TmapKeyHash {
-  size_t operator()(const TmapKey& k) const {
-    return std::hash<const void*>()(k.p) ^ (size_t)(k.rows * 1315423911ll) ^
-           (size_t)(k.cols * 2654435761ll) ^ (size_t)k.box;
-  }
-};
-// Weight tensor maps are built once per (pointer, shape); activation maps are
-// rebuilt every call (their pointers come from the caching allocator).
-static int cached_tmap(CUtensorMap* out, const void* base, int64_t rows, int64_t cols, int box) {
-  static std::mutex mu;
-  static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
-  TmapKey key{base, rows, cols, box};
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) { *out = it->second; return Q3_OK; }
-  }
-  int rc = make_tmap(out, base, rows, cols, box);
-  if (rc != Q3_OK) return rc;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cache.size() > 4096) cache.clear();
-  cache[key] = *out;
-  return Q3_OK;
-}
-
 template <int BN, int EPI>
 static int launch_tc(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
                      cudaStream_t s) {
   using Cfg = TcCfg<BN>;
   CUtensorMap ta, tw;
-  int rc = make_tmap(&ta, A, M, K, kBM);
+  int rc = make_tmap_2d(&ta, A, M, K, kBM, kBK);
   if (rc) return rc;
-  rc = cached_tmap(&tw, W, N, K, BN);
+  rc = cached_tmap_2d(&tw, W, N, K, BN, kBK);
   if (rc) return rc;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -525,9 +270,8 @@ static int launch_tc(const void* A, const void* W, void* C, const void* R, int M
   p.err = device_error_word();
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_tc_kernel<BN, EPI><<<grid, kTcThreads, Cfg::kSmem, s>>>(ta, tw, p);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kTcThreads), Cfg::kSmem, s, 1, ta,
+                   tw, p);
 }
 
 }  // namespace q3
@@ -547,26 +291,8 @@ extern "C" int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t
              "q3_gemm: pointers must be 16-byte aligned");
   if (M == 0) return Q3_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  auto a = (const __nv_bfloat16*)A;
-  auto w = (const __nv_bfloat16*)W;
-  auto c = (__nv_bfloat16*)C;
-  auto r = (const __nv_bfloat16*)aux;
   const int m = (int)M, n = (int)N, k = (int)K;
-  if (M <= 16) {
-    const bool two = M > 8;
-    switch (epilogue) {
-      case Q3_EPI_NONE:
-        return two ? launch_gemv<2, Q3_EPI_NONE>(a, w, c, r, m, n, k, s)
-                   : launch_gemv<1, Q3_EPI_NONE>(a, w, c, r, m, n, k, s);
-      case Q3_EPI_RESIDUAL:
-        return two ? launch_gemv<2, Q3_EPI_RESIDUAL>(a, w, c, r, m, n, k, s)
-                   : launch_gemv<1, Q3_EPI_RESIDUAL>(a, w, c, r, m, n, k, s);
-      default:
-        return two ? launch_gemv<2, Q3_EPI_SWIGLU>(a, w, c, r, m, n, k, s)
-                   : launch_gemv<1, Q3_EPI_SWIGLU>(a, w, c, r, m, n, k, s);
-    }
-  }
-  Q3_REQUIRE(K % 8 == 0, "q3_gemm: K must be a multiple of 8 for TMA");
+  if (M <= 16) return launch_gemv(A, W, C, aux, m, n, k, epilogue, s);
   switch (epilogue) {
     case Q3_EPI_NONE: return launch_tc<256, Q3_EPI_NONE>(A, W, C, aux, m, n, k, s);
     case Q3_EPI_RESIDUAL: return launch_tc<256, Q3_EPI_RESIDUAL>(A, W, C, aux, m, n, k, s);

@@ -1,0 +1,254 @@
+// Decode-shaped projections (M <= 16 tokens): C = A W^T with fused epilogues.
+//
+// Reference: the compiled matmuls of model_fused.py (:103, :141, :165-169,
+// :172, :183) at decode time, where the activation is B x 1 tokens.  Tensor
+// cores are idle at this M, so the kernel is built around HBM streaming:
+//
+//   * one CTA owns a 64-row tile of W ([N, K], K-major) over a K slice;
+//   * a producer warp issues TMA 2-D loads of 64 rows x 64 K (8 KB, 128-byte
+//     swizzle) into a 6-stage shared-memory ring guarded by mbarriers, so up
+//     to 48 KB of weights per CTA (144 KB per SM at 3 CTAs/SM) is in flight;
+//   * four consumer warps each take 16 rows and run bf16 mma.sync m16n8k16
+//     with W as the 16-row A operand and the tokens as B.  The producer loads
+//     the matching 64-wide K slice of the activations (<= 16 rows, 2 KB) into
+//     the same stage by TMA, so consumers never wait on a global load;
+//     Lane (g, t) reads the 16-byte chunks 2t+h (h = 0, 1) of rows g and g+8:
+//     with the 128-byte swizzle (chunk c of row r lives at c ^ (r % 8)) the two
+//     rows of a quarter-warp hit disjoint even/odd chunk sets, so the shared
+//     loads are bank-conflict free; A and B use the same K permutation;
+//   * K is split over the CTAs of a thread-block cluster (up to 8); partials
+//     are reduced over distributed shared memory by cluster rank 0, which runs
+//     the epilogue (plain, residual add, or SwiGLU on 8-row gate/up blocks).
+#include "common.cuh"
+
+namespace q3 {
+
+constexpr int kGvRows = 64;                 // W rows per CTA
+constexpr int kGvBK = 64;                   // K elements per stage (one 128-byte row)
+constexpr int kGvStages = 6;
+constexpr int kGvWBytes = kGvRows * kGvBK * 2;       // 8 KB of W per stage
+constexpr int kGvXBytes = 16 * kGvBK * 2;            // 2 KB of activations (<= 16 tokens)
+constexpr int kGvStageBytes = kGvWBytes + kGvXBytes;  // 1024-byte multiple
+constexpr int kGvConsumers = 4;
+constexpr int kGvThreads = (kGvConsumers + 1) * 32;
+constexpr int kGvSmem = kGvStages * kGvStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+struct GemvParams {
+  const __nv_bfloat16* A;
+  __nv_bfloat16* C;
+  const __nv_bfloat16* R;
+  int M, N, K, ldc;
+  int kb_per_cta;  // 64-wide K blocks per CTA
+  int* err;
+};
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
+    const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+    GemvParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kGvStages * kGvStageBytes);
+  uint64_t* empty = full + kGvStages;
+  __shared__ float red[kGvConsumers][NT * 4][32];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int row0 = tile * kGvRows;
+  const int kb_begin = blockIdx.y * p.kb_per_cta;
+  const int nkb_total = (p.K + kGvBK - 1) / kGvBK;
+  const int kb_end = min(nkb_total, kb_begin + p.kb_per_cta);
+  const int nkb = max(0, kb_end - kb_begin);
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGvStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGvConsumers);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  __syncthreads();
+
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  if (warp == kGvConsumers) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      constexpr uint32_t kTx = kGvWBytes + NT * 8 * kGvBK * 2;
+      // Weights never depend on the previous kernel: fill the ring with W
+      // tiles before waiting for it, then add the activation tiles.
+      const int pre = min(nkb, kGvStages);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kTx);
+        tma_load_2d(ring + i * kGvStageBytes, &tmW, &full[i], (kb_begin + i) * kGvBK, row0,
+                    kCacheEvictFirst);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(ring + i * kGvStageBytes + kGvWBytes, &tmX, &full[i],
+                    (kb_begin + i) * kGvBK, 0, kCacheEvictLast);
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % kGvStages;
+        const uint32_t ph = (i / kGvStages) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.err, 0x301)) break;
+        uint8_t* st = ring + s * kGvStageBytes;
+        mbar_arrive_expect_tx(&full[s], kTx);
+        tma_load_2d(st, &tmW, &full[s], (kb_begin + i) * kGvBK, row0, kCacheEvictFirst);
+        tma_load_2d(st + kGvWBytes, &tmX, &full[s], (kb_begin + i) * kGvBK, 0,
+                    kCacheEvictLast);
+      }
+    }
+  } else {
+    // ---------------- consumers ----------------
+    pdl_wait();  // the epilogue reads R and writes C
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    const uint32_t ring_base = smem_u32(ring);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % kGvStages;
+      const uint32_t ph = (i / kGvStages) & 1;
+      if (!mbar_wait(&full[s], ph, p.err, 0x302)) break;
+      const uint32_t base = ring_base + s * kGvStageBytes;
+      const uint32_t xbase = base + kGvWBytes;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 2 * t + h;
+        const uint4 a0 = lds128(base + r0 * 128 + ((c ^ (r0 & 7)) << 4));
+        const uint4 a1 = lds128(base + r1 * 128 + ((c ^ (r1 & 7)) << 4));
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          // token rows past M and K past the end arrive zero-filled by TMA
+          const int tok = n * 8 + g;
+          const uint4 x = lds128(xbase + tok * 128 + ((c ^ (tok & 7)) << 4));
+          mma_bf16_16816(acc[n], a0.x, a1.x, a0.y, a1.y, x.x, x.y);
+          mma_bf16_16816(acc[n], a0.z, a1.z, a0.w, a1.w, x.z, x.w);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp][n * 4 + e][lane] = acc[n][e];
+  }
+
+  // ---------------- split-K reduction over the cluster ----------------
+  const uint32_t csize = cluster_nctarank();
+  const uint32_t crank = cluster_ctarank();
+  if (csize > 1) cluster_sync_all();
+  else __syncthreads();
+  if (crank == 0 && warp < kGvConsumers) {
+    const int g = lane >> 2, t = lane & 3;
+    float v[NT * 4];
+#pragma unroll
+    for (int i = 0; i < NT * 4; ++i) v[i] = red[warp][i][lane];
+    const uint32_t local = smem_u32(&red[warp][0][lane]);
+    for (uint32_t r = 1; r < csize; ++r) {
+      const uint32_t remote = map_shared_rank(local, r);
+#pragma unroll
+      for (int i = 0; i < NT * 4; ++i) v[i] += ld_shared_cluster_f32(remote + i * 32 * 4);
+    }
+    // c0,c1 = (row g, tokens 2t, 2t+1); c2,c3 = (row g+8, tokens 2t, 2t+1)
+    const int rbase = row0 + warp * 16;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int tok0 = n * 8 + 2 * t;
+      if (EPI == Q3_EPI_SWIGLU) {
+        const int f = rbase / 2 + g;  // rows g / g+8 are gate / up of feature f
+        if (rbase + g + 8 < p.N) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int tok = tok0 + e;
+            if (tok < p.M) {
+              const float gt = rbf(v[n * 4 + e]), up = rbf(v[n * 4 + 2 + e]);
+              p.C[(int64_t)tok * p.ldc + f] = f2bf(silu_ref(gt) * up);
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = rbase + g + (e >= 2 ? 8 : 0);
+          const int tok = tok0 + (e & 1);
+          if (tok < p.M && row < p.N) {
+            float val = rbf(v[n * 4 + e]);
+            if (EPI == Q3_EPI_RESIDUAL) val = bf2f(p.R[(int64_t)tok * p.ldc + row]) + val;
+            p.C[(int64_t)tok * p.ldc + row] = f2bf(val);
+          }
+        }
+      }
+    }
+  }
+  // keep every CTA's shared memory alive until rank 0 has read it
+  if (csize > 1) cluster_sync_all();
+}
+
+template <int NT, int EPI>
+static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, int M, int N,
+                         int K, cudaStream_t s) {
+  CUtensorMap tw, tx;
+  int rc = cached_tmap_2d(&tw, W, N, K, kGvRows, kGvBK);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tx, A, M, K, NT * 8, kGvBK);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(gemv_tma_kernel<NT, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem));
+    attr_set[dev] = true;
+  }
+  const int tiles = (N + kGvRows - 1) / kGvRows;
+  const int nkb = (K + kGvBK - 1) / kGvBK;
+  // Split K over a cluster as far as the grid still fits in ONE wave of
+  // resident CTAs (a second, partial wave would double the tail), keeping at
+  // least 4 K blocks per CTA.
+  static int per_sm_cache[64] = {0};
+  int per_sm = (dev >= 0 && dev < 64) ? per_sm_cache[dev] : 0;
+  if (per_sm == 0) {
+    Q3_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, gemv_tma_kernel<NT, EPI>, kGvThreads, kGvSmem));
+    if (dev >= 0 && dev < 64) per_sm_cache[dev] = per_sm;
+  }
+  const int slots = (per_sm > 0 ? per_sm : 1) * num_sms();
+  int ks = 1;
+  while (ks < 8 && tiles * ks * 2 <= slots && nkb / (ks * 2) >= 4) ks *= 2;
+  GemvParams p;
+  p.A = (const __nv_bfloat16*)A;
+  p.C = (__nv_bfloat16*)C;
+  p.R = (const __nv_bfloat16*)R;
+  p.M = M; p.N = N; p.K = K;
+  p.ldc = EPI == Q3_EPI_SWIGLU ? N / 2 : N;
+  p.kb_per_cta = (nkb + ks - 1) / ks;
+  p.err = device_error_word();
+  return launch_ex(gemv_tma_kernel<NT, EPI>, dim3(tiles, ks, 1), dim3(kGvThreads), kGvSmem, s,
+                   ks, tw, tx, p);
+}
+
+int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
+                int epilogue, cudaStream_t s) {
+  if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
+  if (K % 8 != 0) return fail(Q3_ERR_INVALID, "decode projection needs K %% 8 == 0");
+  const bool two = M > 8;
+  switch (epilogue) {
+    case Q3_EPI_NONE:
+      return two ? launch_gemv_t<2, Q3_EPI_NONE>(A, W, C, R, M, N, K, s)
+                 : launch_gemv_t<1, Q3_EPI_NONE>(A, W, C, R, M, N, K, s);
+    case Q3_EPI_RESIDUAL:
+      return two ? launch_gemv_t<2, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s)
+                 : launch_gemv_t<1, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s);
+    default:
+      return two ? launch_gemv_t<2, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s)
+                 : launch_gemv_t<1, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s);
+  }
+}
+
+}  // namespace q3

@@ -9,6 +9,8 @@ namespace q3 {
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int64_t n, int64_t hidden,
                              int64_t vocab, int* err) {
+  pdl_wait();
+  pdl_launch();
   const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (tok >= n) return;
@@ -27,6 +29,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 // One CTA per row; ties resolve to the lowest index like torch.argmax.
 __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
                                                      int64_t V, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* x = logits + row * V;
   float best = -INFINITY;
@@ -77,6 +81,8 @@ __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* __rest
 // out = bf16(a + b), the bf16 residual add of model_fused.py:269/275.
 __global__ void add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                            uint4* __restrict__ out, int64_t nvec) {
+  pdl_wait();
+  pdl_launch();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
     const uint4 x = a[i], y = b[i];
@@ -103,10 +109,8 @@ extern "C" int q3_add(const void* a, const void* b, void* out, int64_t n, q3_str
   int64_t blocks = (nvec + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
-  add_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-      (const uint4*)a, (const uint4*)b, (uint4*)out, nvec);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(add_kernel, dim3((unsigned)blocks), dim3(256), 0, (cudaStream_t)stream, 1,
+                   (const uint4*)a, (const uint4*)b, (uint4*)out, nvec);
 }
 
 extern "C" int q3_embed(const int64_t* ids, const void* table, void* out, int64_t n,
@@ -116,11 +120,9 @@ extern "C" int q3_embed(const int64_t* ids, const void* table, void* out, int64_
   Q3_REQUIRE(n >= 0 && hidden > 0 && hidden % 8 == 0 && vocab > 0, "q3_embed: bad shape");
   Q3_REQUIRE(aligned(table, 16) && aligned(out, 16) && aligned(ids, 8), "q3_embed: misaligned");
   if (n == 0) return Q3_OK;
-  embed_kernel<<<(unsigned)((n + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-      ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, n, hidden, vocab,
-      device_error_word());
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(embed_kernel, dim3((unsigned)((n + 7) / 8)), dim3(256), 0,
+                   (cudaStream_t)stream, 1, ids, (const __nv_bfloat16*)table,
+                   (__nv_bfloat16*)out, n, hidden, vocab, device_error_word());
 }
 
 extern "C" int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* out_idx,
@@ -131,8 +133,6 @@ extern "C" int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* o
              (long long)V);
   Q3_REQUIRE(aligned(logits, 16), "q3_argmax: misaligned logits");
   if (rows == 0) return Q3_OK;
-  argmax_kernel<<<(unsigned)rows, 512, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)logits, V,
-                                                                  out_idx);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(argmax_kernel, dim3((unsigned)rows), dim3(512), 0, (cudaStream_t)stream, 1,
+                   (const __nv_bfloat16*)logits, V, out_idx);
 }

@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ y, int64_t rows,
                                                       int hidden, float eps) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -125,13 +127,10 @@ extern "C" int q3_rmsnorm(const void* x, const void* add, void* h_out, const voi
   auto Y = (__nv_bfloat16*)y;
   const int hd = (int)hidden;
   if (hidden == 4096)
-    rmsnorm_kernel<16><<<grid, block, 0, s>>>(X, A, H, Wt, Y, rows, hd, eps);
-  else if (hidden == 2048)
-    rmsnorm_kernel<8><<<grid, block, 0, s>>>(X, A, H, Wt, Y, rows, hd, eps);
-  else if (hidden == 1024)
-    rmsnorm_kernel<4><<<grid, block, 0, s>>>(X, A, H, Wt, Y, rows, hd, eps);
-  else
-    rmsnorm_kernel<0><<<grid, block, 0, s>>>(X, A, H, Wt, Y, rows, hd, eps);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+    return launch_ex(rmsnorm_kernel<16>, grid, block, 0, s, 1, X, A, H, Wt, Y, rows, hd, eps);
+  if (hidden == 2048)
+    return launch_ex(rmsnorm_kernel<8>, grid, block, 0, s, 1, X, A, H, Wt, Y, rows, hd, eps);
+  if (hidden == 1024)
+    return launch_ex(rmsnorm_kernel<4>, grid, block, 0, s, 1, X, A, H, Wt, Y, rows, hd, eps);
+  return launch_ex(rmsnorm_kernel<0>, grid, block, 0, s, 1, X, A, H, Wt, Y, rows, hd, eps);
 }

@@ -28,6 +28,8 @@ __device__ __forceinline__ void store4_bf16(__nv_bfloat16* p, const float (&v)[4
 // ---------------------------------------------------------------------------
 __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs,
                             __nv_bfloat16* __restrict__ out, int64_t seq, int heads) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= seq * heads) return;
@@ -57,6 +59,8 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, const float* __
 __global__ void mrope_kernel(const int64_t* __restrict__ pos, const float* __restrict__ inv_freq,
                              int64_t n_tok, int half, int sec_h, int sec_w,
                              float* __restrict__ cos_out, float* __restrict__ sin_out) {
+  pdl_wait();
+  pdl_launch();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_tok * half) return;
   const int64_t t = i / half;
@@ -101,6 +105,8 @@ __global__ void qkv_norm_rope_kernel(
     __nv_bfloat16* __restrict__ v_out, __nv_bfloat16* __restrict__ k_cache,
     __nv_bfloat16* __restrict__ v_cache, int B, int S, int Hq, int Hkv, int64_t start_pos,
     const int32_t* __restrict__ pos_dev, int64_t max_seq, float eps) {
+  pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -168,10 +174,9 @@ extern "C" int q3_rope(const void* x, const float* cos_sin, void* out, int64_t s
   Q3_REQUIRE(aligned(x, 8) && aligned(out, 8) && aligned(cos_sin, 16), "q3_rope: misaligned");
   const int64_t rows = seq * heads;
   if (rows == 0) return Q3_OK;
-  rope_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)x, cos_sin, (__nv_bfloat16*)out, seq, heads);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(rope_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0,
+                   (cudaStream_t)stream, 1, (const __nv_bfloat16*)x, cos_sin,
+                   (__nv_bfloat16*)out, seq, heads);
 }
 
 extern "C" int q3_mrope_cos_sin(const int64_t* pos, const float* inv_freq, int64_t n_tok,
@@ -186,10 +191,9 @@ extern "C" int q3_mrope_cos_sin(const int64_t* pos, const float* inv_freq, int64
   const int half = head_dim / 2;
   const int64_t total = n_tok * half;
   if (total == 0) return Q3_OK;
-  mrope_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      pos, inv_freq, n_tok, half, sec_h, sec_w, cos_out, sin_out);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
+  return launch_ex(mrope_kernel, dim3((unsigned)((total + 255) / 256)), dim3(256), 0,
+                   (cudaStream_t)stream, 1, pos, inv_freq, n_tok, half, sec_h, sec_w, cos_out,
+                   sin_out);
 }
 
 extern "C" int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const void* k_norm_w,
@@ -218,19 +222,17 @@ extern "C" int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const voi
   dim3 grid((unsigned)((rows + 7) / 8)), block(256);
   cudaStream_t st = (cudaStream_t)stream;
   if (cs_dtype == Q3_BF16)
-    qkv_norm_rope_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(
+    return launch_ex(qkv_norm_rope_kernel<__nv_bfloat16>, grid, block, 0, st, 1,
         (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w,
         (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, cs_use_pos, cs_offset, cs_stride_b,
         (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out,
         (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, B, S, Hq, Hkv, start_pos, pos_dev,
         max_seq, eps);
   else
-    qkv_norm_rope_kernel<float><<<grid, block, 0, st>>>(
+    return launch_ex(qkv_norm_rope_kernel<float>, grid, block, 0, st, 1,
         (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w,
         (const float*)cos, (const float*)sin, cs_use_pos, cs_offset, cs_stride_b,
         (__nv_bfloat16*)q_out,
         (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, (__nv_bfloat16*)k_cache,
         (__nv_bfloat16*)v_cache, B, S, Hq, Hkv, start_pos, pos_dev, max_seq, eps);
-  Q3_LAUNCH_CHECK();
-  return Q3_OK;
 }
