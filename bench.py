@@ -126,6 +126,11 @@ def run_ours(args):
     torch.manual_seed(0)
     dec = loader_fused.random_decoder(loader_fused.QWEN3_VL_8B, rank, world, dev, seed=0,
                                       max_seq=BUCKET)
+    # In-kernel NVLink all-reduce for decode projections (opt-in: faster than
+    # GEMV + NCCL in isolation, not yet inside the full decode graph).
+    peer_ar = world > 1 and os.environ.get("Q3VL_PEER_AR", "0") == "1"
+    if peer_ar:
+        dec.enable_peer_allreduce()     # decode o_proj/down: in-kernel NVLink all-reduce
     g = torch.Generator().manual_seed(1234)
     prompt_host = torch.randint(0, 151936, (BATCH, PROMPT), generator=g).pin_memory()
     prompt = prompt_host.to(dev)
@@ -145,7 +150,7 @@ def run_ours(args):
             print(json.dumps({"profile": True, "new_tokens": args.new_tokens,
                               "steps": args.warmup + args.steps}), flush=True)
         if world > 1:
-            dec._graphs.clear()
+            dec.close()
             dist.destroy_process_group()
         return
 
@@ -265,7 +270,9 @@ def run_ours(args):
             "data": "synthetic (random-init N(0,0.02) bf16 weights, uniform random prompt ids)",
             "config": {"workload": WORKLOAD, "model": "Qwen3-VL-8B text decoder shape",
                        "global_batch": BATCH, "seq_len": PROMPT, "new_tokens": NEW_TOKENS,
-                       "parallelism": f"tp{world}", "l2": "weights > L2 (126 MB) every step"},
+                       "parallelism": f"tp{world}", "l2": "weights > L2 (126 MB) every step",
+                       "tp_allreduce": ("decode: in-kernel NVLink peer push; prefill: NCCL"
+                                        if peer_ar else ("NCCL" if world > 1 else "none"))},
             "prefill_tok_s": round(prefill_tps, 1), "decode_tok_s": round(decode_tps, 1),
             "decode_step_ms": round(dec_step_ms, 4),
             "decode_step_hbm": {"bytes": step_bytes, "achieved_gbs": round(step_gbs, 1),
@@ -286,7 +293,7 @@ def run_ours(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        dec._graphs.clear()
+        dec.close()
         dist.barrier()
         dist.destroy_process_group()
 

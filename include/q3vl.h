@@ -151,6 +151,30 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
 Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
             const void* aux, q3_stream_t stream);
 
+/* ---- a10/a11 + 8(e): row-parallel projection fused with the TP all-reduce --
+ * Replaces `x @ W` followed by dist.all_reduce(SUM) and the residual add of
+ * forward_layer (model_fused.py:265-269 for o_proj, :272-275 for down_proj).
+ * A communicator holds one device buffer per rank, opened by every peer
+ * through CUDA IPC:
+ *   q3_comm_create   allocates this rank's buffer (sized for outputs of up to
+ *                    max_cols columns) and writes its IPC handle
+ *                    (q3_comm_handle_bytes() bytes) to ipc_handle_out;
+ *   q3_comm_open_peers takes the world's handles concatenated in rank order
+ *                    (an all-gather done by the caller) and maps the peers;
+ *   q3_comm_destroy  unmaps and frees (after a device synchronize).
+ * q3_gemm_ar: C = residual + sum over ranks of (A W^T), for decode shapes
+ * (1 <= M <= 16, N % 64 == 0); every rank must make the same sequence of calls
+ * (like the reference's collectives).  Each output tile's partial is pushed
+ * to the peers from inside the kernel over NVLink and reduced in rank order,
+ * so all ranks hold identical results.  residual may be NULL. */
+Q3_API int q3_comm_handle_bytes(void);
+Q3_API int q3_comm_create(int rank, int world, int64_t max_cols, void** comm_out,
+                          void* ipc_handle_out);
+Q3_API int q3_comm_open_peers(void* comm, const void* all_handles);
+Q3_API int q3_comm_destroy(void* comm);
+Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
+                      const void* residual, void* comm, q3_stream_t stream);
+
 /* ---- a13: embedding gather and greedy argmax -----------------------------
  * Replaces embed_tokens(input_ids) (model_fused.py:281) and
  * logits.argmax(-1) (model_fused.py:310,320).  ids int64 [n]; table bf16

@@ -19,6 +19,7 @@
 //   * K is split over the CTAs of a thread-block cluster (up to 8); partials
 //     are reduced over distributed shared memory by cluster rank 0, which runs
 //     the epilogue (plain, residual add, or SwiGLU on 8-row gate/up blocks).
+#include "comm.h"
 #include "common.cuh"
 
 namespace q3 {
@@ -33,6 +34,11 @@ constexpr int kGvConsumers = 4;
 constexpr int kGvThreads = (kGvConsumers + 1) * 32;
 constexpr int kGvSmem = kGvStages * kGvStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 
+// Internal epilogue id (not part of the public enum): row-parallel partial,
+// all-reduced across the tensor-parallel ranks through peer memory, plus the
+// optional residual.
+constexpr int kEpiAllReduce = 3;
+
 struct GemvParams {
   const __nv_bfloat16* A;
   __nv_bfloat16* C;
@@ -40,7 +46,116 @@ struct GemvParams {
   int M, N, K, ldc;
   int kb_per_cta;  // 64-wide K blocks per CTA
   int* err;
+  CommDev comm;    // used by kEpiAllReduce only
 };
+
+__device__ __forceinline__ void consumer_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kGvConsumers * 32) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// All-reduce epilogue of one 64-column tile, run by the 128 consumer threads
+// of cluster rank 0.  part[col][tok] holds this rank's partial, already
+// rounded to bf16 like the reference's projection output.
+//
+// Protocol (one-shot, aggregated per rank): every tile CTA pushes its 2 KB
+// partial into every peer's inbox (parity f & 1 of the call number f) and
+// counts itself in with a system-scope acq_rel atomic; the last CTA of the
+// rank to arrive -- after which all of this rank's partials are released --
+// raises ONE flag per peer to f.  Every CTA then waits (bounded) for the flags
+// of all peers, and sums the ranks' bf16 partials of its tile in fp32 in rank
+// order, so every rank stores identical values.  One flag per rank instead of
+// one per tile keeps the number of system-scope fences and remote flag writes
+// independent of N.  Flags only grow, and a peer can be at most one call ahead
+// (it cannot finish call f+1 before this rank's call f pushed), so two inbox
+// parities suffice.  counters[0] holds the last completed call number and
+// counters[1] the arrival count of the call in flight.
+__device__ __forceinline__ void allreduce_tile(const GemvParams& p, int tile, int row0,
+                                               __nv_bfloat16 (*part)[kArTokens],
+                                               uint32_t* f_s) {
+  const int tid = threadIdx.x;  // consumers are threads 0..127
+  const CommDev& cm = p.comm;
+  if (tid == 0) *f_s = ld_relaxed_sys(cm.counters) + 1u;
+  consumer_bar();
+  const uint32_t f = *f_s;
+  const int par = (int)(f & 1u);
+  const size_t slot_self = ((size_t)(par * kMaxRanks + cm.rank) * cm.max_tiles + tile) *
+                           kArTileElems;
+  const uint4* src = reinterpret_cast<const uint4*>(&part[0][0]);
+  for (int r = 0; r < cm.world; ++r) {
+    if (r == cm.rank) continue;
+    uint4* dst = reinterpret_cast<uint4*>(cm.data[r] + slot_self);
+    for (int i = tid; i < kArTileElems / 8; i += kGvConsumers * 32) dst[i] = src[i];
+  }
+  // The CTA barrier orders every thread's peer stores before thread 0's
+  // system-scope fence and arrival (fences are cumulative).
+  consumer_bar();
+  if (tid == 0) {
+    fence_acq_rel_sys();
+    const uint32_t arrived = atom_add_acq_rel_sys(cm.counters + 1, 1u);
+    if (arrived == gridDim.x - 1) {  // last tile CTA of this rank
+      cm.counters[1] = 0u;
+      cm.counters[0] = f;
+      fence_acq_rel_sys();
+      for (int r = 0; r < cm.world; ++r)
+        if (r != cm.rank) st_release_sys(cm.flags[r] + (size_t)cm.rank * cm.max_tiles, f);
+    }
+  }
+  if (tid < cm.world && tid != cm.rank) {
+    // poll with relaxed loads; one acquire fence once the flag has arrived
+    const uint32_t* fl = cm.flags[cm.rank] + (size_t)tid * cm.max_tiles;
+    if ((int)(ld_relaxed_sys(fl) - f) < 0) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while ((int)(ld_relaxed_sys(fl) - f) < 0) {
+        if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+          report_timeout(p.err, 0x501);
+          break;
+        }
+      }
+    }
+    fence_acq_rel_sys();
+  }
+  consumer_bar();
+  for (int idx = tid; idx < kArTileElems; idx += kGvConsumers * 32) {
+    const int col = idx / kArTokens, tok = idx % kArTokens;
+    const int n = row0 + col;
+    if (tok >= p.M || n >= p.N) continue;
+    float s = 0.f;
+    for (int r = 0; r < cm.world; ++r) {
+      if (r == cm.rank) {
+        s += bf2f(part[col][tok]);
+      } else {
+        const size_t slot = ((size_t)(par * kMaxRanks + r) * cm.max_tiles + tile) *
+                            kArTileElems;
+        // written by the peer over NVLink after this kernel started: bypass L1
+        const unsigned short raw = __ldcg(reinterpret_cast<const unsigned short*>(
+            cm.data[cm.rank] + slot + idx));
+        s += __uint_as_float((uint32_t)raw << 16);
+      }
+    }
+    float val = rbf(s);
+    if (p.R) val = bf2f(p.R[(int64_t)tok * p.ldc + n]) + val;
+    p.C[(int64_t)tok * p.ldc + n] = f2bf(val);
+  }
+}
 
 template <int NT, int EPI>
 __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
@@ -61,7 +176,10 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
   const int kb_end = min(nkb_total, kb_begin + p.kb_per_cta);
   const int nkb = max(0, kb_end - kb_begin);
 
-  pdl_launch();
+  // Let the next kernel start its prologue early -- except around the
+  // all-reduce, whose cross-GPU exchange is latency-critical: there the
+  // dependents start when the CTAs exit.
+  if constexpr (EPI != kEpiAllReduce) pdl_launch();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGvStages; ++s) {
       mbar_init(&full[s], 1);
@@ -157,10 +275,26 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
     }
     // c0,c1 = (row g, tokens 2t, 2t+1); c2,c3 = (row g+8, tokens 2t, 2t+1)
     const int rbase = row0 + warp * 16;
+    if constexpr (EPI == kEpiAllReduce) {
+      __shared__ __align__(16) __nv_bfloat16 part[kArCols][kArTokens];
+      __shared__ uint32_t f_s;
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = warp * 16 + g + (e >= 2 ? 8 : 0);
+          const int tok = n * 8 + 2 * t + (e & 1);
+          part[col][tok] = f2bf((n < NT) ? v[(n < NT ? n : 0) * 4 + e] : 0.f);
+        }
+      consumer_bar();
+      allreduce_tile(p, tile, row0, part, &f_s);
+    }
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       const int tok0 = n * 8 + 2 * t;
-      if (EPI == Q3_EPI_SWIGLU) {
+      if (EPI == kEpiAllReduce) {
+        // handled above
+      } else if (EPI == Q3_EPI_SWIGLU) {
         const int f = rbase / 2 + g;  // rows g / g+8 are gate / up of feature f
         if (rbase + g + 8 < p.N) {
 #pragma unroll
@@ -192,7 +326,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
 
 template <int NT, int EPI>
 static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, int M, int N,
-                         int K, cudaStream_t s) {
+                         int K, cudaStream_t s, const CommDev* comm = nullptr) {
   CUtensorMap tw, tx;
   int rc = cached_tmap_2d(&tw, W, N, K, kGvRows, kGvBK);
   if (rc) return rc;
@@ -221,6 +355,11 @@ static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, i
   const int slots = (per_sm > 0 ? per_sm : 1) * num_sms();
   int ks = 1;
   while (ks < 8 && tiles * ks * 2 <= slots && nkb / (ks * 2) >= 4) ks *= 2;
+  // The all-reduce epilogue waits on the same tile of every peer, so every
+  // CTA of the grid must be resident at once.
+  if (EPI == kEpiAllReduce && tiles * ks > slots)
+    return fail(Q3_ERR_UNSUPPORTED, "q3_gemm_ar: %d tiles exceed one wave (%d CTAs)", tiles,
+                slots);
   GemvParams p;
   p.A = (const __nv_bfloat16*)A;
   p.C = (__nv_bfloat16*)C;
@@ -229,6 +368,7 @@ static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, i
   p.ldc = EPI == Q3_EPI_SWIGLU ? N / 2 : N;
   p.kb_per_cta = (nkb + ks - 1) / ks;
   p.err = device_error_word();
+  p.comm = comm ? *comm : CommDev{};
   return launch_ex(gemv_tma_kernel<NT, EPI>, dim3(tiles, ks, 1), dim3(kGvThreads), kGvSmem, s,
                    ks, tw, tx, p);
 }
@@ -249,6 +389,17 @@ int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int
       return two ? launch_gemv_t<2, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s)
                  : launch_gemv_t<1, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s);
   }
+}
+
+}  // namespace q3
+
+namespace q3 {
+
+int launch_gemv_ar(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
+                   const CommDev& comm, cudaStream_t s) {
+  if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
+  return M > 8 ? launch_gemv_t<2, kEpiAllReduce>(A, W, C, R, M, N, K, s, &comm)
+               : launch_gemv_t<1, kEpiAllReduce>(A, W, C, R, M, N, K, s, &comm);
 }
 
 }  // namespace q3

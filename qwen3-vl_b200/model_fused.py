@@ -237,11 +237,26 @@ class Qwen3VLDecoderFused:
 
     # ----------------------------------------------------------------- comm
     def _all_reduce(self, t: torch.Tensor):
+        """model_fused.py:267,274 for shapes the in-kernel path does not cover."""
         if self.tp_size > 1:
-            if self.comm is not None:
-                self.comm.all_reduce(t)
-            else:
-                dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+
+    def enable_peer_allreduce(self, group=None, max_cols: int = 16384):
+        """Switch decode-shaped o_proj/down projections (<= 16 tokens) to the
+        fused in-kernel all-reduce over NVLink peer memory; prefill keeps
+        dist.all_reduce.  Collective: every rank must call it."""
+        if self.tp_size > 1 and self.comm is None:
+            from q3vl.comm import PeerComm
+            self.comm = PeerComm(group=group, max_cols=max_cols, device=self.device)
+            self._graphs.clear()
+        return self.comm
+
+    def close(self):
+        """Release captured graphs and the peer communicator (collective)."""
+        self._graphs.clear()
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     @property
     def _eps(self):
@@ -286,8 +301,13 @@ class Qwen3VLDecoderFused:
             ops.attn_prefill(q, kc, vc, start_pos=start_pos, causal=True, scale=self.scale,
                              out=attn.transpose(1, 2))
             attn = attn.view(T, ab.q_dim)
+        peer = self.tp_size > 1 and self.comm is not None and T <= 16
         if self.tp_size == 1:
             x2 = ops.gemm(attn, L.o_proj.weight_km, "residual", residual=x)
+            h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
+        elif peer:
+            # o_proj partial all-reduced from inside the kernel, residual fused
+            x2 = ops.gemm_ar(attn, L.o_proj.weight_km, self.comm, residual=x)
             h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
         else:
             part = ops.gemm(attn, L.o_proj.weight_km)
@@ -297,6 +317,8 @@ class Qwen3VLDecoderFused:
         act = ops.gemm(h2, mlp.gate_up_weight_il, "swiglu")
         if self.tp_size == 1:
             return ops.gemm(act, mlp.down_weight_km, "residual", residual=x2), None
+        if peer:
+            return ops.gemm_ar(act, mlp.down_weight_km, self.comm, residual=x2), None
         part2 = ops.gemm(act, mlp.down_weight_km)
         self._all_reduce(part2)
         return x2, part2

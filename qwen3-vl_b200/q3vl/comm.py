@@ -1,0 +1,56 @@
+"""Peer-memory communicator for the fused row-parallel projection + all-reduce.
+
+Each rank allocates one device buffer through the C ABI (q3_comm_create); the
+CUDA IPC handles are all-gathered over the existing torch.distributed process
+group and opened by every rank (q3_comm_open_peers), so the q3_gemm_ar kernel
+can push its partial tiles straight into the peers' memory over NVLink.
+torch.distributed is used only for this one-time handle exchange.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import call
+
+
+class PeerComm:
+    def __init__(self, group=None, max_cols: int = 16384, device=None):
+        if not dist.is_initialized():
+            raise RuntimeError("PeerComm needs an initialised torch.distributed process group")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nb = int(lib.q3_comm_handle_bytes())
+        handle = (ctypes.c_char * nb)()
+        self._ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("q3_comm_create", self.rank, self.world, int(max_cols), ctypes.byref(self._ptr),
+                 handle)
+        mine = torch.tensor(bytearray(handle.raw), dtype=torch.uint8)
+        backend = dist.get_backend(group)
+        mine = mine.to(self.device) if backend == "nccl" else mine
+        every = torch.empty(self.world * nb, dtype=torch.uint8, device=mine.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        blob = bytes(every.cpu().numpy().tobytes())
+        with torch.cuda.device(self.device):
+            call("q3_comm_open_peers", self._ptr, ctypes.c_char_p(blob))
+        dist.barrier(group=group)
+        self.max_cols = max_cols
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._ptr
+
+    def close(self):
+        if self._ptr is not None and self._ptr.value:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            call("q3_comm_destroy", self._ptr)
+            self._ptr = ctypes.c_void_p()

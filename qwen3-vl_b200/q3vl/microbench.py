@@ -42,7 +42,7 @@ def _time(fn, iters, warmup, flush):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm"])
+    ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar"])
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=24576)
     ap.add_argument("--K", type=int, default=4096)
@@ -59,6 +59,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-flush", action="store_true", help="keep L2 warm between iterations")
     a = ap.parse_args(argv)
+    if a.kernel == "gemm_ar":
+        return _gemm_ar(a)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
     flush = None if a.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -101,6 +103,61 @@ def main(argv=None):
         ms = _time(lambda: ops.rmsnorm(x, w, out=y), a.iters, a.warmup, flush)
         res.update(rows=a.rows, hidden=a.hidden, ms=ms, gbs=2 * x.numel() * 2 / ms / 1e6)
     print(json.dumps(res), flush=True)
+
+
+def _gemm_ar(a):
+    """Row-parallel decode projection at TP=WORLD_SIZE (run under torchrun):
+    GEMV alone, GEMV + NCCL all-reduce, and the fused in-kernel all-reduce.
+    Back-to-back launches on one stream (no flush), median of 5 runs of
+    `iters` launches, max over ranks."""
+    import torch.distributed as dist
+
+    from q3vl.comm import PeerComm
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    comm = PeerComm(max_cols=a.N, device=dev)
+    bf = torch.bfloat16
+    x = torch.randn(a.M, a.K, device=dev).to(bf)
+    w = (torch.randn(a.N, a.K, device=dev) * 0.02).to(bf)
+    r = torch.randn(a.M, a.N, device=dev).to(bf)
+    out = torch.empty(a.M, a.N, dtype=bf, device=dev)
+
+    def plain():
+        ops.gemm(x, w, out=out)
+
+    def nccl():
+        ops.gemm(x, w, out=out)
+        dist.all_reduce(out)
+
+    def fused():
+        ops.gemm_ar(x, w, comm, residual=r, out=out)
+
+    res = {"kernel": "gemm_ar", "M": a.M, "N": a.N, "K": a.K, "world": world}
+    for name, fn in (("gemv_us", plain), ("gemv_nccl_us", nccl), ("gemm_ar_us", fused)):
+        for _ in range(a.warmup):
+            fn()
+        ts = []
+        for _ in range(5):
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / a.iters)
+        t = torch.tensor([sorted(ts)[2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(float(t), 2)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    comm.close()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -249,6 +249,25 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none", residual: tor
     return out
 
 
+def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
+            out: torch.Tensor = None) -> torch.Tensor:
+    """C = residual + all_reduce_sum(a @ w.T) over the communicator's ranks
+    (decode shapes: a has 1..16 rows).  Every rank must call this in the same
+    order, as with a collective."""
+    _cuda("gemm_ar", a, w, residual, out)
+    _bf16("gemm_ar", a, w, residual, out)
+    _contig("gemm_ar", a, w, residual, out)
+    K = a.shape[-1]
+    N = w.shape[0]
+    M = a.numel() // K
+    if out is None:
+        out = torch.empty(*a.shape[:-1], N, dtype=torch.bfloat16, device=a.device)
+    if residual is not None and residual.numel() != M * N:
+        raise ValueError("gemm_ar: residual must be [M, N]")
+    call("q3_gemm_ar", _p(a), _p(w), _p(out), M, N, K, _p(residual), comm.handle, _stream())
+    return out
+
+
 # ----------------------------------------------------------------------------
 # embedding / argmax
 # ----------------------------------------------------------------------------
