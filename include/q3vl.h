@@ -47,7 +47,8 @@ enum q3_dtype { Q3_F32 = 0, Q3_BF16 = 1 };
 enum q3_epilogue {
   Q3_EPI_NONE = 0,     /* C = A W^T                                          */
   Q3_EPI_RESIDUAL = 1, /* C = bf16(R + bf16(A W^T)); R = aux [M,N]           */
-  Q3_EPI_SWIGLU = 2    /* W rows interleaved gate/up in blocks of 128;
+  Q3_EPI_SWIGLU = 2    /* W rows interleaved gate/up in blocks of 8 (rows
+                          16j..16j+7 = gate 8j..8j+7, 16j+8..16j+15 = up);
                           C[M, N/2] = silu(gate) * up                          */
 };
 
@@ -150,6 +151,29 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
  * the HBM-streaming decode kernel, larger M the tcgen05/TMEM kernel. */
 Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
             const void* aux, q3_stream_t stream);
+
+/* Decode projection with the preceding RMSNorm fused in: C = epilogue(
+ * rmsnorm(A; norm_w, eps) W^T) for 1 <= M <= 16, where rmsnorm is
+ * model_fused.py:37-40 over the full row of A (the input norm of
+ * AttentionBlock, :97-100, before h @ Wqkv; the post-attention norm of
+ * MLPBlock, :159-162, before h @ Wgate_up).  Saves the separate norm kernel
+ * and its activation round trip on every decode layer. */
+Q3_API int q3_gemm_norm(const void* A, const void* norm_w, float eps, const void* W, void* C,
+                        int64_t M, int64_t N, int64_t K, int epilogue, const void* aux,
+                        q3_stream_t stream);
+
+/* General decode projection (1 <= M <= 16) with the fusions of one decoder
+ * layer: C = epilogue(norm(A) W^T) where norm is the RMSNorm above when
+ * norm_w != NULL (else identity).  The norm's per-token sum of squares is
+ * either recomputed from A or, when ss_in != NULL, summed (in a fixed order)
+ * from ss_tiles partials ss_in[ss_tiles][16].  With the residual epilogue,
+ * ss_out != NULL receives those partials for the stored outputs,
+ * ss_out[ceil(N/64)][16], so the next projection can normalise C without
+ * re-reading it.  (The o_proj residual output feeds the post-attention norm
+ * of gate/up; the down residual output feeds the next layer's input norm.) */
+Q3_API int q3_gemm_decode(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
+                          int epilogue, const void* aux, const void* norm_w, float eps,
+                          const float* ss_in, int ss_tiles, float* ss_out, q3_stream_t stream);
 
 /* ---- a10/a11 + 8(e): row-parallel projection fused with the TP all-reduce --
  * Replaces `x @ W` followed by dist.all_reduce(SUM) and the residual add of

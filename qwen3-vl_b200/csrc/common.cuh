@@ -103,9 +103,19 @@ int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   return Q3_OK;
 }
 
-// Decode-shaped (M <= 16) projection, defined in gemv.cu.
+// Decode-shaped (M <= 16) projection, defined in gemv.cu.  Options: a fused
+// input RMSNorm (norm_w, eps), optionally from precomputed per-tile sums of
+// squares (ss_in, ss_tiles), and, for the residual epilogue, per-tile sums of
+// squares of the outputs for the next projection's norm (ss_out).
+struct GemvOpts {
+  const void* norm_w = nullptr;
+  float eps = 0.f;
+  const float* ss_in = nullptr;
+  int ss_tiles = 0;
+  float* ss_out = nullptr;
+};
 int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                int epilogue, cudaStream_t s);
+                int epilogue, cudaStream_t s, const GemvOpts& opts = GemvOpts());
 
 // ---------------------------------------------------------------------------
 // Device helpers

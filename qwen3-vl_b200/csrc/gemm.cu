@@ -299,3 +299,51 @@ extern "C" int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t
     default: return launch_tc<256, Q3_EPI_SWIGLU>(A, W, C, aux, m, n, k, s);
   }
 }
+
+extern "C" int q3_gemm_norm(const void* A, const void* norm_w, float eps, const void* W, void* C,
+                            int64_t M, int64_t N, int64_t K, int epilogue, const void* aux,
+                            q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && norm_w && W && C, "q3_gemm_norm: null pointer");
+  Q3_REQUIRE(M >= 1 && M <= 16, "q3_gemm_norm: M=%lld outside [1, 16] (decode shapes)",
+             (long long)M);
+  Q3_REQUIRE(N > 0 && N % 16 == 0 && K > 0 && K % 32 == 0 && N < (1ll << 31) && K < (1ll << 31),
+             "q3_gemm_norm: bad shape N=%lld K=%lld", (long long)N, (long long)K);
+  Q3_REQUIRE(epilogue == Q3_EPI_NONE || epilogue == Q3_EPI_RESIDUAL || epilogue == Q3_EPI_SWIGLU,
+             "q3_gemm_norm: unknown epilogue %d", epilogue);
+  Q3_REQUIRE(epilogue != Q3_EPI_RESIDUAL || aux, "q3_gemm_norm: residual epilogue needs aux");
+  Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(C, 16) && aligned(norm_w, 16) &&
+                 (!aux || aligned(aux, 16)),
+             "q3_gemm_norm: pointers must be 16-byte aligned");
+  GemvOpts o;
+  o.norm_w = norm_w;
+  o.eps = eps;
+  return launch_gemv(A, W, C, aux, (int)M, (int)N, (int)K, epilogue, (cudaStream_t)stream, o);
+}
+
+extern "C" int q3_gemm_decode(const void* A, const void* W, void* C, int64_t M, int64_t N,
+                              int64_t K, int epilogue, const void* aux, const void* norm_w,
+                              float eps, const float* ss_in, int ss_tiles, float* ss_out,
+                              q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && W && C, "q3_gemm_decode: null pointer");
+  Q3_REQUIRE(M >= 1 && M <= 16, "q3_gemm_decode: M=%lld outside [1, 16]", (long long)M);
+  Q3_REQUIRE(N > 0 && N % 16 == 0 && K > 0 && K % 32 == 0 && N < (1ll << 31) && K < (1ll << 31),
+             "q3_gemm_decode: bad shape N=%lld K=%lld", (long long)N, (long long)K);
+  Q3_REQUIRE(epilogue == Q3_EPI_NONE || epilogue == Q3_EPI_RESIDUAL || epilogue == Q3_EPI_SWIGLU,
+             "q3_gemm_decode: unknown epilogue %d", epilogue);
+  Q3_REQUIRE(epilogue != Q3_EPI_RESIDUAL || aux, "q3_gemm_decode: residual epilogue needs aux");
+  Q3_REQUIRE(!ss_in || (norm_w && ss_tiles > 0), "q3_gemm_decode: ss_in needs norm_w, ss_tiles");
+  Q3_REQUIRE(!ss_out || epilogue == Q3_EPI_RESIDUAL,
+             "q3_gemm_decode: ss_out is produced by the residual epilogue only");
+  Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(C, 16) &&
+                 (!norm_w || aligned(norm_w, 16)) && (!aux || aligned(aux, 16)),
+             "q3_gemm_decode: pointers must be 16-byte aligned");
+  GemvOpts o;
+  o.norm_w = norm_w;
+  o.eps = eps;
+  o.ss_in = ss_in;
+  o.ss_tiles = ss_tiles;
+  o.ss_out = ss_out;
+  return launch_gemv(A, W, C, aux, (int)M, (int)N, (int)K, epilogue, (cudaStream_t)stream, o);
+}

@@ -18,7 +18,12 @@
 //     loads are bank-conflict free; A and B use the same K permutation;
 //   * K is split over the CTAs of a thread-block cluster (up to 8); partials
 //     are reduced over distributed shared memory by cluster rank 0, which runs
-//     the epilogue (plain, residual add, or SwiGLU on 8-row gate/up blocks).
+//     the epilogue (plain, residual add, or SwiGLU on 8-row gate/up blocks);
+//   * optional fusions, chosen at compile time so the plain kernel keeps its
+//     short inner loop: the RMSNorm that precedes the projection (a sixth,
+//     normaliser warp rescales each staged activation tile in shared memory
+//     once, between the TMA landing and the consumers), and, after a residual
+//     epilogue, per-tile sums of squares of the outputs for the next norm.
 #include "comm.h"
 #include "common.cuh"
 
@@ -31,8 +36,16 @@ constexpr int kGvWBytes = kGvRows * kGvBK * 2;       // 8 KB of W per stage
 constexpr int kGvXBytes = 16 * kGvBK * 2;            // 2 KB of activations (<= 16 tokens)
 constexpr int kGvStageBytes = kGvWBytes + kGvXBytes;  // 1024-byte multiple
 constexpr int kGvConsumers = 4;
-constexpr int kGvThreads = (kGvConsumers + 1) * 32;
 constexpr int kGvSmem = kGvStages * kGvStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+// Compile-time fusion flags of gemv_tma_kernel.
+constexpr int kFlNorm = 1;   // RMSNorm of the activations (normaliser warp)
+constexpr int kFlSsOut = 2;  // residual epilogue: per-tile output sums of squares
+
+// warps: consumers, the TMA producer, and with kFlNorm the normaliser
+__host__ __device__ constexpr int gv_threads(int fl) {
+  return (kGvConsumers + 1 + ((fl & kFlNorm) ? 1 : 0)) * 32;
+}
 
 // Internal epilogue id (not part of the public enum): row-parallel partial,
 // all-reduced across the tensor-parallel ranks through peer memory, plus the
@@ -47,7 +60,31 @@ struct GemvParams {
   int kb_per_cta;  // 64-wide K blocks per CTA
   int* err;
   CommDev comm;    // used by kEpiAllReduce only
+  // Fused input RMSNorm (model_fused.py:37-40) when norm_w != nullptr: the
+  // activations are normalised on the fly, x -> bf16(bf16(x * rsqrt(mean(x^2)
+  // + eps)) * norm_w), with the per-token rsqrt computed over the full row.
+  const __nv_bfloat16* norm_w;
+  float eps;
+  // When ss_in is set, the per-token sum of squares of A comes precomputed as
+  // ss_tiles partial sums [ss_tiles][16] (written by the kernel that produced
+  // A, see ss_out) instead of being recomputed from the rows of A.
+  const float* ss_in;
+  int ss_tiles;
+  // Residual epilogue only: per-tile partial sums of squares of the stored
+  // (bf16) outputs, [gridDim.x][16], for the RMSNorm of the next projection.
+  float* ss_out;
 };
+
+__device__ __forceinline__ uint4 rms_scale_chunk(uint4 x, float r, uint4 w) {
+  uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(xs[i]), g = unpack_bf16x2(ws[i]);
+    xs[i] = pack_bf16x2(rbf(f.x * r) * g.x, rbf(f.y * r) * g.y);
+  }
+  return make_uint4(xs[0], xs[1], xs[2], xs[3]);
+}
 
 __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kGvConsumers * 32) : "memory");
@@ -157,15 +194,91 @@ __device__ __forceinline__ void allreduce_tile(const GemvParams& p, int tile, in
   }
 }
 
-template <int NT, int EPI>
-__global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Normaliser warp of the fused-RMSNorm projection: computes every token's
+// inverse RMS (from the producer kernel's per-tile sums of squares, or from
+// the rows of A), then, for each ring stage, rescales the staged activation
+// tile in place, x -> bf16(bf16(x * r_tok) * norm_w[k]) (model_fused.py:37-40),
+// and releases the stage to the consumers through ready[s].  Lane l owns the
+// 16-byte chunk c = l % 8 (8 K elements) of token rows l / 8 + 4j.
+template <int NT>
+__device__ __forceinline__ void gemv_normaliser(const GemvParams& p, uint32_t ring_base,
+                                                uint64_t* full, uint64_t* ready, int kb_begin,
+                                                int nkb, int lane) {
+  __shared__ float rs[16];
+  pdl_wait();  // sums of squares / rows of A come from the previous kernel
+  if (p.ss_in) {
+    if (lane < p.M) {
+      float ss = 0.f;  // fixed order: tile 0, 1, ...
+      for (int t2 = 0; t2 < p.ss_tiles; ++t2) ss += p.ss_in[t2 * 16 + lane];
+      rs[lane] = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+    }
+  } else {
+    for (int tok = 0; tok < p.M; ++tok) {
+      const uint4* xr = reinterpret_cast<const uint4*>(p.A + (int64_t)tok * p.K);
+      float ss = 0.f;
+      for (int v = lane; v < p.K / 8; v += 32) {
+        const uint4 u = xr[v];
+        const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(us[j]);
+          ss = fmaf(f.x, f.x, ss);
+          ss = fmaf(f.y, f.y, ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) rs[tok] = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+    }
+  }
+  __syncwarp();
+  constexpr int kRowsPerLane = NT * 2;
+  const int c = lane & 7;
+  float r[kRowsPerLane];
+#pragma unroll
+  for (int j = 0; j < kRowsPerLane; ++j) {
+    const int tok = (lane >> 3) + 4 * j;
+    r[j] = tok < p.M ? rs[tok] : 0.f;  // rows past M stay zero
+  }
+  auto wchunk = [&](int i) {
+    const int k = (kb_begin + i) * kGvBK + c * 8;
+    return k < p.K ? __ldg(reinterpret_cast<const uint4*>(p.norm_w + k)) : make_uint4(0, 0, 0, 0);
+  };
+  uint4 wn_next = nkb > 0 ? wchunk(0) : make_uint4(0, 0, 0, 0);
+  for (int i = 0; i < nkb; ++i) {
+    const int s = i % kGvStages;
+    const uint32_t ph = (i / kGvStages) & 1;
+    const uint4 wn = wn_next;
+    if (i + 1 < nkb) wn_next = wchunk(i + 1);  // one stage ahead
+    if (!mbar_wait(&full[s], ph, p.err, 0x303)) break;
+    const uint32_t xbase = ring_base + s * kGvStageBytes + kGvWBytes;
+#pragma unroll
+    for (int j = 0; j < kRowsPerLane; ++j) {
+      const int row = (lane >> 3) + 4 * j;
+      const uint32_t addr = xbase + row * 128 + ((c ^ (row & 7)) << 4);
+      sts128(addr, rms_scale_chunk(lds128(addr), r[j], wn));
+    }
+    mbar_arrive(&ready[s]);  // all 32 lanes arrive: each lane's stores are released
+  }
+}
+
+template <int NT, int EPI, int FL>
+__global__ void __launch_bounds__(gv_threads(FL)) gemv_tma_kernel(
     const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
     GemvParams p) {
+  constexpr bool kNorm = (FL & kFlNorm) != 0;
+  constexpr bool kSsOut = (FL & kFlSsOut) != 0 && EPI == Q3_EPI_RESIDUAL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + kGvStages * kGvStageBytes);
   uint64_t* empty = full + kGvStages;
+  uint64_t* ready = empty + kGvStages;  // kNorm: stage normalised
   __shared__ float red[kGvConsumers][NT * 4][32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -184,6 +297,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
     for (int s = 0; s < kGvStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kGvConsumers);
+      if constexpr (kNorm) mbar_init(&ready[s], 32);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tmW);
@@ -222,6 +336,9 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
                     kCacheEvictLast);
       }
     }
+  } else if (warp > kGvConsumers) {
+    // ---------------- normaliser (kNorm only) ----------------
+    if constexpr (kNorm) gemv_normaliser<NT>(p, smem_u32(ring), full, ready, kb_begin, nkb, lane);
   } else {
     // ---------------- consumers ----------------
     pdl_wait();  // the epilogue reads R and writes C
@@ -231,7 +348,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
     for (int i = 0; i < nkb; ++i) {
       const int s = i % kGvStages;
       const uint32_t ph = (i / kGvStages) & 1;
-      if (!mbar_wait(&full[s], ph, p.err, 0x302)) break;
+      if (!mbar_wait(kNorm ? &ready[s] : &full[s], ph, p.err, 0x302)) break;
       const uint32_t base = ring_base + s * kGvStageBytes;
       const uint32_t xbase = base + kGvWBytes;
 #pragma unroll
@@ -288,13 +405,10 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
         }
       consumer_bar();
       allreduce_tile(p, tile, row0, part, &f_s);
-    }
+    } else if constexpr (EPI == Q3_EPI_SWIGLU) {
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int tok0 = n * 8 + 2 * t;
-      if (EPI == kEpiAllReduce) {
-        // handled above
-      } else if (EPI == Q3_EPI_SWIGLU) {
+      for (int n = 0; n < NT; ++n) {
+        const int tok0 = n * 8 + 2 * t;
         const int f = rbase / 2 + g;  // rows g / g+8 are gate / up of feature f
         if (rbase + g + 8 < p.N) {
 #pragma unroll
@@ -306,7 +420,15 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
             }
           }
         }
-      } else {
+      }
+    } else {
+      // squares of the stored outputs, per token (2 tokens x NT per lane)
+      float sq[NT][2];
+#pragma unroll
+      for (int n = 0; n < NT; ++n) sq[n][0] = sq[n][1] = 0.f;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int tok0 = n * 8 + 2 * t;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int row = rbase + g + (e >= 2 ? 8 : 0);
@@ -314,9 +436,33 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
           if (tok < p.M && row < p.N) {
             float val = rbf(v[n * 4 + e]);
             if (EPI == Q3_EPI_RESIDUAL) val = bf2f(p.R[(int64_t)tok * p.ldc + row]) + val;
-            p.C[(int64_t)tok * p.ldc + row] = f2bf(val);
+            const __nv_bfloat16 o = f2bf(val);
+            p.C[(int64_t)tok * p.ldc + row] = o;
+            if constexpr (kSsOut) {
+              const float vr = bf2f(o);
+              sq[n][e & 1] = fmaf(vr, vr, sq[n][e & 1]);
+            }
           }
         }
+      }
+      if constexpr (kSsOut) {
+        // reduce over the 8 lanes that share t (rows g), then over the 4 warps
+        __shared__ float ssw[kGvConsumers][16];
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float x = sq[n][e];
+            x += __shfl_xor_sync(0xffffffffu, x, 4);
+            x += __shfl_xor_sync(0xffffffffu, x, 8);
+            x += __shfl_xor_sync(0xffffffffu, x, 16);
+            if (g == 0) ssw[warp][n * 8 + 2 * t + e] = x;
+          }
+        if (NT == 1 && g == 0) ssw[warp][8 + 2 * t] = ssw[warp][9 + 2 * t] = 0.f;
+        consumer_bar();
+        const int tid = warp * 32 + lane;
+        if (tid < 16)
+          p.ss_out[tile * 16 + tid] = ssw[0][tid] + ssw[1][tid] + ssw[2][tid] + ssw[3][tid];
       }
     }
   }
@@ -324,9 +470,11 @@ __global__ void __launch_bounds__(kGvThreads) gemv_tma_kernel(
   if (csize > 1) cluster_sync_all();
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, int FL>
 static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, int M, int N,
-                         int K, cudaStream_t s, const CommDev* comm = nullptr) {
+                         int K, cudaStream_t s, const CommDev* comm, const GemvOpts& o) {
+  auto kern = gemv_tma_kernel<NT, EPI, FL>;
+  constexpr int kThreads = gv_threads(FL);
   CUtensorMap tw, tx;
   int rc = cached_tmap_2d(&tw, W, N, K, kGvRows, kGvBK);
   if (rc) return rc;
@@ -336,8 +484,8 @@ static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, i
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    Q3_CUDA_CHECK(cudaFuncSetAttribute(gemv_tma_kernel<NT, EPI>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem));
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGvSmem));
     attr_set[dev] = true;
   }
   const int tiles = (N + kGvRows - 1) / kGvRows;
@@ -348,8 +496,8 @@ static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, i
   static int per_sm_cache[64] = {0};
   int per_sm = (dev >= 0 && dev < 64) ? per_sm_cache[dev] : 0;
   if (per_sm == 0) {
-    Q3_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, gemv_tma_kernel<NT, EPI>, kGvThreads, kGvSmem));
+    Q3_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads,
+                                                                kGvSmem));
     if (dev >= 0 && dev < 64) per_sm_cache[dev] = per_sm;
   }
   const int slots = (per_sm > 0 ? per_sm : 1) * num_sms();
@@ -369,37 +517,53 @@ static int launch_gemv_t(const void* A, const void* W, void* C, const void* R, i
   p.kb_per_cta = (nkb + ks - 1) / ks;
   p.err = device_error_word();
   p.comm = comm ? *comm : CommDev{};
-  return launch_ex(gemv_tma_kernel<NT, EPI>, dim3(tiles, ks, 1), dim3(kGvThreads), kGvSmem, s,
-                   ks, tw, tx, p);
+  p.norm_w = (const __nv_bfloat16*)o.norm_w;
+  p.eps = o.eps;
+  p.ss_in = o.ss_in;
+  p.ss_tiles = o.ss_tiles;
+  p.ss_out = o.ss_out;
+  return launch_ex(kern, dim3(tiles, ks, 1), dim3(kThreads), kGvSmem, s, ks, tw, tx, p);
+}
+
+template <int NT, int EPI>
+static int launch_gemv_fl(const void* A, const void* W, void* C, const void* R, int M, int N,
+                          int K, cudaStream_t s, const GemvOpts& o) {
+  if (o.norm_w) {
+    if (o.ss_out) return fail(Q3_ERR_UNSUPPORTED, "decode projection: norm_w with ss_out");
+    return launch_gemv_t<NT, EPI, kFlNorm>(A, W, C, R, M, N, K, s, nullptr, o);
+  }
+  if (o.ss_out) {
+    if constexpr (EPI == Q3_EPI_RESIDUAL)
+      return launch_gemv_t<NT, EPI, kFlSsOut>(A, W, C, R, M, N, K, s, nullptr, o);
+    return fail(Q3_ERR_INVALID, "decode projection: ss_out needs the residual epilogue");
+  }
+  return launch_gemv_t<NT, EPI, 0>(A, W, C, R, M, N, K, s, nullptr, o);
 }
 
 int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                int epilogue, cudaStream_t s) {
+                int epilogue, cudaStream_t s, const GemvOpts& o) {
   if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
   if (K % 8 != 0) return fail(Q3_ERR_INVALID, "decode projection needs K %% 8 == 0");
   const bool two = M > 8;
   switch (epilogue) {
     case Q3_EPI_NONE:
-      return two ? launch_gemv_t<2, Q3_EPI_NONE>(A, W, C, R, M, N, K, s)
-                 : launch_gemv_t<1, Q3_EPI_NONE>(A, W, C, R, M, N, K, s);
+      return two ? launch_gemv_fl<2, Q3_EPI_NONE>(A, W, C, R, M, N, K, s, o)
+                 : launch_gemv_fl<1, Q3_EPI_NONE>(A, W, C, R, M, N, K, s, o);
     case Q3_EPI_RESIDUAL:
-      return two ? launch_gemv_t<2, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s)
-                 : launch_gemv_t<1, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s);
+      return two ? launch_gemv_fl<2, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s, o)
+                 : launch_gemv_fl<1, Q3_EPI_RESIDUAL>(A, W, C, R, M, N, K, s, o);
     default:
-      return two ? launch_gemv_t<2, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s)
-                 : launch_gemv_t<1, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s);
+      return two ? launch_gemv_fl<2, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s, o)
+                 : launch_gemv_fl<1, Q3_EPI_SWIGLU>(A, W, C, R, M, N, K, s, o);
   }
 }
-
-}  // namespace q3
-
-namespace q3 {
 
 int launch_gemv_ar(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
                    const CommDev& comm, cudaStream_t s) {
   if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
-  return M > 8 ? launch_gemv_t<2, kEpiAllReduce>(A, W, C, R, M, N, K, s, &comm)
-               : launch_gemv_t<1, kEpiAllReduce>(A, W, C, R, M, N, K, s, &comm);
+  const GemvOpts o;
+  return M > 8 ? launch_gemv_t<2, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o)
+               : launch_gemv_t<1, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o);
 }
 
 }  // namespace q3

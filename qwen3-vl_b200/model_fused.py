@@ -224,6 +224,8 @@ class Qwen3VLDecoderFused:
         self._graphs = {}
         self._kv_pool = {}
         self.use_graphs = os.environ.get("Q3VL_DECODE_GRAPHS", "1") != "0"
+        # decode: RMSNorms fused into the projections that consume them
+        self.fuse_norm = os.environ.get("Q3VL_FUSE_NORM", "1") != "0"
 
     # ------------------------------------------------------------------ cache
     def init_kv_cache(self, batch_size=1):
@@ -263,22 +265,46 @@ class Qwen3VLDecoderFused:
         return self.layers[0].attn_block.eps
 
     # ----------------------------------------------------------------- layer
+    def _ss_ok(self, B: int, S: int) -> bool:
+        """True when the last layer's down projection left the sums of squares
+        of its output rows in _ss_buf(1) (the TP1 decode path)."""
+        return (B * S <= 16 and self.tp_size == 1 and self.num_layers > 0 and self.fuse_norm and
+                self.layers[-1].attn_block.qkv_bias is None)
+
+    def _ss_buf(self, i: int) -> torch.Tensor:
+        """Per-tile sums of squares handed from a residual projection to the
+        next projection's fused RMSNorm (0: after o_proj, 1: after down)."""
+        if getattr(self, "_ss", None) is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("norm buffers must exist before graph capture")
+            self._ss = torch.zeros(2, 256 * 16, dtype=torch.float32, device=self.device)
+        return self._ss[i]
+
     def _layer(self, x, pend, layer_idx, kv_cache, start_pos, S, B, rope=None, pos_dev=None,
-               kv_len_dev=None, kv_bound=None, rope_delta=0):
+               kv_len_dev=None, kv_bound=None, rope_delta=0, ss_valid=False):
         """One decoder layer on the residual stream x [T, H].  `pend` is a partial
         sum still to be added to x (TP>1 keeps the add fused with the next norm).
-        Returns (x, pend) in the same convention."""
+        `ss_valid` says the previous layer's down projection left the sums of
+        squares of x in _ss_buf(1).  Returns (x, pend) in the same convention."""
         L = self.layers[layer_idx]
         ab, mlp = L.attn_block, L.mlp_block
         H = x.shape[-1]
         T = B * S
+        decode = T <= 16
+        fast = (decode and self.tp_size == 1 and ab.qkv_bias is None and H <= 256 * 64 and
+                self.fuse_norm)
         if pend is not None:
             xn = torch.empty_like(x)
             h = ops.rmsnorm(pend, ab.input_norm_weight, ab.eps, add=x, h_out=xn)
             x = xn
+            qkv = ab.qkv(h)
+        elif decode and ab.qkv_bias is None and self.fuse_norm:
+            # decode: the input RMSNorm runs inside the QKV projection
+            ss = self._ss_buf(1) if (fast and ss_valid) else None
+            qkv = ops.gemm_decode(x, ab.qkv_weight_km, norm_w=ab.input_norm_weight, eps=ab.eps,
+                                  ss_in=ss, ss_tiles=H // 64)
         else:
-            h = ops.rmsnorm(x, ab.input_norm_weight, ab.eps)
-        qkv = ab.qkv(h)
+            qkv = ab.qkv(ops.rmsnorm(x, ab.input_norm_weight, ab.eps))
         kc, vc = kv_cache[layer_idx]
         if rope is None:
             cos, sin, _ = self.rotary.tables(self.device)
@@ -301,20 +327,37 @@ class Qwen3VLDecoderFused:
             ops.attn_prefill(q, kc, vc, start_pos=start_pos, causal=True, scale=self.scale,
                              out=attn.transpose(1, 2))
             attn = attn.view(T, ab.q_dim)
-        peer = self.tp_size > 1 and self.comm is not None and T <= 16
+        if fast:
+            # o_proj + residual (emits the sums of squares of x2), gate/up with the
+            # post-attention norm fused in, down + residual (emits them for the next
+            # layer's input norm)
+            x2 = ops.gemm_decode(attn, L.o_proj.weight_km, "residual", residual=x,
+                                 ss_out=self._ss_buf(0))
+            act = ops.gemm_decode(x2, mlp.gate_up_weight_il, "swiglu",
+                                  norm_w=mlp.post_norm_weight, eps=mlp.eps,
+                                  ss_in=self._ss_buf(0), ss_tiles=H // 64)
+            return ops.gemm_decode(act, mlp.down_weight_km, "residual", residual=x2,
+                                   ss_out=self._ss_buf(1)), None
+        peer = self.tp_size > 1 and self.comm is not None and decode
+        h2 = None
         if self.tp_size == 1:
             x2 = ops.gemm(attn, L.o_proj.weight_km, "residual", residual=x)
-            h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
         elif peer:
             # o_proj partial all-reduced from inside the kernel, residual fused
             x2 = ops.gemm_ar(attn, L.o_proj.weight_km, self.comm, residual=x)
-            h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
         else:
             part = ops.gemm(attn, L.o_proj.weight_km)
             self._all_reduce(part)
             x2 = torch.empty_like(x)
             h2 = ops.rmsnorm(part, mlp.post_norm_weight, mlp.eps, add=x, h_out=x2)
-        act = ops.gemm(h2, mlp.gate_up_weight_il, "swiglu")
+        if h2 is None and decode and self.fuse_norm:
+            # decode: the post-attention RMSNorm runs inside the gate/up projection
+            act = ops.gemm_norm(x2, mlp.post_norm_weight, mlp.gate_up_weight_il, mlp.eps,
+                                "swiglu")
+        else:
+            if h2 is None:
+                h2 = ops.rmsnorm(x2, mlp.post_norm_weight, mlp.eps)
+            act = ops.gemm(h2, mlp.gate_up_weight_il, "swiglu")
         if self.tp_size == 1:
             return ops.gemm(act, mlp.down_weight_km, "residual", residual=x2), None
         if peer:
@@ -340,16 +383,23 @@ class Qwen3VLDecoderFused:
         return ops.mrope_cos_sin(pos, inv)
 
     # --------------------------------------------------------------- logits
-    def _logits(self, x, pend, B, S, logits_out=None):
+    def _logits(self, x, pend, B, S, ss_valid=False):
         H = x.shape[-1]
         if S > 1:
             x = x.view(B, S, H)[:, -1].contiguous()
             pend = pend.view(B, S, H)[:, -1].contiguous() if pend is not None else None
+            ss_valid = False
         if pend is not None:
             h = ops.rmsnorm(pend, self.final_norm.weight, self.final_norm.eps, add=x)
+            local = ops.gemm(h, self.lm_head.weight_km)       # [B, V/tp]
+        elif B <= 16 and self.fuse_norm:
+            # final norm fused into the lm_head projection
+            ss = self._ss_buf(1) if ss_valid else None
+            local = ops.gemm_decode(x, self.lm_head.weight_km, norm_w=self.final_norm.weight,
+                                    eps=self.final_norm.eps, ss_in=ss, ss_tiles=H // 64)
         else:
             h = ops.rmsnorm(x, self.final_norm.weight, self.final_norm.eps)
-        local = ops.gemm(h, self.lm_head.weight_km)           # [B, V/tp]
+            local = ops.gemm(h, self.lm_head.weight_km)
         if self.tp_size == 1:
             return local.view(B, 1, -1)
         gathered = torch.empty(self.tp_size, B, local.shape[-1], dtype=local.dtype,
@@ -366,9 +416,11 @@ class Qwen3VLDecoderFused:
              visual_mask=None, pos_dev=None, kv_len_dev=None, kv_bound=None, rope_delta=0):
         x, pend = hidden2d, None
         for i in range(self.num_layers):
+            # layers after the first find their input norm's sums of squares
+            # left by the previous layer's down projection (decode, TP1)
             x, pend = self._layer(x, pend, i, kv_cache, start_pos, S, B, rope=rope,
                                   pos_dev=pos_dev, kv_len_dev=kv_len_dev, kv_bound=kv_bound,
-                                  rope_delta=rope_delta)
+                                  rope_delta=rope_delta, ss_valid=i > 0)
             if deepstack is not None and i < len(deepstack):
                 if pend is not None:
                     x = ops.add(x, pend)
@@ -392,7 +444,7 @@ class Qwen3VLDecoderFused:
         x = self._embed(input_ids).view(B * S, -1)
         rope = self._mrope(position_ids) if position_ids is not None else None
         x, pend = self._run(x, B, S, start_pos, kv_cache, rope=rope)
-        return self._logits(x, pend, B, S)
+        return self._logits(x, pend, B, S, ss_valid=self._ss_ok(B, S))
 
     def prefill(self, input_ids, kv_cache):
         return self.forward(input_ids, start_pos=0, kv_cache=kv_cache)
@@ -424,7 +476,7 @@ class Qwen3VLDecoderFused:
             x = self._embed(tok.view(B, 1)).view(B, -1)
             x, pend = self._run(x, B, 1, 0, kv_cache, pos_dev=pos, kv_len_dev=kv_len,
                                 kv_bound=bucket, rope_delta=rope_delta)
-            return self._logits(x, pend, B, 1)
+            return self._logits(x, pend, B, 1, ss_valid=self._ss_ok(B, 1))
 
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -510,7 +562,7 @@ class Qwen3VLDecoderFused:
             pos = P + i - 1
             x = self._embed(tok.view(B, 1)).view(B, -1)
             x, pend = self._run(x, B, 1, pos, kv, rope_delta=rope_delta)
-            tok = ops.argmax(self._logits(x, pend, B, 1).view(B, -1))
+            tok = ops.argmax(self._logits(x, pend, B, 1, ss_valid=self._ss_ok(B, 1)).view(B, -1))
             out[:, i] = tok
         return out
 

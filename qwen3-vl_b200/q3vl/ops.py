@@ -249,6 +249,50 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none", residual: tor
     return out
 
 
+def gemm_norm(a: torch.Tensor, norm_w: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+              epilogue: str = "none", residual: torch.Tensor = None,
+              out: torch.Tensor = None) -> torch.Tensor:
+    """C = epilogue(rmsnorm(a; norm_w, eps) @ w.T) for decode shapes (1..16 rows)."""
+    _cuda("gemm_norm", a, norm_w, w, residual, out)
+    _bf16("gemm_norm", a, norm_w, w, residual, out)
+    _contig("gemm_norm", a, norm_w, w, residual, out)
+    K = a.shape[-1]
+    N = w.shape[0]
+    M = a.numel() // K
+    epi = _EPI[epilogue]
+    n_out = N // 2 if epi == Q3_EPI_SWIGLU else N
+    if out is None:
+        out = torch.empty(*a.shape[:-1], n_out, dtype=torch.bfloat16, device=a.device)
+    call("q3_gemm_norm", _p(a), _p(norm_w), float(eps), _p(w), _p(out), M, N, K, epi,
+         _p(residual), _stream())
+    return out
+
+
+def gemm_decode(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none",
+                residual: torch.Tensor = None, norm_w: torch.Tensor = None, eps: float = 1e-6,
+                ss_in: torch.Tensor = None, ss_tiles: int = 0, ss_out: torch.Tensor = None,
+                out: torch.Tensor = None) -> torch.Tensor:
+    """Decode projection (1..16 rows): C = epilogue(rmsnorm?(a) @ w.T), with the
+    norm's sums of squares optionally taken from `ss_in` (ss_tiles x 16 fp32
+    partials) and, for the residual epilogue, written for C into `ss_out`."""
+    _cuda("gemm_decode", a, w, residual, norm_w, ss_in, ss_out, out)
+    _bf16("gemm_decode", a, w, residual, norm_w, out)
+    _contig("gemm_decode", a, w, residual, out)
+    K = a.shape[-1]
+    N = w.shape[0]
+    M = a.numel() // K
+    epi = _EPI[epilogue]
+    n_out = N // 2 if epi == Q3_EPI_SWIGLU else N
+    if out is None:
+        out = torch.empty(*a.shape[:-1], n_out, dtype=torch.bfloat16, device=a.device)
+    for t, need in ((ss_in, ss_tiles * 16), (ss_out, ((N + 63) // 64) * 16)):
+        if t is not None and (t.dtype != torch.float32 or t.numel() < need):
+            raise ValueError("gemm_decode: sum-of-squares buffers are float32 [tiles, 16]")
+    call("q3_gemm_decode", _p(a), _p(w), _p(out), M, N, K, epi, _p(residual), _p(norm_w),
+         float(eps), _p(ss_in), int(ss_tiles), _p(ss_out), _stream())
+    return out
+
+
 def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
             out: torch.Tensor = None) -> torch.Tensor:
     """C = residual + all_reduce_sum(a @ w.T) over the communicator's ranks

@@ -238,6 +238,58 @@ def test_gemm_swiglu(M):
     compare("gemm+swiglu", c, want, max_abs=2e-2, rel_scale=True, min_cos=0.9999)
 
 
+# ------------------------------------------------- decode projections, norm fused
+@pytest.mark.parametrize("M,N,K,epi", [(1, 6144, 4096, "none"), (8, 6144, 4096, "none"),
+                                       (13, 4096, 4096, "none"), (16, 2048, 544, "none"),
+                                       (8, 3072, 4096, "swiglu"), (11, 3072, 4096, "swiglu"),
+                                       (8, 4096, 4096, "residual")])
+def test_gemm_norm_matches_norm_then_gemm(M, N, K, epi):
+    """q3_gemm_norm == rmsnorm (model_fused.py:37-40) followed by the projection;
+    bf16 tolerance: max-abs 1e-2 of the output scale, cosine >= 0.99999."""
+    a = rnd(M, K, seed=50)
+    nw = (1 + rnd(K, seed=51, std=0.1)).to(BF16)
+    w = rnd(N, K, seed=52, std=0.02)
+    r = rnd(M, N, seed=53)
+    h = oref.rmsnorm(a, nw, 1e-6)
+    c = ops.gemm_norm(a.to(DEV), nw.to(DEV), w.to(DEV), 1e-6, epi,
+                      residual=r.to(DEV) if epi == "residual" else None).cpu()
+    if epi == "swiglu":
+        want = ops.gemm(h.to(DEV), w.to(DEV), "swiglu").cpu()
+        compare("gemm_norm swiglu", c, want, max_abs=2e-2, rel_scale=True, min_cos=0.9999)
+        return
+    want = _mm_ref(h, w)
+    if epi == "residual":
+        want = r + want
+    compare(f"gemm_norm {M}x{N}x{K} {epi}", c, want, max_abs=1e-2, rel_scale=True,
+            min_cos=0.99999)
+
+
+@pytest.mark.parametrize("M", [8, 16])
+def test_gemm_decode_sum_of_squares_chain(M):
+    """o_proj-like residual projection emits per-tile sums of squares; the next
+    projection's fused norm consumes them instead of re-reading its input."""
+    H, Kin, N2 = 4096, 1024, 3072
+    a = rnd(M, Kin, seed=60)
+    w1 = rnd(H, Kin, seed=61, std=0.02)
+    x = rnd(M, H, seed=62)
+    nw = (1 + rnd(H, seed=63, std=0.1)).to(BF16)
+    w2 = rnd(N2, H, seed=64, std=0.02)
+    ss = torch.full((H // 64, 16), float("nan"), device=DEV)
+    x2 = ops.gemm_decode(a.to(DEV), w1.to(DEV), "residual", residual=x.to(DEV), ss_out=ss)
+    x2h = x2.cpu()
+    compare("residual projection", x2h, x + _mm_ref(a, w1), max_abs=1e-2, rel_scale=True,
+            min_cos=0.99999)
+    tot = ss[:, :M].sum(0).cpu()
+    want_ss = (x2h.float() ** 2).sum(-1)
+    assert torch.allclose(tot, want_ss, rtol=1e-4), (tot, want_ss)
+    c = ops.gemm_decode(x2, w2.to(DEV), norm_w=nw.to(DEV), eps=1e-6, ss_in=ss,
+                        ss_tiles=H // 64).cpu()
+    c_re = ops.gemm_decode(x2, w2.to(DEV), norm_w=nw.to(DEV), eps=1e-6).cpu()
+    want = _mm_ref(oref.rmsnorm(x2h, nw, 1e-6), w2)
+    compare("norm from ss_in", c, want, max_abs=1e-2, rel_scale=True, min_cos=0.99999)
+    compare("norm recomputed", c_re, want, max_abs=1e-2, rel_scale=True, min_cos=0.99999)
+
+
 # --------------------------------------------------------------------------- a13
 def test_embed_and_argmax():
     V, H = 1000, 512
