@@ -34,6 +34,12 @@ for _p in (PKG, REPO):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the gate/up
+# decode projection (fused-norm variant, 8 tokens, TP1), from an ncu capture
+# of `microbench.py gemv --M 8 --N 24576 --K 4096 --epi swiglu --norm`
+# (201.44 MB read + 4.06 MB written)
+GEMV_TRAFFIC_BYTES = 205502720
+
 METRIC = "decode & prefill tok/s at TP1/2/4/8 (8B shape); attention HBM GB/s vs peak"
 BATCH, PROMPT, NEW_TOKENS, BUCKET = 8, 1024, 256, 2048
 WORKLOAD = (f"Qwen3-VL-8B-shape text decoder (36 layers, hidden 4096, 32/8 heads, inter "
@@ -159,13 +165,18 @@ def run_ours(args):
         dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
 
     # launch accounting: one step run eagerly (graphs replay exactly these kernels);
-    # q3_attn_decode launches a split-K combine kernel as well
+    # q3_attn_decode adds a split-K combine kernel whenever it splits
     import q3vl.ops as ops_mod
     counts = {"n": 0}
     orig_call = ops_mod.call
 
+    ws_bytes = _lib.raw("q3_attn_decode_workspace_bytes")
+
     def counting_call(name, *a):
-        counts["n"] += 2 if name == "q3_attn_decode" else 1
+        n = 1
+        if name == "q3_attn_decode" and ws_bytes(*a[4:9]) > 0:  # split-K: + combine kernel
+            n = 2
+        counts["n"] += n
         return orig_call(name, *a)
 
     ops_mod.call = counting_call
@@ -214,40 +225,70 @@ def run_ours(args):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = BATCH * NEW_TOKENS / (float(te[0]) / 1e3)
 
-    # ---- dominant kernel: decode GEMV over the largest per-layer weight ----
+    # ---- per-kernel launch durations, as CUDA-graph replays (no host gaps) ----
     hbm, tflops, peak_kind = peaks()
+
+    def graph_launch_ms(fns, reps=20):
+        """Average device time of one call, over `reps` rounds of the calls in
+        `fns` captured in one CUDA graph (inputs cycled so they exceed L2)."""
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for f in fns:
+                f()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            for _ in range(reps):
+                for f in fns:
+                    f()
+        for _ in range(3):
+            gr.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(3):
+            gr.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / (3 * reps * len(fns))
+        del gr
+        return ms
+
+    # dominant kernel: the layer's gate/up projection exactly as the decode step
+    # runs it (post-attention RMSNorm fused in from the o_proj's sums of
+    # squares, SwiGLU epilogue); its 201 MB of weights exceed L2 on every call
     mlp = dec.layers[0].mlp_block
-    x = torch.randn(BATCH, 4096, device=dev).to(torch.bfloat16)
+    H = 4096
+    x = torch.randn(BATCH, H, device=dev).to(torch.bfloat16)
     w = mlp.gate_up_weight_il
-    for _ in range(5):
-        ops.gemm(x, w, "swiglu")
-    n_it = 50
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(n_it):
-        ops.gemm(x, w, "swiglu")
-    b.record(stream)
-    torch.cuda.synchronize()
-    gemv_ms = a.elapsed_time(b) / n_it
-    gemv_bytes = w.numel() * 2 + x.numel() * 2 + BATCH * w.shape[0] // 2 * 2
+    ss = (x.float() ** 2).view(BATCH, H // 64, 64).sum(-1).t().contiguous()
+    ss = torch.nn.functional.pad(ss, (0, 16 - BATCH)).contiguous()      # [H/64, 16]
+    act = torch.empty(BATCH, w.shape[0] // 2, dtype=torch.bfloat16, device=dev)
+    fused_norm = dec.fuse_norm
+    if fused_norm:
+        gemv_fn = [lambda: ops.gemm_decode(x, w, "swiglu", norm_w=mlp.post_norm_weight,
+                                           eps=mlp.eps, ss_in=ss, ss_tiles=H // 64, out=act)]
+    else:
+        gemv_fn = [lambda: ops.gemm(x, w, "swiglu", out=act)]
+    gemv_ms = graph_launch_ms(gemv_fn)
+    gemv_bytes = w.numel() * 2 + x.numel() * 2 + act.numel() * 2 + ss.numel() * 4
     gemv_gbs = gemv_bytes / (gemv_ms / 1e3) / 1e9
 
-    # ---- decode attention HBM GB/s at the workload's mid-generation length ----
+    # decode attention at the workload's mid-generation length; four KV sets
+    # (151 MB) cycled so every launch reads its K/V from HBM
     L = PROMPT + NEW_TOKENS // 2
     ab = dec.layers[0].attn_block
-    kc = torch.randn(BATCH, ab.num_kv_heads, BUCKET, 128, device=dev).to(torch.bfloat16)
-    vc = torch.randn_like(kc)
+    sets = []
+    for _ in range(4):
+        kc = torch.randn(BATCH, ab.num_kv_heads, BUCKET, 128, device=dev).to(torch.bfloat16)
+        sets.append((kc, torch.randn_like(kc)))
     q = torch.randn(BATCH, ab.num_q_heads, 128, device=dev).to(torch.bfloat16)
-    for _ in range(5):
-        ops.attn_decode(q, kc, vc, kv_len=L)
-    a.record(stream)
-    for _ in range(n_it):
-        ops.attn_decode(q, kc, vc, kv_len=L)
-    b.record(stream)
-    torch.cuda.synchronize()
-    attn_ms = a.elapsed_time(b) / n_it
+    ao = torch.empty_like(q)
+    attn_ms = graph_launch_ms([lambda kc=kc, vc=vc: ops.attn_decode(q, kc, vc, kv_len=L, out=ao)
+                               for kc, vc in sets])
     attn_bytes = BATCH * ab.num_kv_heads * L * 128 * 2 * 2 + 2 * q.numel() * 2
     attn_gbs = attn_bytes / (attn_ms / 1e3) / 1e9
+    del sets
 
     # decode-step bytes (weights + KV) for the whole-step HBM fraction
     n_params = sum(p.numel() for lyr in dec.layers for p in
@@ -279,11 +320,17 @@ def run_ours(args):
                                 "frac": round(step_gbs / hbm, 4)},
             "attention_hbm_gbs": round(attn_gbs, 1),
             "attention_hbm_frac": round(attn_gbs / hbm, 4),
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<1,SWIGLU> (gate_up, M=8)",
+            "attention_launch_ms": round(attn_ms, 5),
+            "roofline": {"bound": "hbm",
+                         "kernel": ("gemv_tma_kernel<1, SWIGLU, NORM> (gate_up, 8 tokens, "
+                                    "post-attention RMSNorm fused)" if fused_norm else
+                                    "gemv_tma_kernel<1, SWIGLU, 0> (gate_up, 8 tokens)"),
                          "achieved": round(gemv_gbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(gemv_gbs / hbm, 4), "traffic": None,
-                         "peak_source": peak_kind,
-                         "bytes_per_launch": gemv_bytes, "launch_ms": round(gemv_ms, 4)},
+                         "frac": round(gemv_gbs / hbm, 4),
+                         "traffic": GEMV_TRAFFIC_BYTES if fused_norm else None,
+                         "peak_source": f"{peak_kind} (burst copy)",
+                         "bytes_per_launch": gemv_bytes, "launch_ms": round(gemv_ms, 5),
+                         "timing": "CUDA-graph replay of 20 launches, events on the stream"},
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": BATCH * PROMPT * 8,
                     "d2h_bytes_per_step": BATCH * NEW_TOKENS * 8},

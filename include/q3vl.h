@@ -110,7 +110,13 @@ Q3_API int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const void* k
  * max_seq, D]; out [B, Hq, D]; all of dtype `dtype` (Q3_F32 or Q3_BF16).
  * Attends to cache positions [0, kv_len) where kv_len = *kv_len_dev if that
  * is non-NULL, else kv_len; head h reads KV head h / (Hq/Hkv).  Split-K over
- * SMs: workspace must hold q3_attn_decode_workspace_bytes(...) bytes. */
+ * SMs: workspace must hold q3_attn_decode_workspace_bytes(...) bytes.
+ * With kv_len_dev, kv_len is the upper bound the grid is planned for and the
+ * splits share the positions actually present.  Ordering: q and cache row
+ * kv_len-1 may come from the kernel just before this call on the stream (as
+ * q3_qkv_norm_rope writes them); *kv_len_dev and the cache rows below
+ * kv_len-1 must be complete before that kernel is launched, because the bf16
+ * kernel starts streaming them while its predecessor finishes. */
 Q3_API size_t q3_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int head_dim, int64_t max_kv_len);
 Q3_API int q3_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
                    int Hq, int Hkv, int head_dim, int64_t kv_len, const int32_t* kv_len_dev,

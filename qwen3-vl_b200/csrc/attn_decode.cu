@@ -111,6 +111,16 @@ struct DecodeParams {
   float scale;
 };
 
+// Positions per split.  The grid's split count is planned on the host from
+// an upper bound of the length; when the length is read on the device, the
+// chunk is recomputed from it so every split gets an equal share of the
+// positions actually present (whole steps of `step`).
+__device__ __forceinline__ int64_t split_chunk(const DecodeParams& p, int64_t L, int step) {
+  if (!p.kv_len_dev || p.splits <= 1) return p.chunk;
+  const int64_t ch = (L + p.splits - 1) / p.splits;
+  return (ch + step - 1) / step * step;
+}
+
 template <typename T, int G>
 __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(DecodeParams p) {
   pdl_wait();
@@ -119,8 +129,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(DecodeParam
   const int warp = threadIdx.x >> 5;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int64_t L = p.kv_len_dev ? (int64_t)(*p.kv_len_dev) : p.kv_len;
-  const int64_t start = (int64_t)split * p.chunk;
-  const int64_t end = min64(start + p.chunk, L);
+  const int64_t chunk = split_chunk(p, L, kDecStep);
+  const int64_t start = (int64_t)split * chunk;
+  const int64_t end = min64(start + chunk, L);
 
   const T* qb = reinterpret_cast<const T*>(p.q) + ((int64_t)b * p.Hq + (int64_t)kvh * G) * kHD;
   const T* kb = reinterpret_cast<const T*>(p.k) + ((int64_t)b * p.Hkv + kvh) * p.max_seq * kHD;
@@ -349,7 +360,10 @@ template <int G>
 __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     DecodeTcParams prm) {
-  pdl_wait();
+  // No dependency wait yet: cache rows below the newest position were
+  // completed before this launch sequence began (the host API contract), so
+  // the producer streams them while the kernel that writes q and the newest
+  // row finishes.  q, the newest row and the outputs wait for it.
   pdl_launch();
   const DecodeParams& p = prm.p;
   extern __shared__ uint8_t smem_raw[];
@@ -363,8 +377,9 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int64_t L = p.kv_len_dev ? (int64_t)(*p.kv_len_dev) : p.kv_len;
-  const int64_t start = (int64_t)split * p.chunk;
-  const int64_t end = min64(start + p.chunk, L);
+  const int64_t chunk = split_chunk(p, L, kTcTile);
+  const int64_t start = (int64_t)split * chunk;
+  const int64_t end = min64(start + chunk, L);
   const int ntiles = end > start ? (int)((end - start + kTcTile - 1) / kTcTile) : 0;
   const int64_t row_base = ((int64_t)b * p.Hkv + kvh) * p.max_seq + start;
 
@@ -381,9 +396,15 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
 
   if (warp == kTcConsumers) {
     if (lane == 0) {
+      bool waited = false;
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % kTcStages;
         const uint32_t ph = (i / kTcStages) & 1;
+        // a tile reaching the newest row (L - 1) waits for its writer
+        if (!waited && start + (int64_t)(i + 1) * kTcTile > L - 1) {
+          pdl_wait();
+          waited = true;
+        }
         if (!mbar_wait(&empty[s], ph ^ 1, prm.err, 0x401)) break;
         uint8_t* st = ring + s * kTcStageBytes;
         const int y = (int)(row_base + (int64_t)i * kTcTile);
@@ -395,6 +416,7 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
       }
     }
   } else {
+    pdl_wait();  // q and the outputs
     const int g = lane >> 2, t = lane & 3;
     // Q as the A operand: row g = query head kvh*G + g (rows >= G are zero)
     uint32_t qf[8][2];

@@ -7,6 +7,12 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py decode --B 8 --Hq 32 --Hkv 8 --L 1152
     python qwen3-vl_b200/q3vl/microbench.py prefill --B 1 --Hq 32 --Hkv 8 --S 2048
     python qwen3-vl_b200/q3vl/microbench.py rmsnorm --rows 8192 --hidden 4096
+    python qwen3-vl_b200/q3vl/microbench.py layer  --B 8 --L 1152 --bucket 2048
+
+`layer` times every kernel of one TP1 decode layer of the 8B shape, and the
+whole layer, as CUDA-graph replays cycling over 4 layers' weights (1.5 GB, so
+every launch streams its weights from HBM), with the decode graph's arguments
+(length read on the device, grid planned for the bucket).
 """
 from __future__ import annotations
 
@@ -42,11 +48,15 @@ def _time(fn, iters, warmup, flush):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar"])
+    ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
+                                       "layer"])
+    ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=24576)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--epi", default="none", choices=["none", "residual", "swiglu"])
+    ap.add_argument("--norm", action="store_true",
+                    help="gemv: RMSNorm fused in, sums of squares from a prior projection")
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--Hq", type=int, default=32)
     ap.add_argument("--Hkv", type=int, default=8)
@@ -61,6 +71,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
+    if a.kernel == "layer":
+        return _layer(a)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
     flush = None if a.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -72,10 +84,20 @@ def main(argv=None):
         r = torch.randn(a.M, a.N, device=dev).to(bf) if a.epi == "residual" else None
         out_n = a.N // 2 if a.epi == "swiglu" else a.N
         out = torch.empty(a.M, out_n, dtype=bf, device=dev)
-        ms = _time(lambda: ops.gemm(x, w, a.epi, residual=r, out=out), a.iters, a.warmup, flush)
+        if a.norm:
+            if a.M > 16 or a.K % 64:
+                raise SystemExit("--norm: decode shapes (M <= 16, K % 64 == 0) only")
+            nw = torch.ones(a.K, dtype=bf, device=dev)
+            ss = torch.zeros(a.K // 64, 16, device=dev)
+            ss[:, :a.M] = (x.float() ** 2).view(a.M, a.K // 64, 64).sum(-1).t()
+            fn = lambda: ops.gemm_decode(x, w, a.epi, residual=r, norm_w=nw, ss_in=ss,  # noqa
+                                         ss_tiles=a.K // 64, out=out)
+        else:
+            fn = lambda: ops.gemm(x, w, a.epi, residual=r, out=out)  # noqa: E731
+        ms = _time(fn, a.iters, a.warmup, flush)
         nbytes = (w.numel() + x.numel() + out.numel() + (r.numel() if r is not None else 0)) * 2
         flops = 2.0 * a.M * a.N * a.K
-        res.update(M=a.M, N=a.N, K=a.K, epi=a.epi, ms=ms, gbs=nbytes / ms / 1e6,
+        res.update(M=a.M, N=a.N, K=a.K, epi=a.epi, norm=a.norm, ms=ms, gbs=nbytes / ms / 1e6,
                    tflops=flops / ms / 1e9)
     elif a.kernel == "decode":
         dt = torch.float32 if a.dtype == "f32" else bf
@@ -102,6 +124,119 @@ def main(argv=None):
         y = torch.empty_like(x)
         ms = _time(lambda: ops.rmsnorm(x, w, out=y), a.iters, a.warmup, flush)
         res.update(rows=a.rows, hidden=a.hidden, ms=ms, gbs=2 * x.numel() * 2 / ms / 1e6)
+    print(json.dumps(res), flush=True)
+
+
+def _graph_ms(fns, rounds=5):
+    """Device time per call: `rounds` passes over `fns` captured in one graph."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(rounds):
+            for f in fns:
+                f()
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (5 * rounds * len(fns))
+
+
+def _layer(a):
+    import dataclasses
+
+    import loader_fused
+    dev = torch.device("cuda:0")
+    NL = 4
+    spec = dataclasses.replace(loader_fused.QWEN3_VL_8B, layers=NL)
+    dec = loader_fused.random_decoder(spec, 0, 1, dev, seed=0, max_seq=a.bucket)
+    B, L, H = a.B, a.L, spec.hidden
+    kv = dec._kv_for(B, a.bucket)
+    for k, v in kv:
+        k.normal_()
+        v.normal_()
+    pos = torch.tensor([L - 1], dtype=torch.int32, device=dev)
+    kv_len = torch.tensor([L], dtype=torch.int32, device=dev)
+    bf = torch.bfloat16
+    x = torch.randn(B, H, device=dev).to(bf)
+    ss0, ss1 = dec._ss_buf(0), dec._ss_buf(1)
+    ss1.view(-1, 16)[:H // 64, :B] = (x.float() ** 2).view(B, H // 64, 64).sum(-1).t()
+    ss0.copy_(ss1)
+    cos, sin, _ = dec.rotary.tables(dev)
+    L0 = dec.layers[0]
+    ab0, mlp0 = L0.attn_block, L0.mlp_block
+    qkv = torch.empty(B, ab0.qkv_weight_km.shape[0], dtype=bf, device=dev)
+    q = torch.empty(B, ab0.num_q_heads, 1, 128, dtype=bf, device=dev)
+    attn = torch.empty(B, ab0.num_q_heads, 128, dtype=bf, device=dev)
+    x2 = torch.empty_like(x)
+    act = torch.empty(B, mlp0.gate_up_weight_il.shape[0] // 2, dtype=bf, device=dev)
+    y = torch.empty_like(x)
+    ws = ops.decode_workspace(B, ab0.num_q_heads, ab0.num_kv_heads, dev)
+
+    def k_qkv(i):
+        ab = dec.layers[i].attn_block
+        return lambda: ops.gemm_decode(x, ab.qkv_weight_km, norm_w=ab.input_norm_weight,
+                                       eps=ab.eps, ss_in=ss1, ss_tiles=H // 64, out=qkv)
+
+    def k_rope(i):
+        ab = dec.layers[i].attn_block
+        kc, vc = kv[i]
+
+        def f():
+            qq, _, _ = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B,
+                                         S=1, Hq=ab.num_q_heads, Hkv=ab.num_kv_heads,
+                                         pos_dev=pos, k_cache=kc, v_cache=vc, eps=ab.eps)
+            return qq
+        return f
+
+    def k_attn(i):
+        kc, vc = kv[i]
+        return lambda: ops.attn_decode(q.view(B, -1, 128), kc, vc, kv_len=a.bucket,
+                                       kv_len_dev=kv_len, out=attn, workspace=ws)
+
+    def k_o(i):
+        return lambda: ops.gemm_decode(attn.view(B, -1), dec.layers[i].o_proj.weight_km,
+                                       "residual", residual=x, ss_out=ss0, out=x2)
+
+    def k_gu(i):
+        m = dec.layers[i].mlp_block
+        return lambda: ops.gemm_decode(x2, m.gate_up_weight_il, "swiglu", norm_w=m.post_norm_weight,
+                                       eps=m.eps, ss_in=ss0, ss_tiles=H // 64, out=act)
+
+    def k_down(i):
+        return lambda: ops.gemm_decode(act, dec.layers[i].mlp_block.down_weight_km, "residual",
+                                       residual=x2, ss_out=ss1, out=y)
+
+    def k_layer(i):
+        return lambda: dec._layer(x, None, i, kv, 0, 1, B, pos_dev=pos, kv_len_dev=kv_len,
+                                  kv_bound=a.bucket, ss_valid=True)
+
+    W = dict(qkv=ab0.qkv_weight_km.numel() * 2, o_proj=L0.o_proj.weight_km.numel() * 2,
+             gate_up=mlp0.gate_up_weight_il.numel() * 2,
+             down=mlp0.down_weight_km.numel() * 2,
+             attention=2 * B * ab0.num_kv_heads * L * 128 * 2)
+    res = {"kernel": "layer", "B": B, "L": L, "bucket": a.bucket, "us": {}, "gbs": {}}
+    tot = 0.0
+    for name, mk in (("qkv", k_qkv), ("qkv_norm_rope", k_rope), ("attention", k_attn),
+                     ("o_proj", k_o), ("gate_up", k_gu), ("down", k_down)):
+        ms = _graph_ms([mk(i) for i in range(NL)])
+        tot += ms
+        res["us"][name] = round(ms * 1e3, 2)
+        if name in W:
+            res["gbs"][name] = round(W[name] / ms / 1e6, 1)
+    res["us"]["sum_of_kernels"] = round(tot * 1e3, 2)
+    ms = _graph_ms([k_layer(i) for i in range(NL)])
+    res["us"]["layer"] = round(ms * 1e3, 2)
+    res["layer_hbm_gbs"] = round(sum(W.values()) / ms / 1e6, 1)
     print(json.dumps(res), flush=True)
 
 

@@ -158,6 +158,25 @@ def test_decode_attention_device_length():
         compare(f"decode dev len {L}", a, b, max_abs=2e-3, min_cos=0.99999)
 
 
+@pytest.mark.parametrize("dtype", [BF16, torch.float32])
+def test_decode_attention_device_length_decode_graph_shape(dtype):
+    """The decode graph's call: grid planned for the KV bucket (2048), actual
+    length read on the device; the splits share the present positions.  bf16:
+    max-abs <= 1e-2, cosine >= 0.9999 vs the fp32 oracle; fp32: max-abs <= 1e-5."""
+    B, Hq, Hkv, S = 8, 32, 8, 2048
+    q = rnd(B, Hq, 128, seed=13).to(dtype)
+    kc, vc = rnd(B, Hkv, S, 128, seed=14).to(dtype), rnd(B, Hkv, S, 128, seed=15).to(dtype)
+    qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
+    for L in (1, 63, 65, 1152, 1279, 2048):
+        Ld = torch.tensor([L], dtype=torch.int32, device=DEV)
+        got = ops.attn_decode(qd, kd, vd, kv_len=S, kv_len_dev=Ld).cpu()
+        want = oref.decode_attention_fp32(q.float(), kc[:, :, :L].float(), vc[:, :, :L].float())
+        if dtype == BF16:
+            compare(f"graph-shape decode L={L}", got, want, max_abs=1e-2, min_cos=0.9999)
+        else:
+            compare(f"graph-shape decode fp32 L={L}", got, want, max_abs=1e-5)
+
+
 # --------------------------------------------------------------------------- a6/a7 prefill
 def test_prefill_kat_vs_reference_attention_ref():
     """kernels/prefill_attention.py layouts (q [Hq,D,S], k [Hkv,D,S], v [Hkv,S,D])."""
