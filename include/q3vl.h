@@ -205,6 +205,47 @@ Q3_API int q3_comm_destroy(void* comm);
 Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
                       const void* residual, void* comm, q3_stream_t stream);
 
+/* ---- a12/a13: the whole decode step of every layer in one launch ----------
+ * Replaces forward_layer (model_fused.py:234-277) at S = 1 for all layers of
+ * decode_step (model_fused.py:295-300): input RMSNorm, QKV projection,
+ * per-head QK-RMSNorm + RoPE, KV-cache write at the new position, GQA
+ * attention, o_proj + residual, post-attention RMSNorm, gate/up + SwiGLU, down
+ * + residual.  One persistent kernel, one CTA per SM: weights and old cache
+ * rows stream by TMA without waiting for other CTAs, activations wait on
+ * grid-wide phase counters (bounded waits).  Tensor parallelism 1 (the
+ * projections are this rank's shards; no all-reduce is done), 4 query heads
+ * per KV head, head_dim 128, 1..16 sequences (one new token each).
+ * q3_step_layer: per-layer device pointers, weights K-major as for q3_gemm
+ * (gate/up interleaved in blocks of 8 rows); caches [batch, kv_heads,
+ * max_seq, 128].  rope_cos/rope_sin: bf16 [rope_rows, 64] tables
+ * (RotaryEmbedding, model_fused.py:43-58).
+ * q3_decode_step: x bf16 [batch, hidden] holds the embedded new tokens and
+ * receives the last layer's output; ss float [hidden/128][16] receives its
+ * per-128-column sums of squares (for the final norm fused into the lm_head,
+ * q3_gemm_decode with ss_tiles = hidden/128).  *kv_len_dev = new position + 1,
+ * set before the launch; RoPE row = position + rope_delta.  A plan holds
+ * workspaces for one step at a time: order its steps on one stream.  After a
+ * Q3_ERR_TIMEOUT in the device error word, destroy and recreate the plan. */
+typedef struct q3_step_layer {
+  const void* w_qkv;      /* [(q_heads + 2*kv_heads)*128, hidden] */
+  const void* w_o;        /* [hidden, q_heads*128] */
+  const void* w_gate_up;  /* [2*inter, hidden], gate/up interleaved */
+  const void* w_down;     /* [hidden, inter] */
+  const void* input_norm; /* [hidden] */
+  const void* post_norm;  /* [hidden] */
+  const void* q_norm;     /* [128] */
+  const void* k_norm;     /* [128] */
+  void* k_cache;          /* [batch, kv_heads, max_seq, 128] */
+  void* v_cache;
+} q3_step_layer;
+Q3_API int q3_decode_step_create(const q3_step_layer* layers, int n_layers, int batch, int hidden,
+                                 int q_heads, int kv_heads, int inter, int64_t max_seq, float eps,
+                                 const void* rope_cos, const void* rope_sin, int64_t rope_rows,
+                                 void** plan_out);
+Q3_API int q3_decode_step(void* plan, void* x, float* ss, const int32_t* kv_len_dev,
+                          int64_t rope_delta, q3_stream_t stream);
+Q3_API int q3_decode_step_destroy(void* plan);
+
 /* ---- a13: embedding gather and greedy argmax -----------------------------
  * Replaces embed_tokens(input_ids) (model_fused.py:281) and
  * logits.argmax(-1) (model_fused.py:310,320).  ids int64 [n]; table bf16

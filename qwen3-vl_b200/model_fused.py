@@ -226,6 +226,11 @@ class Qwen3VLDecoderFused:
         self.use_graphs = os.environ.get("Q3VL_DECODE_GRAPHS", "1") != "0"
         # decode: RMSNorms fused into the projections that consume them
         self.fuse_norm = os.environ.get("Q3VL_FUSE_NORM", "1") != "0"
+        # decode graphs: every layer in one persistent kernel (q3_decode_step);
+        # opt-in until it beats the per-kernel decode step
+        self.use_step_kernel = os.environ.get("Q3VL_STEP_KERNEL", "0") == "1"
+        self._step_plans = {}
+        self._ss_step = None
 
     # ------------------------------------------------------------------ cache
     def init_kv_cache(self, batch_size=1):
@@ -256,6 +261,9 @@ class Qwen3VLDecoderFused:
     def close(self):
         """Release captured graphs and the peer communicator (collective)."""
         self._graphs.clear()
+        for plan in self._step_plans.values():
+            plan.close()
+        self._step_plans.clear()
         if self.comm is not None:
             self.comm.close()
             self.comm = None
@@ -459,6 +467,53 @@ class Qwen3VLDecoderFused:
                 return b
         return self.max_seq_len
 
+    # ------------------------------------------------------ persistent step
+    def _step_ok(self, B: int) -> bool:
+        """The whole-step kernel covers TP1, head_dim 128, 4 query heads per KV
+        head, no QKV bias, up to 16 sequences."""
+        H = self.layers[0].attn_block.input_norm_weight.numel() if self.num_layers else 0
+        return (self.use_step_kernel and self.tp_size == 1 and self.num_layers > 0 and
+                1 <= B <= 16 and self.head_dim == 128 and H % 128 == 0 and
+                self.num_q_heads == 4 * self.num_kv_heads and
+                all(L.attn_block.qkv_bias is None for L in self.layers))
+
+    def _step_plan(self, B, kv_cache):
+        key = (B, kv_cache[0][0].data_ptr())
+        plan = self._step_plans.get(key)
+        if plan is None:
+            layers = []
+            for L, (kc, vc) in zip(self.layers, kv_cache):
+                ab, mlp = L.attn_block, L.mlp_block
+                layers.append(dict(w_qkv=ab.qkv_weight_km, w_o=L.o_proj.weight_km,
+                                   w_gate_up=mlp.gate_up_weight_il, w_down=mlp.down_weight_km,
+                                   input_norm=ab.input_norm_weight, post_norm=mlp.post_norm_weight,
+                                   q_norm=ab.q_norm_weight, k_norm=ab.k_norm_weight,
+                                   k_cache=kc, v_cache=vc))
+            cos, sin, _ = self.rotary.tables(self.device)
+            mlp0 = self.layers[0].mlp_block
+            plan = ops.DecodeStepPlan(
+                layers, batch=B, hidden=self.layers[0].attn_block.input_norm_weight.numel(),
+                q_heads=self.num_q_heads, kv_heads=self.num_kv_heads,
+                inter=mlp0.down_weight_km.shape[1], max_seq=kv_cache[0][0].shape[2],
+                eps=self._eps, cos=cos, sin=sin)
+            self._step_plans[key] = plan
+        return plan
+
+    def _step_logits(self, B, tok, kv_cache, kv_len, rope_delta):
+        """One decode step through q3_decode_step; the final RMSNorm runs inside
+        the lm_head projection from the step's per-tile sums of squares."""
+        plan = self._step_plan(B, kv_cache)
+        H = plan.hidden
+        if self._ss_step is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("step buffers must exist before graph capture")
+            self._ss_step = torch.zeros(H // 128, 16, dtype=torch.float32, device=self.device)
+        x = self._embed(tok.view(B, 1)).view(B, -1)
+        plan.run(x, self._ss_step, kv_len, rope_delta)
+        local = ops.gemm_decode(x, self.lm_head.weight_km, norm_w=self.final_norm.weight,
+                                eps=self.final_norm.eps, ss_in=self._ss_step, ss_tiles=H // 128)
+        return local.view(B, 1, -1)
+
     def _capture_decode(self, B, kv_cache, bucket, rope_delta=0):
         """Capture one decode step.  Must run before the prefill that fills this
         cache: the warm-up step writes KV slot 0, which the prefill overwrites."""
@@ -472,7 +527,11 @@ class Qwen3VLDecoderFused:
         kv_len = torch.ones(1, dtype=torch.int32, device=dev)
         ops.decode_workspace(B, self.num_q_heads, self.num_kv_heads, dev)
 
+        use_step = self._step_ok(B)
+
         def step():
+            if use_step:
+                return self._step_logits(B, tok, kv_cache, kv_len, rope_delta)
             x = self._embed(tok.view(B, 1)).view(B, -1)
             x, pend = self._run(x, B, 1, 0, kv_cache, pos_dev=pos, kv_len_dev=kv_len,
                                 kv_bound=bucket, rope_delta=rope_delta)

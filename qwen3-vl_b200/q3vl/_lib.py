@@ -60,6 +60,10 @@ SIGNATURES: dict[str, tuple] = {
     "q3_comm_open_peers": (I32, [P, P]),
     "q3_comm_destroy": (I32, [P]),
     "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P]),
+    "q3_decode_step_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64,
+                                    ctypes.POINTER(P)]),
+    "q3_decode_step": (I32, [P, P, P, P, I64, P]),
+    "q3_decode_step_destroy": (I32, [P]),
     "q3_embed": (I32, [P, P, P, I64, I64, I64, P]),
     "q3_add": (I32, [P, P, P, I64, P]),
     "q3_argmax": (I32, [P, I64, I64, P, P]),
@@ -88,6 +92,13 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+class StepLayer(ctypes.Structure):
+    """q3_step_layer of include/q3vl.h (device pointers of one decoder layer)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("w_qkv", "w_o", "w_gate_up", "w_down", "input_norm", "post_norm", "q_norm",
+                 "k_norm", "k_cache", "v_cache")]
 
 
 def exported_symbols() -> list[str]:

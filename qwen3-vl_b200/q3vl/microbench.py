@@ -8,7 +8,10 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py prefill --B 1 --Hq 32 --Hkv 8 --S 2048
     python qwen3-vl_b200/q3vl/microbench.py rmsnorm --rows 8192 --hidden 4096
     python qwen3-vl_b200/q3vl/microbench.py layer  --B 8 --L 1152 --bucket 2048
+    python qwen3-vl_b200/q3vl/microbench.py step   --B 8 --L 1152 --bucket 2048 --layers 36
 
+`step` times q3_decode_step (every layer of a decode step in one persistent
+kernel) as CUDA-graph replays and reports the step's HBM rate (weights + KV).
 `layer` times every kernel of one TP1 decode layer of the 8B shape, and the
 whole layer, as CUDA-graph replays cycling over 4 layers' weights (1.5 GB, so
 every launch streams its weights from HBM), with the decode graph's arguments
@@ -49,7 +52,8 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "layer"])
+                                       "layer", "step"])
+    ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=24576)
@@ -73,6 +77,8 @@ def main(argv=None):
         return _gemm_ar(a)
     if a.kernel == "layer":
         return _layer(a)
+    if a.kernel == "step":
+        return _step(a)
     dev = torch.device("cuda:0")
     torch.manual_seed(0)
     flush = None if a.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -238,6 +244,43 @@ def _layer(a):
     res["us"]["layer"] = round(ms * 1e3, 2)
     res["layer_hbm_gbs"] = round(sum(W.values()) / ms / 1e6, 1)
     print(json.dumps(res), flush=True)
+
+
+def _step(a):
+    import dataclasses
+
+    import loader_fused
+    dev = torch.device("cuda:0")
+    spec = dataclasses.replace(loader_fused.QWEN3_VL_8B, layers=a.layers, vocab=4096)
+    dec = loader_fused.random_decoder(spec, 0, 1, dev, seed=0, max_seq=a.bucket)
+    B, L, H = a.B, a.L, spec.hidden
+    kv = dec._kv_for(B, a.bucket)
+    for k, v in kv:
+        k.normal_()
+        v.normal_()
+    plan = dec._step_plan(B, kv)
+    x0 = torch.randn(B, H, device=dev).to(torch.bfloat16)
+    x = x0.clone()
+    ss = torch.zeros(H // 128, 16, device=dev)
+    kv_len = torch.tensor([L], dtype=torch.int32, device=dev)
+
+    def f():
+        x.copy_(x0)
+        plan.run(x, ss, kv_len)
+    ms = _graph_ms([f], rounds=4)
+    torch.cuda.synchronize()
+    err = ops.device_error(clear=True)
+    L0 = dec.layers[0]
+    wbytes = sum(t.numel() * 2 for t in (L0.attn_block.qkv_weight_km, L0.o_proj.weight_km,
+                                         L0.mlp_block.gate_up_weight_il,
+                                         L0.mlp_block.down_weight_km))
+    kvbytes = 2 * B * L0.attn_block.num_kv_heads * L * 128 * 2
+    tot = a.layers * (wbytes + kvbytes)
+    print(json.dumps({"kernel": "step", "B": B, "L": L, "layers": a.layers,
+                      "ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / a.layers, 2),
+                      "gbs": round(tot / ms / 1e6, 1), "bytes": tot, "device_error": err}),
+          flush=True)
+    plan.close()
 
 
 def _gemm_ar(a):

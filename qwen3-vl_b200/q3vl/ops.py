@@ -293,6 +293,67 @@ def gemm_decode(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none",
     return out
 
 
+class DecodeStepPlan:
+    """One decode step of every layer in one persistent kernel (q3_decode_step).
+
+    `layers`: per layer a dict of K-major bf16 weights (w_qkv, w_o, w_gate_up
+    interleaved, w_down), bf16 norms (input_norm, post_norm, q_norm, k_norm) and
+    the layer's bf16 caches (k_cache, v_cache [B, Hkv, max_seq, 128]).  The
+    tensors must outlive the plan.  `cos`/`sin`: bf16 [rows, 64] rope tables."""
+
+    def __init__(self, layers, *, batch: int, hidden: int, q_heads: int, kv_heads: int,
+                 inter: int, max_seq: int, eps: float, cos: torch.Tensor, sin: torch.Tensor):
+        from ._lib import StepLayer
+        arr = (StepLayer * len(layers))()
+        keep = []
+        for i, d in enumerate(layers):
+            for name, _ in StepLayer._fields_:
+                t = d[name]
+                if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+                    raise ValueError(f"DecodeStepPlan: layer {i} {name} must be contiguous "
+                                     "bf16 on the GPU")
+                setattr(arr[i], name, t.data_ptr())
+                keep.append(t)
+        _cuda("decode_step", cos, sin)
+        _bf16("decode_step", cos, sin)
+        handle = ctypes.c_void_p()
+        call("q3_decode_step_create", ctypes.cast(arr, ctypes.c_void_p), len(layers), batch,
+             hidden, q_heads, kv_heads, inter, int(max_seq), float(eps), _p(cos), _p(sin),
+             cos.shape[0], ctypes.byref(handle))
+        self.handle = handle
+        self.batch, self.hidden = batch, hidden
+        self._keep = keep + [cos, sin]
+
+    def run(self, x: torch.Tensor, ss: torch.Tensor, kv_len_dev: torch.Tensor,
+            rope_delta: int = 0) -> torch.Tensor:
+        """x bf16 [B, hidden] in place: embedded tokens in, last layer out; ss
+        float32 [hidden/128, 16] receives the output's per-tile sums of squares."""
+        if self.handle is None:
+            raise RuntimeError("DecodeStepPlan is closed")
+        if x.shape != (self.batch, self.hidden) or x.dtype != torch.bfloat16:
+            raise ValueError("decode_step: x must be bf16 [batch, hidden]")
+        if ss.dtype != torch.float32 or ss.numel() < (self.hidden // 128) * 16:
+            raise ValueError("decode_step: ss must be float32 [hidden/128, 16]")
+        if kv_len_dev.dtype != torch.int32:
+            raise TypeError("decode_step: kv_len_dev must be int32")
+        _contig("decode_step", x, ss)
+        call("q3_decode_step", self.handle, _p(x), _p(ss), _p(kv_len_dev), int(rope_delta),
+             _stream())
+        return x
+
+    def close(self):
+        if self.handle is not None:
+            call("q3_decode_step_destroy", self.handle)
+            self.handle = None
+            self._keep = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
             out: torch.Tensor = None) -> torch.Tensor:
     """C = residual + all_reduce_sum(a @ w.T) over the communicator's ranks
