@@ -302,7 +302,8 @@ def run_ours(args):
 
     clocks = clk.summary()
     if rank == 0:
-        cpu = cpu_baseline(budget_s=args.cpu_budget) if args.cpu_budget > 0 else None
+        # the CPU baseline is measured on rank 0 of single-GPU runs only
+        cpu = cpu_baseline(budget_s=args.cpu_budget) if (args.cpu_budget > 0 and world == 1) else None
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s",
             "n_gpus": world, "steps": K, "warmup": args.warmup,
