@@ -22,9 +22,10 @@
 // Work split: each phase's units (64-wide K blocks of 128-row weight tiles, or
 // 64-position blocks of a (sequence, KV head) pair) are divided into equal
 // contiguous ranges, one per CTA ("stream-K"), so every SM streams the same
-// number of bytes.  A tile split across CTAs is reduced by the CTA that
-// finishes it last (arrival counter), summing the partials in CTA order, and
-// that CTA runs the tile's epilogue: QK-norm + RoPE + KV write (one head per
+// number of bytes.  A tile split across CTAs is reduced by its owner, the CTA
+// holding its first units (it meets them last, at the end of its range), which
+// waits for the others' arrival counter and sums the partials in CTA order;
+// the owner runs the tile's epilogue: QK-norm + RoPE + KV write (one head per
 // QKV tile), residual + per-tile sums of squares (o_proj, down), SwiGLU
 // (gate/up), or the split-K softmax merge (attention).
 // Every wait is bounded; after a timeout the device error word is set and all
@@ -138,6 +139,27 @@ __device__ __forceinline__ void grid_wait(const unsigned* bar, unsigned target, 
   }
   __syncwarp();
   (void)ld_acquire_gpu(bar);  // every lane orders its later reads after the arrivals
+}
+// The owner of a split tile waits (bounded) until the other `n` contributors
+// have published their partials; one thread polls, then resets the counter.
+__device__ __forceinline__ void wait_contributors(int* cnt, int n, int* err, int code) {
+  if (n <= 0) return;
+  const unsigned* cu = reinterpret_cast<const unsigned*>(cnt);
+  if ((int)ld_acquire_gpu(cu) < n) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while ((int)ld_acquire_gpu(cu) < n) {
+      __nanosleep(32);
+      if ((++spins & 63u) == 0) {
+        if (aborted(err)) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          report_timeout(err, code);
+          break;
+        }
+      }
+    }
+  }
+  *cnt = 0;  // next use of this counter is after a grid-wide phase boundary
 }
 __device__ __forceinline__ void cons_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
@@ -493,39 +515,53 @@ __device__ __forceinline__ void epi_proj(const Params& p, const Layer& Ly, const
     w1 = bf2f(nwq[et + 64]);
   }
   if (cl > cf) {
-    // split tile: publish this CTA's partial, count the arrivals; the last
-    // CTA sums every partial in CTA order
-    float4* mine = reinterpret_cast<float4*>(
-        p.part + ((int64_t)c * 2 + slot_of(c, t, g.U, C, g.KB)) * kTileFloats);
+    // Split tile.  Its owner is the CTA holding its first units (cf): they
+    // come at the end of that CTA's range, so the other contributors, which
+    // meet the tile at the start of theirs, have usually published already.
+    if (c != cf) {
+      float4* mine = reinterpret_cast<float4*>(
+          p.part + ((int64_t)c * 2 + slot_of(c, t, g.U, C, g.KB)) * kTileFloats);
+      const float4* tb4 = reinterpret_cast<const float4*>(tb);
+#pragma unroll
+      for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i)
+        mine[et + i * kEpiThreads] = tb4[et + i * kEpiThreads];
+      epi_bar();
+      if (et == 0) {
+        __threadfence();  // cumulative over the group's stores (ordered by the barrier)
+        atomicAdd(&p.cnt[t], 1);
+      }
+      return;
+    }
+    if (et == 0) wait_contributors(&p.cnt[t], cl - cf, p.err, 0x660);
+    epi_bar();
+    // sum in CTA order: the owner's own partial first, then cf+1 .. cl
+    float4 a[kTileFloats / 4 / kEpiThreads];
     const float4* tb4 = reinterpret_cast<const float4*>(tb);
 #pragma unroll
-    for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i)
-      mine[et + i * kEpiThreads] = tb4[et + i * kEpiThreads];
-    __threadfence();
-    epi_bar();
-    if (et == 0) {
-      const int old = atomicAdd(&p.cnt[t], 1);
-      const int last = old == cl - cf;
-      if (last) p.cnt[t] = 0;
-      *S.flag = last;
-    }
-    epi_bar();
-    if (!*S.flag) return;
-    __threadfence();
-    float4 a[kTileFloats / 4 / kEpiThreads];
-#pragma unroll
-    for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int cc = cf; cc <= cl; ++cc) {
-      const float4* src = reinterpret_cast<const float4*>(
+    for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) a[i] = tb4[et + i * kEpiThreads];
+    for (int cc = cf + 1; cc <= cl; cc += 2) {
+      // two partials' loads in flight per round trip
+      const bool two = cc + 1 <= cl;
+      const float4* src0 = reinterpret_cast<const float4*>(
           p.part + ((int64_t)cc * 2 + slot_of(cc, t, g.U, C, g.KB)) * kTileFloats);
-      float4 v[kTileFloats / 4 / kEpiThreads];
-#pragma unroll
-      for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) v[i] = __ldcg(src + et + i * kEpiThreads);
+      const float4* src1 = two ? reinterpret_cast<const float4*>(
+          p.part + ((int64_t)(cc + 1) * 2 + slot_of(cc + 1, t, g.U, C, g.KB)) * kTileFloats)
+                               : src0;
+      float4 v0[kTileFloats / 4 / kEpiThreads], v1[kTileFloats / 4 / kEpiThreads];
 #pragma unroll
       for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) {
-        a[i].x += v[i].x; a[i].y += v[i].y; a[i].z += v[i].z; a[i].w += v[i].w;
+        v0[i] = __ldcg(src0 + et + i * kEpiThreads);
+        v1[i] = two ? __ldcg(src1 + et + i * kEpiThreads) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) {
+        a[i].x += v0[i].x; a[i].y += v0[i].y; a[i].z += v0[i].z; a[i].w += v0[i].w;
+        if (two) {
+          a[i].x += v1[i].x; a[i].y += v1[i].y; a[i].z += v1[i].z; a[i].w += v1[i].w;
+        }
       }
     }
+    epi_bar();  // every thread has read its own slice of tb
     float4* tbw = reinterpret_cast<float4*>(tb);
 #pragma unroll
     for (int i = 0; i < kTileFloats / 4 / kEpiThreads; ++i) tbw[et + i * kEpiThreads] = a[i];
@@ -641,79 +677,73 @@ __device__ __forceinline__ void epi_att(const Params& p, const Layer& Ly, const 
   }
   const int cf = owner(pair * nt, g.U, C), cl = owner(pair * nt + nt - 1, g.U, C);
   const bool split = cl > cf;
+  const bool own = !split || c == cf;  // the owner merges (see epi_proj)
   float* ap = p.apart + ((int64_t)c * 2 + slot_of(c, pair, g.U, C, nt)) * (G * (kHD + 2));
+  float M[G], A0[G], A1[G], Ls[G];
 #pragma unroll
   for (int gg = 0; gg < G; ++gg) {
-    float M = s_new[gg];
+    float Mx = s_new[gg];
 #pragma unroll
-    for (int w = 0; w < kCons; ++w) M = fmaxf(M, ml[(w * G + gg) * 2]);
+    for (int w = 0; w < kCons; ++w) Mx = fmaxf(Mx, ml[(w * G + gg) * 2]);
     float a0 = 0.f, a1 = 0.f, lsm = 0.f;
 #pragma unroll
     for (int w = 0; w < kCons; ++w) {
       const float mw = ml[(w * G + gg) * 2];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - Mx);
       a0 = fmaf(f, tb[(w * G + gg) * kHD + d0], a0);
       a1 = fmaf(f, tb[(w * G + gg) * kHD + d1], a1);
       lsm = fmaf(f, ml[(w * G + gg) * 2 + 1], lsm);
     }
     if (with_new) {
-      const float f = exp2f(s_new[gg] - M);
+      const float f = exp2f(s_new[gg] - Mx);
       a0 = fmaf(f, vn0, a0);
       a1 = fmaf(f, vn1, a1);
       lsm += f;
     }
-    if (!split) {
-      __nv_bfloat16* out = p.A + ((int64_t)b * p.Hq + kvh * G + gg) * kHD;
-      out[d0] = f2bf(lsm > 0.f ? a0 / lsm : 0.f);
-      out[d1] = f2bf(lsm > 0.f ? a1 / lsm : 0.f);
-    } else {
+    M[gg] = Mx; A0[gg] = a0; A1[gg] = a1; Ls[gg] = lsm;
+    if (!own) {
       ap[gg * (kHD + 2) + 2 + d0] = a0;
       ap[gg * (kHD + 2) + 2 + d1] = a1;
       if (et == 0) {
-        ap[gg * (kHD + 2)] = M;
+        ap[gg * (kHD + 2)] = Mx;
         ap[gg * (kHD + 2) + 1] = lsm;
       }
     }
   }
-  if (!split) return;
-  __threadfence();
-  epi_bar();
-  if (et == 0) {
-    const int old = atomicAdd(&p.cnt[pair], 1);
-    const int last = old == cl - cf;
-    if (last) p.cnt[pair] = 0;
-    *S.flag = last;
-  }
-  epi_bar();
-  if (!*S.flag) return;
-  __threadfence();
-  // merge the segments in CTA order (online: running max, rescaled sums)
-  float M[G], A0[G], A1[G], Ls[G];
-#pragma unroll
-  for (int gg = 0; gg < G; ++gg) {
-    M[gg] = -INFINITY;
-    A0[gg] = A1[gg] = Ls[gg] = 0.f;
-  }
-  for (int cc = cf; cc <= cl; ++cc) {
-    const float* q2 = p.apart + ((int64_t)cc * 2 + slot_of(cc, pair, g.U, C, nt)) * (G * (kHD + 2));
-    float ms[G], ls[G], x0[G], x1[G];
-#pragma unroll
-    for (int gg = 0; gg < G; ++gg) {
-      ms[gg] = __ldcg(q2 + gg * (kHD + 2));
-      ls[gg] = __ldcg(q2 + gg * (kHD + 2) + 1);
-      x0[gg] = __ldcg(q2 + gg * (kHD + 2) + 2 + d0);
-      x1[gg] = __ldcg(q2 + gg * (kHD + 2) + 2 + d1);
+  if (!own) {
+    epi_bar();
+    if (et == 0) {
+      __threadfence();
+      atomicAdd(&p.cnt[pair], 1);
     }
+    return;
+  }
+  if (split) {
+    if (et == 0) wait_contributors(&p.cnt[pair], cl - cf, p.err, 0x661);
+    epi_bar();
+    // merge the other segments in CTA order (online: running max, rescaled sums)
+    for (int cc = cf + 1; cc <= cl; ++cc) {
+      const float* q2 =
+          p.apart + ((int64_t)cc * 2 + slot_of(cc, pair, g.U, C, nt)) * (G * (kHD + 2));
+      float ms[G], ls[G], x0[G], x1[G];
 #pragma unroll
-    for (int gg = 0; gg < G; ++gg) {
-      if (ms[gg] == -INFINITY) continue;
-      const float Mn = fmaxf(M[gg], ms[gg]);
-      const float fo = (M[gg] == -INFINITY) ? 0.f : exp2f(M[gg] - Mn);
-      const float fn = exp2f(ms[gg] - Mn);
-      A0[gg] = A0[gg] * fo + fn * x0[gg];
-      A1[gg] = A1[gg] * fo + fn * x1[gg];
-      Ls[gg] = Ls[gg] * fo + fn * ls[gg];
-      M[gg] = Mn;
+      for (int gg = 0; gg < G; ++gg) {
+        ms[gg] = __ldcg(q2 + gg * (kHD + 2));
+        ls[gg] = __ldcg(q2 + gg * (kHD + 2) + 1);
+        x0[gg] = __ldcg(q2 + gg * (kHD + 2) + 2 + d0);
+        x1[gg] = __ldcg(q2 + gg * (kHD + 2) + 2 + d1);
+      }
+#pragma unroll
+      for (int gg = 0; gg < G; ++gg) {
+        if (ms[gg] == -INFINITY) continue;
+        const float Mn = fmaxf(M[gg], ms[gg]);
+        const float fo = (M[gg] == -INFINITY) ? 0.f : exp2f(M[gg] - Mn);
+        const float fn = exp2f(ms[gg] - Mn);
+        A0[gg] = A0[gg] * fo + fn * x0[gg];
+        A1[gg] = A1[gg] * fo + fn * x1[gg];
+        Ls[gg] = Ls[gg] * fo + fn * ls[gg];
+        M[gg] = Mn;
+      }
     }
   }
 #pragma unroll
