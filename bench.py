@@ -132,9 +132,9 @@ def run_ours(args):
     torch.manual_seed(0)
     dec = loader_fused.random_decoder(loader_fused.QWEN3_VL_8B, rank, world, dev, seed=0,
                                       max_seq=BUCKET)
-    # In-kernel NVLink all-reduce for decode projections (opt-in: faster than
-    # GEMV + NCCL in isolation, not yet inside the full decode graph).
-    peer_ar = world > 1 and os.environ.get("Q3VL_PEER_AR", "0") == "1"
+    # Decode o_proj/down all-reduce inside the projection kernel over NVLink
+    # peer memory (Q3VL_PEER_AR=0 times the NCCL path instead).
+    peer_ar = world > 1 and os.environ.get("Q3VL_PEER_AR", "1") == "1"
     if peer_ar:
         dec.enable_peer_allreduce()     # decode o_proj/down: in-kernel NVLink all-reduce
     g = torch.Generator().manual_seed(1234)

@@ -195,15 +195,18 @@ Q3_API int q3_gemm_decode(const void* A, const void* W, void* C, int64_t M, int6
  * q3_gemm_ar: C = residual + sum over ranks of (A W^T), for decode shapes
  * (1 <= M <= 16, N % 64 == 0); every rank must make the same sequence of calls
  * (like the reference's collectives).  Each output tile's partial is pushed
- * to the peers from inside the kernel over NVLink and reduced in rank order,
- * so all ranks hold identical results.  residual may be NULL. */
+ * to the peers from inside the kernel over NVLink, in 8-byte words that carry
+ * the call number as their arrival flag, and reduced in rank order, so all
+ * ranks hold identical results.  residual may be NULL.  ss_out, when not NULL,
+ * receives per-64-column-tile sums of squares of C, ss_out[N/64][16], for the
+ * RMSNorm fused into the next projection (q3_gemm_decode's ss_in). */
 Q3_API int q3_comm_handle_bytes(void);
 Q3_API int q3_comm_create(int rank, int world, int64_t max_cols, void** comm_out,
                           void* ipc_handle_out);
 Q3_API int q3_comm_open_peers(void* comm, const void* all_handles);
 Q3_API int q3_comm_destroy(void* comm);
 Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
-                      const void* residual, void* comm, q3_stream_t stream);
+                      const void* residual, float* ss_out, void* comm, q3_stream_t stream);
 
 /* ---- a12/a13: the whole decode step of every layer in one launch ----------
  * Replaces forward_layer (model_fused.py:234-277) at S = 1 for all layers of

@@ -10,14 +10,11 @@ namespace q3 {
 CommDev Comm::dev() const {
   CommDev d{};
   const size_t data_bytes = comm_data_bytes(max_tiles);
-  const size_t flag_bytes = (size_t)kMaxRanks * max_tiles * sizeof(uint32_t);
   for (int r = 0; r < kMaxRanks; ++r) {
     void* base = (r == rank) ? local : peers[r];
-    d.data[r] = base ? reinterpret_cast<__nv_bfloat16*>(base) : nullptr;
-    d.flags[r] = base ? reinterpret_cast<uint32_t*>(static_cast<char*>(base) + data_bytes)
-                      : nullptr;
+    d.inbox[r] = base ? reinterpret_cast<uint2*>(base) : nullptr;
   }
-  d.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(local) + data_bytes + flag_bytes);
+  d.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(local) + data_bytes);
   d.rank = rank;
   d.world = world;
   d.max_tiles = max_tiles;
@@ -26,7 +23,7 @@ CommDev Comm::dev() const {
 
 // Decode-shaped projection with the all-reduce fused in (gemv.cu).
 int launch_gemv_ar(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                   const CommDev& comm, cudaStream_t s);
+                   float* ss_out, const CommDev& comm, cudaStream_t s);
 
 }  // namespace q3
 
@@ -103,7 +100,7 @@ extern "C" int q3_comm_destroy(void* comm) {
 }
 
 extern "C" int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
-                          const void* residual, void* comm, q3_stream_t stream) {
+                          const void* residual, float* ss_out, void* comm, q3_stream_t stream) {
   using namespace q3;
   Q3_REQUIRE(A && W && C && comm, "q3_gemm_ar: null pointer");
   Comm* c = static_cast<Comm*>(comm);
@@ -117,6 +114,6 @@ extern "C" int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int6
   Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(C, 16) &&
                  (!residual || aligned(residual, 16)),
              "q3_gemm_ar: pointers must be 16-byte aligned");
-  return launch_gemv_ar(A, W, C, residual, (int)M, (int)N, (int)K, c->dev(),
+  return launch_gemv_ar(A, W, C, residual, (int)M, (int)N, (int)K, ss_out, c->dev(),
                         (cudaStream_t)stream);
 }

@@ -5,13 +5,15 @@
 // and opened on every rank, so kernels receive plain peer pointers.
 //
 // Layout of a rank's buffer (max_tiles tiles of 64 output columns):
-//   data     [2 parities][kMaxRanks sources][max_tiles][64 cols x 16 tokens] bf16
-//   flags    [kMaxRanks sources][max_tiles] uint32   (written by the source rank)
-//   counters [max_tiles] uint32                      (local call sequence numbers)
-// A tile exchange of call number f (per tile, counted identically on every
-// rank) writes parity f & 1 and raises the source's flag to f.  Partials travel
-// as bf16, the dtype the reference all-reduces (its o_proj/down outputs are
-// bf16 tensors, model_fused.py:266-267, 273-274).
+//   inbox    [2 parities][kMaxRanks sources][max_tiles][kArWords] 8-byte words
+//   counters [max_tiles] uint32   (per-tile call numbers of this rank)
+// Each inbox word carries two bf16 partial values and the call number f that
+// wrote them, so a receiver knows a word has arrived when its flag reads f:
+// no fence, no flag store and no atomic is needed to publish a partial, and
+// 8-byte stores over NVLink land whole.  Call f uses parity f & 1; flags only
+// grow and start at 0, so stale words never match.  Partials travel as bf16,
+// the dtype the reference all-reduces (its o_proj/down outputs are bf16
+// tensors, model_fused.py:266-267, 273-274).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,11 +25,11 @@ constexpr int kMaxRanks = 8;
 constexpr int kArCols = 64;    // output columns per exchanged tile
 constexpr int kArTokens = 16;  // token slots per tile (decode M <= 16)
 constexpr int kArTileElems = kArCols * kArTokens;
+constexpr int kArWords = kArTileElems / 2;  // (2 x bf16 data, uint32 flag) words per tile
 
 struct CommDev {
-  __nv_bfloat16* data[kMaxRanks];  // base of each rank's data region (peer-mapped)
-  uint32_t* flags[kMaxRanks];   // base of each rank's flag region (peer-mapped)
-  uint32_t* counters;           // this rank's per-tile sequence numbers
+  uint2* inbox[kMaxRanks];  // each rank's inbox (peer-mapped; own for rank)
+  uint32_t* counters;       // this rank's per-tile call numbers
   int rank, world, max_tiles;
 };
 
@@ -42,11 +44,10 @@ struct Comm {
 };
 
 inline size_t comm_data_bytes(int max_tiles) {
-  return (size_t)2 * kMaxRanks * max_tiles * kArTileElems * sizeof(__nv_bfloat16);
+  return (size_t)2 * kMaxRanks * max_tiles * kArWords * sizeof(uint2);
 }
 inline size_t comm_bytes(int max_tiles) {
-  return comm_data_bytes(max_tiles) + (size_t)kMaxRanks * max_tiles * sizeof(uint32_t) +
-         (size_t)max_tiles * sizeof(uint32_t);
+  return comm_data_bytes(max_tiles) + (size_t)max_tiles * sizeof(uint32_t);
 }
 
 }  // namespace q3

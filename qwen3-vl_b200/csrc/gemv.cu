@@ -89,109 +89,133 @@ __device__ __forceinline__ uint4 rms_scale_chunk(uint4 x, float r, uint4 w) {
 __device__ __forceinline__ void consumer_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kGvConsumers * 32) : "memory");
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_acq_rel_sys() {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+__device__ __forceinline__ void st_word_peer(uint2* p, uint32_t data, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag)
                : "memory");
-  return old;
+}
+__device__ __forceinline__ uint2 ld_word_inbox(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p)
+               : "memory");
+  return v;
 }
 
 // All-reduce epilogue of one 64-column tile, run by the 128 consumer threads
 // of cluster rank 0.  part[col][tok] holds this rank's partial, already
 // rounded to bf16 like the reference's projection output.
 //
-// Protocol (one-shot, aggregated per rank): every tile CTA pushes its 2 KB
-// partial into every peer's inbox (parity f & 1 of the call number f) and
-// counts itself in with a system-scope acq_rel atomic; the last CTA of the
-// rank to arrive -- after which all of this rank's partials are released --
-// raises ONE flag per peer to f.  Every CTA then waits (bounded) for the flags
-// of all peers, and sums the ranks' bf16 partials of its tile in fp32 in rank
-// order, so every rank stores identical values.  One flag per rank instead of
-// one per tile keeps the number of system-scope fences and remote flag writes
-// independent of N.  Flags only grow, and a peer can be at most one call ahead
-// (it cannot finish call f+1 before this rank's call f pushed), so two inbox
-// parities suffice.  counters[0] holds the last completed call number and
-// counters[1] the arrival count of the call in flight.
+// Protocol (one-shot, flag in every word): the tile's call number f comes from
+// this rank's per-tile counter, which every rank advances identically (all
+// ranks make the same calls).  Each thread owns word w = (column w / 8, token
+// pair w % 8) of the tile and stores {data, f} into every peer's inbox
+// (parity f & 1, source slot = this rank) with one 8-byte store; then it
+// polls the same word of every peer in its own inbox until the flag reads f
+// (bounded wait), and sums the ranks' bf16 values in fp32 in rank order, so
+// every rank stores identical values.  A peer can be at most one call ahead
+// (it cannot finish call f+1 before receiving this rank's call f+1 words,
+// which this rank sends after its call f finished), so two parities suffice.
 __device__ __forceinline__ void allreduce_tile(const GemvParams& p, int tile, int row0,
                                                __nv_bfloat16 (*part)[kArTokens],
                                                uint32_t* f_s) {
   const int tid = threadIdx.x;  // consumers are threads 0..127
   const CommDev& cm = p.comm;
-  if (tid == 0) *f_s = ld_relaxed_sys(cm.counters) + 1u;
+  if (tid == 0) *f_s = cm.counters[tile] + 1u;  // this rank's own memory
   consumer_bar();
   const uint32_t f = *f_s;
   const int par = (int)(f & 1u);
-  const size_t slot_self = ((size_t)(par * kMaxRanks + cm.rank) * cm.max_tiles + tile) *
-                           kArTileElems;
-  const uint4* src = reinterpret_cast<const uint4*>(&part[0][0]);
+  const int pairs = (p.M + 1) >> 1;  // token pairs that carry data
+  constexpr int kWordsPerThread = kArWords / (kGvConsumers * 32);
+  uint32_t mine[kWordsPerThread];
+#pragma unroll
+  for (int i = 0; i < kWordsPerThread; ++i) {
+    const int w = tid + i * kGvConsumers * 32;
+    mine[i] = reinterpret_cast<const uint32_t*>(&part[w >> 3][0])[w & 7];
+  }
+  // push this rank's words to every peer
+  const size_t slot_self = ((size_t)(par * kMaxRanks + cm.rank) * cm.max_tiles + tile) * kArWords;
   for (int r = 0; r < cm.world; ++r) {
     if (r == cm.rank) continue;
-    uint4* dst = reinterpret_cast<uint4*>(cm.data[r] + slot_self);
-    for (int i = tid; i < kArTileElems / 8; i += kGvConsumers * 32) dst[i] = src[i];
-  }
-  // The CTA barrier orders every thread's peer stores before thread 0's
-  // system-scope fence and arrival (fences are cumulative).
-  consumer_bar();
-  if (tid == 0) {
-    fence_acq_rel_sys();
-    const uint32_t arrived = atom_add_acq_rel_sys(cm.counters + 1, 1u);
-    if (arrived == gridDim.x - 1) {  // last tile CTA of this rank
-      cm.counters[1] = 0u;
-      cm.counters[0] = f;
-      fence_acq_rel_sys();
-      for (int r = 0; r < cm.world; ++r)
-        if (r != cm.rank) st_release_sys(cm.flags[r] + (size_t)cm.rank * cm.max_tiles, f);
+    uint2* dst = cm.inbox[r] + slot_self;
+#pragma unroll
+    for (int i = 0; i < kWordsPerThread; ++i) {
+      const int w = tid + i * kGvConsumers * 32;
+      if ((w & 7) < pairs) st_word_peer(dst + w, mine[i], f);
     }
   }
-  if (tid < cm.world && tid != cm.rank) {
-    // poll with relaxed loads; one acquire fence once the flag has arrived
-    const uint32_t* fl = cm.flags[cm.rank] + (size_t)tid * cm.max_tiles;
-    if ((int)(ld_relaxed_sys(fl) - f) < 0) {
-      const uint64_t t0 = globaltimer_ns();
-      uint32_t spins = 0;
-      while ((int)(ld_relaxed_sys(fl) - f) < 0) {
-        if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
-          report_timeout(p.err, 0x501);
-          break;
-        }
-      }
-    }
-    fence_acq_rel_sys();
-  }
-  consumer_bar();
-  for (int idx = tid; idx < kArTileElems; idx += kGvConsumers * 32) {
-    const int col = idx / kArTokens, tok = idx % kArTokens;
-    const int n = row0 + col;
-    if (tok >= p.M || n >= p.N) continue;
-    float s = 0.f;
-    for (int r = 0; r < cm.world; ++r) {
+  // collect the peers' words and reduce in rank order
+  float s0[kWordsPerThread], s1[kWordsPerThread];
+#pragma unroll
+  for (int i = 0; i < kWordsPerThread; ++i) s0[i] = s1[i] = 0.f;
+  bool gave_up = false;
+  for (int r = 0; r < cm.world; ++r) {
+#pragma unroll
+    for (int i = 0; i < kWordsPerThread; ++i) {
+      const int w = tid + i * kGvConsumers * 32;
+      if ((w & 7) >= pairs) continue;
+      uint32_t d;
       if (r == cm.rank) {
-        s += bf2f(part[col][tok]);
+        d = mine[i];
       } else {
-        const size_t slot = ((size_t)(par * kMaxRanks + r) * cm.max_tiles + tile) *
-                            kArTileElems;
-        // written by the peer over NVLink after this kernel started: bypass L1
-        const unsigned short raw = __ldcg(reinterpret_cast<const unsigned short*>(
-            cm.data[cm.rank] + slot + idx));
-        s += __uint_as_float((uint32_t)raw << 16);
+        const uint2* src = cm.inbox[cm.rank] +
+                           ((size_t)(par * kMaxRanks + r) * cm.max_tiles + tile) * kArWords + w;
+        uint2 v = ld_word_inbox(src);
+        if (v.y != f && !gave_up) {
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t spins = 0;
+          while ((v = ld_word_inbox(src)).y != f) {
+            if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+              report_timeout(p.err, 0x501);
+              gave_up = true;
+              break;
+            }
+          }
+        }
+        d = v.x;
       }
+      const float2 fv = unpack_bf16x2(d);
+      s0[i] += fv.x;
+      s1[i] += fv.y;
     }
-    float val = rbf(s);
-    if (p.R) val = bf2f(p.R[(int64_t)tok * p.ldc + n]) + val;
-    p.C[(int64_t)tok * p.ldc + n] = f2bf(val);
   }
+  // every thread holds token pair tid & 7 (128 threads cover 8 pairs x 16 columns)
+  float sq0 = 0.f, sq1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kWordsPerThread; ++i) {
+    const int w = tid + i * kGvConsumers * 32;
+    const int col = w >> 3, tok0 = (w & 7) * 2;
+    const int n = row0 + col;
+    if (n >= p.N) continue;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int tok = tok0 + e;
+      if (tok >= p.M) continue;
+      float val = rbf(e ? s1[i] : s0[i]);
+      if (p.R) val = bf2f(p.R[(int64_t)tok * p.ldc + n]) + val;
+      const __nv_bfloat16 o = f2bf(val);
+      p.C[(int64_t)tok * p.ldc + n] = o;
+      const float vr = bf2f(o);
+      if (e) sq1 = fmaf(vr, vr, sq1);
+      else sq0 = fmaf(vr, vr, sq0);
+    }
+  }
+  if (p.ss_out) {
+    // per-tile sums of squares of the stored outputs (identical on every rank)
+    // for the RMSNorm fused into the next projection
+    __shared__ float ssw[kGvConsumers][16];
+    sq0 += __shfl_xor_sync(0xffffffffu, sq0, 8);
+    sq0 += __shfl_xor_sync(0xffffffffu, sq0, 16);
+    sq1 += __shfl_xor_sync(0xffffffffu, sq1, 8);
+    sq1 += __shfl_xor_sync(0xffffffffu, sq1, 16);
+    const int lane = tid & 31, warp = tid >> 5;
+    if (lane < 8) {
+      ssw[warp][2 * lane] = sq0;
+      ssw[warp][2 * lane + 1] = sq1;
+    }
+    consumer_bar();
+    if (tid < 16)
+      p.ss_out[tile * 16 + tid] = ssw[0][tid] + ssw[1][tid] + ssw[2][tid] + ssw[3][tid];
+  }
+  if (tid == 0) cm.counters[tile] = f;
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
@@ -222,6 +246,7 @@ __device__ __forceinline__ void gemv_normaliser(const GemvParams& p, uint32_t ri
     for (int tok = 0; tok < p.M; ++tok) {
       const uint4* xr = reinterpret_cast<const uint4*>(p.A + (int64_t)tok * p.K);
       float ss = 0.f;
+#pragma unroll 8
       for (int v = lane; v < p.K / 8; v += 32) {
         const uint4 u = xr[v];
         const uint32_t us[4] = {u.x, u.y, u.z, u.w};
@@ -559,9 +584,10 @@ int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int
 }
 
 int launch_gemv_ar(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                   const CommDev& comm, cudaStream_t s) {
+                   float* ss_out, const CommDev& comm, cudaStream_t s) {
   if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
-  const GemvOpts o;
+  GemvOpts o;
+  o.ss_out = ss_out;
   return M > 8 ? launch_gemv_t<2, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o)
                : launch_gemv_t<1, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o);
 }

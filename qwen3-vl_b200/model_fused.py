@@ -275,8 +275,10 @@ class Qwen3VLDecoderFused:
     # ----------------------------------------------------------------- layer
     def _ss_ok(self, B: int, S: int) -> bool:
         """True when the last layer's down projection left the sums of squares
-        of its output rows in _ss_buf(1) (the TP1 decode path)."""
-        return (B * S <= 16 and self.tp_size == 1 and self.num_layers > 0 and self.fuse_norm and
+        of its output rows in _ss_buf(1) (decode at TP1, or with the in-kernel
+        all-reduce, whose outputs are identical on every rank)."""
+        return (B * S <= 16 and (self.tp_size == 1 or self.comm is not None) and
+                self.num_layers > 0 and self.fuse_norm and
                 self.layers[-1].attn_block.qkv_bias is None)
 
     def _ss_buf(self, i: int) -> torch.Tensor:
@@ -299,8 +301,11 @@ class Qwen3VLDecoderFused:
         H = x.shape[-1]
         T = B * S
         decode = T <= 16
-        fast = (decode and self.tp_size == 1 and ab.qkv_bias is None and H <= 256 * 64 and
-                self.fuse_norm)
+        peer = self.tp_size > 1 and self.comm is not None and decode
+        # decode with per-tile sums of squares handed between projections: every
+        # RMSNorm runs inside the projection that consumes it
+        fast = (decode and (self.tp_size == 1 or peer) and ab.qkv_bias is None and
+                H <= 256 * 64 and self.fuse_norm)
         if pend is not None:
             xn = torch.empty_like(x)
             h = ops.rmsnorm(pend, ab.input_norm_weight, ab.eps, add=x, h_out=xn)
@@ -338,15 +343,22 @@ class Qwen3VLDecoderFused:
         if fast:
             # o_proj + residual (emits the sums of squares of x2), gate/up with the
             # post-attention norm fused in, down + residual (emits them for the next
-            # layer's input norm)
-            x2 = ops.gemm_decode(attn, L.o_proj.weight_km, "residual", residual=x,
+            # layer's input norm); at TP>1 both row-parallel projections all-reduce
+            # from inside the kernel
+            if peer:
+                x2 = ops.gemm_ar(attn, L.o_proj.weight_km, self.comm, residual=x,
                                  ss_out=self._ss_buf(0))
+            else:
+                x2 = ops.gemm_decode(attn, L.o_proj.weight_km, "residual", residual=x,
+                                     ss_out=self._ss_buf(0))
             act = ops.gemm_decode(x2, mlp.gate_up_weight_il, "swiglu",
                                   norm_w=mlp.post_norm_weight, eps=mlp.eps,
                                   ss_in=self._ss_buf(0), ss_tiles=H // 64)
+            if peer:
+                return ops.gemm_ar(act, mlp.down_weight_km, self.comm, residual=x2,
+                                   ss_out=self._ss_buf(1)), None
             return ops.gemm_decode(act, mlp.down_weight_km, "residual", residual=x2,
                                    ss_out=self._ss_buf(1)), None
-        peer = self.tp_size > 1 and self.comm is not None and decode
         h2 = None
         if self.tp_size == 1:
             x2 = ops.gemm(attn, L.o_proj.weight_km, "residual", residual=x)

@@ -59,7 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "q3_comm_create": (I32, [I32, I32, I64, ctypes.POINTER(P), P]),
     "q3_comm_open_peers": (I32, [P, P]),
     "q3_comm_destroy": (I32, [P]),
-    "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P]),
+    "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P, P]),
     "q3_decode_step_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64,
                                     ctypes.POINTER(P)]),
     "q3_decode_step": (I32, [P, P, P, P, I64, P]),

@@ -355,11 +355,12 @@ class DecodeStepPlan:
 
 
 def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
-            out: torch.Tensor = None) -> torch.Tensor:
+            out: torch.Tensor = None, ss_out: torch.Tensor = None) -> torch.Tensor:
     """C = residual + all_reduce_sum(a @ w.T) over the communicator's ranks
     (decode shapes: a has 1..16 rows).  Every rank must call this in the same
-    order, as with a collective."""
-    _cuda("gemm_ar", a, w, residual, out)
+    order, as with a collective.  `ss_out` (float32, (N/64) x 16) receives the
+    per-tile sums of squares of C for a following norm-fused projection."""
+    _cuda("gemm_ar", a, w, residual, out, ss_out)
     _bf16("gemm_ar", a, w, residual, out)
     _contig("gemm_ar", a, w, residual, out)
     K = a.shape[-1]
@@ -369,7 +370,10 @@ def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = Non
         out = torch.empty(*a.shape[:-1], N, dtype=torch.bfloat16, device=a.device)
     if residual is not None and residual.numel() != M * N:
         raise ValueError("gemm_ar: residual must be [M, N]")
-    call("q3_gemm_ar", _p(a), _p(w), _p(out), M, N, K, _p(residual), comm.handle, _stream())
+    if ss_out is not None and (ss_out.dtype != torch.float32 or ss_out.numel() < (N // 64) * 16):
+        raise ValueError("gemm_ar: ss_out must be float32 [N/64, 16]")
+    call("q3_gemm_ar", _p(a), _p(w), _p(out), M, N, K, _p(residual), _p(ss_out), comm.handle,
+         _stream())
     return out
 
 

@@ -61,16 +61,21 @@ def _worker(rank, world, port, q):
         Ws = [(torch.randn(N, K, generator=g_) * 0.05).to(torch.bfloat16) for g_ in gen]
         R = torch.randn(M, N, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
         outs = []
-        for _ in range(3):   # repeated calls exercise the flag/parity protocol
+        ss = torch.full((N // 64, 16), float("nan"), device=dev)
+        for i in range(3):   # repeated calls exercise the flag/parity protocol
             outs.append(ops.gemm_ar(As[rank].to(dev), Ws[rank].to(dev), dec.comm,
-                                    residual=R.to(dev)).cpu())
+                                    residual=R.to(dev), ss_out=ss if i == 2 else None).cpu())
+        # per-64-column sums of squares of the stored output, for the next norm
+        want_ss = (outs[-1].float() ** 2).view(M, N // 64, 64).sum(-1).t()
+        ss_ok = bool(torch.allclose(ss[:, :M].cpu(), want_ss, rtol=1e-4) and
+                     torch.all(ss[:, M:] == 0).item())
         want = R.float() + sum((As[r].float() @ Ws[r].float().t()) for r in range(world))
         gathered = [torch.zeros(M, N, dtype=torch.bfloat16, device=dev) for _ in range(world)]
         dist.all_gather(gathered, outs[-1].to(dev))
         same = all(torch.equal(gathered[0].cpu(), x.cpu()) for x in gathered)
         err = max((o.float() - want).abs().max().item() for o in outs)
         if rank == 0:
-            q.put((logits.numpy(), toks, toks_peer, err, same))
+            q.put((logits.numpy(), toks, toks_peer, err, same, ss_ok))
         dist.barrier()
         dec.close()
         dist.barrier()
@@ -91,7 +96,7 @@ def test_tp2_decoder_matches_reference():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    logits, toks, toks_peer, err, same = q.get(timeout=300)
+    logits, toks, toks_peer, err, same, ss_ok = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -106,3 +111,4 @@ def test_tp2_decoder_matches_reference():
     assert toks_peer == want, f"peer all-reduce: first mismatch at step {first_diff(toks_peer)}"
     assert same, "ranks disagree on the all-reduced projection"
     assert err < 0.25, f"gemm_ar max-abs {err} (bf16 output of magnitude ~10)"
+    assert ss_ok, "gemm_ar sums of squares (ss_out) disagree with the stored output"
