@@ -158,6 +158,22 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
 Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
             const void* aux, q3_stream_t stream);
 
+/* Prefill QKV projection with its epilogue fused (tcgen05 GEMM): h @ Wqkv
+ * (model_fused.py:103) followed by the per-head QK-RMSNorm, rotate-half RoPE
+ * and KV-cache write of AttentionBlock.forward (:107-129) and forward_layer
+ * (:244-246), without materialising qkv.  A bf16 [B*S, hidden] (the normed
+ * input rows, B*S > 16); W bf16 [(Hq+2*Hkv)*128, hidden] K-major, rows
+ * [q | k | v]; RoPE rows, tables and outputs as for q3_qkv_norm_rope (token
+ * (b, s) sits at cache position start_pos + s; the tables must hold every
+ * row the tokens use).  q_out bf16 [B, Hq, S, 128]; k_cache/v_cache bf16
+ * [B, Hkv, max_seq, 128] written at start_pos .. start_pos + S - 1. */
+Q3_API int q3_gemm_qkv_rope(const void* A, const void* W, int64_t hidden, const void* q_norm_w,
+                            const void* k_norm_w, const void* cos, const void* sin, int cs_dtype,
+                            int cs_use_pos, int64_t cs_offset, int64_t cs_stride_b, void* q_out,
+                            void* k_cache, void* v_cache, int B, int S, int Hq, int Hkv,
+                            int head_dim, int64_t start_pos, int64_t max_seq, float eps,
+                            q3_stream_t stream);
+
 /* Decode projection with the preceding RMSNorm fused in: C = epilogue(
  * rmsnorm(A; norm_w, eps) W^T) for 1 <= M <= 16, where rmsnorm is
  * model_fused.py:37-40 over the full row of A (the input norm of

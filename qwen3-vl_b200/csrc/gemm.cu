@@ -46,13 +46,65 @@ struct TcCfg {
   static constexpr int kTmemCols = 2 * BN;
 };
 
+// Internal epilogue id of the fused QKV projection: per-head QK-RMSNorm,
+// rotate-half RoPE and the KV-cache write (AttentionBlock.forward after the
+// matmul, model_fused.py:107-129, and the cache write, :244-246).
+constexpr int kEpiQkvRope = 3;
+
+struct TcQkv {
+  const __nv_bfloat16* q_norm;  // [128]
+  const __nv_bfloat16* k_norm;  // [128]
+  const void* cos;              // [rows, 64] bf16 or f32
+  const void* sin;
+  int cs_f32, cs_use_pos;
+  int64_t cs_offset, cs_stride_b;
+  __nv_bfloat16* q_out;    // [B, Hq, S, 128]
+  __nv_bfloat16* k_cache;  // [B, Hkv, max_seq, 128], rows start_pos .. start_pos + S - 1
+  __nv_bfloat16* v_cache;
+  int S, Hq, Hkv;
+  int64_t start_pos, max_seq;
+  float eps;
+};
+
 struct TcParams {
   __nv_bfloat16* C;
   const __nv_bfloat16* R;
   int M, N, K, ldc;
   int m_tiles, n_tiles;
   int* err;
+  TcQkv qkv;  // kEpiQkvRope only
 };
+
+// 8 consecutive RoPE table entries (bf16 tables as RotaryEmbedding builds them;
+// f32 M-RoPE rows are rounded to bf16 as the reference casts them to x.dtype)
+__device__ __forceinline__ void load8_cs(const TcQkv& q, const void* tab, int64_t row, int j,
+                                         float (&v)[8]) {
+  if (q.cs_f32) {
+    const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(tab) + row * 64 + j);
+    const float4 a = f[0], b = f[1];
+    v[0] = rbf(a.x); v[1] = rbf(a.y); v[2] = rbf(a.z); v[3] = rbf(a.w);
+    v[4] = rbf(b.x); v[5] = rbf(b.y); v[6] = rbf(b.z); v[7] = rbf(b.w);
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(
+        static_cast<const __nv_bfloat16*>(tab) + row * 64 + j);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+__device__ __forceinline__ void unpack8(uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -163,6 +215,103 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const int row = mt * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(sub * 32) << 16);
+      if constexpr (EPI == kEpiQkvRope) {
+        // The tile's columns are whole heads (BN = 2 x 128; rows of W are
+        // [q heads | k heads | v heads] x 128); this thread owns token `row`.
+        const TcQkv& q = p.qkv;
+        const int b = row / q.S, s = row - (row / q.S) * q.S;
+        const int64_t pos = q.start_pos + s;  // cache row of this token
+        // RoPE row, as q3_qkv_norm_rope: base position + offset + b * stride + s
+        const int64_t crow =
+            q.cs_use_pos * q.start_pos + q.cs_offset + (int64_t)b * q.cs_stride_b + s;
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) {
+          const int head = nt * (BN / 128) + hh;
+          if (head * 128 >= p.N) break;
+          const uint32_t t_head = t_row + hh * 128;
+          if (head >= q.Hq + q.Hkv) {
+            // value head: the bf16 projection output goes to the cache
+            const int hv = head - q.Hq - q.Hkv;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld_32cols(t_head + c * 32, r);
+              tc_wait_ld();
+              if (row < p.M) {
+                uint4* dst = reinterpret_cast<uint4*>(
+                    q.v_cache + (((int64_t)b * q.Hkv + hv) * q.max_seq + pos) * 128 + c * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  uint32_t o[4];
+#pragma unroll
+                  for (int i = 0; i < 4; ++i)
+                    o[i] = pack_bf16x2(__uint_as_float(r[v * 8 + 2 * i]),
+                                       __uint_as_float(r[v * 8 + 2 * i + 1]));
+                  dst[v] = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+              }
+            }
+            continue;
+          }
+          // q or k head: RMSNorm over the head's 128 bf16 values, then RoPE
+          float ss = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32cols(t_head + c * 32, r);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float v = rbf(__uint_as_float(r[i]));
+              ss = fmaf(v, v, ss);
+            }
+          }
+          const float rr = 1.0f / sqrtf(ss * (1.0f / 128) + q.eps);  // IEEE, as torch.rsqrt on CPU
+          const bool is_q = head < q.Hq;
+          const __nv_bfloat16* nw = is_q ? q.q_norm : q.k_norm;
+          __nv_bfloat16* dst_row =
+              is_q ? q.q_out + (((int64_t)b * q.Hq + head) * q.S + s) * 128
+                   : q.k_cache + (((int64_t)b * q.Hkv + (head - q.Hq)) * q.max_seq + pos) * 128;
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            // dims c*32 .. +31 (lo) pair with dims 64 + c*32 .. +31 (hi)
+            uint32_t lo[32], hi[32];
+            tmem_ld_32cols(t_head + c * 32, lo);
+            tmem_ld_32cols(t_head + 64 + c * 32, hi);
+            tc_wait_ld();
+            if (row >= p.M) continue;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int j = c * 32 + g * 8;  // table column of both halves
+              float co[8], si[8], wl[8], wh[8];
+              load8_cs(q, q.cos, crow, j, co);
+              load8_cs(q, q.sin, crow, j, si);
+              unpack8(*reinterpret_cast<const uint4*>(nw + j), wl);
+              unpack8(*reinterpret_cast<const uint4*>(nw + 64 + j), wh);
+              uint32_t olo[4], ohi[4];
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                float a[2], bb[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const float nl = rbf(rbf(rbf(__uint_as_float(lo[g * 8 + i + e])) * rr) * wl[i + e]);
+                  const float nh = rbf(rbf(rbf(__uint_as_float(hi[g * 8 + i + e])) * rr) * wh[i + e]);
+                  a[e] = rbf(nl * co[i + e]) + rbf(-nh * si[i + e]);
+                  bb[e] = rbf(nh * co[i + e]) + rbf(nl * si[i + e]);
+                }
+                olo[i / 2] = pack_bf16x2(a[0], a[1]);
+                ohi[i / 2] = pack_bf16x2(bb[0], bb[1]);
+              }
+              *reinterpret_cast<uint4*>(dst_row + j) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+              *reinterpret_cast<uint4*>(dst_row + 64 + j) =
+                  make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -245,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------
 template <int BN, int EPI>
 static int launch_tc(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                     cudaStream_t s) {
+                     cudaStream_t s, const TcQkv* qkv = nullptr) {
   using Cfg = TcCfg<BN>;
   CUtensorMap ta, tw;
   int rc = make_tmap_2d(&ta, A, M, K, kBM, kBK);
@@ -268,6 +417,7 @@ static int launch_tc(const void* A, const void* W, void* C, const void* R, int M
   p.m_tiles = (M + kBM - 1) / kBM;
   p.n_tiles = (N + BN - 1) / BN;
   p.err = device_error_word();
+  p.qkv = qkv ? *qkv : TcQkv{};
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   return launch_ex(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kTcThreads), Cfg::kSmem, s, 1, ta,
@@ -346,4 +496,48 @@ extern "C" int q3_gemm_decode(const void* A, const void* W, void* C, int64_t M, 
   o.ss_tiles = ss_tiles;
   o.ss_out = ss_out;
   return launch_gemv(A, W, C, aux, (int)M, (int)N, (int)K, epilogue, (cudaStream_t)stream, o);
+}
+
+extern "C" int q3_gemm_qkv_rope(const void* A, const void* W, int64_t hidden, const void* q_norm_w,
+                                const void* k_norm_w, const void* cos, const void* sin,
+                                int cs_dtype, int cs_use_pos, int64_t cs_offset,
+                                int64_t cs_stride_b, void* q_out, void* k_cache, void* v_cache,
+                                int B, int S, int Hq, int Hkv, int head_dim, int64_t start_pos,
+                                int64_t max_seq, float eps, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && W && q_norm_w && k_norm_w && cos && sin && q_out && k_cache && v_cache,
+             "q3_gemm_qkv_rope: null pointer");
+  Q3_REQUIRE(head_dim == 128, "q3_gemm_qkv_rope: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && (int64_t)B * S > 16 &&
+                 (int64_t)B * S < (1ll << 31),
+             "q3_gemm_qkv_rope: needs B*S > 16 tokens (prefill); B=%d S=%d", B, S);
+  Q3_REQUIRE(hidden > 0 && hidden % 32 == 0 && hidden < (1ll << 31),
+             "q3_gemm_qkv_rope: hidden=%lld must be a multiple of 32", (long long)hidden);
+  Q3_REQUIRE(cs_dtype == Q3_F32 || cs_dtype == Q3_BF16, "q3_gemm_qkv_rope: bad cs_dtype");
+  Q3_REQUIRE(start_pos >= 0 && start_pos + S <= max_seq,
+             "q3_gemm_qkv_rope: positions %lld..%lld outside the cache (%lld rows)",
+             (long long)start_pos, (long long)(start_pos + S - 1), (long long)max_seq);
+  Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(q_norm_w, 16) && aligned(k_norm_w, 16) &&
+                 aligned(cos, 16) && aligned(sin, 16) && aligned(q_out, 16) &&
+                 aligned(k_cache, 16) && aligned(v_cache, 16),
+             "q3_gemm_qkv_rope: pointers must be 16-byte aligned");
+  TcQkv q;
+  q.q_norm = (const __nv_bfloat16*)q_norm_w;
+  q.k_norm = (const __nv_bfloat16*)k_norm_w;
+  q.cos = cos;
+  q.sin = sin;
+  q.cs_f32 = cs_dtype == Q3_F32;
+  q.cs_use_pos = cs_use_pos ? 1 : 0;
+  q.cs_offset = cs_offset;
+  q.cs_stride_b = cs_stride_b;
+  q.q_out = (__nv_bfloat16*)q_out;
+  q.k_cache = (__nv_bfloat16*)k_cache;
+  q.v_cache = (__nv_bfloat16*)v_cache;
+  q.S = S; q.Hq = Hq; q.Hkv = Hkv;
+  q.start_pos = start_pos;
+  q.max_seq = max_seq;
+  q.eps = eps;
+  const int M = B * S, N = (Hq + 2 * Hkv) * 128;
+  return launch_tc<256, kEpiQkvRope>(A, W, nullptr, nullptr, M, N, (int)hidden,
+                                     (cudaStream_t)stream, &q);
 }

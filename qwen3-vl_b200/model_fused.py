@@ -229,6 +229,8 @@ class Qwen3VLDecoderFused:
         # decode graphs: every layer in one persistent kernel (q3_decode_step);
         # opt-in until it beats the per-kernel decode step
         self.use_step_kernel = os.environ.get("Q3VL_STEP_KERNEL", "0") == "1"
+        # prefill: QK-norm, RoPE and the KV write in the QKV GEMM's epilogue
+        self.fuse_qkv = os.environ.get("Q3VL_FUSE_QKV", "1") != "0"
         self._step_plans = {}
         self._ss_step = None
 
@@ -306,18 +308,25 @@ class Qwen3VLDecoderFused:
         # RMSNorm runs inside the projection that consumes it
         fast = (decode and (self.tp_size == 1 or peer) and ab.qkv_bias is None and
                 H <= 256 * 64 and self.fuse_norm)
+        # prefill without a QKV bias: the QKV GEMM's epilogue applies the head
+        # norms and RoPE and writes the caches (no qkv tensor)
+        fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv
+        qkv = None
         if pend is not None:
             xn = torch.empty_like(x)
             h = ops.rmsnorm(pend, ab.input_norm_weight, ab.eps, add=x, h_out=xn)
             x = xn
-            qkv = ab.qkv(h)
+            if not fused_qkv:
+                qkv = ab.qkv(h)
         elif decode and ab.qkv_bias is None and self.fuse_norm:
             # decode: the input RMSNorm runs inside the QKV projection
             ss = self._ss_buf(1) if (fast and ss_valid) else None
             qkv = ops.gemm_decode(x, ab.qkv_weight_km, norm_w=ab.input_norm_weight, eps=ab.eps,
                                   ss_in=ss, ss_tiles=H // 64)
         else:
-            qkv = ab.qkv(ops.rmsnorm(x, ab.input_norm_weight, ab.eps))
+            h = ops.rmsnorm(x, ab.input_norm_weight, ab.eps)
+            if not fused_qkv:
+                qkv = ab.qkv(h)
         kc, vc = kv_cache[layer_idx]
         if rope is None:
             cos, sin, _ = self.rotary.tables(self.device)
@@ -325,10 +334,19 @@ class Qwen3VLDecoderFused:
         else:
             cos, sin = rope
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
-        q, _, _ = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B, S=S,
-                                    Hq=ab.num_q_heads, Hkv=ab.num_kv_heads, start_pos=start_pos,
-                                    pos_dev=pos_dev, cs_use_pos=cs_use_pos, cs_offset=cs_offset,
-                                    cs_stride_b=cs_stride_b, k_cache=kc, v_cache=vc, eps=ab.eps)
+        if fused_qkv:
+            q = ops.gemm_qkv_rope(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
+                                  ab.k_norm_weight, cos, sin, B=B, S=S, Hq=ab.num_q_heads,
+                                  Hkv=ab.num_kv_heads, k_cache=kc, v_cache=vc,
+                                  start_pos=start_pos, cs_use_pos=cs_use_pos, cs_offset=cs_offset,
+                                  cs_stride_b=cs_stride_b, eps=ab.eps)
+        else:
+            q, _, _ = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B,
+                                        S=S, Hq=ab.num_q_heads, Hkv=ab.num_kv_heads,
+                                        start_pos=start_pos, pos_dev=pos_dev,
+                                        cs_use_pos=cs_use_pos, cs_offset=cs_offset,
+                                        cs_stride_b=cs_stride_b, k_cache=kc, v_cache=vc,
+                                        eps=ab.eps)
         if S == 1:
             bound = kv_bound if kv_bound is not None else start_pos + 1
             attn = ops.attn_decode(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,

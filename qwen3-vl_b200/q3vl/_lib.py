@@ -54,6 +54,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, P, P, P, P]),
     "q3_gemm": (I32, [P, P, P, I64, I64, I64, I32, P, P]),
     "q3_gemm_norm": (I32, [P, P, F32, P, P, I64, I64, I64, I32, P, P]),
+    "q3_gemm_qkv_rope": (I32, [P, P, I64, P, P, P, P, I32, I32, I64, I64, P, P, P, I32, I32,
+                               I32, I32, I32, I64, I64, F32, P]),
     "q3_gemm_decode": (I32, [P, P, P, I64, I64, I64, I32, P, P, F32, P, I32, P, P]),
     "q3_comm_handle_bytes": (I32, []),
     "q3_comm_create": (I32, [I32, I32, I64, ctypes.POINTER(P), P]),

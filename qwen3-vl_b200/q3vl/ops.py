@@ -249,6 +249,33 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none", residual: tor
     return out
 
 
+def gemm_qkv_rope(h: torch.Tensor, w: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *, B: int,
+                  S: int, Hq: int, Hkv: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  start_pos: int = 0, cs_use_pos: bool = True, cs_offset: int = 0,
+                  cs_stride_b: int = 0, eps: float = 1e-6) -> torch.Tensor:
+    """Prefill QKV projection with per-head QK-RMSNorm, RoPE and the KV-cache
+    write in the tcgen05 epilogue.  h bf16 [B*S, hidden] (normed); returns q
+    [B, Hq, S, 128]; k/v go to the caches at start_pos .. start_pos + S - 1."""
+    _cuda("gemm_qkv_rope", h, w, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache)
+    _bf16("gemm_qkv_rope", h, w, q_norm_w, k_norm_w, k_cache, v_cache)
+    _contig("gemm_qkv_rope", h, w, cos, sin, k_cache, v_cache)
+    hidden = h.shape[-1]
+    if h.numel() != B * S * hidden or w.shape != ((Hq + 2 * Hkv) * HEAD_DIM, hidden):
+        raise ValueError("gemm_qkv_rope: h must be [B*S, hidden], w [(Hq+2Hkv)*128, hidden]")
+    if cos.dtype == torch.bfloat16:
+        cs_dtype = Q3_BF16
+    elif cos.dtype == torch.float32:
+        cs_dtype = Q3_F32
+    else:
+        raise TypeError("gemm_qkv_rope: cos/sin must be bf16 or f32")
+    q = torch.empty(B, Hq, S, HEAD_DIM, dtype=torch.bfloat16, device=h.device)
+    call("q3_gemm_qkv_rope", _p(h), _p(w), hidden, _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin),
+         cs_dtype, 1 if cs_use_pos else 0, int(cs_offset), int(cs_stride_b), _p(q),
+         _p(k_cache), _p(v_cache), B, S, Hq, Hkv, HEAD_DIM, int(start_pos), k_cache.shape[2],
+         float(eps), _stream())
+    return q
+
+
 def gemm_norm(a: torch.Tensor, norm_w: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
               epilogue: str = "none", residual: torch.Tensor = None,
               out: torch.Tensor = None) -> torch.Tensor:

@@ -257,6 +257,47 @@ def test_gemm_swiglu(M):
     compare("gemm+swiglu", c, want, max_abs=2e-2, rel_scale=True, min_cos=0.9999)
 
 
+# ------------------------------------- prefill QKV with norm + RoPE in the epilogue
+@pytest.mark.parametrize("B,S,Hq,Hkv,H,start,mrope", [(1, 40, 4, 1, 512, 0, False),
+                                                      (2, 300, 32, 8, 4096, 17, False),
+                                                      (2, 100, 8, 2, 1024, 0, True),
+                                                      (3, 129, 4, 1, 2048, 5, False)])
+def test_gemm_qkv_rope_matches_gemm_then_norm_rope(B, S, Hq, Hkv, H, start, mrope):
+    """q3_gemm_qkv_rope == q3_gemm followed by q3_qkv_norm_rope (the same
+    rounding points; the head norm's sum runs in another order, so a bf16 value
+    may differ by one rounding step): max-abs <= 2e-2 of the output scale,
+    cosine >= 0.99999, at most 1% of elements differing."""
+    D, maxS = 128, 512
+    h = rnd(B * S, H, seed=70)
+    w = rnd((Hq + 2 * Hkv) * D, H, seed=71, std=0.02)
+    qn = (1 + rnd(D, seed=72, std=0.1)).to(BF16)
+    kn = (1 + rnd(D, seed=73, std=0.1)).to(BF16)
+    if mrope:   # per-token f32 rows, as M-RoPE builds them
+        ang = torch.rand(B * S, 64, generator=torch.Generator().manual_seed(74)) * 50
+        cos, sin = ang.cos(), ang.sin()
+        kw = dict(cs_use_pos=False, cs_offset=0, cs_stride_b=S)
+    else:       # bf16 tables indexed by position, as RotaryEmbedding builds them
+        cos, sin = oref.rotary_tables(D, maxS + 8, 5e6)
+        kw = dict(cs_use_pos=True, cs_offset=3, cs_stride_b=0)
+    dv = dict(device=DEV)
+    hd, wd, cd, sd = h.to(DEV), w.to(DEV), cos.to(DEV), sin.to(DEV)
+    caches = [torch.zeros(B, Hkv, maxS, D, dtype=BF16, **dv) for _ in range(4)]
+    q1 = ops.gemm_qkv_rope(hd, wd, qn.to(DEV), kn.to(DEV), cd, sd, B=B, S=S, Hq=Hq, Hkv=Hkv,
+                           k_cache=caches[0], v_cache=caches[1], start_pos=start, **kw)
+    qkv = ops.gemm(hd, wd)
+    q2, _, _ = ops.qkv_norm_rope(qkv, qn.to(DEV), kn.to(DEV), cd, sd, B=B, S=S, Hq=Hq, Hkv=Hkv,
+                                 start_pos=start, k_cache=caches[2], v_cache=caches[3], **kw)
+    for name, a, b in (("q", q1, q2), ("k cache", caches[0], caches[2]),
+                       ("v cache", caches[1], caches[3])):
+        compare(f"fused qkv {name}", a.cpu(), b.cpu(), max_abs=2e-2, rel_scale=True,
+                min_cos=0.99999)
+        diff = (a.view(torch.int16) != b.view(torch.int16)).float().mean().item()
+        assert diff < 0.01, f"fused qkv {name}: {diff:.3%} of elements differ"
+    # rows outside start .. start + S - 1 untouched
+    assert torch.count_nonzero(caches[0][:, :, :start]) == 0
+    assert torch.count_nonzero(caches[0][:, :, start + S:]) == 0
+
+
 # ------------------------------------------------- decode projections, norm fused
 @pytest.mark.parametrize("M,N,K,epi", [(1, 6144, 4096, "none"), (8, 6144, 4096, "none"),
                                        (13, 4096, 4096, "none"), (16, 2048, 544, "none"),
