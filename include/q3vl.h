@@ -123,6 +123,23 @@ Q3_API int q3_attn_decode(const void* q, const void* k_cache, const void* v_cach
                    int64_t max_seq, float scale, int dtype, void* workspace,
                    size_t workspace_bytes, q3_stream_t stream);
 
+/* Decode attention with the head norms, RoPE and the KV-cache write folded in:
+ * replaces q3_qkv_norm_rope (its decode use) followed by q3_attn_decode, for
+ * bf16 caches and bf16 RoPE tables.  qkv bf16 [B, (Hq+2*Hkv)*128] is the raw
+ * QKV projection of the new tokens ([q | k | v] per token); the new token sits
+ * at cache position kv_len-1 (kv_len = *kv_len_dev when that is non-NULL) and
+ * uses RoPE row kv_len-1 + cs_offset.  Each (sequence, KV head) normalises and
+ * rotates its query heads itself; the split that holds the new position
+ * writes the new k (normed, rotated) and v rows to the caches and adds them to
+ * its softmax, and the other rows [0, kv_len-1) stream from the caches without
+ * waiting for the preceding kernel.  Workspace as for q3_attn_decode. */
+Q3_API int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                              const void* cos, const void* sin, int64_t cs_offset, void* k_cache,
+                              void* v_cache, void* out, int B, int Hq, int Hkv, int head_dim,
+                              int64_t kv_len, const int32_t* kv_len_dev, int64_t max_seq,
+                              float scale, float eps, void* workspace, size_t workspace_bytes,
+                              q3_stream_t stream);
+
 /* Same computation as q3_attn_decode, for callers that cannot allocate device
  * memory at call time (a runtime whose free HBM is already committed to its
  * own pools, or a binding that owns only these buffers).  No counterpart in

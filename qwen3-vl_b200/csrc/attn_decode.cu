@@ -109,6 +109,17 @@ struct DecodeParams {
   const int32_t* kv_len_dev;
   int64_t max_seq;
   float scale;
+  // fused variant (q3_attn_decode_qkv): q and the new K/V row come from the
+  // raw qkv row [B, (Hq+2*Hkv)*128]; QK-RMSNorm + RoPE run here
+  const __nv_bfloat16* qkv;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const __nv_bfloat16* cos;  // bf16 [rows, 64]; row of the new token = pos + cs_offset
+  const __nv_bfloat16* sin;
+  int64_t cs_offset;
+  float eps;
+  __nv_bfloat16* k_cache_w;  // the caches again, for writing the new row
+  __nv_bfloat16* v_cache_w;
 };
 
 // Positions per split.  The grid's split count is planned on the host from
@@ -356,7 +367,53 @@ struct DecodeTcParams {
   int* err;
 };
 
-template <int G>
+// One head row of the fused variant, computed by one warp as q3_qkv_norm_rope
+// computes it (lane owns dims 4*lane .. 4*lane+3, partner dims via lane ^ 16):
+// RMSNorm over the head (model_fused.py:113-119) and rotate-half RoPE
+// (:122-129) in the reference's bf16 rounding points.
+// The lane's norm-weight and RoPE-table entries (static data: loadable before
+// the wait on the kernel that produced qkv).
+struct HeadTabs {
+  uint2 w, c, s;
+};
+__device__ __forceinline__ HeadTabs head_tabs(const __nv_bfloat16* w, const __nv_bfloat16* cs_cos,
+                                              const __nv_bfloat16* cs_sin, int64_t crow,
+                                              int lane) {
+  const int d0 = lane * 4, j0 = d0 & 63;
+  HeadTabs t;
+  t.w = *reinterpret_cast<const uint2*>(w + d0);
+  t.c = *reinterpret_cast<const uint2*>(cs_cos + crow * 64 + j0);
+  t.s = *reinterpret_cast<const uint2*>(cs_sin + crow * 64 + j0);
+  return t;
+}
+__device__ __forceinline__ void head_norm_rope(const __nv_bfloat16* x, const HeadTabs& tb,
+                                               float eps, int lane, float (&o)[4]) {
+  const int d0 = lane * 4;
+  const uint2 u = *reinterpret_cast<const uint2*>(x + d0);
+  const float2 a = unpack_bf16x2(u.x), bb = unpack_bf16x2(u.y);
+  const float v[4] = {a.x, a.y, bb.x, bb.y};
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss * (1.0f / kHD) + eps);
+  const float2 w0 = unpack_bf16x2(tb.w.x), w1 = unpack_bf16x2(tb.w.y);
+  const float wv[4] = {w0.x, w0.y, w1.x, w1.y};
+  const float2 c0 = unpack_bf16x2(tb.c.x), c1 = unpack_bf16x2(tb.c.y);
+  const float2 s0 = unpack_bf16x2(tb.s.x), s1 = unpack_bf16x2(tb.s.y);
+  const float cv[4] = {c0.x, c0.y, c1.x, c1.y}, sv[4] = {s0.x, s0.y, s1.x, s1.y};
+  float n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = rbf(rbf(v[i] * r) * wv[i]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float pp = __shfl_xor_sync(0xffffffffu, n[i], 16);
+    const float rot = (lane < 16) ? -pp : pp;
+    o[i] = rbf(rbf(n[i] * cv[i]) + rbf(rot * sv[i]));
+  }
+}
+
+template <int G, bool FQ>
 __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     DecodeTcParams prm) {
@@ -373,13 +430,19 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
   uint64_t* empty = full + kTcStages;
   __shared__ float sm_o[kTcConsumers][G][kHD];
   __shared__ float sm_ml[kTcConsumers][G][2];
+  __shared__ __align__(16) __nv_bfloat16 q_s[FQ ? G : 1][kHD];  // FQ: normed, rotated q
+  __shared__ float new_s[FQ ? 2 : 1][kHD];                       // FQ: new k and v rows
+  __shared__ float snew_s[FQ ? G : 1];                           // FQ: new row's scores
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int64_t L = p.kv_len_dev ? (int64_t)(*p.kv_len_dev) : p.kv_len;
   const int64_t chunk = split_chunk(p, L, kTcTile);
   const int64_t start = (int64_t)split * chunk;
-  const int64_t end = min64(start + chunk, L);
+  // FQ: the cache rows streamed are the old ones [0, L-1); the new token's
+  // row L-1 is computed here and added by the split whose range holds it
+  const int64_t end = min64(start + chunk, FQ ? L - 1 : L);
+  const bool with_new = FQ && start <= L - 1 && L - 1 < start + chunk;
   const int ntiles = end > start ? (int)((end - start + kTcTile - 1) / kTcTile) : 0;
   const int64_t row_base = ((int64_t)b * p.Hkv + kvh) * p.max_seq + start;
 
@@ -400,8 +463,9 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % kTcStages;
         const uint32_t ph = (i / kTcStages) & 1;
-        // a tile reaching the newest row (L - 1) waits for its writer
-        if (!waited && start + (int64_t)(i + 1) * kTcTile > L - 1) {
+        // a tile reaching the newest row (L - 1) waits for its writer (the
+        // fused variant never reads that row from the cache)
+        if (!FQ && !waited && start + (int64_t)(i + 1) * kTcTile > L - 1) {
           pdl_wait();
           waited = true;
         }
@@ -416,13 +480,27 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
       }
     }
   } else {
+    HeadTabs qtab{};
+    if constexpr (FQ) qtab = head_tabs(p.q_norm, p.cos, p.sin, (L - 1) + p.cs_offset, lane);
     pdl_wait();  // q and the outputs
     const int g = lane >> 2, t = lane & 3;
+    if constexpr (FQ) {
+      // this KV head's G query heads, normed and rotated, into shared memory
+      const int ld = (p.Hq + 2 * p.Hkv) * kHD;
+      for (int gg = warp; gg < G; gg += kTcConsumers) {
+        float o4[4];
+        head_norm_rope(p.qkv + (int64_t)b * ld + (kvh * G + gg) * kHD, qtab, p.eps, lane, o4);
+        *reinterpret_cast<uint2*>(&q_s[gg][lane * 4]) =
+            make_uint2(pack_bf16x2(o4[0], o4[1]), pack_bf16x2(o4[2], o4[3]));
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kTcConsumers * 32) : "memory");
+    }
     // Q as the A operand: row g = query head kvh*G + g (rows >= G are zero)
     uint32_t qf[8][2];
     {
       const __nv_bfloat16* qh =
-          reinterpret_cast<const __nv_bfloat16*>(p.q) + ((int64_t)b * p.Hq + kvh * G + g) * kHD;
+          FQ ? &q_s[g < G ? g : 0][0]
+             : reinterpret_cast<const __nv_bfloat16*>(p.q) + ((int64_t)b * p.Hq + kvh * G + g) * kHD;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         if (g < G) {
@@ -522,12 +600,51 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
     }
   }
   __syncthreads();
+  if constexpr (FQ) {
+    if (with_new) {
+      // the new token's k (normed, rotated) and v rows: into the caches and
+      // into this split's merge (warps 0 and 1; the producer warp idles)
+      const int ld = (p.Hq + 2 * p.Hkv) * kHD;
+      const int64_t pos = L - 1;
+      const int64_t crow = pos + p.cs_offset;
+      const int64_t crow_off = (((int64_t)b * p.Hkv + kvh) * p.max_seq + pos) * kHD;
+      if (warp == 0) {
+        float o4[4];
+        head_norm_rope(p.qkv + (int64_t)b * ld + (p.Hq + kvh) * kHD,
+                       head_tabs(p.k_norm, p.cos, p.sin, crow, lane), p.eps, lane, o4);
+        const uint2 pk = make_uint2(pack_bf16x2(o4[0], o4[1]), pack_bf16x2(o4[2], o4[3]));
+        *reinterpret_cast<uint2*>(p.k_cache_w + crow_off + lane * 4) = pk;
+        const float2 a0 = unpack_bf16x2(pk.x), a1 = unpack_bf16x2(pk.y);
+        new_s[0][lane * 4 + 0] = a0.x; new_s[0][lane * 4 + 1] = a0.y;
+        new_s[0][lane * 4 + 2] = a1.x; new_s[0][lane * 4 + 3] = a1.y;
+      } else if (warp == 1) {
+        const uint2 pv = *reinterpret_cast<const uint2*>(
+            p.qkv + (int64_t)b * ld + (p.Hq + p.Hkv + kvh) * kHD + lane * 4);
+        *reinterpret_cast<uint2*>(p.v_cache_w + crow_off + lane * 4) = pv;
+        const float2 a0 = unpack_bf16x2(pv.x), a1 = unpack_bf16x2(pv.y);
+        new_s[1][lane * 4 + 0] = a0.x; new_s[1][lane * 4 + 1] = a0.y;
+        new_s[1][lane * 4 + 2] = a1.x; new_s[1][lane * 4 + 3] = a1.y;
+      }
+      __syncthreads();
+      const float sl2 = p.scale * 1.4426950408889634f;
+      for (int gg = warp; gg < G; gg += kTcConsumers + 1) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc = fmaf(bf2f(q_s[gg][lane * 4 + i]), new_s[0][lane * 4 + i], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) snew_s[gg] = acc * sl2;
+      }
+      __syncthreads();
+    }
+  }
   // ---- merge the consumer warps; write the partial or the output ----
   for (int idx = threadIdx.x; idx < G * kHD; idx += blockDim.x) {
     const int gg = idx / kHD, d = idx % kHD;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kTcConsumers; ++w) M = fmaxf(M, sm_ml[w][gg][0]);
+    if (FQ && with_new) M = fmaxf(M, snew_s[FQ ? gg : 0]);
     float a = 0.f, l = 0.f;
 #pragma unroll
     for (int w = 0; w < kTcConsumers; ++w) {
@@ -535,6 +652,11 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
       const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       a = fmaf(f, sm_o[w][gg][d], a);
       l = fmaf(f, sm_ml[w][gg][1], l);
+    }
+    if (FQ && with_new) {
+      const float f = exp2f(snew_s[FQ ? gg : 0] - M);
+      a = fmaf(f, new_s[FQ ? 1 : 0][d], a);
+      l += f;
     }
     const int h = kvh * G + gg;
     if (p.splits == 1) {
@@ -555,17 +677,18 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
 static void decode_split_plan_step(int B, int Hkv, int64_t max_kv_len, int step, int* splits,
                                    int* chunk);
 
-static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s) {
+static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_qkv = false) {
   void (*kern)(const CUtensorMap, const CUtensorMap, DecodeTcParams) = nullptr;
   int gi = 0;
   switch (G) {
-    case 1: kern = attn_decode_tc_kernel<1>; gi = 0; break;
-    case 2: kern = attn_decode_tc_kernel<2>; gi = 1; break;
-    case 4: kern = attn_decode_tc_kernel<4>; gi = 2; break;
-    case 8: kern = attn_decode_tc_kernel<8>; gi = 3; break;
+    case 1: kern = fused_qkv ? attn_decode_tc_kernel<1, true> : attn_decode_tc_kernel<1, false>; gi = 0; break;
+    case 2: kern = fused_qkv ? attn_decode_tc_kernel<2, true> : attn_decode_tc_kernel<2, false>; gi = 1; break;
+    case 4: kern = fused_qkv ? attn_decode_tc_kernel<4, true> : attn_decode_tc_kernel<4, false>; gi = 2; break;
+    case 8: kern = fused_qkv ? attn_decode_tc_kernel<8, true> : attn_decode_tc_kernel<8, false>; gi = 3; break;
     default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
   }
-  static int per_sm_cache[64][4] = {{0}};
+  if (fused_qkv) gi += 4;
+  static int per_sm_cache[64][8] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
   const bool cacheable = dev >= 0 && dev < 64;
@@ -681,6 +804,50 @@ extern "C" int q3_attn_decode(const void* q, const void* k_cache, const void* v_
   const int G = Hq / Hkv;
   cudaStream_t s = (cudaStream_t)stream;
   return dtype == Q3_F32 ? launch_decode<float>(p, G, s) : launch_decode<__nv_bfloat16>(p, G, s);
+}
+
+extern "C" int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                  const void* cos, const void* sin, int64_t cs_offset,
+                                  void* k_cache, void* v_cache, void* out, int B, int Hq, int Hkv,
+                                  int head_dim, int64_t kv_len, const int32_t* kv_len_dev,
+                                  int64_t max_seq, float scale, float eps, void* workspace,
+                                  size_t workspace_bytes, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(qkv && q_norm_w && k_norm_w && cos && sin && k_cache && v_cache && out,
+             "q3_attn_decode_qkv: null pointer");
+  Q3_REQUIRE(head_dim == kHD, "q3_attn_decode_qkv: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+             "q3_attn_decode_qkv: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  Q3_REQUIRE(kv_len >= 1 && kv_len <= max_seq,
+             "q3_attn_decode_qkv: kv_len=%lld outside [1, max_seq=%lld]", (long long)kv_len,
+             (long long)max_seq);
+  Q3_REQUIRE(aligned(qkv, 8) && aligned(q_norm_w, 8) && aligned(k_norm_w, 8) && aligned(cos, 8) &&
+                 aligned(sin, 8) && aligned(k_cache, 16) && aligned(v_cache, 16) &&
+                 aligned(out, 8),
+             "q3_attn_decode_qkv: misaligned pointer");
+  DecodeParams p{};
+  p.q = nullptr; p.k = k_cache; p.v = v_cache; p.out = out;
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv;
+  p.kv_len = kv_len; p.kv_len_dev = kv_len_dev; p.max_seq = max_seq; p.scale = scale;
+  p.qkv = (const __nv_bfloat16*)qkv;
+  p.q_norm = (const __nv_bfloat16*)q_norm_w;
+  p.k_norm = (const __nv_bfloat16*)k_norm_w;
+  p.cos = (const __nv_bfloat16*)cos;
+  p.sin = (const __nv_bfloat16*)sin;
+  p.cs_offset = cs_offset;
+  p.eps = eps;
+  p.k_cache_w = (__nv_bfloat16*)k_cache;
+  p.v_cache_w = (__nv_bfloat16*)v_cache;
+  decode_split_plan(B, Hkv, kv_len, &p.splits, &p.chunk);
+  if (p.splits > 1) {
+    const size_t need = (size_t)B * Hq * p.splits * (kHD + 2) * sizeof(float);
+    Q3_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+               "q3_attn_decode_qkv: workspace of %zu bytes needed (got %zu)", need,
+               workspace_bytes);
+    p.ws_acc = reinterpret_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + (size_t)B * Hq * p.splits * kHD;
+  }
+  return launch_decode_tc(p, Hq / Hkv, (cudaStream_t)stream, true);
 }
 
 // ---------------------------------------------------------------------------

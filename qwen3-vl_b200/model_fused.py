@@ -231,6 +231,10 @@ class Qwen3VLDecoderFused:
         self.use_step_kernel = os.environ.get("Q3VL_STEP_KERNEL", "0") == "1"
         # prefill: QK-norm, RoPE and the KV write in the QKV GEMM's epilogue
         self.fuse_qkv = os.environ.get("Q3VL_FUSE_QKV", "1") != "0"
+        # decode: QK-norm, RoPE and the KV write inside the attention kernel
+        # (opt-in: the separate norm/RoPE kernel already hides under the
+        # attention kernel's early K/V stream, and measured 0.4% faster)
+        self.fuse_attn_qkv = os.environ.get("Q3VL_FUSE_ATTN_QKV", "0") == "1"
         self._step_plans = {}
         self._ss_step = None
 
@@ -334,7 +338,11 @@ class Qwen3VLDecoderFused:
         else:
             cos, sin = rope
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
-        if fused_qkv:
+        fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
+                      cos.dtype == torch.bfloat16)
+        if fused_attn:
+            q = None  # computed inside the attention kernel from qkv
+        elif fused_qkv:
             q = ops.gemm_qkv_rope(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
                                   ab.k_norm_weight, cos, sin, B=B, S=S, Hq=ab.num_q_heads,
                                   Hkv=ab.num_kv_heads, k_cache=kc, v_cache=vc,
@@ -349,8 +357,14 @@ class Qwen3VLDecoderFused:
                                         eps=ab.eps)
         if S == 1:
             bound = kv_bound if kv_bound is not None else start_pos + 1
-            attn = ops.attn_decode(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
-                                   kv_len=bound, kv_len_dev=kv_len_dev, scale=self.scale)
+            if fused_attn:
+                attn = ops.attn_decode_qkv(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, kc,
+                                           vc, Hq=ab.num_q_heads, Hkv=ab.num_kv_heads,
+                                           kv_len=bound, kv_len_dev=kv_len_dev,
+                                           cs_offset=cs_offset, scale=self.scale, eps=ab.eps)
+            else:
+                attn = ops.attn_decode(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
+                                       kv_len=bound, kv_len_dev=kv_len_dev, scale=self.scale)
             attn = attn.view(T, ab.q_dim)
         else:
             attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,

@@ -192,6 +192,33 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, k
     return o
 
 
+def attn_decode_qkv(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, k_cache: torch.Tensor,
+                    v_cache: torch.Tensor, *, Hq: int, Hkv: int, kv_len: int,
+                    kv_len_dev: torch.Tensor = None, cs_offset: int = 0, scale: float = None,
+                    eps: float = 1e-6, out: torch.Tensor = None) -> torch.Tensor:
+    """Decode attention straight from the raw QKV projection: per-head
+    QK-RMSNorm + RoPE of the new token, its K/V row written to the caches at
+    kv_len-1, and GQA attention over [0, kv_len).  qkv bf16 [B, (Hq+2Hkv)*128];
+    bf16 cos/sin tables; returns out [B, Hq, 128]."""
+    _cuda("attn_decode_qkv", qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, kv_len_dev)
+    _bf16("attn_decode_qkv", qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache)
+    _contig("attn_decode_qkv", qkv, cos, sin, k_cache, v_cache)
+    B = qkv.shape[0]
+    if qkv.numel() != B * (Hq + 2 * Hkv) * HEAD_DIM:
+        raise ValueError("attn_decode_qkv: qkv must be [B, (Hq+2Hkv)*128]")
+    if kv_len_dev is not None and kv_len_dev.dtype != torch.int32:
+        raise TypeError("attn_decode_qkv: kv_len_dev must be int32")
+    scale = 1.0 / math.sqrt(HEAD_DIM) if scale is None else scale
+    o = torch.empty(B, Hq, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device) if out is None \
+        else out
+    ws = decode_workspace(B, Hq, Hkv, qkv.device)
+    call("q3_attn_decode_qkv", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin),
+         int(cs_offset), _p(k_cache), _p(v_cache), _p(o), B, Hq, Hkv, HEAD_DIM, int(kv_len),
+         _p(kv_len_dev), k_cache.shape[2], float(scale), float(eps), _p(ws),
+         0 if ws is None else ws.numel(), _stream())
+    return o
+
+
 # ----------------------------------------------------------------------------
 # a6/a7: prefill attention
 # ----------------------------------------------------------------------------

@@ -177,6 +177,43 @@ def test_decode_attention_device_length_decode_graph_shape(dtype):
             compare(f"graph-shape decode fp32 L={L}", got, want, max_abs=1e-5)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,L,dev_len,offset", [(8, 32, 8, 1152, True, 0),
+                                                       (8, 32, 8, 65, True, 3),
+                                                       (8, 32, 8, 1, False, 0),
+                                                       (1, 4, 1, 40, False, 5),
+                                                       (3, 8, 1, 300, True, 0),
+                                                       (16, 32, 8, 2048, True, 0)])
+def test_decode_attention_from_qkv_matches_norm_rope_then_attention(B, Hq, Hkv, L, dev_len,
+                                                                     offset):
+    """q3_attn_decode_qkv == q3_qkv_norm_rope (new row written at L-1) followed
+    by q3_attn_decode: the new K/V cache rows bit-identical; the attention
+    output max-abs <= 2e-2 of its scale, cosine >= 0.9999 (the new row's
+    probability is not rounded to bf16 before P.V here)."""
+    D, S = 128, 2048
+    qkv = rnd(B, (Hq + 2 * Hkv) * D, seed=80)
+    qn = (1 + rnd(D, seed=81, std=0.1)).to(BF16)
+    kn = (1 + rnd(D, seed=82, std=0.1)).to(BF16)
+    cos, sin = oref.rotary_tables(D, S + 16, 5e6)
+    kc = rnd(B, Hkv, S, D, seed=83)
+    vc = rnd(B, Hkv, S, D, seed=84)
+    kc1, vc1, kc2, vc2 = kc.to(DEV), vc.to(DEV), kc.to(DEV), vc.to(DEV)
+    qkvd, qnd, knd, cd, sd = qkv.to(DEV), qn.to(DEV), kn.to(DEV), cos.to(DEV), sin.to(DEV)
+    pos = L - 1
+    Ld = torch.tensor([L], dtype=torch.int32, device=DEV) if dev_len else None
+    bound = S if dev_len else L
+    got = ops.attn_decode_qkv(qkvd, qnd, knd, cd, sd, kc1, vc1, Hq=Hq, Hkv=Hkv, kv_len=bound,
+                              kv_len_dev=Ld, cs_offset=offset)
+    q, _, _ = ops.qkv_norm_rope(qkvd, qnd, knd, cd, sd, B=B, S=1, Hq=Hq, Hkv=Hkv,
+                                start_pos=pos, cs_offset=offset, k_cache=kc2, v_cache=vc2)
+    want = ops.attn_decode(q.view(B, Hq, D), kc2, vc2, kv_len=L)
+    torch.cuda.synchronize()
+    assert torch.equal(kc1[:, :, pos].cpu(), kc2[:, :, pos].cpu()), "new k row differs"
+    assert torch.equal(vc1[:, :, pos].cpu(), vc2[:, :, pos].cpu()), "new v row differs"
+    assert torch.equal(kc1.cpu(), kc2.cpu()) and torch.equal(vc1.cpu(), vc2.cpu())
+    compare(f"attn from qkv B={B} L={L}", got.cpu(), want.cpu(), max_abs=2e-2, rel_scale=True,
+            min_cos=0.9999)
+
+
 # --------------------------------------------------------------------------- a6/a7 prefill
 def test_prefill_kat_vs_reference_attention_ref():
     """kernels/prefill_attention.py layouts (q [Hq,D,S], k [Hkv,D,S], v [Hkv,S,D])."""
