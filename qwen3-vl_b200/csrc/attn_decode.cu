@@ -16,6 +16,10 @@
 //   ends with one head's score.  Online softmax runs in fp32 per warp; warps
 //   merge in shared memory; splits merge in a second small kernel through the
 //   fp32 workspace.
+// That CUDA-core kernel serves the fp32 case (config 1); bf16 caches use the
+// tensor-core kernel further down (TMA-fed K/V ring, mma.sync), which also has
+// a variant that starts from the raw QKV row (q3_attn_decode_qkv): it applies
+// the head norms and RoPE itself and writes the new token's K/V row.
 #include <math.h>
 
 #include "common.cuh"

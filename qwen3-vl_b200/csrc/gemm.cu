@@ -6,19 +6,15 @@
 // stored [N, K] (K-major).  Epilogues reproduce the reference's bf16 rounding
 // points: every torch op on bf16 tensors rounds its result to bf16.
 //
-// Two kernels:
-//  * M <= 16 (decode): HBM-streaming kernel.  Tensor cores are idle at this M,
-//    so the design goal is bytes in flight: each warp streams 16 weight rows in
-//    32-element K steps with 16-byte loads and feeds bf16 mma.sync m16n8k16 with
-//    the weights as the 16-row A operand and the (L1-resident) activations as B.
-//    K is split across the warps of a CTA and across the CTAs of a thread-block
-//    cluster; partial sums are reduced in shared memory and then over the
-//    cluster's distributed shared memory, so no workspace or atomics are used.
-//  * M > 16 (prefill): persistent warp-specialised tcgen05 kernel.  Warp 0
-//    issues TMA loads (128-byte swizzle, no multicast) into a 4-6 stage smem
-//    ring, warp 1 issues tcgen05.mma (M=128, N=BN, K=16 per instruction) into a
-//    double-buffered TMEM accumulator, warps 2-5 drain TMEM with tcgen05.ld and
-//    run the epilogue while the next tile accumulates.
+// Dispatch: M <= 16 (decode) goes to the TMA-ring GEMV of gemv.cu (tensor
+// cores idle at this M; the design goal is bytes in flight).  M > 16
+// (prefill) runs the persistent warp-specialised tcgen05 kernel below: warp 0
+// issues TMA loads (128-byte swizzle, no multicast) into a 4-6 stage smem
+// ring, warp 1 issues tcgen05.mma (M=128, N=BN, K=16 per instruction) into a
+// double-buffered TMEM accumulator, warps 2-5 drain TMEM with tcgen05.ld and
+// run the epilogue while the next tile accumulates.  Epilogues: plain,
+// residual add, SwiGLU on interleaved gate/up rows, and (q3_gemm_qkv_rope) the
+// per-head QK-RMSNorm + RoPE + KV-cache write of the QKV projection.
 #include <math.h>
 
 #include <mutex>
