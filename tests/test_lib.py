@@ -56,6 +56,37 @@ def test_invalid_arguments_are_rejected_on_the_host():
     assert b"max_seq" in lib.q3_last_error()
 
 
+def test_fused_entry_points_reject_bad_arguments_on_the_host():
+    lib = _lib.load()
+    one = ctypes.c_void_p(16)
+    # fused prefill QKV: decode-sized token count (B*S <= 16) belongs to the GEMV path
+    rc = lib.q3_gemm_qkv_rope(one, one, 4096, one, one, one, one, 1, 1, 0, 0, one, one, one,
+                              1, 16, 32, 8, 128, 0, 2048, 1e-6, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"B*S > 16" in lib.q3_last_error()
+    # ... and positions past the cache
+    rc = lib.q3_gemm_qkv_rope(one, one, 4096, one, one, one, one, 1, 1, 0, 0, one, one, one,
+                              2, 100, 32, 8, 128, 2000, 2048, 1e-6, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"outside the cache" in lib.q3_last_error()
+    # decode attention from qkv: Hq must be a multiple of Hkv
+    rc = lib.q3_attn_decode_qkv(one, one, one, one, one, 0, one, one, one, 1, 6, 4, 128, 8,
+                                None, 16, 0.1, 1e-6, None, 0, None)
+    assert rc == _lib.Q3_ERR_INVALID
+    # in-kernel all-reduce needs a communicator
+    rc = lib.q3_gemm_ar(one, one, one, 8, 4096, 512, None, None, None, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
+    # decode projection: sums of squares come out of the residual epilogue only
+    rc = lib.q3_gemm_decode(one, one, one, 8, 4096, 4096, 0, None, None, 1e-6, None, 0, one,
+                            None)
+    assert rc == _lib.Q3_ERR_INVALID and b"residual" in lib.q3_last_error()
+    # whole-step kernel: 1..16 sequences
+    plan = ctypes.c_void_p()
+    layer = _lib.StepLayer()
+    rc = lib.q3_decode_step_create(ctypes.byref(layer), 1, 17, 4096, 32, 8, 12288, 2048, 1e-6,
+                                   one, one, 2048, ctypes.byref(plan))
+    assert rc == _lib.Q3_ERR_INVALID and b"batch" in lib.q3_last_error()
+    assert not plan.value
+
+
 def test_error_raises_q3error():
     with pytest.raises(_lib.Q3Error) as e:
         _lib.call("q3_rmsnorm", None, None, None, None, None, 1, 8, 1e-6, None)
