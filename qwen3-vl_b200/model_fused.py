@@ -481,13 +481,22 @@ class Qwen3VLDecoderFused:
         return x, pend
 
     def _deepstack_add(self, x, B, S, feats, visual_mask):
-        """model_fused.py:339-341 (batch row 0, as the reference)."""
+        """Deepstack injection after an early layer (model_fused.py:339-341):
+        hidden[visual positions] += feats.  A 1-D mask [S] addresses batch row 0,
+        as the reference does; a [B, S] mask addresses every sequence, with the
+        feature rows of all sequences concatenated in (row, position) order."""
         H = x.shape[-1]
-        xv = x.view(B, S, H)
-        idx = torch.nonzero(visual_mask.to(self.device).reshape(-1)).flatten()
-        rows = xv[0].index_select(0, idx).contiguous()
+        m = visual_mask.to(self.device)
+        if m.dim() == 2 and m.shape != (B, S):
+            raise ValueError(f"visual_mask must be [S] or [B, S]=[{B}, {S}], got {tuple(m.shape)}")
+        flat = x.view(B * S, H)
+        idx = torch.nonzero(m.reshape(-1)).flatten()   # row-0 positions for a 1-D mask
+        if feats.shape[0] != idx.numel():
+            raise ValueError(f"deepstack features: {feats.shape[0]} rows for {idx.numel()} "
+                             "visual positions")
+        rows = flat.index_select(0, idx).contiguous()
         upd = ops.add(rows, feats.to(self.device, torch.bfloat16).contiguous())
-        xv[0].index_copy_(0, idx, upd)
+        flat.index_copy_(0, idx, upd)
         return x
 
     def forward(self, input_ids, start_pos, kv_cache, position_ids=None):

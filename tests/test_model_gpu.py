@@ -147,6 +147,32 @@ def test_generate_with_embeds_deepstack():
     assert got == toks
 
 
+def test_generate_with_embeds_deepstack_batched_rows():
+    """A [B, S] visual mask injects each sequence's own deepstack rows: a batch
+    of two prompts gives the tokens each prompt gives alone."""
+    name = "decoder_tiny_tp1"
+    c = cases.DECODER_CASES[name]
+    w = cases.decoder_weights(name)
+    dec = _decoder(w, c["spec"], max_seq=c["max_seq"])
+    ids = cases.decoder_prompt(name)
+    P = ids.shape[1]
+    ids2 = torch.roll(ids, 7, dims=1)
+    emb = torch.cat([w["embed"][ids], w["embed"][ids2]], 0)      # [2, P, H]
+    mask = torch.zeros(2, P, dtype=torch.bool)
+    mask[0, 5:15] = True
+    mask[1, 20:26] = True
+    gen = torch.Generator().manual_seed(5)
+    ds = [torch.randn(16, 512, generator=gen).to(torch.bfloat16) for _ in range(2)]
+    got = dec.generate_with_embeds(emb.to(DEV), max_new_tokens=8, eos_token_id=-1,
+                                   deepstack_embeds=[d.to(DEV) for d in ds],
+                                   visual_mask=mask.to(DEV))
+    for b, (lo, hi) in enumerate(((0, 10), (10, 16))):
+        one = dec.generate_with_embeds(emb[b:b + 1].to(DEV), max_new_tokens=8, eos_token_id=-1,
+                                       deepstack_embeds=[d[lo:hi].to(DEV) for d in ds],
+                                       visual_mask=mask[b].to(DEV))
+        assert got[b] == one, f"row {b}: batched {got[b]} vs alone {one}"
+
+
 def test_random_init_loader_shapes():
     spec = loader_fused.TextSpec(hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=2048,
                                  layers=2)
