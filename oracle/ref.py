@@ -102,6 +102,75 @@ def config2_position_ids(seq: int = 2048, text0: int = 100, grid: int = 16) -> t
     return pos[:, None, :seq]   # [3, 1, S]
 
 
+def rope_index(types, mask, image_thw, video_thw, merge: int = 2):
+    """3-axis position ids and per-sequence rope deltas, restating
+    transformers 5.5.0 modeling_qwen3_vl.py:1031-1122 (Qwen3VLModel.get_rope_index)
+    with get_vision_position_ids :975-1029 (temp_merge_size 1, time_interval 1).
+
+    types [B, S] int (0 text, 1 image, 2 video); mask [B, S] or None (nonzero =
+    kept); image_thw [Ni, 3] / video_thw [Nv, 3] ints or None.  Returns
+    (pos int64 [3, B, S], delta int64 [B]).  Steps:
+      - each video is split into t frames of grid (1, h, w) (:1071-1073);
+      - the kept tokens of a sequence are cut into runs of one type (:1096-1101);
+      - a text run takes consecutive positions on all three axes from the
+        running position and advances it by its length (:1106-1110);
+      - an image / frame run takes the next grid of its kind (grids are
+        consumed in batch order, :1082-1085) and token i of the run gets
+        t = p, h = p + i // (w' t), w = p + i % w' with h' = h // merge,
+        w' = w // merge (:1013-1024); p advances by max(h, w) // merge (:1118);
+      - masked tokens keep position 0; delta = max position + 1 - kept tokens.
+    A run whose length differs from its grid's token count, or a run with no
+    grid left, raises ValueError (the reference fails on both)."""
+    import numpy as np
+    types = np.asarray(types, dtype=np.int64)
+    B, S = types.shape
+    keep = np.ones((B, S), dtype=bool) if mask is None else (np.asarray(mask) != 0)
+    grids = {1: [], 2: []}
+    if image_thw is not None:
+        grids[1] = [tuple(int(v) for v in g) for g in np.asarray(image_thw).reshape(-1, 3)]
+    if video_thw is not None:
+        for t, h, w in np.asarray(video_thw).reshape(-1, 3):
+            grids[2] += [(1, int(h), int(w))] * int(t)
+    nxt = {1: 0, 2: 0}
+    pos = np.zeros((3, B, S), dtype=np.int64)
+    delta = np.zeros(B, dtype=np.int64)
+    for b in range(B):
+        idx = np.nonzero(keep[b])[0]
+        tt = types[b, idx]
+        if len(idx) == 0:
+            raise ValueError("rope_index: a sequence with no kept token")
+        if ((tt < 0) | (tt > 2)).any():
+            raise ValueError("rope_index: token type outside {0, 1, 2}")
+        out = np.zeros((3, len(idx)), dtype=np.int64)
+        p, j = 0, 0
+        while j < len(idx):
+            e = j
+            while e < len(idx) and tt[e] == tt[j]:
+                e += 1
+            n = e - j
+            kind = int(tt[j])
+            if kind == 0:
+                out[:, j:e] = p + np.arange(n)
+                p += n
+            else:
+                if nxt[kind] >= len(grids[kind]):
+                    raise ValueError("rope_index: more vision runs than grids")
+                gt, gh, gw = grids[kind][nxt[kind]]
+                nxt[kind] += 1
+                hh, ww = gh // merge, gw // merge
+                if n != gt * hh * ww:
+                    raise ValueError("rope_index: vision run length differs from its grid")
+                i = np.arange(n)
+                out[0, j:e] = p
+                out[1, j:e] = p + i // (ww * gt)
+                out[2, j:e] = p + i % ww
+                p += max(gh, gw) // merge
+            j = e
+        pos[:, b, idx] = out
+        delta[b] = out.max() + 1 - len(idx)
+    return torch.from_numpy(pos), torch.from_numpy(delta)
+
+
 # ---------------------------------------------------------------------------
 # a3: AttentionBlock.forward -- model_fused.py:87-131
 # ---------------------------------------------------------------------------

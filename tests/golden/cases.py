@@ -137,3 +137,118 @@ def hf_mrope_reference():
 
 def attention_scale() -> float:
     return 1.0 / math.sqrt(128)
+
+
+# ---- multimodal position ids (get_rope_index): seeded token-type layouts ----
+def _vision_tokens(t, h, w, merge):
+    return t * (h // merge) * (w // merge)
+
+
+def rope_index_layout(seed: int, B: int, runs: int, merge: int = 2, pad_max: int = 6,
+                      max_side: int = 10, holes: bool = True):
+    """B sequences of alternating text and vision runs, left-padded to one length.
+
+    Text runs are 1..12 tokens.  An image run takes a grid (t, h, w) with
+    t in {1, 2} and h, w in merge*[1, max_side] (+1 now and then, which the
+    // merge floors away).  A video is t frames of one (h, w) grid, each frame
+    run preceded by a 1..3 token text run (the timestamp).  Grids are listed
+    in batch order, as the model consumes them.  Padding tokens have random
+    types (masked tokens are dropped before grouping); with `holes`, a few
+    masked tokens also sit inside text runs.  Returns a dict of numpy arrays:
+    types [B, S] int32, mask [B, S] int32, image_thw [Ni, 3], video_thw [Nv, 3]
+    (int64, possibly with zero rows)."""
+    import random
+    import numpy as np
+    rnd = random.Random(seed)
+    seqs, masks, imgs, vids = [], [], [], []
+    for _ in range(B):
+        ty, mk = [], []
+
+        def text(n):
+            for _ in range(n):
+                ty.append(0)
+                mk.append(1)
+                if holes and rnd.random() < 0.03:
+                    ty.append(rnd.randrange(3))
+                    mk.append(0)
+        text(rnd.randint(1, 12))
+        for _ in range(runs):
+            side = lambda: merge * rnd.randint(1, max_side) + (1 if rnd.random() < 0.2 else 0)
+            if rnd.random() < 0.6:
+                g = (rnd.choice((1, 1, 2)), side(), side())
+                imgs.append(g)
+                n = _vision_tokens(*g, merge)
+                ty += [1] * n
+                mk += [1] * n
+            else:
+                t, h, w = rnd.randint(1, 4), side(), side()
+                vids.append((t, h, w))
+                for f in range(t):
+                    if f:
+                        text(rnd.randint(1, 3))
+                    n = _vision_tokens(1, h, w, merge)
+                    ty += [2] * n
+                    mk += [1] * n
+            text(rnd.randint(1, 12))
+        seqs.append(ty)
+        masks.append(mk)
+    S = max(len(s) for s in seqs) + rnd.randint(0, pad_max)
+    types = np.zeros((B, S), dtype=np.int32)
+    mask = np.zeros((B, S), dtype=np.int32)
+    for b, (ty, mk) in enumerate(zip(seqs, masks)):
+        off = S - len(ty)
+        types[b, :off] = [rnd.randrange(3) for _ in range(off)]
+        types[b, off:] = ty
+        mask[b, off:] = mk
+    return {"types": types, "mask": mask,
+            "image_thw": np.array(imgs, dtype=np.int64).reshape(-1, 3),
+            "video_thw": np.array(vids, dtype=np.int64).reshape(-1, 3)}
+
+
+def rope_index_fixture_cases():
+    """(name, layout, merge) of the get_rope_index fixture."""
+    import numpy as np
+    text_only = {"types": np.zeros((1, 37), np.int32), "mask": None,
+                 "image_thw": np.zeros((0, 3), np.int64), "video_thw": np.zeros((0, 3), np.int64)}
+    two_images = {"types": np.array([[0] * 5 + [1] * 24 + [0] * 3 + [1] * 6 + [0] * 7], np.int32),
+                  "mask": None, "image_thw": np.array([[1, 8, 12], [1, 6, 4]], np.int64),
+                  "video_thw": np.zeros((0, 3), np.int64)}
+    return [("text_only", text_only, 2),
+            ("two_images", two_images, 2),
+            ("mixed_b2", rope_index_layout(11, 2, 3), 2),
+            ("mixed_b3_nohole", rope_index_layout(12, 3, 4, holes=False), 2),
+            ("mixed_b4_merge1", rope_index_layout(13, 4, 2, merge=1, max_side=5), 1),
+            ("mixed_b2_long", rope_index_layout(14, 2, 12), 2)]
+
+
+def hf_rope_index(layout, merge):
+    """transformers 5.5.0 Qwen3VLModel.get_rope_index, called on an object that
+    carries only what the method reads (config.vision_config.spatial_merge_size
+    and get_vision_position_ids), so no model weights are built."""
+    import functools
+    import types as pytypes
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLModel
+    host = pytypes.SimpleNamespace(
+        config=pytypes.SimpleNamespace(
+            vision_config=pytypes.SimpleNamespace(spatial_merge_size=merge)))
+    host.get_vision_position_ids = functools.partial(Qwen3VLModel.get_vision_position_ids, host)
+    ty = torch.from_numpy(layout["types"]).long()
+    mask = None if layout["mask"] is None else torch.from_numpy(layout["mask"]).long()
+    img = torch.from_numpy(layout["image_thw"]) if len(layout["image_thw"]) else None
+    vid = torch.from_numpy(layout["video_thw"]).clone() if len(layout["video_thw"]) else None
+    ids = torch.zeros_like(ty)
+    pos, delta = Qwen3VLModel.get_rope_index(host, ids, ty, img, vid, mask)
+    return pos, delta.reshape(-1)
+
+
+def rope_index_checksum() -> int:
+    """Position-weighted sum over every fixture layout (catches a changed generator)."""
+    import numpy as np
+    total = 0
+    for _, lay, merge in rope_index_fixture_cases():
+        for a in (lay["types"], lay["mask"], lay["image_thw"], lay["video_thw"]):
+            if a is not None and a.size:
+                w = np.arange(1, a.size + 1, dtype=np.int64)
+                total += int((a.reshape(-1).astype(np.int64) * w).sum())
+        total += merge
+    return total
