@@ -85,6 +85,26 @@ Q3_API int q3_rope(const void* x, const float* cos_sin, void* out, int64_t seq, 
 Q3_API int q3_mrope_cos_sin(const int64_t* pos, const float* inv_freq, int64_t n_tok, int head_dim,
                      int sec_h, int sec_w, float* cos_out, float* sin_out, q3_stream_t stream);
 
+/* ---- a4: multimodal 3-axis position ids ----------------------------------
+ * Replaces Qwen3VLModel.get_rope_index (transformers 5.5.0
+ * modeling_qwen3_vl.py:1031-1122, with get_vision_position_ids :975-1029).
+ * types int32 [B, S] (0 text, 1 image, 2 video); mask int32 [B, S] or NULL
+ * (nonzero = kept); image_thw int64 [n_image, 3]; video_thw int64 [n_video, 3]
+ * (each video is t frames of grid (1, h, w); n_video <= 4096); merge = the
+ * vision spatial merge size.  Grids are consumed in batch order.
+ * pos_out int64 [3, B, S] (masked tokens 0); delta_out int64 [B] = max
+ * position + 1 - kept tokens.  status_out int32 [B]: 0, or per sequence
+ * 1 more vision runs than grids, 2 a run length differs from its grid's
+ * token count, 3 a type outside {0, 1, 2}, 4 no kept token (the cases the
+ * reference rejects); outputs of a sequence with a nonzero status are
+ * unspecified.  workspace: q3_rope_index_workspace_bytes(B) bytes of device
+ * memory.  Asynchronous on `stream`. */
+Q3_API size_t q3_rope_index_workspace_bytes(int B);
+Q3_API int q3_rope_index(const int32_t* types, const int32_t* mask, int B, int64_t S,
+                  const int64_t* image_thw, int n_image, const int64_t* video_thw, int n_video,
+                  int merge, int64_t* pos_out, int64_t* delta_out, int32_t* status_out,
+                  void* workspace, size_t workspace_bytes, q3_stream_t stream);
+
 /* ---- a3 epilogue + a5: per-head QK-RMSNorm, RoPE, KV-cache write ---------
  * Replaces AttentionBlock.forward after the QKV matmul (model_fused.py:107-129)
  * and the cache slice assignment (model_fused.py:244-246).

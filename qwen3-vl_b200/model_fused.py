@@ -434,6 +434,20 @@ class Qwen3VLDecoderFused:
         pos = position_ids.to(self.device, torch.int64)
         return ops.mrope_cos_sin(pos, inv)
 
+    # vision_config.spatial_merge_size of the Qwen3-VL checkpoints
+    spatial_merge_size = 2
+
+    def get_rope_index(self, input_ids, mm_token_type_ids, image_grid_thw=None,
+                       video_grid_thw=None, attention_mask=None, **kwargs):
+        """Qwen3VLModel.get_rope_index (transformers 5.5.0
+        modeling_qwen3_vl.py:1031-1122) on the device: returns position_ids
+        int64 [3, B, S] for generate_with_embeds and the rope deltas int64
+        [B, 1] (the decode steps' RoPE rows are cache position + delta)."""
+        if tuple(mm_token_type_ids.shape) != tuple(input_ids.shape):
+            raise ValueError("get_rope_index: mm_token_type_ids must match input_ids")
+        return ops.rope_index(mm_token_type_ids.to(self.device), image_grid_thw, video_grid_thw,
+                              attention_mask, spatial_merge_size=self.spatial_merge_size)
+
     # --------------------------------------------------------------- logits
     def _logits(self, x, pend, B, S, ss_valid=False):
         H = x.shape[-1]

@@ -46,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_rmsnorm": (I32, [P, P, P, P, P, I64, I64, F32, P]),
     "q3_rope": (I32, [P, P, P, I64, I32, I32, P]),
     "q3_mrope_cos_sin": (I32, [P, P, I64, I32, I32, I32, P, P, P]),
+    "q3_rope_index_workspace_bytes": (SZ, [I32]),
+    "q3_rope_index": (I32, [P, P, I32, I64, P, I32, P, I32, I32, P, P, P, P, SZ, P]),
     "q3_qkv_norm_rope": (I32, [P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I32, I32, I32,
                                I32, I32, I64, P, I64, F32, P]),
     "q3_attn_decode_workspace_bytes": (SZ, [I32, I32, I32, I32, I64]),

@@ -9,9 +9,14 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py rmsnorm --rows 8192 --hidden 4096
     python qwen3-vl_b200/q3vl/microbench.py layer  --B 8 --L 1152 --bucket 2048
     python qwen3-vl_b200/q3vl/microbench.py step   --B 8 --L 1152 --bucket 2048 --layers 36
+    python qwen3-vl_b200/q3vl/microbench.py rope_index --B 8 --S 16384 [--hf]
 
 `step` times q3_decode_step (every layer of a decode step in one persistent
 kernel) as CUDA-graph replays and reports the step's HBM rate (weights + KV).
+`rope_index` times q3_rope_index (3-axis position ids of a multimodal prompt:
+text runs of 16 tokens between 32x32-patch images, merge 2) and, with --hf,
+transformers' Qwen3VLModel.get_rope_index on the host cores for the same
+layout.
 `layer` times every kernel of one TP1 decode layer of the 8B shape, and the
 whole layer, as CUDA-graph replays cycling over 4 layers' weights (1.5 GB, so
 every launch streams its weights from HBM), with the decode graph's arguments
@@ -52,7 +57,7 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "layer", "step"])
+                                       "layer", "step", "rope_index"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
@@ -72,7 +77,11 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-flush", action="store_true", help="keep L2 warm between iterations")
+    ap.add_argument("--hf", action="store_true",
+                    help="rope_index: also time transformers' get_rope_index on the host")
     a = ap.parse_args(argv)
+    if a.kernel == "rope_index":
+        return _rope_index(a)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
     if a.kernel == "layer":
@@ -336,6 +345,62 @@ def _gemm_ar(a):
         print(json.dumps(res), flush=True)
     comm.close()
     dist.destroy_process_group()
+
+
+def _rope_layout(B, S, side=32, text=16, merge=2):
+    """Token types [B, S] int32: text runs of `text` tokens between
+    (1, side, side) images, the tail text; image grids in batch order."""
+    n_img = (side // merge) ** 2
+    types = torch.zeros(B, S, dtype=torch.int32)
+    grids = []
+    for b in range(B):
+        s = text
+        while s + n_img + text <= S:
+            types[b, s:s + n_img] = 1
+            grids.append((1, side, side))
+            s += n_img + text
+    return types, torch.tensor(grids, dtype=torch.int64).reshape(-1, 3)
+
+
+def _rope_index(a):
+    import ctypes
+    from q3vl import _lib
+    dev = torch.device("cuda:0")
+    types_h, grids_h = _rope_layout(a.B, a.S)
+    types, grids = types_h.to(dev), grids_h.to(dev)
+    B, S = types.shape
+    pos = torch.empty(3, B, S, dtype=torch.int64, device=dev)
+    delta = torch.empty(B, dtype=torch.int64, device=dev)
+    status = torch.empty(B, dtype=torch.int32, device=dev)
+    nbytes = _lib.raw("q3_rope_index_workspace_bytes")(B)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    fn = lambda: _lib.call("q3_rope_index", p(types), None, B, S, p(grids), grids.shape[0],  # noqa
+                           None, 0, 2, p(pos), p(delta), p(status), p(ws), nbytes, st)
+    flush = None if a.no_flush else torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ms = _time(fn, a.iters, a.warmup, flush)
+    if int(status.abs().sum()) != 0:
+        raise SystemExit("rope_index: nonzero status on a valid layout")
+    nbytes_io = B * S * (4 + 24) + B * 8
+    res = {"kernel": "rope_index", "B": B, "S": S, "images": int(grids.shape[0]), "ms": ms,
+           "mtok_s": B * S / ms / 1e3, "gbs": nbytes_io / ms / 1e6}
+    if a.hf:
+        import time
+        import types as pytypes
+        import functools
+        from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLModel
+        host = pytypes.SimpleNamespace(config=pytypes.SimpleNamespace(
+            vision_config=pytypes.SimpleNamespace(spatial_merge_size=2)))
+        host.get_vision_position_ids = functools.partial(Qwen3VLModel.get_vision_position_ids,
+                                                         host)
+        ids = torch.zeros(B, S, dtype=torch.int64)
+        t0 = time.perf_counter()
+        hp, hd = Qwen3VLModel.get_rope_index(host, ids, types_h.long(), grids_h, None, None)
+        hf_ms = (time.perf_counter() - t0) * 1e3
+        same = torch.equal(hp, pos.cpu()) and torch.equal(hd.view(-1), delta.cpu())
+        res.update(hf_ms=hf_ms, hf_threads=torch.get_num_threads(), hf_equal=same)
+    print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":

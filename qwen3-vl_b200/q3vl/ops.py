@@ -99,6 +99,55 @@ def mrope_cos_sin(position_ids: torch.Tensor, inv_freq: torch.Tensor,
     return cos, sin
 
 
+_ROPE_INDEX_ERRORS = {
+    1: "more vision runs than grids",
+    2: "vision run length differs from its grid",
+    3: "token type outside {0, 1, 2}",
+    4: "a sequence with no kept token",
+}
+
+
+def rope_index(mm_token_type_ids: torch.Tensor, image_grid_thw: torch.Tensor = None,
+               video_grid_thw: torch.Tensor = None, attention_mask: torch.Tensor = None, *,
+               spatial_merge_size: int = 2):
+    """3-axis position ids [3, B, S] int64 and rope deltas [B, 1] int64 on the
+    device (Qwen3VLModel.get_rope_index, transformers 5.5.0
+    modeling_qwen3_vl.py:1031-1122).  Synchronizes once to read the
+    per-sequence status, and raises ValueError where the reference fails."""
+    _cuda("rope_index", mm_token_type_ids)
+    dev = mm_token_type_ids.device
+    if mm_token_type_ids.dim() != 2:
+        raise ValueError("rope_index: mm_token_type_ids must be [B, S]")
+    B, S = mm_token_type_ids.shape
+    types = mm_token_type_ids.to(dev, torch.int32).contiguous()
+    mask = None
+    if attention_mask is not None:
+        if tuple(attention_mask.shape) != (B, S):
+            raise ValueError("rope_index: attention_mask must match mm_token_type_ids")
+        mask = (attention_mask.to(dev) != 0).to(torch.int32).contiguous()
+
+    def grids(g):
+        if g is None or g.numel() == 0:
+            return None, 0
+        g = g.to(dev, torch.int64).reshape(-1, 3).contiguous()
+        return g, g.shape[0]
+    img, n_img = grids(image_grid_thw)
+    vid, n_vid = grids(video_grid_thw)
+    pos = torch.empty(3, B, S, dtype=torch.int64, device=dev)
+    delta = torch.empty(B, dtype=torch.int64, device=dev)
+    status = torch.empty(B, dtype=torch.int32, device=dev)
+    nbytes = _lib.raw("q3_rope_index_workspace_bytes")(B)
+    ws = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=dev)
+    call("q3_rope_index", _p(types), _p(mask), B, S, _p(img), n_img, _p(vid), n_vid,
+         int(spatial_merge_size), _p(pos), _p(delta), _p(status), _p(ws), nbytes, _stream())
+    bad = status.cpu()
+    if bool((bad != 0).any()):
+        b = int((bad != 0).nonzero()[0, 0])
+        raise ValueError(f"rope_index: sequence {b}: "
+                         f"{_ROPE_INDEX_ERRORS.get(int(bad[b]), int(bad[b]))}")
+    return pos, delta.view(B, 1)
+
+
 # ----------------------------------------------------------------------------
 # a3 epilogue + a5: QK-norm, RoPE, KV write
 # ----------------------------------------------------------------------------
