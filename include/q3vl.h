@@ -314,6 +314,17 @@ Q3_API int q3_embed(const int64_t* ids, const void* table, void* out, int64_t n,
 Q3_API int q3_add(const void* a, const void* b, void* out, int64_t n, q3_stream_t stream);
 /* Row-wise argmax of bf16 logits [rows, V] (first index on ties), int64 out. */
 Q3_API int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* out_idx, q3_stream_t stream);
+/* Distributed greedy argmax at TP > 1: replaces the all_gather of every rank's
+ * logits followed by argmax (model_fused.py:289-292,310,320).  Each rank
+ * writes, per row of its slice [rows, V] whose first column is vocabulary
+ * index col_offset, an int64 key that orders by value and then by lower
+ * global index; a MAX all-reduce (any library) of the ranks' keys followed by
+ * q3_argmax_key_index gives torch.argmax of the gathered logits, first index
+ * on ties.  col_offset + V < 2^32. */
+Q3_API int q3_argmax_key(const void* logits, int64_t rows, int64_t V, int64_t col_offset,
+                  int64_t* out_key, q3_stream_t stream);
+Q3_API int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* out_idx,
+                        q3_stream_t stream);
 
 #ifdef __cplusplus
 }

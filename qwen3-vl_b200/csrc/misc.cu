@@ -1,5 +1,8 @@
 // a13: embedding gather (model_fused.py:281) and greedy argmax
 // (model_fused.py:310,320).  Both are HBM-bound copies/scans with 16-byte loads.
+// At TP > 1 the argmax is distributed: each rank reduces its vocabulary slice
+// to one int64 key per row, and a MAX all-reduce of the keys replaces the
+// all_gather of the full logits (model_fused.py:289-292).
 #include <float.h>
 
 #include "common.cuh"
@@ -26,9 +29,24 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
   for (int64_t v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
 }
 
-// One CTA per row; ties resolve to the lowest index like torch.argmax.
+// Order-preserving int64 key of (value, global index): the high word orders
+// the float (sign-magnitude bits mapped to two's complement order), the low
+// word is ~index, so the larger key is the larger value and, on equal values,
+// the lower index.  A MAX reduction of the ranks' keys is then the argmax of
+// the concatenated vocabulary with torch.argmax's first-index tie rule.
+__device__ __forceinline__ int64_t argmax_key(float v, int64_t gidx) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  const int64_t hi = (int64_t)(int32_t)(ord ^ 0x80000000u);
+  return (int64_t)((uint64_t)hi << 32) | (int64_t)(0xffffffffu - (uint32_t)gidx);
+}
+
+// One CTA per row; ties resolve to the lowest index like torch.argmax.  With
+// KEY, writes argmax_key(max, col_offset + index) instead of the index.
+template <bool KEY>
 __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
-                                                     int64_t V, int64_t* __restrict__ out) {
+                                                     int64_t V, int64_t* __restrict__ out,
+                                                     int64_t col_offset) {
   pdl_wait();
   pdl_launch();
   const int64_t row = blockIdx.x;
@@ -74,8 +92,21 @@ __global__ void __launch_bounds__(512) argmax_kernel(const __nv_bfloat16* __rest
       const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
     }
-    if (lane == 0) out[row] = (bi == INT64_MAX) ? 0 : bi;
+    if (lane == 0) {
+      if constexpr (KEY)
+        out[row] = argmax_key(best, col_offset + ((bi == INT64_MAX) ? 0 : bi));
+      else
+        out[row] = (bi == INT64_MAX) ? 0 : bi;
+    }
   }
+}
+
+__global__ void argmax_key_index_kernel(const int64_t* __restrict__ keys, int64_t rows,
+                                        int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows) out[i] = (int64_t)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffff));
 }
 
 // out = bf16(a + b), the bf16 residual add of model_fused.py:269/275.
@@ -133,6 +164,32 @@ extern "C" int q3_argmax(const void* logits, int64_t rows, int64_t V, int64_t* o
              (long long)V);
   Q3_REQUIRE(aligned(logits, 16), "q3_argmax: misaligned logits");
   if (rows == 0) return Q3_OK;
-  return launch_ex(argmax_kernel, dim3((unsigned)rows), dim3(512), 0, (cudaStream_t)stream, 1,
-                   (const __nv_bfloat16*)logits, V, out_idx);
+  return launch_ex(argmax_kernel<false>, dim3((unsigned)rows), dim3(512), 0,
+                   (cudaStream_t)stream, 1, (const __nv_bfloat16*)logits, V, out_idx,
+                   (int64_t)0);
+}
+
+extern "C" int q3_argmax_key(const void* logits, int64_t rows, int64_t V, int64_t col_offset,
+                             int64_t* out_key, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(logits && out_key, "q3_argmax_key: null pointer");
+  Q3_REQUIRE(rows >= 0 && V > 0 && V % 8 == 0, "q3_argmax_key: V=%lld must be a multiple of 8",
+             (long long)V);
+  Q3_REQUIRE(col_offset >= 0 && col_offset + V <= 0xffffffffLL,
+             "q3_argmax_key: indices must fit in 32 bits");
+  Q3_REQUIRE(aligned(logits, 16) && aligned(out_key, 8), "q3_argmax_key: misaligned");
+  if (rows == 0) return Q3_OK;
+  return launch_ex(argmax_kernel<true>, dim3((unsigned)rows), dim3(512), 0,
+                   (cudaStream_t)stream, 1, (const __nv_bfloat16*)logits, V, out_key, col_offset);
+}
+
+extern "C" int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* out_idx,
+                                   q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(keys && out_idx, "q3_argmax_key_index: null pointer");
+  Q3_REQUIRE(rows >= 0, "q3_argmax_key_index: bad rows");
+  Q3_REQUIRE(aligned(keys, 8) && aligned(out_idx, 8), "q3_argmax_key_index: misaligned");
+  if (rows == 0) return Q3_OK;
+  return launch_ex(argmax_key_index_kernel, dim3((unsigned)((rows + 127) / 128)), dim3(128), 0,
+                   (cudaStream_t)stream, 1, keys, rows, out_idx);
 }

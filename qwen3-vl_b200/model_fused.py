@@ -197,8 +197,8 @@ class DecoderLayer:
 class _DecodeGraph:
     """One captured decode step for a fixed batch, KV bucket and cache storage."""
 
-    def __init__(self, graph, tok, pos, kv_len, logits):
-        self.graph, self.tok, self.pos, self.kv_len, self.logits = graph, tok, pos, kv_len, logits
+    def __init__(self, graph, tok, pos, kv_len):
+        self.graph, self.tok, self.pos, self.kv_len = graph, tok, pos, kv_len
 
 
 class Qwen3VLDecoderFused:
@@ -235,6 +235,9 @@ class Qwen3VLDecoderFused:
         # (opt-in: the separate norm/RoPE kernel already hides under the
         # attention kernel's early K/V stream, and measured 0.4% faster)
         self.fuse_attn_qkv = os.environ.get("Q3VL_FUSE_ATTN_QKV", "0") == "1"
+        # greedy decoding at TP > 1: MAX all-reduce of per-rank argmax keys
+        # instead of the all_gather of every rank's logits
+        self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
         self._step_plans = {}
         self._ss_step = None
 
@@ -450,6 +453,37 @@ class Qwen3VLDecoderFused:
 
     # --------------------------------------------------------------- logits
     def _logits(self, x, pend, B, S, ss_valid=False):
+        """Full-vocabulary logits [B, 1, V] (model_fused.py:286-292)."""
+        local = self._local_logits(x, pend, B, S, ss_valid)
+        if self.tp_size == 1:
+            return local.view(B, 1, -1)
+        return self._gather(local, B).view(B, 1, -1)
+
+    def _greedy(self, x, pend, B, S, ss_valid=False, out=None):
+        """Greedy next tokens int64 [B]: argmax of _logits (model_fused.py:310,320).
+        At TP > 1 each rank reduces its vocabulary slice to one key per row and
+        a MAX all-reduce of B int64 keys replaces the all_gather of the logits;
+        the key orders by value, then by lower index (torch.argmax's ties)."""
+        local = self._local_logits(x, pend, B, S, ss_valid)
+        if self.tp_size == 1 or not self.dist_argmax:
+            if self.tp_size > 1:
+                local = self._gather(local, B)
+            return ops.argmax(local.view(B, -1), out=out)
+        keys = ops.argmax_key(local.view(B, -1), self._rank() * local.shape[-1])
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+        return ops.argmax_key_index(keys, out=out)
+
+    def _gather(self, local, B):
+        gathered = torch.empty(self.tp_size, B, local.shape[-1], dtype=local.dtype,
+                               device=local.device)
+        dist.all_gather_into_tensor(gathered, local)
+        return gathered.permute(1, 0, 2).reshape(B, -1)
+
+    def _rank(self):
+        return dist.get_rank() if dist.is_initialized() else 0
+
+    def _local_logits(self, x, pend, B, S, ss_valid=False):
+        """This rank's vocabulary slice of the last position's logits [B, V/tp]."""
         H = x.shape[-1]
         if S > 1:
             x = x.view(B, S, H)[:, -1].contiguous()
@@ -466,12 +500,7 @@ class Qwen3VLDecoderFused:
         else:
             h = ops.rmsnorm(x, self.final_norm.weight, self.final_norm.eps)
             local = ops.gemm(h, self.lm_head.weight_km)
-        if self.tp_size == 1:
-            return local.view(B, 1, -1)
-        gathered = torch.empty(self.tp_size, B, local.shape[-1], dtype=local.dtype,
-                               device=local.device)
-        dist.all_gather_into_tensor(gathered, local)
-        return gathered.permute(1, 0, 2).reshape(B, 1, -1)
+        return local
 
     def _embed(self, input_ids):
         table = self.embed_tokens.weight if hasattr(self.embed_tokens, "weight") \
@@ -597,12 +626,14 @@ class Qwen3VLDecoderFused:
         use_step = self._step_ok(B)
 
         def step():
+            """One decode step; the next tokens land in `tok` (read at the start)."""
             if use_step:
-                return self._step_logits(B, tok, kv_cache, kv_len, rope_delta)
+                logits = self._step_logits(B, tok, kv_cache, kv_len, rope_delta)
+                return ops.argmax(logits.view(B, -1), out=tok)
             x = self._embed(tok.view(B, 1)).view(B, -1)
             x, pend = self._run(x, B, 1, 0, kv_cache, pos_dev=pos, kv_len_dev=kv_len,
                                 kv_bound=bucket, rope_delta=rope_delta)
-            return self._logits(x, pend, B, 1, ss_valid=self._ss_ok(B, 1))
+            return self._greedy(x, pend, B, 1, ss_valid=self._ss_ok(B, 1), out=tok)
 
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))
@@ -611,9 +642,8 @@ class Qwen3VLDecoderFused:
         torch.cuda.current_stream(dev).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            logits = step()
-            ops.argmax(logits.view(B, -1), out=tok)
-        g = _DecodeGraph(graph, tok, pos, kv_len, logits)
+            step()
+        g = _DecodeGraph(graph, tok, pos, kv_len)
         self._graphs[key] = g
         return g
 
@@ -660,9 +690,8 @@ class Qwen3VLDecoderFused:
         rope = self._mrope(position_ids) if position_ids is not None else None
         x, pend = self._run(x, B, P, 0, kv, rope=rope, deepstack=deepstack_embeds,
                             visual_mask=visual_mask)
-        logits = self._logits(x, pend, B, P)
         out = torch.empty(B, max_new_tokens, dtype=torch.int64, device=self.device)
-        out[:, 0] = ops.argmax(logits.view(B, -1))
+        out[:, 0] = self._greedy(x, pend, B, P)
         if prefill_done is not None:
             prefill_done.record(torch.cuda.current_stream(self.device))
         if max_new_tokens == 1:
@@ -688,7 +717,7 @@ class Qwen3VLDecoderFused:
             pos = P + i - 1
             x = self._embed(tok.view(B, 1)).view(B, -1)
             x, pend = self._run(x, B, 1, pos, kv, rope_delta=rope_delta)
-            tok = ops.argmax(self._logits(x, pend, B, 1, ss_valid=self._ss_ok(B, 1)).view(B, -1))
+            tok = self._greedy(x, pend, B, 1, ss_valid=self._ss_ok(B, 1))
             out[:, i] = tok
         return out
 

@@ -73,6 +73,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_embed": (I32, [P, P, P, I64, I64, I64, P]),
     "q3_add": (I32, [P, P, P, I64, P]),
     "q3_argmax": (I32, [P, I64, I64, P, P]),
+    "q3_argmax_key": (I32, [P, I64, I64, I64, P, P]),
+    "q3_argmax_key_index": (I32, [P, I64, P, P]),
 }
 
 _lib = None

@@ -520,6 +520,30 @@ def argmax(logits: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     return out
 
 
+def argmax_key(logits: torch.Tensor, col_offset: int, out: torch.Tensor = None) -> torch.Tensor:
+    """Per-row int64 keys of a vocabulary slice whose MAX over ranks encodes the
+    global argmax (first index on ties); decode with argmax_key_index."""
+    _cuda("argmax_key", logits, out)
+    _bf16("argmax_key", logits)
+    _contig("argmax_key", logits)
+    V = logits.shape[-1]
+    rows = logits.numel() // V
+    if out is None:
+        out = torch.empty(logits.shape[:-1], dtype=torch.int64, device=logits.device)
+    call("q3_argmax_key", _p(logits), rows, V, int(col_offset), _p(out), _stream())
+    return out
+
+
+def argmax_key_index(keys: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    _cuda("argmax_key_index", keys, out)
+    if keys.dtype != torch.int64 or not keys.is_contiguous():
+        raise TypeError("argmax_key_index: contiguous int64 keys")
+    if out is None:
+        out = torch.empty_like(keys)
+    call("q3_argmax_key_index", _p(keys), keys.numel(), _p(out), _stream())
+    return out
+
+
 def device_error(clear: bool = True) -> int:
     """Error code recorded by a kernel whose bounded wait timed out (0 = none)."""
     return int(_lib.raw("q3_device_error")(1 if clear else 0))

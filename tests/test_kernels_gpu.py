@@ -402,5 +402,33 @@ def test_embed_and_argmax():
     assert idx[2].item() == 77
 
 
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_distributed_argmax_keys_match_gathered_argmax(tp):
+    """Per-rank keys of the vocabulary slices, MAX-reduced (emulated here by
+    an elementwise max over the slices' keys), decode to torch.argmax of the
+    concatenated logits, first index on ties: ties inside a slice, across
+    slices, negative maxima, an all-equal row and -inf entries."""
+    V = 151936
+    logits = rnd(8, V, seed=42)
+    n = V // tp
+    logits[0, n // 2] = 50.0
+    logits[0, n + 3] = 50.0                      # same value in a later slice
+    logits[1] = -3.0                             # all equal -> index 0
+    logits[2] = -float("inf")
+    logits[2, V - 1] = -1e30                     # only finite entry, last slice
+    logits[3, 17] = 9.0
+    logits[3, 18] = 9.0                          # tie inside one slice
+    logits[4] = -(logits[4].abs() + 1)           # every value negative
+    logits[5, n - 1] = 30.0
+    logits[5, n] = 30.0                          # tie across a slice boundary
+    d = logits.to(DEV)
+    keys = torch.stack([ops.argmax_key(d[:, r * n:(r + 1) * n].contiguous(), r * n)
+                        for r in range(tp)])
+    idx = ops.argmax_key_index(keys.max(dim=0).values.contiguous()).cpu()
+    assert idx.tolist() == logits.float().argmax(-1).tolist()
+    assert idx[0].item() == n // 2 and idx[1].item() == 0 and idx[2].item() == V - 1
+    assert idx[3].item() == 17 and idx[5].item() == n - 1
+
+
 def test_device_error_word_clear():
     assert ops.device_error(clear=True) == 0

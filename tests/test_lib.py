@@ -71,6 +71,12 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     rc = lib.q3_attn_decode_qkv(one, one, one, one, one, 0, one, one, one, 1, 6, 4, 128, 8,
                                 None, 16, 0.1, 1e-6, None, 0, None)
     assert rc == _lib.Q3_ERR_INVALID
+    # distributed argmax keys hold 32-bit vocabulary indices
+    rc = lib.q3_argmax_key(one, 8, 1 << 16, (1 << 32) - 8, one, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"32 bits" in lib.q3_last_error()
+    # position ids: merge size must be positive
+    rc = lib.q3_rope_index(one, None, 1, 16, None, 0, None, 0, 0, one, one, one, one, 64, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"merge" in lib.q3_last_error()
     # in-kernel all-reduce needs a communicator
     rc = lib.q3_gemm_ar(one, one, one, 8, 4096, 512, None, None, None, None)
     assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
