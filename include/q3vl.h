@@ -39,7 +39,8 @@ enum q3_status {
   Q3_ERR_UNSUPPORTED = 2, /* valid request this build does not implement  */
   Q3_ERR_CUDA = 3,        /* CUDA runtime/driver error                    */
   Q3_ERR_TIMEOUT = 4,     /* a bounded in-kernel wait gave up             */
-  Q3_ERR_COMM = 5         /* peer setup / exchange failure                */
+  Q3_ERR_COMM = 5,        /* peer setup / exchange failure                */
+  Q3_ERR_NO_MEMORY = 6    /* a pool (KV pages) has too few free entries   */
 };
 
 enum q3_dtype { Q3_F32 = 0, Q3_BF16 = 1 };
@@ -84,6 +85,33 @@ Q3_API int q3_rope(const void* x, const float* cos_sin, void* out, int64_t seq, 
  * cos_out/sin_out f32 [n_tok, head_dim/2]. */
 Q3_API int q3_mrope_cos_sin(const int64_t* pos, const float* inv_freq, int64_t n_tok, int head_dim,
                      int sec_h, int sec_w, float* cos_out, float* sin_out, q3_stream_t stream);
+
+/* ---- paged KV cache: page allocator (host only) ---------------------------
+ * Replaces the per-request contiguous cache of init_kv_cache
+ * (model_fused.py:224-232) with pages shared by every sequence.  The caller
+ * owns the device storage, [num_pages, Hkv, page_tokens, D] per layer for K
+ * and for V; the allocator hands out page indices.  A slot (a sequence) owns
+ * pages in position order: position p lives in page row[p / page_tokens] at
+ * offset p % page_tokens.  page_tokens is a multiple of 64.  A reservation
+ * grows the slot to the smallest bucket (ascending token capacities, each a
+ * multiple of page_tokens) that covers `tokens`, or with no buckets to whole
+ * pages; it is all-or-nothing and returns Q3_ERR_NO_MEMORY when the pool is
+ * short.  Pages come from a LIFO free list that starts in ascending order,
+ * so ranks issuing the same calls hold identical tables.  Thread-safe. */
+Q3_API int q3_kv_pages_create(int num_pages, int page_tokens, int max_seqs, int max_pages_per_seq,
+                       const int64_t* buckets, int n_buckets, void** pool_out);
+Q3_API int q3_kv_pages_destroy(void* pool);
+/* Grow `slot` to cover `tokens` positions; capacity_out (may be NULL) gets the
+ * slot's capacity in tokens after the call. */
+Q3_API int q3_kv_pages_reserve(void* pool, int slot, int64_t tokens, int64_t* capacity_out);
+/* Return every page of `slot` to the pool. */
+Q3_API int q3_kv_pages_release(void* pool, int slot);
+/* Block-table rows of n slots into host int32 [n, width]; entries past a
+ * slot's pages are -1. */
+Q3_API int q3_kv_pages_table(const void* pool, const int32_t* slots, int n, int width,
+                      int32_t* table_out);
+/* Free pages of the pool and, if slot_pages is non-NULL, pages held by `slot`. */
+Q3_API int q3_kv_pages_stats(const void* pool, int slot, int64_t* free_pages, int64_t* slot_pages);
 
 /* ---- a4: multimodal 3-axis position ids ----------------------------------
  * Replaces Qwen3VLModel.get_rope_index (transformers 5.5.0

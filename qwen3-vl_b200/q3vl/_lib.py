@@ -13,7 +13,8 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libq3vl.so")
 
-Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_CUDA, Q3_ERR_TIMEOUT, Q3_ERR_COMM = range(6)
+(Q3_OK, Q3_ERR_INVALID, Q3_ERR_UNSUPPORTED, Q3_ERR_CUDA, Q3_ERR_TIMEOUT, Q3_ERR_COMM,
+ Q3_ERR_NO_MEMORY) = range(7)
 Q3_F32, Q3_BF16 = 0, 1
 Q3_EPI_NONE, Q3_EPI_RESIDUAL, Q3_EPI_SWIGLU = 0, 1, 2
 
@@ -23,6 +24,7 @@ _STATUS_NAMES = {
     Q3_ERR_CUDA: "CUDA error",
     Q3_ERR_TIMEOUT: "in-kernel wait timed out",
     Q3_ERR_COMM: "communication error",
+    Q3_ERR_NO_MEMORY: "pool exhausted",
 }
 
 
@@ -46,6 +48,12 @@ SIGNATURES: dict[str, tuple] = {
     "q3_rmsnorm": (I32, [P, P, P, P, P, I64, I64, F32, P]),
     "q3_rope": (I32, [P, P, P, I64, I32, I32, P]),
     "q3_mrope_cos_sin": (I32, [P, P, I64, I32, I32, I32, P, P, P]),
+    "q3_kv_pages_create": (I32, [I32, I32, I32, I32, P, I32, P]),
+    "q3_kv_pages_destroy": (I32, [P]),
+    "q3_kv_pages_reserve": (I32, [P, I32, I64, P]),
+    "q3_kv_pages_release": (I32, [P, I32]),
+    "q3_kv_pages_table": (I32, [P, P, I32, I32, P]),
+    "q3_kv_pages_stats": (I32, [P, I32, P, P]),
     "q3_rope_index_workspace_bytes": (SZ, [I32]),
     "q3_rope_index": (I32, [P, P, I32, I64, P, I32, P, I32, I32, P, P, P, P, SZ, P]),
     "q3_qkv_norm_rope": (I32, [P, P, P, P, P, I32, I32, I64, I64, P, P, P, P, P, I32, I32, I32,
