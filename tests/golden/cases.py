@@ -252,3 +252,81 @@ def rope_index_checksum() -> int:
                 total += int((a.reshape(-1).astype(np.int64) * w).sum())
         total += merge
     return total
+
+
+# ---- vision tower: a small Qwen3VLVisionModel with the real head_dim (72) ----
+VISION_TINY = dict(depth=3, hidden_size=144, num_heads=2, intermediate_size=256,
+                   out_hidden_size=128, num_position_embeddings=64, patch_size=16,
+                   temporal_patch_size=2, in_channels=3, spatial_merge_size=2,
+                   deepstack_visual_indexes=[0, 2])
+VISION_GRIDS = [[1, 8, 12], [2, 6, 4]]     # an image and a two-frame clip
+
+
+def vision_tiny_weights(seed: int = 31) -> dict:
+    """Seeded fp32 weights named as Qwen3VLVisionModel.state_dict() (N(0, 0.05)
+    matrices, N(0, 0.02) biases, LayerNorm weights near 1)."""
+    c = VISION_TINY
+    g = torch.Generator().manual_seed(seed)
+    H, I, O = c["hidden_size"], c["intermediate_size"], c["out_hidden_size"]
+    M = H * c["spatial_merge_size"] ** 2
+    inp = c["in_channels"] * c["temporal_patch_size"] * c["patch_size"] ** 2
+
+    def mat(o, i, std=0.05):
+        return torch.randn(o, i, generator=g) * std
+
+    def vec(n, std=0.02, base=0.0):
+        return base + torch.randn(n, generator=g) * std
+
+    p = {"patch_embed.proj.weight": mat(H, inp, 0.03).view(H, c["in_channels"],
+                                                           c["temporal_patch_size"],
+                                                           c["patch_size"], c["patch_size"]),
+         "patch_embed.proj.bias": vec(H),
+         "pos_embed.weight": torch.randn(c["num_position_embeddings"], H, generator=g) * 0.5}
+    for i in range(c["depth"]):
+        b = f"blocks.{i}."
+        p.update({b + "norm1.weight": vec(H, 0.1, 1.0), b + "norm1.bias": vec(H),
+                  b + "norm2.weight": vec(H, 0.1, 1.0), b + "norm2.bias": vec(H),
+                  b + "attn.qkv.weight": mat(3 * H, H), b + "attn.qkv.bias": vec(3 * H),
+                  b + "attn.proj.weight": mat(H, H), b + "attn.proj.bias": vec(H),
+                  b + "mlp.linear_fc1.weight": mat(I, H), b + "mlp.linear_fc1.bias": vec(I),
+                  b + "mlp.linear_fc2.weight": mat(H, I), b + "mlp.linear_fc2.bias": vec(H)})
+    mergers = ["merger."] + [f"deepstack_merger_list.{j}."
+                             for j in range(len(c["deepstack_visual_indexes"]))]
+    for j, m in enumerate(mergers):
+        n = H if j == 0 else M
+        p.update({m + "norm.weight": vec(n, 0.1, 1.0), m + "norm.bias": vec(n),
+                  m + "linear_fc1.weight": mat(M, M), m + "linear_fc1.bias": vec(M),
+                  m + "linear_fc2.weight": mat(O, M), m + "linear_fc2.bias": vec(O)})
+    return p
+
+
+def vision_tiny_inputs(seed: int = 32):
+    """Flattened patches [N, C*T*P*P] ~ N(0, 1) and grid_thw int64 [2, 3]."""
+    c = VISION_TINY
+    grid = torch.tensor(VISION_GRIDS, dtype=torch.int64)
+    n = int((grid[:, 0] * grid[:, 1] * grid[:, 2]).sum())
+    g = torch.Generator().manual_seed(seed)
+    inp = c["in_channels"] * c["temporal_patch_size"] * c["patch_size"] ** 2
+    return torch.randn(n, inp, generator=g), grid
+
+
+def hf_vision_tiny(dtype=torch.float32):
+    """transformers 5.5.0 Qwen3VLVisionModel (eager attention) on the seeded
+    weights and inputs: (pooler_output, deepstack features, last_hidden_state)."""
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLVisionConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLVisionModel
+    cfg = Qwen3VLVisionConfig(**VISION_TINY)
+    cfg._attn_implementation = "eager"
+    model = Qwen3VLVisionModel(cfg).eval()
+    missing, unexpected = model.load_state_dict(vision_tiny_weights(), strict=True)
+    assert not missing and not unexpected
+    model = model.to(dtype)
+    # from_pretrained(dtype=bf16), as the reference loads the model
+    # (loader_fused.py:56-58), keeps this buffer fp32 (_init_weights
+    # computes it in float); .to(dtype) would round it
+    rot = model.rotary_pos_emb
+    rot.inv_freq = 1.0 / (rot.theta ** (torch.arange(0, rot.dim, 2, dtype=torch.float) / rot.dim))
+    x, grid = vision_tiny_inputs()
+    with torch.no_grad():
+        out = model(x.to(dtype), grid_thw=grid)
+    return out.pooler_output, list(out.deepstack_features), out.last_hidden_state
