@@ -48,9 +48,14 @@ enum q3_dtype { Q3_F32 = 0, Q3_BF16 = 1 };
 enum q3_epilogue {
   Q3_EPI_NONE = 0,     /* C = A W^T                                          */
   Q3_EPI_RESIDUAL = 1, /* C = bf16(R + bf16(A W^T)); R = aux [M,N]           */
-  Q3_EPI_SWIGLU = 2    /* W rows interleaved gate/up in blocks of 8 (rows
+  Q3_EPI_SWIGLU = 2,   /* W rows interleaved gate/up in blocks of 8 (rows
                           16j..16j+7 = gate 8j..8j+7, 16j+8..16j+15 = up);
                           C[M, N/2] = silu(gate) * up                          */
+  /* q3_gemm_bias only (nn.Linear with bias; v = bf16(A W^T + b)):           */
+  Q3_EPI_BIAS = 3,           /* C = v                                        */
+  Q3_EPI_BIAS_GELU_TANH = 4, /* C = bf16(gelu_tanh(v))                       */
+  Q3_EPI_BIAS_GELU = 5,      /* C = bf16(gelu_erf(v))                        */
+  Q3_EPI_BIAS_RESIDUAL = 6   /* C = bf16(R + v); R = aux [M, N]              */
 };
 
 /* ---- library ---------------------------------------------------------- */
@@ -112,6 +117,39 @@ Q3_API int q3_kv_pages_table(const void* pool, const int32_t* slots, int n, int 
                       int32_t* table_out);
 /* Free pages of the pool and, if slot_pages is non-NULL, pages held by `slot`. */
 Q3_API int q3_kv_pages_stats(const void* pool, int slot, int64_t* free_pages, int64_t* slot_pages);
+
+/* ---- vision tower (transformers 5.5.0 Qwen3VLVisionModel, which the
+ * reference runs at vision.py:51-53, :74-76) --------------------------------
+ * Tokens are patches in merge-block order.  The image table `imgs` is int32
+ * [n_img][4] = {t, h, w, first token} in device memory, with the same table in
+ * host memory as `imgs_host` (checked before launch: h, w multiples of merge,
+ * first tokens the running sums of t*h*w, n_tok tokens in all). */
+
+/* LayerNorm over the last dim: y = bf16((x - mean) * rstd * w + b), fp32
+ * statistics (nn.LayerNorm of Qwen3VLVisionBlock :268-269 and the mergers
+ * :113).  x, y bf16 [rows, cols]; w, b bf16 [cols]; cols % 8 == 0. */
+Q3_API int q3_layernorm(const void* x, const void* w, const void* b, void* y, int64_t rows, int64_t cols,
+                 float eps, q3_stream_t stream);
+/* Bilinear position embeddings, fast_pos_embed_interpolate :702-763: table
+ * bf16 [side*side, hidden]; out bf16 [n_tok, hidden] in merge-block order. */
+Q3_API int q3_vision_pos_embed(const void* table, int side, int hidden, const int32_t* imgs,
+                        const int32_t* imgs_host, int n_img, int merge, int64_t n_tok, void* out,
+                        q3_stream_t stream);
+/* 2-D vision RoPE in place on q and k of the packed qkv bf16 [n_tok, 3*heads*72]
+ * (rot_pos_emb :662-700, apply_rotary_pos_emb_vision :131-142); inv_freq f32
+ * [18] (head_dim/4 frequencies; the first 18 angles use the patch row, the
+ * next 18 the column). */
+Q3_API int q3_vision_rope(void* qkv, int heads, int head_dim, const float* inv_freq,
+                   const int32_t* imgs, const int32_t* imgs_host, int n_img, int merge,
+                   int64_t n_tok, q3_stream_t stream);
+/* Non-causal attention inside each frame (Qwen3VLVisionAttention.forward
+ * :196-262): qkv bf16 [n_tok, 3*heads*72] after the RoPE; out bf16 [n_tok,
+ * heads*72].  blocks int32 [n_blocks][3] = {frame first token, frame length,
+ * first query row (a multiple of 128)}: one entry per 128-row query block of
+ * every frame, device and host copies. */
+Q3_API int q3_vision_attention(const void* qkv, void* out, int heads, int head_dim,
+                        const int32_t* blocks, const int32_t* blocks_host, int n_blocks,
+                        int64_t n_tok, q3_stream_t stream);
 
 /* ---- a4: multimodal 3-axis position ids ----------------------------------
  * Replaces Qwen3VLModel.get_rope_index (transformers 5.5.0
@@ -222,6 +260,18 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
  * the HBM-streaming decode kernel, larger M the tcgen05/TMEM kernel. */
 Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
             const void* aux, q3_stream_t stream);
+
+/* ---- vision tower linears: nn.Linear with bias (tcgen05 GEMM) -------------
+ * Replaces the vision tower's linears (transformers 5.5.0 modeling_qwen3_vl.py:
+ * attn.qkv / attn.proj :189-190, mlp.linear_fc1/fc2 :64-65, merger fc1/fc2
+ * :114-116, the patch-embed Conv3d :72-89 as a GEMM) with the epilogues that
+ * follow them: Q3_EPI_BIAS, Q3_EPI_BIAS_GELU_TANH (MLP), Q3_EPI_BIAS_GELU
+ * (mergers), Q3_EPI_BIAS_RESIDUAL (block residual adds :288-295, and the
+ * position-embedding add after the patch embed :783).  A bf16 [M, K]; W bf16
+ * [N, K] (nn.Linear's own layout); bias bf16 [N]; C bf16 [M, N]; aux = R
+ * [M, N].  K % 8 == 0 and N % 8 == 0; K and N need not fill the tiles. */
+Q3_API int q3_gemm_bias(const void* A, const void* W, const void* bias, void* C, int64_t M, int64_t N,
+                 int64_t K, int epilogue, const void* aux, q3_stream_t stream);
 
 /* Prefill QKV projection with its epilogue fused (tcgen05 GEMM): h @ Wqkv
  * (model_fused.py:103) followed by the per-head QK-RMSNorm, rotate-half RoPE

@@ -45,7 +45,34 @@ struct TcCfg {
 // Internal epilogue id of the fused QKV projection: per-head QK-RMSNorm,
 // rotate-half RoPE and the KV-cache write (AttentionBlock.forward after the
 // matmul, model_fused.py:107-129, and the cache write, :244-246).
-constexpr int kEpiQkvRope = 3;
+constexpr int kEpiQkvRope = 16;
+
+// Bias epilogues of nn.Linear (the vision tower's linears): v = bf16(acc + b)
+// -- one rounding, as a linear with bias computes -- then Q3_EPI_BIAS_GELU_TANH
+// bf16(gelu_tanh(v)), Q3_EPI_BIAS_GELU bf16(gelu_erf(v)), or
+// Q3_EPI_BIAS_RESIDUAL bf16(R + v).
+__device__ __forceinline__ bool epi_has_bias(int e) {
+  return e == Q3_EPI_BIAS || e == Q3_EPI_BIAS_GELU_TANH || e == Q3_EPI_BIAS_GELU ||
+         e == Q3_EPI_BIAS_RESIDUAL;
+}
+// torch's tanh-approximated GELU: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float kBeta = 0.7978845608028654f, kKappa = 0.044715f;
+  const float inner = kBeta * (x + kKappa * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+// exact GELU: 0.5 x (1 + erf(x / sqrt(2)))
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+}
+template <int EPI>
+__device__ __forceinline__ float bias_epilogue(float acc, float bias, float res) {
+  float v = rbf(acc + bias);
+  if constexpr (EPI == Q3_EPI_BIAS_GELU_TANH) v = rbf(gelu_tanh(v));
+  if constexpr (EPI == Q3_EPI_BIAS_GELU) v = rbf(gelu_erf(v));
+  if constexpr (EPI == Q3_EPI_BIAS_RESIDUAL) v = rbf(res + v);
+  return v;
+}
 
 struct TcQkv {
   const __nv_bfloat16* q_norm;  // [128]
@@ -65,6 +92,7 @@ struct TcQkv {
 struct TcParams {
   __nv_bfloat16* C;
   const __nv_bfloat16* R;
+  const __nv_bfloat16* bias;  // [N], bias epilogues only
   int M, N, K, ldc;
   int m_tiles, n_tiles;
   int* err;
@@ -334,6 +362,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
               dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
             }
+          } else if constexpr (EPI == Q3_EPI_BIAS || EPI == Q3_EPI_BIAS_GELU_TANH ||
+                               EPI == Q3_EPI_BIAS_GELU || EPI == Q3_EPI_BIAS_RESIDUAL) {
+            const int col0 = nt * BN + c * 32;
+            __nv_bfloat16* dst = p.C + (int64_t)row * p.ldc + col0;
+            const __nv_bfloat16* rrow = p.R + (int64_t)row * p.ldc + col0;
+            if (col0 + 32 <= p.N) {
+              uint32_t o[16];
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const uint4 bv = *reinterpret_cast<const uint4*>(p.bias + col0 + v * 8);
+                const uint4 rv = EPI == Q3_EPI_BIAS_RESIDUAL
+                                     ? *reinterpret_cast<const uint4*>(rrow + v * 8)
+                                     : make_uint4(0, 0, 0, 0);
+                const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 bb = unpack_bf16x2(bw[i]);
+                  const float2 res = unpack_bf16x2(rw[i]);
+                  o[v * 4 + i] = pack_bf16x2(
+                      bias_epilogue<EPI>(__uint_as_float(r[v * 8 + 2 * i]), bb.x, res.x),
+                      bias_epilogue<EPI>(__uint_as_float(r[v * 8 + 2 * i + 1]), bb.y, res.y));
+                }
+              }
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                d4[v] = make_uint4(o[v * 4], o[v * 4 + 1], o[v * 4 + 2], o[v * 4 + 3]);
+            } else {
+              for (int i = 0; i < 32 && col0 + i < p.N; ++i) {
+                const float res = EPI == Q3_EPI_BIAS_RESIDUAL ? bf2f(rrow[i]) : 0.f;
+                dst[i] = f2bf(bias_epilogue<EPI>(__uint_as_float(r[i]), bf2f(p.bias[col0 + i]), res));
+              }
+            }
           } else {
             const int col0 = nt * BN + c * 32;
             uint32_t o[16];
@@ -390,7 +452,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------
 template <int BN, int EPI>
 static int launch_tc(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                     cudaStream_t s, const TcQkv* qkv = nullptr) {
+                     cudaStream_t s, const TcQkv* qkv = nullptr, const void* bias = nullptr) {
   using Cfg = TcCfg<BN>;
   CUtensorMap ta, tw;
   int rc = make_tmap_2d(&ta, A, M, K, kBM, kBK);
@@ -408,6 +470,7 @@ static int launch_tc(const void* A, const void* W, void* C, const void* R, int M
   TcParams p;
   p.C = (__nv_bfloat16*)C;
   p.R = (const __nv_bfloat16*)R;
+  p.bias = (const __nv_bfloat16*)bias;
   p.M = M; p.N = N; p.K = K;
   p.ldc = EPI == Q3_EPI_SWIGLU ? N / 2 : N;
   p.m_tiles = (M + kBM - 1) / kBM;
@@ -536,4 +599,36 @@ extern "C" int q3_gemm_qkv_rope(const void* A, const void* W, int64_t hidden, co
   const int M = B * S, N = (Hq + 2 * Hkv) * 128;
   return launch_tc<256, kEpiQkvRope>(A, W, nullptr, nullptr, M, N, (int)hidden,
                                      (cudaStream_t)stream, &q);
+}
+
+extern "C" int q3_gemm_bias(const void* A, const void* W, const void* bias, void* C, int64_t M,
+                            int64_t N, int64_t K, int epilogue, const void* aux,
+                            q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && W && bias && C, "q3_gemm_bias: null pointer");
+  Q3_REQUIRE(M >= 0 && N > 0 && K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
+             "q3_gemm_bias: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+             (long long)K);
+  Q3_REQUIRE(K % 8 == 0, "q3_gemm_bias: K=%lld must be a multiple of 8 (16-byte rows)",
+             (long long)K);
+  Q3_REQUIRE(N % 8 == 0, "q3_gemm_bias: N=%lld must be a multiple of 8", (long long)N);
+  Q3_REQUIRE(epilogue == Q3_EPI_BIAS || epilogue == Q3_EPI_BIAS_GELU_TANH ||
+                 epilogue == Q3_EPI_BIAS_GELU || epilogue == Q3_EPI_BIAS_RESIDUAL,
+             "q3_gemm_bias: epilogue %d is not a bias epilogue", epilogue);
+  Q3_REQUIRE(epilogue != Q3_EPI_BIAS_RESIDUAL || aux, "q3_gemm_bias: residual epilogue needs aux");
+  Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(C, 16) && aligned(bias, 16) &&
+                 (!aux || aligned(aux, 16)),
+             "q3_gemm_bias: pointers must be 16-byte aligned");
+  if (M == 0) return Q3_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int m = (int)M, n = (int)N, k = (int)K;
+  switch (epilogue) {
+    case Q3_EPI_BIAS: return launch_tc<256, Q3_EPI_BIAS>(A, W, C, aux, m, n, k, s, nullptr, bias);
+    case Q3_EPI_BIAS_GELU_TANH:
+      return launch_tc<256, Q3_EPI_BIAS_GELU_TANH>(A, W, C, aux, m, n, k, s, nullptr, bias);
+    case Q3_EPI_BIAS_GELU:
+      return launch_tc<256, Q3_EPI_BIAS_GELU>(A, W, C, aux, m, n, k, s, nullptr, bias);
+    default:
+      return launch_tc<256, Q3_EPI_BIAS_RESIDUAL>(A, W, C, aux, m, n, k, s, nullptr, bias);
+  }
 }

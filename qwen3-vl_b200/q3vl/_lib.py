@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libq3vl.so")
  Q3_ERR_NO_MEMORY) = range(7)
 Q3_F32, Q3_BF16 = 0, 1
 Q3_EPI_NONE, Q3_EPI_RESIDUAL, Q3_EPI_SWIGLU = 0, 1, 2
+Q3_EPI_BIAS, Q3_EPI_BIAS_GELU_TANH, Q3_EPI_BIAS_GELU, Q3_EPI_BIAS_RESIDUAL = 3, 4, 5, 6
 
 _STATUS_NAMES = {
     Q3_ERR_INVALID: "invalid argument",
@@ -48,6 +49,11 @@ SIGNATURES: dict[str, tuple] = {
     "q3_rmsnorm": (I32, [P, P, P, P, P, I64, I64, F32, P]),
     "q3_rope": (I32, [P, P, P, I64, I32, I32, P]),
     "q3_mrope_cos_sin": (I32, [P, P, I64, I32, I32, I32, P, P, P]),
+    "q3_gemm_bias": (I32, [P, P, P, P, I64, I64, I64, I32, P, P]),
+    "q3_layernorm": (I32, [P, P, P, P, I64, I64, F32, P]),
+    "q3_vision_pos_embed": (I32, [P, I32, I32, P, P, I32, I32, I64, P, P]),
+    "q3_vision_rope": (I32, [P, I32, I32, P, P, P, I32, I32, I64, P]),
+    "q3_vision_attention": (I32, [P, P, I32, I32, P, P, I32, I64, P]),
     "q3_kv_pages_create": (I32, [I32, I32, I32, I32, P, I32, P]),
     "q3_kv_pages_destroy": (I32, [P]),
     "q3_kv_pages_reserve": (I32, [P, I32, I64, P]),

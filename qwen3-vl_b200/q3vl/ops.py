@@ -99,6 +99,90 @@ def mrope_cos_sin(position_ids: torch.Tensor, inv_freq: torch.Tensor,
     return cos, sin
 
 
+# ----------------------------------------------------------------------------
+# vision tower: linears with bias epilogues, LayerNorm, position embeddings,
+# 2-D RoPE, frame-local attention
+# ----------------------------------------------------------------------------
+_EPI_BIAS = {"bias": _lib.Q3_EPI_BIAS, "bias_gelu_tanh": _lib.Q3_EPI_BIAS_GELU_TANH,
+             "bias_gelu": _lib.Q3_EPI_BIAS_GELU, "bias_residual": _lib.Q3_EPI_BIAS_RESIDUAL}
+
+
+def gemm_bias(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, epilogue: str = "bias",
+              residual: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+    """nn.Linear with bias (w [N, K], the module's own layout) and a fused
+    epilogue: "bias", "bias_gelu_tanh", "bias_gelu" (erf) or "bias_residual"
+    (out = residual + linear; `out` may be `residual` itself)."""
+    _cuda("gemm_bias", a, w, bias, residual, out)
+    _bf16("gemm_bias", a, w, bias)
+    _contig("gemm_bias", a, w, bias)
+    if epilogue not in _EPI_BIAS:
+        raise ValueError(f"gemm_bias: unknown epilogue {epilogue!r}")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K or bias.numel() != N:
+        raise ValueError(f"gemm_bias: shapes a {tuple(a.shape)} w {tuple(w.shape)} "
+                         f"bias {tuple(bias.shape)}")
+    if epilogue == "bias_residual":
+        if residual is None or tuple(residual.shape) != (M, N) or not residual.is_contiguous():
+            raise ValueError("gemm_bias: bias_residual needs a contiguous [M, N] residual")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    call("q3_gemm_bias", _p(a), _p(w), _p(bias), _p(out), M, N, K, _EPI_BIAS[epilogue],
+         _p(residual), _stream())
+    return out
+
+
+def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-6,
+              out: torch.Tensor = None) -> torch.Tensor:
+    """nn.LayerNorm over the last dim (bf16 in and out, fp32 statistics)."""
+    _cuda("layernorm", x, w, b, out)
+    _bf16("layernorm", x, w, b)
+    _contig("layernorm", x, w, b)
+    cols = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    call("q3_layernorm", _p(x), _p(w), _p(b), _p(out), x.numel() // cols, cols, float(eps),
+         _stream())
+    return out
+
+
+def vision_pos_embed(table: torch.Tensor, imgs: torch.Tensor, imgs_host: torch.Tensor,
+                     merge: int, n_tok: int) -> torch.Tensor:
+    """Bilinear position embeddings [n_tok, hidden] in merge-block token order;
+    imgs int32 [n_img, 4] = (t, h, w, first token) on the device, imgs_host the
+    same on the host."""
+    _cuda("vision_pos_embed", table, imgs)
+    side = int(round(table.shape[0] ** 0.5))
+    out = torch.empty(n_tok, table.shape[1], dtype=torch.bfloat16, device=table.device)
+    call("q3_vision_pos_embed", _p(table), side, table.shape[1], _p(imgs), _p(imgs_host),
+         imgs.shape[0], int(merge), int(n_tok), _p(out), _stream())
+    return out
+
+
+def vision_rope(qkv: torch.Tensor, heads: int, inv_freq: torch.Tensor, imgs: torch.Tensor,
+                imgs_host: torch.Tensor, merge: int) -> torch.Tensor:
+    """2-D RoPE in place on q and k of the packed qkv [n_tok, 3 * heads * 72]."""
+    _cuda("vision_rope", qkv, inv_freq, imgs)
+    _contig("vision_rope", qkv)
+    call("q3_vision_rope", _p(qkv), int(heads), qkv.shape[1] // (3 * heads), _p(inv_freq),
+         _p(imgs), _p(imgs_host), imgs.shape[0], int(merge), qkv.shape[0], _stream())
+    return qkv
+
+
+def vision_attention(qkv: torch.Tensor, heads: int, blocks: torch.Tensor,
+                     blocks_host: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """Attention inside each frame: qkv [n_tok, 3 * heads * 72] -> [n_tok, heads * 72];
+    blocks int32 [n_blocks, 3] = (frame first token, frame length, first query row)."""
+    _cuda("vision_attention", qkv, blocks, out)
+    _contig("vision_attention", qkv)
+    n_tok, width = qkv.shape
+    hd = width // (3 * heads)
+    if out is None:
+        out = torch.empty(n_tok, heads * hd, dtype=torch.bfloat16, device=qkv.device)
+    call("q3_vision_attention", _p(qkv), _p(out), int(heads), hd, _p(blocks), _p(blocks_host),
+         blocks.shape[0], n_tok, _stream())
+    return out
+
+
 _ROPE_INDEX_ERRORS = {
     1: "more vision runs than grids",
     2: "vision run length differs from its grid",

@@ -263,9 +263,13 @@ VISION_GRIDS = [[1, 8, 12], [2, 6, 4]]     # an image and a two-frame clip
 
 
 def vision_tiny_weights(seed: int = 31) -> dict:
-    """Seeded fp32 weights named as Qwen3VLVisionModel.state_dict() (N(0, 0.05)
-    matrices, N(0, 0.02) biases, LayerNorm weights near 1)."""
-    c = VISION_TINY
+    """Seeded fp32 weights of VISION_TINY (see vision_weights)."""
+    return vision_weights(VISION_TINY, seed)
+
+
+def vision_weights(c: dict, seed: int) -> dict:
+    """Seeded fp32 weights named as Qwen3VLVisionModel.state_dict() for config
+    dict `c` (N(0, 0.05) matrices, N(0, 0.02) biases, LayerNorm weights near 1)."""
     g = torch.Generator().manual_seed(seed)
     H, I, O = c["hidden_size"], c["intermediate_size"], c["out_hidden_size"]
     M = H * c["spatial_merge_size"] ** 2
