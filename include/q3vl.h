@@ -117,6 +117,27 @@ Q3_API int q3_kv_pages_table(const void* pool, const int32_t* slots, int n, int 
                       int32_t* table_out);
 /* Free pages of the pool and, if slot_pages is non-NULL, pages held by `slot`. */
 Q3_API int q3_kv_pages_stats(const void* pool, int slot, int64_t* free_pages, int64_t* slot_pages);
+/* Device side: copy new K/V rows bf16 [B, Hkv, S, 128] (as q3_qkv_norm_rope
+ * writes k_out / v_out) into the page pools at positions pos .. pos+S-1 of
+ * each sequence, pos = *pos_dev if non-NULL else start_pos; block_table int32
+ * [B, table_stride] on the device (q3_kv_pages_table rows).  A position past
+ * the table or a page outside [0, num_pages) is skipped and recorded in the
+ * device error word (q3_device_error). */
+Q3_API int q3_kv_pages_write(const void* k_src, const void* v_src, void* k_pages, void* v_pages, int B,
+                      int Hkv, int S, int head_dim, const int32_t* block_table,
+                      int64_t table_stride, int page_tokens, int num_pages, int64_t start_pos,
+                      const int32_t* pos_dev, q3_stream_t stream);
+/* Decode attention over paged K/V (q3_attn_decode semantics, bf16): k_pages,
+ * v_pages [num_pages, Hkv, page_tokens, 128]; position t of sequence b is read
+ * from page block_table[b * table_stride + t / page_tokens].  page_tokens is a
+ * multiple of 64; workspace as q3_attn_decode_workspace_bytes(B, Hq, Hkv, 128,
+ * kv_len).  A table entry outside the pool is recorded in the device error
+ * word and page 0 read in its place. */
+Q3_API int q3_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages, void* out,
+                         int B, int Hq, int Hkv, int head_dim, int64_t kv_len,
+                         const int32_t* kv_len_dev, const int32_t* block_table,
+                         int64_t table_stride, int page_tokens, int num_pages, float scale,
+                         void* workspace, size_t workspace_bytes, q3_stream_t stream);
 
 /* ---- vision tower (transformers 5.5.0 Qwen3VLVisionModel, which the
  * reference runs at vision.py:51-53, :74-76) --------------------------------

@@ -124,6 +124,12 @@ struct DecodeParams {
   float eps;
   __nv_bfloat16* k_cache_w;  // the caches again, for writing the new row
   __nv_bfloat16* v_cache_w;
+  // paged variant (q3_attn_decode_paged): k/v are page pools [num_pages, Hkv,
+  // page_tokens, 128]; position t of sequence b lives in page
+  // pages[b * pages_stride + t / page_tokens] at offset t % page_tokens
+  const int32_t* pages;
+  int64_t pages_stride;
+  int page_tokens, num_pages;
 };
 
 // Positions per split.  The grid's split count is planned on the host from
@@ -417,7 +423,7 @@ __device__ __forceinline__ void head_norm_rope(const __nv_bfloat16* x, const Hea
   }
 }
 
-template <int G, bool FQ>
+template <int G, bool FQ, bool PAGED = false>
 __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
     DecodeTcParams prm) {
@@ -475,7 +481,19 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
         }
         if (!mbar_wait(&empty[s], ph ^ 1, prm.err, 0x401)) break;
         uint8_t* st = ring + s * kTcStageBytes;
-        const int y = (int)(row_base + (int64_t)i * kTcTile);
+        int y;
+        if constexpr (PAGED) {
+          // a 64-position tile never straddles pages (page_tokens % 64 == 0)
+          const int64_t t = start + (int64_t)i * kTcTile;
+          int pg = p.pages[(int64_t)b * p.pages_stride + t / p.page_tokens];
+          if (pg < 0 || pg >= p.num_pages) {  // a bad table entry: record it, read page 0
+            report_timeout(prm.err, 0x402);
+            pg = 0;
+          }
+          y = (int)(((int64_t)pg * p.Hkv + kvh) * p.page_tokens + t % p.page_tokens);
+        } else {
+          y = (int)(row_base + (int64_t)i * kTcTile);
+        }
         mbar_arrive_expect_tx(&full[s], kTcStageBytes);
         tma_load_2d(st, &tmK, &full[s], 0, y, kCacheEvictFirst);
         tma_load_2d(st + kTcHalfBytes, &tmK, &full[s], 64, y, kCacheEvictFirst);
@@ -681,18 +699,29 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
 static void decode_split_plan_step(int B, int Hkv, int64_t max_kv_len, int step, int* splits,
                                    int* chunk);
 
-static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_qkv = false) {
+static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_qkv = false,
+                            bool paged = false) {
   void (*kern)(const CUtensorMap, const CUtensorMap, DecodeTcParams) = nullptr;
   int gi = 0;
-  switch (G) {
-    case 1: kern = fused_qkv ? attn_decode_tc_kernel<1, true> : attn_decode_tc_kernel<1, false>; gi = 0; break;
-    case 2: kern = fused_qkv ? attn_decode_tc_kernel<2, true> : attn_decode_tc_kernel<2, false>; gi = 1; break;
-    case 4: kern = fused_qkv ? attn_decode_tc_kernel<4, true> : attn_decode_tc_kernel<4, false>; gi = 2; break;
-    case 8: kern = fused_qkv ? attn_decode_tc_kernel<8, true> : attn_decode_tc_kernel<8, false>; gi = 3; break;
-    default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
+  if (paged) {
+    switch (G) {
+      case 1: kern = attn_decode_tc_kernel<1, false, true>; gi = 8; break;
+      case 2: kern = attn_decode_tc_kernel<2, false, true>; gi = 9; break;
+      case 4: kern = attn_decode_tc_kernel<4, false, true>; gi = 10; break;
+      case 8: kern = attn_decode_tc_kernel<8, false, true>; gi = 11; break;
+      default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
+    }
+  } else {
+    switch (G) {
+      case 1: kern = fused_qkv ? attn_decode_tc_kernel<1, true> : attn_decode_tc_kernel<1, false>; gi = 0; break;
+      case 2: kern = fused_qkv ? attn_decode_tc_kernel<2, true> : attn_decode_tc_kernel<2, false>; gi = 1; break;
+      case 4: kern = fused_qkv ? attn_decode_tc_kernel<4, true> : attn_decode_tc_kernel<4, false>; gi = 2; break;
+      case 8: kern = fused_qkv ? attn_decode_tc_kernel<8, true> : attn_decode_tc_kernel<8, false>; gi = 3; break;
+      default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
+    }
+    if (fused_qkv) gi += 4;
   }
-  if (fused_qkv) gi += 4;
-  static int per_sm_cache[64][8] = {{0}};
+  static int per_sm_cache[64][12] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
   const bool cacheable = dev >= 0 && dev < 64;
@@ -724,7 +753,8 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   p.chunk = (int)ch;
   if (sp > 1) p.ws_ml = p.ws_acc + (size_t)p.B * p.Hq * sp * kHD;
   CUtensorMap tk, tv;
-  const int64_t rows = (int64_t)p.B * p.Hkv * p.max_seq;
+  const int64_t rows = paged ? (int64_t)p.num_pages * p.Hkv * p.page_tokens
+                             : (int64_t)p.B * p.Hkv * p.max_seq;
   int rc = cached_tmap_2d(&tk, p.k, rows, kHD, kTcTile, 64);
   if (rc) return rc;
   rc = cached_tmap_2d(&tv, p.v, rows, kHD, kTcTile, 64);
@@ -943,4 +973,47 @@ extern "C" int q3_attn_decode_noalloc(const void* q, const void* k_cache, const 
   const int G = Hq / Hkv;
   cudaStream_t s = (cudaStream_t)stream;
   return dtype == Q3_F32 ? launch_decode<float>(p, G, s) : launch_decode<__nv_bfloat16>(p, G, s);
+}
+
+extern "C" int q3_attn_decode_paged(const void* q, const void* k_pages, const void* v_pages,
+                                    void* out, int B, int Hq, int Hkv, int head_dim,
+                                    int64_t kv_len, const int32_t* kv_len_dev,
+                                    const int32_t* block_table, int64_t table_stride,
+                                    int page_tokens, int num_pages, float scale, void* workspace,
+                                    size_t workspace_bytes, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(q && k_pages && v_pages && out && block_table, "q3_attn_decode_paged: null pointer");
+  Q3_REQUIRE(head_dim == kHD, "q3_attn_decode_paged: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+             "q3_attn_decode_paged: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  Q3_REQUIRE(page_tokens > 0 && page_tokens % kTcTile == 0 && num_pages > 0,
+             "q3_attn_decode_paged: page_tokens=%d must be a positive multiple of %d",
+             page_tokens, kTcTile);
+  Q3_REQUIRE((int64_t)num_pages * Hkv * page_tokens < (1ll << 31),
+             "q3_attn_decode_paged: pool of %d pages too large for 32-bit rows", num_pages);
+  Q3_REQUIRE(table_stride > 0 && kv_len >= 1 && kv_len <= table_stride * page_tokens,
+             "q3_attn_decode_paged: kv_len=%lld beyond the table width (%lld pages of %d)",
+             (long long)kv_len, (long long)table_stride, page_tokens);
+  Q3_REQUIRE(aligned(q, 8) && aligned(k_pages, 16) && aligned(v_pages, 16) && aligned(out, 8) &&
+                 aligned(block_table, 4),
+             "q3_attn_decode_paged: misaligned pointer");
+  DecodeParams p{};
+  p.q = q; p.k = k_pages; p.v = v_pages; p.out = out;
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv;
+  p.kv_len = kv_len; p.kv_len_dev = kv_len_dev; p.max_seq = table_stride * page_tokens;
+  p.scale = scale;
+  p.pages = block_table;
+  p.pages_stride = table_stride;
+  p.page_tokens = page_tokens;
+  p.num_pages = num_pages;
+  decode_split_plan(B, Hkv, kv_len, &p.splits, &p.chunk);
+  if (p.splits > 1) {
+    const size_t need = (size_t)B * Hq * p.splits * (kHD + 2) * sizeof(float);
+    Q3_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+               "q3_attn_decode_paged: workspace of %zu bytes needed (got %zu)", need,
+               workspace_bytes);
+    p.ws_acc = reinterpret_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + (size_t)B * Hq * p.splits * kHD;
+  }
+  return launch_decode_tc(p, Hq / Hkv, (cudaStream_t)stream, false, true);
 }

@@ -13,7 +13,12 @@
 // fixed table width.  With no buckets, capacity is rounded up to whole pages.
 // Allocation is all-or-nothing and deterministic (a LIFO free list that
 // starts in ascending page order), so tensor-parallel ranks that issue the
-// same calls hold the same tables.  All calls are host-only and thread-safe.
+// same calls hold the same tables.  The allocator calls are host-only and
+// thread-safe.
+//
+// q3_kv_pages_write is the device side of the KV write (model_fused.py:244-246
+// for a paged cache): it copies the new K/V rows, as q3_qkv_norm_rope emits
+// them densely, into their pages, one warp per 256-byte row.
 #include <algorithm>
 #include <mutex>
 #include <new>
@@ -41,8 +46,68 @@ int64_t capacity_for(const KvPages& p, int64_t tokens) {
   return -1;
 }
 
+constexpr int kPageHd = 128;
+
+// One warp per (b, kv head, s, K|V) row: 32 lanes x 8 bytes.  A position past
+// the table or a page index outside the pool is recorded in the device error
+// word and its row skipped (no write outside the pool).
+__global__ void __launch_bounds__(256) kv_page_write_kernel(
+    const __nv_bfloat16* __restrict__ k_src, const __nv_bfloat16* __restrict__ v_src,
+    __nv_bfloat16* __restrict__ k_pages, __nv_bfloat16* __restrict__ v_pages,
+    const int32_t* __restrict__ table, int64_t stride, int page_tokens, int num_pages, int B,
+    int Hkv, int S, int64_t start_pos, const int32_t* __restrict__ pos_dev, int* err) {
+  pdl_wait();
+  pdl_launch();
+  const int lane = threadIdx.x & 31;
+  const int64_t job = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t rows = (int64_t)B * Hkv * S;
+  if (job >= 2 * rows) return;
+  const bool is_v = job >= rows;
+  const int64_t r = is_v ? job - rows : job;  // (b * Hkv + h) * S + s
+  const int s = (int)(r % S);
+  const int64_t bh = r / S;
+  const int h = (int)(bh % Hkv), b = (int)(bh / Hkv);
+  const int64_t t = (pos_dev ? (int64_t)(*pos_dev) : start_pos) + s;
+  const int64_t slot = t / page_tokens;
+  const int pg = (t >= 0 && slot < stride) ? table[(int64_t)b * stride + slot] : -1;
+  if (pg < 0 || pg >= num_pages) {
+    if (lane == 0) report_timeout(err, 0x403);
+    return;
+  }
+  const uint2* src = reinterpret_cast<const uint2*>((is_v ? v_src : k_src) + r * kPageHd);
+  uint2* dst = reinterpret_cast<uint2*>((is_v ? v_pages : k_pages) +
+                                        (((int64_t)pg * Hkv + h) * page_tokens + t % page_tokens) *
+                                            kPageHd);
+  dst[lane] = src[lane];
+}
+
 }  // namespace
 }  // namespace q3
+
+extern "C" int q3_kv_pages_write(const void* k_src, const void* v_src, void* k_pages,
+                                 void* v_pages, int B, int Hkv, int S, int head_dim,
+                                 const int32_t* block_table, int64_t table_stride,
+                                 int page_tokens, int num_pages, int64_t start_pos,
+                                 const int32_t* pos_dev, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(k_src && v_src && k_pages && v_pages && block_table,
+             "q3_kv_pages_write: null pointer");
+  Q3_REQUIRE(head_dim == kPageHd, "q3_kv_pages_write: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && Hkv > 0 && S > 0 && table_stride > 0 && page_tokens > 0 && num_pages > 0,
+             "q3_kv_pages_write: bad shape");
+  Q3_REQUIRE(pos_dev || (start_pos >= 0 && start_pos + S <= table_stride * page_tokens),
+             "q3_kv_pages_write: positions %lld..%lld beyond the table width",
+             (long long)start_pos, (long long)(start_pos + S - 1));
+  Q3_REQUIRE(aligned(k_src, 8) && aligned(v_src, 8) && aligned(k_pages, 8) &&
+                 aligned(v_pages, 8) && aligned(block_table, 4),
+             "q3_kv_pages_write: misaligned pointer");
+  const int64_t jobs = 2 * (int64_t)B * Hkv * S;
+  return launch_ex(kv_page_write_kernel, dim3((unsigned)((jobs + 7) / 8)), dim3(256), 0,
+                   (cudaStream_t)stream, 1, (const __nv_bfloat16*)k_src,
+                   (const __nv_bfloat16*)v_src, (__nv_bfloat16*)k_pages,
+                   (__nv_bfloat16*)v_pages, block_table, table_stride, page_tokens, num_pages, B,
+                   Hkv, S, start_pos, pos_dev, device_error_word());
+}
 
 extern "C" int q3_kv_pages_create(int num_pages, int page_tokens, int max_seqs,
                                   int max_pages_per_seq, const int64_t* buckets, int n_buckets,

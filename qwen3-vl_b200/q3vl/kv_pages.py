@@ -84,6 +84,17 @@ class KVPagePool:
                   ctypes.c_void_p(out.data_ptr()))
         return out
 
+    def device_table(self, slots, width: int | None = None, out: torch.Tensor = None,
+                     device=None) -> torch.Tensor:
+        """table() copied to the device (into `out`, whose address a captured
+        decode graph may hold, when given)."""
+        host = self.table(slots, width)
+        if out is None:
+            dev = device if device is not None else (self.k[0].device if self.k else "cuda")
+            return host.to(dev)
+        out.copy_(host)
+        return out
+
     @property
     def free_pages(self) -> int:
         free = ctypes.c_int64()

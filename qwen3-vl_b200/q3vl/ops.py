@@ -325,6 +325,44 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, k
     return o
 
 
+def attn_decode_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
+                      block_table: torch.Tensor, kv_len: int, scale: float = None,
+                      kv_len_dev: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+    """attn_decode over paged K/V: q bf16 [B, Hq, 128]; k_pages / v_pages
+    [num_pages, Hkv, page_tokens, 128]; block_table int32 [B, width] on the
+    device (position t of row b in page block_table[b, t // page_tokens])."""
+    _cuda("attn_decode_paged", q, k_pages, v_pages, block_table, kv_len_dev)
+    _bf16("attn_decode_paged", q, k_pages, v_pages)
+    _contig("attn_decode_paged", q, k_pages, v_pages, block_table)
+    if block_table.dtype != torch.int32:
+        raise TypeError("attn_decode_paged: block_table must be int32")
+    B, Hq, D = q.shape
+    num_pages, Hkv, page_tokens, _ = k_pages.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    o = torch.empty_like(q) if out is None else out
+    ws = decode_workspace(B, Hq, Hkv, q.device)
+    call("q3_attn_decode_paged", _p(q), _p(k_pages), _p(v_pages), _p(o), B, Hq, Hkv, D,
+         int(kv_len), _p(kv_len_dev), _p(block_table), block_table.shape[1], page_tokens,
+         num_pages, float(scale), _p(ws), 0 if ws is None else ws.numel(), _stream())
+    return o
+
+
+def kv_pages_write(k_rows: torch.Tensor, v_rows: torch.Tensor, k_pages: torch.Tensor,
+                   v_pages: torch.Tensor, block_table: torch.Tensor, start_pos: int = 0,
+                   pos_dev: torch.Tensor = None) -> None:
+    """Copy new K/V rows bf16 [B, Hkv, S, 128] into their pages at positions
+    start_pos (or *pos_dev) .. + S - 1 of each sequence."""
+    _cuda("kv_pages_write", k_rows, v_rows, k_pages, v_pages, block_table, pos_dev)
+    _bf16("kv_pages_write", k_rows, v_rows, k_pages, v_pages)
+    _contig("kv_pages_write", k_rows, v_rows, k_pages, v_pages, block_table)
+    B, Hkv, S, D = k_rows.shape
+    num_pages, _, page_tokens, _ = k_pages.shape
+    call("q3_kv_pages_write", _p(k_rows), _p(v_rows), _p(k_pages), _p(v_pages), B, Hkv, S, D,
+         _p(block_table), block_table.shape[1], page_tokens, num_pages, int(start_pos),
+         _p(pos_dev), _stream())
+
+
 def attn_decode_qkv(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, k_cache: torch.Tensor,
                     v_cache: torch.Tensor, *, Hq: int, Hkv: int, kv_len: int,
                     kv_len_dev: torch.Tensor = None, cs_offset: int = 0, scale: float = None,

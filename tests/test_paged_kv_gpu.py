@@ -1,0 +1,61 @@
+"""Paged KV on the GPU: the page write and decode attention through a block
+table reproduce the contiguous cache path bit for bit (same kernel arithmetic,
+only the row addresses differ).  Marked gpu_pending until their first GPU run."""
+import pytest
+import torch
+
+from q3vl import ops
+from q3vl.kv_pages import KVPagePool
+
+pytestmark = [pytest.mark.gpu, pytest.mark.gpu_pending]
+DEV = "cuda:0"
+BF16 = torch.bfloat16
+
+
+def rnd(*shape, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(BF16)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,lens,page", [(3, 32, 8, (700, 64, 1500), 256),
+                                                 (2, 8, 2, (1, 333), 64),
+                                                 (4, 16, 16, (2048, 2048, 100, 1024), 128)])
+def test_paged_decode_matches_contiguous(B, Hq, Hkv, lens, page):
+    pool = KVPagePool(64 if page >= 128 else 96, page, max_seqs=B, buckets=(2048,), layers=1,
+                      kv_heads=Hkv, device=DEV)
+    pool.reserve(B - 1, 10)                                  # interleave the slots' pages
+    for b in range(B):
+        pool.reserve(b, lens[b])
+    L = max(lens)
+    table = pool.device_table(range(B))
+    k = rnd(B, Hkv, L, 128, seed=1).to(DEV)
+    v = rnd(B, Hkv, L, 128, seed=2).to(DEV)
+    # write every position through the page-write kernel, then decode each row
+    ops.kv_pages_write(k, v, pool.k[0], pool.v[0], table, start_pos=0)
+    assert ops.device_error(clear=True) == 0
+    q = rnd(B, Hq, 128, seed=3).to(DEV)
+    for b in range(B):
+        n = lens[b]
+        want = ops.attn_decode(q[b:b + 1].contiguous(), k[b:b + 1].contiguous(),
+                               v[b:b + 1].contiguous(), kv_len=n)
+        got = ops.attn_decode_paged(q[b:b + 1].contiguous(), pool.k[0], pool.v[0],
+                                    table[b:b + 1].contiguous(), kv_len=n)
+        assert torch.equal(got, want), f"row {b} (len {n})"
+    assert ops.device_error(clear=True) == 0
+    pool.close()
+
+
+def test_page_write_at_a_device_position_and_bad_table_entries():
+    pool = KVPagePool(8, 64, max_seqs=2, buckets=(), layers=1, kv_heads=2, device=DEV)
+    pool.reserve(0, 128)
+    table = pool.device_table([0, 1])                     # slot 1 holds no pages (-1)
+    k = rnd(2, 2, 1, 128, seed=4).to(DEV)
+    v = rnd(2, 2, 1, 128, seed=5).to(DEV)
+    pos = torch.tensor([70], dtype=torch.int32, device=DEV)
+    ops.kv_pages_write(k, v, pool.k[0], pool.v[0], table, pos_dev=pos)
+    torch.cuda.synchronize()
+    assert ops.device_error(clear=True) == 0x403          # row 1 skipped, recorded
+    pg = int(table[0, 70 // 64])
+    assert torch.equal(pool.k[0][pg, :, 70 % 64].cpu(), k[0, :, 0].cpu())
+    assert torch.equal(pool.v[0][pg, :, 70 % 64].cpu(), v[0, :, 0].cpu())
+    pool.close()
