@@ -10,6 +10,8 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py layer  --B 8 --L 1152 --bucket 2048
     python qwen3-vl_b200/q3vl/microbench.py step   --B 8 --L 1152 --bucket 2048 --layers 36
     python qwen3-vl_b200/q3vl/microbench.py rope_index --B 8 --S 16384 [--hf]
+    python qwen3-vl_b200/q3vl/microbench.py vision --B 16 --side 448 [--depth 27]
+    python qwen3-vl_b200/q3vl/microbench.py paged  --B 8 --L 1152 --page 256
 
 `step` times q3_decode_step (every layer of a decode step in one persistent
 kernel) as CUDA-graph replays and reports the step's HBM rate (weights + KV).
@@ -17,6 +19,11 @@ kernel) as CUDA-graph replays and reports the step's HBM rate (weights + KV).
 text runs of 16 tokens between 32x32-patch images, merge 2) and, with --hf,
 transformers' Qwen3VLModel.get_rope_index on the host cores for the same
 layout.
+`vision` times the vision tower (random weights of the 8B model's tower:
+1152 hidden, 16 heads, MLP 4304, merger to 4096) on B images of side x side
+pixels (patch 16, merge 2) and reports TFLOP/s over its GEMM and attention
+FLOPs.  `paged` times decode attention through a block table against the
+contiguous cache on the same K/V.
 `layer` times every kernel of one TP1 decode layer of the 8B shape, and the
 whole layer, as CUDA-graph replays cycling over 4 layers' weights (1.5 GB, so
 every launch streams its weights from HBM), with the decode graph's arguments
@@ -57,7 +64,7 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "layer", "step", "rope_index"])
+                                       "layer", "step", "rope_index", "vision", "paged"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
@@ -77,11 +84,18 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-flush", action="store_true", help="keep L2 warm between iterations")
+    ap.add_argument("--side", type=int, default=448, help="vision: image side in pixels")
+    ap.add_argument("--depth", type=int, default=27, help="vision: transformer blocks")
+    ap.add_argument("--page", type=int, default=256, help="paged: tokens per page")
     ap.add_argument("--hf", action="store_true",
                     help="rope_index: also time transformers' get_rope_index on the host")
     a = ap.parse_args(argv)
     if a.kernel == "rope_index":
         return _rope_index(a)
+    if a.kernel == "vision":
+        return _vision(a)
+    if a.kernel == "paged":
+        return _paged(a)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
     if a.kernel == "layer":
@@ -401,6 +415,83 @@ def _rope_index(a):
         same = torch.equal(hp, pos.cpu()) and torch.equal(hd.view(-1), delta.cpu())
         res.update(hf_ms=hf_ms, hf_threads=torch.get_num_threads(), hf_equal=same)
     print(json.dumps(res), flush=True)
+
+
+
+def _vision(a):
+    """The vision tower on B images of side x side pixels (config 5 at B=16, 448)."""
+    from q3vl.vision_tower import VisionTower
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    depth = a.depth
+    H, I, O, M = 1152, 4304, 4096, 1152 * 4
+    c = dict(depth=depth, hidden_size=H, num_heads=16, intermediate_size=I, out_hidden_size=O,
+             num_position_embeddings=2304, spatial_merge_size=2,
+             deepstack_visual_indexes=[i for i in (8, 16, 24) if i < depth])
+    bf = torch.bfloat16
+
+    def mat(o, i):
+        return (torch.randn(o, i, device=dev) * (i ** -0.5)).to(bf)
+
+    def vec(n, base=0.0):
+        return (base + torch.randn(n, device=dev) * 0.02).to(bf)
+
+    w = {"patch_embed.proj.weight": mat(H, 1536).view(H, 3, 2, 16, 16),
+         "patch_embed.proj.bias": vec(H), "pos_embed.weight": mat(2304, H)}
+    for i in range(depth):
+        b = f"blocks.{i}."
+        w.update({b + "norm1.weight": vec(H, 1.0), b + "norm1.bias": vec(H),
+                  b + "norm2.weight": vec(H, 1.0), b + "norm2.bias": vec(H),
+                  b + "attn.qkv.weight": mat(3 * H, H), b + "attn.qkv.bias": vec(3 * H),
+                  b + "attn.proj.weight": mat(H, H), b + "attn.proj.bias": vec(H),
+                  b + "mlp.linear_fc1.weight": mat(I, H), b + "mlp.linear_fc1.bias": vec(I),
+                  b + "mlp.linear_fc2.weight": mat(H, I), b + "mlp.linear_fc2.bias": vec(H)})
+    for j, m in enumerate(["merger."] + [f"deepstack_merger_list.{k}."
+                                         for k in range(len(c["deepstack_visual_indexes"]))]):
+        n = H if j == 0 else M
+        w.update({m + "norm.weight": vec(n, 1.0), m + "norm.bias": vec(n),
+                  m + "linear_fc1.weight": mat(M, M), m + "linear_fc1.bias": vec(M),
+                  m + "linear_fc2.weight": mat(O, M), m + "linear_fc2.bias": vec(O)})
+    tower = VisionTower(w, c, dev)
+    g = a.side // 16
+    grid = torch.tensor([[1, g, g]] * a.B)
+    n = a.B * g * g
+    x = torch.rand(n, 1536, device=dev).to(bf)
+    ms = _time(lambda: tower(x, grid), a.iters, a.warmup, None)
+    per_img = g * g
+    blk = 2 * per_img * H * (3 * H + H + 2 * I) + 4 * per_img * per_img * H
+    flops = a.B * (depth * blk + 2 * per_img * 1536 * H
+                   + (1 + len(c["deepstack_visual_indexes"])) * 2 * (per_img // 4) * M * (M + O))
+    print(json.dumps({"kernel": "vision", "images": a.B, "side": a.side, "patches": n,
+                      "layers": depth, "ms": ms, "tflops": flops / ms / 1e9}), flush=True)
+
+
+def _paged(a):
+    """Decode attention through a block table vs the contiguous cache."""
+    from q3vl.kv_pages import KVPagePool
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    bf = torch.bfloat16
+    B, Hq, Hkv, L, page = a.B, a.Hq, a.Hkv, a.L, a.page
+    width = (L + page - 1) // page
+    pool = KVPagePool(B * width + 8, page, max_seqs=B, buckets=(), max_pages_per_seq=width,
+                      layers=1, kv_heads=Hkv, device=dev)
+    for b in reversed(range(B)):
+        pool.reserve(b, L)
+    table = pool.device_table(range(B))
+    k = torch.randn(B, Hkv, L, 128, device=dev).to(bf)
+    v = torch.randn_like(k)
+    ops.kv_pages_write(k, v, pool.k[0], pool.v[0], table)
+    q = torch.randn(B, Hq, 128, device=dev).to(bf)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    t_c = _time(lambda: ops.attn_decode(q, k, v, kv_len=L, out=out), a.iters, a.warmup, flush)
+    t_p = _time(lambda: ops.attn_decode_paged(q, pool.k[0], pool.v[0], table, kv_len=L, out=out),
+                a.iters, a.warmup, flush)
+    nbytes = 2 * k.numel() * 2
+    print(json.dumps({"kernel": "paged", "B": B, "L": L, "page": page, "contiguous_ms": t_c,
+                      "paged_ms": t_p, "contiguous_gbs": nbytes / t_c / 1e6,
+                      "paged_gbs": nbytes / t_p / 1e6}), flush=True)
 
 
 if __name__ == "__main__":
