@@ -26,6 +26,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from q3vl import layout, ops
+from q3vl.kv_pages import KVPagePool, PagedLayer
 
 KV_BUCKETS = (2048, 4096, 8192)
 
@@ -240,6 +241,7 @@ class Qwen3VLDecoderFused:
         self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
         self._step_plans = {}
         self._ss_step = None
+        self._page_tables = {}
 
     # ------------------------------------------------------------------ cache
     def init_kv_cache(self, batch_size=1):
@@ -315,9 +317,14 @@ class Qwen3VLDecoderFused:
         # RMSNorm runs inside the projection that consumes it
         fast = (decode and (self.tp_size == 1 or peer) and ab.qkv_bias is None and
                 H <= 256 * 64 and self.fuse_norm)
+        # a paged cache (PagedLayer): K/V rows are written through the block
+        # table, and decode attention reads through it
+        paged = isinstance(kv_cache[layer_idx], PagedLayer)
+        if paged and not decode and start_pos != 0:
+            raise NotImplementedError("paged KV: prefill starts at position 0")
         # prefill without a QKV bias: the QKV GEMM's epilogue applies the head
         # norms and RoPE and writes the caches (no qkv tensor)
-        fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv
+        fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv and not paged
         qkv = None
         if pend is not None:
             xn = torch.empty_like(x)
@@ -342,8 +349,18 @@ class Qwen3VLDecoderFused:
             cos, sin = rope
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
         fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
-                      cos.dtype == torch.bfloat16)
-        if fused_attn:
+                      cos.dtype == torch.bfloat16 and not paged)
+        k_new = v_new = None
+        if paged:
+            q, k_new, v_new = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin,
+                                                B=B, S=S, Hq=ab.num_q_heads,
+                                                Hkv=ab.num_kv_heads, start_pos=start_pos,
+                                                pos_dev=pos_dev, cs_use_pos=cs_use_pos,
+                                                cs_offset=cs_offset, cs_stride_b=cs_stride_b,
+                                                want_kv=True, eps=ab.eps)
+            ops.kv_pages_write(k_new, v_new, kc, vc, kv_cache[layer_idx].table,
+                               start_pos=start_pos, pos_dev=pos_dev)
+        elif fused_attn:
             q = None  # computed inside the attention kernel from qkv
         elif fused_qkv:
             q = ops.gemm_qkv_rope(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
@@ -360,7 +377,11 @@ class Qwen3VLDecoderFused:
                                         eps=ab.eps)
         if S == 1:
             bound = kv_bound if kv_bound is not None else start_pos + 1
-            if fused_attn:
+            if paged:
+                attn = ops.attn_decode_paged(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
+                                             kv_cache[layer_idx].table, kv_len=bound,
+                                             kv_len_dev=kv_len_dev, scale=self.scale)
+            elif fused_attn:
                 attn = ops.attn_decode_qkv(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, kc,
                                            vc, Hq=ab.num_q_heads, Hkv=ab.num_kv_heads,
                                            kv_len=bound, kv_len_dev=kv_len_dev,
@@ -372,7 +393,9 @@ class Qwen3VLDecoderFused:
         else:
             attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,
                                device=x.device)
-            ops.attn_prefill(q, kc, vc, start_pos=start_pos, causal=True, scale=self.scale,
+            # a paged prefill starts at 0: the prompt's own K/V are all it reads
+            ops.attn_prefill(q, k_new if paged else kc, v_new if paged else vc,
+                             start_pos=start_pos, causal=True, scale=self.scale,
                              out=attn.transpose(1, 2))
             attn = attn.view(T, ab.q_dim)
         if fast:
@@ -623,7 +646,7 @@ class Qwen3VLDecoderFused:
         kv_len = torch.ones(1, dtype=torch.int32, device=dev)
         ops.decode_workspace(B, self.num_q_heads, self.num_kv_heads, dev)
 
-        use_step = self._step_ok(B)
+        use_step = self._step_ok(B) and not isinstance(kv_cache[0], PagedLayer)
 
         def step():
             """One decode step; the next tokens land in `tok` (read at the start)."""
@@ -647,6 +670,28 @@ class Qwen3VLDecoderFused:
         self._graphs[key] = g
         return g
 
+    def _paged_kv(self, pool: KVPagePool, B, bucket, slots=None):
+        """Per-layer PagedLayer views of `pool` for a batch: every slot grows to
+        cover the bucket, and the block table goes into a device tensor kept per
+        (pool, batch) so that captured decode graphs read its current rows."""
+        if len(pool.k) != self.num_layers:
+            raise ValueError(f"page pool holds {len(pool.k)} layers, the decoder {self.num_layers}")
+        slots = list(range(B)) if slots is None else [int(sl) for sl in slots]
+        if len(slots) != B:
+            raise ValueError(f"{len(slots)} slots for a batch of {B}")
+        if pool.max_pages_per_seq * pool.page_tokens < bucket:
+            raise ValueError(f"page pool covers {pool.max_pages_per_seq * pool.page_tokens} "
+                             f"positions per sequence, the KV bucket is {bucket}")
+        for sl in slots:
+            pool.reserve(sl, bucket)
+        key = (id(pool), B)
+        table = self._page_tables.get(key)
+        if table is None:
+            table = torch.empty(B, pool.max_pages_per_seq, dtype=torch.int32, device=self.device)
+            self._page_tables[key] = table
+        pool.device_table(slots, out=table)
+        return pool.layers(table)
+
     def _kv_for(self, B, bucket):
         key = (B, bucket)
         kv = self._kv_pool.get(key)
@@ -663,13 +708,17 @@ class Qwen3VLDecoderFused:
     def generate_tokens(self, input_ids=None, max_new_tokens=256, eos_token_id=151645,
                         inputs_embeds=None, position_ids=None, deepstack_embeds=None,
                         visual_mask=None, rope_delta=0, eos_check_every=32,
-                        prefill_done=None):
+                        prefill_done=None, kv_pages: KVPagePool = None, slots=None):
         """Batched greedy generation with a device-resident decode loop.
 
         Returns int64 [B, T] (T <= max_new_tokens): generation stops once every row
         has produced EOS; rows that stop early keep producing tokens after their
         EOS, which callers cut (see generate).  `prefill_done` (a CUDA event) is
-        recorded on the current stream between prefill and decode."""
+        recorded on the current stream between prefill and decode.
+
+        With `kv_pages` (a KVPagePool holding this decoder's layers), the KV
+        cache lives in that pool's pages: row b uses slot slots[b] (default b),
+        which is grown to the KV bucket here and left to the caller to release."""
         if inputs_embeds is not None:
             B, P, _ = inputs_embeds.shape
         else:
@@ -679,7 +728,10 @@ class Qwen3VLDecoderFused:
             raise ValueError(f"prompt {P} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.max_seq_len}")
         bucket = self._bucket(need)
-        kv = self._kv_for(B, bucket)
+        if kv_pages is not None:
+            kv = self._paged_kv(kv_pages, B, bucket, slots)
+        else:
+            kv = self._kv_for(B, bucket)
         g = None
         if self.use_graphs and max_new_tokens > 1:
             g = self._capture_decode(B, kv, bucket, rope_delta)

@@ -24,6 +24,17 @@ from . import _lib
 DEFAULT_BUCKETS = (2048, 4096, 8192)
 
 
+class PagedLayer(tuple):
+    """One layer's page pools as a (k_pages, v_pages) pair, plus the batch's
+    device block table [B, width] int32: a drop-in for the (k_cache, v_cache)
+    pair of a contiguous cache wherever the decoder takes one."""
+
+    def __new__(cls, k_pages: torch.Tensor, v_pages: torch.Tensor, table: torch.Tensor):
+        obj = super().__new__(cls, (k_pages, v_pages))
+        obj.table = table
+        return obj
+
+
 def pages_for_bytes(nbytes: int, layers: int, kv_heads: int, page_tokens: int,
                     head_dim: int = 128, elem_bytes: int = 2) -> int:
     """Pages that fit in `nbytes` of device memory (K and V of every layer)."""
@@ -83,6 +94,10 @@ class KVPagePool:
         _lib.call("q3_kv_pages_table", self._h, sl, len(slots), width,
                   ctypes.c_void_p(out.data_ptr()))
         return out
+
+    def layers(self, table: torch.Tensor) -> list:
+        """The per-layer PagedLayer list for a batch whose block table is `table`."""
+        return [PagedLayer(k, v, table) for k, v in zip(self.k, self.v)]
 
     def device_table(self, slots, width: int | None = None, out: torch.Tensor = None,
                      device=None) -> torch.Tensor:

@@ -224,3 +224,32 @@ def test_ranks_issuing_the_same_calls_hold_the_same_tables():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert same
+
+
+def test_decoder_page_tables_for_a_batch():
+    """Qwen3VLDecoderFused._paged_kv: slots grow to the KV bucket, the block
+    table lands in one persistent tensor per (pool, batch), and a pool that
+    does not match the decoder is refused (host logic, CPU tensors)."""
+    from model_fused import Qwen3VLDecoderFused
+    from q3vl.kv_pages import PagedLayer
+    dec = Qwen3VLDecoderFused.__new__(Qwen3VLDecoderFused)
+    dec.num_layers, dec.device, dec._page_tables = 2, torch.device("cpu"), {}
+    pool = KVPagePool(40, 64, max_seqs=4, buckets=(256, 512), layers=2, kv_heads=1,
+                      head_dim=8, device="cpu")
+    pool.reserve(3, 1)
+    layers = dec._paged_kv(pool, 2, 512, slots=[1, 3])
+    assert len(layers) == 2 and all(isinstance(x, PagedLayer) for x in layers)
+    k, v = layers[0]
+    assert k is pool.k[0] and v is pool.v[0]
+    table = layers[0].table
+    assert table.shape == (2, 8) and table.dtype == torch.int32
+    assert pool.slot_pages(1) == 8 and pool.slot_pages(3) == 8
+    assert table[1, :4].tolist() == [0, 1, 2, 3]        # slot 3 kept its first pages
+    again = dec._paged_kv(pool, 2, 256, slots=[1, 3])
+    assert again[0].table is table                      # one tensor per (pool, batch)
+    with pytest.raises(ValueError, match="layers"):
+        dec._paged_kv(KVPagePool(8, 64, max_seqs=1, buckets=(256,), layers=1, kv_heads=1,
+                                 head_dim=8, device="cpu"), 1, 256)
+    with pytest.raises(ValueError, match="bucket"):
+        dec._paged_kv(pool, 1, 1024)
+    pool.close()

@@ -59,3 +59,31 @@ def test_page_write_at_a_device_position_and_bad_table_entries():
     assert torch.equal(pool.k[0][pg, :, 70 % 64].cpu(), k[0, :, 0].cpu())
     assert torch.equal(pool.v[0][pg, :, 70 % 64].cpu(), v[0, :, 0].cpu())
     pool.close()
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_tiny_decoder_generates_the_reference_tokens_through_pages(graphs):
+    """generate_tokens with the KV cache in a page pool (slot 2, whose pages do
+    not start at page 0) reproduces the reference decoder's 32 greedy tokens."""
+    import loader_fused
+    from tests.golden import cases
+    from tests.helpers import load_golden
+    name = "decoder_tiny_tp1"
+    g = load_golden(name)
+    c = cases.DECODER_CASES[name]
+    s = c["spec"]
+    spec = loader_fused.TextSpec(hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads,
+                                 inter=s.inter, vocab=s.vocab, layers=s.layers,
+                                 rope_theta=s.rope_theta, eps=s.eps)
+    w = cases.decoder_weights(name)
+    dec = loader_fused.build_decoder(w["layers"], w["embed"], w["final_norm"], w["lm_head"],
+                                     spec, 0, 1, DEV, c["max_seq"])
+    dec.use_graphs = graphs
+    pool = KVPagePool(24, 64, max_seqs=4, buckets=(256,), layers=s.layers, kv_heads=s.kv_heads,
+                      device=DEV)
+    pool.reserve(0, 10)
+    ids = cases.decoder_prompt(name).to(DEV)
+    toks = dec.generate_tokens(ids, c["new_tokens"], eos_token_id=-1, kv_pages=pool, slots=[2])
+    assert toks[0].tolist() == g["tokens"].tolist()
+    assert ops.device_error(clear=True) == 0
+    pool.close()
