@@ -272,6 +272,17 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
                     int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
                     const int64_t* q_strides, const int64_t* kv_strides, const int64_t* o_strides,
                     q3_stream_t stream);
+/* The same over paged K/V: k_pages, v_pages [num_pages, Hkv, page_tokens, 128];
+ * key position t of sequence b is read from page block_table[b * table_stride
+ * + t / page_tokens] (page_tokens a multiple of 64).  Keys 0..start_pos+S-1
+ * must already be in the pages.  A table entry outside the pool is recorded
+ * in the device error word and page 0 read in its place. */
+Q3_API int q3_attn_prefill_paged(const void* q, const void* k_pages, const void* v_pages, void* out,
+                          int B, int Hq, int Hkv, int S, int head_dim, int64_t start_pos,
+                          int causal, float scale, const int64_t* q_strides,
+                          const int64_t* o_strides, const int32_t* block_table,
+                          int64_t table_stride, int page_tokens, int num_pages,
+                          q3_stream_t stream);
 
 /* ---- a3/a10/a11: bf16 GEMM with fused epilogues ---------------------------
  * Replaces the projections h @ Wqkv (model_fused.py:103), x @ Wo (:141),

@@ -68,7 +68,28 @@ struct PrefillParams {
   int64_t start;
   int causal;
   float scale_log2;  // scale * log2(e)
+  // paged K/V (q3_attn_prefill_paged): k/v are page pools [num_pages, Hkv,
+  // page_tokens, 128]; key position t of row b lives in page
+  // pages[b * pages_stride + t / page_tokens] at offset t % page_tokens
+  const int32_t* pages;
+  int64_t pages_stride;
+  int page_tokens, num_pages;
+  int* err;
 };
+
+// Paged caches: first row of the 64-key tile starting at key position k0 (a
+// multiple of 64; a tile never straddles pages since page_tokens % 64 == 0).
+// A table entry outside the pool is recorded and page 0 read instead.
+__device__ __forceinline__ const __nv_bfloat16* paged_tile(const PrefillParams& p,
+                                                           const __nv_bfloat16* base, int b,
+                                                           int kvh, int64_t k0) {
+  int pg = p.pages[(int64_t)b * p.pages_stride + k0 / p.page_tokens];
+  if (pg < 0 || pg >= p.num_pages) {
+    if (threadIdx.x == 0) report_timeout(p.err, 0x404);
+    pg = 0;
+  }
+  return base + (((int64_t)pg * p.Hkv + kvh) * p.page_tokens + k0 % p.page_tokens) * kPD;
+}
 
 // Copy `rows` rows (global row stride `gstride` elements) of a [rows][128]
 // tile into swizzled smem; rows >= valid are zero-filled.
@@ -82,6 +103,7 @@ __device__ __forceinline__ void load_tile(uint32_t smem, const __nv_bfloat16* g,
   }
 }
 
+template <bool PAGED>
 __global__ void __launch_bounds__(kPThreads, 1) attn_prefill_kernel(PrefillParams p) {
   pdl_wait();
   pdl_launch();
@@ -108,8 +130,13 @@ __global__ void __launch_bounds__(kPThreads, 1) attn_prefill_kernel(PrefillParam
   load_tile(sQ, qg, p.qs_s, kPBM, q_valid);
   {
     const int valid = (int)min64(kPBN, kv_total);
-    load_tile(sK0, kg, p.ks_s, kPBN, valid);
-    load_tile(sV0, vg, p.ks_s, kPBN, valid);
+    if constexpr (PAGED) {
+      load_tile(sK0, paged_tile(p, p.k, b, kvh, 0), kPD, kPBN, valid);
+      load_tile(sV0, paged_tile(p, p.v, b, kvh, 0), kPD, kPBN, valid);
+    } else {
+      load_tile(sK0, kg, p.ks_s, kPBN, valid);
+      load_tile(sV0, vg, p.ks_s, kPBN, valid);
+    }
   }
   cp_async_commit();
 
@@ -129,8 +156,13 @@ __global__ void __launch_bounds__(kPThreads, 1) attn_prefill_kernel(PrefillParam
       const int valid = (int)min64(kPBN, kv_total - k0);
       const uint32_t sKn = sK0 + (st ^ 1) * kPBN * kPD * 2;
       const uint32_t sVn = sV0 + (st ^ 1) * kPBN * kPD * 2;
-      load_tile(sKn, kg + k0 * p.ks_s, p.ks_s, kPBN, valid);
-      load_tile(sVn, vg + k0 * p.ks_s, p.ks_s, kPBN, valid);
+      if constexpr (PAGED) {
+        load_tile(sKn, paged_tile(p, p.k, b, kvh, k0), kPD, kPBN, valid);
+        load_tile(sVn, paged_tile(p, p.v, b, kvh, k0), kPD, kPBN, valid);
+      } else {
+        load_tile(sKn, kg + k0 * p.ks_s, p.ks_s, kPBN, valid);
+        load_tile(sVn, vg + k0 * p.ks_s, p.ks_s, kPBN, valid);
+      }
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -281,7 +313,7 @@ extern "C" int q3_attn_prefill(const void* q, const void* k, const void* v, void
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel,
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
     attr_set[dev] = true;
   }
@@ -298,6 +330,59 @@ extern "C" int q3_attn_prefill(const void* q, const void* k, const void* v, void
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
   dim3 grid((S + kPBM - 1) / kPBM, Hq, B);
-  return launch_ex(attn_prefill_kernel, grid, dim3(kPThreads), kPSmem, (cudaStream_t)stream, 1,
-                   p);
+  return launch_ex(attn_prefill_kernel<false>, grid, dim3(kPThreads), kPSmem,
+                   (cudaStream_t)stream, 1, p);
+}
+
+extern "C" int q3_attn_prefill_paged(const void* q, const void* k_pages, const void* v_pages,
+                                     void* out, int B, int Hq, int Hkv, int S, int head_dim,
+                                     int64_t start_pos, int causal, float scale,
+                                     const int64_t* q_strides, const int64_t* o_strides,
+                                     const int32_t* block_table, int64_t table_stride,
+                                     int page_tokens, int num_pages, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(q && k_pages && v_pages && out && q_strides && o_strides && block_table,
+             "q3_attn_prefill_paged: null pointer");
+  Q3_REQUIRE(head_dim == kPD, "q3_attn_prefill_paged: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && start_pos >= 0,
+             "q3_attn_prefill_paged: bad shape B=%d S=%d Hq=%d Hkv=%d", B, S, Hq, Hkv);
+  Q3_REQUIRE(page_tokens > 0 && page_tokens % kPBN == 0 && num_pages > 0,
+             "q3_attn_prefill_paged: page_tokens=%d must be a positive multiple of %d",
+             page_tokens, kPBN);
+  Q3_REQUIRE(table_stride > 0 && start_pos + S <= table_stride * page_tokens,
+             "q3_attn_prefill_paged: positions up to %lld beyond the table width",
+             (long long)(start_pos + S - 1));
+  for (int i = 0; i < 3; ++i)
+    Q3_REQUIRE(q_strides[i] % 8 == 0 && o_strides[i] % 2 == 0,
+               "q3_attn_prefill_paged: strides must keep 16-byte rows aligned");
+  Q3_REQUIRE(aligned(q, 16) && aligned(k_pages, 16) && aligned(v_pages, 16) && aligned(out, 4) &&
+                 aligned(block_table, 4),
+             "q3_attn_prefill_paged: misaligned pointer");
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem));
+    attr_set[dev] = true;
+  }
+  PrefillParams p{};
+  p.q = (const __nv_bfloat16*)q;
+  p.k = (const __nv_bfloat16*)k_pages;
+  p.v = (const __nv_bfloat16*)v_pages;
+  p.out = (__nv_bfloat16*)out;
+  p.qs_b = q_strides[0]; p.qs_h = q_strides[1]; p.qs_s = q_strides[2];
+  p.os_b = o_strides[0]; p.os_h = o_strides[1]; p.os_s = o_strides[2];
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.S = S;
+  p.start = start_pos;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.pages = block_table;
+  p.pages_stride = table_stride;
+  p.page_tokens = page_tokens;
+  p.num_pages = num_pages;
+  p.err = device_error_word();
+  dim3 grid((S + kPBM - 1) / kPBM, Hq, B);
+  return launch_ex(attn_prefill_kernel<true>, grid, dim3(kPThreads), kPSmem,
+                   (cudaStream_t)stream, 1, p);
 }

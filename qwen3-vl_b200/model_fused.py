@@ -320,8 +320,6 @@ class Qwen3VLDecoderFused:
         # a paged cache (PagedLayer): K/V rows are written through the block
         # table, and decode attention reads through it
         paged = isinstance(kv_cache[layer_idx], PagedLayer)
-        if paged and not decode and start_pos != 0:
-            raise NotImplementedError("paged KV: prefill starts at position 0")
         # prefill without a QKV bias: the QKV GEMM's epilogue applies the head
         # norms and RoPE and writes the caches (no qkv tensor)
         fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv and not paged
@@ -393,10 +391,16 @@ class Qwen3VLDecoderFused:
         else:
             attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,
                                device=x.device)
-            # a paged prefill starts at 0: the prompt's own K/V are all it reads
-            ops.attn_prefill(q, k_new if paged else kc, v_new if paged else vc,
-                             start_pos=start_pos, causal=True, scale=self.scale,
-                             out=attn.transpose(1, 2))
+            if paged and start_pos > 0:
+                # earlier positions live in the pages (written by earlier calls)
+                ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
+                                       start_pos=start_pos, causal=True, scale=self.scale,
+                                       out=attn.transpose(1, 2))
+            else:
+                # from position 0 the prompt's own K/V are all a paged prefill reads
+                ops.attn_prefill(q, k_new if paged else kc, v_new if paged else vc,
+                                 start_pos=start_pos, causal=True, scale=self.scale,
+                                 out=attn.transpose(1, 2))
             attn = attn.view(T, ab.q_dim)
         if fast:
             # o_proj + residual (emits the sums of squares of x2), gate/up with the

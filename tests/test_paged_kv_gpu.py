@@ -87,3 +87,34 @@ def test_tiny_decoder_generates_the_reference_tokens_through_pages(graphs):
     assert toks[0].tolist() == g["tokens"].tolist()
     assert ops.device_error(clear=True) == 0
     pool.close()
+
+
+@pytest.mark.parametrize("split", [8, 24])
+def test_chunked_prefill_through_pages_matches_one_shot(split):
+    """Prefill in two calls on a page pool (the second reads the first call's
+    K/V through the block table) gives the one-shot prefill's last logits."""
+    import loader_fused
+    from tests.golden import cases
+    from tests.helpers import compare
+    name = "decoder_tiny_tp1"
+    c = cases.DECODER_CASES[name]
+    s = c["spec"]
+    spec = loader_fused.TextSpec(hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads,
+                                 inter=s.inter, vocab=s.vocab, layers=s.layers,
+                                 rope_theta=s.rope_theta, eps=s.eps)
+    w = cases.decoder_weights(name)
+    dec = loader_fused.build_decoder(w["layers"], w["embed"], w["final_norm"], w["lm_head"],
+                                     spec, 0, 1, DEV, c["max_seq"])
+    pool = KVPagePool(24, 64, max_seqs=2, buckets=(256,), layers=s.layers, kv_heads=s.kv_heads,
+                      device=DEV)
+    pool.reserve(0, 10)
+    pool.reserve(1, 256)
+    kv = pool.layers(pool.device_table([1]))
+    ids = cases.decoder_prompt(name).to(DEV)
+    dec.forward(ids[:, :split], 0, kv)
+    got = dec.forward(ids[:, split:].contiguous(), split, kv)
+    want = dec.forward(ids, 0, dec.init_kv_cache(1))
+    compare("chunked paged prefill", got.float().cpu(), want.float().cpu(), max_abs=5e-2,
+            rel_scale=True, min_cos=0.999)
+    assert ops.device_error(clear=True) == 0
+    pool.close()
