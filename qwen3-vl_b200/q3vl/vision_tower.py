@@ -41,6 +41,46 @@ def _cfg_get(cfg, name):
     return getattr(cfg, name, _DEFAULTS[name])
 
 
+def shard_images(grid_thw, world: int, rank: int, merge: int = 2):
+    """Contiguous split of the images over `world` ranks, balanced by patch
+    count.  Returns (first image, end image, first patch, end patch, merged
+    token offsets of every rank's share) for `rank`; the offsets list has
+    world + 1 entries (merged tokens = patches / merge^2)."""
+    grid = [tuple(int(v) for v in g) for g in
+            (grid_thw.tolist() if hasattr(grid_thw, "tolist") else grid_thw)]
+    sizes = [t * h * w for t, h, w in grid]
+    total = sum(sizes)
+    bounds, acc, img = [0], 0, 0
+    for r in range(1, world):
+        target = total * r / world
+        while img < len(sizes) and acc + sizes[img] / 2 <= target:
+            acc += sizes[img]
+            img += 1
+        bounds.append(img)
+    bounds.append(len(sizes))
+    patch_off = [0]
+    for s in sizes:
+        patch_off.append(patch_off[-1] + s)
+    mm = merge * merge
+    merged = [patch_off[b] // mm for b in bounds]
+    i0, i1 = bounds[rank], bounds[rank + 1]
+    return i0, i1, patch_off[i0], patch_off[i1], merged
+
+
+def gather_rows(local: torch.Tensor, merged_offsets, group=None) -> torch.Tensor:
+    """All-gather every rank's rows [n_r, width] into [sum n_r, width] in rank
+    order (shares differ in size: rows are padded to the largest share)."""
+    import torch.distributed as dist
+    world = len(merged_offsets) - 1
+    counts = [merged_offsets[r + 1] - merged_offsets[r] for r in range(world)]
+    pad = max(counts)
+    buf = torch.zeros(pad, local.shape[1], dtype=local.dtype, device=local.device)
+    buf[:local.shape[0]] = local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([parts[r][:counts[r]] for r in range(world)])
+
+
 class VisionPlan:
     """Host-built token layout of one forward: image table [n_img, 4] =
     (t, h, w, first token) and query blocks [n_blocks, 3] = (frame first
@@ -150,5 +190,31 @@ class VisionTower:
             if i in self.deepstack:
                 feats.append(self._merge(h, self.ds_mergers[self.deepstack.index(i)], True))
         return self._merge(h, self.merger, False), feats, h
+
+    @torch.no_grad()
+    def forward_sharded(self, pixel_values: torch.Tensor, grid_thw, group=None):
+        """forward() with the images split over the ranks of `group` (data
+        parallel: each rank encodes its share, then the merged outputs are
+        all-gathered).  Every rank returns the full pooler output and
+        deepstack features, as forward() would; the last hidden state is
+        this rank's share only."""
+        import torch.distributed as dist
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if world == 1:
+            return self.forward(pixel_values, grid_thw)
+        rank = dist.get_rank(group)
+        grid = grid_thw.tolist() if hasattr(grid_thw, "tolist") else list(grid_thw)
+        i0, i1, p0, p1, merged = shard_images(grid, world, rank, self.merge)
+        if i1 > i0:
+            pooler, feats, last = self.forward(pixel_values[p0:p1], grid[i0:i1])
+        else:
+            out_w = self.merger["linear_fc2.weight"].shape[0]
+            pooler = torch.empty(0, out_w, dtype=torch.bfloat16, device=self.device)
+            feats = [torch.empty(0, out_w, dtype=torch.bfloat16, device=self.device)
+                     for _ in self.deepstack]
+            last = torch.empty(0, self.hidden, dtype=torch.bfloat16, device=self.device)
+        pooler = gather_rows(pooler, merged, group)
+        feats = [gather_rows(f, merged, group) for f in feats]
+        return pooler, feats, last
 
     __call__ = forward

@@ -21,6 +21,8 @@ The merge rules are the reference's, kept for parity of the returned tensors:
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from q3vl import ops
@@ -39,6 +41,18 @@ def vision_tower_for(hf_model, device) -> VisionTower:
         tower = VisionTower.from_hf(visual, dev)
         visual._q3vl_tower = tower
     return tower
+
+
+def _encode(tower, pixels, grid):
+    """The tower on every rank (replicated, as the reference runs it), or with
+    Q3VL_VISION_DP=1 and a process group of several ranks, data parallel: each
+    rank encodes its share of the images and the outputs are all-gathered
+    (every rank must then call prepare_vision_embeds, as SPMD serving does)."""
+    import torch.distributed as dist
+    if (os.environ.get("Q3VL_VISION_DP", "0") == "1" and dist.is_initialized()
+            and dist.get_world_size() > 1):
+        return tower.forward_sharded(pixels, grid)
+    return tower(pixels, grid)
 
 
 def _embed_table(hf_model):
@@ -67,7 +81,7 @@ def prepare_vision_embeds(hf_model, processor, inputs, device):
 
     if pixel_values is not None and image_grid_thw is not None:
         tower = vision_tower_for(hf_model, device)
-        feats, img_deep, _ = tower(pixel_values, image_grid_thw)
+        feats, img_deep, _ = _encode(tower, pixel_values, image_grid_thw)
         image_mask = ids0 == IMAGE_TOKEN_ID
         n_img = int(image_mask.sum())
         if n_img > 0 and feats.shape[0] >= n_img:
@@ -77,7 +91,7 @@ def prepare_vision_embeds(hf_model, processor, inputs, device):
 
     if pixel_values_videos is not None and video_grid_thw is not None:
         tower = tower or vision_tower_for(hf_model, device)
-        vfeats, vid_deep, _ = tower(pixel_values_videos, video_grid_thw)
+        vfeats, vid_deep, _ = _encode(tower, pixel_values_videos, video_grid_thw)
         video_mask = ids0 == VIDEO_TOKEN_ID
         n_fill = min(int(vfeats.shape[0]), int(video_mask.sum()))
         if n_fill > 0:

@@ -95,3 +95,92 @@ def test_vision_entry_points_reject_bad_arguments_on_the_host():
     assert rc == _lib.Q3_ERR_INVALID
     rc = lib.q3_layernorm(one, one, one, one, 4, 100, 1e-6, None)
     assert rc == _lib.Q3_ERR_INVALID
+
+
+def test_shard_images_balances_patches_and_covers_every_image():
+    from q3vl.vision_tower import shard_images
+    grid = [[1, 28, 28]] * 16
+    shares = [shard_images(grid, 8, r) for r in range(8)]
+    assert [(i0, i1) for i0, i1, *_ in shares] == [(2 * r, 2 * r + 2) for r in range(8)]
+    uneven = [[1, 40, 40], [1, 8, 8], [2, 16, 16], [1, 8, 12], [1, 32, 32]]
+    for world in (2, 3, 7):
+        shares = [shard_images(uneven, world, r) for r in range(world)]
+        assert shares[0][0] == 0 and shares[-1][1] == len(uneven)
+        for a, b in zip(shares, shares[1:]):
+            assert a[1] == b[0] and a[3] == b[2]
+        merged = shares[0][4]
+        assert merged[-1] == sum(t * h * w for t, h, w in uneven) // 4
+
+
+def _sharded_worker(rank, world, port, q):
+    import os
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    repo = os.path.dirname(here)
+    for p in (os.path.join(repo, "qwen3-vl_b200"), repo):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    from q3vl.vision_tower import VisionTower
+
+    class StandIn(VisionTower):
+        """forward() replaced by a function of (image, merged token): the
+        sharding and the gather are what is under test."""
+
+        def forward(self, pixel_values, grid_thw):
+            rows, off = [], 0
+            for t, h, w in (grid_thw.tolist() if hasattr(grid_thw, "tolist") else grid_thw):
+                img = int(pixel_values[off, 0])           # image index stored in its patches
+                n = t * h * w // 4
+                rows.append(torch.stack([torch.full((n,), float(img)),
+                                         torch.arange(n, dtype=torch.float)], dim=1))
+                off += t * h * w
+            pooler = (torch.cat(rows) if rows else torch.empty(0, 2)).to(torch.bfloat16)
+            return pooler, [pooler * 2, pooler * 3], torch.empty(0, 2, dtype=torch.bfloat16)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tower = StandIn.__new__(StandIn)
+        tower.merge, tower.deepstack, tower.hidden = 2, (0, 1), 2
+        tower.device = torch.device("cpu")
+        tower.merger = {"linear_fc2.weight": torch.zeros(2, 2)}
+        results = []
+        for grid in ([[1, 8, 8], [2, 4, 4], [1, 16, 8], [1, 4, 12]], [[1, 8, 8]]):
+            n = sum(t * h * w for t, h, w in grid)
+            pix = torch.zeros(n, 3)
+            off = 0
+            for i, (t, h, w) in enumerate(grid):
+                pix[off:off + t * h * w, 0] = i          # image index in every patch
+                off += t * h * w
+            full = StandIn.forward(tower, pix, grid)
+            got = tower.forward_sharded(pix, torch.tensor(grid))
+            results.append(torch.equal(got[0], full[0]) and
+                           all(torch.equal(a, b) for a, b in zip(got[1], full[1])))
+        if rank == 0:
+            q.put(results)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put(repr(e))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_tower_gathers_every_image_in_order():
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == [True, True]
