@@ -320,6 +320,19 @@ Q3_API int q3_gemm_qkv_rope(const void* A, const void* W, int64_t hidden, const 
                             void* k_cache, void* v_cache, int B, int S, int Hq, int Hkv,
                             int head_dim, int64_t start_pos, int64_t max_seq, float eps,
                             q3_stream_t stream);
+/* The same with k/v written into page pools [num_pages, Hkv, page_tokens, 128]
+ * through block_table (int32 [B, table_stride] on the device; position t of
+ * sequence b in page block_table[b * table_stride + t / page_tokens]).  A
+ * table entry outside the pool is recorded in the device error word and that
+ * row not written. */
+Q3_API int q3_gemm_qkv_rope_paged(const void* A, const void* W, int64_t hidden,
+                                  const void* q_norm_w, const void* k_norm_w, const void* cos,
+                                  const void* sin, int cs_dtype, int cs_use_pos,
+                                  int64_t cs_offset, int64_t cs_stride_b, void* q_out,
+                                  void* k_pages, void* v_pages, int B, int S, int Hq, int Hkv,
+                                  int head_dim, int64_t start_pos, const int32_t* block_table,
+                                  int64_t table_stride, int page_tokens, int num_pages,
+                                  float eps, q3_stream_t stream);
 
 /* Decode projection with the preceding RMSNorm fused in: C = epilogue(
  * rmsnorm(A; norm_w, eps) W^T) for 1 <= M <= 16, where rmsnorm is

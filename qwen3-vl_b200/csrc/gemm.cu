@@ -46,6 +46,8 @@ struct TcCfg {
 // rotate-half RoPE and the KV-cache write (AttentionBlock.forward after the
 // matmul, model_fused.py:107-129, and the cache write, :244-246).
 constexpr int kEpiQkvRope = 16;
+// The same with the K/V rows written into a page pool through a block table.
+constexpr int kEpiQkvRopePaged = 17;
 
 // Bias epilogues of nn.Linear (the vision tower's linears): v = bf16(acc + b)
 // -- one rounding, as a linear with bias computes -- then Q3_EPI_BIAS_GELU_TANH
@@ -87,7 +89,26 @@ struct TcQkv {
   int S, Hq, Hkv;
   int64_t start_pos, max_seq;
   float eps;
+  // kEpiQkvRopePaged: k_cache / v_cache are page pools [num_pages, Hkv,
+  // page_tokens, 128]; position t of sequence b lives in page
+  // pages[b * pages_stride + t / page_tokens] at offset t % page_tokens
+  const int32_t* pages;
+  int64_t pages_stride;
+  int page_tokens, num_pages;
 };
+
+// Element offset of cache row (b, kv head hkv, position pos), or -1 when a
+// paged table entry lies outside the pool (the row is then not written).
+template <int EPI>
+__device__ __forceinline__ int64_t kv_row(const TcQkv& q, int b, int hkv, int64_t pos) {
+  if constexpr (EPI == kEpiQkvRopePaged) {
+    const int pg = q.pages[(int64_t)b * q.pages_stride + pos / q.page_tokens];
+    if (pg < 0 || pg >= q.num_pages) return -1;
+    return (((int64_t)pg * q.Hkv + hkv) * q.page_tokens + pos % q.page_tokens) * 128;
+  } else {
+    return (((int64_t)b * q.Hkv + hkv) * q.max_seq + pos) * 128;
+  }
+}
 
 struct TcParams {
   __nv_bfloat16* C;
@@ -239,7 +260,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const int row = mt * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(sub * 32) << 16);
-      if constexpr (EPI == kEpiQkvRope) {
+      if constexpr (EPI == kEpiQkvRope || EPI == kEpiQkvRopePaged) {
         // The tile's columns are whole heads (BN = 2 x 128; rows of W are
         // [q heads | k heads | v heads] x 128); this thread owns token `row`.
         const TcQkv& q = p.qkv;
@@ -261,9 +282,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               uint32_t r[32];
               tmem_ld_32cols(t_head + c * 32, r);
               tc_wait_ld();
-              if (row < p.M) {
+              int64_t vrow = 0;
+              if constexpr (EPI == kEpiQkvRopePaged) {
+                vrow = row < p.M ? kv_row<EPI>(q, b, hv, pos) : 0;
+                if (vrow < 0 && c == 0) report_timeout(p.err, 0x405);
+              }
+              if (row < p.M && vrow >= 0) {
                 uint4* dst = reinterpret_cast<uint4*>(
-                    q.v_cache + (((int64_t)b * q.Hkv + hv) * q.max_seq + pos) * 128 + c * 32);
+                    EPI == kEpiQkvRopePaged
+                        ? q.v_cache + vrow + c * 32
+                        : q.v_cache + (((int64_t)b * q.Hkv + hv) * q.max_seq + pos) * 128 + c * 32);
 #pragma unroll
                 for (int v = 0; v < 4; ++v) {
                   uint32_t o[4];
@@ -293,9 +321,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const float rr = 1.0f / sqrtf(ss * (1.0f / 128) + q.eps);  // IEEE, as torch.rsqrt on CPU
           const bool is_q = head < q.Hq;
           const __nv_bfloat16* nw = is_q ? q.q_norm : q.k_norm;
-          __nv_bfloat16* dst_row =
-              is_q ? q.q_out + (((int64_t)b * q.Hq + head) * q.S + s) * 128
-                   : q.k_cache + (((int64_t)b * q.Hkv + (head - q.Hq)) * q.max_seq + pos) * 128;
+          __nv_bfloat16* dst_row;
+          if constexpr (EPI == kEpiQkvRopePaged) {
+            const int64_t krow = (is_q || row >= p.M) ? 0 : kv_row<EPI>(q, b, head - q.Hq, pos);
+            if (krow < 0) report_timeout(p.err, 0x405);
+            dst_row = is_q ? q.q_out + (((int64_t)b * q.Hq + head) * q.S + s) * 128
+                           : (krow >= 0 ? q.k_cache + krow : nullptr);
+          } else {
+            dst_row =
+                is_q ? q.q_out + (((int64_t)b * q.Hq + head) * q.S + s) * 128
+                     : q.k_cache + (((int64_t)b * q.Hkv + (head - q.Hq)) * q.max_seq + pos) * 128;
+          }
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             // dims c*32 .. +31 (lo) pair with dims 64 + c*32 .. +31 (hi)
@@ -303,7 +339,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tmem_ld_32cols(t_head + c * 32, lo);
             tmem_ld_32cols(t_head + 64 + c * 32, hi);
             tc_wait_ld();
-            if (row >= p.M) continue;
+            if (row >= p.M || (EPI == kEpiQkvRopePaged && dst_row == nullptr)) continue;
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               const int j = c * 32 + g * 8;  // table column of both halves
@@ -631,4 +667,56 @@ extern "C" int q3_gemm_bias(const void* A, const void* W, const void* bias, void
     default:
       return launch_tc<256, Q3_EPI_BIAS_RESIDUAL>(A, W, C, aux, m, n, k, s, nullptr, bias);
   }
+}
+
+extern "C" int q3_gemm_qkv_rope_paged(const void* A, const void* W, int64_t hidden,
+                                      const void* q_norm_w, const void* k_norm_w, const void* cos,
+                                      const void* sin, int cs_dtype, int cs_use_pos,
+                                      int64_t cs_offset, int64_t cs_stride_b, void* q_out,
+                                      void* k_pages, void* v_pages, int B, int S, int Hq, int Hkv,
+                                      int head_dim, int64_t start_pos, const int32_t* block_table,
+                                      int64_t table_stride, int page_tokens, int num_pages,
+                                      float eps, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && W && q_norm_w && k_norm_w && cos && sin && q_out && k_pages && v_pages &&
+                 block_table,
+             "q3_gemm_qkv_rope_paged: null pointer");
+  Q3_REQUIRE(head_dim == 128, "q3_gemm_qkv_rope_paged: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && (int64_t)B * S > 16 &&
+                 (int64_t)B * S < (1ll << 31),
+             "q3_gemm_qkv_rope_paged: needs B*S > 16 tokens (prefill); B=%d S=%d", B, S);
+  Q3_REQUIRE(hidden > 0 && hidden % 32 == 0 && hidden < (1ll << 31),
+             "q3_gemm_qkv_rope_paged: hidden=%lld must be a multiple of 32", (long long)hidden);
+  Q3_REQUIRE(cs_dtype == Q3_F32 || cs_dtype == Q3_BF16, "q3_gemm_qkv_rope_paged: bad cs_dtype");
+  Q3_REQUIRE(page_tokens > 0 && num_pages > 0 && table_stride > 0 && start_pos >= 0 &&
+                 start_pos + S <= table_stride * page_tokens,
+             "q3_gemm_qkv_rope_paged: positions %lld..%lld beyond the table width",
+             (long long)start_pos, (long long)(start_pos + S - 1));
+  Q3_REQUIRE(aligned(A, 16) && aligned(W, 16) && aligned(q_norm_w, 16) && aligned(k_norm_w, 16) &&
+                 aligned(cos, 16) && aligned(sin, 16) && aligned(q_out, 16) &&
+                 aligned(k_pages, 16) && aligned(v_pages, 16) && aligned(block_table, 4),
+             "q3_gemm_qkv_rope_paged: pointers must be 16-byte aligned");
+  TcQkv q{};
+  q.q_norm = (const __nv_bfloat16*)q_norm_w;
+  q.k_norm = (const __nv_bfloat16*)k_norm_w;
+  q.cos = cos;
+  q.sin = sin;
+  q.cs_f32 = cs_dtype == Q3_F32;
+  q.cs_use_pos = cs_use_pos ? 1 : 0;
+  q.cs_offset = cs_offset;
+  q.cs_stride_b = cs_stride_b;
+  q.q_out = (__nv_bfloat16*)q_out;
+  q.k_cache = (__nv_bfloat16*)k_pages;
+  q.v_cache = (__nv_bfloat16*)v_pages;
+  q.S = S; q.Hq = Hq; q.Hkv = Hkv;
+  q.start_pos = start_pos;
+  q.max_seq = table_stride * page_tokens;
+  q.eps = eps;
+  q.pages = block_table;
+  q.pages_stride = table_stride;
+  q.page_tokens = page_tokens;
+  q.num_pages = num_pages;
+  const int M = B * S, N = (Hq + 2 * Hkv) * 128;
+  return launch_tc<256, kEpiQkvRopePaged>(A, W, nullptr, nullptr, M, N, (int)hidden,
+                                          (cudaStream_t)stream, &q);
 }

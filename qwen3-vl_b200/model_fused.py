@@ -322,7 +322,7 @@ class Qwen3VLDecoderFused:
         paged = isinstance(kv_cache[layer_idx], PagedLayer)
         # prefill without a QKV bias: the QKV GEMM's epilogue applies the head
         # norms and RoPE and writes the caches (no qkv tensor)
-        fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv and not paged
+        fused_qkv = not decode and ab.qkv_bias is None and self.fuse_qkv
         qkv = None
         if pend is not None:
             xn = torch.empty_like(x)
@@ -349,7 +349,15 @@ class Qwen3VLDecoderFused:
         fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
                       cos.dtype == torch.bfloat16 and not paged)
         k_new = v_new = None
-        if paged:
+        if paged and fused_qkv:
+            q = ops.gemm_qkv_rope_paged(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
+                                        ab.k_norm_weight, cos, sin, B=B, S=S,
+                                        Hq=ab.num_q_heads, Hkv=ab.num_kv_heads, k_pages=kc,
+                                        v_pages=vc, block_table=kv_cache[layer_idx].table,
+                                        start_pos=start_pos, cs_use_pos=cs_use_pos,
+                                        cs_offset=cs_offset, cs_stride_b=cs_stride_b,
+                                        eps=ab.eps)
+        elif paged:
             q, k_new, v_new = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin,
                                                 B=B, S=S, Hq=ab.num_q_heads,
                                                 Hkv=ab.num_kv_heads, start_pos=start_pos,
@@ -391,8 +399,9 @@ class Qwen3VLDecoderFused:
         else:
             attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,
                                device=x.device)
-            if paged and start_pos > 0:
-                # earlier positions live in the pages (written by earlier calls)
+            if paged and (start_pos > 0 or k_new is None):
+                # K/V only in the pages: earlier calls' rows, or this call's
+                # rows written by the fused QKV epilogue
                 ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
                                        start_pos=start_pos, causal=True, scale=self.scale,
                                        out=attn.transpose(1, 2))

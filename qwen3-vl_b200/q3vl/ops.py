@@ -498,6 +498,34 @@ def gemm_qkv_rope(h: torch.Tensor, w: torch.Tensor, q_norm_w, k_norm_w, cos, sin
     return q
 
 
+def gemm_qkv_rope_paged(h: torch.Tensor, w: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *,
+                        B: int, S: int, Hq: int, Hkv: int, k_pages: torch.Tensor,
+                        v_pages: torch.Tensor, block_table: torch.Tensor, start_pos: int = 0,
+                        cs_use_pos: bool = True, cs_offset: int = 0, cs_stride_b: int = 0,
+                        eps: float = 1e-6) -> torch.Tensor:
+    """gemm_qkv_rope with k/v written into page pools through block_table."""
+    _cuda("gemm_qkv_rope_paged", h, w, q_norm_w, k_norm_w, cos, sin, k_pages, v_pages,
+          block_table)
+    _bf16("gemm_qkv_rope_paged", h, w, q_norm_w, k_norm_w, k_pages, v_pages)
+    _contig("gemm_qkv_rope_paged", h, w, cos, sin, k_pages, v_pages, block_table)
+    hidden = h.shape[-1]
+    if h.numel() != B * S * hidden or w.shape != ((Hq + 2 * Hkv) * HEAD_DIM, hidden):
+        raise ValueError("gemm_qkv_rope_paged: h must be [B*S, hidden], "
+                         "w [(Hq+2Hkv)*128, hidden]")
+    if block_table.dtype != torch.int32:
+        raise TypeError("gemm_qkv_rope_paged: block_table must be int32")
+    cs_dtype = {torch.bfloat16: Q3_BF16, torch.float32: Q3_F32}.get(cos.dtype)
+    if cs_dtype is None:
+        raise TypeError("gemm_qkv_rope_paged: cos/sin must be bf16 or f32")
+    num_pages, _, page_tokens, _ = k_pages.shape
+    q = torch.empty(B, Hq, S, HEAD_DIM, dtype=torch.bfloat16, device=h.device)
+    call("q3_gemm_qkv_rope_paged", _p(h), _p(w), hidden, _p(q_norm_w), _p(k_norm_w), _p(cos),
+         _p(sin), cs_dtype, 1 if cs_use_pos else 0, int(cs_offset), int(cs_stride_b), _p(q),
+         _p(k_pages), _p(v_pages), B, S, Hq, Hkv, HEAD_DIM, int(start_pos), _p(block_table),
+         block_table.shape[1], page_tokens, num_pages, float(eps), _stream())
+    return q
+
+
 def gemm_norm(a: torch.Tensor, norm_w: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
               epilogue: str = "none", residual: torch.Tensor = None,
               out: torch.Tensor = None) -> torch.Tensor:
