@@ -137,6 +137,19 @@ def run_ours(args):
     peer_ar = world > 1 and os.environ.get("Q3VL_PEER_AR", "1") == "1"
     if peer_ar:
         dec.enable_peer_allreduce()     # decode o_proj/down: in-kernel NVLink all-reduce
+    # Q3VL_BENCH_KV=paged: the KV cache of every generate step lives in a page
+    # pool (256-token pages, one slot per batch row) instead of contiguous
+    # per-batch caches
+    kv_mode = os.environ.get("Q3VL_BENCH_KV", "contiguous")
+    gen_kw = {}
+    if kv_mode == "paged":
+        from q3vl.kv_pages import KVPagePool
+        page = 256
+        pool = KVPagePool(BATCH * (BUCKET // page), page, max_seqs=BATCH, buckets=(BUCKET,),
+                          layers=dec.num_layers, kv_heads=dec.num_kv_heads, device=dev)
+        gen_kw = {"kv_pages": pool}
+    elif kv_mode != "contiguous":
+        raise SystemExit(f"Q3VL_BENCH_KV={kv_mode!r}: expected contiguous or paged")
     g = torch.Generator().manual_seed(1234)
     prompt_host = torch.randint(0, 151936, (BATCH, PROMPT), generator=g).pin_memory()
     prompt = prompt_host.to(dev)
@@ -150,7 +163,7 @@ def run_ours(args):
         # profiling mode (for ncu launch lists): the same generate step with
         # --new-tokens decode tokens, no side measurements
         for _ in range(args.warmup + args.steps):
-            dec.generate_tokens(prompt, args.new_tokens, eos_token_id=None)
+            dec.generate_tokens(prompt, args.new_tokens, eos_token_id=None, **gen_kw)
         torch.cuda.synchronize()
         if rank == 0:
             print(json.dumps({"profile": True, "new_tokens": args.new_tokens,
@@ -162,7 +175,7 @@ def run_ours(args):
 
     # warm-up (includes CUDA-graph capture of the decode step)
     for _ in range(args.warmup):
-        dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
+        dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, **gen_kw)
 
     # launch accounting: one step run eagerly (graphs replay exactly these kernels);
     # q3_attn_decode adds a split-K combine kernel whenever it splits
@@ -174,14 +187,15 @@ def run_ours(args):
 
     def counting_call(name, *a):
         n = 1
-        if name == "q3_attn_decode" and ws_bytes(*a[4:9]) > 0:  # split-K: + combine kernel
+        if name in ("q3_attn_decode", "q3_attn_decode_paged") and ws_bytes(*a[4:9]) > 0:
+            # split-K: + combine kernel
             n = 2
         counts["n"] += n
         return orig_call(name, *a)
 
     ops_mod.call = counting_call
     dec.use_graphs = False
-    dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None)
+    dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, **gen_kw)
     dec.use_graphs = True
     ops_mod.call = orig_call
     launches_per_step = counts["n"]
@@ -193,7 +207,8 @@ def run_ours(args):
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             ev[i][0].record(stream)
-            dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, prefill_done=ev[i][1])
+            dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, prefill_done=ev[i][1],
+                                **gen_kw)
             ev[i][2].record(stream)
         barrier()
     tot = sum(e[0].elapsed_time(e[2]) for e in ev)
@@ -216,7 +231,7 @@ def run_ours(args):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         p = prompt_host.to(dev, non_blocking=True)
-        toks = dec.generate_tokens(p, NEW_TOKENS, eos_token_id=None).cpu()
+        toks = dec.generate_tokens(p, NEW_TOKENS, eos_token_id=None, **gen_kw).cpu()
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms.append(e0.elapsed_time(e1))
@@ -314,7 +329,9 @@ def run_ours(args):
                        "global_batch": BATCH, "seq_len": PROMPT, "new_tokens": NEW_TOKENS,
                        "parallelism": f"tp{world}", "l2": "weights > L2 (126 MB) every step",
                        "tp_allreduce": ("decode: in-kernel NVLink peer push; prefill: NCCL"
-                                        if peer_ar else ("NCCL" if world > 1 else "none"))},
+                                        if peer_ar else ("NCCL" if world > 1 else "none")),
+                       "kv_cache": ("paged (256-token pages)" if kv_mode == "paged"
+                                    else f"contiguous per batch, bucket {BUCKET}")},
             "prefill_tok_s": round(prefill_tps, 1), "decode_tok_s": round(decode_tps, 1),
             "decode_step_ms": round(dec_step_ms, 4),
             "decode_step_hbm": {"bytes": step_bytes, "achieved_gbs": round(step_gbs, 1),
