@@ -721,7 +721,8 @@ class Qwen3VLDecoderFused:
     def generate_tokens(self, input_ids=None, max_new_tokens=256, eos_token_id=151645,
                         inputs_embeds=None, position_ids=None, deepstack_embeds=None,
                         visual_mask=None, rope_delta=0, eos_check_every=32,
-                        prefill_done=None, kv_pages: KVPagePool = None, slots=None):
+                        prefill_done=None, kv_pages: KVPagePool = None, slots=None,
+                        health=None):
         """Batched greedy generation with a device-resident decode loop.
 
         Returns int64 [B, T] (T <= max_new_tokens): generation stops once every row
@@ -731,7 +732,12 @@ class Qwen3VLDecoderFused:
 
         With `kv_pages` (a KVPagePool holding this decoder's layers), the KV
         cache lives in that pool's pages: row b uses slot slots[b] (default b),
-        which is grown to the KV bucket here and left to the caller to release."""
+        which is grown to the KV bucket here and left to the caller to release.
+
+        With `health` (a q3vl.health.RankHealth), every eos_check_every decode
+        steps each rank records its progress and waits (bounded) for its peers
+        before launching more steps, so a dead peer raises RankFailure on the
+        host instead of being met by the kernels' bounded waits."""
         if inputs_embeds is not None:
             B, P, _ = inputs_embeds.shape
         else:
@@ -772,8 +778,12 @@ class Qwen3VLDecoderFused:
                 out[:, i].copy_(g.tok)
                 g.pos.add_(1)
                 g.kv_len.add_(1)
-                if eos_token_id is not None and i % eos_check_every == 0:
-                    if bool((out[:, :i + 1] == eos_token_id).any(dim=1).all()):
+                if i % eos_check_every == 0:
+                    if health is not None:
+                        torch.cuda.current_stream(self.device).synchronize()
+                        health.wait_for_peers(health.tick())
+                    if eos_token_id is not None and \
+                            bool((out[:, :i + 1] == eos_token_id).any(dim=1).all()):
                         done_at = i + 1
                         break
             return out[:, :done_at]

@@ -22,7 +22,16 @@ class RankFailure(RuntimeError):
 class RankHealth:
     def __init__(self, store, rank: int, world: int, prefix: str = "q3vl/health"):
         self.store, self.rank, self.world, self.prefix = store, rank, world, prefix
+        self._step = -1
         self.beat(-1)
+
+    def tick(self) -> int:
+        """Record the next step of a sequence that only grows (across calls of
+        whatever loop uses it) and return its number; every rank ticks the
+        same number of times."""
+        self._step += 1
+        self.beat(self._step)
+        return self._step
 
     def _key(self, r: int, what: str) -> str:
         return f"{self.prefix}/{r}/{what}"

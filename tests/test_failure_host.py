@@ -66,6 +66,25 @@ def _run(scenario):
     return res, time.monotonic() - t0
 
 
+def test_tick_numbers_keep_growing_across_loops():
+    _paths()
+    from q3vl.health import RankHealth
+
+    class Store(dict):
+        def set(self, k, v):
+            self[k] = v.encode()
+
+        def get(self, k):
+            return dict.__getitem__(self, k)
+
+        def check(self, keys):
+            return all(k in self for k in keys)
+
+    h = RankHealth(Store(), 0, 1)
+    assert [h.tick() for _ in range(3)] == [0, 1, 2]
+    assert [h.tick() for _ in range(2)] == [3, 4]      # a second loop continues the count
+
+
 def test_healthy_ranks_pass_every_step():
     res, _ = _run("none")
     assert res == ("ok", None)
