@@ -12,6 +12,7 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py rope_index --B 8 --S 16384 [--hf]
     python qwen3-vl_b200/q3vl/microbench.py vision --B 16 --side 448 [--depth 27]
     python qwen3-vl_b200/q3vl/microbench.py paged  --B 8 --L 1152 --page 256
+    python qwen3-vl_b200/q3vl/microbench.py e2e_vision --B 16 --side 448
 
 `step` times q3_decode_step (every layer of a decode step in one persistent
 kernel) as CUDA-graph replays and reports the step's HBM rate (weights + KV).
@@ -64,7 +65,8 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "layer", "step", "rope_index", "vision", "paged"])
+                                       "layer", "step", "rope_index", "vision", "paged",
+                                       "e2e_vision"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
@@ -96,6 +98,8 @@ def main(argv=None):
         return _vision(a)
     if a.kernel == "paged":
         return _paged(a)
+    if a.kernel == "e2e_vision":
+        return _e2e_vision(a)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
     if a.kernel == "layer":
@@ -418,12 +422,10 @@ def _rope_index(a):
 
 
 
-def _vision(a):
-    """The vision tower on B images of side x side pixels (config 5 at B=16, 448)."""
+def _random_tower(depth, dev):
+    """The 8B model's vision tower shape with random weights (1152 hidden, 16
+    heads, MLP 4304, merger to 4096, deepstack after blocks 8/16/24)."""
     from q3vl.vision_tower import VisionTower
-    dev = torch.device("cuda:0")
-    torch.manual_seed(0)
-    depth = a.depth
     H, I, O, M = 1152, 4304, 4096, 1152 * 4
     c = dict(depth=depth, hidden_size=H, num_heads=16, intermediate_size=I, out_hidden_size=O,
              num_position_embeddings=2304, spatial_merge_size=2,
@@ -452,7 +454,17 @@ def _vision(a):
         w.update({m + "norm.weight": vec(n, 1.0), m + "norm.bias": vec(n),
                   m + "linear_fc1.weight": mat(M, M), m + "linear_fc1.bias": vec(M),
                   m + "linear_fc2.weight": mat(O, M), m + "linear_fc2.bias": vec(O)})
-    tower = VisionTower(w, c, dev)
+    return VisionTower(w, c, dev), c
+
+
+def _vision(a):
+    """The vision tower on B images of side x side pixels (config 5 at B=16, 448)."""
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    depth = a.depth
+    H, I, O, M = 1152, 4304, 4096, 1152 * 4
+    bf = torch.bfloat16
+    tower, c = _random_tower(depth, dev)
     g = a.side // 16
     grid = torch.tensor([[1, g, g]] * a.B)
     n = a.B * g * g
@@ -492,6 +504,55 @@ def _paged(a):
     print(json.dumps({"kernel": "paged", "B": B, "L": L, "page": page, "contiguous_ms": t_c,
                       "paged_ms": t_p, "contiguous_gbs": nbytes / t_c / 1e6,
                       "paged_gbs": nbytes / t_p / 1e6}), flush=True)
+
+
+
+def _e2e_vision(a):
+    """Vision + text end to end at one GPU (the multimodal workload at B=16):
+    B images of side x side pixels through the tower, the merged image tokens
+    in front of a 256-token random text prompt, device position ids, then the
+    36-layer decoder generating 128 tokens with M-RoPE rows and deepstack."""
+    import loader_fused
+    dev = torch.device("cuda:0")
+    torch.manual_seed(0)
+    B, g = a.B, a.side // 16
+    n_img = (g // 2) ** 2
+    text_len, new_tokens = 256, 128
+    S = n_img + text_len
+    tower, _ = _random_tower(a.depth, dev)
+    dec = loader_fused.random_decoder(loader_fused.QWEN3_VL_8B, 0, 1, dev, seed=0, max_seq=2048)
+    grid = torch.tensor([[1, g, g]] * B)
+    x = torch.rand(B * g * g, 1536, device=dev).to(torch.bfloat16)
+    ids = torch.randint(0, 151936, (B, S), device=dev)
+    types = torch.zeros(B, S, dtype=torch.int32, device=dev)
+    types[:, :n_img] = 1
+    mask = types == 1
+
+    def step():
+        pooler, deep, _ = tower(x, grid)
+        emb = dec._embed(ids).view(B, S, -1)
+        emb[mask] = pooler
+        pos, delta = dec.get_rope_index(ids, types, grid)
+        return dec.generate_tokens(None, new_tokens, eos_token_id=None, inputs_embeds=emb,
+                                   position_ids=pos, deepstack_embeds=deep, visual_mask=mask,
+                                   rope_delta=int(delta[0, 0]))
+
+    for _ in range(max(1, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_v0, t_v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_v0.record()
+    tower(x, grid)
+    t_v1.record()
+    e0.record()
+    toks = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    print(json.dumps({"kernel": "e2e_vision", "B": B, "side": a.side, "prompt": S,
+                      "new_tokens": new_tokens, "vision_ms": t_v0.elapsed_time(t_v1),
+                      "step_ms": ms, "gen_tok_s": B * toks.shape[1] / ms * 1e3}), flush=True)
 
 
 if __name__ == "__main__":
