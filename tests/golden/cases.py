@@ -334,3 +334,53 @@ def hf_vision_tiny(dtype=torch.float32):
     with torch.no_grad():
         out = model(x.to(dtype), grid_thw=grid)
     return out.pooler_output, list(out.deepstack_features), out.last_hidden_state
+
+
+# ---- a4 + a12: one text decoder layer with interleaved M-RoPE (transformers) ----
+MROPE_LAYER_SPEC = odec.Spec(hidden=512, q_heads=4, kv_heads=1, inter=1024, vocab=64, layers=1,
+                             max_seq=512)
+MROPE_LAYER_S = 300
+
+
+def mrope_layer_case(seed: int = 17):
+    """Seeded layer weights (HF [out, in] convention, random norms), hidden
+    states [1, 300, 512] and the text / 16x16 image / text position ids."""
+    w = odec.make_weights(MROPE_LAYER_SPEC, seed=seed, std=0.05, random_norms=True)
+    g = torch.Generator().manual_seed(seed + 1)
+    hidden = torch.randn(1, MROPE_LAYER_S, 512, generator=g).to(BF16)
+    pos = oref.config2_position_ids(seq=MROPE_LAYER_S)
+    return w["layers"][0], hidden, pos
+
+
+def hf_mrope_layer(dtype=torch.float32):
+    """transformers 5.5.0 Qwen3VLTextDecoderLayer (eager attention, causal mask)
+    with Qwen3VLTextRotaryEmbedding on mrope_layer_case()'s inputs."""
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import (Qwen3VLTextDecoderLayer,
+                                                                Qwen3VLTextRotaryEmbedding)
+    s = MROPE_LAYER_SPEC
+    cfg = Qwen3VLTextConfig(hidden_size=s.hidden, num_attention_heads=s.q_heads,
+                            num_key_value_heads=s.kv_heads, head_dim=128,
+                            intermediate_size=s.inter, rms_norm_eps=s.eps,
+                            rope_parameters={"rope_type": "default", "rope_theta": 5e6,
+                                             "mrope_section": [24, 20, 20],
+                                             "mrope_interleaved": True})
+    cfg._attn_implementation = "eager"
+    lw, hidden, pos = mrope_layer_case()
+    layer = Qwen3VLTextDecoderLayer(cfg, 0).eval()
+    sd = {"self_attn.q_proj.weight": lw["q"], "self_attn.k_proj.weight": lw["k"],
+          "self_attn.v_proj.weight": lw["v"], "self_attn.o_proj.weight": lw["o"],
+          "self_attn.q_norm.weight": lw["q_norm"], "self_attn.k_norm.weight": lw["k_norm"],
+          "mlp.gate_proj.weight": lw["gate"], "mlp.up_proj.weight": lw["up"],
+          "mlp.down_proj.weight": lw["down"], "input_layernorm.weight": lw["input_norm"],
+          "post_attention_layernorm.weight": lw["post_norm"]}
+    layer.load_state_dict({k: v.float() for k, v in sd.items()}, strict=True)
+    layer = layer.to(dtype)
+    rot = Qwen3VLTextRotaryEmbedding(cfg)
+    x = hidden.to(dtype)
+    cos, sin = rot(x, pos)
+    S = x.shape[1]
+    mask = torch.full((S, S), float("-inf"), dtype=dtype).triu(1)[None, None]
+    with torch.no_grad():
+        out = layer(x, position_embeddings=(cos, sin), attention_mask=mask)
+    return out, cos, sin

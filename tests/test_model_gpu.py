@@ -116,6 +116,21 @@ def test_mrope_prefill_vs_oracle():
     compare("mrope layer", out, want, max_abs=5e-2, rel_scale=True, min_cos=0.999)
 
 
+def test_mrope_layer_vs_transformers_layer():
+    """forward_layer with 3-axis position_ids on a text / 16x16 image / text
+    prompt vs transformers' Qwen3VLTextDecoderLayer (fixture mrope_layer,
+    bf16): max-abs <= 5e-2 of the output scale, cosine >= 0.999."""
+    g = load_golden("mrope_layer")
+    spec = cases.MROPE_LAYER_SPEC
+    w = odec.make_weights(spec, seed=17, std=0.05, random_norms=True)
+    _, hidden, pos = cases.mrope_layer_case()
+    dec = _decoder(w, spec, max_seq=spec.max_seq)
+    out = dec.forward_layer(hidden.to(DEV), 0, dec.init_kv_cache(1), 0, cases.MROPE_LAYER_S,
+                            position_ids=pos.to(DEV)).cpu()
+    compare("mrope layer vs transformers", out, as_tensor(g["bf16"]), max_abs=5e-2,
+            rel_scale=True, min_cos=0.999)
+
+
 def test_generate_with_embeds_deepstack():
     name = "decoder_tiny_tp1"
     c = cases.DECODER_CASES[name]
