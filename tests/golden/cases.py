@@ -384,3 +384,80 @@ def hf_mrope_layer(dtype=torch.float32):
     with torch.no_grad():
         out = layer(x, position_embeddings=(cos, sin), attention_mask=mask)
     return out, cos, sin
+
+
+# ---- a4 + a13 + 8(f)2: multimodal prefill and one decode step (transformers) ----
+MM_PROMPT = dict(text0=6, grid=(1, 12, 12), text1=18)   # 6 + 36 image tokens + 18 = 60
+
+
+def mm_decode_case(seed: int = 23):
+    """Inputs of the multimodal prefill + decode fixture on the tiny TP1
+    decoder's weights: inputs_embeds [1, 60, 512] (text rows from the
+    embedding, image rows random), 3-axis position ids and rope delta (from
+    the oracle's get_rope_index), the visual mask and two deepstack levels."""
+    import numpy as np
+    w = decoder_weights("decoder_tiny_tp1")
+    t0, (gt, gh, gw), t1 = MM_PROMPT["text0"], MM_PROMPT["grid"], MM_PROMPT["text1"]
+    n_img = gt * (gh // 2) * (gw // 2)
+    P = t0 + n_img + t1
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, 1024, (1, P), generator=g)
+    emb = w["embed"][ids].clone()
+    types = np.zeros((1, P), np.int32)
+    types[0, t0:t0 + n_img] = 1
+    mask = torch.from_numpy(types[0] == 1)
+    emb[0, mask] = (torch.randn(n_img, 512, generator=g) * 0.05).to(BF16)
+    deep = [(torch.randn(n_img, 512, generator=g) * 0.05).to(BF16) for _ in range(2)]
+    pos, delta = oref.rope_index(types, None, np.array([[gt, gh, gw]]), None, 2)
+    return w, emb, pos, int(delta[0]), mask, deep
+
+
+def hf_mm_decode():
+    """transformers 5.5.0 Qwen3VLTextModel (eager, bf16) on mm_decode_case():
+    the multimodal prefill with deepstack, then one cached decode step at
+    position P + delta on all three axes.  Greedy tokens use the decoder's
+    lm_head on the returned hidden states."""
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+    spec = DECODER_CASES["decoder_tiny_tp1"]["spec"]
+    w, emb, pos, delta, mask, deep = mm_decode_case()
+    cfg = Qwen3VLTextConfig(hidden_size=spec.hidden, num_attention_heads=spec.q_heads,
+                            num_key_value_heads=spec.kv_heads, head_dim=128,
+                            intermediate_size=spec.inter, num_hidden_layers=spec.layers,
+                            vocab_size=spec.vocab, rms_norm_eps=spec.eps,
+                            rope_parameters={"rope_type": "default", "rope_theta": spec.rope_theta,
+                                             "mrope_section": [24, 20, 20],
+                                             "mrope_interleaved": True})
+    cfg._attn_implementation = "eager"
+    model = Qwen3VLTextModel(cfg).eval()
+    sd = {"embed_tokens.weight": w["embed"], "norm.weight": w["final_norm"]}
+    for i, lw in enumerate(w["layers"]):
+        p = f"layers.{i}."
+        sd.update({p + "self_attn.q_proj.weight": lw["q"], p + "self_attn.k_proj.weight": lw["k"],
+                   p + "self_attn.v_proj.weight": lw["v"], p + "self_attn.o_proj.weight": lw["o"],
+                   p + "self_attn.q_norm.weight": lw["q_norm"],
+                   p + "self_attn.k_norm.weight": lw["k_norm"],
+                   p + "mlp.gate_proj.weight": lw["gate"], p + "mlp.up_proj.weight": lw["up"],
+                   p + "mlp.down_proj.weight": lw["down"],
+                   p + "input_layernorm.weight": lw["input_norm"],
+                   p + "post_attention_layernorm.weight": lw["post_norm"]})
+    model.load_state_dict({k: v.float() for k, v in sd.items()}, strict=True)
+    model = model.to(BF16)
+    # keep the rotary frequencies fp32, as from_pretrained(dtype=bf16) leaves them
+    inv = model.rotary_emb.inv_freq
+    model.rotary_emb.inv_freq = 1.0 / (spec.rope_theta ** (
+        torch.arange(0, 128, 2, dtype=torch.float) / 128))
+    assert inv.shape == model.rotary_emb.inv_freq.shape
+    P = emb.shape[1]
+    with torch.no_grad():
+        out = model(inputs_embeds=emb, position_ids=pos, use_cache=True,
+                    visual_pos_masks=mask[None], deepstack_visual_embeds=deep)
+        h_pre = out.last_hidden_state
+        t0 = int((h_pre[0, -1] @ w["lm_head"].t()).float().argmax())
+        x1 = w["embed"][torch.tensor([[t0]])]
+        p1 = torch.full((3, 1, 1), P + delta, dtype=torch.long)
+        out1 = model(inputs_embeds=x1, position_ids=p1, past_key_values=out.past_key_values,
+                     use_cache=True)
+        h_dec = out1.last_hidden_state
+        t1 = int((h_dec[0, -1] @ w["lm_head"].t()).float().argmax())
+    return h_pre, h_dec, [t0, t1]

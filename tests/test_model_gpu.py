@@ -131,6 +131,25 @@ def test_mrope_layer_vs_transformers_layer():
             rel_scale=True, min_cos=0.999)
 
 
+@pytest.mark.parametrize("graphs", [True, False])
+def test_multimodal_generate_matches_transformers(graphs):
+    """generate_with_embeds on a text / image / text prompt with 3-axis
+    position ids, deepstack features and the rope delta: the two greedy tokens
+    of transformers' Qwen3VLTextModel (prefill, then a cached decode step at
+    P + delta; fixture mm_decode)."""
+    g = load_golden("mm_decode")
+    name = "decoder_tiny_tp1"
+    c = cases.DECODER_CASES[name]
+    w, emb, pos, delta, mask, deep = cases.mm_decode_case()
+    dec = _decoder(w, c["spec"], max_seq=c["max_seq"])
+    dec.use_graphs = graphs
+    toks = dec.generate_with_embeds(emb.to(DEV), max_new_tokens=2, eos_token_id=-1,
+                                    deepstack_embeds=[d.to(DEV) for d in deep],
+                                    visual_mask=mask.to(DEV), position_ids=pos.to(DEV),
+                                    rope_delta=delta)
+    assert toks == g["tokens"].tolist()
+
+
 def test_generate_with_embeds_deepstack():
     name = "decoder_tiny_tp1"
     c = cases.DECODER_CASES[name]
