@@ -1,0 +1,401 @@
+// a6/a7: causal GQA prefill attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM), flash-style with an online softmax in fp32.
+//
+// Semantics are those of q3_attn_prefill (attn_prefill.cu): the S > 1 eager
+// attention of forward_layer (model_fused.py:248-262) and
+// prefill_gqa_flash_attention (kernels/prefill_attention.py:28-149);
+// out = softmax(q k^T * scale + causal) v, query row s at absolute position
+// start_pos + s, head h reading KV head h / (Hq/Hkv).
+//
+// One CTA = one 128-row query block of one head, 256 threads:
+//   warp 0      TMA producer: Q once (two 128x64 SW128 boxes), then K and V
+//               tiles of 64 keys (two 64x64 boxes each) into a 2-deep ring;
+//   warp 1      MMA issuer (one thread): S_j = Q K_j^T (M=128, N=64, K=128)
+//               into TMEM, O_j = P_j V_j (M=128, N=128, K=64) into TMEM; S of
+//               tile j+1 is issued before O of tile j so QK^T overlaps softmax;
+//   warps 2-3   V transposers: V_j [keys, d] -> V_j^T [d, keys] in the 128-byte
+//               swizzled K-major layout the MMA reads (every operand is
+//               K-major: the descriptors are the GEMM's);
+//   warps 4-7   softmax: thread t owns query row t (TMEM lane t); reads S_j,
+//               masks, updates the running max and sum, writes P_j (bf16,
+//               swizzled K-major), then folds O_j into fp32 registers with the
+//               running-max correction; finally O / l to global memory.
+// TMEM: S double-buffered (2 x 64 columns), O_j double-buffered (2 x 128).
+// Every wait is bounded; on a timeout the kernel records the error word, stops
+// issuing, waits (bounded) for its own copies and MMAs, frees TMEM, returns.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace q3 {
+namespace {
+
+constexpr int kFM = 128;      // query rows per CTA
+constexpr int kFN = 64;       // keys per tile
+constexpr int kFD = 128;      // head dim
+constexpr int kFThreads = 256;
+constexpr int kQBytes = kFM * kFD * 2;    // 32 KB (two 16 KB boxes)
+constexpr int kKVBytes = kFN * kFD * 2;   // 16 KB (two 8 KB boxes)
+constexpr int kPBytes = kFM * kFN * 2;    // 16 KB
+constexpr int kVTBytes = kFD * kFN * 2;   // 16 KB
+// smem: Q | K[2] | V[2] | VT[2] | P[2]
+constexpr int kOffK = kQBytes;
+constexpr int kOffV = kOffK + 2 * kKVBytes;
+constexpr int kOffVT = kOffV + 2 * kKVBytes;
+constexpr int kOffP = kOffVT + 2 * kVTBytes;
+constexpr int kOffBar = kOffP + 2 * kPBytes;   // 163840
+constexpr int kFSmem = kOffBar + 256 + 1024;   // + barriers + alignment slack
+constexpr uint32_t kTmemCols = 512;            // S: 0 / 64; O: 128 / 256
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts128v(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                        uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// byte offset of element (row, col) in a 128-byte-swizzled tile whose rows
+// hold 64 bf16 (8 rows x 128 B = one 1024-byte swizzle atom)
+__device__ __forceinline__ uint32_t sw128(int row, int col) {
+  return row * 128 + ((((col >> 3) ^ (row & 7)) & 7) << 4) + (col & 7) * 2;
+}
+
+struct FlashParams {
+  __nv_bfloat16* out;
+  int64_t os_b, os_h, os_s;
+  int Hq, Hkv, S;
+  int64_t q_rows_per_head;   // rows of one (b, h) in the Q map (= S)
+  int64_t kv_rows_per_head;  // rows of one (b, kv head) in the K/V maps (= cache length)
+  int64_t start;
+  int causal;
+  float scale_log2;
+  int* err;
+};
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                           const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, FlashParams p) {
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t s_base = smem_u32(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;    // [2]
+  uint64_t* kv_empty = bar + 3;   // [2] MMA commit (K done) + transposers (V done)
+  uint64_t* s_full = bar + 5;     // [2]
+  uint64_t* s_free = bar + 7;     // [2] 128 softmax threads
+  uint64_t* p_full = bar + 9;     // [2] 128 softmax threads
+  uint64_t* vt_full = bar + 11;   // [2] 64 transposer threads
+  uint64_t* o_full = bar + 13;    // [2]
+  uint64_t* o_free = bar + 15;    // [2] 128 softmax threads
+  uint64_t* mma_done = bar + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int q0 = qb * kFM;
+  const int q_valid = min(kFM, p.S - q0);
+  const int64_t kv_total = p.start + p.S;
+  const int64_t kv_need = p.causal ? min64(p.start + q0 + kFM, kv_total) : kv_total;
+  const int n_kb = (int)((kv_need + kFN - 1) / kFN);
+  const int q_row0 = (int)(((int64_t)b * p.Hq + h) * p.q_rows_per_head + q0);
+  const int kv_row0 = (int)(((int64_t)b * p.Hkv + kvh) * p.kv_rows_per_head);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 2);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&vt_full[i], 64);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      tma_load_2d(smem, &tmQ, q_full, 0, q_row0, kCacheEvictNormal);
+      tma_load_2d(smem + kQBytes / 2, &tmQ, q_full, 64, q_row0, kCacheEvictNormal);
+      int issued = 0;
+      for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, 0x601)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* dk = smem + kOffK + s * kKVBytes;
+        uint8_t* dv = smem + kOffV + s * kKVBytes;
+        const int y = kv_row0 + j * kFN;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
+        tma_load_2d(dk, &tmK, &kv_full[s], 0, y, kCacheEvictNormal);
+        tma_load_2d(dk + kKVBytes / 2, &tmK, &kv_full[s], 64, y, kCacheEvictNormal);
+        tma_load_2d(dv, &tmV, &kv_full[s], 0, y, kCacheEvictNormal);
+        tma_load_2d(dv + kKVBytes / 2, &tmV, &kv_full[s], 64, y, kCacheEvictNormal);
+        issued = j + 1;
+      }
+      // on an abort, let the copies this thread issued land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, 0);
+      for (int j = max(0, issued - 2); j < issued; ++j)
+        mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kFM, kFN);
+      constexpr uint32_t idesc_o = umma_idesc_bf16(kFM, kFD);
+      bool ok = mbar_wait(q_full, 0, p.err, 0x602);
+      tc_fence_after();
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.err, 0x603)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, p.err, 0x604)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + s * kFN;
+#pragma unroll
+        for (int ks = 0; ks < kFD / 16; ++ks) {
+          const uint32_t qa = s_base + (ks >> 2) * (kQBytes / 2);
+          const uint32_t kb = s_base + kOffK + s * kKVBytes + (ks >> 2) * (kKVBytes / 2);
+          tc_mma_bf16(d, umma_desc_k_sw128(qa) + 2 * (ks & 3),
+                      umma_desc_k_sw128(kb) + 2 * (ks & 3), idesc_s, ks != 0);
+        }
+        tc_commit(&s_full[s]);
+        tc_commit(&kv_empty[s]);  // K of this stage consumed
+        return true;
+      };
+      if (ok && n_kb > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kb && !*abort_flag; ++j) {
+        if (j + 1 < n_kb && !issue_s(j + 1)) { ok = false; break; }
+        const int s = j & 1;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.err, 0x605) ||
+            !mbar_wait(&vt_full[s], (j >> 1) & 1, p.err, 0x606) ||
+            (j >= 2 && !mbar_wait(&o_free[s], ((j >> 1) - 1) & 1, p.err, 0x607))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + 2 * kFN + s * kFD;
+        const uint32_t pa = s_base + kOffP + s * kPBytes;
+        const uint32_t vb = s_base + kOffVT + s * kVTBytes;
+#pragma unroll
+        for (int ks = 0; ks < kFN / 16; ++ks)
+          tc_mma_bf16(d, umma_desc_k_sw128(pa) + 2 * ks, umma_desc_k_sw128(vb) + 2 * ks, idesc_o,
+                      ks != 0);
+        tc_commit(&o_full[s]);
+      }
+      if (!ok) *abort_flag = 1;
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, 0);
+    }
+  } else if (warp < 4) {
+    // ----------------------------- V transposers ------------------------------
+    const int t = threadIdx.x - 64;  // 0..63
+    for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.err, 0x608)) { *abort_flag = 1; break; }
+      // VT[s] was last read by the MMA of tile j - 2
+      if (j >= 2 && !mbar_wait(&o_full[s], ((j >> 1) - 1) & 1, p.err, 0x609)) {
+        *abort_flag = 1;
+        break;
+      }
+      const uint32_t v = s_base + kOffV + s * kKVBytes;
+      const uint32_t vt = s_base + kOffVT + s * kVTBytes;
+      // thread t: key pair kp = t & 31 (keys 2kp, 2kp+1), dims d in [ (t>>5)*64, +64 )
+      const int kp = t & 31, dh = t >> 5;
+#pragma unroll 4
+      for (int dd = 0; dd < 64; dd += 2) {
+        const int d = dh * 64 + dd;
+        const int box = d >> 6, dc = d & 63;
+        const uint32_t r0 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp, dc));
+        const uint32_t r1 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp + 1, dc));
+        // (key 2kp, dims d, d+1) and (key 2kp+1, dims d, d+1) -> rows d, d+1 of VT
+        sts32(vt + sw128(d, 2 * kp), __byte_perm(r0, r1, 0x5410));
+        sts32(vt + sw128(d + 1, 2 * kp), __byte_perm(r0, r1, 0x7632));
+      }
+      fence_async_smem();
+      mbar_arrive(&vt_full[s]);
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+      if (t == 0) mbar_arrive(&kv_empty[s]);  // V of this stage consumed
+    }
+  } else {
+    // -------------------------------- softmax ---------------------------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int64_t qpos = p.start + q0 + row;
+    float m = -INFINITY, l = 0.f;
+    float o[kFD];
+#pragma unroll
+    for (int i = 0; i < kFD; ++i) o[i] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kb; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.err, 0x60a)) { ok = false; break; }
+      tc_fence_after();
+      float sc[kFN];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld_32cols(tmem + lane_off + s * kFN + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const int64_t kbase = (int64_t)j * kFN;
+      float mx = m;
+#pragma unroll
+      for (int c = 0; c < kFN; ++c) {
+        const int64_t key = kbase + c;
+        float x = sc[c] * p.scale_log2;
+        if (key >= kv_total || (p.causal && key > qpos)) x = -INFINITY;
+        sc[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      const float base = (mx == -INFINITY) ? 0.f : mx;
+      const float corr = exp2f(m - base);  // m = -inf -> 0
+      float rs = 0.f;
+      const uint32_t prow = s_base + kOffP + s * kPBytes;
+#pragma unroll
+      for (int c = 0; c < kFN; c += 8) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float p0 = exp2f(sc[c + e] - base), p1 = exp2f(sc[c + e + 1] - base);
+          rs += p0 + p1;
+          w4[e / 2] = pack_bf16x2(p0, p1);
+        }
+        sts128v(prow + sw128(row, c), w4[0], w4[1], w4[2], w4[3]);
+      }
+      fence_async_smem();
+      mbar_arrive(&p_full[s]);
+      l = l * corr + rs;
+      m = mx;
+      // fold O_j in, after rescaling the running sum to the new maximum
+      if (!mbar_wait(&o_full[s], (j >> 1) & 1, p.err, 0x60b)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < kFD / 32; ++c) {
+          tmem_ld_32cols(tmem + lane_off + 2 * kFN + s * kFD + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], corr, __uint_as_float(r[i]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_free[s]);
+    }
+    if (!ok) *abort_flag = 1;
+    if (ok && row < q_valid) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + b * p.os_b + h * p.os_h + (int64_t)(q0 + row) * p.os_s;
+#pragma unroll
+      for (int d = 0; d < kFD; d += 8) {
+        uint4 u;
+        u.x = pack_bf16x2(o[d] * inv, o[d + 1] * inv);
+        u.y = pack_bf16x2(o[d + 2] * inv, o[d + 3] * inv);
+        u.z = pack_bf16x2(o[d + 4] * inv, o[d + 5] * inv);
+        u.w = pack_bf16x2(o[d + 6] * inv, o[d + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + d) = u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+}  // namespace q3
+
+extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B,
+                                  int Hq, int Hkv, int S, int head_dim, int64_t start_pos,
+                                  int causal, float scale, int64_t kv_rows_per_head,
+                                  const int64_t* o_strides, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(q && k && v && out && o_strides, "q3_attn_prefill_tc: null pointer");
+  Q3_REQUIRE(head_dim == kFD, "q3_attn_prefill_tc: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && start_pos >= 0,
+             "q3_attn_prefill_tc: bad shape B=%d S=%d Hq=%d Hkv=%d", B, S, Hq, Hkv);
+  Q3_REQUIRE(kv_rows_per_head >= start_pos + S,
+             "q3_attn_prefill_tc: the cache holds %lld rows per head, need %lld",
+             (long long)kv_rows_per_head, (long long)(start_pos + S));
+  Q3_REQUIRE((int64_t)B * Hq * S < (1ll << 31) && (int64_t)B * Hkv * kv_rows_per_head < (1ll << 31),
+             "q3_attn_prefill_tc: tensors too large for 32-bit TMA rows");
+  Q3_REQUIRE(o_strides[2] % 8 == 0 && o_strides[1] % 8 == 0 && o_strides[0] % 8 == 0,
+             "q3_attn_prefill_tc: output rows must stay 16-byte aligned");
+  Q3_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16),
+             "q3_attn_prefill_tc: pointers must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_2d(&tq, q, (int64_t)B * Hq * S, kFD, kFM, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tk, k, (int64_t)B * Hkv * kv_rows_per_head, kFD, kFN, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v, (int64_t)B * Hkv * kv_rows_per_head, kFD, kFN, 64);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem));
+    attr_set[dev] = true;
+  }
+  FlashParams p{};
+  p.out = (__nv_bfloat16*)out;
+  p.os_b = o_strides[0]; p.os_h = o_strides[1]; p.os_s = o_strides[2];
+  p.Hq = Hq; p.Hkv = Hkv; p.S = S;
+  p.q_rows_per_head = S;
+  p.kv_rows_per_head = kv_rows_per_head;
+  p.start = start_pos;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = device_error_word();
+  dim3 grid((S + kFM - 1) / kFM, Hq, B);
+  return launch_ex(attn_prefill_tc_kernel, grid, dim3(kFThreads), kFSmem, (cudaStream_t)stream,
+                   1, tq, tk, tv, p);
+}

@@ -239,6 +239,8 @@ class Qwen3VLDecoderFused:
         # greedy decoding at TP > 1: MAX all-reduce of per-rank argmax keys
         # instead of the all_gather of every rank's logits
         self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
+        # prefill attention on the tcgen05 tensor cores (opt-in until measured)
+        self.prefill_tc = os.environ.get("Q3VL_PREFILL_TC", "0") == "1"
         self._step_plans = {}
         self._ss_step = None
         self._page_tables = {}
@@ -405,6 +407,10 @@ class Qwen3VLDecoderFused:
                 ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
                                        start_pos=start_pos, causal=True, scale=self.scale,
                                        out=attn.transpose(1, 2))
+            elif self.prefill_tc and q.is_contiguous():
+                ops.attn_prefill_tc(q, k_new if paged else kc, v_new if paged else vc,
+                                    start_pos=start_pos, causal=True, scale=self.scale,
+                                    out=attn.transpose(1, 2))
             else:
                 # from position 0 the prompt's own K/V are all a paged prefill reads
                 ops.attn_prefill(q, k_new if paged else kc, v_new if paged else vc,

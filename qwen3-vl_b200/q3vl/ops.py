@@ -423,6 +423,27 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_pos
     return out
 
 
+def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_pos: int = 0,
+                    causal: bool = True, scale: float = None, out: torch.Tensor = None):
+    """attn_prefill on the tcgen05 tensor cores.  q contiguous [B, Hq, S, 128];
+    k/v [B, Hkv, rows, 128] contiguous with rows >= start_pos + S; out any
+    [B, Hq, S, 128] view whose strides are multiples of 8."""
+    _cuda("attn_prefill_tc", q, k, v, out)
+    _bf16("attn_prefill_tc", q, k, v, out)
+    _contig("attn_prefill_tc", q, k, v)
+    B, Hq, S, D = q.shape
+    _, Hkv, rows, _ = k.shape
+    if v.shape != k.shape or rows < start_pos + S:
+        raise ValueError("attn_prefill_tc: k/v must hold start_pos + S positions")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device=q.device)
+    call("q3_attn_prefill_tc", _p(q), _p(k), _p(v), _p(out), B, Hq, Hkv, S, D, int(start_pos),
+         1 if causal else 0, float(scale), rows, _strides_bhs(out, "out"), _stream())
+    return out
+
+
 def attn_prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
                        block_table: torch.Tensor, *, start_pos: int, causal: bool = True,
                        scale: float = None, out: torch.Tensor = None):
