@@ -5,7 +5,7 @@ for ncu captures of a single kernel.
     python qwen3-vl_b200/q3vl/microbench.py gemv   --M 8 --N 24576 --K 4096 --epi swiglu
     python qwen3-vl_b200/q3vl/microbench.py gemm   --M 8192 --N 6144 --K 4096
     python qwen3-vl_b200/q3vl/microbench.py decode --B 8 --Hq 32 --Hkv 8 --L 1152
-    python qwen3-vl_b200/q3vl/microbench.py prefill --B 1 --Hq 32 --Hkv 8 --S 2048
+    python qwen3-vl_b200/q3vl/microbench.py prefill --B 1 --Hq 32 --Hkv 8 --S 2048 [--tc]
     python qwen3-vl_b200/q3vl/microbench.py rmsnorm --rows 8192 --hidden 4096
     python qwen3-vl_b200/q3vl/microbench.py layer  --B 8 --L 1152 --bucket 2048
     python qwen3-vl_b200/q3vl/microbench.py step   --B 8 --L 1152 --bucket 2048 --layers 36
@@ -89,6 +89,7 @@ def main(argv=None):
     ap.add_argument("--side", type=int, default=448, help="vision: image side in pixels")
     ap.add_argument("--depth", type=int, default=27, help="vision: transformer blocks")
     ap.add_argument("--page", type=int, default=256, help="paged: tokens per page")
+    ap.add_argument("--tc", action="store_true", help="prefill: the tcgen05 kernel")
     ap.add_argument("--hf", action="store_true",
                     help="rope_index: also time transformers' get_rope_index on the host")
     a = ap.parse_args(argv)
@@ -148,9 +149,10 @@ def main(argv=None):
         k = torch.randn(a.B, a.Hkv, a.S, 128, device=dev).to(bf)
         v = torch.randn_like(k)
         out = torch.empty_like(q)
-        ms = _time(lambda: ops.attn_prefill(q, k, v, out=out), a.iters, a.warmup, flush)
+        fn = ops.attn_prefill_tc if a.tc else ops.attn_prefill
+        ms = _time(lambda: fn(q, k, v, out=out), a.iters, a.warmup, flush)
         flops = 4.0 * a.B * a.Hq * a.S * a.S * 128 / 2
-        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, S=a.S, ms=ms, tflops=flops / ms / 1e9)
+        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, S=a.S, tc=a.tc, ms=ms, tflops=flops / ms / 1e9)
     else:
         x = torch.randn(a.rows, a.hidden, device=dev).to(bf)
         w = torch.ones(a.hidden, dtype=bf, device=dev)
