@@ -71,6 +71,21 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     rc = lib.q3_attn_decode_qkv(one, one, one, one, one, 0, one, one, one, 1, 6, 4, 128, 8,
                                 None, 16, 0.1, 1e-6, None, 0, None)
     assert rc == _lib.Q3_ERR_INVALID
+    # tcgen05 prefill attention: the cache must hold the prompt's positions
+    strides = (ctypes.c_int64 * 3)(8 * 128 * 100, 128, 8 * 128)
+    rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 128, 50, 1, 0.1, 120, strides,
+                                None)
+    assert rc == _lib.Q3_ERR_INVALID and b"rows per head" in lib.q3_last_error()
+    rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 64, 0, 1, 0.1, 128, strides,
+                                None)
+    assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()
+    # paged attention: positions must stay inside the block table
+    rc = lib.q3_attn_prefill_paged(one, one, one, one, 1, 8, 2, 100, 128, 200, 1, 0.1, strides,
+                                   strides, one, 4, 64, 16, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"table width" in lib.q3_last_error()
+    rc = lib.q3_attn_decode_paged(one, one, one, one, 1, 8, 2, 128, 300, None, one, 4, 64, 16,
+                                  0.1, None, 0, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"table width" in lib.q3_last_error()
     # distributed argmax keys hold 32-bit vocabulary indices
     rc = lib.q3_argmax_key(one, 8, 1 << 16, (1 << 32) - 8, one, None)
     assert rc == _lib.Q3_ERR_INVALID and b"32 bits" in lib.q3_last_error()
