@@ -35,7 +35,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 // the lower index.  A MAX reduction of the ranks' keys is then the argmax of
 // the concatenated vocabulary with torch.argmax's first-index tie rule.
 __device__ __forceinline__ int64_t argmax_key(float v, int64_t gidx) {
-  const uint32_t u = __float_as_uint(v);
+  // -0.0 + 0.0 = +0.0: equal values get equal high words, as torch.argmax sees them
+  const uint32_t u = __float_as_uint(v + 0.0f);
   const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   const int64_t hi = (int64_t)(int32_t)(ord ^ 0x80000000u);
   return (int64_t)((uint64_t)hi << 32) | (int64_t)(0xffffffffu - (uint32_t)gidx);
