@@ -74,6 +74,12 @@ DECODER_CASES = {
         spec=odec.Spec(hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=1024, layers=2,
                        max_seq=256),
         tp=2, seed=12, prompt_len=40, new_tokens=32, max_seq=256),
+    # the TP2 case's weights and prompt at TP1: a greedy sequence that changes
+    # token from step to step, checkable on one GPU
+    "decoder_tiny8_tp1": dict(
+        spec=odec.Spec(hidden=512, q_heads=8, kv_heads=2, inter=1024, vocab=1024, layers=2,
+                       max_seq=256),
+        tp=1, seed=12, prompt_len=40, new_tokens=32, max_seq=256),
 }
 
 
