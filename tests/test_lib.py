@@ -126,3 +126,16 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(2, 4096, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.rmsnorm(x, torch.ones(4096, dtype=torch.bfloat16))
+
+
+def test_header_is_plain_c():
+    """include/*.h is the boundary for foreign bindings: it must compile as C99."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    for h in HEADERS:
+        r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x",
+                            "c", h], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
