@@ -210,6 +210,20 @@ Q3_API int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const void* k
                      int S, int Hq, int Hkv, int head_dim, int64_t start_pos,
                      const int32_t* pos_dev, int64_t max_seq, float eps, q3_stream_t stream);
 
+/* The same with the K/V rows written into page pools [num_pages, Hkv,
+ * page_tokens, 128] through block_table (int32 [B, table_stride] on the
+ * device): row (b, s) at position pos + s lives in page
+ * block_table[b * table_stride + (pos + s) / page_tokens].  q_out may be
+ * NULL.  A position the table does not map into the pool is recorded in the
+ * device error word and that row not written. */
+Q3_API int q3_qkv_norm_rope_paged(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                           const void* cos, const void* sin, int cs_dtype, int cs_use_pos,
+                           int64_t cs_offset, int64_t cs_stride_b, void* q_out, void* k_pages,
+                           void* v_pages, int B, int S, int Hq, int Hkv, int head_dim,
+                           int64_t start_pos, const int32_t* pos_dev, const int32_t* block_table,
+                           int64_t table_stride, int page_tokens, int num_pages, float eps,
+                           q3_stream_t stream);
+
 /* ---- a6/a8: GQA decode attention (one query token) -----------------------
  * Replaces the S=1 case of the eager attention in forward_layer
  * (model_fused.py:248-262) and the unfinished decode_attention_simple

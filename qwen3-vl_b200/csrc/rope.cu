@@ -96,7 +96,28 @@ __device__ __forceinline__ void load4_cs<float>(const float* p, float (&v)[4]) {
   v[0] = rbf(f.x); v[1] = rbf(f.y); v[2] = rbf(f.z); v[3] = rbf(f.w);
 }
 
-template <typename CsT>
+// Page-pool addressing of the K/V rows (q3_qkv_norm_rope_paged).
+struct PageRef {
+  const int32_t* table;  // [B, stride]
+  int64_t stride;
+  int page_tokens, num_pages;
+  int* err;
+};
+
+// Element offset of K/V row (b, kv head, position t) in a page pool, or -1
+// (recorded in the error word) when the table does not map t into the pool.
+__device__ __forceinline__ int64_t page_row(const PageRef& pr, int b, int hkv, int Hkv,
+                                            int64_t t) {
+  const int64_t slot = t / pr.page_tokens;
+  const int pg = (t >= 0 && slot < pr.stride) ? pr.table[(int64_t)b * pr.stride + slot] : -1;
+  if (pg < 0 || pg >= pr.num_pages) {
+    report_timeout(pr.err, 0x406);
+    return -1;
+  }
+  return (((int64_t)pg * Hkv + hkv) * pr.page_tokens + t % pr.page_tokens) * kHeadDim;
+}
+
+template <typename CsT, bool PAGED = false>
 __global__ void qkv_norm_rope_kernel(
     const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
     const __nv_bfloat16* __restrict__ kw, const CsT* __restrict__ cosp,
@@ -104,7 +125,7 @@ __global__ void qkv_norm_rope_kernel(
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,
     __nv_bfloat16* __restrict__ v_out, __nv_bfloat16* __restrict__ k_cache,
     __nv_bfloat16* __restrict__ v_cache, int B, int S, int Hq, int Hkv, int64_t start_pos,
-    const int32_t* __restrict__ pos_dev, int64_t max_seq, float eps) {
+    const int32_t* __restrict__ pos_dev, int64_t max_seq, float eps, PageRef pr) {
   pdl_wait();
   pdl_launch();
   const int lane = threadIdx.x & 31;
@@ -124,8 +145,13 @@ __global__ void qkv_norm_rope_kernel(
   if (h >= Hq + Hkv) {  // value head: straight copy
     const int hv = h - Hq - Hkv;
     if (v_out) store4_bf16(v_out + (((int64_t)b * Hkv + hv) * S + s) * kHeadDim + d0, v);
-    if (v_cache)
-      store4_bf16(v_cache + (((int64_t)b * Hkv + hv) * max_seq + pos + s) * kHeadDim + d0, v);
+    if constexpr (PAGED) {
+      const int64_t off = page_row(pr, b, hv, Hkv, pos + s);
+      if (off >= 0) store4_bf16(v_cache + off + d0, v);
+    } else {
+      if (v_cache)
+        store4_bf16(v_cache + (((int64_t)b * Hkv + hv) * max_seq + pos + s) * kHeadDim + d0, v);
+    }
     return;
   }
   const bool is_q = h < Hq;
@@ -158,8 +184,13 @@ __global__ void qkv_norm_rope_kernel(
   } else {
     const int hk = h - Hq;
     if (k_out) store4_bf16(k_out + (((int64_t)b * Hkv + hk) * S + s) * kHeadDim + d0, o);
-    if (k_cache)
-      store4_bf16(k_cache + (((int64_t)b * Hkv + hk) * max_seq + pos + s) * kHeadDim + d0, o);
+    if constexpr (PAGED) {
+      const int64_t off = page_row(pr, b, hk, Hkv, pos + s);
+      if (off >= 0) store4_bf16(k_cache + off + d0, o);
+    } else {
+      if (k_cache)
+        store4_bf16(k_cache + (((int64_t)b * Hkv + hk) * max_seq + pos + s) * kHeadDim + d0, o);
+    }
   }
 }
 
@@ -227,12 +258,57 @@ extern "C" int q3_qkv_norm_rope(const void* qkv, const void* q_norm_w, const voi
         (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, cs_use_pos, cs_offset, cs_stride_b,
         (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out,
         (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, B, S, Hq, Hkv, start_pos, pos_dev,
-        max_seq, eps);
+        max_seq, eps, PageRef{});
   else
     return launch_ex(qkv_norm_rope_kernel<float>, grid, block, 0, st, 1,
         (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w,
         (const float*)cos, (const float*)sin, cs_use_pos, cs_offset, cs_stride_b,
         (__nv_bfloat16*)q_out,
         (__nv_bfloat16*)k_out, (__nv_bfloat16*)v_out, (__nv_bfloat16*)k_cache,
-        (__nv_bfloat16*)v_cache, B, S, Hq, Hkv, start_pos, pos_dev, max_seq, eps);
+        (__nv_bfloat16*)v_cache, B, S, Hq, Hkv, start_pos, pos_dev, max_seq, eps, PageRef{});
+}
+
+extern "C" int q3_qkv_norm_rope_paged(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                      const void* cos, const void* sin, int cs_dtype,
+                                      int cs_use_pos, int64_t cs_offset, int64_t cs_stride_b,
+                                      void* q_out, void* k_pages, void* v_pages, int B, int S,
+                                      int Hq, int Hkv, int head_dim, int64_t start_pos,
+                                      const int32_t* pos_dev, const int32_t* block_table,
+                                      int64_t table_stride, int page_tokens, int num_pages,
+                                      float eps, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(qkv && q_norm_w && k_norm_w && cos && sin && k_pages && v_pages && block_table,
+             "q3_qkv_norm_rope_paged: null input");
+  Q3_REQUIRE(head_dim == kHeadDim, "q3_qkv_norm_rope_paged: head_dim must be 128 (got %d)",
+             head_dim);
+  Q3_REQUIRE(B >= 0 && S >= 0 && Hq > 0 && Hkv > 0 && table_stride > 0 && page_tokens > 0 &&
+                 num_pages > 0,
+             "q3_qkv_norm_rope_paged: bad shape");
+  Q3_REQUIRE(cs_dtype == Q3_F32 || cs_dtype == Q3_BF16, "q3_qkv_norm_rope_paged: bad cs_dtype");
+  Q3_REQUIRE(pos_dev || start_pos + S <= table_stride * page_tokens,
+             "q3_qkv_norm_rope_paged: positions %lld..%lld beyond the table width",
+             (long long)start_pos, (long long)(start_pos + S - 1));
+  Q3_REQUIRE(aligned(qkv, 8) && (!q_out || aligned(q_out, 8)) && aligned(k_pages, 8) &&
+                 aligned(v_pages, 8) && aligned(block_table, 4) &&
+                 aligned(cos, cs_dtype == Q3_F32 ? 16 : 8) &&
+                 aligned(sin, cs_dtype == Q3_F32 ? 16 : 8),
+             "q3_qkv_norm_rope_paged: misaligned pointer");
+  const int64_t rows = (int64_t)B * S * (Hq + 2 * Hkv);
+  if (rows == 0) return Q3_OK;
+  dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  cudaStream_t st = (cudaStream_t)stream;
+  const PageRef pr{block_table, table_stride, page_tokens, num_pages, device_error_word()};
+  if (cs_dtype == Q3_BF16)
+    return launch_ex(qkv_norm_rope_kernel<__nv_bfloat16, true>, grid, block, 0, st, 1,
+        (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w,
+        (const __nv_bfloat16*)cos, (const __nv_bfloat16*)sin, cs_use_pos, cs_offset, cs_stride_b,
+        (__nv_bfloat16*)q_out, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr,
+        (__nv_bfloat16*)k_pages, (__nv_bfloat16*)v_pages, B, S, Hq, Hkv, start_pos, pos_dev,
+        (int64_t)0, eps, pr);
+  return launch_ex(qkv_norm_rope_kernel<float, true>, grid, block, 0, st, 1,
+      (const __nv_bfloat16*)qkv, (const __nv_bfloat16*)q_norm_w, (const __nv_bfloat16*)k_norm_w,
+      (const float*)cos, (const float*)sin, cs_use_pos, cs_offset, cs_stride_b,
+      (__nv_bfloat16*)q_out, (__nv_bfloat16*)nullptr, (__nv_bfloat16*)nullptr,
+      (__nv_bfloat16*)k_pages, (__nv_bfloat16*)v_pages, B, S, Hq, Hkv, start_pos, pos_dev,
+      (int64_t)0, eps, pr);
 }

@@ -350,7 +350,6 @@ class Qwen3VLDecoderFused:
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
         fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
                       cos.dtype == torch.bfloat16 and not paged)
-        k_new = v_new = None
         if paged and fused_qkv:
             q = ops.gemm_qkv_rope_paged(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
                                         ab.k_norm_weight, cos, sin, B=B, S=S,
@@ -360,14 +359,13 @@ class Qwen3VLDecoderFused:
                                         cs_offset=cs_offset, cs_stride_b=cs_stride_b,
                                         eps=ab.eps)
         elif paged:
-            q, k_new, v_new = ops.qkv_norm_rope(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin,
-                                                B=B, S=S, Hq=ab.num_q_heads,
-                                                Hkv=ab.num_kv_heads, start_pos=start_pos,
-                                                pos_dev=pos_dev, cs_use_pos=cs_use_pos,
-                                                cs_offset=cs_offset, cs_stride_b=cs_stride_b,
-                                                want_kv=True, eps=ab.eps)
-            ops.kv_pages_write(k_new, v_new, kc, vc, kv_cache[layer_idx].table,
-                               start_pos=start_pos, pos_dev=pos_dev)
+            # K/V rows go straight into their pages (no dense copy)
+            q = ops.qkv_norm_rope_paged(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B,
+                                        S=S, Hq=ab.num_q_heads, Hkv=ab.num_kv_heads, k_pages=kc,
+                                        v_pages=vc, block_table=kv_cache[layer_idx].table,
+                                        start_pos=start_pos, pos_dev=pos_dev,
+                                        cs_use_pos=cs_use_pos, cs_offset=cs_offset,
+                                        cs_stride_b=cs_stride_b, eps=ab.eps)
         elif fused_attn:
             q = None  # computed inside the attention kernel from qkv
         elif fused_qkv:
@@ -401,20 +399,17 @@ class Qwen3VLDecoderFused:
         else:
             attn = torch.empty(B, S, ab.num_q_heads, self.head_dim, dtype=torch.bfloat16,
                                device=x.device)
-            if paged and (start_pos > 0 or k_new is None):
-                # K/V only in the pages: earlier calls' rows, or this call's
-                # rows written by the fused QKV epilogue
+            if paged:
+                # this call's K/V rows went into the pages above; earlier
+                # positions are there from earlier calls
                 ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
                                        start_pos=start_pos, causal=True, scale=self.scale,
                                        out=attn.transpose(1, 2))
             elif self.prefill_tc and q.is_contiguous():
-                ops.attn_prefill_tc(q, k_new if paged else kc, v_new if paged else vc,
-                                    start_pos=start_pos, causal=True, scale=self.scale,
-                                    out=attn.transpose(1, 2))
+                ops.attn_prefill_tc(q, kc, vc, start_pos=start_pos, causal=True,
+                                    scale=self.scale, out=attn.transpose(1, 2))
             else:
-                # from position 0 the prompt's own K/V are all a paged prefill reads
-                ops.attn_prefill(q, k_new if paged else kc, v_new if paged else vc,
-                                 start_pos=start_pos, causal=True, scale=self.scale,
+                ops.attn_prefill(q, kc, vc, start_pos=start_pos, causal=True, scale=self.scale,
                                  out=attn.transpose(1, 2))
             attn = attn.view(T, ab.q_dim)
         if fast:

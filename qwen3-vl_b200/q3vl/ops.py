@@ -272,6 +272,33 @@ def qkv_norm_rope(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *, B: int, S:
     return q, k, v
 
 
+def qkv_norm_rope_paged(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *, B: int, S: int,
+                        Hq: int, Hkv: int, k_pages: torch.Tensor, v_pages: torch.Tensor,
+                        block_table: torch.Tensor, start_pos: int = 0,
+                        pos_dev: torch.Tensor = None, cs_use_pos: bool = True,
+                        cs_offset: int = 0, cs_stride_b: int = 0, eps: float = 1e-6):
+    """qkv_norm_rope with the rotated k and v written into page pools through
+    block_table; returns q [B, Hq, S, 128]."""
+    _cuda("qkv_norm_rope_paged", qkv, q_norm_w, k_norm_w, cos, sin, k_pages, v_pages,
+          block_table, pos_dev)
+    _bf16("qkv_norm_rope_paged", qkv, q_norm_w, k_norm_w, k_pages, v_pages)
+    _contig("qkv_norm_rope_paged", qkv, cos, sin, k_pages, v_pages, block_table)
+    if qkv.numel() != B * S * (Hq + 2 * Hkv) * HEAD_DIM:
+        raise ValueError("qkv_norm_rope_paged: qkv size does not match B,S,Hq,Hkv")
+    cs_dtype = {torch.bfloat16: Q3_BF16, torch.float32: Q3_F32}.get(cos.dtype)
+    if cs_dtype is None:
+        raise TypeError("qkv_norm_rope_paged: cos/sin must be bf16 or f32")
+    if block_table.dtype != torch.int32 or (pos_dev is not None and pos_dev.dtype != torch.int32):
+        raise TypeError("qkv_norm_rope_paged: block_table and pos_dev must be int32")
+    num_pages, _, page_tokens, _ = k_pages.shape
+    q = torch.empty(B, Hq, S, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+    call("q3_qkv_norm_rope_paged", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin),
+         cs_dtype, 1 if cs_use_pos else 0, int(cs_offset), int(cs_stride_b), _p(q), _p(k_pages),
+         _p(v_pages), B, S, Hq, Hkv, HEAD_DIM, int(start_pos), _p(pos_dev), _p(block_table),
+         block_table.shape[1], page_tokens, num_pages, float(eps), _stream())
+    return q
+
+
 # ----------------------------------------------------------------------------
 # a6/a8: decode attention
 # ----------------------------------------------------------------------------

@@ -61,14 +61,45 @@ def test_page_write_at_a_device_position_and_bad_table_entries():
     pool.close()
 
 
+def test_norm_rope_writes_the_same_rows_into_pages():
+    """q3_qkv_norm_rope_paged: q and the K/V rows it writes through the table
+    equal q3_qkv_norm_rope's q and contiguous cache rows, bit for bit."""
+    B, S, Hq, Hkv, start = 2, 5, 8, 2, 70
+    qkv = rnd(B * S, (Hq + 2 * Hkv) * 128, seed=6).to(DEV)
+    qn, kn = (1 + 0.1 * rnd(128, seed=7).float()).to(BF16).to(DEV), \
+        (1 + 0.1 * rnd(128, seed=8).float()).to(BF16).to(DEV)
+    t = torch.arange(256, dtype=torch.float32)[:, None] * 0.01
+    cos, sin = t.cos().repeat(1, 64).to(BF16).to(DEV), t.sin().repeat(1, 64).to(BF16).to(DEV)
+    kc = torch.zeros(B, Hkv, 256, 128, dtype=BF16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q_ref, _, _ = ops.qkv_norm_rope(qkv, qn, kn, cos, sin, B=B, S=S, Hq=Hq, Hkv=Hkv,
+                                    start_pos=start, k_cache=kc, v_cache=vc)
+    pool = KVPagePool(16, 64, max_seqs=2, buckets=(256,), layers=1, kv_heads=Hkv, device=DEV)
+    pool.reserve(1, 256)
+    pool.reserve(0, 256)
+    table = pool.device_table([0, 1])
+    q = ops.qkv_norm_rope_paged(qkv, qn, kn, cos, sin, B=B, S=S, Hq=Hq, Hkv=Hkv,
+                                k_pages=pool.k[0], v_pages=pool.v[0], block_table=table,
+                                start_pos=start)
+    assert torch.equal(q, q_ref)
+    tab = table.cpu()
+    for b in range(B):
+        for pos in range(start, start + S):
+            pg = int(tab[b, pos // 64])
+            assert torch.equal(pool.k[0][pg, :, pos % 64], kc[b, :, pos])
+            assert torch.equal(pool.v[0][pg, :, pos % 64], vc[b, :, pos])
+    assert ops.device_error(clear=True) == 0
+    pool.close()
+
+
+@pytest.mark.parametrize("name", ["decoder_tiny_tp1", "decoder_tiny8_tp1"])
 @pytest.mark.parametrize("graphs", [True, False])
-def test_tiny_decoder_generates_the_reference_tokens_through_pages(graphs):
+def test_tiny_decoder_generates_the_reference_tokens_through_pages(graphs, name):
     """generate_tokens with the KV cache in a page pool (slot 2, whose pages do
     not start at page 0) reproduces the reference decoder's 32 greedy tokens."""
     import loader_fused
     from tests.golden import cases
     from tests.helpers import load_golden
-    name = "decoder_tiny_tp1"
     g = load_golden(name)
     c = cases.DECODER_CASES[name]
     s = c["spec"]
