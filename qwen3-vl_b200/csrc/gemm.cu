@@ -116,6 +116,7 @@ struct TcParams {
   const __nv_bfloat16* bias;  // [N], bias epilogues only
   int M, N, K, ldc;
   int m_tiles, n_tiles;
+  int group_m;  // 0: tiles in column order (M fastest); g > 0: grouped raster, g M-tiles per group
   int* err;
   TcQkv qkv;  // kEpiQkvRope only
 };
@@ -149,6 +150,24 @@ __device__ __forceinline__ void unpack8(uint4 u, float (&v)[8]) {
     v[2 * i] = f.x;
     v[2 * i + 1] = f.y;
   }
+}
+
+// Output tile of linear tile index `tile`.  group_m == 0: column order (M
+// fastest).  group_m = g: tiles run over g M-tiles x every N-tile per group,
+// so one wave of CTAs shares fewer A rows and B columns in L2.  Both orders
+// are bijections of [0, m_tiles * n_tiles).
+__device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& mt, int& nt) {
+  if (p.group_m <= 0) {
+    mt = tile % p.m_tiles;
+    nt = tile / p.m_tiles;
+    return;
+  }
+  const int per_group = p.group_m * p.n_tiles;
+  const int first_m = (tile / per_group) * p.group_m;
+  const int gm = min(p.m_tiles - first_m, p.group_m);
+  const int in = tile % per_group;
+  mt = first_m + in % gm;
+  nt = in / gm;
 }
 
 template <int BN, int EPI>
@@ -202,7 +221,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+        int mt, nt;
+        tile_coords(p, tile, mt, nt);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.err, 0x101)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * Cfg::kStageBytes;
@@ -253,7 +273,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int row_in_tile = sub * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int mt = tile % p.m_tiles, nt = tile / p.m_tiles;
+      int mt, nt;
+      tile_coords(p, tile, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, 0x104)) { *abort_flag = 1; break; }
@@ -486,6 +507,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side: launch
 // ---------------------------------------------------------------------------
+// Tile raster of the tcgen05 GEMM: Q3VL_GEMM_GROUP_M=g (g > 0) selects the
+// grouped order; unset or 0 keeps the column order.
+static int gemm_group_m() {
+  static const int g = [] {
+    const char* e = getenv("Q3VL_GEMM_GROUP_M");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 0;
+  }();
+  return g;
+}
+
 template <int BN, int EPI>
 static int launch_tc(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
                      cudaStream_t s, const TcQkv* qkv = nullptr, const void* bias = nullptr) {
@@ -511,6 +543,7 @@ static int launch_tc(const void* A, const void* W, void* C, const void* R, int M
   p.ldc = EPI == Q3_EPI_SWIGLU ? N / 2 : N;
   p.m_tiles = (M + kBM - 1) / kBM;
   p.n_tiles = (N + BN - 1) / BN;
+  p.group_m = gemm_group_m();
   p.err = device_error_word();
   p.qkv = qkv ? *qkv : TcQkv{};
   const int tiles = p.m_tiles * p.n_tiles;
