@@ -195,6 +195,16 @@ class DecoderLayer:
         self.mlp_block = mlp_block
 
 
+class RowRope:
+    """RoPE rows for decode when the rope delta differs per sequence (batched
+    multimodal prompts): cos/sin bf16 [B * rows, 64] with row b * rows + t
+    holding position t + delta_b, built with RotaryEmbedding's own ops so a
+    position's row equals the shared table's."""
+
+    def __init__(self, cos, sin, rows):
+        self.cos, self.sin, self.rows = cos, sin, rows
+
+
 class _DecodeGraph:
     """One captured decode step for a fixed batch, KV bucket and cache storage."""
 
@@ -244,6 +254,7 @@ class Qwen3VLDecoderFused:
         self._step_plans = {}
         self._ss_step = None
         self._page_tables = {}
+        self._row_ropes = {}
 
     # ------------------------------------------------------------------ cache
     def init_kv_cache(self, batch_size=1):
@@ -342,14 +353,18 @@ class Qwen3VLDecoderFused:
             if not fused_qkv:
                 qkv = ab.qkv(h)
         kc, vc = kv_cache[layer_idx]
-        if rope is None:
+        if rope is None and isinstance(rope_delta, RowRope):
+            cos, sin = rope_delta.cos, rope_delta.sin
+            cs_use_pos, cs_stride_b, cs_offset = True, rope_delta.rows, 0
+        elif rope is None:
             cos, sin, _ = self.rotary.tables(self.device)
             cs_use_pos, cs_stride_b, cs_offset = True, 0, rope_delta
         else:
             cos, sin = rope
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
         fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
-                      cos.dtype == torch.bfloat16 and not paged)
+                      cos.dtype == torch.bfloat16 and not paged and
+                      not isinstance(rope_delta, RowRope))
         if paged and fused_qkv:
             q = ops.gemm_qkv_rope_paged(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
                                         ab.k_norm_weight, cos, sin, B=B, S=S,
@@ -650,7 +665,9 @@ class Qwen3VLDecoderFused:
     def _capture_decode(self, B, kv_cache, bucket, rope_delta=0):
         """Capture one decode step.  Must run before the prefill that fills this
         cache: the warm-up step writes KV slot 0, which the prefill overwrites."""
-        key = (B, bucket, kv_cache[0][0].data_ptr(), rope_delta)
+        key = (B, bucket, kv_cache[0][0].data_ptr(),
+               ("rows", rope_delta.cos.data_ptr()) if isinstance(rope_delta, RowRope)
+               else rope_delta)
         g = self._graphs.get(key)
         if g is not None:
             return g
@@ -660,7 +677,8 @@ class Qwen3VLDecoderFused:
         kv_len = torch.ones(1, dtype=torch.int32, device=dev)
         ops.decode_workspace(B, self.num_q_heads, self.num_kv_heads, dev)
 
-        use_step = self._step_ok(B) and not isinstance(kv_cache[0], PagedLayer)
+        use_step = (self._step_ok(B) and not isinstance(kv_cache[0], PagedLayer) and
+                    not isinstance(rope_delta, RowRope))
 
         def step():
             """One decode step; the next tokens land in `tok` (read at the start)."""
@@ -683,6 +701,32 @@ class Qwen3VLDecoderFused:
         g = _DecodeGraph(graph, tok, pos, kv_len)
         self._graphs[key] = g
         return g
+
+    def _decode_rope(self, rope_delta, B, bucket):
+        """An int delta as is; per-sequence deltas (a tensor or list of B, as
+        get_rope_index returns them) as one int when they agree, else as
+        RowRope tables kept per (batch, bucket) so captured graphs read the
+        current rows."""
+        if isinstance(rope_delta, (int, RowRope)):
+            return rope_delta
+        d = [int(v) for v in torch.as_tensor(rope_delta).reshape(-1).tolist()]
+        if len(d) != B:
+            raise ValueError(f"{len(d)} rope deltas for a batch of {B}")
+        if all(v == d[0] for v in d):
+            return d[0]
+        inv = self.rotary.inv_freq
+        t = (torch.arange(bucket)[None, :] + torch.tensor(d)[:, None]).reshape(-1).float()
+        freqs = torch.outer(t, inv)
+        cos, sin = freqs.cos().to(torch.bfloat16), freqs.sin().to(torch.bfloat16)
+        key = (B, bucket)
+        rr = self._row_ropes.get(key)
+        if rr is None:
+            rr = RowRope(torch.empty_like(cos, device=self.device),
+                         torch.empty_like(sin, device=self.device), bucket)
+            self._row_ropes[key] = rr
+        rr.cos.copy_(cos)
+        rr.sin.copy_(sin)
+        return rr
 
     def _paged_kv(self, pool: KVPagePool, B, bucket, slots=None):
         """Per-layer PagedLayer views of `pool` for a batch: every slot grows to
@@ -748,6 +792,7 @@ class Qwen3VLDecoderFused:
             raise ValueError(f"prompt {P} + {max_new_tokens} new tokens exceeds max_seq_len "
                              f"{self.max_seq_len}")
         bucket = self._bucket(need)
+        rope_delta = self._decode_rope(rope_delta, B, bucket)
         if kv_pages is not None:
             kv = self._paged_kv(kv_pages, B, bucket, slots)
         else:
@@ -822,7 +867,9 @@ class Qwen3VLDecoderFused:
     def generate_with_embeds(self, inputs_embeds, max_new_tokens=256, eos_token_id=151645,
                              deepstack_embeds=None, visual_mask=None, position_ids=None,
                              rope_delta=0):
-        """model_fused.py:330-362 (+ optional 3-axis M-RoPE position_ids)."""
+        """model_fused.py:330-362 (+ optional 3-axis M-RoPE position_ids, and a
+        rope delta that is one int or one per sequence, as get_rope_index
+        returns them)."""
         toks = self.generate_tokens(None, max_new_tokens, eos_token_id,
                                     inputs_embeds=inputs_embeds, position_ids=position_ids,
                                     deepstack_embeds=deepstack_embeds, visual_mask=visual_mask,

@@ -253,3 +253,26 @@ def test_decoder_page_tables_for_a_batch():
     with pytest.raises(ValueError, match="bucket"):
         dec._paged_kv(pool, 1, 1024)
     pool.close()
+
+
+
+def test_per_sequence_rope_delta_rows_equal_the_shared_table():
+    """Qwen3VLDecoderFused._decode_rope: equal deltas collapse to one int;
+    different deltas give RowRope tables whose row b * rows + t is the shared
+    RotaryEmbedding row t + delta_b, bit for bit (CPU)."""
+    from model_fused import Qwen3VLDecoderFused, RotaryEmbedding, RowRope
+    dec = Qwen3VLDecoderFused.__new__(Qwen3VLDecoderFused)
+    dec.device, dec._row_ropes = torch.device("cpu"), {}
+    dec.rotary = RotaryEmbedding(128, max_seq_len=4096, base=5e6)
+    assert dec._decode_rope(7, 2, 256) == 7
+    assert dec._decode_rope(torch.tensor([[-3], [-3]]), 2, 256) == -3
+    rr = dec._decode_rope(torch.tensor([[-30], [-24]]), 2, 256)
+    assert isinstance(rr, RowRope) and rr.rows == 256
+    for b, d in enumerate((-30, -24)):
+        for t in (30, 100, 255):
+            assert torch.equal(rr.cos[b * 256 + t], dec.rotary.cos_cached[t + d])
+            assert torch.equal(rr.sin[b * 256 + t], dec.rotary.sin_cached[t + d])
+    again = dec._decode_rope([-1, -2], 2, 256)
+    assert again is rr and torch.equal(rr.cos[5], dec.rotary.cos_cached[4])   # same buffer
+    with pytest.raises(ValueError, match="rope deltas"):
+        dec._decode_rope([1, 2, 3], 2, 256)

@@ -151,6 +151,41 @@ def test_multimodal_generate_matches_transformers(graphs):
     assert toks == g["tokens"].tolist()
 
 
+@pytest.mark.parametrize("graphs", [True, False])
+def test_batched_multimodal_generate_with_per_sequence_deltas(graphs):
+    """Two image prompts of one length but different layouts (rope deltas -30
+    and -24) generated as one batch give each prompt's own tokens."""
+    import numpy as np
+    name = "decoder_tiny8_tp1"
+    c = cases.DECODER_CASES[name]
+    w = cases.decoder_weights(name)
+    dec = _decoder(w, c["spec"], max_seq=c["max_seq"])
+    dec.use_graphs = graphs
+    g = torch.Generator().manual_seed(3)
+
+    def prompt(t0, grid, t1):
+        n_img = grid[0] * (grid[1] // 2) * (grid[2] // 2)
+        P = t0 + n_img + t1
+        ids = torch.randint(0, 1024, (1, P), generator=g)
+        emb = w["embed"][ids].clone()
+        types = np.zeros((1, P), np.int32)
+        types[0, t0:t0 + n_img] = 1
+        emb[0, torch.from_numpy(types[0] == 1)] = (torch.randn(n_img, 512, generator=g) *
+                                                   0.05).to(torch.bfloat16)
+        pos, delta = oref.rope_index(types, None, np.array([list(grid)]), None, 2)
+        return emb, pos, int(delta[0])
+
+    rows = [prompt(6, (1, 12, 12), 18), prompt(10, (1, 8, 16), 18)]
+    assert [d for _, _, d in rows] == [-30, -24]
+    alone = [dec.generate_with_embeds(e.to(DEV), max_new_tokens=6, eos_token_id=-1,
+                                      position_ids=p.to(DEV), rope_delta=d) for e, p, d in rows]
+    batch = dec.generate_with_embeds(torch.cat([r[0] for r in rows]).to(DEV), max_new_tokens=6,
+                                     eos_token_id=-1,
+                                     position_ids=torch.cat([r[1] for r in rows], 1).to(DEV),
+                                     rope_delta=torch.tensor([[-30], [-24]]))
+    assert batch == alone
+
+
 def test_generate_with_embeds_deepstack():
     name = "decoder_tiny_tp1"
     c = cases.DECODER_CASES[name]
