@@ -15,7 +15,8 @@
 //               tile j+1 is issued before O of tile j so QK^T overlaps softmax;
 //   warps 2-3   V transposers: V_j [keys, d] -> V_j^T [d, keys] in the 128-byte
 //               swizzled K-major layout the MMA reads (every operand is
-//               K-major: the descriptors are the GEMM's);
+//               K-major: the descriptors are the GEMM's); rows of keys past
+//               the cache end are written as zeros;
 //   warps 4-7   softmax: thread t owns query row t (TMEM lane t); reads S_j,
 //               masks, updates the running max and sum, writes P_j (bf16,
 //               swizzled K-major), then folds O_j into fp32 registers with the
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bar + 0;
   uint64_t* kv_full = bar + 1;    // [2]
-  uint64_t* kv_empty = bar + 3;   // [2] MMA commit (K done) + transposers (V done)
+  uint64_t* kv_empty = bar + 3;   // [2] MMA commit (K done) + one per transposer warp (V done)
   uint64_t* s_full = bar + 5;     // [2]
   uint64_t* s_free = bar + 7;     // [2] 128 softmax threads
   uint64_t* p_full = bar + 9;     // [2] 128 softmax threads
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 2);
+      mbar_init(&kv_empty[i], 3);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
@@ -236,22 +237,31 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
       const uint32_t v = s_base + kOffV + s * kKVBytes;
       const uint32_t vt = s_base + kOffVT + s * kVTBytes;
-      // thread t: key pair kp = t & 31 (keys 2kp, 2kp+1), dims d in [ (t>>5)*64, +64 )
+      // thread t: key pair kp = t & 31 (keys 2kp, 2kp+1), dims d in [ (t>>5)*64, +64 ).
+      // Keys at or past the end of the cache get zero rows: their P is 0, and
+      // whatever bytes the copy brought (the next head's rows, stale cache)
+      // must not turn 0 * V into NaN.
       const int kp = t & 31, dh = t >> 5;
+      const int64_t key0 = (int64_t)j * kFN + 2 * kp;
+      const uint32_t keep0 = key0 < kv_total ? 0xffffffffu : 0u;
+      const uint32_t keep1 = key0 + 1 < kv_total ? 0xffffffffu : 0u;
 #pragma unroll 4
       for (int dd = 0; dd < 64; dd += 2) {
         const int d = dh * 64 + dd;
         const int box = d >> 6, dc = d & 63;
-        const uint32_t r0 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp, dc));
-        const uint32_t r1 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp + 1, dc));
+        const uint32_t r0 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp, dc)) & keep0;
+        const uint32_t r1 = lds32(v + box * (kKVBytes / 2) + sw128(2 * kp + 1, dc)) & keep1;
         // (key 2kp, dims d, d+1) and (key 2kp+1, dims d, d+1) -> rows d, d+1 of VT
         sts32(vt + sw128(d, 2 * kp), __byte_perm(r0, r1, 0x5410));
         sts32(vt + sw128(d + 1, 2 * kp), __byte_perm(r0, r1, 0x7632));
       }
       fence_async_smem();
       mbar_arrive(&vt_full[s]);
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-      if (t == 0) mbar_arrive(&kv_empty[s]);  // V of this stage consumed
+      // V of this stage consumed by this warp.  Each warp releases its own
+      // share (no named barrier across the two warps: one that left the loop
+      // on a timeout would hold the other at that barrier for good).
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kv_empty[s]);
     }
   } else {
     // -------------------------------- softmax ---------------------------------

@@ -1,0 +1,357 @@
+"""Host model of the warp-specialised pipeline of attn_prefill_tc_kernel
+(csrc/attn_prefill_tc.cu), for protocol tests on CPU.
+
+The model replays the kernel's synchronisation, not its arithmetic:
+  - mbarriers with an arrival count, a transaction-byte count and a completed
+    phase count; a wait names the logical phase it expects and passes its
+    parity, as the kernel does; a wait that finds the barrier two phases on
+    (the waiter was lapped, where the hardware would block on the parity) is
+    an error;
+  - TMA loads complete at random times, each adding its bytes to its barrier;
+  - tensor-core MMAs and tcgen05.commit markers complete in issue order;
+  - thread roles: the producer (warp 0), the MMA issuer (warp 1), two V
+    transposer warps (2-3) and four softmax warps (4-7), each a generator
+    that mirrors its branch of the kernel statement for statement;
+  - every shared-memory / TMEM buffer carries the tile index last written
+    into it; a reader checks it sees the tile it expects, and overlapping
+    accesses of two agents where either writes are reported as races.
+A seeded scheduler picks at random among the roles that can run and the async
+completions that are due.  `fault_at` makes one blocked wait (one that
+records an error code) give up, as a bounded wait that ran out would; any
+wait left blocked with nothing else able to run then also gives up, as the
+bounded waits of the kernel do.  `named_barrier=True` restores the earlier
+transposer hand-off (a `bar.sync` across both transposer warps, with no time
+limit, and one kv_empty arrival for both) to show the hang it allowed.
+"""
+from __future__ import annotations
+
+import random
+from collections import defaultdict, deque
+
+Q_BYTES = 128 * 128 * 2
+KV_BYTES = 64 * 128 * 2
+
+
+class Bar:
+    def __init__(self, name: str, count: int):
+        self.name, self.count = name, count
+        self.pending, self.tx, self.phase = count, 0, 0
+
+    def _maybe(self):
+        if self.pending == 0 and self.tx == 0:
+            self.phase += 1
+            self.pending = self.count
+
+    def arrive(self, n: int = 1):
+        self.pending -= n
+        assert self.pending >= 0, f"{self.name}: more arrivals than its count"
+        self._maybe()
+
+    def arrive_expect_tx(self, nbytes: int):
+        self.tx += nbytes
+        self.arrive()
+
+    def complete_tx(self, nbytes: int):
+        self.tx -= nbytes
+        self._maybe()
+
+
+class Wait:
+    def __init__(self, bar: Bar, phase: int, code):
+        self.bar, self.phase, self.code = bar, phase, code
+
+    def ready(self) -> bool:
+        return self.bar.phase >= self.phase + 1
+
+
+class NamedBarrier:
+    """bar.sync over `threads` (no time limit)."""
+
+    def __init__(self, parties: int):
+        self.parties, self.arrived, self.gen = parties, 0, 0
+
+
+class NamedWait:
+    def __init__(self, nb: NamedBarrier):
+        self.nb = nb
+        nb.arrived += 1
+        self.gen = nb.gen
+        if nb.arrived == nb.parties:
+            nb.arrived, nb.gen = 0, nb.gen + 1
+
+    def ready(self) -> bool:
+        return self.nb.gen > self.gen
+
+
+class Model:
+    def __init__(self, n_kb: int, seed: int, fault_at=None, named_barrier: bool = False):
+        self.n_kb, self.rng = n_kb, random.Random(seed)
+        self.fault_at, self.named = fault_at, named_barrier
+        self.q_full = Bar("q_full", 1)
+        self.kv_full = [Bar(f"kv_full{i}", 1) for i in range(2)]
+        self.kv_empty = [Bar(f"kv_empty{i}", 2 if named_barrier else 3) for i in range(2)]
+        self.s_full = [Bar(f"s_full{i}", 1) for i in range(2)]
+        self.s_free = [Bar(f"s_free{i}", 128) for i in range(2)]
+        self.p_full = [Bar(f"p_full{i}", 128) for i in range(2)]
+        self.vt_full = [Bar(f"vt_full{i}", 64) for i in range(2)]
+        self.o_full = [Bar(f"o_full{i}", 1) for i in range(2)]
+        self.o_free = [Bar(f"o_free{i}", 128) for i in range(2)]
+        self.mma_done = Bar("mma_done", 1)
+        self.tr_bar = NamedBarrier(2)
+        self.abort = False
+        self.err = 0
+        self.tma: list = []            # in-flight loads (agent, buf, bar, bytes, tag)
+        self.pipe: deque = deque()     # ("mma", agent, reads, writes) | ("commit", bar)
+        self.mem: dict = {}
+        self.access = defaultdict(list)
+        self.errors: list = []
+        self.seen = defaultdict(list)  # softmax warp -> tiles whose O it folded in
+        self._n = 0
+
+    # ------------------------------------------------------------ accesses
+    def begin(self, agent, buf, kind):
+        for a, k in self.access[buf]:
+            if a != agent and "w" in (k, kind):
+                self.errors.append(f"race on {buf}: {agent} {kind} against {a} {k}")
+        self.access[buf].append((agent, kind))
+
+    def end(self, agent, buf, kind):
+        self.access[buf].remove((agent, kind))
+
+    def check(self, who, buf, tag):
+        if self.mem.get(buf) != tag:
+            self.errors.append(f"{who} read {buf} holding {self.mem.get(buf)!r}, wanted {tag!r}")
+
+    # ------------------------------------------------------------ async units
+    def tma_load(self, buf, bar, nbytes, tag):
+        self._n += 1
+        agent = f"tma{self._n}"
+        self.begin(agent, buf, "w")
+        self.tma.append((agent, buf, bar, nbytes, tag))
+
+    def mma(self, reads, writes):
+        self._n += 1
+        agent = f"mma{self._n}"
+        for b, _ in reads:
+            self.begin(agent, b, "r")
+        for b, _ in writes:
+            self.begin(agent, b, "w")
+        self.pipe.append(("mma", agent, reads, writes))
+
+    def commit(self, bar):
+        self.pipe.append(("commit", bar))
+
+    def _complete_tma(self, i):
+        agent, buf, bar, nbytes, tag = self.tma.pop(i)
+        self.mem[buf] = tag
+        self.end(agent, buf, "w")
+        bar.complete_tx(nbytes)
+
+    def _complete_pipe(self):
+        op = self.pipe.popleft()
+        if op[0] == "commit":
+            op[1].arrive()
+            return
+        _, agent, reads, writes = op
+        for b, tag in reads:
+            self.check(agent, b, tag)
+            self.end(agent, b, "r")
+        for b, tag in writes:
+            self.mem[b] = tag
+            self.end(agent, b, "w")
+
+    # ------------------------------------------------------------ roles
+    def producer(self):
+        n_kb = self.n_kb
+        self.q_full.arrive_expect_tx(Q_BYTES)
+        self.tma_load("Q", self.q_full, Q_BYTES, "q")
+        yield None
+        issued = 0
+        for j in range(n_kb):
+            if self.abort:
+                break
+            s = j & 1
+            if j >= 2 and not (yield Wait(self.kv_empty[s], (j >> 1) - 1, 0x601)):
+                self.abort = True
+                break
+            self.kv_full[s].arrive_expect_tx(2 * KV_BYTES)
+            self.tma_load(f"K{s}", self.kv_full[s], KV_BYTES, j)
+            self.tma_load(f"V{s}", self.kv_full[s], KV_BYTES, j)
+            issued = j + 1
+            yield None
+        yield Wait(self.q_full, 0, None)
+        for j in range(max(0, issued - 2), issued):
+            yield Wait(self.kv_full[j & 1], j >> 1, None)
+
+    def mma_issuer(self):
+        n_kb = self.n_kb
+        ok = yield Wait(self.q_full, 0, 0x602)
+
+        def issue_s(j):
+            s = j & 1
+            if not (yield Wait(self.kv_full[s], j >> 1, 0x603)):
+                return False
+            if j >= 2 and not (yield Wait(self.s_free[s], (j >> 1) - 1, 0x604)):
+                return False
+            self.mma([("Q", "q"), (f"K{s}", j)], [(f"S{s}.{w}", j) for w in range(4)])
+            self.commit(self.s_full[s])
+            self.commit(self.kv_empty[s])
+            return True
+
+        if ok and n_kb > 0:
+            ok = yield from issue_s(0)
+        j = 0
+        while ok and j < n_kb and not self.abort:
+            if j + 1 < n_kb and not (yield from issue_s(j + 1)):
+                ok = False
+                break
+            s = j & 1
+            if (not (yield Wait(self.p_full[s], j >> 1, 0x605))
+                    or not (yield Wait(self.vt_full[s], j >> 1, 0x606))
+                    or (j >= 2 and not (yield Wait(self.o_free[s], (j >> 1) - 1, 0x607)))):
+                ok = False
+                break
+            self.mma([(f"P{s}.{w}", j) for w in range(4)] + [(f"VT{s}.{h}", j) for h in range(2)],
+                     [(f"O{s}.{w}", j) for w in range(4)])
+            self.commit(self.o_full[s])
+            j += 1
+            yield None
+        if not ok:
+            self.abort = True
+        self.commit(self.mma_done)
+        yield Wait(self.mma_done, 0, None)
+
+    def transposer(self, w):
+        agent = f"transposer{w}"
+        for j in range(self.n_kb):
+            if self.abort:
+                break
+            s = j & 1
+            if not (yield Wait(self.kv_full[s], j >> 1, 0x608)):
+                self.abort = True
+                break
+            if j >= 2 and not (yield Wait(self.o_full[s], (j >> 1) - 1, 0x609)):
+                self.abort = True
+                break
+            self.begin(agent, f"V{s}", "r")
+            self.check(agent, f"V{s}", j)
+            self.begin(agent, f"VT{s}.{w}", "w")
+            self.mem[f"VT{s}.{w}"] = j
+            yield None
+            self.end(agent, f"VT{s}.{w}", "w")
+            self.vt_full[s].arrive(32)
+            if self.named:
+                self.end(agent, f"V{s}", "r")
+                yield NamedWait(self.tr_bar)
+                if w == 0:
+                    self.kv_empty[s].arrive()
+            else:
+                self.end(agent, f"V{s}", "r")
+                self.kv_empty[s].arrive()
+            yield None
+
+    def softmax(self, w):
+        agent = f"softmax{w}"
+        ok = True
+        for j in range(self.n_kb):
+            s = j & 1
+            if not (yield Wait(self.s_full[s], j >> 1, 0x60a)):
+                ok = False
+                break
+            self.begin(agent, f"S{s}.{w}", "r")
+            self.check(agent, f"S{s}.{w}", j)
+            yield None
+            self.end(agent, f"S{s}.{w}", "r")
+            self.s_free[s].arrive(32)
+            self.begin(agent, f"P{s}.{w}", "w")
+            self.mem[f"P{s}.{w}"] = j
+            yield None
+            self.end(agent, f"P{s}.{w}", "w")
+            self.p_full[s].arrive(32)
+            if not (yield Wait(self.o_full[s], j >> 1, 0x60b)):
+                ok = False
+                break
+            self.begin(agent, f"O{s}.{w}", "r")
+            self.check(agent, f"O{s}.{w}", j)
+            yield None
+            self.end(agent, f"O{s}.{w}", "r")
+            self.o_free[s].arrive(32)
+            self.seen[w].append(j)
+        if not ok:
+            self.abort = True
+
+    # ------------------------------------------------------------ scheduler
+    def run(self, max_steps: int = 200000) -> str:
+        """Returns "done" or "deadlock" (roles blocked on a barrier without a
+        time limit).  Errors are collected in self.errors."""
+        roles = {"producer": self.producer(), "mma": self.mma_issuer()}
+        for w in range(2):
+            roles[f"transposer{w}"] = self.transposer(w)
+        for w in range(4):
+            roles[f"softmax{w}"] = self.softmax(w)
+        pending = {}
+        for name, g in roles.items():
+            pending[name] = self._advance(g, None, name)
+        pending = {k: v for k, v in pending.items() if v != "exit"}
+        faulted = self.fault_at is None
+        steps = 0
+        while pending and steps < max_steps:
+            steps += 1
+            runnable = [n for n, w in pending.items() if w is None or w.ready()]
+            asyncs = [("tma", i) for i in range(len(self.tma))] + ([("pipe", 0)] if self.pipe else [])
+            timed = [n for n, w in pending.items()
+                     if isinstance(w, Wait) and not w.ready() and w.code is not None]
+            if not faulted and steps >= self.fault_at and timed:
+                faulted = True
+                name = self.rng.choice(timed)
+                self._give_up(pending[name])
+                pending[name] = self._advance(roles[name], False, name)
+                if pending[name] == "exit":
+                    del pending[name]
+                continue
+            choices = [("role", n) for n in runnable] + asyncs
+            if not choices:
+                blocked = [n for n, w in pending.items() if isinstance(w, Wait)]
+                if not blocked:
+                    return "deadlock"
+                name = self.rng.choice(blocked)    # a bounded wait runs out
+                self._give_up(pending[name])
+                pending[name] = self._advance(roles[name], False, name)
+                if pending[name] == "exit":
+                    del pending[name]
+                continue
+            kind, x = self.rng.choice(choices)
+            if kind == "tma":
+                self._complete_tma(x)
+            elif kind == "pipe":
+                self._complete_pipe()
+            else:
+                w = pending[x]
+                val = None
+                if w is not None:
+                    val = True
+                    if isinstance(w, Wait) and w.bar.phase != w.phase + 1:
+                        self.errors.append(f"{x} waited for phase {w.phase} of {w.bar.name}, "
+                                           f"which is at {w.bar.phase} (lapped)")
+                pending[x] = self._advance(roles[x], val, x)
+                if pending[x] == "exit":
+                    del pending[x]
+        if pending:
+            return "deadlock"
+        # the CTA's exit: TMEM is freed and shared memory released
+        if self.tma:
+            self.errors.append(f"{len(self.tma)} TMA loads still in flight at exit")
+        if self.pipe:
+            self.errors.append(f"{len(self.pipe)} tensor-core operations still queued at exit")
+        return "done"
+
+    def _give_up(self, w: Wait):
+        if w.code is not None and self.err == 0:
+            self.err = w.code
+
+    @staticmethod
+    def _advance(gen, value, name):
+        try:
+            return gen.send(value) if value is not None else next(gen)
+        except StopIteration:
+            return "exit"
