@@ -314,6 +314,18 @@ Q3_API int q3_attn_prefill_paged(const void* q, const void* k_pages, const void*
 Q3_API int q3_gemm(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K, int epilogue,
             const void* aux, q3_stream_t stream);
 
+/* MLPBlock's gate/up projection with SwiGLU (model_fused.py:160-169):
+ * C[M, inter] = silu(h Wgate) * (h Wup) with h = rmsnorm(A; norm_w, eps)
+ * (model_fused.py:37-40) when norm_w != NULL, else h = A.  A bf16 [M, K];
+ * W_gate_up bf16 [2*inter, K] K-major with gate and up rows interleaved in
+ * blocks of 8 (Q3_EPI_SWIGLU); inter % 8 == 0.  The fused norm is for decode
+ * shapes (M <= 16); larger M takes the normalised rows (q3_rmsnorm) and runs
+ * the tcgen05 kernel.  The down projection follows through q3_gemm or
+ * q3_gemm_ar. */
+Q3_API int q3_gate_up_swiglu(const void* A, const void* W_gate_up, void* C, int64_t M,
+                             int64_t inter, int64_t K, const void* norm_w, float eps,
+                             q3_stream_t stream);
+
 /* ---- vision tower linears: nn.Linear with bias (tcgen05 GEMM) -------------
  * Replaces the vision tower's linears (transformers 5.5.0 modeling_qwen3_vl.py:
  * attn.qkv / attn.proj :189-190, mlp.linear_fc1/fc2 :64-65, merger fc1/fc2
@@ -402,6 +414,11 @@ Q3_API int q3_comm_create(int rank, int world, int64_t max_cols, void** comm_out
                           void* ipc_handle_out);
 Q3_API int q3_comm_open_peers(void* comm, const void* all_handles);
 Q3_API int q3_comm_destroy(void* comm);
+/* q3_init_comm(rank, world, peer IPC handles): the set-up step in one call
+ * for a communicator made by q3_comm_create: checks that comm was created for
+ * this rank and world size, then maps every peer's buffer as
+ * q3_comm_open_peers does (all_handles: every rank's handle in rank order). */
+Q3_API int q3_init_comm(void* comm, int rank, int world, const void* all_handles);
 Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
                       const void* residual, float* ss_out, void* comm, q3_stream_t stream);
 
@@ -469,6 +486,19 @@ Q3_API int q3_argmax_key(const void* logits, int64_t rows, int64_t V, int64_t co
                   int64_t* out_key, q3_stream_t stream);
 Q3_API int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* out_idx,
                         q3_stream_t stream);
+/* The greedy next token of each row in one call: the final RMSNorm
+ * (model_fused.py:286; skipped when norm_w is NULL and hidden is already
+ * normalised), the lm_head projection (:289) and the argmax (:310,320).
+ * hidden bf16 [rows, K]; norm_w bf16 [K] needs rows <= 16 (decode shapes);
+ * W_lm bf16 [V, K] K-major, this rank's vocabulary slice whose first row is
+ * vocabulary index col_offset; logits_ws bf16 [rows, V] receives the slice's
+ * logits.  keys == 0: out[rows] = argmax index over the slice (col_offset must
+ * be 0: the slice is the whole vocabulary); keys != 0: out[rows] = the
+ * q3_argmax_key keys, for a MAX all-reduce across ranks and then
+ * q3_argmax_key_index. */
+Q3_API int q3_lm_head_argmax(const void* hidden, const void* norm_w, float eps, const void* W_lm,
+                             int64_t rows, int64_t V, int64_t K, int64_t col_offset,
+                             void* logits_ws, int keys, int64_t* out, q3_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -87,6 +87,16 @@ extern "C" int q3_comm_open_peers(void* comm, const void* all_handles) {
   return Q3_OK;
 }
 
+extern "C" int q3_init_comm(void* comm, int rank, int world, const void* all_handles) {
+  using namespace q3;
+  Q3_REQUIRE(comm && all_handles, "q3_init_comm: null pointer");
+  const Comm* c = static_cast<const Comm*>(comm);
+  Q3_REQUIRE(c->rank == rank && c->world == world,
+             "q3_init_comm: communicator was created for rank %d of %d, not %d of %d", c->rank,
+             c->world, rank, world);
+  return q3_comm_open_peers(comm, all_handles);
+}
+
 extern "C" int q3_comm_destroy(void* comm) {
   using namespace q3;
   if (!comm) return Q3_OK;

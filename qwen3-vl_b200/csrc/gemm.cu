@@ -599,6 +599,25 @@ extern "C" int q3_gemm_norm(const void* A, const void* norm_w, float eps, const 
   return launch_gemv(A, W, C, aux, (int)M, (int)N, (int)K, epilogue, (cudaStream_t)stream, o);
 }
 
+extern "C" int q3_gate_up_swiglu(const void* A, const void* W_gate_up, void* C, int64_t M,
+                                 int64_t inter, int64_t K, const void* norm_w, float eps,
+                                 q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(A && W_gate_up && C, "q3_gate_up_swiglu: null pointer");
+  Q3_REQUIRE(M >= 0 && inter > 0 && inter % 8 == 0 && inter < (1ll << 30),
+             "q3_gate_up_swiglu: bad shape M=%lld inter=%lld (inter %% 8 == 0)", (long long)M,
+             (long long)inter);
+  Q3_REQUIRE(!norm_w || M <= 16,
+             "q3_gate_up_swiglu: the fused norm is for M <= 16 (got %lld); normalise first",
+             (long long)M);
+  if (norm_w) {
+    if (M == 0) return Q3_OK;
+    return q3_gemm_norm(A, norm_w, eps, W_gate_up, C, M, 2 * inter, K, Q3_EPI_SWIGLU, nullptr,
+                        stream);
+  }
+  return q3_gemm(A, W_gate_up, C, M, 2 * inter, K, Q3_EPI_SWIGLU, nullptr, stream);
+}
+
 extern "C" int q3_gemm_decode(const void* A, const void* W, void* C, int64_t M, int64_t N,
                               int64_t K, int epilogue, const void* aux, const void* norm_w,
                               float eps, const float* ss_in, int ss_tiles, float* ss_out,

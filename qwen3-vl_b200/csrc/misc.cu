@@ -194,3 +194,27 @@ extern "C" int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* o
   return launch_ex(argmax_key_index_kernel, dim3((unsigned)((rows + 127) / 128)), dim3(128), 0,
                    (cudaStream_t)stream, 1, keys, rows, out_idx);
 }
+
+extern "C" int q3_lm_head_argmax(const void* hidden, const void* norm_w, float eps,
+                                 const void* W_lm, int64_t rows, int64_t V, int64_t K,
+                                 int64_t col_offset, void* logits_ws, int keys, int64_t* out,
+                                 q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(hidden && W_lm && logits_ws && out, "q3_lm_head_argmax: null pointer");
+  Q3_REQUIRE(rows >= 0 && V > 0 && K > 0, "q3_lm_head_argmax: bad shape rows=%lld V=%lld K=%lld",
+             (long long)rows, (long long)V, (long long)K);
+  Q3_REQUIRE(!norm_w || rows <= 16,
+             "q3_lm_head_argmax: the fused final norm is for rows <= 16 (got %lld)",
+             (long long)rows);
+  Q3_REQUIRE(keys || col_offset == 0,
+             "q3_lm_head_argmax: indices over a vocabulary slice need keys (col_offset %lld)",
+             (long long)col_offset);
+  if (rows == 0) return Q3_OK;
+  const int rc = norm_w ? q3_gemm_norm(hidden, norm_w, eps, W_lm, logits_ws, rows, V, K,
+                                       Q3_EPI_NONE, nullptr, stream)
+                        : q3_gemm(hidden, W_lm, logits_ws, rows, V, K, Q3_EPI_NONE, nullptr,
+                                  stream);
+  if (rc) return rc;
+  return keys ? q3_argmax_key(logits_ws, rows, V, col_offset, out, stream)
+              : q3_argmax(logits_ws, rows, V, out, stream);
+}

@@ -82,12 +82,14 @@ SIGNATURES: dict[str, tuple] = {
     "q3_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, P, P, P, P]),
     "q3_gemm": (I32, [P, P, P, I64, I64, I64, I32, P, P]),
     "q3_gemm_norm": (I32, [P, P, F32, P, P, I64, I64, I64, I32, P, P]),
+    "q3_gate_up_swiglu": (I32, [P, P, P, I64, I64, I64, P, F32, P]),
     "q3_gemm_qkv_rope": (I32, [P, P, I64, P, P, P, P, I32, I32, I64, I64, P, P, P, I32, I32,
                                I32, I32, I32, I64, I64, F32, P]),
     "q3_gemm_decode": (I32, [P, P, P, I64, I64, I64, I32, P, P, F32, P, I32, P, P]),
     "q3_comm_handle_bytes": (I32, []),
     "q3_comm_create": (I32, [I32, I32, I64, ctypes.POINTER(P), P]),
     "q3_comm_open_peers": (I32, [P, P]),
+    "q3_init_comm": (I32, [P, I32, I32, P]),
     "q3_comm_destroy": (I32, [P]),
     "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P, P]),
     "q3_decode_step_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64,
@@ -99,6 +101,7 @@ SIGNATURES: dict[str, tuple] = {
     "q3_argmax": (I32, [P, I64, I64, P, P]),
     "q3_argmax_key": (I32, [P, I64, I64, I64, P, P]),
     "q3_argmax_key_index": (I32, [P, I64, P, P]),
+    "q3_lm_head_argmax": (I32, [P, P, F32, P, I64, I64, I64, I64, P, I32, P, P]),
 }
 
 _lib = None

@@ -519,6 +519,26 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: str = "none", residual: tor
     return out
 
 
+def gate_up_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, norm_w: torch.Tensor = None,
+                   eps: float = 1e-6, out: torch.Tensor = None) -> torch.Tensor:
+    """MLPBlock's silu(h @ Wg) * (h @ Wu) (model_fused.py:160-169) through
+    q3_gate_up_swiglu: a [..., K]; w_gate_up [2*inter, K] K-major with gate/up
+    rows interleaved in blocks of 8; h = rmsnorm(a; norm_w) when norm_w is
+    given (1..16 rows), else a.  Returns [..., inter]."""
+    _cuda("gate_up_swiglu", a, w_gate_up, norm_w, out)
+    _bf16("gate_up_swiglu", a, w_gate_up, norm_w, out)
+    _contig("gate_up_swiglu", a, w_gate_up, out)
+    K = a.shape[-1]
+    if w_gate_up.shape[1] != K or w_gate_up.shape[0] % 2:
+        raise ValueError(f"gate_up_swiglu: weight {tuple(w_gate_up.shape)} does not match K={K}")
+    M, inter = a.numel() // K, w_gate_up.shape[0] // 2
+    if out is None:
+        out = torch.empty(*a.shape[:-1], inter, dtype=torch.bfloat16, device=a.device)
+    call("q3_gate_up_swiglu", _p(a), _p(w_gate_up), _p(out), M, inter, K, _p(norm_w),
+         float(eps), _stream())
+    return out
+
+
 def gemm_qkv_rope(h: torch.Tensor, w: torch.Tensor, q_norm_w, k_norm_w, cos, sin, *, B: int,
                   S: int, Hq: int, Hkv: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                   start_pos: int = 0, cs_use_pos: bool = True, cs_offset: int = 0,
@@ -763,6 +783,33 @@ def argmax_key_index(keys: torch.Tensor, out: torch.Tensor = None) -> torch.Tens
     if out is None:
         out = torch.empty_like(keys)
     call("q3_argmax_key_index", _p(keys), keys.numel(), _p(out), _stream())
+    return out
+
+
+def lm_head_argmax(h: torch.Tensor, w_lm: torch.Tensor, norm_w: torch.Tensor = None,
+                   eps: float = 1e-6, col_offset: int = 0, keys: bool = False,
+                   logits: torch.Tensor = None, out: torch.Tensor = None) -> torch.Tensor:
+    """Final norm (when norm_w is given; 1..16 rows), lm_head projection and
+    greedy argmax in one library call (q3_lm_head_argmax).  h [rows, K];
+    w_lm [V, K] K-major, the vocabulary slice starting at col_offset.
+    Returns int64 [rows]: indices, or with keys=True the argmax_key keys of the
+    slice.  `logits` [rows, V] bf16, when given, receives the logits."""
+    _cuda("lm_head_argmax", h, w_lm, norm_w, logits, out)
+    _bf16("lm_head_argmax", h, w_lm, norm_w, logits)
+    _contig("lm_head_argmax", h, w_lm, logits)
+    K = h.shape[-1]
+    V = w_lm.shape[0]
+    if w_lm.shape[1] != K:
+        raise ValueError(f"lm_head_argmax: weight [V={V}, K={w_lm.shape[1]}] does not match K={K}")
+    rows = h.numel() // K
+    if logits is None:
+        logits = torch.empty(rows, V, dtype=torch.bfloat16, device=h.device)
+    elif logits.numel() != rows * V:
+        raise ValueError("lm_head_argmax: logits must be [rows, V]")
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=h.device)
+    call("q3_lm_head_argmax", _p(h), _p(norm_w), float(eps), _p(w_lm), rows, V, K,
+         int(col_offset), _p(logits), 1 if keys else 0, _p(out), _stream())
     return out
 
 

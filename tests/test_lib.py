@@ -99,6 +99,22 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     rc = lib.q3_gemm_decode(one, one, one, 8, 4096, 4096, 0, None, None, 1e-6, None, 0, one,
                             None)
     assert rc == _lib.Q3_ERR_INVALID and b"residual" in lib.q3_last_error()
+    # gate/up + SwiGLU: the fused norm is for decode shapes; inter must be a multiple of 8
+    rc = lib.q3_gate_up_swiglu(one, one, one, 64, 12288, 4096, one, 1e-6, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"M <= 16" in lib.q3_last_error()
+    rc = lib.q3_gate_up_swiglu(one, one, one, 8, 100, 4096, None, 1e-6, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"inter" in lib.q3_last_error()
+    # lm_head + argmax: indices over a slice need keys; the fused norm needs <= 16 rows
+    rc = lib.q3_lm_head_argmax(one, None, 1e-6, one, 8, 18992, 4096, 18992, one, 0, one, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"need keys" in lib.q3_last_error()
+    rc = lib.q3_lm_head_argmax(one, one, 1e-6, one, 32, 18992, 4096, 0, one, 0, one, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"rows <= 16" in lib.q3_last_error()
+    # ... and the projection's own checks still apply (V % 16)
+    rc = lib.q3_lm_head_argmax(one, None, 1e-6, one, 4, 1000, 4096, 0, one, 0, one, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"multiple of 16" in lib.q3_last_error()
+    # communicator set-up needs a communicator
+    rc = lib.q3_init_comm(None, 0, 2, one)
+    assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
     # whole-step kernel: 1..16 sequences
     plan = ctypes.c_void_p()
     layer = _lib.StepLayer()
