@@ -237,7 +237,11 @@ Q3_API int q3_qkv_norm_rope_paged(const void* qkv, const void* q_norm_w, const v
  * kv_len-1 may come from the kernel just before this call on the stream (as
  * q3_qkv_norm_rope writes them); *kv_len_dev and the cache rows below
  * kv_len-1 must be complete before that kernel is launched, because the bf16
- * kernel starts streaming them while its predecessor finishes. */
+ * kernel starts streaming them while its predecessor finishes.
+ * Cache rows from kv_len up to the next multiple of 64 are read and given
+ * probability 0, as the reference's masked softmax gives the rows past the
+ * prompt (model_fused.py:259-262): they must hold finite values, which
+ * zero-filled caches (init_kv_cache, :224-232) and rows written earlier do. */
 Q3_API size_t q3_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int head_dim, int64_t max_kv_len);
 Q3_API int q3_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
                    int Hq, int Hkv, int head_dim, int64_t kv_len, const int32_t* kv_len_dev,
