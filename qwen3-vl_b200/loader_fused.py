@@ -137,6 +137,15 @@ def _hf_layer_weights(lang_model, i, H, D):
     return lw
 
 
+def _head_dim(cfg) -> int:
+    """The attention head size of a text config.  loader_fused.py:69 takes
+    hidden // heads, which equals the config's head_dim for Qwen3-VL-8B (4096 /
+    32 = 128); other sizes set head_dim apart from it (the weights' shapes
+    follow head_dim), so it is read from the config when present."""
+    hd = getattr(cfg, "head_dim", None)
+    return int(hd) if hd else cfg.hidden_size // cfg.num_attention_heads
+
+
 def load_model(model_path, rank, world_size, device, compile_backend='neuron'):
     """loader_fused.py:38-237.  Returns (decoder, vision_model, processor, hf_model);
     the random-init path returns (decoder, None, None, None)."""
@@ -163,7 +172,7 @@ def load_model(model_path, rank, world_size, device, compile_backend='neuron'):
         rope_theta = (getattr(cfg, "rope_scaling", {}) or {}).get("rope_theta", 1000000.0)
     spec = TextSpec(hidden=cfg.hidden_size, q_heads=cfg.num_attention_heads,
                     kv_heads=cfg.num_key_value_heads,
-                    head_dim=cfg.hidden_size // cfg.num_attention_heads,
+                    head_dim=_head_dim(cfg),
                     inter=cfg.intermediate_size, vocab=hf_model.lm_head.weight.shape[0],
                     layers=cfg.num_hidden_layers, rope_theta=rope_theta, eps=cfg.rms_norm_eps)
     layers = [_hf_layer_weights(lang, i, spec.hidden, spec.head_dim) for i in range(spec.layers)]
