@@ -70,18 +70,34 @@ def prepare_vision_embeds(hf_model, processor, inputs, device):
     image_grid_thw = inputs.get("image_grid_thw")
     pixel_values_videos = inputs.get("pixel_values_videos")
     video_grid_thw = inputs.get("video_grid_thw")
-    tower = None
 
     table = _embed_table(hf_model).to(device)
     inputs_embeds = ops.embed(input_ids, table.to(torch.bfloat16).contiguous())
+    image = video = None
+    if pixel_values is not None and image_grid_thw is not None:
+        feats, deep, _ = _encode(vision_tower_for(hf_model, device), pixel_values,
+                                 image_grid_thw)
+        image = (feats, deep)
+    if pixel_values_videos is not None and video_grid_thw is not None:
+        feats, deep, _ = _encode(vision_tower_for(hf_model, device), pixel_values_videos,
+                                 video_grid_thw)
+        video = (feats, deep)
+    return merge_vision(inputs_embeds, input_ids[0], image, video)
+
+
+def merge_vision(inputs_embeds, ids0, image=None, video=None):
+    """The reference's merge of the tower outputs into batch row 0 of the text
+    embeddings (vision.py:57-129).  image / video: (features [n, H], deepstack
+    levels) from one tower call each, or None.  inputs_embeds is updated in
+    place.  Returns (inputs_embeds, deepstack list or None, visual_mask or
+    None)."""
+    device = inputs_embeds.device
     dtype = inputs_embeds.dtype
-    ids0 = input_ids[0]
     visual_mask = torch.zeros(ids0.shape[-1], dtype=torch.bool, device=device)
     deepstack = []
 
-    if pixel_values is not None and image_grid_thw is not None:
-        tower = vision_tower_for(hf_model, device)
-        feats, img_deep, _ = _encode(tower, pixel_values, image_grid_thw)
+    if image is not None:
+        feats, img_deep = image
         image_mask = ids0 == IMAGE_TOKEN_ID
         n_img = int(image_mask.sum())
         if n_img > 0 and feats.shape[0] >= n_img:
@@ -89,9 +105,8 @@ def prepare_vision_embeds(hf_model, processor, inputs, device):
             visual_mask |= image_mask
             deepstack = [d[:n_img].to(dtype) for d in img_deep]
 
-    if pixel_values_videos is not None and video_grid_thw is not None:
-        tower = tower or vision_tower_for(hf_model, device)
-        vfeats, vid_deep, _ = _encode(tower, pixel_values_videos, video_grid_thw)
+    if video is not None:
+        vfeats, vid_deep = video
         video_mask = ids0 == VIDEO_TOKEN_ID
         n_fill = min(int(vfeats.shape[0]), int(video_mask.sum()))
         if n_fill > 0:

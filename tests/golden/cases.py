@@ -342,6 +342,71 @@ def hf_vision_tiny(dtype=torch.float32):
     return out.pooler_output, list(out.deepstack_features), out.last_hidden_state
 
 
+# ---- the drop-in vision.py: the reference's prepare_vision_embeds end to end ----
+DROPIN_TEXT = dict(hidden_size=128, num_attention_heads=1, num_key_value_heads=1, head_dim=128,
+                   intermediate_size=256, num_hidden_layers=1, vocab_size=151936,
+                   rms_norm_eps=1e-6,
+                   rope_parameters={"rope_type": "default", "rope_theta": 5e6,
+                                    "mrope_section": [24, 20, 20], "mrope_interleaved": True})
+DROPIN_CASES = ("image", "video_short", "image_video")
+IMAGE_TOKEN, VIDEO_TOKEN = 151655, 151656
+
+
+def dropin_embed_table(seed: int = 41) -> torch.Tensor:
+    """bf16 [151936, 128] text embeddings of the drop-in model."""
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(DROPIN_TEXT["vocab_size"], 128, generator=g) * 0.5).to(BF16)
+
+
+def dropin_hf_model():
+    """A seeded transformers 5.5.0 Qwen3VLForConditionalGeneration in bf16 with
+    eager attention: VISION_TINY's tower (out width 128) over a one-layer text
+    model with the real vocabulary, so the image / video token ids embed.
+    Only the tower and the embeddings are used by prepare_vision_embeds."""
+    from transformers import Qwen3VLConfig, Qwen3VLForConditionalGeneration
+    cfg = Qwen3VLConfig(text_config=dict(DROPIN_TEXT), vision_config=dict(VISION_TINY))
+    for c in (cfg, cfg.text_config, cfg.vision_config):
+        c._attn_implementation = "eager"
+    model = Qwen3VLForConditionalGeneration(cfg).eval()
+    missing, unexpected = model.model.visual.load_state_dict(vision_tiny_weights(), strict=True)
+    assert not missing and not unexpected
+    model = model.to(BF16)
+    with torch.no_grad():
+        model.model.language_model.embed_tokens.weight.copy_(dropin_embed_table())
+    # from_pretrained(dtype=bf16) keeps this buffer fp32
+    rot = model.model.visual.rotary_pos_emb
+    rot.inv_freq = 1.0 / (rot.theta ** (torch.arange(0, rot.dim, 2, dtype=torch.float) / rot.dim))
+    return model
+
+
+def dropin_inputs(name: str) -> dict:
+    """Processor-style inputs: input_ids [1, S] with <image> / <video> runs,
+    flattened patches and grids (VISION_TINY's image and clip).  video_short
+    has 10 <video> positions for the clip's 12 features (the reference fills
+    10 and cuts the deepstack rows to 10)."""
+    x, grid = vision_tiny_inputs()
+    img_px, vid_px = x[:96], x[96:]
+    g = torch.Generator().manual_seed(43 + DROPIN_CASES.index(name))
+
+    def text(n):
+        return torch.randint(0, 151000, (n,), generator=g)
+
+    def run(tok, n):
+        return torch.full((n,), tok, dtype=torch.int64)
+
+    if name == "image":
+        ids = torch.cat([text(5), run(IMAGE_TOKEN, 24), text(7)])
+        return dict(input_ids=ids[None], pixel_values=img_px, image_grid_thw=grid[:1])
+    if name == "video_short":
+        ids = torch.cat([text(3), run(VIDEO_TOKEN, 10), text(4)])
+        return dict(input_ids=ids[None], pixel_values_videos=vid_px, video_grid_thw=grid[1:])
+    if name == "image_video":
+        ids = torch.cat([text(2), run(IMAGE_TOKEN, 24), text(3), run(VIDEO_TOKEN, 12), text(5)])
+        return dict(input_ids=ids[None], pixel_values=img_px, image_grid_thw=grid[:1],
+                    pixel_values_videos=vid_px, video_grid_thw=grid[1:])
+    raise KeyError(name)
+
+
 # ---- a4 + a12: one text decoder layer with interleaved M-RoPE (transformers) ----
 MROPE_LAYER_SPEC = odec.Spec(hidden=512, q_heads=4, kv_heads=1, inter=1024, vocab=64, layers=1,
                              max_seq=512)

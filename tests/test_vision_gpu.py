@@ -148,3 +148,25 @@ def test_full_width_block_matches_oracle():
     pooler, deep, last = ovis.vision_forward(x, grid, w, depth=1, heads=16, merge=2,
                                              deepstack=(0,), dtype=BF16)
     _check_tower(VisionTower(w, c, DEV), x, grid, pooler, deep, last)
+
+
+@pytest.mark.parametrize("name", cases.DROPIN_CASES)
+def test_dropin_prepare_vision_embeds_matches_the_reference(name):
+    """The drop-in vision.prepare_vision_embeds on the GPU against the
+    reference's own prepare_vision_embeds (fixture) on the same seeded
+    transformers model: text rows and the visual mask identical, visual rows
+    and deepstack levels within the tower's tolerance."""
+    import vision
+    g = load_golden("vision_dropin")
+    model = cases.dropin_hf_model()
+    emb, deep, mask = vision.prepare_vision_embeds(model, None, cases.dropin_inputs(name), DEV)
+    want_mask = torch.from_numpy(g[name + "_mask"])
+    assert torch.equal(mask.cpu(), want_mask)
+    want = as_tensor(g[name + "_embeds"])
+    assert torch.equal(emb[0, ~mask].cpu(), want[0, ~want_mask])
+    compare("visual rows", emb[0, mask].cpu(), want[0, want_mask], max_abs=5e-2, rel_scale=True,
+            min_cos=0.999)
+    assert len(deep) == int(g[name + "_levels"])
+    for j, d in enumerate(deep):
+        compare(f"deepstack {j}", d.cpu(), as_tensor(g[f"{name}_deepstack{j}"]), max_abs=5e-2,
+                rel_scale=True, min_cos=0.999)
