@@ -332,7 +332,9 @@ def run_ours(args):
                                         if peer_ar else ("NCCL" if world > 1 else "none")),
                        "kv_cache": ("paged (256-token pages)" if kv_mode == "paged"
                                     else f"contiguous per batch, bucket {BUCKET}"),
-                       "prefill_attention": "tcgen05" if dec.prefill_tc else "mma.sync"},
+                       "prefill_attention": "tcgen05" if dec.prefill_tc else "mma.sync",
+                       "l2_prefetch": "o_proj weights during decode attention"
+                       if dec.l2_prefetch_oproj else "none"},
             "prefill_tok_s": round(prefill_tps, 1), "decode_tok_s": round(decode_tps, 1),
             "decode_step_ms": round(dec_step_ms, 4),
             "decode_step_hbm": {"bytes": step_bytes, "achieved_gbs": round(step_gbs, 1),

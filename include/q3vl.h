@@ -490,6 +490,15 @@ Q3_API int q3_argmax_key(const void* logits, int64_t rows, int64_t V, int64_t co
                   int64_t* out_key, q3_stream_t stream);
 Q3_API int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* out_idx,
                         q3_stream_t stream);
+/* Brings [ptr, ptr + bytes) into L2 with bulk prefetches and writes nothing:
+ * launched before a kernel that leaves HBM bandwidth idle (decode attention
+ * reads only the cache rows of a few sequences), it loads the weights of the
+ * projection that follows (o_proj, model_fused.py:141) so that projection
+ * reads them from L2.  The kernel lets the next kernel start at once and
+ * completes after the kernel before it, so stream order is kept.  ptr 16-byte
+ * aligned, bytes a multiple of 16. */
+Q3_API int q3_l2_prefetch(const void* ptr, int64_t bytes, q3_stream_t stream);
+
 /* The greedy next token of each row in one call: the final RMSNorm
  * (model_fused.py:286; skipped when norm_w is NULL and hidden is already
  * normalised), the lm_head projection (:289) and the argmax (:310,320).

@@ -195,6 +195,45 @@ extern "C" int q3_argmax_key_index(const int64_t* keys, int64_t rows, int64_t* o
                    (cudaStream_t)stream, 1, keys, rows, out_idx);
 }
 
+namespace q3 {
+namespace {
+constexpr int64_t kPrefetchPiece = 32 << 10;
+
+// Brings a byte range into L2 with bulk prefetches (no data is written
+// anywhere).  One thread per CTA issues its slice.  The kernel lets its
+// dependent start at once and completes only after its own predecessor, so
+// the stream's order holds for the kernel after it.
+__global__ void l2_prefetch_kernel(const uint8_t* base, int64_t bytes, int64_t chunk) {
+  pdl_launch();
+  const int64_t off = (int64_t)blockIdx.x * chunk;
+  if (threadIdx.x == 0 && off < bytes) {
+    const int64_t n = min64(chunk, bytes - off);
+    for (int64_t o = 0; o < n; o += kPrefetchPiece) {
+      const uint32_t sz = (uint32_t)min64(kPrefetchPiece, n - o);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off + o), "r"(sz)
+                   : "memory");
+    }
+  }
+  pdl_wait();
+}
+}  // namespace
+}  // namespace q3
+
+extern "C" int q3_l2_prefetch(const void* ptr, int64_t bytes, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(ptr, "q3_l2_prefetch: null pointer");
+  Q3_REQUIRE(bytes >= 0 && bytes % 16 == 0, "q3_l2_prefetch: bytes=%lld must be a multiple of 16",
+             (long long)bytes);
+  Q3_REQUIRE(aligned(ptr, 16), "q3_l2_prefetch: the range must start 16-byte aligned");
+  if (bytes == 0) return Q3_OK;
+  int64_t ctas = (bytes + kPrefetchPiece - 1) / kPrefetchPiece;
+  if (ctas > num_sms()) ctas = num_sms();
+  const int64_t chunk = ((bytes + ctas - 1) / ctas + 15) / 16 * 16;
+  ctas = (bytes + chunk - 1) / chunk;
+  return launch_ex(l2_prefetch_kernel, dim3((unsigned)ctas), dim3(32), 0, (cudaStream_t)stream,
+                   1, (const uint8_t*)ptr, bytes, chunk);
+}
+
 extern "C" int q3_lm_head_argmax(const void* hidden, const void* norm_w, float eps,
                                  const void* W_lm, int64_t rows, int64_t V, int64_t K,
                                  int64_t col_offset, void* logits_ws, int keys, int64_t* out,

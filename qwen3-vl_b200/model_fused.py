@@ -251,6 +251,9 @@ class Qwen3VLDecoderFused:
         self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
         # prefill attention on the tcgen05 tensor cores (opt-in until measured)
         self.prefill_tc = os.environ.get("Q3VL_PREFILL_TC", "0") == "1"
+        # decode: prefetch o_proj's weights into L2 while the attention kernel,
+        # which leaves HBM bandwidth idle, runs (opt-in until measured)
+        self.l2_prefetch_oproj = os.environ.get("Q3VL_L2_PREFETCH", "") == "oproj"
         self._step_plans = {}
         self._ss_step = None
         self._page_tables = {}
@@ -398,6 +401,8 @@ class Qwen3VLDecoderFused:
                                         eps=ab.eps)
         if S == 1:
             bound = kv_bound if kv_bound is not None else start_pos + 1
+            if self.l2_prefetch_oproj:
+                ops.l2_prefetch(L.o_proj.weight_km)
             if paged:
                 attn = ops.attn_decode_paged(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
                                              kv_cache[layer_idx].table, kv_len=bound,

@@ -102,6 +102,7 @@ SIGNATURES: dict[str, tuple] = {
     "q3_argmax_key": (I32, [P, I64, I64, I64, P, P]),
     "q3_argmax_key_index": (I32, [P, I64, P, P]),
     "q3_lm_head_argmax": (I32, [P, P, F32, P, I64, I64, I64, I64, P, I32, P, P]),
+    "q3_l2_prefetch": (I32, [P, I64, P]),
 }
 
 _lib = None

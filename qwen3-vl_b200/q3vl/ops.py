@@ -813,6 +813,14 @@ def lm_head_argmax(h: torch.Tensor, w_lm: torch.Tensor, norm_w: torch.Tensor = N
     return out
 
 
+def l2_prefetch(t: torch.Tensor) -> None:
+    """Prefetch a contiguous tensor's bytes into L2 (q3_l2_prefetch), ahead of
+    the kernel that reads it."""
+    _cuda("l2_prefetch", t)
+    _contig("l2_prefetch", t)
+    call("q3_l2_prefetch", _p(t), t.numel() * t.element_size(), _stream())
+
+
 def device_error(clear: bool = True) -> int:
     """Error code recorded by a kernel whose bounded wait timed out (0 = none)."""
     return int(_lib.raw("q3_device_error")(1 if clear else 0))

@@ -77,3 +77,39 @@ def test_init_comm_checks_rank_and_world():
         assert lib.q3_init_comm(comm, 0, 1, handle) == _lib.Q3_ERR_INVALID   # already open
     finally:
         lib.q3_comm_destroy(comm)
+
+
+def test_l2_prefetch_changes_no_result():
+    """q3_l2_prefetch writes nothing: eager and inside a graph, and the tiny
+    decoder with o_proj weights prefetched before each decode attention
+    generates the reference's golden tokens, with and without graphs."""
+    import loader_fused
+    from tests.golden import cases
+    from tests.helpers import load_golden
+    w = rnd(4096, 4096, seed=8)
+    before = w.clone()
+    ops.l2_prefetch(w)
+    ops.l2_prefetch(w[:1])
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.l2_prefetch(w)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(w, before)
+    name = "decoder_tiny_tp1"
+    gold = load_golden(name)
+    c = cases.DECODER_CASES[name]
+    s = c["spec"]
+    spec = loader_fused.TextSpec(hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads,
+                                 inter=s.inter, vocab=s.vocab, layers=s.layers,
+                                 rope_theta=s.rope_theta, eps=s.eps)
+    wt = cases.decoder_weights(name)
+    dec = loader_fused.build_decoder(wt["layers"], wt["embed"], wt["final_norm"], wt["lm_head"],
+                                     spec, 0, 1, DEV, c["max_seq"])
+    dec.l2_prefetch_oproj = True
+    ids = cases.decoder_prompt(name).to(DEV)
+    for graphs in (False, True):
+        dec.use_graphs = graphs
+        toks = dec.generate(ids, max_new_tokens=c["new_tokens"], eos_token_id=-1)
+        assert toks == gold["tokens"].tolist(), graphs
+    assert ops.device_error(clear=True) == 0

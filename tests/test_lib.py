@@ -112,6 +112,11 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     # ... and the projection's own checks still apply (V % 16)
     rc = lib.q3_lm_head_argmax(one, None, 1e-6, one, 4, 1000, 4096, 0, one, 0, one, None)
     assert rc == _lib.Q3_ERR_INVALID and b"multiple of 16" in lib.q3_last_error()
+    # L2 prefetch: 16-byte aligned start, whole 16-byte units
+    rc = lib.q3_l2_prefetch(one, 100, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"multiple of 16" in lib.q3_last_error()
+    rc = lib.q3_l2_prefetch(ctypes.c_void_p(24), 160, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"aligned" in lib.q3_last_error()
     # communicator set-up needs a communicator
     rc = lib.q3_init_comm(None, 0, 2, one)
     assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
