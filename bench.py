@@ -333,8 +333,9 @@ def run_ours(args):
                        "kv_cache": ("paged (256-token pages)" if kv_mode == "paged"
                                     else f"contiguous per batch, bucket {BUCKET}"),
                        "prefill_attention": "tcgen05" if dec.prefill_tc else "mma.sync",
-                       "l2_prefetch": "o_proj weights during decode attention"
-                       if dec.l2_prefetch_oproj else "none"},
+                       "l2_prefetch": "+".join(
+                           n for n, on in (("o_proj", dec.l2_prefetch_oproj),
+                                           ("next QKV", dec.l2_prefetch_qkv)) if on) or "none"},
             "prefill_tok_s": round(prefill_tps, 1), "decode_tok_s": round(decode_tps, 1),
             "decode_step_ms": round(dec_step_ms, 4),
             "decode_step_hbm": {"bytes": step_bytes, "achieved_gbs": round(step_gbs, 1),

@@ -251,9 +251,12 @@ class Qwen3VLDecoderFused:
         self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
         # prefill attention on the tcgen05 tensor cores (opt-in until measured)
         self.prefill_tc = os.environ.get("Q3VL_PREFILL_TC", "0") == "1"
-        # decode: prefetch o_proj's weights into L2 while the attention kernel,
-        # which leaves HBM bandwidth idle, runs (opt-in until measured)
-        self.l2_prefetch_oproj = os.environ.get("Q3VL_L2_PREFETCH", "") == "oproj"
+        # decode: weights brought into L2 while the attention kernel, which
+        # leaves HBM bandwidth idle, runs (opt-in until measured):
+        # "oproj" this layer's o_proj, "qkv" the next layer's QKV projection
+        pf = {t.strip() for t in os.environ.get("Q3VL_L2_PREFETCH", "").split(",") if t.strip()}
+        self.l2_prefetch_oproj = "oproj" in pf
+        self.l2_prefetch_qkv = "qkv" in pf
         self._step_plans = {}
         self._ss_step = None
         self._page_tables = {}
@@ -403,6 +406,8 @@ class Qwen3VLDecoderFused:
             bound = kv_bound if kv_bound is not None else start_pos + 1
             if self.l2_prefetch_oproj:
                 ops.l2_prefetch(L.o_proj.weight_km)
+            if self.l2_prefetch_qkv and layer_idx + 1 < self.num_layers:
+                ops.l2_prefetch(self.layers[layer_idx + 1].attn_block.qkv_weight_km)
             if paged:
                 attn = ops.attn_decode_paged(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
                                              kv_cache[layer_idx].table, kv_len=bound,
