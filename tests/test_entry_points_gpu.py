@@ -81,8 +81,9 @@ def test_init_comm_checks_rank_and_world():
 
 def test_l2_prefetch_changes_no_result():
     """q3_l2_prefetch writes nothing: eager and inside a graph, and the tiny
-    decoder with o_proj weights prefetched before each decode attention
-    generates the reference's golden tokens, with and without graphs."""
+    decoder with o_proj and next-layer QKV weights prefetched before each
+    decode attention generates the reference's golden tokens, with and
+    without graphs."""
     import loader_fused
     from tests.golden import cases
     from tests.helpers import load_golden
@@ -106,7 +107,7 @@ def test_l2_prefetch_changes_no_result():
     wt = cases.decoder_weights(name)
     dec = loader_fused.build_decoder(wt["layers"], wt["embed"], wt["final_norm"], wt["lm_head"],
                                      spec, 0, 1, DEV, c["max_seq"])
-    dec.l2_prefetch_oproj = True
+    dec.l2_prefetch_oproj = dec.l2_prefetch_qkv = True
     ids = cases.decoder_prompt(name).to(DEV)
     for graphs in (False, True):
         dec.use_graphs = graphs
