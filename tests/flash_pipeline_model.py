@@ -57,11 +57,25 @@ class Bar:
 
 
 class Wait:
+    """A parity wait for logical phase `phase`.  The hardware compares only
+    the parity of the barrier's current phase, so the wait is sound only
+    while the barrier has completed `phase` or `phase + 1` phases, i.e. the
+    completed count c stays in {phase, phase + 1} until the wait returns: at
+    c < phase the parity test would pass at once (premature), at c > phase + 1
+    it would block (lapped)."""
+
     def __init__(self, bar: Bar, phase: int, code):
         self.bar, self.phase, self.code = bar, phase, code
 
     def ready(self) -> bool:
         return self.bar.phase >= self.phase + 1
+
+    def hazard(self):
+        c = self.bar.phase
+        if c < self.phase:
+            return (f"waits for phase {self.phase} of {self.bar.name} while it has completed "
+                    f"{c} (the parity test would pass early)")
+        return None
 
 
 class NamedBarrier:
@@ -297,6 +311,11 @@ class Model:
         steps = 0
         while pending and steps < max_steps:
             steps += 1
+            for n, w in pending.items():
+                if isinstance(w, Wait):
+                    h = w.hazard()
+                    if h and h not in self.errors:
+                        self.errors.append(f"{n} {h}")
             runnable = [n for n, w in pending.items() if w is None or w.ready()]
             asyncs = [("tma", i) for i in range(len(self.tma))] + ([("pipe", 0)] if self.pipe else [])
             timed = [n for n, w in pending.items()
