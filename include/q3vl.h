@@ -290,13 +290,19 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
                     int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
                     const int64_t* q_strides, const int64_t* kv_strides, const int64_t* o_strides,
                     q3_stream_t stream);
-/* The same on the tcgen05 tensor cores (S and O accumulate in TMEM, softmax in
- * fp32 registers).  q contiguous [B, Hq, S, 128]; k/v [B, Hkv, kv_rows_per_head,
- * 128] (a cache with kv_rows_per_head >= start_pos + S rows per head); out
- * strides o_strides (b, h, s) in elements, multiples of 8. */
+/* The same on the tcgen05 tensor cores (S accumulates in TMEM, softmax in fp32).
+ * q contiguous [B, Hq, S, 128]; k/v [B, Hkv, kv_rows_per_head, 128] (a cache
+ * with kv_rows_per_head >= start_pos + S rows per head); out strides o_strides
+ * (b, h, s) in elements, multiples of 8.  variant 0: V is transposed in shared
+ * memory so every MMA operand is K-major, and each tile's P V is folded into
+ * fp32 registers; variant 1: V feeds the MMA as an MN-major operand and O
+ * accumulates in TMEM, rescaled only when a row's maximum grows by more than
+ * 2^8.  Cache rows past start_pos + S up to the next multiple of 64 are read
+ * with probability 0 and must hold finite values (variant 0 zeroes them). */
 Q3_API int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B, int Hq,
                        int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
-                       int64_t kv_rows_per_head, const int64_t* o_strides, q3_stream_t stream);
+                       int64_t kv_rows_per_head, const int64_t* o_strides, int variant,
+                       q3_stream_t stream);
 /* The same over paged K/V: k_pages, v_pages [num_pages, Hkv, page_tokens, 128];
  * key position t of sequence b is read from page block_table[b * table_stride
  * + t / page_tokens] (page_tokens a multiple of 64).  Keys 0..start_pos+S-1

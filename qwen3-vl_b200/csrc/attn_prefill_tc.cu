@@ -359,16 +359,298 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Variant 1: V read in place as an MN-major operand, O accumulated in TMEM.
+//   warp 0      TMA producer, as in variant 0;
+//   warp 1      MMA issuer: S_j = Q K_j^T into TMEM S[j&1]; O += P_j V_j into
+//               one TMEM accumulator across all tiles, with V_j taken straight
+//               from its TMA tile through an MN-major descriptor (rows of 64
+//               head dims per key, 1024-byte atoms of 8 keys; the two 64-dim
+//               boxes are the two MN blocks), so nothing is transposed;
+//   warps 2-5   softmax, row (warp % 4) * 32 + lane (TMEM lane quarter warp % 4).
+//               P_j is taken relative to a base that moves only when a row's
+//               maximum grows by more than 2^8 (P stays <= 256 between moves);
+//               when it moves, the warp rescales its rows of O in TMEM, after
+//               O_{j-1} has completed and before it releases P_j.
+// P[s] is reused two tiles later, after O of that tile completes: o_full[s]
+// counts the O MMAs of tiles with parity s, so each softmax wait is for the
+// next phase of one barrier (never two phases ahead).
+// TMEM: S at columns 0 / 64, O at 128..255 (256 allocated).
+constexpr int kMnThreads = 192;
+constexpr int kMnOffK = kQBytes;
+constexpr int kMnOffV = kMnOffK + 2 * kKVBytes;
+constexpr int kMnOffP = kMnOffV + 2 * kKVBytes;
+constexpr int kMnOffBar = kMnOffP + 2 * kPBytes;    // 131072
+constexpr int kMnSmem = kMnOffBar + 256 + 1024;
+constexpr uint32_t kMnTmemCols = 256;
+constexpr uint32_t kMnTmemO = 128;
+constexpr float kRescaleLog2 = 8.0f;
+
+// a bounded wait whose outcome every lane of the warp shares, so the
+// warp-collective tcgen05 loads and stores that follow stay converged
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
+}
+
+__global__ void __launch_bounds__(kMnThreads, 1)
+    attn_prefill_tc_mn_kernel(const __grid_constant__ CUtensorMap tmQ,
+                              const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, FlashParams p) {
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t s_base = smem_u32(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kMnOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;    // [2]
+  uint64_t* kv_empty = bar + 3;   // [2] MMA commit after O_j (S_j and O_j done)
+  uint64_t* s_full = bar + 5;     // [2]
+  uint64_t* p_full = bar + 7;     // [2] 128 softmax threads
+  uint64_t* o_full = bar + 9;     // [2] O MMAs of even / odd tiles
+  uint64_t* mma_done = bar + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int q0 = qb * kFM;
+  const int q_valid = min(kFM, p.S - q0);
+  const int64_t kv_total = p.start + p.S;
+  const int64_t kv_need = p.causal ? min64(p.start + q0 + kFM, kv_total) : kv_total;
+  const int n_kb = (int)((kv_need + kFN - 1) / kFN);
+  const int q_row0 = (int)(((int64_t)b * p.Hq + h) * p.q_rows_per_head + q0);
+  const int kv_row0 = (int)(((int64_t)b * p.Hkv + kvh) * p.kv_rows_per_head);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kMnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      tma_load_2d(smem, &tmQ, q_full, 0, q_row0, kCacheEvictNormal);
+      tma_load_2d(smem + kQBytes / 2, &tmQ, q_full, 64, q_row0, kCacheEvictNormal);
+      int issued = 0;
+      for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, 0x611)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* dk = smem + kMnOffK + s * kKVBytes;
+        uint8_t* dv = smem + kMnOffV + s * kKVBytes;
+        const int y = kv_row0 + j * kFN;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kKVBytes);
+        tma_load_2d(dk, &tmK, &kv_full[s], 0, y, kCacheEvictNormal);
+        tma_load_2d(dk + kKVBytes / 2, &tmK, &kv_full[s], 64, y, kCacheEvictNormal);
+        tma_load_2d(dv, &tmV, &kv_full[s], 0, y, kCacheEvictNormal);
+        tma_load_2d(dv + kKVBytes / 2, &tmV, &kv_full[s], 64, y, kCacheEvictNormal);
+        issued = j + 1;
+      }
+      // let the copies this thread issued land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, 0);
+      for (int j = max(0, issued - 2); j < issued; ++j)
+        mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kFM, kFN);
+      constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(kFM, kFD);
+      bool ok = mbar_wait(q_full, 0, p.err, 0x612);
+      tc_fence_after();
+      // S[(j)&1] is free: the softmax released P_{j-2} (read S_{j-2} first),
+      // which this thread waited for before issuing O_{j-2}
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.err, 0x613)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + s * kFN;
+#pragma unroll
+        for (int ks = 0; ks < kFD / 16; ++ks) {
+          const uint32_t qa = s_base + (ks >> 2) * (kQBytes / 2);
+          const uint32_t kb = s_base + kMnOffK + s * kKVBytes + (ks >> 2) * (kKVBytes / 2);
+          tc_mma_bf16(d, umma_desc_k_sw128(qa) + 2 * (ks & 3),
+                      umma_desc_k_sw128(kb) + 2 * (ks & 3), idesc_s, ks != 0);
+        }
+        tc_commit(&s_full[s]);
+        return true;
+      };
+      if (ok && n_kb > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kb && !*abort_flag; ++j) {
+        if (j + 1 < n_kb && !issue_s(j + 1)) { ok = false; break; }
+        const int s = j & 1;
+        if (!mbar_wait(&p_full[s], (j >> 1) & 1, p.err, 0x614)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = s_base + kMnOffP + s * kPBytes;
+        const uint32_t vb = s_base + kMnOffV + s * kKVBytes;
+#pragma unroll
+        for (int ks = 0; ks < kFN / 16; ++ks)
+          tc_mma_bf16(tmem + kMnTmemO, umma_desc_k_sw128(pa) + 2 * ks,
+                      umma_desc_mn_sw128(vb + ks * 2048, kKVBytes / 2, 1024), idesc_o,
+                      j > 0 || ks > 0);
+        tc_commit(&o_full[s]);
+        tc_commit(&kv_empty[s]);  // K_j and V_j consumed
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, 0);
+    }
+  } else {
+    // -------------------------------- softmax ---------------------------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int64_t qpos = p.start + q0 + row;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+      const int s = j & 1;
+      if (!warp_wait(&s_full[s], (j >> 1) & 1, p.err, 0x615)) { ok = false; break; }
+      tc_fence_after();
+      float sc[kFN];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld_32cols(tmem + lane_off + s * kFN + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(r[i]);
+        }
+      }
+      const int64_t kbase = (int64_t)j * kFN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kFN; ++c) {
+        const int64_t key = kbase + c;
+        float x = sc[c] * p.scale_log2;
+        if (key >= kv_total || (p.causal && key > qpos)) x = -INFINITY;
+        sc[c] = x;
+        mx = fmaxf(mx, x);
+      }
+      // P[s] was read by O_{j-2}
+      if (j >= 2 && !warp_wait(&o_full[s], ((j >> 1) - 1) & 1, p.err, 0x616)) {
+        ok = false;
+        break;
+      }
+      const float m_new = fmaxf(m_used, mx);
+      const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
+      const bool rescale = move && j > 0 && m_used != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O holds tiles 0..j-1 at the old base: wait for O_{j-1}, then scale
+        if (!warp_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, 0x617)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float corr = rescale ? exp2f(m_used - m_new) : 1.f;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < kFD / 32; ++c) {
+          const uint32_t a = tmem + lane_off + kMnTmemO + c * 32;
+          tmem_ld_32cols(a, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+          tmem_st_32cols(a, r);
+        }
+        tc_wait_st();
+      }
+      if (move) {
+        l *= exp2f(m_used - m_new);  // m_used = -inf: l is 0 and stays 0
+        m_used = m_new;
+      }
+      const float base = (m_used == -INFINITY) ? 0.f : m_used;
+      float rs = 0.f;
+      const uint32_t prow = s_base + kMnOffP + s * kPBytes;
+#pragma unroll
+      for (int c = 0; c < kFN; c += 8) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float p0 = exp2f(sc[c + e] - base), p1 = exp2f(sc[c + e + 1] - base);
+          rs += p0 + p1;
+          w4[e / 2] = pack_bf16x2(p0, p1);
+        }
+        sts128v(prow + sw128(row, c), w4[0], w4[1], w4[2], w4[3]);
+      }
+      l += rs;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[s]);
+    }
+    if (!ok) *abort_flag = 1;
+    // the last O MMA, then O / l to global memory
+    if (ok && !*abort_flag &&
+        warp_wait(&o_full[(n_kb - 1) & 1], ((n_kb - 1) >> 1) & 1, p.err, 0x618)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + b * p.os_b + h * p.os_h + (int64_t)(q0 + row) * p.os_s;
+      uint32_t r[32];
+#pragma unroll
+      for (int c = 0; c < kFD / 32; ++c) {
+        tmem_ld_32cols(tmem + lane_off + kMnTmemO + c * 32, r);
+        tc_wait_ld();
+        if (row < q_valid) {
+#pragma unroll
+          for (int d = 0; d < 32; d += 8) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(r[d + 4]) * inv, __uint_as_float(r[d + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(r[d + 6]) * inv, __uint_as_float(r[d + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + d) = u;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kMnTmemCols);
+  }
+}
+
 }  // namespace
 }  // namespace q3
 
 extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B,
                                   int Hq, int Hkv, int S, int head_dim, int64_t start_pos,
                                   int causal, float scale, int64_t kv_rows_per_head,
-                                  const int64_t* o_strides, q3_stream_t stream) {
+                                  const int64_t* o_strides, int variant, q3_stream_t stream) {
   using namespace q3;
   Q3_REQUIRE(q && k && v && out && o_strides, "q3_attn_prefill_tc: null pointer");
   Q3_REQUIRE(head_dim == kFD, "q3_attn_prefill_tc: head_dim must be 128 (got %d)", head_dim);
+  Q3_REQUIRE(variant == 0 || variant == 1, "q3_attn_prefill_tc: unknown variant %d", variant);
   Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && start_pos >= 0,
              "q3_attn_prefill_tc: bad shape B=%d S=%d Hq=%d Hkv=%d", B, S, Hq, Hkv);
   Q3_REQUIRE(kv_rows_per_head >= start_pos + S,
@@ -393,6 +675,8 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem));
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_mn_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kMnSmem));
     attr_set[dev] = true;
   }
   FlashParams p{};
@@ -406,6 +690,9 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_word();
   dim3 grid((S + kFM - 1) / kFM, Hq, B);
+  if (variant == 1)
+    return launch_ex(attn_prefill_tc_mn_kernel, grid, dim3(kMnThreads), kMnSmem,
+                     (cudaStream_t)stream, 1, tq, tk, tv, p);
   return launch_ex(attn_prefill_tc_kernel, grid, dim3(kFThreads), kFSmem, (cudaStream_t)stream,
                    1, tq, tk, tv, p);
 }

@@ -274,6 +274,23 @@ __device__ __forceinline__ void tmem_ld_32cols(uint32_t taddr, uint32_t (&r)[32]
       : "r"(taddr));
 }
 
+// Store 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 64 bf16, 8-row / 1024-byte swizzle atoms).
 // Bit layout: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46), version=1
@@ -287,6 +304,20 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   d |= (uint64_t)2u << 61;             // SWIZZLE_128B
   return d;
 }
+// The same for an MN-major operand with the 128-byte swizzle: each 128-byte
+// row holds 64 consecutive MN elements of one k, 8 k-rows form a 1024-byte
+// atom; `lbo` is the byte stride between 64-element blocks along MN, `sbo`
+// the byte stride between 8-row groups along K.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo,
+                                                       uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
 // Instruction descriptor: kind::f16, A=B=bf16, D=f32, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
   return (1u << 4)                      // D format f32
@@ -294,6 +325,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
          | (1u << 10)                   // B format bf16
          | ((uint32_t)(n >> 3) << 17)   // N / 8
          | ((uint32_t)(m >> 4) << 24);  // M / 16
+}
+// ... with B MN-major (the transpose-B bit).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) {
+  return umma_idesc_bf16(m, n) | (1u << 16);
 }
 
 // F.silu on a bf16 tensor (model_fused.py:169): computed in fp32, rounded to bf16.

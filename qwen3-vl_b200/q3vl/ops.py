@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -451,10 +452,15 @@ def attn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_pos
 
 
 def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_pos: int = 0,
-                    causal: bool = True, scale: float = None, out: torch.Tensor = None):
+                    causal: bool = True, scale: float = None, out: torch.Tensor = None,
+                    variant: int = None):
     """attn_prefill on the tcgen05 tensor cores.  q contiguous [B, Hq, S, 128];
     k/v [B, Hkv, rows, 128] contiguous with rows >= start_pos + S; out any
-    [B, Hq, S, 128] view whose strides are multiples of 8."""
+    [B, Hq, S, 128] view whose strides are multiples of 8.  variant 0 (V
+    transposed in shared memory) or 1 (V as an MN-major operand, O in TMEM);
+    default Q3VL_PREFILL_TC_VARIANT, else 0."""
+    if variant is None:
+        variant = int(os.environ.get("Q3VL_PREFILL_TC_VARIANT", "0"))
     _cuda("attn_prefill_tc", q, k, v, out)
     _bf16("attn_prefill_tc", q, k, v, out)
     _contig("attn_prefill_tc", q, k, v)
@@ -467,7 +473,8 @@ def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_
     if out is None:
         out = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device=q.device)
     call("q3_attn_prefill_tc", _p(q), _p(k), _p(v), _p(out), B, Hq, Hkv, S, D, int(start_pos),
-         1 if causal else 0, float(scale), rows, _strides_bhs(out, "out"), _stream())
+         1 if causal else 0, float(scale), rows, _strides_bhs(out, "out"), int(variant),
+         _stream())
     return out
 
 

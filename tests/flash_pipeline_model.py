@@ -144,8 +144,10 @@ class Model:
         self.tma.append((agent, buf, bar, nbytes, tag))
 
     def mma(self, reads, writes):
-        self._n += 1
-        agent = f"mma{self._n}"
+        # one agent: MMAs issued by the one MMA thread execute in issue order,
+        # so two of them never overlap on a buffer (the tags still check each
+        # one reads what it should)
+        agent = "tensor-pipe"
         for b, _ in reads:
             self.begin(agent, b, "r")
         for b, _ in writes:
@@ -295,14 +297,18 @@ class Model:
             self.abort = True
 
     # ------------------------------------------------------------ scheduler
-    def run(self, max_steps: int = 200000) -> str:
-        """Returns "done" or "deadlock" (roles blocked on a barrier without a
-        time limit).  Errors are collected in self.errors."""
+    def roles(self) -> dict:
         roles = {"producer": self.producer(), "mma": self.mma_issuer()}
         for w in range(2):
             roles[f"transposer{w}"] = self.transposer(w)
         for w in range(4):
             roles[f"softmax{w}"] = self.softmax(w)
+        return roles
+
+    def run(self, max_steps: int = 200000) -> str:
+        """Returns "done" or "deadlock" (roles blocked on a barrier without a
+        time limit).  Errors are collected in self.errors."""
+        roles = self.roles()
         pending = {}
         for name, g in roles.items():
             pending[name] = self._advance(g, None, name)
@@ -374,3 +380,129 @@ class Model:
             return gen.send(value) if value is not None else next(gen)
         except StopIteration:
             return "exit"
+
+
+class ModelMN(Model):
+    """Variant 1 of the kernel (attn_prefill_tc_mn_kernel): no transposers; V
+    feeds the O MMA in place; O accumulates in TMEM across tiles (each O MMA
+    reads the previous tile's O and writes its own); kv_empty takes one commit
+    after O_j; o_full[s] counts the O MMAs of tiles with parity s; a softmax
+    warp that moves its base (drawn at random here, `rescale_p`) waits for
+    O_{j-1} and rewrites its quarter of O before releasing P_j.  Softmax waits
+    are warp-uniform in the kernel, so one warp is one role."""
+
+    def __init__(self, n_kb: int, seed: int, fault_at=None, rescale_p: float = 0.3):
+        super().__init__(n_kb, seed, fault_at)
+        self.kv_empty = [Bar(f"kv_empty{i}", 1) for i in range(2)]
+        self.rescale_p = rescale_p
+        self.rescales = 0
+
+    def roles(self) -> dict:
+        roles = {"producer": self.producer(), "mma": self.mma_issuer()}
+        for w in range(4):
+            roles[f"softmax{w}"] = self.softmax(w)
+        return roles
+
+    def producer(self):
+        n_kb = self.n_kb
+        self.q_full.arrive_expect_tx(Q_BYTES)
+        self.tma_load("Q", self.q_full, Q_BYTES, "q")
+        yield None
+        issued = 0
+        for j in range(n_kb):
+            if self.abort:
+                break
+            s = j & 1
+            if j >= 2 and not (yield Wait(self.kv_empty[s], (j >> 1) - 1, 0x611)):
+                self.abort = True
+                break
+            self.kv_full[s].arrive_expect_tx(2 * KV_BYTES)
+            self.tma_load(f"K{s}", self.kv_full[s], KV_BYTES, j)
+            self.tma_load(f"V{s}", self.kv_full[s], KV_BYTES, j)
+            issued = j + 1
+            yield None
+        yield Wait(self.q_full, 0, None)
+        for j in range(max(0, issued - 2), issued):
+            yield Wait(self.kv_full[j & 1], j >> 1, None)
+
+    def mma_issuer(self):
+        n_kb = self.n_kb
+        ok = yield Wait(self.q_full, 0, 0x612)
+
+        def issue_s(j):
+            s = j & 1
+            if not (yield Wait(self.kv_full[s], j >> 1, 0x613)):
+                return False
+            self.mma([("Q", "q"), (f"K{s}", j)], [(f"S{s}.{w}", j) for w in range(4)])
+            self.commit(self.s_full[s])
+            return True
+
+        if ok and n_kb > 0:
+            ok = yield from issue_s(0)
+        j = 0
+        while ok and j < n_kb and not self.abort:
+            if j + 1 < n_kb and not (yield from issue_s(j + 1)):
+                ok = False
+                break
+            s = j & 1
+            if not (yield Wait(self.p_full[s], j >> 1, 0x614)):
+                ok = False
+                break
+            reads = [(f"P{s}.{w}", j) for w in range(4)] + [(f"V{s}", j)]
+            if j > 0:
+                reads += [(f"O.{w}", j - 1) for w in range(4)]
+            self.mma(reads, [(f"O.{w}", j) for w in range(4)])
+            self.commit(self.o_full[s])
+            self.commit(self.kv_empty[s])
+            j += 1
+            yield None
+        if not ok:
+            self.abort = True
+        self.commit(self.mma_done)
+        yield Wait(self.mma_done, 0, None)
+
+    def transposer(self, w):      # not in this variant
+        return iter(())
+
+    def softmax(self, w):
+        agent = f"softmax{w}"
+        n_kb = self.n_kb
+        ok = True
+        for j in range(n_kb):
+            if self.abort:
+                break
+            s = j & 1
+            if not (yield Wait(self.s_full[s], j >> 1, 0x615)):
+                ok = False
+                break
+            self.begin(agent, f"S{s}.{w}", "r")
+            self.check(agent, f"S{s}.{w}", j)
+            yield None
+            self.end(agent, f"S{s}.{w}", "r")
+            if j >= 2 and not (yield Wait(self.o_full[s], (j >> 1) - 1, 0x616)):
+                ok = False
+                break
+            if j > 0 and self.rng.random() < self.rescale_p:
+                if not (yield Wait(self.o_full[(j - 1) & 1], (j - 1) >> 1, 0x617)):
+                    ok = False
+                    break
+                self.rescales += 1
+                self.begin(agent, f"O.{w}", "w")
+                self.check(agent, f"O.{w}", j - 1)
+                yield None
+                self.end(agent, f"O.{w}", "w")
+            self.begin(agent, f"P{s}.{w}", "w")
+            self.mem[f"P{s}.{w}"] = j
+            yield None
+            self.end(agent, f"P{s}.{w}", "w")
+            self.p_full[s].arrive(32)
+        if not ok:
+            self.abort = True
+        if ok and not self.abort and n_kb > 0:
+            last = n_kb - 1
+            if (yield Wait(self.o_full[last & 1], last >> 1, 0x618)):
+                self.begin(agent, f"O.{w}", "r")
+                self.check(agent, f"O.{w}", last)
+                yield None
+                self.end(agent, f"O.{w}", "r")
+                self.seen[w] = list(range(n_kb))

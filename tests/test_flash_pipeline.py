@@ -5,7 +5,7 @@ buffer and no lapped barrier, and a wait that runs out ends the kernel with
 its error code and nothing in flight.  CPU only."""
 import pytest
 
-from tests.flash_pipeline_model import Model
+from tests.flash_pipeline_model import Model, ModelMN
 
 
 @pytest.mark.parametrize("n_kb", [1, 2, 3, 4, 5, 8, 13])
@@ -43,3 +43,33 @@ def test_the_named_barrier_handoff_could_hang_after_a_timeout():
     for seed in range(150):                          # without a fault it is fine too
         m = Model(4, seed, named_barrier=True)
         assert m.run() == "done" and m.errors == []
+
+
+@pytest.mark.parametrize("n_kb", [1, 2, 3, 4, 5, 8, 13])
+@pytest.mark.parametrize("rescale_p", [0.0, 0.3, 1.0])
+def test_mn_variant_delivers_each_tile_without_races(n_kb, rescale_p):
+    """Variant 1 (V in place, O accumulated in TMEM, lazy rescale): every O MMA
+    reads the previous tile's O, softmax rescales touch O only between two O
+    MMAs, P buffers are rewritten only after the O MMA that read them."""
+    rescaled = 0
+    for seed in range(150):
+        m = ModelMN(n_kb, seed, rescale_p=rescale_p)
+        assert m.run() == "done", (n_kb, seed)
+        assert m.errors == [], (n_kb, seed, m.errors[:3])
+        assert m.err == 0 and not m.abort
+        assert all(m.seen[w] == list(range(n_kb)) for w in range(4))
+        rescaled += m.rescales
+    assert rescaled > 0 or rescale_p == 0.0 or n_kb == 1
+
+
+@pytest.mark.parametrize("n_kb", [2, 3, 6])
+def test_mn_variant_ends_cleanly_after_a_timeout(n_kb):
+    codes = set()
+    for seed in range(300):
+        m = ModelMN(n_kb, seed, fault_at=1 + seed % 40)
+        assert m.run() == "done", (n_kb, seed)
+        assert m.errors == [], (n_kb, seed, m.errors[:3])
+        if m.err:
+            codes.add(m.err)
+            assert 0x611 <= m.err <= 0x618
+    assert len(codes) >= 3, sorted(hex(c) for c in codes)

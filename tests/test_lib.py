@@ -74,10 +74,16 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     # tcgen05 prefill attention: the cache must hold the prompt's positions
     strides = (ctypes.c_int64 * 3)(8 * 128 * 100, 128, 8 * 128)
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 128, 50, 1, 0.1, 120, strides,
-                                None)
+                                0, None)
     assert rc == _lib.Q3_ERR_INVALID and b"rows per head" in lib.q3_last_error()
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 64, 0, 1, 0.1, 128, strides,
-                                None)
+                                0, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()
+    rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 128, 0, 1, 0.1, 128, strides,
+                                2, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"variant" in lib.q3_last_error()
+    rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 64, 0, 1, 0.1, 128, strides,
+                                1, None)
     assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()
     # paged attention: positions must stay inside the block table
     rc = lib.q3_attn_prefill_paged(one, one, one, one, 1, 8, 2, 100, 128, 200, 1, 0.1, strides,
