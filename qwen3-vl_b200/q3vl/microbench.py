@@ -90,6 +90,8 @@ def main(argv=None):
     ap.add_argument("--depth", type=int, default=27, help="vision: transformer blocks")
     ap.add_argument("--page", type=int, default=256, help="paged: tokens per page")
     ap.add_argument("--tc", action="store_true", help="prefill: the tcgen05 kernel")
+    ap.add_argument("--variant", type=int, default=0,
+                    help="prefill --tc: 0 V transposed in shared memory, 1 V MN-major, O in TMEM")
     ap.add_argument("--hf", action="store_true",
                     help="rope_index: also time transformers' get_rope_index on the host")
     a = ap.parse_args(argv)
@@ -149,10 +151,15 @@ def main(argv=None):
         k = torch.randn(a.B, a.Hkv, a.S, 128, device=dev).to(bf)
         v = torch.randn_like(k)
         out = torch.empty_like(q)
-        fn = ops.attn_prefill_tc if a.tc else ops.attn_prefill
+        if a.tc:
+            fn = lambda q_, k_, v_, out: ops.attn_prefill_tc(q_, k_, v_, out=out,  # noqa: E731
+                                                             variant=a.variant)
+        else:
+            fn = ops.attn_prefill
         ms = _time(lambda: fn(q, k, v, out=out), a.iters, a.warmup, flush)
         flops = 4.0 * a.B * a.Hq * a.S * a.S * 128 / 2
-        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, S=a.S, tc=a.tc, ms=ms, tflops=flops / ms / 1e9)
+        res.update(B=a.B, Hq=a.Hq, Hkv=a.Hkv, S=a.S, tc=a.tc, variant=a.variant if a.tc else None,
+                   ms=ms, tflops=flops / ms / 1e9)
     else:
         x = torch.randn(a.rows, a.hidden, device=dev).to(bf)
         w = torch.ones(a.hidden, dtype=bf, device=dev)
