@@ -333,6 +333,9 @@ def run_ours(args):
                        "kv_cache": ("paged (256-token pages)" if kv_mode == "paged"
                                     else f"contiguous per batch, bucket {BUCKET}"),
                        "prefill_attention": "tcgen05" if dec.prefill_tc else "mma.sync",
+                       "prefill_allreduce": "two-shot over peer memory (q3_gemm_allreduce)"
+                       if getattr(dec, "pcomm", None) is not None else
+                       ("nccl" if args.gpus > 1 else "none"),
                        "l2_prefetch": "+".join(
                            n for n, on in (("o_proj", dec.l2_prefetch_oproj),
                                            ("next QKV", dec.l2_prefetch_qkv)) if on) or "none"},

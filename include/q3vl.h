@@ -432,6 +432,35 @@ Q3_API int q3_init_comm(void* comm, int rank, int world, const void* all_handles
 Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
                       const void* residual, float* ss_out, void* comm, q3_stream_t stream);
 
+/* ---- a10/a11 + 8(e), prefill shapes: projection + two-shot all-reduce -----
+ * Replaces `x @ W`, dist.all_reduce(SUM) and the residual add of forward_layer
+ * (model_fused.py:265-269, :272-275) for calls of many tokens.  The output
+ * rows are split into one stripe of 128-row tiles per rank; the tcgen05 GEMM's
+ * epilogue writes each bf16 partial tile into the owning rank's receive
+ * stripe over NVLink (reduce-scatter, overlapped with the MMAs of later
+ * tiles); each rank then sums its stripe in rank order (fp32, rounded to
+ * bf16), adds the residual, and pulls the other stripes from their owners
+ * (all-gather).  C = residual + sum over ranks of (A W^T), identical bits on
+ * every rank.  Every rank must make the same calls in the same order.
+ *   q3_prefill_comm_create  allocates this rank's exchange buffer, sized for
+ *                           calls of up to max_rows x max_cols outputs
+ *                           (max_cols a multiple of 32), and writes its IPC
+ *                           handle (q3_comm_handle_bytes() bytes);
+ *   q3_prefill_comm_open    maps every peer's buffer (the world's handles
+ *                           concatenated in rank order);
+ *   q3_gemm_allreduce       A bf16 [M, K], W bf16 [N, K] K-major (this rank's
+ *                           row shard), C / residual bf16 [M, N]; 16 < M <=
+ *                           max_rows, N % 32 == 0, K % 32 == 0; residual may
+ *                           be NULL.  A peer that never delivers ends the wait
+ *                           after a bounded time with Q3_ERR_TIMEOUT codes
+ *                           0x701 / 0x702 in the device error word. */
+Q3_API int q3_prefill_comm_create(int rank, int world, int64_t max_rows, int64_t max_cols,
+                                  void** comm_out, void* ipc_handle_out);
+Q3_API int q3_prefill_comm_open(void* comm, const void* all_handles);
+Q3_API int q3_prefill_comm_destroy(void* comm);
+Q3_API int q3_gemm_allreduce(const void* A, const void* W, void* C, int64_t M, int64_t N,
+                             int64_t K, const void* residual, void* comm, q3_stream_t stream);
+
 /* ---- a12/a13: the whole decode step of every layer in one launch ----------
  * Replaces forward_layer (model_fused.py:234-277) at S = 1 for all layers of
  * decode_step (model_fused.py:295-300): input RMSNorm, QKV projection,

@@ -145,6 +145,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // kernel unwind instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// System-scope release store / acquire load of a 32-bit flag (peer memory).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void report_timeout(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

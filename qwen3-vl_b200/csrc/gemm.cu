@@ -49,6 +49,12 @@ constexpr int kEpiQkvRope = 16;
 // The same with the K/V rows written into a page pool through a block table.
 constexpr int kEpiQkvRopePaged = 17;
 
+// Internal epilogue id of the prefill all-reduce's first half: the bf16
+// partial tile goes over NVLink into the receive stripe of the rank that owns
+// its rows, and each epilogue warp then publishes a flag for its 32 rows.
+constexpr int kEpiPushStripe = 18;
+constexpr int kPushMaxRanks = 8;
+
 // Bias epilogues of nn.Linear (the vision tower's linears): v = bf16(acc + b)
 // -- one rounding, as a linear with bias computes -- then Q3_EPI_BIAS_GELU_TANH
 // bf16(gelu_tanh(v)), Q3_EPI_BIAS_GELU bf16(gelu_erf(v)), or
@@ -110,6 +116,19 @@ __device__ __forceinline__ int64_t kv_row(const TcQkv& q, int b, int hkv, int64_
   }
 }
 
+// kEpiPushStripe: rows [o * stripe, (o + 1) * stripe) belong to rank o; this
+// rank's partial of row r lands at recv[o] + (r - o * stripe) * N and the
+// flag of (m-tile mt, n-tile nt, epilogue warp w) at flags[o] + (mt * n_tiles +
+// nt) * 4 + w, set to `call`
+// once the warp's rows are stored (the owner's receive region and flag array
+// for this source rank and this call's parity).
+struct TcPush {
+  __nv_bfloat16* recv[kPushMaxRanks];
+  uint32_t* flags[kPushMaxRanks];
+  int stripe;
+  uint32_t call;
+};
+
 struct TcParams {
   __nv_bfloat16* C;
   const __nv_bfloat16* R;
@@ -119,6 +138,7 @@ struct TcParams {
   int group_m;  // 0: tiles in column order (M fastest); g > 0: grouped raster, g M-tiles per group
   int* err;
   TcQkv qkv;  // kEpiQkvRope only
+  TcPush push;  // kEpiPushStripe only
 };
 
 // 8 consecutive RoPE table entries (bf16 tables as RotaryEmbedding builds them;
@@ -277,7 +297,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tile_coords(p, tile, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, p.err, 0x104)) { *abort_flag = 1; break; }
+      bool got;
+      if constexpr (EPI == kEpiPushStripe)  // the warp stays converged for its flag
+        got = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, p.err, 0x104));
+      else
+        got = mbar_wait(&tfull[acc], acc_phase, p.err, 0x104);
+      if (!got) { *abort_flag = 1; break; }
       tc_fence_after();
       const int row = mt * kBM + row_in_tile;
       const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(sub * 32) << 16);
@@ -388,6 +413,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                   make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
             }
           }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      if constexpr (EPI == kEpiPushStripe) {
+        const TcPush& q = p.push;
+        const int owner = (mt * kBM) / q.stripe;
+        __nv_bfloat16* dst_row =
+            q.recv[owner] + (int64_t)(row - owner * q.stripe) * p.N + nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32cols(t_row + c * 32, r);
+          tc_wait_ld();
+          if (row < p.M && nt * BN + c * 32 + 32 <= p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(
+                  pack_bf16x2(__uint_as_float(r[8 * v]), __uint_as_float(r[8 * v + 1])),
+                  pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3])),
+                  pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5])),
+                  pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7])));
+          }
+        }
+        // the warp's 32 rows are out: publish them to the owner
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_system();
+          // keyed by (m-tile, n-tile), whatever order the tiles ran in
+          st_release_sys(q.flags[owner] + ((int64_t)mt * p.n_tiles + nt) * 4 + sub, q.call);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
@@ -520,7 +577,8 @@ static int gemm_group_m() {
 
 template <int BN, int EPI>
 static int launch_tc(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
-                     cudaStream_t s, const TcQkv* qkv = nullptr, const void* bias = nullptr) {
+                     cudaStream_t s, const TcQkv* qkv = nullptr, const void* bias = nullptr,
+                     const TcPush* push = nullptr) {
   using Cfg = TcCfg<BN>;
   CUtensorMap ta, tw;
   int rc = make_tmap_2d(&ta, A, M, K, kBM, kBK);
@@ -546,10 +604,27 @@ static int launch_tc(const void* A, const void* W, void* C, const void* R, int M
   p.group_m = gemm_group_m();
   p.err = device_error_word();
   p.qkv = qkv ? *qkv : TcQkv{};
+  p.push = push ? *push : TcPush{};
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   return launch_ex(gemm_tc_kernel<BN, EPI>, dim3(grid), dim3(kTcThreads), Cfg::kSmem, s, 1, ta,
                    tw, p);
+}
+
+// The partial-product GEMM of the prefill all-reduce (comm_prefill.cu): bf16
+// tiles pushed into the owners' receive stripes with per-warp flags.
+int launch_gemm_push(const void* A, const void* W, int M, int N, int K,
+                     __nv_bfloat16* const* recv, uint32_t* const* flags, int world, int stripe,
+                     uint32_t call, cudaStream_t s) {
+  TcPush push{};
+  for (int r = 0; r < world && r < kPushMaxRanks; ++r) {
+    push.recv[r] = recv[r];
+    push.flags[r] = flags[r];
+  }
+  push.stripe = stripe;
+  push.call = call;
+  return launch_tc<256, kEpiPushStripe>(A, W, nullptr, nullptr, M, N, K, s, nullptr, nullptr,
+                                        &push);
 }
 
 }  // namespace q3

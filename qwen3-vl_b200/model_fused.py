@@ -232,6 +232,7 @@ class Qwen3VLDecoderFused:
         self.q_dim = num_q_heads * head_dim
         self.scale = 1.0 / math.sqrt(head_dim)
         self.comm = None            # optional in-kernel all-reduce (q3vl.comm)
+        self.pcomm = None           # optional prefill two-shot all-reduce (q3vl.comm)
         self._graphs = {}
         self._kv_pool = {}
         self.use_graphs = os.environ.get("Q3VL_DECODE_GRAPHS", "1") != "0"
@@ -286,7 +287,23 @@ class Qwen3VLDecoderFused:
             from q3vl.comm import PeerComm
             self.comm = PeerComm(group=group, max_cols=max_cols, device=self.device)
             self._graphs.clear()
+        rows = os.environ.get("Q3VL_PREFILL_AR", "") == "peer"
+        if self.tp_size > 1 and rows and self.pcomm is None:
+            self.enable_prefill_allreduce(group=group)
         return self.comm
+
+    def enable_prefill_allreduce(self, group=None, max_rows: int = 8192):
+        """Switch prefill-shaped o_proj/down projections (16 < tokens <=
+        max_rows) to the two-shot all-reduce over NVLink peer memory
+        (q3_gemm_allreduce) in place of dist.all_reduce.  Collective: every
+        rank must call it.  Opt-in (Q3VL_PREFILL_AR=peer with
+        enable_peer_allreduce) until measured."""
+        if self.tp_size > 1 and self.pcomm is None:
+            from q3vl.comm import PrefillComm
+            hidden = self.layers[0].attn_block.input_norm_weight.numel()
+            self.pcomm = PrefillComm(group=group, max_rows=max_rows, max_cols=hidden,
+                                     device=self.device)
+        return self.pcomm
 
     def close(self):
         """Release captured graphs and the peer communicator (collective)."""
@@ -297,6 +314,9 @@ class Qwen3VLDecoderFused:
         if self.comm is not None:
             self.comm.close()
             self.comm = None
+        if self.pcomm is not None:
+            self.pcomm.close()
+            self.pcomm = None
 
     @property
     def _eps(self):
@@ -332,6 +352,9 @@ class Qwen3VLDecoderFused:
         T = B * S
         decode = T <= 16
         peer = self.tp_size > 1 and self.comm is not None and decode
+        # prefill: projection + two-shot all-reduce + residual in the library
+        two_shot = (self.tp_size > 1 and self.pcomm is not None and not decode and
+                    T <= self.pcomm.max_rows and H <= self.pcomm.max_cols and H % 32 == 0)
         # decode with per-tile sums of squares handed between projections: every
         # RMSNorm runs inside the projection that consumes it
         fast = (decode and (self.tp_size == 1 or peer) and ab.qkv_bias is None and
@@ -462,6 +485,8 @@ class Qwen3VLDecoderFused:
         elif peer:
             # o_proj partial all-reduced from inside the kernel, residual fused
             x2 = ops.gemm_ar(attn, L.o_proj.weight_km, self.comm, residual=x)
+        elif two_shot:
+            x2 = ops.gemm_allreduce(attn, L.o_proj.weight_km, self.pcomm, residual=x)
         else:
             part = ops.gemm(attn, L.o_proj.weight_km)
             self._all_reduce(part)
@@ -479,6 +504,8 @@ class Qwen3VLDecoderFused:
             return ops.gemm(act, mlp.down_weight_km, "residual", residual=x2), None
         if peer:
             return ops.gemm_ar(act, mlp.down_weight_km, self.comm, residual=x2), None
+        if two_shot:
+            return ops.gemm_allreduce(act, mlp.down_weight_km, self.pcomm, residual=x2), None
         part2 = ops.gemm(act, mlp.down_weight_km)
         self._all_reduce(part2)
         return x2, part2

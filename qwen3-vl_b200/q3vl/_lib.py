@@ -89,6 +89,10 @@ SIGNATURES: dict[str, tuple] = {
     "q3_comm_handle_bytes": (I32, []),
     "q3_comm_create": (I32, [I32, I32, I64, ctypes.POINTER(P), P]),
     "q3_comm_open_peers": (I32, [P, P]),
+    "q3_prefill_comm_create": (I32, [I32, I32, I64, I64, P, P]),
+    "q3_prefill_comm_open": (I32, [P, P]),
+    "q3_prefill_comm_destroy": (I32, [P]),
+    "q3_gemm_allreduce": (I32, [P, P, P, I64, I64, I64, P, P, P]),
     "q3_init_comm": (I32, [P, I32, I32, P]),
     "q3_comm_destroy": (I32, [P]),
     "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P, P]),

@@ -54,3 +54,46 @@ class PeerComm:
             dist.barrier(group=self.group)
             call("q3_comm_destroy", self._ptr)
             self._ptr = ctypes.c_void_p()
+
+
+class PrefillComm:
+    """The exchange buffers of the prefill all-reduce (q3_gemm_allreduce): one
+    IPC-shared device buffer per rank holding every source's receive stripe,
+    the reduced stripe and the flags, sized for calls of up to max_rows x
+    max_cols outputs.  Collective: every rank of `group` constructs it."""
+
+    def __init__(self, group=None, max_rows: int = 8192, max_cols: int = 4096, device=None):
+        if not dist.is_initialized():
+            raise RuntimeError("PrefillComm needs an initialised torch.distributed process group")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nb = int(lib.q3_comm_handle_bytes())
+        handle = (ctypes.c_char * nb)()
+        self._ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("q3_prefill_comm_create", self.rank, self.world, int(max_rows), int(max_cols),
+                 ctypes.byref(self._ptr), handle)
+        mine = torch.tensor(bytearray(handle.raw), dtype=torch.uint8)
+        mine = mine.to(self.device) if dist.get_backend(group) == "nccl" else mine
+        every = torch.empty(self.world * nb, dtype=torch.uint8, device=mine.device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        blob = bytes(every.cpu().numpy().tobytes())
+        with torch.cuda.device(self.device):
+            call("q3_prefill_comm_open", self._ptr, ctypes.c_char_p(blob))
+        dist.barrier(group=group)
+        self.max_rows, self.max_cols = max_rows, max_cols
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._ptr
+
+    def close(self):
+        if self._ptr is not None and self._ptr.value:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            call("q3_prefill_comm_destroy", self._ptr)
+            self._ptr = ctypes.c_void_p()

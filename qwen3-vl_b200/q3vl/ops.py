@@ -732,6 +732,28 @@ def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = Non
 # ----------------------------------------------------------------------------
 # embedding / argmax
 # ----------------------------------------------------------------------------
+def gemm_allreduce(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
+                   out: torch.Tensor = None) -> torch.Tensor:
+    """Prefill row-parallel projection + all-reduce (+ residual) in one call
+    (q3_gemm_allreduce): out = residual + sum over ranks of a @ w.T, with a
+    [M, K] (16 < M), w [N, K] this rank's K-major shard.  Collective."""
+    _cuda("gemm_allreduce", a, w, residual, out)
+    _bf16("gemm_allreduce", a, w, residual, out)
+    _contig("gemm_allreduce", a, w, residual, out)
+    K = a.shape[-1]
+    N = w.shape[0]
+    M = a.numel() // K
+    if w.shape[1] != K:
+        raise ValueError(f"gemm_allreduce: weight [N={N}, K={w.shape[1]}] does not match K={K}")
+    if residual is not None and residual.numel() != M * N:
+        raise ValueError("gemm_allreduce: residual must be [M, N]")
+    if out is None:
+        out = torch.empty(*a.shape[:-1], N, dtype=torch.bfloat16, device=a.device)
+    call("q3_gemm_allreduce", _p(a), _p(w), _p(out), M, N, K, _p(residual), comm.handle,
+         _stream())
+    return out
+
+
 def embed(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     _cuda("embed", ids, table, out)
     _bf16("embed", table, out)

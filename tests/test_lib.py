@@ -123,6 +123,16 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
     assert rc == _lib.Q3_ERR_INVALID and b"multiple of 16" in lib.q3_last_error()
     rc = lib.q3_l2_prefetch(ctypes.c_void_p(24), 160, None)
     assert rc == _lib.Q3_ERR_INVALID and b"aligned" in lib.q3_last_error()
+    # prefill all-reduce: a communicator, and column counts in whole 32-column chunks
+    rc = lib.q3_gemm_allreduce(one, one, one, 64, 4096, 4096, None, None, None)
+    assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
+    comm = ctypes.c_void_p()
+    blob = ctypes.create_string_buffer(64)
+    rc = lib.q3_prefill_comm_create(0, 2, 8192, 4100, ctypes.byref(comm), blob)
+    assert rc == _lib.Q3_ERR_INVALID and b"multiple of 32" in lib.q3_last_error()
+    rc = lib.q3_prefill_comm_create(2, 2, 8192, 4096, ctypes.byref(comm), blob)
+    assert rc == _lib.Q3_ERR_INVALID and b"rank 2 / world 2" in lib.q3_last_error()
+    assert not comm.value
     # communicator set-up needs a communicator
     rc = lib.q3_init_comm(None, 0, 2, one)
     assert rc == _lib.Q3_ERR_INVALID and b"null" in lib.q3_last_error()
