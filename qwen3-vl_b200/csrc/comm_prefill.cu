@@ -87,9 +87,9 @@ struct RsParams {
   int* err;
 };
 
-__device__ bool wait_flag(const uint32_t* f, uint32_t want, int* err, int code) {
-  if (ld_acquire_sys(f) == want) return true;
-  const uint64_t t0 = globaltimer_ns();
+// Spin until *f == want or the tile's deadline (one budget for all the flags
+// of a tile) passes.
+__device__ bool wait_flag(const uint32_t* f, uint32_t want, uint64_t t0, int* err, int code) {
   uint32_t spins = 0;
   while (ld_acquire_sys(f) != want) {
     if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -141,12 +141,13 @@ __global__ void __launch_bounds__(kRsThreads) rs_ag_kernel(RsParams p) {
     const int owner = r0 / p.stripe;
     if (threadIdx.x == 0) {
       bool ok = true;
+      const uint64_t t0 = globaltimer_ns();
       if (mine) {
         for (int src = 0; src < p.world && ok; ++src)
           for (int sub = 0; sub < 4 && ok; ++sub)
-            ok = wait_flag(p.pflag[src] + (int64_t)tile * 4 + sub, p.call, p.err, 0x701);
+            ok = wait_flag(p.pflag[src] + (int64_t)tile * 4 + sub, p.call, t0, p.err, 0x701);
       } else {
-        ok = wait_flag(p.rflag_peer[owner] + tile, p.call, p.err, 0x702);
+        ok = wait_flag(p.rflag_peer[owner] + tile, p.call, t0, p.err, 0x702);
       }
       go = ok;
     }
