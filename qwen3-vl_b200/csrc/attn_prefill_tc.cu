@@ -71,6 +71,13 @@ __device__ __forceinline__ uint32_t sw128(int row, int col) {
   return row * 128 + ((((col >> 3) ^ (row & 7)) & 7) << 4) + (col & 7) * 2;
 }
 
+// a bounded wait whose outcome every lane of the warp shares, so the
+// warp-collective instructions that follow (tcgen05 loads and stores,
+// __syncwarp) stay converged
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
+}
+
 struct FlashParams {
   __nv_bfloat16* out;
   int64_t os_b, os_h, os_s;
@@ -227,11 +234,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
   } else if (warp < 4) {
     // ----------------------------- V transposers ------------------------------
     const int t = threadIdx.x - 64;  // 0..63
-    for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+    for (int j = 0; j < n_kb; ++j) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // as a warp
       const int s = j & 1;
-      if (!mbar_wait(&kv_full[s], (j >> 1) & 1, p.err, 0x608)) { *abort_flag = 1; break; }
+      if (!warp_wait(&kv_full[s], (j >> 1) & 1, p.err, 0x608)) { *abort_flag = 1; break; }
       // VT[s] was last read by the MMA of tile j - 2
-      if (j >= 2 && !mbar_wait(&o_full[s], ((j >> 1) - 1) & 1, p.err, 0x609)) {
+      if (j >= 2 && !warp_wait(&o_full[s], ((j >> 1) - 1) & 1, p.err, 0x609)) {
         *abort_flag = 1;
         break;
       }
@@ -276,7 +284,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     bool ok = true;
     for (int j = 0; j < n_kb; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j >> 1) & 1, p.err, 0x60a)) { ok = false; break; }
+      if (!warp_wait(&s_full[s], (j >> 1) & 1, p.err, 0x60a)) { ok = false; break; }
       tc_fence_after();
       float sc[kFN];
       {
@@ -321,7 +329,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       l = l * corr + rs;
       m = mx;
       // fold O_j in, after rescaling the running sum to the new maximum
-      if (!mbar_wait(&o_full[s], (j >> 1) & 1, p.err, 0x60b)) { ok = false; break; }
+      if (!warp_wait(&o_full[s], (j >> 1) & 1, p.err, 0x60b)) { ok = false; break; }
       tc_fence_after();
       {
         uint32_t r[32];
@@ -386,11 +394,6 @@ constexpr uint32_t kMnTmemCols = 256;
 constexpr uint32_t kMnTmemO = 128;
 constexpr float kRescaleLog2 = 8.0f;
 
-// a bounded wait whose outcome every lane of the warp shares, so the
-// warp-collective tcgen05 loads and stores that follow stay converged
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
-}
 
 __global__ void __launch_bounds__(kMnThreads, 1)
     attn_prefill_tc_mn_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -530,7 +533,9 @@ __global__ void __launch_bounds__(kMnThreads, 1)
     const int64_t qpos = p.start + q0 + row;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+    for (int j = 0; j < n_kb; ++j) {
+      // the abort flag is read once per lane: leave the loop as a warp
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
       const int s = j & 1;
       if (!warp_wait(&s_full[s], (j >> 1) & 1, p.err, 0x615)) { ok = false; break; }
       tc_fence_after();
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(kMnThreads, 1)
     }
     if (!ok) *abort_flag = 1;
     // the last O MMA, then O / l to global memory
-    if (ok && !*abort_flag &&
+    if (__all_sync(0xffffffffu, ok && *abort_flag == 0) &&
         warp_wait(&o_full[(n_kb - 1) & 1], ((n_kb - 1) >> 1) & 1, p.err, 0x618)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
