@@ -190,6 +190,8 @@ def run_ours(args):
         if name in ("q3_attn_decode", "q3_attn_decode_paged") and ws_bytes(*a[4:9]) > 0:
             # split-K: + combine kernel
             n = 2
+        elif name == "q3_gemm_allreduce":
+            n = 2  # the pushing GEMM + the reduce/gather kernel
         counts["n"] += n
         return orig_call(name, *a)
 
