@@ -160,8 +160,10 @@ __global__ void __launch_bounds__(kRsThreads) rs_ag_kernel(RsParams p) {
           const int row = r0 + i / nvec, col = c0 + (i % nvec) * 8;
           const int64_t lo = (int64_t)(row - own_r0) * p.N + col;
           float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          // data written by peers: read at L2 (ld.global.cg), never from a
+          // line this SM may hold from an earlier call
           for (int src = 0; src < p.world; ++src)
-            add8(a, *reinterpret_cast<const uint4*>(p.recv[src] + lo));
+            add8(a, __ldcg(reinterpret_cast<const uint4*>(p.recv[src] + lo)));
           uint32_t o[4];
           if (p.R) {
             const uint4 ru = *reinterpret_cast<const uint4*>(p.R + (int64_t)row * p.N + col);
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_ag_kernel(RsParams p) {
             const int i = i0 + u * kRsThreads;
             if (i < total) {
               const int row = r0 + i / nvec, col = c0 + (i % nvec) * 8;
-              v[u] = *reinterpret_cast<const uint4*>(src + (int64_t)(row - o_r0) * p.N + col);
+              v[u] = __ldcg(reinterpret_cast<const uint4*>(src + (int64_t)(row - o_r0) * p.N + col));
             }
           }
 #pragma unroll
