@@ -297,8 +297,11 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
  * memory so every MMA operand is K-major, and each tile's P V is folded into
  * fp32 registers; variant 1: V feeds the MMA as an MN-major operand and O
  * accumulates in TMEM, rescaled only when a row's maximum grows by more than
- * 2^8.  Cache rows past start_pos + S up to the next multiple of 64 are read
- * with probability 0 and must hold finite values (variant 0 zeroes them). */
+ * 2^8; variant 2 is variant 1 with the V descriptor's two stride fields
+ * exchanged, kept as a diagnostic of their order (its results are wrong when
+ * variant 1's are right).  Cache rows past start_pos + S up to the next
+ * multiple of 64 are read with probability 0 and must hold finite values
+ * (variant 0 zeroes them). */
 Q3_API int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B, int Hq,
                        int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
                        int64_t kv_rows_per_head, const int64_t* o_strides, int variant,

@@ -101,3 +101,20 @@ def test_tc_prefill_variant1_rescales_on_growing_scores():
         out = ops.attn_prefill_tc(q.to(DEV), k.to(DEV), v.to(DEV), variant=variant).cpu()
         compare(f"growing scores, variant {variant}", out, want, max_abs=2e-2, min_cos=0.9999)
     assert ops.device_error(clear=True) == 0
+
+
+
+def test_variant1_descriptor_order_diagnostic():
+    """Variant 2 runs variant 1 with the V descriptor's MN and K stride fields
+    exchanged.  Exactly one of the two orders can be right; this records
+    which, so a failing variant 1 points straight at the field order."""
+    B, Hq, Hkv, S = 1, 4, 1, 256
+    q, k, v = rnd(B, Hq, S, 128, seed=40), rnd(B, Hkv, S, 128, seed=41), rnd(B, Hkv, S, 128, seed=42)
+    want = oref.causal_attention_fp32(q, k, v, 0).double().flatten()
+    cos = {}
+    for variant in (1, 2):
+        out = ops.attn_prefill_tc(q.to(DEV), k.to(DEV), v.to(DEV), variant=variant).cpu()
+        got = out.double().flatten()
+        cos[variant] = float(torch.nn.functional.cosine_similarity(got, want, dim=0))
+    assert sum(c >= 0.9999 for c in cos.values()) == 1, cos
+    assert cos[1] >= 0.9999, f"the swapped order matches: {cos}"
