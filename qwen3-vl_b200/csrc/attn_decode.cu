@@ -699,6 +699,18 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
 static void decode_split_plan_step(int B, int Hkv, int64_t max_kv_len, int step, int* splits,
                                    int* chunk);
 
+// Decode attention CTAs per SM the split plan may use (Q3VL_DECODE_SLOTS_PER_SM
+// = 1 or 2; unset: as many as are resident, at most 2), for sweeping the
+// split on a GPU without a rebuild.
+static int decode_slots_per_sm() {
+  static const int v = [] {
+    const char* e = getenv("Q3VL_DECODE_SLOTS_PER_SM");
+    const int x = e ? atoi(e) : 0;
+    return (x == 1 || x == 2) ? x : 0;
+  }();
+  return v;
+}
+
 static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_qkv = false,
                             bool paged = false) {
   void (*kern)(const CUtensorMap, const CUtensorMap, DecodeTcParams) = nullptr;
@@ -738,6 +750,8 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   // than the workspace was sized for (two CTAs per SM, 16-position chunks).
   int64_t slots = (int64_t)per_sm * num_sms();
   if (slots > 2 * (int64_t)num_sms()) slots = 2 * (int64_t)num_sms();
+  if (decode_slots_per_sm() > 0 && decode_slots_per_sm() <= per_sm)
+    slots = (int64_t)decode_slots_per_sm() * num_sms();
   const int64_t pairs = (int64_t)p.B * p.Hkv;
   const int64_t L = p.kv_len < 1 ? 1 : p.kv_len;
   int64_t sp = slots / pairs;
