@@ -65,8 +65,8 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "layer", "step", "rope_index", "vision", "paged",
-                                       "e2e_vision"])
+                                       "gemm_allreduce", "layer", "step", "rope_index", "vision",
+                                       "paged", "e2e_vision"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
@@ -105,6 +105,8 @@ def main(argv=None):
         return _e2e_vision(a)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
+    if a.kernel == "gemm_allreduce":
+        return _gemm_allreduce(a)
     if a.kernel == "layer":
         return _layer(a)
     if a.kernel == "step":
@@ -368,6 +370,68 @@ def _gemm_ar(a):
         t = torch.tensor([sorted(ts)[2]], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         res[name] = round(float(t), 2)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    comm.close()
+    dist.destroy_process_group()
+
+
+def _gemm_allreduce(a):
+    """Row-parallel prefill projection at TP=WORLD_SIZE (run under torchrun):
+    the tcgen05 GEMM alone, GEMM + NCCL all-reduce + residual add, and the
+    two-shot exchange started from the GEMM epilogue (q3_gemm_allreduce).
+    Median of 5 runs of `iters` calls, max over ranks.  The roofline of the
+    fused call is the slower of its FLOPs at the tensor peak and the bytes
+    each rank must send over NVLink, 2 * (world - 1) / world * M * N * 2 B
+    (reduce-scatter plus all-gather), at the link's bandwidth."""
+    import torch.distributed as dist
+
+    from q3vl.comm import PrefillComm
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev)
+    comm = PrefillComm(max_rows=a.M, max_cols=a.N, device=dev)
+    bf = torch.bfloat16
+    x = torch.randn(a.M, a.K, device=dev).to(bf)
+    w = (torch.randn(a.N, a.K, device=dev) * 0.02).to(bf)
+    r = torch.randn(a.M, a.N, device=dev).to(bf)
+    part = torch.empty(a.M, a.N, dtype=bf, device=dev)
+    out = torch.empty(a.M, a.N, dtype=bf, device=dev)
+
+    def plain():
+        ops.gemm(x, w, out=part)
+
+    def nccl():
+        ops.gemm(x, w, out=part)
+        dist.all_reduce(part)
+        ops.add(part, r, out=out)
+
+    def fused():
+        ops.gemm_allreduce(x, w, comm, residual=r, out=out)
+
+    res = {"kernel": "gemm_allreduce", "M": a.M, "N": a.N, "K": a.K, "world": world,
+           "nvlink_bytes_per_rank": 2 * (world - 1) * a.M * a.N * 2 // world}
+    for name, fn in (("gemm_us", plain), ("gemm_nccl_us", nccl), ("gemm_allreduce_us", fused)):
+        for _ in range(a.warmup):
+            fn()
+        ts = []
+        for _ in range(5):
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / a.iters)
+        t = torch.tensor([sorted(ts)[2]], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(float(t), 2)
+    res["device_error"] = ops.device_error(clear=True)
     if rank == 0:
         print(json.dumps(res), flush=True)
     comm.close()
