@@ -273,7 +273,13 @@ Q3_API int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const void*
  * requests needing more are rejected with Q3_ERR_INVALID.  All calls on a
  * device share that array, so calls that overlap on the GPU race; order them
  * on one stream.  The first call on a device looks up the array's address:
- * make it before any stream capture.  Allocates nothing. */
+ * make it before any stream capture.  That address is kept for the life of
+ * the process, so after a device reset (cudaDeviceReset) the library must be
+ * reloaded before this entry point is called again.  The split plan launches
+ * at most about two CTAs per SM, so on a 148-SM B200 the partials of any
+ * supported head ratio (1, 2, 4, 8) need at most about 2.5 MB: the 4 MiB limit
+ * binds only on GPUs with more SMs, or for shapes the kernels do not support.
+ * Allocates nothing. */
 Q3_API int q3_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                   void* out, int B, int Hq, int Hkv, int head_dim,
                                   int64_t kv_len, const int32_t* kv_len_dev, int64_t max_seq,
@@ -297,9 +303,7 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
  * memory so every MMA operand is K-major, and each tile's P V is folded into
  * fp32 registers; variant 1: V feeds the MMA as an MN-major operand and O
  * accumulates in TMEM, rescaled only when a row's maximum grows by more than
- * 2^8; variant 2 is variant 1 with the V descriptor's two stride fields
- * exchanged, kept as a diagnostic of their order (its results are wrong when
- * variant 1's are right).  Cache rows past start_pos + S up to the next
+ * 2^8; any other variant is rejected.  Cache rows past start_pos + S up to the next
  * multiple of 64 are read with probability 0 and must hold finite values
  * (variant 0 zeroes them). */
 Q3_API int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B, int Hq,
@@ -432,6 +436,24 @@ Q3_API int q3_comm_destroy(void* comm);
  * this rank and world size, then maps every peer's buffer as
  * q3_comm_open_peers does (all_handles: every rank's handle in rank order). */
 Q3_API int q3_init_comm(void* comm, int rank, int world, const void* all_handles);
+/* Peers reached without IPC (no counterpart in the reference, whose
+ * collectives go through torch.distributed): q3_comm_buffer returns this
+ * rank's exchange buffer and its size; q3_comm_attach_peer gives the
+ * communicator a device pointer to peer_rank's buffer that the caller mapped
+ * itself (one process driving several GPUs with peer access enabled, or
+ * memory shared by other means).  Once every peer has a buffer the
+ * communicator is open.  Attached buffers are not unmapped by
+ * q3_comm_destroy.
+ * q3_comm_set_wait_limit bounds every in-kernel wait on a peer's words
+ * (default 2 s, accepted range 1 ms .. 60 s); when it runs out the kernel
+ * records 0x501 in the device error word, stops waiting and completes, so a
+ * peer that never arrives surfaces on the host as Q3_ERR_TIMEOUT instead of
+ * a hang.  The partial results of such a call are undefined, and the
+ * communicator's call numbers are then out of step with its peers: destroy
+ * it and create a new one. */
+Q3_API int q3_comm_buffer(const void* comm, void** buffer_out, size_t* bytes_out);
+Q3_API int q3_comm_attach_peer(void* comm, int peer_rank, void* peer_buffer);
+Q3_API int q3_comm_set_wait_limit(void* comm, uint64_t wait_ns);
 Q3_API int q3_gemm_ar(const void* A, const void* W, void* C, int64_t M, int64_t N, int64_t K,
                       const void* residual, float* ss_out, void* comm, q3_stream_t stream);
 
@@ -461,6 +483,11 @@ Q3_API int q3_prefill_comm_create(int rank, int world, int64_t max_rows, int64_t
                                   void** comm_out, void* ipc_handle_out);
 Q3_API int q3_prefill_comm_open(void* comm, const void* all_handles);
 Q3_API int q3_prefill_comm_destroy(void* comm);
+/* As q3_comm_buffer / q3_comm_attach_peer / q3_comm_set_wait_limit, for the
+ * prefill exchange (its waits record 0x701 / 0x702 when they run out). */
+Q3_API int q3_prefill_comm_buffer(const void* comm, void** buffer_out, size_t* bytes_out);
+Q3_API int q3_prefill_comm_attach_peer(void* comm, int peer_rank, void* peer_buffer);
+Q3_API int q3_prefill_comm_set_wait_limit(void* comm, uint64_t wait_ns);
 Q3_API int q3_gemm_allreduce(const void* A, const void* W, void* C, int64_t M, int64_t N,
                              int64_t K, const void* residual, void* comm, q3_stream_t stream);
 

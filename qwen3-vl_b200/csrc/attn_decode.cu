@@ -918,7 +918,13 @@ extern "C" int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const v
 //    each other's partials: order them on one stream;
 //  * the first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current).  Make that first call
-//    before any stream capture on the device.
+//    before any stream capture on the device.  The address is kept for the
+//    life of the process: after cudaDeviceReset the module may load elsewhere,
+//    so reload the library before calling this entry point again;
+//  * the split plan launches at most 2 x SMs + B x Hkv CTAs, so the partials
+//    need at most (4 x SMs) x G x 520 bytes (G = Hq / Hkv <= 8): about 2.5 MB
+//    on a 148-SM B200.  The limit binds only on larger GPUs or for head ratios
+//    the kernels do not support.
 // ---------------------------------------------------------------------------
 #include <mutex>
 

@@ -89,8 +89,8 @@ struct FlashParams {
   float scale_log2;
   int* err;
   // variant 1's V descriptor strides: the byte stride between the two 64-dim
-  // blocks (MN) and between 8-key groups (K); variant 2 passes them swapped,
-  // as a diagnostic of the descriptor's field order
+  // blocks (MN, the descriptor's leading offset) and between 8-key groups (K,
+  // its stride offset)
   uint32_t v_mn_stride, v_k_stride;
 };
 
@@ -659,7 +659,7 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   using namespace q3;
   Q3_REQUIRE(q && k && v && out && o_strides, "q3_attn_prefill_tc: null pointer");
   Q3_REQUIRE(head_dim == kFD, "q3_attn_prefill_tc: head_dim must be 128 (got %d)", head_dim);
-  Q3_REQUIRE(variant >= 0 && variant <= 2, "q3_attn_prefill_tc: unknown variant %d", variant);
+  Q3_REQUIRE(variant == 0 || variant == 1, "q3_attn_prefill_tc: unknown variant %d", variant);
   Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && start_pos >= 0,
              "q3_attn_prefill_tc: bad shape B=%d S=%d Hq=%d Hkv=%d", B, S, Hq, Hkv);
   Q3_REQUIRE(kv_rows_per_head >= start_pos + S,
@@ -699,10 +699,10 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   p.scale_log2 = scale * 1.4426950408889634f;
   p.err = device_error_word();
   // V of one stage: two 64-dim boxes 8 KB apart (MN), 8-key groups 1 KB apart (K)
-  p.v_mn_stride = variant == 2 ? 1024u : (uint32_t)(kKVBytes / 2);
-  p.v_k_stride = variant == 2 ? (uint32_t)(kKVBytes / 2) : 1024u;
+  p.v_mn_stride = (uint32_t)(kKVBytes / 2);
+  p.v_k_stride = 1024u;
   dim3 grid((S + kFM - 1) / kFM, Hq, B);
-  if (variant >= 1)
+  if (variant == 1)
     return launch_ex(attn_prefill_tc_mn_kernel, grid, dim3(kMnThreads), kMnSmem,
                      (cudaStream_t)stream, 1, tq, tk, tv, p);
   return launch_ex(attn_prefill_tc_kernel, grid, dim3(kFThreads), kFSmem, (cudaStream_t)stream,

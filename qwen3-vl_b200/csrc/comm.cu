@@ -18,6 +18,7 @@ CommDev Comm::dev() const {
   d.rank = rank;
   d.world = world;
   d.max_tiles = max_tiles;
+  d.wait_ns = wait_ns;
   return d;
 }
 
@@ -97,13 +98,52 @@ extern "C" int q3_init_comm(void* comm, int rank, int world, const void* all_han
   return q3_comm_open_peers(comm, all_handles);
 }
 
+extern "C" int q3_comm_buffer(const void* comm, void** buffer_out, size_t* bytes_out) {
+  using namespace q3;
+  Q3_REQUIRE(comm && buffer_out, "q3_comm_buffer: null pointer");
+  const Comm* c = static_cast<const Comm*>(comm);
+  *buffer_out = c->local;
+  if (bytes_out) *bytes_out = c->bytes;
+  return Q3_OK;
+}
+
+extern "C" int q3_comm_attach_peer(void* comm, int peer_rank, void* peer_buffer) {
+  using namespace q3;
+  Q3_REQUIRE(comm && peer_buffer, "q3_comm_attach_peer: null pointer");
+  Comm* c = static_cast<Comm*>(comm);
+  Q3_REQUIRE(peer_rank >= 0 && peer_rank < c->world && peer_rank != c->rank,
+             "q3_comm_attach_peer: peer rank %d is not another rank of world %d", peer_rank,
+             c->world);
+  Q3_REQUIRE(!c->peers[peer_rank], "q3_comm_attach_peer: rank %d already has a buffer",
+             peer_rank);
+  Q3_REQUIRE(aligned(peer_buffer, 256), "q3_comm_attach_peer: buffer must be 256-byte aligned");
+  c->peers[peer_rank] = peer_buffer;
+  c->attached[peer_rank] = true;
+  bool all = true;
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && !c->peers[r]) all = false;
+  c->open = all;
+  return Q3_OK;
+}
+
+extern "C" int q3_comm_set_wait_limit(void* comm, uint64_t wait_ns) {
+  using namespace q3;
+  Q3_REQUIRE(comm, "q3_comm_set_wait_limit: null pointer");
+  Q3_REQUIRE(wait_ns >= kMinWaitNs && wait_ns <= kMaxWaitNs,
+             "q3_comm_set_wait_limit: %llu ns outside [%llu, %llu]",
+             (unsigned long long)wait_ns, (unsigned long long)kMinWaitNs,
+             (unsigned long long)kMaxWaitNs);
+  static_cast<Comm*>(comm)->wait_ns = wait_ns;
+  return Q3_OK;
+}
+
 extern "C" int q3_comm_destroy(void* comm) {
   using namespace q3;
   if (!comm) return Q3_OK;
   Comm* c = static_cast<Comm*>(comm);
   cudaDeviceSynchronize();
   for (int r = 0; r < kMaxRanks; ++r)
-    if (c->peers[r]) cudaIpcCloseMemHandle(c->peers[r]);
+    if (c->peers[r] && !c->attached[r]) cudaIpcCloseMemHandle(c->peers[r]);
   if (c->local) cudaFree(c->local);
   delete c;
   return Q3_OK;

@@ -31,6 +31,7 @@ struct CommDev {
   uint2* inbox[kMaxRanks];  // each rank's inbox (peer-mapped; own for rank)
   uint32_t* counters;       // this rank's per-tile call numbers
   int rank, world, max_tiles;
+  uint64_t wait_ns;         // bound of every wait on a peer's words
 };
 
 struct Comm {
@@ -40,8 +41,14 @@ struct Comm {
   void* peers[kMaxRanks] = {nullptr};  // opened IPC mappings (nullptr for self)
   int device = 0;
   bool open = false;
+  bool attached[kMaxRanks] = {false};  // peers set by q3_comm_attach_peer (not IPC)
+  uint64_t wait_ns = 2000000000ull;    // q3_comm_set_wait_limit
   CommDev dev() const;
 };
+
+// Range accepted for a communicator's wait limit: 1 ms .. 60 s.
+constexpr uint64_t kMinWaitNs = 1000000ull;
+constexpr uint64_t kMaxWaitNs = 60000000000ull;
 
 inline size_t comm_data_bytes(int max_tiles) {
   return (size_t)2 * kMaxRanks * max_tiles * kArWords * sizeof(uint2);

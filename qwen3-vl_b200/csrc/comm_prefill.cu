@@ -27,8 +27,8 @@
 // has finished reading the partials of call f, and an owner rewrites its
 // reduced stripe for f + 1 only after every source pushed f + 1, i.e. after
 // every rank finished gathering call f.  Buffers still alternate by call
-// parity, as a margin.  Every wait is bounded: after
-// kWaitLimitNs the kernel records 0x701 (partials) or 0x702 (reduced tiles)
+// parity, as a margin.  Every wait is bounded: after the
+// communicator's wait limit (2 s unless set) the kernel records 0x701 (partials) or 0x702 (reduced tiles)
 // in the device error word and skips the tile.  No TMA or bulk copy touches
 // peer memory: peer traffic is plain stores (epilogue) and loads (gather).
 #include <string.h>
@@ -57,8 +57,10 @@ struct PrefillComm {
   size_t off_recv = 0, off_red = 0, off_pflag = 0, off_rflag = 0, bytes = 0;
   char* local = nullptr;
   char* peers[kMaxRanks] = {nullptr};
+  bool attached[kMaxRanks] = {false};  // peers set by q3_prefill_comm_attach_peer (not IPC)
   bool open = false;
   uint32_t calls = 0;
+  uint64_t wait_ns = 2000000000ull;    // q3_prefill_comm_set_wait_limit
 
   char* base(int r) const { return r == rank ? local : peers[r]; }
   // recv[parity][src]: stripe_max x max_cols bf16
@@ -84,15 +86,17 @@ struct RsParams {
   const __nv_bfloat16* R;
   int M, N, stripe, n_tiles, world, rank;
   uint32_t call;
+  uint64_t wait_ns;  // the communicator's wait limit
   int* err;
 };
 
-// Spin until *f == want or the tile's deadline (one budget for all the flags
-// of a tile) passes.
-__device__ bool wait_flag(const uint32_t* f, uint32_t want, uint64_t t0, int* err, int code) {
+// Spin until *f == want or the tile's deadline (one budget of `limit` ns for
+// all the flags of a tile) passes.
+__device__ bool wait_flag(const uint32_t* f, uint32_t want, uint64_t t0, uint64_t limit, int* err,
+                          int code) {
   uint32_t spins = 0;
   while (ld_acquire_sys(f) != want) {
-    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit) {
       report_timeout(err, code);
       return false;
     }
@@ -145,9 +149,10 @@ __global__ void __launch_bounds__(kRsThreads) rs_ag_kernel(RsParams p) {
       if (mine) {
         for (int src = 0; src < p.world && ok; ++src)
           for (int sub = 0; sub < 4 && ok; ++sub)
-            ok = wait_flag(p.pflag[src] + (int64_t)tile * 4 + sub, p.call, t0, p.err, 0x701);
+            ok = wait_flag(p.pflag[src] + (int64_t)tile * 4 + sub, p.call, t0, p.wait_ns,
+                           p.err, 0x701);
       } else {
-        ok = wait_flag(p.rflag_peer[owner] + tile, p.call, t0, p.err, 0x702);
+        ok = wait_flag(p.rflag_peer[owner] + tile, p.call, t0, p.wait_ns, p.err, 0x702);
       }
       go = ok;
     }
@@ -291,13 +296,53 @@ extern "C" int q3_prefill_comm_open(void* comm, const void* all_handles) {
   return Q3_OK;
 }
 
+extern "C" int q3_prefill_comm_buffer(const void* comm, void** buffer_out, size_t* bytes_out) {
+  using namespace q3;
+  Q3_REQUIRE(comm && buffer_out, "q3_prefill_comm_buffer: null pointer");
+  const PrefillComm* c = static_cast<const PrefillComm*>(comm);
+  *buffer_out = c->local;
+  if (bytes_out) *bytes_out = c->bytes;
+  return Q3_OK;
+}
+
+extern "C" int q3_prefill_comm_attach_peer(void* comm, int peer_rank, void* peer_buffer) {
+  using namespace q3;
+  Q3_REQUIRE(comm && peer_buffer, "q3_prefill_comm_attach_peer: null pointer");
+  PrefillComm* c = static_cast<PrefillComm*>(comm);
+  Q3_REQUIRE(peer_rank >= 0 && peer_rank < c->world && peer_rank != c->rank,
+             "q3_prefill_comm_attach_peer: peer rank %d is not another rank of world %d",
+             peer_rank, c->world);
+  Q3_REQUIRE(!c->peers[peer_rank], "q3_prefill_comm_attach_peer: rank %d already has a buffer",
+             peer_rank);
+  Q3_REQUIRE(aligned(peer_buffer, 256),
+             "q3_prefill_comm_attach_peer: buffer must be 256-byte aligned");
+  c->peers[peer_rank] = static_cast<char*>(peer_buffer);
+  c->attached[peer_rank] = true;
+  bool all = true;
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && !c->peers[r]) all = false;
+  c->open = all;
+  return Q3_OK;
+}
+
+extern "C" int q3_prefill_comm_set_wait_limit(void* comm, uint64_t wait_ns) {
+  using namespace q3;
+  Q3_REQUIRE(comm, "q3_prefill_comm_set_wait_limit: null pointer");
+  Q3_REQUIRE(wait_ns >= kMinWaitNs && wait_ns <= kMaxWaitNs,
+             "q3_prefill_comm_set_wait_limit: %llu ns outside [%llu, %llu]",
+             (unsigned long long)wait_ns, (unsigned long long)kMinWaitNs,
+             (unsigned long long)kMaxWaitNs);
+  static_cast<PrefillComm*>(comm)->wait_ns = wait_ns;
+  return Q3_OK;
+}
+
 extern "C" int q3_prefill_comm_destroy(void* comm) {
   using namespace q3;
   if (!comm) return Q3_OK;
   PrefillComm* c = static_cast<PrefillComm*>(comm);
   cudaDeviceSynchronize();
   for (int r = 0; r < kMaxRanks; ++r)
-    if (c->peers[r]) cudaIpcCloseMemHandle(c->peers[r]);
+    if (c->peers[r] && !c->attached[r]) cudaIpcCloseMemHandle(c->peers[r]);
   if (c->local) cudaFree(c->local);
   delete c;
   return Q3_OK;
@@ -352,6 +397,7 @@ extern "C" int q3_gemm_allreduce(const void* A, const void* W, void* C, int64_t 
   rp.world = world;
   rp.rank = c->rank;
   rp.call = call;
+  rp.wait_ns = c->wait_ns;
   rp.err = device_error_word();
   int rc = launch_gemm_push(A, W, (int)M, (int)N, (int)K, recv, flags, world, stripe, call, s);
   if (rc) return rc;

@@ -471,11 +471,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 o[h * 4 + i / 2] = pack_bf16x2(silu_ref(g0) * u0, silu_ref(g1) * u1);
               }
             }
-            if (f0 + 16 <= p.ldc) {
-              uint4* dst = reinterpret_cast<uint4*>(p.C + (int64_t)row * p.ldc + f0);
-              dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-              dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-            }
+            // N is a multiple of 16, so the last chunk may hold one [gate 8 | up 8]
+            // pair (8 outputs) instead of two
+            uint4* dst = reinterpret_cast<uint4*>(p.C + (int64_t)row * p.ldc + f0);
+            if (f0 + 8 <= p.ldc) dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            if (f0 + 16 <= p.ldc) dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
           } else if constexpr (EPI == Q3_EPI_BIAS || EPI == Q3_EPI_BIAS_GELU_TANH ||
                                EPI == Q3_EPI_BIAS_GELU || EPI == Q3_EPI_BIAS_RESIDUAL) {
             const int col0 = nt * BN + c * 32;

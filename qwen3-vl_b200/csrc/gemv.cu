@@ -163,7 +163,7 @@ __device__ __forceinline__ void allreduce_tile(const GemvParams& p, int tile, in
           const uint64_t t0 = globaltimer_ns();
           uint32_t spins = 0;
           while ((v = ld_word_inbox(src)).y != f) {
-            if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+            if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > cm.wait_ns) {
               report_timeout(p.err, 0x501);
               gave_up = true;
               break;

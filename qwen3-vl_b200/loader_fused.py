@@ -147,19 +147,26 @@ def _head_dim(cfg) -> int:
 
 
 def load_model(model_path, rank, world_size, device, compile_backend='neuron'):
-    """loader_fused.py:38-237.  Returns (decoder, vision_model, processor, hf_model);
-    the random-init path returns (decoder, None, None, None)."""
+    """loader_fused.py:38-237.  Returns (decoder, vision_model, processor, hf_model).
+
+    model_path names a local Hugging Face checkpoint directory; a path that
+    does not exist raises FileNotFoundError, as from_pretrained does in the
+    reference (loader_fused.py:56-60).  Random-init weights are served only on
+    an explicit request: model_path "random" (seed 0) or "random:<seed>", which
+    returns (decoder, None, None, None)."""
     t0 = time.time()
-    if model_path is None or str(model_path).startswith("random") or \
-            not os.path.isdir(str(model_path)):
-        seed = 0
-        if model_path and str(model_path).startswith("random:"):
-            seed = int(str(model_path).split(":", 1)[1])
+    mp = "" if model_path is None else str(model_path)
+    if mp == "random" or mp.startswith("random:"):
+        seed = int(mp.split(":", 1)[1]) if ":" in mp else 0
         dec = random_decoder(QWEN3_VL_8B, rank, world_size, device, seed=seed)
         if rank == 0:
             print(f"[LOAD] random-init Qwen3-VL-8B text decoder, TP-{world_size}: "
                   f"{time.time() - t0:.1f}s")
         return dec, None, None, None
+    if not os.path.isdir(mp):
+        raise FileNotFoundError(
+            f"load_model: checkpoint directory {mp!r} does not exist (pass 'random' or "
+            f"'random:<seed>' for random-init weights)")
 
     from transformers import AutoModelForImageTextToText, AutoProcessor
     processor = AutoProcessor.from_pretrained(model_path)

@@ -96,6 +96,12 @@ SIGNATURES: dict[str, tuple] = {
     "q3_init_comm": (I32, [P, I32, I32, P]),
     "q3_comm_destroy": (I32, [P]),
     "q3_gemm_ar": (I32, [P, P, P, I64, I64, I64, P, P, P, P]),
+    "q3_comm_buffer": (I32, [P, ctypes.POINTER(P), ctypes.POINTER(SZ)]),
+    "q3_comm_attach_peer": (I32, [P, I32, P]),
+    "q3_comm_set_wait_limit": (I32, [P, ctypes.c_uint64]),
+    "q3_prefill_comm_buffer": (I32, [P, ctypes.POINTER(P), ctypes.POINTER(SZ)]),
+    "q3_prefill_comm_attach_peer": (I32, [P, I32, P]),
+    "q3_prefill_comm_set_wait_limit": (I32, [P, ctypes.c_uint64]),
     "q3_decode_step_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64,
                                     ctypes.POINTER(P)]),
     "q3_decode_step": (I32, [P, P, P, P, I64, P]),

@@ -48,6 +48,11 @@ class PeerComm:
     def handle(self) -> ctypes.c_void_p:
         return self._ptr
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Bound of each in-kernel wait on a peer (q3_comm_set_wait_limit;
+        1 ms .. 60 s, default 2 s)."""
+        call("q3_comm_set_wait_limit", self._ptr, int(seconds * 1e9))
+
     def close(self):
         if self._ptr is not None and self._ptr.value:
             torch.cuda.synchronize(self.device)
@@ -90,6 +95,11 @@ class PrefillComm:
     @property
     def handle(self) -> ctypes.c_void_p:
         return self._ptr
+
+    def set_wait_limit(self, seconds: float) -> None:
+        """Bound of each in-kernel wait on a peer (q3_prefill_comm_set_wait_limit;
+        1 ms .. 60 s, default 2 s)."""
+        call("q3_prefill_comm_set_wait_limit", self._ptr, int(seconds * 1e9))
 
     def close(self):
         if self._ptr is not None and self._ptr.value:

@@ -458,8 +458,7 @@ def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_
     k/v [B, Hkv, rows, 128] contiguous with rows >= start_pos + S; out any
     [B, Hq, S, 128] view whose strides are multiples of 8.  variant 0 (V
     transposed in shared memory) or 1 (V as an MN-major operand, O in TMEM);
-    2 is variant 1 with the V descriptor's stride fields exchanged (a
-    diagnostic); default Q3VL_PREFILL_TC_VARIANT, else 0."""
+    default Q3VL_PREFILL_TC_VARIANT, else 0."""
     if variant is None:
         variant = int(os.environ.get("Q3VL_PREFILL_TC_VARIANT", "0"))
     _cuda("attn_prefill_tc", q, k, v, out)
@@ -854,3 +853,23 @@ def l2_prefetch(t: torch.Tensor) -> None:
 def device_error(clear: bool = True) -> int:
     """Error code recorded by a kernel whose bounded wait timed out (0 = none)."""
     return int(_lib.raw("q3_device_error")(1 if clear else 0))
+
+
+# device error words of the peer exchanges' bounded waits: the decode
+# all-reduce (q3_gemm_ar) and the prefill two-shot exchange (partials, reduced
+# tiles)
+PEER_TIMEOUT_CODES = (0x501, 0x701, 0x702)
+
+
+def check_device_error(where: str = "") -> None:
+    """Read and clear the device error word; raise Q3Error if a kernel recorded
+    one: Q3_ERR_TIMEOUT for a peer exchange whose bounded wait ran out (a rank
+    that never delivered), Q3_ERR_CUDA for any other recorded code."""
+    code = device_error(clear=True)
+    if not code:
+        return
+    if code in PEER_TIMEOUT_CODES:
+        raise _lib.Q3Error(_lib.Q3_ERR_TIMEOUT, where or "device",
+                           f"a peer never delivered its partials (code {code:#x})")
+    raise _lib.Q3Error(_lib.Q3_ERR_CUDA, where or "device", f"kernel recorded error {code:#x}")
+

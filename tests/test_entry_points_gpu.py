@@ -1,8 +1,7 @@
 """The one-call entry points of the C ABI (q3_gate_up_swiglu, q3_lm_head_argmax,
 q3_init_comm) against the kernels they are made of: identical bits to
 q3_gemm / q3_gemm_norm with the SwiGLU epilogue, to q3_gemm_norm followed by
-q3_argmax / q3_argmax_key, and the communicator checks on one GPU.  Marked
-gpu_pending until their first GPU run."""
+q3_argmax / q3_argmax_key, and the communicator checks on one GPU."""
 import ctypes
 
 import pytest
@@ -11,7 +10,7 @@ import torch
 from q3vl import _lib, ops
 from tests.helpers import compare
 
-pytestmark = [pytest.mark.gpu, pytest.mark.gpu_pending]
+pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 BF16 = torch.bfloat16
 

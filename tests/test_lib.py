@@ -54,6 +54,13 @@ def test_invalid_arguments_are_rejected_on_the_host():
                               1, 8, 4, 1, 128, 60, None, 64, 1e-6, None)  # cache overflow
     assert rc == _lib.Q3_ERR_INVALID
     assert b"max_seq" in lib.q3_last_error()
+    # communicator set-up calls check their arguments before touching a device
+    for fn in ("q3_comm_set_wait_limit", "q3_prefill_comm_set_wait_limit"):
+        assert getattr(lib, fn)(None, 50_000_000) == _lib.Q3_ERR_INVALID
+    for fn in ("q3_comm_attach_peer", "q3_prefill_comm_attach_peer"):
+        assert getattr(lib, fn)(None, 1, one) == _lib.Q3_ERR_INVALID
+    for fn in ("q3_comm_buffer", "q3_prefill_comm_buffer"):
+        assert getattr(lib, fn)(None, None, None) == _lib.Q3_ERR_INVALID
 
 
 def test_fused_entry_points_reject_bad_arguments_on_the_host():
@@ -80,7 +87,7 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
                                 0, None)
     assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 128, 0, 1, 0.1, 128, strides,
-                                3, None)
+                                2, None)
     assert rc == _lib.Q3_ERR_INVALID and b"variant" in lib.q3_last_error()
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 64, 0, 1, 0.1, 128, strides,
                                 1, None)
@@ -155,6 +162,22 @@ def test_decode_workspace_sizing_is_host_only():
     f = _lib.raw("q3_attn_decode_workspace_bytes")
     assert f(1, 32, 8, 128, 1024) > 0
     assert f(0, 32, 8, 128, 1024) == 0
+
+
+def test_noalloc_bound_holds_for_supported_shapes():
+    """q3_attn_decode_noalloc keeps split-K partials in a 4 MiB built-in array.
+    Its need is the workspace q3_attn_decode asks for (same split plan).  With
+    no GPU the plan assumes a 148-SM B200: every supported shape stays under
+    the limit, so the entry point's refusal only matters on larger GPUs."""
+    f = _lib.raw("q3_attn_decode_workspace_bytes")
+    worst = 0
+    for B in (1, 2, 3, 4, 7, 8, 16, 32, 37, 64, 128, 256, 512):
+        for Hkv in (1, 2, 4, 8):
+            for G in (1, 2, 4, 8):
+                for L in (1, 63, 64, 1000, 1024, 2048, 8192, 32768, 262144):
+                    worst = max(worst, f(B, Hkv * G, Hkv, 128, L))
+    assert 0 < worst <= 4 << 20, worst
+    assert worst <= 4 * 148 * 8 * 520
 
 
 def test_ops_refuse_cpu_tensors():

@@ -98,3 +98,12 @@ def test_head_dim_comes_from_the_config(tmp_path, no_processor):
     ab = dec.layers[0].attn_block
     assert ab.head_dim == 128 and ab.num_q_heads == 4
     assert ab.qkv_weight.shape == (384, (4 + 2 * 2) * 128)
+
+
+def test_missing_checkpoint_raises_instead_of_serving_random_weights(tmp_path):
+    """A mistyped model path must fail, not quietly build a random-init model;
+    random weights come only from an explicit 'random' / 'random:<seed>'."""
+    with pytest.raises(FileNotFoundError, match="does not exist"):
+        loader_fused.load_model(str(tmp_path / "no_such_checkpoint"), 0, 1, "cpu")
+    with pytest.raises(FileNotFoundError):
+        loader_fused.load_model(None, 0, 1, "cpu")

@@ -151,7 +151,6 @@ def test_multimodal_generate_matches_transformers(graphs):
     assert toks == g["tokens"].tolist()
 
 
-@pytest.mark.gpu_pending
 @pytest.mark.parametrize("graphs", [True, False])
 def test_batched_multimodal_generate_with_per_sequence_deltas(graphs):
     """Two image prompts of one length but different layouts (rope deltas -30

@@ -1,13 +1,13 @@
 """Paged KV on the GPU: the page write and decode attention through a block
 table reproduce the contiguous cache path bit for bit (same kernel arithmetic,
-only the row addresses differ).  Marked gpu_pending until their first GPU run."""
+only the row addresses differ)."""
 import pytest
 import torch
 
 from q3vl import ops
 from q3vl.kv_pages import KVPagePool
 
-pytestmark = [pytest.mark.gpu, pytest.mark.gpu_pending]
+pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 BF16 = torch.bfloat16
 

@@ -7,8 +7,7 @@ process per GPU): every rank's output equals residual + sum of the ranks'
 partials (max-abs <= 3e-2 of the output scale, cosine >= 0.9999, fp32
 reference of bf16 partials), all ranks hold identical bits, including shapes
 where one rank owns no rows; and the TP2 tiny decoder with the two-shot
-prefill gives the reference's greedy tokens.  Marked gpu_pending until its
-first GPU run."""
+prefill gives the reference's greedy tokens."""
 import ctypes
 import os
 import socket
@@ -16,7 +15,7 @@ import socket
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu, pytest.mark.gpu_pending]
+pytestmark = pytest.mark.gpu
 BF16 = torch.bfloat16
 
 

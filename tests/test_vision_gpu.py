@@ -6,10 +6,7 @@ Tolerances, per test: bias-epilogue linears max-abs <= 6.25e-2 and cosine
 points; LayerNorm max-abs <= 3.2e-2; position embeddings bit-exact; RoPE
 max-abs <= 1.6e-2 (the cos/sin implementations may differ in the last fp32
 bit); attention max-abs <= 2e-2 and cosine >= 0.9999 against fp32 attention;
-whole tower cosine >= 0.999 on every output.
-
-Marked gpu_pending: these kernels run on a GPU for the first time under
-Q3VL_PENDING_GPU_TESTS=1, before the marker comes off."""
+whole tower cosine >= 0.999 on every output."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -20,7 +17,7 @@ from q3vl.vision_tower import VisionPlan, VisionTower
 from tests.golden import cases
 from tests.helpers import as_tensor, compare, load_golden
 
-pytestmark = [pytest.mark.gpu, pytest.mark.gpu_pending]
+pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 BF16 = torch.bfloat16
 
