@@ -35,10 +35,14 @@ QWEN3_VL_8B = Spec()
 
 
 def make_weights(spec: Spec, seed: int = 0, std: float = 0.02, random_norms: bool = False,
-                 n_layers: int | None = None):
+                 n_layers: int | None = None, on_layer=None):
     """HF-convention ([out, in]) seeded N(0, std) bf16 weights, drawn layer by
     layer (q, k, v, o, gate, up, down, norms), then embedding, final norm and
-    lm_head.  Norm weights are 1.0 unless random_norms (1 + N(0, 0.1))."""
+    lm_head.  Norm weights are 1.0 unless random_norms (1 + N(0, 0.1)).
+    on_layer(i, layer_dict), when given, receives each layer as soon as it is
+    drawn and its return value is kept in its place (a caller that shards the
+    layer keeps only its shard, so an 8B-shape model never sits whole in
+    memory); the draws, and so the weights, are the same either way."""
     g = torch.Generator().manual_seed(seed)
     H, I = spec.hidden, spec.inter
     qd, kd = spec.q_heads * D, spec.kv_heads * D
@@ -52,11 +56,12 @@ def make_weights(spec: Spec, seed: int = 0, std: float = 0.02, random_norms: boo
         return torch.ones(n, dtype=torch.bfloat16)
 
     layers = []
-    for _ in range(spec.layers if n_layers is None else n_layers):
-        layers.append(dict(
+    for i in range(spec.layers if n_layers is None else n_layers):
+        lw = dict(
             q=rn(qd, H), k=rn(kd, H), v=rn(kd, H), o=rn(H, qd),
             gate=rn(I, H), up=rn(I, H), down=rn(H, I),
-            input_norm=norm(H), post_norm=norm(H), q_norm=norm(D), k_norm=norm(D)))
+            input_norm=norm(H), post_norm=norm(H), q_norm=norm(D), k_norm=norm(D))
+        layers.append(lw if on_layer is None else on_layer(i, lw))
     embed = rn(spec.vocab, H)
     final_norm = norm(H)
     lm_head = rn(spec.vocab, H)

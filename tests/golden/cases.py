@@ -64,6 +64,61 @@ def layer8b_case(seed: int = 1):
     return dict(spec=spec, weights=w, hidden=hidden, hidden_dec=hidden_dec, S=8, max_seq=64)
 
 
+# ---- config 3: one Qwen3-VL-8B-shape layer at TP8 sharding ----
+# N(0, 0.02) bf16 weights (norms 1.0), hidden states N(0, 1): prefill of
+# 4 x 512 tokens, then 128 decode steps of 4 x 1 fresh N(0, 1) states.  The
+# fixture keeps a fingerprint of every output (the layer's contribution,
+# out - in, projected on 16 seeded directions) and a few whole rows.
+LAYER_TP8 = dict(seed=5, B=4, S=512, steps=128, tp=8, max_seq=1024, proj_dim=16,
+                 pre_tokens=(0, 1, 200, 511), dec_steps=(0, 64, 127))
+
+
+def layer_tp8_case():
+    c = LAYER_TP8
+    spec = odec.Spec(layers=1, vocab=16, max_seq=c["max_seq"])
+    w = odec.make_weights(spec, seed=c["seed"])
+    g = torch.Generator().manual_seed(c["seed"] + 100)
+    hidden = torch.randn(c["B"], c["S"], 4096, generator=g).to(BF16)
+    dec_in = torch.randn(c["steps"], c["B"], 1, 4096, generator=g).to(BF16)
+    return dict(spec=spec, weights=w, hidden=hidden, dec_in=dec_in)
+
+
+def fingerprint_matrix(dim: int = 16, hidden: int = 4096, seed: int = 999) -> torch.Tensor:
+    """Seeded directions [hidden, dim] (unit scale) for output fingerprints."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(hidden, dim, generator=g) / math.sqrt(hidden)
+
+
+def layer_fingerprint(out: torch.Tensor, inp: torch.Tensor, R: torch.Tensor) -> torch.Tensor:
+    """fp32 projection of a layer's contribution (out - in) on R's directions."""
+    return (out.float().cpu() - inp.float().cpu()) @ R
+
+
+# ---- config 4: the 36-layer Qwen3-VL-8B-shape decoder at TP8 sharding ----
+# N(0, 0.02) bf16 weights (norms 1.0) with a peaky lm_head, batch 8 prompts
+# of 1024 uniform random ids, greedy tokens over the first 32 steps.
+DECODER8B_TP8 = dict(seed=21, B=8, prompt_len=1024, new_tokens=32, tp=8, max_seq=2048, topk=8)
+
+
+def decoder8b_spec() -> "odec.Spec":
+    return odec.Spec(max_seq=DECODER8B_TP8["max_seq"])
+
+
+def decoder8b_weights(on_layer=None) -> dict:
+    """The config-4 weights (8B shape, 36 layers); on_layer as in
+    oracle.decoder.make_weights, so a rank can keep only its shards."""
+    c = DECODER8B_TP8
+    w = odec.make_weights(decoder8b_spec(), seed=c["seed"], on_layer=on_layer)
+    w["lm_head"] = peaky(w["lm_head"], c["seed"])
+    return w
+
+
+def decoder8b_prompt() -> torch.Tensor:
+    c = DECODER8B_TP8
+    g = torch.Generator().manual_seed(c["seed"] + 1)
+    return torch.randint(0, decoder8b_spec().vocab, (c["B"], c["prompt_len"]), generator=g)
+
+
 # ---- tiny full decoders (reference generate), TP1 and TP2 ----
 DECODER_CASES = {
     "decoder_tiny_tp1": dict(

@@ -1,0 +1,86 @@
+"""The 8B-shape workloads, through the drop-in API on one GPU, against
+fixtures the reference produced at TP8 (tests/golden/make_golden.py: eight
+gloo ranks running model_fused.Qwen3VLDecoderFused over shards made by
+loader_fused.shard_column / shard_row).
+
+Config 3: one Qwen3-VL-8B-shape layer, batch 4, a 512-token prefill of
+N(0, 1) hidden states, then 128 single-token decode steps.  The library runs
+the whole layer on one GPU (TP1); the reference's TP8 sum of bf16 partials
+rounds differently, which the tolerance covers.  Compared: the layer's
+contribution (out - in) projected on 16 seeded directions for every token of
+every call (max-abs <= 3e-2 of the fingerprint scale, cosine >= 0.9999), and
+whole output rows of a few tokens and steps (max-abs <= 5e-2 of the output
+scale, cosine >= 0.999).
+
+Config 4: the 36-layer decoder, batch 8, prompts of 1024 random ids, greedy
+tokens over the first 32 steps: identical token ids, and the prefill logits'
+top-8 ids equal with values within 5e-2 of their scale."""
+import pytest
+import torch
+
+import loader_fused
+from tests.golden import cases
+from tests.helpers import as_tensor, compare, load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _spec(s) -> loader_fused.TextSpec:
+    return loader_fused.TextSpec(hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads,
+                                 inter=s.inter, vocab=s.vocab, layers=s.layers,
+                                 rope_theta=s.rope_theta, eps=s.eps)
+
+
+def test_config3_layer_prefill_and_128_decode_steps_vs_reference_tp8():
+    cfg = cases.LAYER_TP8
+    g = load_golden("layer8b_tp8")
+    c = cases.layer_tp8_case()
+    w = c["weights"]
+    assert cases.weights_checksum(w) == float(g["weights_checksum"])
+    dec = loader_fused.build_decoder(w["layers"], w["embed"], w["final_norm"], w["lm_head"],
+                                     _spec(c["spec"]), 0, 1, DEV, cfg["max_seq"])
+    R = cases.fingerprint_matrix(cfg["proj_dim"])
+    kv = dec.init_kv_cache(cfg["B"])
+    pre = dec.forward_layer(c["hidden"].to(DEV), 0, kv, 0, cfg["S"]).cpu()
+    steps = [dec.forward_layer(c["dec_in"][i].to(DEV), 0, kv, cfg["S"] + i, 1).cpu()
+             for i in range(cfg["steps"])]
+    steps = torch.stack(steps)
+    compare("config 3 prefill fingerprint", cases.layer_fingerprint(pre, c["hidden"], R),
+            as_tensor(g["pre_fp"]), max_abs=3e-2, rel_scale=True, min_cos=0.9999)
+    compare("config 3 prefill rows", pre[:, list(cfg["pre_tokens"])],
+            as_tensor(g["pre_rows"]), max_abs=5e-2, rel_scale=True, min_cos=0.999)
+    compare("config 3 decode fingerprint", cases.layer_fingerprint(steps, c["dec_in"], R),
+            as_tensor(g["dec_fp"]), max_abs=3e-2, rel_scale=True, min_cos=0.9999)
+    compare("config 3 decode rows", steps[list(cfg["dec_steps"])],
+            as_tensor(g["dec_rows"]), max_abs=5e-2, rel_scale=True, min_cos=0.999)
+    # every decode step on its own (a wrong position or cache row shows in one step)
+    fp = cases.layer_fingerprint(steps, c["dec_in"], R)
+    want = as_tensor(g["dec_fp"])
+    for i in range(cfg["steps"]):
+        compare(f"config 3 decode step {i}", fp[i], want[i], max_abs=3e-2, rel_scale=True,
+                min_cos=0.999)
+
+
+def test_config4_decoder_greedy_tokens_vs_reference_tp8():
+    cfg = cases.DECODER8B_TP8
+    g = load_golden("decoder8b_tp8")
+    # weights drawn layer by layer on the host and moved to the GPU at once
+    w = cases.decoder8b_weights(on_layer=lambda i, lw: {k: v.to(DEV) for k, v in lw.items()})
+    checksum = float(w["embed"].double().abs().sum() + w["lm_head"].double().abs().sum())
+    assert checksum == float(g["embed_lm_checksum"])
+    dec = loader_fused.build_decoder(w["layers"], w["embed"], w["final_norm"], w["lm_head"],
+                                     _spec(cases.decoder8b_spec()), 0, 1, DEV, cfg["max_seq"])
+    del w
+    ids = cases.decoder8b_prompt().to(DEV)
+    logits = dec.prefill(ids, dec.init_kv_cache(ids.shape[0]))[:, -1, :].float().cpu()
+    top = torch.topk(logits, cfg["topk"], dim=-1)
+    want_ids = torch.from_numpy(g["prefill_top_ids"])
+    assert torch.equal(top.indices[:, 0], want_ids[:, 0]), (top.indices[:, 0], want_ids[:, 0])
+    compare("config 4 prefill top logits", top.values, torch.from_numpy(g["prefill_top_vals"]),
+            max_abs=5e-2, rel_scale=True)
+    toks = dec.generate_tokens(ids, cfg["new_tokens"], eos_token_id=None).cpu()
+    want = torch.from_numpy(g["tokens"])
+    assert toks.shape == want.shape, (toks.shape, want.shape)
+    mism = (toks != want).nonzero().tolist()
+    assert not mism, f"greedy tokens differ at (row, step) {mism[:8]}"
