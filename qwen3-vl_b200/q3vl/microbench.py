@@ -68,6 +68,8 @@ def main(argv=None):
                                        "gemm_allreduce", "layer", "step", "rope_index", "vision",
                                        "paged", "e2e_vision"])
     ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="layer: time one rank's shard at this tensor-parallel degree")
     ap.add_argument("--bucket", type=int, default=2048)
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=24576)
@@ -200,9 +202,24 @@ def _layer(a):
 
     import loader_fused
     dev = torch.device("cuda:0")
-    NL = 4
+    # with --tp N: one rank's shard of each layer (4N layers cycled, so the
+    # weights still exceed L2); the all-reduce projections run as q3_gemm_ar
+    # on a single-rank communicator (the kernel and its epilogue, no peers)
+    NL = 4 * a.tp
     spec = dataclasses.replace(loader_fused.QWEN3_VL_8B, layers=NL)
-    dec = loader_fused.random_decoder(spec, 0, 1, dev, seed=0, max_seq=a.bucket)
+    dec = loader_fused.random_decoder(spec, 0, a.tp, dev, seed=0, max_seq=a.bucket)
+    comm = None
+    if a.tp > 1:
+        import ctypes
+
+        from . import _lib
+
+        class _Solo:
+            handle = ctypes.c_void_p()
+        comm = _Solo()
+        nb = int(_lib.load().q3_comm_handle_bytes())
+        _lib.call("q3_comm_create", 0, 1, spec.hidden, ctypes.byref(comm.handle),
+                  (ctypes.c_char * nb)())
     B, L, H = a.B, a.L, spec.hidden
     kv = dec._kv_for(B, a.bucket)
     for k, v in kv:
@@ -248,6 +265,9 @@ def _layer(a):
                                        kv_len_dev=kv_len, out=attn, workspace=ws)
 
     def k_o(i):
+        if comm is not None:
+            return lambda: ops.gemm_ar(attn.view(B, -1), dec.layers[i].o_proj.weight_km, comm,
+                                       residual=x, ss_out=ss0, out=x2)
         return lambda: ops.gemm_decode(attn.view(B, -1), dec.layers[i].o_proj.weight_km,
                                        "residual", residual=x, ss_out=ss0, out=x2)
 
@@ -257,10 +277,17 @@ def _layer(a):
                                        eps=m.eps, ss_in=ss0, ss_tiles=H // 64, out=act)
 
     def k_down(i):
+        if comm is not None:
+            return lambda: ops.gemm_ar(act, dec.layers[i].mlp_block.down_weight_km, comm,
+                                       residual=x2, ss_out=ss1, out=y)
         return lambda: ops.gemm_decode(act, dec.layers[i].mlp_block.down_weight_km, "residual",
                                        residual=x2, ss_out=ss1, out=y)
 
     def k_layer(i):
+        if comm is not None:
+            # the rank's six launches back to back (no exchange with peers)
+            fs = [k(i) for k in (k_qkv, k_rope, k_attn, k_o, k_gu, k_down)]
+            return lambda: [f() for f in fs]
         return lambda: dec._layer(x, None, i, kv, 0, 1, B, pos_dev=pos, kv_len_dev=kv_len,
                                   kv_bound=a.bucket, ss_valid=True)
 
@@ -268,7 +295,8 @@ def _layer(a):
              gate_up=mlp0.gate_up_weight_il.numel() * 2,
              down=mlp0.down_weight_km.numel() * 2,
              attention=2 * B * ab0.num_kv_heads * L * 128 * 2)
-    res = {"kernel": "layer", "B": B, "L": L, "bucket": a.bucket, "us": {}, "gbs": {}}
+    res = {"kernel": "layer", "tp": a.tp, "B": B, "L": L, "bucket": a.bucket, "us": {},
+           "gbs": {}}
     tot = 0.0
     for name, mk in (("qkv", k_qkv), ("qkv_norm_rope", k_rope), ("attention", k_attn),
                      ("o_proj", k_o), ("gate_up", k_gu), ("down", k_down)):
