@@ -141,7 +141,7 @@ def run_ours(args):
     # Q3VL_BENCH_KV=paged: the KV cache of every generate step lives in a page
     # pool (256-token pages, one slot per batch row) instead of contiguous
     # per-batch caches
-    kv_mode = os.environ.get("Q3VL_BENCH_KV", "contiguous")
+    kv_mode = os.environ.get("Q3VL_BENCH_KV", "paged")
     gen_kw = {}
     if kv_mode == "paged":
         from q3vl.kv_pages import KVPagePool

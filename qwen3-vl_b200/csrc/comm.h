@@ -32,6 +32,7 @@ struct CommDev {
   uint32_t* counters;       // this rank's per-tile call numbers
   int rank, world, max_tiles;
   uint64_t wait_ns;         // bound of every wait on a peer's words
+  int early_dependents;     // let the next kernel launch once the weights are consumed
 };
 
 struct Comm {

@@ -564,12 +564,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side: launch
 // ---------------------------------------------------------------------------
-// Tile raster of the tcgen05 GEMM: Q3VL_GEMM_GROUP_M=g (g > 0) selects the
-// grouped order; unset or 0 keeps the column order.
+// Tile raster of the tcgen05 GEMM: groups of 32 M-tiles swept across every
+// N-tile (measured on B200 for 8192 x 6144 x 4096: 1333 TFLOP/s against 1250
+// in column order, whose waves re-read A from DRAM).  Q3VL_GEMM_GROUP_M=g
+// sets another group size; 0 selects the column order.
 static int gemm_group_m() {
   static const int g = [] {
     const char* e = getenv("Q3VL_GEMM_GROUP_M");
-    const int v = e ? atoi(e) : 0;
+    const int v = e ? atoi(e) : 32;
     return v > 0 ? v : 0;
   }();
   return g;

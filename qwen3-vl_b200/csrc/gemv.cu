@@ -404,6 +404,12 @@ __global__ void __launch_bounds__(gv_threads(FL)) gemv_tma_kernel(
   const uint32_t crank = cluster_ctarank();
   if (csize > 1) cluster_sync_all();
   else __syncthreads();
+  // All-reduce epilogue with early dependents: this CTA's weight stream is
+  // done, so the next kernel may launch and start its own weight stream
+  // while this one exchanges partials with its peers.
+  if constexpr (EPI == kEpiAllReduce) {
+    if (p.comm.early_dependents) pdl_launch();
+  }
   if (crank == 0 && warp < kGvConsumers) {
     const int g = lane >> 2, t = lane & 3;
     float v[NT * 4];
@@ -583,13 +589,25 @@ int launch_gemv(const void* A, const void* W, void* C, const void* R, int M, int
   }
 }
 
+// Q3VL_AR_EARLY_PDL=1: the all-reduce projection lets its dependent kernel
+// launch once its own weights are consumed, before the exchange with peers.
+static int ar_early_dependents() {
+  static const int on = [] {
+    const char* v = getenv("Q3VL_AR_EARLY_PDL");
+    return (v && v[0] == '1') ? 1 : 0;
+  }();
+  return on;
+}
+
 int launch_gemv_ar(const void* A, const void* W, void* C, const void* R, int M, int N, int K,
                    float* ss_out, const CommDev& comm, cudaStream_t s) {
   if (M < 1 || M > 16) return fail(Q3_ERR_INVALID, "decode projection needs 1 <= M <= 16");
   GemvOpts o;
   o.ss_out = ss_out;
-  return M > 8 ? launch_gemv_t<2, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o)
-               : launch_gemv_t<1, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &comm, o);
+  CommDev cd = comm;
+  cd.early_dependents = ar_early_dependents();
+  return M > 8 ? launch_gemv_t<2, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &cd, o)
+               : launch_gemv_t<1, kEpiAllReduce, 0>(A, W, C, R, M, N, K, s, &cd, o);
 }
 
 }  // namespace q3

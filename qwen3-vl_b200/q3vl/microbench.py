@@ -212,7 +212,7 @@ def _layer(a):
     if a.tp > 1:
         import ctypes
 
-        from . import _lib
+        from q3vl import _lib
 
         class _Solo:
             handle = ctypes.c_void_p()

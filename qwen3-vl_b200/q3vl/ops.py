@@ -458,9 +458,9 @@ def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_
     k/v [B, Hkv, rows, 128] contiguous with rows >= start_pos + S; out any
     [B, Hq, S, 128] view whose strides are multiples of 8.  variant 0 (V
     transposed in shared memory) or 1 (V as an MN-major operand, O in TMEM);
-    default Q3VL_PREFILL_TC_VARIANT, else 0."""
+    default Q3VL_PREFILL_TC_VARIANT, else 1 (the faster on B200)."""
     if variant is None:
-        variant = int(os.environ.get("Q3VL_PREFILL_TC_VARIANT", "0"))
+        variant = int(os.environ.get("Q3VL_PREFILL_TC_VARIANT", "1"))
     _cuda("attn_prefill_tc", q, k, v, out)
     _bf16("attn_prefill_tc", q, k, v, out)
     _contig("attn_prefill_tc", q, k, v)

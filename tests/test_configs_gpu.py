@@ -13,8 +13,11 @@ whole output rows of a few tokens and steps (max-abs <= 5e-2 of the output
 scale, cosine >= 0.999).
 
 Config 4: the 36-layer decoder, batch 8, prompts of 1024 random ids, greedy
-tokens over the first 32 steps: identical token ids, and the prefill logits'
-top-8 ids equal with values within 5e-2 of their scale."""
+tokens over the first 32 steps, the lm_head made peaky so most steps have a
+clear winner: teacher-forced argmax equal to the reference's at every step
+whose top-2 margin exceeds 2 % of the top logit, top logits within 3e-2 of
+their scale after the prefill, and free-running greedy tokens identical up to
+each row's first near-tie step."""
 import pytest
 import torch
 
@@ -63,6 +66,13 @@ def test_config3_layer_prefill_and_128_decode_steps_vs_reference_tp8():
 
 
 def test_config4_decoder_greedy_tokens_vs_reference_tp8():
+    """Teacher-forced: after the prefill, every decode step is fed the
+    reference's token, so each of the 8 x 32 steps is compared on its own.
+    Where the reference's top-2 logits are further apart than the tolerance
+    (2 % of the top logit: the two bf16 all-reduce orders may move a logit
+    by about that much), the argmax must be the reference's token.  Then
+    free-running greedy generation must give the reference's tokens in every
+    row up to that row's first near-tie step."""
     cfg = cases.DECODER8B_TP8
     g = load_golden("decoder8b_tp8")
     # weights drawn layer by layer on the host and moved to the GPU at once
@@ -73,14 +83,28 @@ def test_config4_decoder_greedy_tokens_vs_reference_tp8():
                                      _spec(cases.decoder8b_spec()), 0, 1, DEV, cfg["max_seq"])
     del w
     ids = cases.decoder8b_prompt().to(DEV)
-    logits = dec.prefill(ids, dec.init_kv_cache(ids.shape[0]))[:, -1, :].float().cpu()
-    top = torch.topk(logits, cfg["topk"], dim=-1)
-    want_ids = torch.from_numpy(g["prefill_top_ids"])
-    assert torch.equal(top.indices[:, 0], want_ids[:, 0]), (top.indices[:, 0], want_ids[:, 0])
-    compare("config 4 prefill top logits", top.values, torch.from_numpy(g["prefill_top_vals"]),
-            max_abs=5e-2, rel_scale=True)
-    toks = dec.generate_tokens(ids, cfg["new_tokens"], eos_token_id=None).cpu()
-    want = torch.from_numpy(g["tokens"])
-    assert toks.shape == want.shape, (toks.shape, want.shape)
-    mism = (toks != want).nonzero().tolist()
-    assert not mism, f"greedy tokens differ at (row, step) {mism[:8]}"
+    B, P = ids.shape
+    T = cfg["new_tokens"]
+    want = torch.from_numpy(g["tokens"])                       # [B, T]
+    vals = torch.from_numpy(g["top_vals"])                     # [B, T, k]
+    clear = (vals[:, :, 0] - vals[:, :, 1]) > 0.02 * vals[:, :, 0].abs()   # [B, T]
+    got = torch.empty(B, T, dtype=torch.long)
+    kv = dec.init_kv_cache(B)
+    logits = dec.prefill(ids, kv)[:, -1, :].float()
+    got[:, 0] = logits.argmax(-1).cpu()
+    compare("config 4 prefill top logit", logits.max(-1).values.cpu(), vals[:, 0, 0],
+            max_abs=3e-2, rel_scale=True)
+    for i in range(T - 1):
+        tok = want[:, i].to(DEV).view(B, 1)
+        logits = dec.forward(tok, P + i, kv)[:, -1, :].float()
+        got[:, i + 1] = logits.argmax(-1).cpu()
+    bad = ((got != want) & clear).nonzero().tolist()
+    assert not bad, f"argmax differs from the reference at clear (row, step) {bad[:8]}"
+    assert clear.float().mean() > 0.8, "too few clear steps for the check to mean anything"
+    # free-running greedy generation through the decode graph
+    toks = dec.generate_tokens(ids, T, eos_token_id=None).cpu()
+    for b in range(B):
+        ties = (~clear[b]).nonzero()
+        n = int(ties[0]) if len(ties) else T
+        assert torch.equal(toks[b, :n], want[b, :n]), \
+            f"row {b}: greedy tokens differ before its first near-tie step {n}"
