@@ -649,6 +649,311 @@ __global__ void __launch_bounds__(kMnThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Variant 2: two query tiles per CTA, 128-key tiles, P kept in TMEM.
+//   One CTA holds the same 128 query rows of two heads that share a KV head
+//   (G = Hq / Hkv even), so both tiles read the same K/V tiles and masks.
+//   warp 0      TMA producer: Q (two heads x two 128x64 boxes), then K_j and
+//               V_j (128 keys x two 64-dim boxes each) into 2-deep K and V
+//               rings.  The K/V maps are 3-D (dim, key, head) and end at the
+//               last valid key, so keys past it arrive as zeros;
+//   warp 1      MMA issuer (one thread), alternating between the tiles:
+//               S_0(0), S_0(1), then for each j: PV_j(0), S_{j+1}(0), PV_j(1),
+//               S_{j+1}(1), where S_j(t) = Q_t K_j^T (M=128, N=128, K=128)
+//               goes to TMEM S[t] and PV_j(t) accumulates P_j(t) V_j into
+//               TMEM O[t], with P read from TMEM (it overwrites the first 64
+//               columns of S[t], two bf16 per column) and V as an MN-major
+//               shared-memory operand.  While one tile's softmax runs, the
+//               tensor core works on the other tile;
+//   warps 2-5   softmax of tile 0, warps 6-9 of tile 1; row 32 (warp % 4) +
+//               lane, the warp's TMEM lane quarter.  P_j = 2^(s - m) against a
+//               base m that moves only when a row's maximum grows by more
+//               than 2^8; when it moves, the row of O[t] is rescaled in TMEM.
+//               The commit of S_j(t) also covers PV_{j-1}(t), issued before
+//               it, so O[t] is complete when S_j(t) is.  Finally O / l.
+// TMEM (512 columns): S[0] 0..127, S[1] 128..255, O[0] 256..383, O[1] 384..511.
+constexpr int kPpThreads = 320;           // 10 warps
+constexpr int kPpN = 128;                 // keys per tile
+constexpr int kPpQBytes = kFM * kFD * 2;  // 32 KB per query tile
+constexpr int kPpKVBytes = kPpN * kFD * 2;  // 32 KB per K or V tile
+constexpr int kPpHalf = kPpKVBytes / 2;   // one 64-dim box of 128 keys
+constexpr int kPpOffK = 2 * kPpQBytes;
+constexpr int kPpOffV = kPpOffK + 2 * kPpKVBytes;
+constexpr int kPpOffBar = kPpOffV + 2 * kPpKVBytes;  // 196608
+constexpr int kPpSmem = kPpOffBar + 256 + 1024;
+constexpr uint32_t kPpTmemCols = 512;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kPpThreads, 1)
+    attn_prefill_tc_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
+                              const __grid_constant__ CUtensorMap tmK,
+                              const __grid_constant__ CUtensorMap tmV, FlashParams p) {
+  pdl_wait();
+  pdl_launch();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t s_base = smem_u32(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kPpOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* k_full = bar + 1;    // [2]
+  uint64_t* k_empty = bar + 3;   // [2] MMA commit after S_j of both tiles
+  uint64_t* v_full = bar + 5;    // [2]
+  uint64_t* v_empty = bar + 7;   // [2] MMA commit after PV_j of both tiles
+  uint64_t* s_full = bar + 9;    // [tile] S_j(t) (and PV_{j-1}(t)) complete
+  uint64_t* p_full = bar + 11;   // [tile] P_j(t) in TMEM: one arrival per softmax warp
+  uint64_t* o_final = bar + 13;  // [tile] the last PV of the tile complete
+  uint64_t* mma_done = bar + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int h0 = 2 * blockIdx.y, b = blockIdx.z;
+  const int kvh = h0 / (p.Hq / p.Hkv);
+  const int q0 = qb * kFM;
+  const int q_valid = min(kFM, p.S - q0);
+  const int64_t kv_total = p.start + p.S;
+  const int64_t kv_need = p.causal ? min64(p.start + q0 + kFM, kv_total) : kv_total;
+  const int n_kb = (int)((kv_need + kPpN - 1) / kPpN);
+  const int kv_plane = b * p.Hkv + kvh;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_final[i], 1);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kPpTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kPpQBytes);
+      for (int t = 0; t < 2; ++t) {
+        const int qrow = (int)(((int64_t)b * p.Hq + h0 + t) * p.q_rows_per_head + q0);
+        tma_load_2d(smem + t * kPpQBytes, &tmQ, q_full, 0, qrow, kCacheEvictNormal);
+        tma_load_2d(smem + t * kPpQBytes + kPpQBytes / 2, &tmQ, q_full, 64, qrow,
+                    kCacheEvictNormal);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_kb && !*abort_flag; ++j) {
+        const int s = j & 1;
+        const uint32_t ph_prev = ((j >> 1) - 1) & 1;
+        const int key0 = j * kPpN;
+        if (j >= 2 && !mbar_wait(&k_empty[s], ph_prev, p.err, 0x631)) { *abort_flag = 1; break; }
+        uint8_t* dk = smem + kPpOffK + s * kPpKVBytes;
+        mbar_arrive_expect_tx(&k_full[s], kPpKVBytes);
+        tma_load_3d(dk, &tmK, &k_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+        tma_load_3d(dk + kPpHalf, &tmK, &k_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        if (j >= 2 && !mbar_wait(&v_empty[s], ph_prev, p.err, 0x632)) {
+          *abort_flag = 1;
+          issued = -(j + 1);  // K_j issued, V_j not
+          break;
+        }
+        uint8_t* dv = smem + kPpOffV + s * kPpKVBytes;
+        mbar_arrive_expect_tx(&v_full[s], kPpKVBytes);
+        tma_load_3d(dv, &tmV, &v_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+        tma_load_3d(dv + kPpHalf, &tmV, &v_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        issued = j + 1;
+      }
+      // let the copies this thread issued land before the CTA exits
+      mbar_wait(q_full, 0, nullptr, 0);
+      const int nk = issued < 0 ? -issued : issued;
+      const int nv = issued < 0 ? -issued - 1 : issued;
+      for (int j = max(0, nk - 2); j < nk; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, 0);
+      for (int j = max(0, nv - 2); j < nv; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kFM, kPpN);
+      constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(kFM, kFD);
+      auto issue_s = [&](int j, int t) {
+        const uint32_t kb = s_base + kPpOffK + (j & 1) * kPpKVBytes;
+        const uint32_t qa = s_base + t * kPpQBytes;
+#pragma unroll 1
+        for (int ks = 0; ks < kFD / 16; ++ks)
+          tc_mma_bf16(tmem + t * kPpN, umma_desc_k_sw128(qa + (ks >> 2) * (kPpQBytes / 2)) + 2 * (ks & 3),
+                      umma_desc_k_sw128(kb + (ks >> 2) * kPpHalf) + 2 * (ks & 3), idesc_s, ks != 0);
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int j, int t) {
+        const uint32_t vb = s_base + kPpOffV + (j & 1) * kPpKVBytes;
+#pragma unroll 1
+        for (int ks = 0; ks < kPpN / 16; ++ks)
+          tc_mma_bf16_ts(tmem + 2 * kPpN + t * kFD, tmem + t * kPpN + ks * 8,
+                         umma_desc_mn_sw128(vb + ks * 2048, kPpHalf, 1024u), idesc_o,
+                         j > 0 || ks > 0);
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, 0x633) && mbar_wait(&k_full[0], 0, p.err, 0x634);
+      tc_fence_after();
+      if (ok) {
+        issue_s(0, 0);
+        issue_s(0, 1);
+        tc_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kb && !*abort_flag; ++j) {
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 0x635)) { ok = false; break; }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, p.err, 0x636)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(j, t);
+          if (t == 1) tc_commit(&v_empty[j & 1]);
+          if (j + 1 < n_kb) {
+            if (t == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err, 0x637)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(j + 1, t);
+            if (t == 1) tc_commit(&k_empty[(j + 1) & 1]);
+          } else {
+            tc_commit(&o_final[t]);
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, nullptr, 0);
+    }
+  } else {
+    // -------------------------------- softmax ---------------------------------
+    const int t = (warp - 2) >> 2;         // query tile (head h0 + t)
+    const int quarter = warp & 3;          // TMEM lane quarter of this warp
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + t * kPpN;
+    const uint32_t o_col = tmem + lane_off + 2 * kPpN + t * kFD;
+    const int64_t qpos = p.start + q0 + row;
+    const int64_t qpos_min = p.start + q0;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kb; ++j) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      if (!warp_wait(&s_full[t], j & 1, p.err, 0x638)) { ok = false; break; }
+      tc_fence_after();
+      float sc[kPpN];
+#pragma unroll
+      for (int c = 0; c < kPpN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32cols(s_col + c * 32, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+      }
+      const int kbase = j * kPpN;
+      // masks only where a key can lie past a row's position or past the end
+      if (kbase + kPpN - 1 > qpos_min || kbase + kPpN > kv_total) {
+        const int lim = (int)min64(kv_total - 1, p.causal ? qpos : kv_total - 1) - kbase;
+#pragma unroll
+        for (int c = 0; c < kPpN; ++c)
+          if (c > lim) sc[c] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kPpN; ++c) mx = fmaxf(mx, sc[c]);
+      const float m_new = fmaxf(m_used, mx);
+      const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
+      const bool rescale = move && j > 0 && m_used != -INFINITY;
+      const float corr = rescale ? ex2_approx(m_used - m_new) : 1.f;
+      if (move) {
+        l *= ex2_approx(m_used - m_new);  // m_used = -inf: l is 0 and stays 0
+        m_used = m_new;
+      }
+      const float base = (m_used == -INFINITY) ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kPpN / 32; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2_approx(sc[c * 32 + 2 * i] - base);
+          const float p1 = ex2_approx(sc[c * 32 + 2 * i + 1] - base);
+          rs += p0 + p1;
+          w[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O[t] holds tiles 0..j-1, complete (covered by the commit of S_j(t)):
+        // rescale it to the new base before PV_j adds to it
+#pragma unroll 1
+        for (int c = 0; c < kFD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32cols(o_col + c * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+          tmem_st_32cols(o_col + c * 32, r);
+        }
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+      l += rs;
+    }
+    if (!ok) *abort_flag = 1;
+    // the last PV of this tile, then O / l to global memory
+    if (__all_sync(0xffffffffu, ok) && n_kb > 0 && warp_wait(&o_final[t], 0, p.err, 0x639)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst =
+          p.out + b * p.os_b + (int64_t)(h0 + t) * p.os_h + (int64_t)(q0 + row) * p.os_s;
+#pragma unroll
+      for (int c = 0; c < kFD / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32cols(o_col + c * 32, r);
+        tc_wait_ld();
+        if (row < q_valid) {
+#pragma unroll
+          for (int d = 0; d < 32; d += 8) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(r[d + 4]) * inv, __uint_as_float(r[d + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(r[d + 6]) * inv, __uint_as_float(r[d + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + d) = u;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPpTmemCols);
+  }
+}
+
 }  // namespace
 }  // namespace q3
 
@@ -659,7 +964,9 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   using namespace q3;
   Q3_REQUIRE(q && k && v && out && o_strides, "q3_attn_prefill_tc: null pointer");
   Q3_REQUIRE(head_dim == kFD, "q3_attn_prefill_tc: head_dim must be 128 (got %d)", head_dim);
-  Q3_REQUIRE(variant == 0 || variant == 1, "q3_attn_prefill_tc: unknown variant %d", variant);
+  Q3_REQUIRE(variant >= 0 && variant <= 2, "q3_attn_prefill_tc: unknown variant %d", variant);
+  Q3_REQUIRE(variant != 2 || (Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0),
+             "q3_attn_prefill_tc: variant 2 pairs query heads of one KV head (Hq/Hkv even)");
   Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && start_pos >= 0,
              "q3_attn_prefill_tc: bad shape B=%d S=%d Hq=%d Hkv=%d", B, S, Hq, Hkv);
   Q3_REQUIRE(kv_rows_per_head >= start_pos + S,
@@ -686,6 +993,8 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem));
     Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_mn_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kMnSmem));
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_pp_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem));
     attr_set[dev] = true;
   }
   FlashParams p{};
@@ -701,6 +1010,18 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   // V of one stage: two 64-dim boxes 8 KB apart (MN), 8-key groups 1 KB apart (K)
   p.v_mn_stride = (uint32_t)(kKVBytes / 2);
   p.v_k_stride = 1024u;
+  if (variant == 2) {
+    // K/V as (dim, key, head) maps that end at the last valid key
+    rc = make_tmap_3d_rows128(&tk, k, start_pos + S, (int64_t)B * Hkv, kv_rows_per_head * kFD,
+                              kPpN);
+    if (rc) return rc;
+    rc = make_tmap_3d_rows128(&tv, v, start_pos + S, (int64_t)B * Hkv, kv_rows_per_head * kFD,
+                              kPpN);
+    if (rc) return rc;
+    dim3 grid2((S + kFM - 1) / kFM, Hq / 2, B);
+    return launch_ex(attn_prefill_tc_pp_kernel, grid2, dim3(kPpThreads), kPpSmem,
+                     (cudaStream_t)stream, 1, tq, tk, tv, p);
+  }
   dim3 grid((S + kFM - 1) / kFM, Hq, B);
   if (variant == 1)
     return launch_ex(attn_prefill_tc_mn_kernel, grid, dim3(kMnThreads), kMnSmem,

@@ -59,6 +59,12 @@ int* device_error_word();
 // elements, 128-byte swizzle (box_cols * 2 must be 128).  The cached variant
 // keeps one map per (pointer, shape, box) for weights, whose addresses are
 // stable; activation maps are rebuilt per call.
+// 3-D bf16 tensor map over `planes` planes of `rows` rows of 128 elements
+// (row stride 256 bytes, plane stride plane_stride_elems elements), boxes of
+// box_rows rows x 64 elements with the 128-byte swizzle.  Rows at or past
+// `rows` in a plane read as zeros.
+int make_tmap_3d_rows128(CUtensorMap* map, const void* base, int64_t rows, int64_t planes,
+                         int64_t plane_stride_elems, int box_rows);
 int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
                  int box_cols);
 int cached_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
@@ -226,6 +232,15 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(cache_hint)
       : "memory");
 }
+// 3-D tiled load (x: element, y: row, z: plane) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar,
+                                            int x, int y, int z, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(cache_hint)
+      : "memory");
+}
 constexpr uint64_t kCacheEvictNormal = 0x1000000000000000ull;
 constexpr uint64_t kCacheEvictFirst = 0x12F0000000000000ull;
 constexpr uint64_t kCacheEvictLast = 0x14F0000000000000ull;
@@ -258,6 +273,18 @@ __device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem], bf16 inputs, fp32 accumulate: A (M = 128
+// rows on the TMEM lanes, two bf16 of consecutive K per 32-bit column) is
+// read from tensor memory.
+__device__ __forceinline__ void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
@@ -295,6 +322,16 @@ __device__ __forceinline__ void tmem_st_32cols(uint32_t taddr, const uint32_t (&
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st_16cols(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tc_wait_st() {

@@ -46,6 +46,25 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
   return Q3_OK;
 }
 
+int make_tmap_3d_rows128(CUtensorMap* map, const void* base, int64_t rows, int64_t planes,
+                         int64_t plane_stride_elems, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (box_rows < 1 || box_rows > 256 || rows < 1 || planes < 1)
+    return fail(Q3_ERR_INVALID, "3-D tensor map: bad rows/planes/box");
+  if (!aligned(base, 16) || (plane_stride_elems * 2) % 16 != 0)
+    return fail(Q3_ERR_INVALID, "3-D tensor map: base/plane stride must be 16-byte aligned");
+  cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)planes};
+  cuuint64_t strides[2] = {256, (cuuint64_t)plane_stride_elems * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return Q3_OK;
+}
+
 namespace {
 struct TmapKey {
   const void* p;

@@ -73,3 +73,37 @@ def test_mn_variant_ends_cleanly_after_a_timeout(n_kb):
             codes.add(m.err)
             assert 0x611 <= m.err <= 0x618
     assert len(codes) >= 3, sorted(hex(c) for c in codes)
+
+
+@pytest.mark.parametrize("n_kb", [1, 2, 3, 4, 5, 8, 13])
+@pytest.mark.parametrize("rescale_p", [0.0, 0.3, 1.0])
+def test_two_tile_variant_delivers_each_tile_without_races(n_kb, rescale_p):
+    """Variant 2 (two query tiles, separate K and V rings, P written over S in
+    TMEM): every PV reads the P of its own tile and step, every S MMA writes
+    only after the PV that read the P it overwrites, O rescales fall between
+    two PVs of the tile, and K/V stages are refilled only after both tiles
+    are done with them."""
+    from tests.flash_pipeline_model import ModelPP
+    rescaled = 0
+    for seed in range(150):
+        m = ModelPP(n_kb, seed, rescale_p=rescale_p)
+        assert m.run() == "done", (n_kb, seed)
+        assert m.errors == [], (n_kb, seed, m.errors[:3])
+        assert m.err == 0 and not m.abort
+        assert all(m.seen[(t, w)] == list(range(n_kb)) for t in range(2) for w in range(4))
+        rescaled += m.rescales
+    assert rescaled > 0 or rescale_p == 0.0 or n_kb == 1
+
+
+@pytest.mark.parametrize("n_kb", [2, 3, 6])
+def test_two_tile_variant_ends_cleanly_after_a_timeout(n_kb):
+    from tests.flash_pipeline_model import ModelPP
+    codes = set()
+    for seed in range(300):
+        m = ModelPP(n_kb, seed, fault_at=1 + seed % 40)
+        assert m.run() == "done", (n_kb, seed)
+        assert m.errors == [], (n_kb, seed, m.errors[:3])
+        if m.err:
+            codes.add(m.err)
+            assert 0x631 <= m.err <= 0x639
+    assert len(codes) >= 3, sorted(hex(c) for c in codes)

@@ -87,8 +87,11 @@ def test_fused_entry_points_reject_bad_arguments_on_the_host():
                                 0, None)
     assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 128, 0, 1, 0.1, 128, strides,
-                                2, None)
+                                3, None)
     assert rc == _lib.Q3_ERR_INVALID and b"variant" in lib.q3_last_error()
+    rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 6, 2, 100, 128, 0, 1, 0.1, 128, strides,
+                                2, None)                               # Hq/Hkv odd
+    assert rc == _lib.Q3_ERR_INVALID and b"variant 2" in lib.q3_last_error()
     rc = lib.q3_attn_prefill_tc(one, one, one, one, 1, 8, 2, 100, 64, 0, 1, 0.1, 128, strides,
                                 1, None)
     assert rc == _lib.Q3_ERR_INVALID and b"head_dim" in lib.q3_last_error()

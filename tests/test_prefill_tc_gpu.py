@@ -1,8 +1,9 @@
 """Prefill attention on the tcgen05 tensor cores (q3_attn_prefill_tc) vs fp32
 attention and vs the mma.sync kernel, and through the decoder
-(Q3VL_PREFILL_TC).  Both variants (0: V transposed in shared memory; 1: V as an MN-major
-operand with O in TMEM).  Tolerances: max-abs <= 2e-2 and cosine >= 0.9999
-against fp32, as for q3_attn_prefill."""
+(Q3VL_PREFILL_TC).  Variants 0 (V transposed in shared memory), 1 (V as an
+MN-major operand with O in TMEM) and 2 (two heads of a KV group per CTA,
+128-key tiles, P in TMEM; needs Hq/Hkv even).  Tolerances: max-abs <= 2e-2
+and cosine >= 0.9999 against fp32, as for q3_attn_prefill."""
 import math
 
 import pytest
@@ -29,9 +30,12 @@ def rnd(*shape, seed=0):
                           (1, 4, 1, 130, 70, True, 512),      # prompt continuing at 70
                           (1, 8, 8, 96, 0, False, 96),
                           (3, 4, 4, 1, 37, True, 64),          # one query row
-                          (1, 4, 1, 700, 0, True, 700)])       # 6 query blocks, ragged tail
-@pytest.mark.parametrize("variant", [0, 1])
+                          (1, 4, 1, 700, 0, True, 700),        # 6 query blocks, ragged tail
+                          (2, 8, 2, 333, 5, False, 400)])      # non-causal, ragged, offset
+@pytest.mark.parametrize("variant", [0, 1, 2])
 def test_tc_prefill_matches_fp32(B, Hq, Hkv, S, start, causal, rows, variant):
+    if variant == 2 and (Hq // Hkv) % 2:
+        pytest.skip("variant 2 pairs the query heads of a KV head")
     q = rnd(B, Hq, S, 128, seed=30)
     k = rnd(B, Hkv, rows, 128, seed=31)
     v = rnd(B, Hkv, rows, 128, seed=32)
@@ -40,9 +44,10 @@ def test_tc_prefill_matches_fp32(B, Hq, Hkv, S, start, causal, rows, variant):
     if causal:
         want = oref.causal_attention_fp32(q, k, v, start)
     else:
-        rep = Hq // Hkv
-        s = q.float() @ k.float().repeat_interleave(rep, 1).transpose(-2, -1) / math.sqrt(128)
-        want = torch.softmax(s, -1) @ v.float().repeat_interleave(rep, 1)
+        # keys 0 .. start + S - 1 (the cache rows this call may read)
+        rep, kk, vv = Hq // Hkv, k[:, :, :start + S], v[:, :, :start + S]
+        s = q.float() @ kk.float().repeat_interleave(rep, 1).transpose(-2, -1) / math.sqrt(128)
+        want = torch.softmax(s, -1) @ vv.float().repeat_interleave(rep, 1)
     compare("prefill tc", out, want, max_abs=2e-2, min_cos=0.9999)
     # and the mma.sync kernel on the same inputs
     legacy = ops.attn_prefill(q.to(DEV), k.to(DEV), v.to(DEV), start_pos=start,
@@ -51,7 +56,7 @@ def test_tc_prefill_matches_fp32(B, Hq, Hkv, S, start, causal, rows, variant):
     assert ops.device_error(clear=True) == 0
 
 
-@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("variant", [0, 1, 2])
 def test_tc_prefill_writes_the_bshd_layout(variant):
     B, Hq, Hkv, S = 2, 8, 2, 160
     q, k, v = rnd(B, Hq, S, 128, seed=33), rnd(B, Hkv, S, 128, seed=34), rnd(B, Hkv, S, 128, seed=35)
@@ -61,7 +66,7 @@ def test_tc_prefill_writes_the_bshd_layout(variant):
     compare("prefill tc bshd", o.cpu(), want, max_abs=2e-2, min_cos=0.9999)
 
 
-@pytest.mark.parametrize("variant", ["0", "1"])
+@pytest.mark.parametrize("variant", ["0", "1", "2"])
 def test_decoder_generates_the_reference_tokens_with_tc_prefill(variant, monkeypatch):
     monkeypatch.setenv("Q3VL_PREFILL_TC_VARIANT", variant)
     import loader_fused
@@ -97,7 +102,7 @@ def test_tc_prefill_variant1_rescales_on_growing_scores():
     v = torch.randn(B, Hkv, S, 128, generator=g)
     q, k, v = q.to(BF16), k.to(BF16), v.to(BF16)
     want = oref.causal_attention_fp32(q, k, v, 0)
-    for variant in (0, 1):
+    for variant in (0, 1, 2):
         out = ops.attn_prefill_tc(q.to(DEV), k.to(DEV), v.to(DEV), variant=variant).cpu()
         compare(f"growing scores, variant {variant}", out, want, max_abs=2e-2, min_cos=0.9999)
     assert ops.device_error(clear=True) == 0
