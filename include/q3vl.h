@@ -303,13 +303,29 @@ Q3_API int q3_attn_prefill(const void* q, const void* k, const void* v, void* ou
  * memory so every MMA operand is K-major, and each tile's P V is folded into
  * fp32 registers; variant 1: V feeds the MMA as an MN-major operand and O
  * accumulates in TMEM, rescaled only when a row's maximum grows by more than
- * 2^8; any other variant is rejected.  Cache rows past start_pos + S up to the next
+ * 2^8; variant 2: one CTA holds the same 128 query rows of two heads of one KV
+ * head (Hq / Hkv even), 128-key tiles, P kept in TMEM and read by the MMA from
+ * there, the two tiles' softmax and MMAs overlapped; any other variant is
+ * rejected.  Cache rows past start_pos + S up to the next
  * multiple of 64 are read with probability 0 and must hold finite values
  * (variant 0 zeroes them). */
 Q3_API int q3_attn_prefill_tc(const void* q, const void* k, const void* v, void* out, int B, int Hq,
                        int Hkv, int S, int head_dim, int64_t start_pos, int causal, float scale,
                        int64_t kv_rows_per_head, const int64_t* o_strides, int variant,
                        q3_stream_t stream);
+/* q3_attn_prefill_tc variant 2 over paged K/V: k_pages, v_pages [num_pages,
+ * Hkv, page_tokens, 128] (page_tokens a multiple of 128); key position t of
+ * sequence b is read from page block_table[b * table_stride + t / page_tokens]
+ * (entries outside [0, num_pages) are recorded in the device error word and
+ * page 0 is read).  q contiguous [B, Hq, S, 128], Hq / Hkv even; out strides as
+ * for q3_attn_prefill_tc.  Key rows past start_pos + S in the last page are
+ * read with probability 0 and must hold finite values. */
+Q3_API int q3_attn_prefill_tc_paged(const void* q, const void* k_pages, const void* v_pages,
+                                    void* out, int B, int Hq, int Hkv, int S, int head_dim,
+                                    int64_t start_pos, int causal, float scale,
+                                    const int64_t* o_strides, const int32_t* block_table,
+                                    int64_t table_stride, int page_tokens, int num_pages,
+                                    q3_stream_t stream);
 /* The same over paged K/V: k_pages, v_pages [num_pages, Hkv, page_tokens, 128];
  * key position t of sequence b is read from page block_table[b * table_stride
  * + t / page_tokens] (page_tokens a multiple of 64).  Keys 0..start_pos+S-1

@@ -92,6 +92,12 @@ struct FlashParams {
   // blocks (MN, the descriptor's leading offset) and between 8-key groups (K,
   // its stride offset)
   uint32_t v_mn_stride, v_k_stride;
+  // variant 2 over a page pool (q3_attn_prefill_tc_paged): K/V maps are 2-D
+  // over [num_pages * Hkv * page_tokens, 128]; key position t of sequence b
+  // lives in page pages[b * pages_stride + t / page_tokens]
+  const int32_t* pages;
+  int64_t pages_stride;
+  int page_tokens, num_pages;
 };
 
 __global__ void __launch_bounds__(kFThreads, 1)
@@ -690,6 +696,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+template <bool PAGED>
 __global__ void __launch_bounds__(kPpThreads, 1)
     attn_prefill_tc_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
                               const __grid_constant__ CUtensorMap tmK,
@@ -767,10 +774,26 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         const uint32_t ph_prev = ((j >> 1) - 1) & 1;
         const int key0 = j * kPpN;
         if (j >= 2 && !mbar_wait(&k_empty[s], ph_prev, p.err, 0x631)) { *abort_flag = 1; break; }
+        // paged: the tile's rows in the pool (a 128-key tile never straddles
+        // pages); an entry outside the pool is recorded and page 0 read
+        int prow = 0;
+        if constexpr (PAGED) {
+          int pg = p.pages[(int64_t)b * p.pages_stride + key0 / p.page_tokens];
+          if (pg < 0 || pg >= p.num_pages) {
+            report_timeout(p.err, 0x63a);
+            pg = 0;
+          }
+          prow = (int)(((int64_t)pg * p.Hkv + kvh) * p.page_tokens + key0 % p.page_tokens);
+        }
         uint8_t* dk = smem + kPpOffK + s * kPpKVBytes;
         mbar_arrive_expect_tx(&k_full[s], kPpKVBytes);
-        tma_load_3d(dk, &tmK, &k_full[s], 0, key0, kv_plane, kCacheEvictNormal);
-        tma_load_3d(dk + kPpHalf, &tmK, &k_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        if constexpr (PAGED) {
+          tma_load_2d(dk, &tmK, &k_full[s], 0, prow, kCacheEvictNormal);
+          tma_load_2d(dk + kPpHalf, &tmK, &k_full[s], 64, prow, kCacheEvictNormal);
+        } else {
+          tma_load_3d(dk, &tmK, &k_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+          tma_load_3d(dk + kPpHalf, &tmK, &k_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        }
         if (j >= 2 && !mbar_wait(&v_empty[s], ph_prev, p.err, 0x632)) {
           *abort_flag = 1;
           issued = -(j + 1);  // K_j issued, V_j not
@@ -778,8 +801,13 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         }
         uint8_t* dv = smem + kPpOffV + s * kPpKVBytes;
         mbar_arrive_expect_tx(&v_full[s], kPpKVBytes);
-        tma_load_3d(dv, &tmV, &v_full[s], 0, key0, kv_plane, kCacheEvictNormal);
-        tma_load_3d(dv + kPpHalf, &tmV, &v_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        if constexpr (PAGED) {
+          tma_load_2d(dv, &tmV, &v_full[s], 0, prow, kCacheEvictNormal);
+          tma_load_2d(dv + kPpHalf, &tmV, &v_full[s], 64, prow, kCacheEvictNormal);
+        } else {
+          tma_load_3d(dv, &tmV, &v_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+          tma_load_3d(dv + kPpHalf, &tmV, &v_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+        }
         issued = j + 1;
       }
       // let the copies this thread issued land before the CTA exits
@@ -993,7 +1021,9 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem));
     Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_mn_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kMnSmem));
-    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_pp_kernel,
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_pp_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem));
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_pp_kernel<true>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem));
     attr_set[dev] = true;
   }
@@ -1019,7 +1049,7 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
                               kPpN);
     if (rc) return rc;
     dim3 grid2((S + kFM - 1) / kFM, Hq / 2, B);
-    return launch_ex(attn_prefill_tc_pp_kernel, grid2, dim3(kPpThreads), kPpSmem,
+    return launch_ex(attn_prefill_tc_pp_kernel<false>, grid2, dim3(kPpThreads), kPpSmem,
                      (cudaStream_t)stream, 1, tq, tk, tv, p);
   }
   dim3 grid((S + kFM - 1) / kFM, Hq, B);
@@ -1028,4 +1058,67 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
                      (cudaStream_t)stream, 1, tq, tk, tv, p);
   return launch_ex(attn_prefill_tc_kernel, grid, dim3(kFThreads), kFSmem, (cudaStream_t)stream,
                    1, tq, tk, tv, p);
+}
+
+extern "C" int q3_attn_prefill_tc_paged(const void* q, const void* k_pages, const void* v_pages,
+                                        void* out, int B, int Hq, int Hkv, int S, int head_dim,
+                                        int64_t start_pos, int causal, float scale,
+                                        const int64_t* o_strides, const int32_t* block_table,
+                                        int64_t table_stride, int page_tokens, int num_pages,
+                                        q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(q && k_pages && v_pages && out && o_strides && block_table,
+             "q3_attn_prefill_tc_paged: null pointer");
+  Q3_REQUIRE(head_dim == kFD, "q3_attn_prefill_tc_paged: head_dim must be 128 (got %d)",
+             head_dim);
+  Q3_REQUIRE(B > 0 && S > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) % 2 == 0 &&
+                 start_pos >= 0,
+             "q3_attn_prefill_tc_paged: bad shape B=%d S=%d Hq=%d Hkv=%d (Hq/Hkv must be even)",
+             B, S, Hq, Hkv);
+  Q3_REQUIRE(page_tokens > 0 && page_tokens % kPpN == 0 && num_pages > 0,
+             "q3_attn_prefill_tc_paged: page_tokens=%d must be a positive multiple of %d",
+             page_tokens, kPpN);
+  Q3_REQUIRE(table_stride > 0 && start_pos + S <= table_stride * page_tokens,
+             "q3_attn_prefill_tc_paged: positions up to %lld beyond the table width",
+             (long long)(start_pos + S - 1));
+  Q3_REQUIRE((int64_t)B * Hq * S < (1ll << 31) &&
+                 (int64_t)num_pages * Hkv * page_tokens < (1ll << 31),
+             "q3_attn_prefill_tc_paged: tensors too large for 32-bit TMA rows");
+  Q3_REQUIRE(o_strides[2] % 8 == 0 && o_strides[1] % 8 == 0 && o_strides[0] % 8 == 0,
+             "q3_attn_prefill_tc_paged: output rows must stay 16-byte aligned");
+  Q3_REQUIRE(aligned(q, 16) && aligned(k_pages, 16) && aligned(v_pages, 16) && aligned(out, 16) &&
+                 aligned(block_table, 4),
+             "q3_attn_prefill_tc_paged: misaligned pointer");
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_2d(&tq, q, (int64_t)B * Hq * S, kFD, kFM, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tk, k_pages, (int64_t)num_pages * Hkv * page_tokens, kFD, kPpN, 64);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v_pages, (int64_t)num_pages * Hkv * page_tokens, kFD, kPpN, 64);
+  if (rc) return rc;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    Q3_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_tc_pp_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kPpSmem));
+    attr_set[dev] = true;
+  }
+  FlashParams p{};
+  p.out = (__nv_bfloat16*)out;
+  p.os_b = o_strides[0]; p.os_h = o_strides[1]; p.os_s = o_strides[2];
+  p.Hq = Hq; p.Hkv = Hkv; p.S = S;
+  p.q_rows_per_head = S;
+  p.kv_rows_per_head = 0;
+  p.start = start_pos;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.err = device_error_word();
+  p.pages = block_table;
+  p.pages_stride = table_stride;
+  p.page_tokens = page_tokens;
+  p.num_pages = num_pages;
+  dim3 grid((S + kFM - 1) / kFM, Hq / 2, B);
+  return launch_ex(attn_prefill_tc_pp_kernel<true>, grid, dim3(kPpThreads), kPpSmem,
+                   (cudaStream_t)stream, 1, tq, tk, tv, p);
 }

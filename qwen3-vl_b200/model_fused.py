@@ -452,9 +452,15 @@ class Qwen3VLDecoderFused:
             if paged:
                 # this call's K/V rows went into the pages above; earlier
                 # positions are there from earlier calls
-                ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
-                                       start_pos=start_pos, causal=True, scale=self.scale,
-                                       out=attn.transpose(1, 2))
+                if (self.prefill_tc and q.is_contiguous() and kc.shape[2] % 128 == 0 and
+                        (ab.num_q_heads // ab.num_kv_heads) % 2 == 0):
+                    ops.attn_prefill_tc_paged(q, kc, vc, kv_cache[layer_idx].table,
+                                              start_pos=start_pos, causal=True, scale=self.scale,
+                                              out=attn.transpose(1, 2))
+                else:
+                    ops.attn_prefill_paged(q, kc, vc, kv_cache[layer_idx].table,
+                                           start_pos=start_pos, causal=True, scale=self.scale,
+                                           out=attn.transpose(1, 2))
             elif self.prefill_tc and q.is_contiguous():
                 ops.attn_prefill_tc(q, kc, vc, start_pos=start_pos, causal=True,
                                     scale=self.scale, out=attn.transpose(1, 2))

@@ -65,6 +65,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_qkv_norm_rope_paged": (I32, [P, P, P, P, P, I32, I32, I64, I64, P, P, P, I32, I32, I32,
                                      I32, I32, I64, P, P, I64, I32, I32, F32, P]),
     "q3_attn_prefill_tc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, I64, P, I32, P]),
+    "q3_attn_prefill_tc_paged": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, P, P,
+                                       I64, I32, I32, P]),
     "q3_attn_prefill_paged": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, P, P, P,
                                     I64, I32, I32, P]),
     "q3_kv_pages_write": (I32, [P, P, P, P, I32, I32, I32, I32, P, I64, I32, I32, I64, P, P]),

@@ -502,6 +502,29 @@ def attn_prefill_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Te
     return out
 
 
+def attn_prefill_tc_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tensor,
+                          block_table: torch.Tensor, *, start_pos: int, causal: bool = True,
+                          scale: float = None, out: torch.Tensor = None):
+    """attn_prefill_paged on the tcgen05 tensor cores (q3_attn_prefill_tc_paged,
+    variant 2): q contiguous [B, Hq, S, 128] with Hq / Hkv even; pages of a
+    multiple of 128 tokens."""
+    _cuda("attn_prefill_tc_paged", q, k_pages, v_pages, block_table, out)
+    _bf16("attn_prefill_tc_paged", q, k_pages, v_pages, out)
+    _contig("attn_prefill_tc_paged", q, k_pages, v_pages, block_table)
+    if block_table.dtype != torch.int32:
+        raise TypeError("attn_prefill_tc_paged: block_table must be int32")
+    B, Hq, S, D = q.shape
+    num_pages, Hkv, page_tokens, _ = k_pages.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, S, D, dtype=torch.bfloat16, device=q.device)
+    call("q3_attn_prefill_tc_paged", _p(q), _p(k_pages), _p(v_pages), _p(out), B, Hq, Hkv, S,
+         D, int(start_pos), 1 if causal else 0, float(scale), _strides_bhs(out, "out"),
+         _p(block_table), block_table.shape[1], page_tokens, num_pages, _stream())
+    return out
+
+
 # ----------------------------------------------------------------------------
 # GEMM
 # ----------------------------------------------------------------------------

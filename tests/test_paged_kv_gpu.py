@@ -149,3 +149,26 @@ def test_chunked_prefill_through_pages_matches_one_shot(split):
             rel_scale=True, min_cos=0.999)
     assert ops.device_error(clear=True) == 0
     pool.close()
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,start,page", [(2, 32, 8, 700, 0, 256),
+                                                  (3, 8, 2, 300, 90, 128)])
+def test_tc_prefill_through_pages_matches_contiguous(B, Hq, Hkv, S, start, page):
+    """q3_attn_prefill_tc_paged (variant 2 through a block table) gives the
+    contiguous variant 2's bits: the same arithmetic, and the page rows past
+    the last key hold finite values that get probability 0."""
+    L = start + S
+    pool = KVPagePool(64, page, max_seqs=B, buckets=(2048,), layers=1, kv_heads=Hkv, device=DEV)
+    pool.reserve(B - 1, 10)                                  # interleave the slots' pages
+    for b in range(B):
+        pool.reserve(b, L)
+    table = pool.device_table(range(B))
+    k = rnd(B, Hkv, L, 128, seed=6).to(DEV)
+    v = rnd(B, Hkv, L, 128, seed=7).to(DEV)
+    ops.kv_pages_write(k, v, pool.k[0], pool.v[0], table, start_pos=0)
+    q = rnd(B, Hq, S, 128, seed=8).to(DEV)
+    want = ops.attn_prefill_tc(q, k, v, start_pos=start, variant=2)
+    got = ops.attn_prefill_tc_paged(q, pool.k[0], pool.v[0], table, start_pos=start)
+    assert torch.equal(got, want)
+    assert ops.device_error(clear=True) == 0
+    pool.close()
