@@ -74,7 +74,8 @@ def main(argv=None):
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=24576)
     ap.add_argument("--K", type=int, default=4096)
-    ap.add_argument("--epi", default="none", choices=["none", "residual", "swiglu"])
+    ap.add_argument("--epi", default="none", choices=["none", "residual", "swiglu", "allreduce"],
+                    help="allreduce (gemv): q3_gemm_ar on a single-rank communicator")
     ap.add_argument("--norm", action="store_true",
                     help="gemv: RMSNorm fused in, sums of squares from a prior projection")
     ap.add_argument("--B", type=int, default=8)
@@ -121,7 +122,8 @@ def main(argv=None):
     if a.kernel in ("gemv", "gemm"):
         x = torch.randn(a.M, a.K, device=dev).to(bf)
         w = (torch.randn(a.N, a.K, device=dev) * 0.02).to(bf)
-        r = torch.randn(a.M, a.N, device=dev).to(bf) if a.epi == "residual" else None
+        r = torch.randn(a.M, a.N, device=dev).to(bf) if a.epi in ("residual", "allreduce") \
+            else None
         out_n = a.N // 2 if a.epi == "swiglu" else a.N
         out = torch.empty(a.M, out_n, dtype=bf, device=dev)
         if a.norm:
@@ -132,6 +134,21 @@ def main(argv=None):
             ss[:, :a.M] = (x.float() ** 2).view(a.M, a.K // 64, 64).sum(-1).t()
             fn = lambda: ops.gemm_decode(x, w, a.epi, residual=r, norm_w=nw, ss_in=ss,  # noqa
                                          ss_tiles=a.K // 64, out=out)
+        elif a.epi == "allreduce":
+            # q3_gemm_ar on a single-rank communicator: the all-reduce
+            # projection's kernel and epilogue with no peer to exchange with
+            import ctypes
+
+            from q3vl import _lib
+
+            class _Solo:
+                handle = ctypes.c_void_p()
+            solo = _Solo()
+            nb = int(_lib.load().q3_comm_handle_bytes())
+            _lib.call("q3_comm_create", 0, 1, a.N, ctypes.byref(solo.handle),
+                      (ctypes.c_char * nb)())
+            ss_out = torch.empty(a.N // 64, 16, device=dev)
+            fn = lambda: ops.gemm_ar(x, w, solo, residual=r, out=out, ss_out=ss_out)  # noqa
         else:
             fn = lambda: ops.gemm(x, w, a.epi, residual=r, out=out)  # noqa: E731
         ms = _time(fn, a.iters, a.warmup, flush)

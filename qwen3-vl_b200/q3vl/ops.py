@@ -457,10 +457,16 @@ def attn_prefill_tc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, start_
     """attn_prefill on the tcgen05 tensor cores.  q contiguous [B, Hq, S, 128];
     k/v [B, Hkv, rows, 128] contiguous with rows >= start_pos + S; out any
     [B, Hq, S, 128] view whose strides are multiples of 8.  variant 0 (V
-    transposed in shared memory) or 1 (V as an MN-major operand, O in TMEM);
-    default Q3VL_PREFILL_TC_VARIANT, else 1 (the faster on B200)."""
+    transposed in shared memory), 1 (V as an MN-major operand, O in TMEM) or 2
+    (two heads of a KV group per CTA, 128-key tiles, P in TMEM; Hq/Hkv even);
+    default Q3VL_PREFILL_TC_VARIANT, else 2 where it applies (the fastest on
+    B200), else 1."""
     if variant is None:
-        variant = int(os.environ.get("Q3VL_PREFILL_TC_VARIANT", "1"))
+        env = os.environ.get("Q3VL_PREFILL_TC_VARIANT")
+        if env is not None:
+            variant = int(env)
+        else:
+            variant = 2 if (q.shape[1] // max(1, k.shape[1])) % 2 == 0 else 1
     _cuda("attn_prefill_tc", q, k, v, out)
     _bf16("attn_prefill_tc", q, k, v, out)
     _contig("attn_prefill_tc", q, k, v)
