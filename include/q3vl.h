@@ -548,6 +548,38 @@ Q3_API int q3_decode_step(void* plan, void* x, float* ss, const int32_t* kv_len_
                           int64_t rope_delta, q3_stream_t stream);
 Q3_API int q3_decode_step_destroy(void* plan);
 
+/* ---- a12/a13 + 8(e): the decode step at tensor parallelism in one launch ---
+ * Replaces forward_layer (model_fused.py:234-277) at S = 1 for every layer,
+ * with its two dist.all_reduce calls per layer (:267, :274), on one rank of a
+ * tensor-parallel group (layers: this rank's shards, as q3_step_layer gives
+ * them; q_heads, kv_heads and inter per rank).  One persistent kernel per GPU
+ * (one CTA per SM, cooperative launch) runs every phase of every layer,
+ * separated by grid-wide barriers; weight tiles stream through a TMA ring
+ * across phase boundaries; o_proj and down reduce over the ranks inside the
+ * kernel through the communicator's peer buffers (8-byte words that carry
+ * their call number; ranks summed in rank order, so every rank holds the same
+ * bits).  `comm` is a q3_comm_create communicator of this rank's group with
+ * max_cols >= hidden, opened, and used by this plan only (its buffer holds
+ * this kernel's words).  batch 1..8; every projection's rows must fit 16
+ * granules of 8 rows per SM (the 8B shape needs TP >= 2); the reduction
+ * lengths (hidden, q_heads * 128, inter) must leave room in shared memory
+ * (up to 6144).
+ * q3_decode_tp: x bf16 [batch, hidden]: the embedded new tokens in, the last
+ * layer's output (before the final norm) out.  *kv_len_dev = new position +
+ * 1 (the same for every sequence); RoPE row = position + rope_delta.  Every
+ * rank of the group must run the same steps in the same order.  A plan holds
+ * workspaces for one step at a time: order its steps on one stream.  After a
+ * Q3_ERR_TIMEOUT in the device error word (0x501: a peer never delivered;
+ * 0x801-0x805: a barrier or ring wait ran out), destroy and recreate the
+ * plan and the communicator. */
+Q3_API int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, int batch, int hidden,
+                               int q_heads, int kv_heads, int inter, int64_t max_seq, float eps,
+                               const void* rope_cos, const void* rope_sin, int64_t rope_rows,
+                               void* comm, void** plan_out);
+Q3_API int q3_decode_tp(void* plan, void* x, const int32_t* kv_len_dev, int64_t rope_delta,
+                        q3_stream_t stream);
+Q3_API int q3_decode_tp_destroy(void* plan);
+
 /* ---- a13: embedding gather and greedy argmax -----------------------------
  * Replaces embed_tokens(input_ids) (model_fused.py:281) and
  * logits.argmax(-1) (model_fused.py:310,320).  ids int64 [n]; table bf16

@@ -26,6 +26,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from q3vl import layout, ops
+from q3vl._lib import Q3Error
 from q3vl.kv_pages import KVPagePool, PagedLayer
 
 KV_BUCKETS = (2048, 4096, 8192)
@@ -241,6 +242,11 @@ class Qwen3VLDecoderFused:
         # decode graphs: every layer in one persistent kernel (q3_decode_step);
         # opt-in until it beats the per-kernel decode step
         self.use_step_kernel = os.environ.get("Q3VL_STEP_KERNEL", "0") == "1"
+        # decode at tensor parallelism: every layer of a step in one persistent
+        # kernel per GPU with the all-reduce inside (q3_decode_tp)
+        self.use_tp_kernel = os.environ.get("Q3VL_TP_KERNEL", "0") == "1"
+        self.mk_comm = None
+        self._tp_plans = {}
         # prefill: QK-norm, RoPE and the KV write in the QKV GEMM's epilogue
         self.fuse_qkv = os.environ.get("Q3VL_FUSE_QKV", "1") != "0"
         # decode: QK-norm, RoPE and the KV write inside the attention kernel
@@ -289,6 +295,12 @@ class Qwen3VLDecoderFused:
             from q3vl.comm import PeerComm
             self.comm = PeerComm(group=group, max_cols=max_cols, device=self.device)
             self._graphs.clear()
+        if self.tp_size > 1 and self.use_tp_kernel and self.mk_comm is None:
+            # the step kernel's own exchange buffers (its words must not meet
+            # q3_gemm_ar's)
+            from q3vl.comm import PeerComm
+            H = self.layers[0].attn_block.input_norm_weight.numel()
+            self.mk_comm = PeerComm(group=group, max_cols=H, device=self.device)
         rows = os.environ.get("Q3VL_PREFILL_AR", "") == "peer"
         if self.tp_size > 1 and rows and self.pcomm is None:
             self.enable_prefill_allreduce(group=group)
@@ -313,6 +325,13 @@ class Qwen3VLDecoderFused:
         for plan in self._step_plans.values():
             plan.close()
         self._step_plans.clear()
+        for plan in self._tp_plans.values():
+            if plan is not None:
+                plan.close()
+        self._tp_plans.clear()
+        if self.mk_comm is not None:
+            self.mk_comm.close()
+            self.mk_comm = None
         if self.comm is not None:
             self.comm.close()
             self.comm = None
@@ -707,6 +726,48 @@ class Qwen3VLDecoderFused:
                                 eps=self.final_norm.eps, ss_in=self._ss_step, ss_tiles=H // 128)
         return local.view(B, 1, -1)
 
+    # ------------------------------------------- tensor-parallel step kernel
+    def _tp_ok(self, B: int, kv_cache, rope_delta) -> bool:
+        """The step kernel covers up to 8 sequences, head_dim 128, no QKV bias,
+        contiguous caches and one RoPE delta for the batch; at TP > 1 it needs
+        its communicator (enable_peer_allreduce with Q3VL_TP_KERNEL=1)."""
+        return (self.use_tp_kernel and self.num_layers > 0 and 1 <= B <= 8 and
+                self.head_dim == 128 and not isinstance(kv_cache[0], PagedLayer) and
+                not isinstance(rope_delta, RowRope) and
+                all(L.attn_block.qkv_bias is None for L in self.layers) and
+                (self.tp_size == 1 or self.mk_comm is not None))
+
+    def _tp_plan(self, B, kv_cache):
+        """The step kernel's plan for this batch and cache, or None when the
+        library rejects the shapes (then the per-kernel step runs)."""
+        key = (B, kv_cache[0][0].data_ptr())
+        if key in self._tp_plans:
+            return self._tp_plans[key]
+        if self.tp_size == 1 and self.mk_comm is None:
+            from q3vl.comm import SoloComm
+            H = self.layers[0].attn_block.input_norm_weight.numel()
+            self.mk_comm = SoloComm(max_cols=H, device=self.device)
+        layers = []
+        for L, (kc, vc) in zip(self.layers, kv_cache):
+            ab, mlp = L.attn_block, L.mlp_block
+            layers.append(dict(w_qkv=ab.qkv_weight_km, w_o=L.o_proj.weight_km,
+                               w_gate_up=mlp.gate_up_weight_il, w_down=mlp.down_weight_km,
+                               input_norm=ab.input_norm_weight, post_norm=mlp.post_norm_weight,
+                               q_norm=ab.q_norm_weight, k_norm=ab.k_norm_weight,
+                               k_cache=kc, v_cache=vc))
+        cos, sin, _ = self.rotary.tables(self.device)
+        mlp0 = self.layers[0].mlp_block
+        try:
+            plan = ops.DecodeTPPlan(
+                layers, batch=B, hidden=self.layers[0].attn_block.input_norm_weight.numel(),
+                q_heads=self.num_q_heads, kv_heads=self.num_kv_heads,
+                inter=mlp0.down_weight_km.shape[1], max_seq=kv_cache[0][0].shape[2],
+                eps=self._eps, cos=cos, sin=sin, comm=self.mk_comm)
+        except Q3Error:
+            plan = None
+        self._tp_plans[key] = plan
+        return plan
+
     def _capture_decode(self, B, kv_cache, bucket, rope_delta=0):
         """Capture one decode step.  Must run before the prefill that fills this
         cache: the warm-up step writes KV slot 0, which the prefill overwrites."""
@@ -724,9 +785,14 @@ class Qwen3VLDecoderFused:
 
         use_step = (self._step_ok(B) and not isinstance(kv_cache[0], PagedLayer) and
                     not isinstance(rope_delta, RowRope))
+        tp_plan = self._tp_plan(B, kv_cache) if self._tp_ok(B, kv_cache, rope_delta) else None
 
         def step():
             """One decode step; the next tokens land in `tok` (read at the start)."""
+            if tp_plan is not None:
+                x = self._embed(tok.view(B, 1)).view(B, -1)
+                tp_plan.run(x, kv_len, int(rope_delta))
+                return self._greedy(x, None, B, 1, out=tok)
             if use_step:
                 logits = self._step_logits(B, tok, kv_cache, kv_len, rope_delta)
                 return ops.argmax(logits.view(B, -1), out=tok)

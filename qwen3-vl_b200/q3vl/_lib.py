@@ -108,6 +108,10 @@ SIGNATURES: dict[str, tuple] = {
                                     ctypes.POINTER(P)]),
     "q3_decode_step": (I32, [P, P, P, P, I64, P]),
     "q3_decode_step_destroy": (I32, [P]),
+    "q3_decode_tp_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64, P,
+                                  ctypes.POINTER(P)]),
+    "q3_decode_tp": (I32, [P, P, P, I64, P]),
+    "q3_decode_tp_destroy": (I32, [P]),
     "q3_embed": (I32, [P, P, P, I64, I64, I64, P]),
     "q3_add": (I32, [P, P, P, I64, P]),
     "q3_argmax": (I32, [P, I64, I64, P, P]),

@@ -107,3 +107,30 @@ class PrefillComm:
             dist.barrier(group=self.group)
             call("q3_prefill_comm_destroy", self._ptr)
             self._ptr = ctypes.c_void_p()
+
+
+class SoloComm:
+    """A single-rank communicator (q3_comm_create with world 1), for the
+    decode step kernel on one GPU: its all-reduce is the identity, and no
+    process group is needed."""
+
+    def __init__(self, max_cols: int = 16384, device=None):
+        self.device = torch.device(device) if device is not None else \
+            torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nb = int(lib.q3_comm_handle_bytes())
+        self._ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            call("q3_comm_create", 0, 1, int(max_cols), ctypes.byref(self._ptr),
+                 (ctypes.c_char * nb)())
+        self.rank, self.world, self.max_cols = 0, 1, max_cols
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._ptr
+
+    def close(self):
+        if self._ptr is not None and self._ptr.value:
+            call("q3_comm_destroy", self._ptr)
+            self._ptr = ctypes.c_void_p()
+

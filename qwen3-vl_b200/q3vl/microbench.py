@@ -65,8 +65,8 @@ def _time(fn, iters, warmup, flush):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["gemv", "gemm", "decode", "prefill", "rmsnorm", "gemm_ar",
-                                       "gemm_allreduce", "layer", "step", "rope_index", "vision",
-                                       "paged", "e2e_vision"])
+                                       "gemm_allreduce", "layer", "step", "tpstep", "rope_index",
+                                       "vision", "paged", "e2e_vision"])
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--tp", type=int, default=1,
                     help="layer: time one rank's shard at this tensor-parallel degree")
@@ -108,6 +108,8 @@ def main(argv=None):
         return _e2e_vision(a)
     if a.kernel == "gemm_ar":
         return _gemm_ar(a)
+    if a.kernel == "tpstep":
+        return _tpstep(a)
     if a.kernel == "gemm_allreduce":
         return _gemm_allreduce(a)
     if a.kernel == "layer":
@@ -364,6 +366,63 @@ def _step(a):
                       "gbs": round(tot / ms / 1e6, 1), "bytes": tot, "device_error": err}),
           flush=True)
     plan.close()
+
+
+def _tpstep(a):
+    """The tensor-parallel decode step kernel (q3_decode_tp) on one GPU at the
+    shard shapes of one rank at TP = --tp (8B model, --layers layers), on a
+    single-rank communicator (no peer exchange), as CUDA-graph replays;
+    against the same rank's per-kernel layer (the layer microbench's kernels)
+    it shows what one launch per step saves."""
+    import dataclasses
+
+    import loader_fused
+    from q3vl.comm import SoloComm
+    dev = torch.device("cuda:0")
+    base = loader_fused.QWEN3_VL_8B
+    spec = dataclasses.replace(base, layers=a.layers, vocab=4096, q_heads=base.q_heads // a.tp,
+                               kv_heads=base.kv_heads // a.tp, inter=base.inter // a.tp)
+    dec = loader_fused.random_decoder(spec, 0, 1, dev, seed=0, max_seq=a.bucket)
+    B, L, H = a.B, a.L, spec.hidden
+    kv = dec._kv_for(B, a.bucket)
+    for k, v in kv:
+        k.normal_()
+        v.normal_()
+    comm = SoloComm(max_cols=H, device=dev)
+    layers = []
+    for Ly, (kc, vc) in zip(dec.layers, kv):
+        ab, mlp = Ly.attn_block, Ly.mlp_block
+        layers.append(dict(w_qkv=ab.qkv_weight_km, w_o=Ly.o_proj.weight_km,
+                           w_gate_up=mlp.gate_up_weight_il, w_down=mlp.down_weight_km,
+                           input_norm=ab.input_norm_weight, post_norm=mlp.post_norm_weight,
+                           q_norm=ab.q_norm_weight, k_norm=ab.k_norm_weight, k_cache=kc,
+                           v_cache=vc))
+    cos, sin, _ = dec.rotary.tables(dev)
+    plan = ops.DecodeTPPlan(layers, batch=B, hidden=H, q_heads=spec.q_heads,
+                            kv_heads=spec.kv_heads, inter=spec.inter, max_seq=a.bucket,
+                            eps=spec.eps, cos=cos, sin=sin, comm=comm)
+    x0 = (torch.randn(B, H, device=dev) * 0.02).to(torch.bfloat16)
+    x = x0.clone()
+    kv_len = torch.tensor([L], dtype=torch.int32, device=dev)
+
+    def f():
+        x.copy_(x0)
+        plan.run(x, kv_len)
+    ms = _graph_ms([f], rounds=4)
+    torch.cuda.synchronize()
+    err = ops.device_error(clear=True)
+    L0 = dec.layers[0]
+    wbytes = sum(t.numel() * 2 for t in (L0.attn_block.qkv_weight_km, L0.o_proj.weight_km,
+                                         L0.mlp_block.gate_up_weight_il,
+                                         L0.mlp_block.down_weight_km))
+    kvbytes = 2 * B * L0.attn_block.num_kv_heads * L * 128 * 2
+    tot = a.layers * (wbytes + kvbytes)
+    print(json.dumps({"kernel": "tpstep", "tp": a.tp, "B": B, "L": L, "layers": a.layers,
+                      "ms": round(ms, 4), "us_per_layer": round(ms * 1e3 / a.layers, 2),
+                      "gbs": round(tot / ms / 1e6, 1), "bytes": tot, "device_error": err}),
+          flush=True)
+    plan.close()
+    comm.close()
 
 
 def _gemm_ar(a):

@@ -735,6 +735,65 @@ class DecodeStepPlan:
             pass
 
 
+class DecodeTPPlan:
+    """One decode step of every layer, with the tensor-parallel all-reduce
+    inside, as one persistent kernel per GPU (q3_decode_tp).
+
+    `layers` as for DecodeStepPlan (this rank's shards); `comm` an object with
+    a `.handle` to a q3_comm_create communicator of this rank's group, opened,
+    with max_cols >= hidden, used by this plan only.  The tensors must outlive
+    the plan."""
+
+    def __init__(self, layers, *, batch: int, hidden: int, q_heads: int, kv_heads: int,
+                 inter: int, max_seq: int, eps: float, cos: torch.Tensor, sin: torch.Tensor,
+                 comm):
+        from ._lib import StepLayer
+        arr = (StepLayer * len(layers))()
+        keep = []
+        for i, d in enumerate(layers):
+            for name, _ in StepLayer._fields_:
+                t = d[name]
+                if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+                    raise ValueError(f"DecodeTPPlan: layer {i} {name} must be contiguous "
+                                     "bf16 on the GPU")
+                setattr(arr[i], name, t.data_ptr())
+                keep.append(t)
+        _cuda("decode_tp", cos, sin)
+        _bf16("decode_tp", cos, sin)
+        handle = ctypes.c_void_p()
+        call("q3_decode_tp_create", ctypes.cast(arr, ctypes.c_void_p), len(layers), batch,
+             hidden, q_heads, kv_heads, inter, int(max_seq), float(eps), _p(cos), _p(sin),
+             cos.shape[0], comm.handle, ctypes.byref(handle))
+        self.handle = handle
+        self.batch, self.hidden = batch, hidden
+        self._keep = keep + [cos, sin, comm]
+
+    def run(self, x: torch.Tensor, kv_len_dev: torch.Tensor, rope_delta: int = 0) -> torch.Tensor:
+        """x bf16 [B, hidden] in place: embedded tokens in, last layer out."""
+        if self.handle is None:
+            raise RuntimeError("DecodeTPPlan is closed")
+        if x.shape != (self.batch, self.hidden) or x.dtype != torch.bfloat16:
+            raise ValueError("decode_tp: x must be bf16 [batch, hidden]")
+        if kv_len_dev.dtype != torch.int32:
+            raise TypeError("decode_tp: kv_len_dev must be int32")
+        _cuda("decode_tp", x, kv_len_dev)
+        _contig("decode_tp", x)
+        call("q3_decode_tp", self.handle, _p(x), _p(kv_len_dev), int(rope_delta), _stream())
+        return x
+
+    def close(self):
+        if self.handle is not None:
+            call("q3_decode_tp_destroy", self.handle)
+            self.handle = None
+            self._keep = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def gemm_ar(a: torch.Tensor, w: torch.Tensor, comm, residual: torch.Tensor = None,
             out: torch.Tensor = None, ss_out: torch.Tensor = None) -> torch.Tensor:
     """C = residual + all_reduce_sum(a @ w.T) over the communicator's ranks

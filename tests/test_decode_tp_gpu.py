@@ -1,0 +1,96 @@
+"""The tensor-parallel decode step kernel (q3_decode_tp) on one GPU, on a
+single-rank communicator (its all-reduce is the identity):
+
+- through the drop-in decoder (Q3VL_TP_KERNEL=1, decode graph): the tiny
+  decoders' greedy tokens equal the reference's golden tokens;
+- at one TP8 rank's shard shapes of the 8B model (hidden 4096, 4 query heads,
+  1 KV head, inter 1536): two consecutive decode steps through the kernel
+  match the per-kernel path layer by layer's output (max-abs <= 3e-2 of the
+  output scale, cosine >= 0.9999), and the K/V rows it writes match.
+The two-GPU run of the same kernel is in tests/test_tp_gpu.py."""
+import pytest
+import torch
+
+import loader_fused
+from q3vl import ops
+from q3vl.comm import SoloComm
+from tests.golden import cases
+from tests.helpers import compare, load_golden
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _spec(s):
+    return loader_fused.TextSpec(hidden=s.hidden, q_heads=s.q_heads, kv_heads=s.kv_heads,
+                                 inter=s.inter, vocab=s.vocab, layers=s.layers,
+                                 rope_theta=s.rope_theta, eps=s.eps)
+
+
+@pytest.mark.parametrize("name", ["decoder_tiny_tp1", "decoder_tiny8_tp1"])
+def test_tiny_decoder_greedy_tokens_through_the_step_kernel(name, monkeypatch):
+    monkeypatch.setenv("Q3VL_TP_KERNEL", "1")
+    g = load_golden(name)
+    c = cases.DECODER_CASES[name]
+    w = cases.decoder_weights(name)
+    dec = loader_fused.build_decoder(w["layers"], w["embed"], w["final_norm"], w["lm_head"],
+                                     _spec(c["spec"]), 0, 1, DEV, c["max_seq"])
+    assert dec.use_tp_kernel
+    ids = cases.decoder_prompt(name).to(DEV)
+    toks = dec.generate(ids, max_new_tokens=c["new_tokens"], eos_token_id=-1)
+    assert any(p is not None for p in dec._tp_plans.values()), "the step kernel did not run"
+    assert toks == g["tokens"].tolist()
+    assert ops.device_error(clear=True) == 0
+    dec.close()
+
+
+def _plan(dec, kv, B, comm):
+    layers = []
+    for Ly, (kc, vc) in zip(dec.layers, kv):
+        ab, mlp = Ly.attn_block, Ly.mlp_block
+        layers.append(dict(w_qkv=ab.qkv_weight_km, w_o=Ly.o_proj.weight_km,
+                           w_gate_up=mlp.gate_up_weight_il, w_down=mlp.down_weight_km,
+                           input_norm=ab.input_norm_weight, post_norm=mlp.post_norm_weight,
+                           q_norm=ab.q_norm_weight, k_norm=ab.k_norm_weight, k_cache=kc,
+                           v_cache=vc))
+    cos, sin, _ = dec.rotary.tables(DEV)
+    H = dec.layers[0].attn_block.input_norm_weight.numel()
+    return ops.DecodeTPPlan(layers, batch=B, hidden=H, q_heads=dec.num_q_heads,
+                            kv_heads=dec.num_kv_heads,
+                            inter=dec.layers[0].mlp_block.down_weight_km.shape[1],
+                            max_seq=kv[0][0].shape[2], eps=dec._eps, cos=cos, sin=sin, comm=comm)
+
+
+@pytest.mark.parametrize("B,P", [(8, 200), (3, 1000)])
+def test_tp8_shard_step_matches_the_per_kernel_layers(B, P):
+    spec = loader_fused.TextSpec(hidden=4096, q_heads=4, kv_heads=1, inter=1536, vocab=2048,
+                                 layers=2)
+    dec = loader_fused.random_decoder(spec, 0, 1, DEV, seed=3, max_seq=2048)
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, spec.vocab, (B, P), generator=g).to(DEV)
+    kv = dec.init_kv_cache(B)
+    dec.prefill(ids, kv)
+    kv2 = [(k.clone(), v.clone()) for k, v in kv]
+    comm = SoloComm(max_cols=spec.hidden, device=DEV)
+    plan = _plan(dec, kv2, B, comm)
+    tok = torch.randint(0, spec.vocab, (B, 2), generator=g).to(DEV)
+    for step in range(2):
+        pos = P + step
+        x0 = dec._embed(tok[:, step:step + 1]).view(B, -1)
+        want = x0.view(B, 1, -1)
+        for i in range(spec.layers):
+            want = dec.forward_layer(want, i, kv, pos, 1)
+        got = x0.clone()
+        kv_len = torch.tensor([pos + 1], dtype=torch.int32, device=DEV)
+        plan.run(got, kv_len)
+        torch.cuda.synchronize()
+        assert ops.device_error(clear=True) == 0
+        compare(f"step {step} hidden", got.float().cpu(), want.view(B, -1).float().cpu(),
+                max_abs=3e-2, rel_scale=True, min_cos=0.9999)
+        for i in range(spec.layers):
+            compare(f"step {step} layer {i} k row", kv2[i][0][:, :, pos].float().cpu(),
+                    kv[i][0][:, :, pos].float().cpu(), max_abs=2e-2, min_cos=0.9999)
+            compare(f"step {step} layer {i} v row", kv2[i][1][:, :, pos].float().cpu(),
+                    kv[i][1][:, :, pos].float().cpu(), max_abs=2e-2, min_cos=0.9999)
+    plan.close()
+    comm.close()

@@ -1,6 +1,8 @@
 """Tensor-parallel decoder on 2 GPUs (one process per GPU, NCCL): greedy
 tokens and prefill logits vs the reference decoder run at TP2 (fixture
-decoder_tiny_tp2).  Skipped when fewer than 2 GPUs are visible."""
+decoder_tiny_tp2), through NCCL, through the in-kernel all-reduce of the
+row-parallel projections, and through the step kernel (every layer of a decode
+step in one launch per GPU).  Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -53,6 +55,15 @@ def _worker(rank, world, port, q):
         # same decode with o_proj/down all-reduced inside the kernel (peer memory)
         dec.enable_peer_allreduce()
         toks_peer = dec.generate(ids, max_new_tokens=c["new_tokens"], eos_token_id=-1)
+        # same decode through the step kernel: every layer of a step in one
+        # launch per GPU, the all-reduce inside it (q3_decode_tp)
+        dec.use_tp_kernel = True
+        dec._graphs.clear()
+        dec.enable_peer_allreduce()          # creates the step kernel's communicator
+        toks_mk = dec.generate(ids, max_new_tokens=c["new_tokens"], eos_token_id=-1)
+        mk_ran = any(p_ is not None for p_ in dec._tp_plans.values())
+        dec.use_tp_kernel = False
+        dec._graphs.clear()
         # the fused kernel on its own: C = R + sum_r A_r W_r^T, identical on all ranks
         from q3vl import ops
         M, N, K = 8, 4096, 1024
@@ -75,7 +86,7 @@ def _worker(rank, world, port, q):
         same = all(torch.equal(gathered[0].cpu(), x.cpu()) for x in gathered)
         err = max((o.float() - want).abs().max().item() for o in outs)
         if rank == 0:
-            q.put((logits.numpy(), toks, toks_peer, err, same, ss_ok))
+            q.put((logits.numpy(), toks, toks_peer, toks_mk, mk_ran, err, same, ss_ok))
         dist.barrier()
         dec.close()
         dist.barrier()
@@ -96,7 +107,7 @@ def test_tp2_decoder_matches_reference():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    logits, toks, toks_peer, err, same, ss_ok = q.get(timeout=300)
+    logits, toks, toks_peer, toks_mk, mk_ran, err, same, ss_ok = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -109,6 +120,8 @@ def test_tp2_decoder_matches_reference():
 
     assert toks == want, f"NCCL path: first mismatch at step {first_diff(toks)}"
     assert toks_peer == want, f"peer all-reduce: first mismatch at step {first_diff(toks_peer)}"
+    assert mk_ran, "the step kernel did not run"
+    assert toks_mk == want, f"step kernel: first mismatch at step {first_diff(toks_mk)}"
     assert same, "ranks disagree on the all-reduced projection"
     assert err < 0.25, f"gemm_ar max-abs {err} (bf16 output of magnitude ~10)"
     assert ss_ok, "gemm_ar sums of squares (ss_out) disagree with the stored output"
