@@ -81,7 +81,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 struct FlashParams {
   __nv_bfloat16* out;
   int64_t os_b, os_h, os_s;
-  int Hq, Hkv, S;
+  int Hq, Hkv, S, B;
   int64_t q_rows_per_head;   // rows of one (b, h) in the Q map (= S)
   int64_t kv_rows_per_head;  // rows of one (b, kv head) in the K/V maps (= cache length)
   int64_t start;
@@ -696,6 +696,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// The kernel is persistent: min(items, SMs) CTAs, where an item is one
+// (query row block, head pair, sequence).  Items run longest first (the
+// causal work of a row block grows with its index), dealt to the CTAs in a
+// snake order (round r gives item r * grid + c, or r * grid + grid - 1 - c on
+// odd rounds) so each CTA's total work is nearly the same.  Barrier phases run
+// on across items: the producer loads an item's Q once the previous item's S
+// MMAs are done (q_empty), and the first PV of an item overwrites O[t] only
+// after the softmax warps have read out the previous item's O[t] (o_empty).
+struct PpItem {
+  int qb, h0, b;
+};
+__device__ __forceinline__ int pp_items(const FlashParams& p) {
+  return ((p.S + kFM - 1) / kFM) * (p.Hq / 2) * p.B;
+}
+__device__ __forceinline__ bool pp_item(const FlashParams& p, int round, PpItem& it) {
+  const int n = pp_items(p), G = gridDim.x, c = blockIdx.x;
+  const int idx = round * G + ((round & 1) ? (G - 1 - c) : c);
+  if (idx >= n) return false;
+  const int pairs = p.Hq / 2, per = pairs * p.B, nqb = (p.S + kFM - 1) / kFM;
+  it.qb = nqb - 1 - idx / per;
+  const int rem = idx % per;
+  it.h0 = 2 * (rem % pairs);
+  it.b = rem / pairs;
+  return true;
+}
+
 template <bool PAGED>
 __global__ void __launch_bounds__(kPpThreads, 1)
     attn_prefill_tc_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -715,24 +741,26 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   uint64_t* v_empty = bar + 7;   // [2] MMA commit after PV_j of both tiles
   uint64_t* s_full = bar + 9;    // [tile] S_j(t) (and PV_{j-1}(t)) complete
   uint64_t* p_full = bar + 11;   // [tile] P_j(t) in TMEM: one arrival per softmax warp
-  uint64_t* o_final = bar + 13;  // [tile] the last PV of the tile complete
-  uint64_t* mma_done = bar + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+  uint64_t* o_final = bar + 13;  // [tile] the item's last PV of the tile complete
+  uint64_t* o_empty = bar + 15;  // [tile] the item's O[t] read out: one arrival per warp
+  uint64_t* q_empty = bar + 17;  // the item's S MMAs complete (Q may be replaced)
+  uint64_t* mma_done = bar + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
-  const int h0 = 2 * blockIdx.y, b = blockIdx.z;
-  const int kvh = h0 / (p.Hq / p.Hkv);
-  const int q0 = qb * kFM;
-  const int q_valid = min(kFM, p.S - q0);
   const int64_t kv_total = p.start + p.S;
-  const int64_t kv_need = p.causal ? min64(p.start + q0 + kFM, kv_total) : kv_total;
-  const int n_kb = (int)((kv_need + kPpN - 1) / kPpN);
-  const int kv_plane = b * p.Hkv + kvh;
+  const int G = p.Hq / p.Hkv;
+  const int n_items = pp_items(p);
+  const int rounds = (n_items + gridDim.x - 1) / gridDim.x;
+  auto n_kb_of = [&](int qb) {
+    const int64_t kv_need = p.causal ? min64(p.start + qb * kFM + kFM, kv_total) : kv_total;
+    return (int)((kv_need + kPpN - 1) / kPpN);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -741,6 +769,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_final[i], 1);
+      mbar_init(&o_empty[i], 4);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -761,59 +790,64 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * kPpQBytes);
-      for (int t = 0; t < 2; ++t) {
-        const int qrow = (int)(((int64_t)b * p.Hq + h0 + t) * p.q_rows_per_head + q0);
-        tma_load_2d(smem + t * kPpQBytes, &tmQ, q_full, 0, qrow, kCacheEvictNormal);
-        tma_load_2d(smem + t * kPpQBytes + kPpQBytes / 2, &tmQ, q_full, 64, qrow,
-                    kCacheEvictNormal);
-      }
-      int issued = 0;
-      for (int j = 0; j < n_kb && !*abort_flag; ++j) {
-        const int s = j & 1;
-        const uint32_t ph_prev = ((j >> 1) - 1) & 1;
-        const int key0 = j * kPpN;
-        if (j >= 2 && !mbar_wait(&k_empty[s], ph_prev, p.err, 0x631)) { *abort_flag = 1; break; }
-        // paged: the tile's rows in the pool (a 128-key tile never straddles
-        // pages); an entry outside the pool is recorded and page 0 read
-        int prow = 0;
-        if constexpr (PAGED) {
-          int pg = p.pages[(int64_t)b * p.pages_stride + key0 / p.page_tokens];
-          if (pg < 0 || pg >= p.num_pages) {
-            report_timeout(p.err, 0x63a);
-            pg = 0;
+      int T = 0, ic = 0, nk = 0, nv = 0;
+      bool ok = true;
+      for (int r = 0; ok && r < rounds && !*abort_flag; ++r) {
+        PpItem itm;
+        if (!pp_item(p, r, itm)) continue;
+        const int q0 = itm.qb * kFM, n_kb = n_kb_of(itm.qb);
+        const int kvh = itm.h0 / G, kv_plane = itm.b * p.Hkv + kvh;
+        if (ic >= 1 && !mbar_wait(q_empty, (ic - 1) & 1, p.err, 0x63b)) { ok = false; break; }
+        mbar_arrive_expect_tx(q_full, 2 * kPpQBytes);
+        for (int t = 0; t < 2; ++t) {
+          const int qrow = (int)(((int64_t)itm.b * p.Hq + itm.h0 + t) * p.q_rows_per_head + q0);
+          tma_load_2d(smem + t * kPpQBytes, &tmQ, q_full, 0, qrow, kCacheEvictNormal);
+          tma_load_2d(smem + t * kPpQBytes + kPpQBytes / 2, &tmQ, q_full, 64, qrow,
+                      kCacheEvictNormal);
+        }
+        ++ic;
+        for (int j = 0; j < n_kb; ++j, ++T) {
+          const int s = T & 1;
+          const uint32_t ph_prev = ((T >> 1) - 1) & 1;
+          const int key0 = j * kPpN;
+          if (T >= 2 && !mbar_wait(&k_empty[s], ph_prev, p.err, 0x631)) { ok = false; break; }
+          // paged: the tile's rows in the pool (a 128-key tile never straddles
+          // pages); an entry outside the pool is recorded and page 0 read
+          int prow = 0;
+          if constexpr (PAGED) {
+            int pg = p.pages[(int64_t)itm.b * p.pages_stride + key0 / p.page_tokens];
+            if (pg < 0 || pg >= p.num_pages) {
+              report_timeout(p.err, 0x63a);
+              pg = 0;
+            }
+            prow = (int)(((int64_t)pg * p.Hkv + kvh) * p.page_tokens + key0 % p.page_tokens);
           }
-          prow = (int)(((int64_t)pg * p.Hkv + kvh) * p.page_tokens + key0 % p.page_tokens);
+          uint8_t* dk = smem + kPpOffK + s * kPpKVBytes;
+          mbar_arrive_expect_tx(&k_full[s], kPpKVBytes);
+          if constexpr (PAGED) {
+            tma_load_2d(dk, &tmK, &k_full[s], 0, prow, kCacheEvictNormal);
+            tma_load_2d(dk + kPpHalf, &tmK, &k_full[s], 64, prow, kCacheEvictNormal);
+          } else {
+            tma_load_3d(dk, &tmK, &k_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+            tma_load_3d(dk + kPpHalf, &tmK, &k_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+          }
+          nk = T + 1;
+          if (T >= 2 && !mbar_wait(&v_empty[s], ph_prev, p.err, 0x632)) { ok = false; break; }
+          uint8_t* dv = smem + kPpOffV + s * kPpKVBytes;
+          mbar_arrive_expect_tx(&v_full[s], kPpKVBytes);
+          if constexpr (PAGED) {
+            tma_load_2d(dv, &tmV, &v_full[s], 0, prow, kCacheEvictNormal);
+            tma_load_2d(dv + kPpHalf, &tmV, &v_full[s], 64, prow, kCacheEvictNormal);
+          } else {
+            tma_load_3d(dv, &tmV, &v_full[s], 0, key0, kv_plane, kCacheEvictNormal);
+            tma_load_3d(dv + kPpHalf, &tmV, &v_full[s], 64, key0, kv_plane, kCacheEvictNormal);
+          }
+          nv = T + 1;
         }
-        uint8_t* dk = smem + kPpOffK + s * kPpKVBytes;
-        mbar_arrive_expect_tx(&k_full[s], kPpKVBytes);
-        if constexpr (PAGED) {
-          tma_load_2d(dk, &tmK, &k_full[s], 0, prow, kCacheEvictNormal);
-          tma_load_2d(dk + kPpHalf, &tmK, &k_full[s], 64, prow, kCacheEvictNormal);
-        } else {
-          tma_load_3d(dk, &tmK, &k_full[s], 0, key0, kv_plane, kCacheEvictNormal);
-          tma_load_3d(dk + kPpHalf, &tmK, &k_full[s], 64, key0, kv_plane, kCacheEvictNormal);
-        }
-        if (j >= 2 && !mbar_wait(&v_empty[s], ph_prev, p.err, 0x632)) {
-          *abort_flag = 1;
-          issued = -(j + 1);  // K_j issued, V_j not
-          break;
-        }
-        uint8_t* dv = smem + kPpOffV + s * kPpKVBytes;
-        mbar_arrive_expect_tx(&v_full[s], kPpKVBytes);
-        if constexpr (PAGED) {
-          tma_load_2d(dv, &tmV, &v_full[s], 0, prow, kCacheEvictNormal);
-          tma_load_2d(dv + kPpHalf, &tmV, &v_full[s], 64, prow, kCacheEvictNormal);
-        } else {
-          tma_load_3d(dv, &tmV, &v_full[s], 0, key0, kv_plane, kCacheEvictNormal);
-          tma_load_3d(dv + kPpHalf, &tmV, &v_full[s], 64, key0, kv_plane, kCacheEvictNormal);
-        }
-        issued = j + 1;
       }
+      if (!ok) *abort_flag = 1;
       // let the copies this thread issued land before the CTA exits
-      mbar_wait(q_full, 0, nullptr, 0);
-      const int nk = issued < 0 ? -issued : issued;
-      const int nv = issued < 0 ? -issued - 1 : issued;
+      if (ic > 0) mbar_wait(q_full, (ic - 1) & 1, nullptr, 0);
       for (int j = max(0, nk - 2); j < nk; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, 0);
       for (int j = max(0, nv - 2); j < nv; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, 0);
     }
@@ -822,8 +856,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kFM, kPpN);
       constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(kFM, kFD);
-      auto issue_s = [&](int j, int t) {
-        const uint32_t kb = s_base + kPpOffK + (j & 1) * kPpKVBytes;
+      auto issue_s = [&](int T, int t) {
+        const uint32_t kb = s_base + kPpOffK + (T & 1) * kPpKVBytes;
         const uint32_t qa = s_base + t * kPpQBytes;
 #pragma unroll 1
         for (int ks = 0; ks < kFD / 16; ++ks)
@@ -831,40 +865,60 @@ __global__ void __launch_bounds__(kPpThreads, 1)
                       umma_desc_k_sw128(kb + (ks >> 2) * kPpHalf) + 2 * (ks & 3), idesc_s, ks != 0);
         tc_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int j, int t) {
-        const uint32_t vb = s_base + kPpOffV + (j & 1) * kPpKVBytes;
+      auto issue_pv = [&](int T, int t, bool first) {
+        const uint32_t vb = s_base + kPpOffV + (T & 1) * kPpKVBytes;
 #pragma unroll 1
         for (int ks = 0; ks < kPpN / 16; ++ks)
           tc_mma_bf16_ts(tmem + 2 * kPpN + t * kFD, tmem + t * kPpN + ks * 8,
                          umma_desc_mn_sw128(vb + ks * 2048, kPpHalf, 1024u), idesc_o,
-                         j > 0 || ks > 0);
+                         !first || ks > 0);
       };
-      bool ok = mbar_wait(q_full, 0, p.err, 0x633) && mbar_wait(&k_full[0], 0, p.err, 0x634);
-      tc_fence_after();
-      if (ok) {
-        issue_s(0, 0);
-        issue_s(0, 1);
-        tc_commit(&k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_kb && !*abort_flag; ++j) {
-        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 0x635)) { ok = false; break; }
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, p.err, 0x636)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(j, t);
-          if (t == 1) tc_commit(&v_empty[j & 1]);
-          if (j + 1 < n_kb) {
-            if (t == 0 && !mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err, 0x637)) {
+      bool ok = true;
+      int T = 0, ic = 0;
+      for (int r = 0; ok && r < rounds && !*abort_flag; ++r) {
+        PpItem itm;
+        if (!pp_item(p, r, itm)) continue;
+        const int n_kb = n_kb_of(itm.qb);
+        if (!mbar_wait(q_full, ic & 1, p.err, 0x633) ||
+            !mbar_wait(&k_full[T & 1], (T >> 1) & 1, p.err, 0x634)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_s(T, 0);
+        issue_s(T, 1);
+        tc_commit(&k_empty[T & 1]);
+        if (n_kb == 1) tc_commit(q_empty);
+        for (int j = 0; ok && j < n_kb; ++j) {
+          const int Tj = T + j;
+          if (!mbar_wait(&v_full[Tj & 1], (Tj >> 1) & 1, p.err, 0x635)) { ok = false; break; }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!mbar_wait(&p_full[t], Tj & 1, p.err, 0x636) ||
+                (j == 0 && ic >= 1 && !mbar_wait(&o_empty[t], (ic - 1) & 1, p.err, 0x63c))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_s(j + 1, t);
-            if (t == 1) tc_commit(&k_empty[(j + 1) & 1]);
-          } else {
-            tc_commit(&o_final[t]);
+            issue_pv(Tj, t, j == 0);
+            if (t == 1) tc_commit(&v_empty[Tj & 1]);
+            if (j + 1 < n_kb) {
+              if (t == 0 && !mbar_wait(&k_full[(Tj + 1) & 1], ((Tj + 1) >> 1) & 1, p.err, 0x637)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_s(Tj + 1, t);
+              if (t == 1) {
+                tc_commit(&k_empty[(Tj + 1) & 1]);
+                if (j + 2 == n_kb) tc_commit(q_empty);  // the item's last S MMAs
+              }
+            } else {
+              tc_commit(&o_final[t]);
+            }
           }
         }
+        T += n_kb;
+        ++ic;
       }
       if (!ok) *abort_flag = 1;
       // every MMA issued above has completed before TMEM is released
@@ -879,100 +933,117 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_off + t * kPpN;
     const uint32_t o_col = tmem + lane_off + 2 * kPpN + t * kFD;
-    const int64_t qpos = p.start + q0 + row;
-    const int64_t qpos_min = p.start + q0;
-    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kb; ++j) {
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      if (!warp_wait(&s_full[t], j & 1, p.err, 0x638)) { ok = false; break; }
-      tc_fence_after();
-      float sc[kPpN];
+    int T = 0, ic = 0;
+    for (int r = 0; ok && r < rounds; ++r) {
+      PpItem itm;
+      if (!pp_item(p, r, itm)) continue;
+      const int q0 = itm.qb * kFM, n_kb = n_kb_of(itm.qb);
+      const int q_valid = min(kFM, p.S - q0);
+      const int64_t qpos = p.start + q0 + row;
+      const int64_t qpos_min = p.start + q0;
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_kb; ++j) {
+        const int Tj = T + j;
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+        if (!warp_wait(&s_full[t], Tj & 1, p.err, 0x638)) { ok = false; break; }
+        tc_fence_after();
+        float sc[kPpN];
+        {
+          uint32_t rr[kPpN];
 #pragma unroll
-      for (int c = 0; c < kPpN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32cols(s_col + c * 32, r);
-        tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sc[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
-      }
-      const int kbase = j * kPpN;
-      // masks only where a key can lie past a row's position or past the end
-      if (kbase + kPpN - 1 > qpos_min || kbase + kPpN > kv_total) {
-        const int lim = (int)min64(kv_total - 1, p.causal ? qpos : kv_total - 1) - kbase;
-#pragma unroll
-        for (int c = 0; c < kPpN; ++c)
-          if (c > lim) sc[c] = -INFINITY;
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kPpN; ++c) mx = fmaxf(mx, sc[c]);
-      const float m_new = fmaxf(m_used, mx);
-      const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
-      const bool rescale = move && j > 0 && m_used != -INFINITY;
-      const float corr = rescale ? ex2_approx(m_used - m_new) : 1.f;
-      if (move) {
-        l *= ex2_approx(m_used - m_new);  // m_used = -inf: l is 0 and stays 0
-        m_used = m_new;
-      }
-      const float base = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < kPpN / 32; ++c) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2_approx(sc[c * 32 + 2 * i] - base);
-          const float p1 = ex2_approx(sc[c * 32 + 2 * i + 1] - base);
-          rs += p0 + p1;
-          w[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O[t] holds tiles 0..j-1, complete (covered by the commit of S_j(t)):
-        // rescale it to the new base before PV_j adds to it
-#pragma unroll 1
-        for (int c = 0; c < kFD / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32cols(o_col + c * 32, r);
+          for (int c = 0; c < kPpN / 32; ++c) {
+            uint32_t(&r32)[32] = *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]);
+            tmem_ld_32cols(s_col + c * 32, r32);
+          }
           tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st_32cols(o_col + c * 32, r);
+          for (int i = 0; i < kPpN; ++i) sc[i] = __uint_as_float(rr[i]) * p.scale_log2;
         }
+        const int kbase = j * kPpN;
+        // masks only where a key can lie past a row's position or past the end
+        if (kbase + kPpN - 1 > qpos_min || kbase + kPpN > kv_total) {
+          const int lim = (int)min64(kv_total - 1, p.causal ? qpos : kv_total - 1) - kbase;
+#pragma unroll
+          for (int c = 0; c < kPpN; ++c)
+            if (c > lim) sc[c] = -INFINITY;
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kPpN; ++c) mx = fmaxf(mx, sc[c]);
+        const float m_new = fmaxf(m_used, mx);
+        const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
+        const bool rescale = move && j > 0 && m_used != -INFINITY;
+        const float corr = rescale ? ex2_approx(m_used - m_new) : 1.f;
+        if (move) {
+          l *= ex2_approx(m_used - m_new);  // m_used = -inf: l is 0 and stays 0
+          m_used = m_new;
+        }
+        const float base = (m_used == -INFINITY) ? 0.f : m_used;
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < kPpN / 32; ++c) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2_approx(sc[c * 32 + 2 * i] - base);
+            const float p1 = ex2_approx(sc[c * 32 + 2 * i + 1] - base);
+            rs += p0 + p1;
+            w[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O[t] holds tiles 0..j-1 of this item, complete (covered by the
+          // commit of S_j(t)): rescale it to the new base before PV_j adds to it
+#pragma unroll 1
+          for (int c = 0; c < kFD / 32; ++c) {
+            uint32_t r32[32];
+            tmem_ld_32cols(o_col + c * 32, r32);
+            tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r32[i] = __float_as_uint(__uint_as_float(r32[i]) * corr);
+            tmem_st_32cols(o_col + c * 32, r32);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+        l += rs;
       }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-      l += rs;
-    }
-    if (!ok) *abort_flag = 1;
-    // the last PV of this tile, then O / l to global memory
-    if (__all_sync(0xffffffffu, ok) && n_kb > 0 && warp_wait(&o_final[t], 0, p.err, 0x639)) {
+      if (!ok) break;
+      // the item's last PV of this tile, then O / l to global memory, then O[t]
+      // is free for the next item
+      if (!warp_wait(&o_final[t], ic & 1, p.err, 0x639)) { ok = false; break; }
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst =
-          p.out + b * p.os_b + (int64_t)(h0 + t) * p.os_h + (int64_t)(q0 + row) * p.os_s;
+      __nv_bfloat16* dst = p.out + itm.b * p.os_b + (int64_t)(itm.h0 + t) * p.os_h +
+                           (int64_t)(q0 + row) * p.os_s;
 #pragma unroll
       for (int c = 0; c < kFD / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32cols(o_col + c * 32, r);
+        uint32_t r32[32];
+        tmem_ld_32cols(o_col + c * 32, r32);
         tc_wait_ld();
         if (row < q_valid) {
 #pragma unroll
           for (int d = 0; d < 32; d += 8) {
             uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv);
-            u.y = pack_bf16x2(__uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
-            u.z = pack_bf16x2(__uint_as_float(r[d + 4]) * inv, __uint_as_float(r[d + 5]) * inv);
-            u.w = pack_bf16x2(__uint_as_float(r[d + 6]) * inv, __uint_as_float(r[d + 7]) * inv);
+            u.x = pack_bf16x2(__uint_as_float(r32[d]) * inv, __uint_as_float(r32[d + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(r32[d + 2]) * inv, __uint_as_float(r32[d + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(r32[d + 4]) * inv, __uint_as_float(r32[d + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(r32[d + 6]) * inv, __uint_as_float(r32[d + 7]) * inv);
             *reinterpret_cast<uint4*>(dst + c * 32 + d) = u;
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[t]);
+      T += n_kb;
+      ++ic;
     }
+    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -1030,7 +1101,7 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
   FlashParams p{};
   p.out = (__nv_bfloat16*)out;
   p.os_b = o_strides[0]; p.os_h = o_strides[1]; p.os_s = o_strides[2];
-  p.Hq = Hq; p.Hkv = Hkv; p.S = S;
+  p.Hq = Hq; p.Hkv = Hkv; p.S = S; p.B = B;
   p.q_rows_per_head = S;
   p.kv_rows_per_head = kv_rows_per_head;
   p.start = start_pos;
@@ -1048,7 +1119,8 @@ extern "C" int q3_attn_prefill_tc(const void* q, const void* k, const void* v, v
     rc = make_tmap_3d_rows128(&tv, v, start_pos + S, (int64_t)B * Hkv, kv_rows_per_head * kFD,
                               kPpN);
     if (rc) return rc;
-    dim3 grid2((S + kFM - 1) / kFM, Hq / 2, B);
+    const int64_t items = (int64_t)((S + kFM - 1) / kFM) * (Hq / 2) * B;
+    dim3 grid2((unsigned)min64(items, (int64_t)num_sms()));
     return launch_ex(attn_prefill_tc_pp_kernel<false>, grid2, dim3(kPpThreads), kPpSmem,
                      (cudaStream_t)stream, 1, tq, tk, tv, p);
   }
@@ -1107,7 +1179,7 @@ extern "C" int q3_attn_prefill_tc_paged(const void* q, const void* k_pages, cons
   FlashParams p{};
   p.out = (__nv_bfloat16*)out;
   p.os_b = o_strides[0]; p.os_h = o_strides[1]; p.os_s = o_strides[2];
-  p.Hq = Hq; p.Hkv = Hkv; p.S = S;
+  p.Hq = Hq; p.Hkv = Hkv; p.S = S; p.B = B;
   p.q_rows_per_head = S;
   p.kv_rows_per_head = 0;
   p.start = start_pos;
@@ -1118,7 +1190,8 @@ extern "C" int q3_attn_prefill_tc_paged(const void* q, const void* k_pages, cons
   p.pages_stride = table_stride;
   p.page_tokens = page_tokens;
   p.num_pages = num_pages;
-  dim3 grid((S + kFM - 1) / kFM, Hq / 2, B);
+  const int64_t items = (int64_t)((S + kFM - 1) / kFM) * (Hq / 2) * B;
+  dim3 grid((unsigned)min64(items, (int64_t)num_sms()));
   return launch_ex(attn_prefill_tc_pp_kernel<true>, grid, dim3(kPpThreads), kPpSmem,
                    (cudaStream_t)stream, 1, tq, tk, tv, p);
 }

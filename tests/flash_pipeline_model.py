@@ -509,21 +509,26 @@ class ModelMN(Model):
 
 
 class ModelPP(Model):
-    """Variant 2 of the kernel (attn_prefill_tc_pp_kernel): two query tiles
-    (two heads of one KV head) per CTA and 128-key tiles.  K and V have their
-    own 2-deep rings (k_empty after S_j of both tiles, v_empty after PV_j of
-    both); the MMA thread alternates PV_j(0), S_{j+1}(0), PV_j(1), S_{j+1}(1);
-    P_j(t) overwrites S[t] in TMEM (same buffer here, tagged ("p", j)), so the
-    next S MMA of the tile may only run after the PV that reads it, which
-    program order on the tensor pipe gives; O[t] accumulates in TMEM and a
-    softmax warp may rescale its quarter of O[t] once it has seen S_j(t) (the
-    commit of S_j(t) covers PV_{j-1}(t)).  One role per softmax warp: warps
-    2-5 hold tile 0, warps 6-9 tile 1."""
+    """Variant 2 of the kernel (attn_prefill_tc_pp_kernel): persistent, two
+    query tiles (two heads of one KV head) per item, 128-key tiles.  `items`
+    lists the key-tile count of each item this CTA runs in order (n_kb alone
+    is one item).  K and V have their own 2-deep rings (k_empty after S_j of
+    both tiles, v_empty after PV_j of both); the MMA thread alternates
+    PV_j(0), S_{j+1}(0), PV_j(1), S_{j+1}(1); P_j(t) overwrites S[t] in TMEM
+    (same buffer here, tagged ("p", item, j)), so the next S MMA of the tile
+    runs only after the PV that reads it (program order on the tensor pipe);
+    O[t] accumulates in TMEM and a softmax warp may rescale its quarter once it
+    has seen S_j(t) (the commit of S_j(t) covers PV_{j-1}(t)).  Across items:
+    the producer reloads Q after q_empty (the item's last S MMAs), and an
+    item's first PV overwrites O[t] only after every softmax warp of the tile
+    read out the previous item's O[t] (o_empty).  One role per softmax warp:
+    warps 2-5 hold tile 0, warps 6-9 tile 1."""
 
     KV128 = 128 * 128 * 2
 
-    def __init__(self, n_kb: int, seed: int, fault_at=None, rescale_p: float = 0.3):
+    def __init__(self, n_kb: int, seed: int, fault_at=None, rescale_p: float = 0.3, items=None):
         super().__init__(n_kb, seed, fault_at)
+        self.items = list(items) if items is not None else [n_kb]
         self.k_full = [Bar(f"k_full{i}", 1) for i in range(2)]
         self.k_empty = [Bar(f"k_empty{i}", 1) for i in range(2)]
         self.v_full = [Bar(f"v_full{i}", 1) for i in range(2)]
@@ -531,6 +536,8 @@ class ModelPP(Model):
         self.s_full = [Bar(f"s_full{t}", 1) for t in range(2)]
         self.p_full = [Bar(f"p_full{t}", 4) for t in range(2)]
         self.o_final = [Bar(f"o_final{t}", 1) for t in range(2)]
+        self.o_empty = [Bar(f"o_empty{t}", 4) for t in range(2)]
+        self.q_empty = Bar("q_empty", 1)
         self.rescale_p = rescale_p
         self.rescales = 0
 
@@ -542,78 +549,103 @@ class ModelPP(Model):
         return roles
 
     def producer(self):
-        n_kb, KV = self.n_kb, self.KV128
-        self.q_full.arrive_expect_tx(2 * Q_BYTES)
-        self.tma_load("Q0", self.q_full, Q_BYTES, "q")
-        self.tma_load("Q1", self.q_full, Q_BYTES, "q")
-        yield None
-        nk = nv = 0
-        for j in range(n_kb):
-            if self.abort:
+        KV = self.KV128
+        T = ic = nk = nv = 0
+        ok = True
+        for it, n_kb in enumerate(self.items):
+            if not ok or self.abort:
                 break
-            s = j & 1
-            if j >= 2 and not (yield Wait(self.k_empty[s], (j >> 1) - 1, 0x631)):
-                self.abort = True
+            if ic >= 1 and not (yield Wait(self.q_empty, ic - 1, 0x63b)):
+                ok = False
                 break
-            self.k_full[s].arrive_expect_tx(KV)
-            self.tma_load(f"K{s}", self.k_full[s], KV, j)
-            nk = j + 1
-            if j >= 2 and not (yield Wait(self.v_empty[s], (j >> 1) - 1, 0x632)):
-                self.abort = True
-                break
-            self.v_full[s].arrive_expect_tx(KV)
-            self.tma_load(f"V{s}", self.v_full[s], KV, j)
-            nv = j + 1
+            self.q_full.arrive_expect_tx(2 * Q_BYTES)
+            self.tma_load("Q0", self.q_full, Q_BYTES, ("q", it))
+            self.tma_load("Q1", self.q_full, Q_BYTES, ("q", it))
+            ic += 1
             yield None
-        yield Wait(self.q_full, 0, None)
+            for j in range(n_kb):
+                s = T & 1
+                if T >= 2 and not (yield Wait(self.k_empty[s], (T >> 1) - 1, 0x631)):
+                    ok = False
+                    break
+                self.k_full[s].arrive_expect_tx(KV)
+                self.tma_load(f"K{s}", self.k_full[s], KV, (it, j))
+                nk = T + 1
+                if T >= 2 and not (yield Wait(self.v_empty[s], (T >> 1) - 1, 0x632)):
+                    ok = False
+                    break
+                self.v_full[s].arrive_expect_tx(KV)
+                self.tma_load(f"V{s}", self.v_full[s], KV, (it, j))
+                nv = T + 1
+                T += 1
+                yield None
+        if not ok:
+            self.abort = True
+        if ic > 0:
+            yield Wait(self.q_full, ic - 1, None)
         for j in range(max(0, nk - 2), nk):
             yield Wait(self.k_full[j & 1], j >> 1, None)
         for j in range(max(0, nv - 2), nv):
             yield Wait(self.v_full[j & 1], j >> 1, None)
 
     def mma_issuer(self):
-        n_kb = self.n_kb
-
-        def issue_s(j, t):
-            self.mma([(f"Q{t}", "q"), (f"K{j & 1}", j)],
-                     [(f"S{t}.{w}", ("s", j)) for w in range(4)])
+        def issue_s(it, j, T, t):
+            self.mma([(f"Q{t}", ("q", it)), (f"K{T & 1}", (it, j))],
+                     [(f"S{t}.{w}", ("s", it, j)) for w in range(4)])
             self.commit(self.s_full[t])
 
-        def issue_pv(j, t):
-            reads = [(f"S{t}.{w}", ("p", j)) for w in range(4)] + [(f"V{j & 1}", j)]
+        def issue_pv(it, j, T, t):
+            reads = [(f"S{t}.{w}", ("p", it, j)) for w in range(4)] + [(f"V{T & 1}", (it, j))]
             if j > 0:
-                reads += [(f"O{t}.{w}", j - 1) for w in range(4)]
-            self.mma(reads, [(f"O{t}.{w}", j) for w in range(4)])
+                reads += [(f"O{t}.{w}", (it, j - 1)) for w in range(4)]
+            self.mma(reads, [(f"O{t}.{w}", (it, j)) for w in range(4)])
 
-        ok = (yield Wait(self.q_full, 0, 0x633)) and (yield Wait(self.k_full[0], 0, 0x634))
-        if ok:
-            issue_s(0, 0)
-            issue_s(0, 1)
-            self.commit(self.k_empty[0])
-        j = 0
-        while ok and j < n_kb and not self.abort:
-            if not (yield Wait(self.v_full[j & 1], j >> 1, 0x635)):
+        ok = True
+        T = ic = 0
+        for it, n_kb in enumerate(self.items):
+            if not ok or self.abort:
+                break
+            if not (yield Wait(self.q_full, ic, 0x633)) or \
+                    not (yield Wait(self.k_full[T & 1], T >> 1, 0x634)):
                 ok = False
                 break
-            for t in range(2):
-                if not (yield Wait(self.p_full[t], j, 0x636)):
+            issue_s(it, 0, T, 0)
+            issue_s(it, 0, T, 1)
+            self.commit(self.k_empty[T & 1])
+            if n_kb == 1:
+                self.commit(self.q_empty)
+            for j in range(n_kb):
+                Tj = T + j
+                if not (yield Wait(self.v_full[Tj & 1], Tj >> 1, 0x635)):
                     ok = False
                     break
-                issue_pv(j, t)
-                if t == 1:
-                    self.commit(self.v_empty[j & 1])
-                if j + 1 < n_kb:
-                    if t == 0 and not (yield Wait(self.k_full[(j + 1) & 1], (j + 1) >> 1,
-                                                  0x637)):
+                for t in range(2):
+                    if not (yield Wait(self.p_full[t], Tj, 0x636)):
                         ok = False
                         break
-                    issue_s(j + 1, t)
+                    if j == 0 and ic >= 1 and not (yield Wait(self.o_empty[t], ic - 1, 0x63c)):
+                        ok = False
+                        break
+                    issue_pv(it, j, Tj, t)
                     if t == 1:
-                        self.commit(self.k_empty[(j + 1) & 1])
-                else:
-                    self.commit(self.o_final[t])
-                yield None
-            j += 1
+                        self.commit(self.v_empty[Tj & 1])
+                    if j + 1 < n_kb:
+                        if t == 0 and not (yield Wait(self.k_full[(Tj + 1) & 1], (Tj + 1) >> 1,
+                                                      0x637)):
+                            ok = False
+                            break
+                        issue_s(it, j + 1, Tj + 1, t)
+                        if t == 1:
+                            self.commit(self.k_empty[(Tj + 1) & 1])
+                            if j + 2 == n_kb:
+                                self.commit(self.q_empty)
+                    else:
+                        self.commit(self.o_final[t])
+                    yield None
+                if not ok:
+                    break
+            T += n_kb
+            ic += 1
         if not ok:
             self.abort = True
         self.commit(self.mma_done)
@@ -621,37 +653,45 @@ class ModelPP(Model):
 
     def softmax(self, t, w):
         agent = f"softmax{t}.{w}"
-        n_kb = self.n_kb
         ok = True
-        for j in range(n_kb):
-            if self.abort:
-                ok = False
-                break
-            if not (yield Wait(self.s_full[t], j, 0x638)):
-                ok = False
-                break
-            buf = f"S{t}.{w}"
-            self.begin(agent, buf, "r")
-            self.check(agent, buf, ("s", j))
-            yield None
-            self.end(agent, buf, "r")
-            self.begin(agent, buf, "w")            # P_j over S_j
-            self.mem[buf] = ("p", j)
-            yield None
-            self.end(agent, buf, "w")
-            if j > 0 and self.rng.random() < self.rescale_p:
-                self.rescales += 1
-                self.begin(agent, f"O{t}.{w}", "w")
-                self.check(agent, f"O{t}.{w}", j - 1)
+        T = ic = 0
+        for it, n_kb in enumerate(self.items):
+            for j in range(n_kb):
+                Tj = T + j
+                if self.abort:
+                    ok = False
+                    break
+                if not (yield Wait(self.s_full[t], Tj, 0x638)):
+                    ok = False
+                    break
+                buf = f"S{t}.{w}"
+                self.begin(agent, buf, "r")
+                self.check(agent, buf, ("s", it, j))
                 yield None
-                self.end(agent, f"O{t}.{w}", "w")
-            self.p_full[t].arrive()
+                self.end(agent, buf, "r")
+                self.begin(agent, buf, "w")            # P_j over S_j
+                self.mem[buf] = ("p", it, j)
+                yield None
+                self.end(agent, buf, "w")
+                if j > 0 and self.rng.random() < self.rescale_p:
+                    self.rescales += 1
+                    self.begin(agent, f"O{t}.{w}", "w")
+                    self.check(agent, f"O{t}.{w}", (it, j - 1))
+                    yield None
+                    self.end(agent, f"O{t}.{w}", "w")
+                self.p_full[t].arrive()
+            if not ok:
+                break
+            if not (yield Wait(self.o_final[t], ic, 0x639)):
+                ok = False
+                break
+            self.begin(agent, f"O{t}.{w}", "r")
+            self.check(agent, f"O{t}.{w}", (it, n_kb - 1))
+            yield None
+            self.end(agent, f"O{t}.{w}", "r")
+            self.o_empty[t].arrive()
+            self.seen[(t, w)].append(it)
+            T += n_kb
+            ic += 1
         if not ok:
             self.abort = True
-        if ok and n_kb > 0:
-            if (yield Wait(self.o_final[t], 0, 0x639)):
-                self.begin(agent, f"O{t}.{w}", "r")
-                self.check(agent, f"O{t}.{w}", n_kb - 1)
-                yield None
-                self.end(agent, f"O{t}.{w}", "r")
-                self.seen[(t, w)] = list(range(n_kb))

@@ -88,9 +88,11 @@ def test_tp8_shard_step_matches_the_per_kernel_layers(B, P):
         compare(f"step {step} hidden", got.float().cpu(), want.view(B, -1).float().cpu(),
                 max_abs=3e-2, rel_scale=True, min_cos=0.9999)
         for i in range(spec.layers):
+            # k rows are normed (values up to about 4, where a bf16 step is 1/32):
+            # the two paths round the projection's sum in a different order
             compare(f"step {step} layer {i} k row", kv2[i][0][:, :, pos].float().cpu(),
-                    kv[i][0][:, :, pos].float().cpu(), max_abs=2e-2, min_cos=0.9999)
+                    kv[i][0][:, :, pos].float().cpu(), max_abs=5e-2, min_cos=0.9999)
             compare(f"step {step} layer {i} v row", kv2[i][1][:, :, pos].float().cpu(),
-                    kv[i][1][:, :, pos].float().cpu(), max_abs=2e-2, min_cos=0.9999)
+                    kv[i][1][:, :, pos].float().cpu(), max_abs=5e-2, min_cos=0.9999)
     plan.close()
     comm.close()
