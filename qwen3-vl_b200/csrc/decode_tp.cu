@@ -64,6 +64,7 @@ constexpr int kHD = 128;
 constexpr int kPos = 64;                      // cache positions per attention tile
 constexpr int kMaxG = 8;                      // query heads per KV head
 constexpr int kPairs = kTok / 2;              // token pairs per exchanged row
+constexpr int kMaxSplitsMerge = 256;          // attention splits of one pair, at most
 constexpr int kSmemLimit = 232448;
 enum { kQKV = 0, kATT = 1, kO = 2, kGU = 3, kDN = 4, kPhases = 5 };
 
@@ -192,6 +193,7 @@ __device__ __forceinline__ void grid_sync(const Params& p, unsigned& target) {
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
       while (ld_acquire_gpu_u32(p.gbar) < target) {
+        __nanosleep(20);
         if ((++spins & 63u) == 0) {
           if (aborted(p)) break;
           if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -308,69 +310,111 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
 }
 
 // ------------------------------------------------------------- staging
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // Rows 0..M-1 of a [M, K] activation into the staging buffer (row stride
 // x_stride bytes), rows M..7 zero.  MODE 0: as is; 1: RMSNorm with weight w
 // (model_fused.py:37-40: x * rsqrt(mean(x^2) + eps) rounded to bf16, times w
 // rounded to bf16); 2: SwiGLU of the interleaved gate/up rows (gu [M, 2K]:
 // 8 gate then 8 up columns per block of 8 features), silu(gate) * up with the
 // reference's bf16 rounding after each op (model_fused.py:169).
+// The activations come from L2 (written by other CTAs in this launch): modes
+// 0 and 1 copy them with cp.async.cg (every chunk in flight at once), then
+// mode 1 normalises in shared memory; mode 2 loads gate/up chunks four at a
+// time per thread.  Ends with the consumers' barrier.
 template <int MODE>
 __device__ void stage(const Params& p, uint32_t xs, const __nv_bfloat16* src, int K,
                       const __nv_bfloat16* w) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < kTok; r += kCons) {
-    const uint32_t dst = xs + r * p.x_stride;
-    if (r >= p.M) {
-      for (int k8 = lane; k8 < K / 8; k8 += 32) sts128(dst + k8 * 16, make_uint4(0, 0, 0, 0));
-      continue;
-    }
-    if constexpr (MODE == 2) {
-      const __nv_bfloat16* row = src + (int64_t)r * 2 * K;
-      for (int k8 = lane; k8 < K / 8; k8 += 32) {
-        const uint4 gv = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16));
-        const uint4 uv = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16 + 8));
-        const uint32_t ga[4] = {gv.x, gv.y, gv.z, gv.w}, ua[4] = {uv.x, uv.y, uv.z, uv.w};
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int kT = kCons * 32;
+  const int cpr = K / 8;  // 16-byte chunks per row
+  if constexpr (MODE == 2) {
+    const int n = kTok * cpr;
+    for (int i0 = tid; i0 < n; i0 += 4 * kT) {
+      uint4 gv[4], uv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kT;
+        const int r = i / cpr, k8 = i % cpr;
+        if (i < n && r < p.M) {
+          const __nv_bfloat16* row = src + (int64_t)r * 2 * K;
+          gv[u] = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16));
+          uv[u] = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16 + 8));
+        } else {
+          gv[u] = uv[u] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kT;
+        if (i >= n) continue;
+        const int r = i / cpr, k8 = i % cpr;
+        const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
+        const uint32_t ua[4] = {uv[u].x, uv[u].y, uv[u].z, uv[u].w};
         uint32_t o[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 gg = unpack_bf16x2(ga[i]), uu = unpack_bf16x2(ua[i]);
-          o[i] = pack_bf16x2(silu_ref(gg.x) * uu.x, silu_ref(gg.y) * uu.y);
+        for (int e = 0; e < 4; ++e) {
+          const float2 gg = unpack_bf16x2(ga[e]), uu = unpack_bf16x2(ua[e]);
+          o[e] = r < p.M ? pack_bf16x2(silu_ref(gg.x) * uu.x, silu_ref(gg.y) * uu.y) : 0u;
         }
-        sts128(dst + k8 * 16, make_uint4(o[0], o[1], o[2], o[3]));
+        sts128(xs + r * p.x_stride + k8 * 16, make_uint4(o[0], o[1], o[2], o[3]));
       }
-    } else {
-      const __nv_bfloat16* row = src + (int64_t)r * K;
-      float rinv = 1.f;
-      if constexpr (MODE == 1) {
+    }
+    cons_bar();
+    return;
+  } else {
+    for (int i = tid; i < kTok * cpr; i += kT) {
+      const int r = i / cpr, k8 = i % cpr;
+      const bool ok = r < p.M;
+      cp_async16(xs + r * p.x_stride + k8 * 16, ok ? src + (int64_t)r * K + k8 * 8 : src,
+                 ok ? 16 : 0);  // rows past M: zero-filled
+    }
+    cp_async_wait_all();
+    cons_bar();
+    if constexpr (MODE == 1) {
+      for (int r = warp; r < p.M; r += kCons) {
+        const uint32_t row = xs + r * p.x_stride;
         float ss = 0.f;
-        for (int k8 = lane; k8 < K / 8; k8 += 32) {
-          const uint4 u = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 8));
+        for (int k8 = lane; k8 < cpr; k8 += 32) {
+          uint4 u;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                       : "r"(row + k8 * 16));
           const uint32_t ua[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_bf16x2(ua[i]);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(ua[e]);
             ss = fmaf(f.x, f.x, ss);
             ss = fmaf(f.y, f.y, ss);
           }
         }
         ss = warp_sum(ss);
-        rinv = 1.0f / sqrtf(ss / (float)K + p.eps);
-      }
-      for (int k8 = lane; k8 < K / 8; k8 += 32) {
-        uint4 u = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 8));
-        if constexpr (MODE == 1) {
+        const float rinv = 1.0f / sqrtf(ss / (float)K + p.eps);
+#pragma unroll 4
+        for (int k8 = lane; k8 < cpr; k8 += 32) {
+          uint4 u;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                       : "r"(row + k8 * 16));
           const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + k8 * 8));
           uint32_t xa[4] = {u.x, u.y, u.z, u.w};
           const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = unpack_bf16x2(xa[i]), g = unpack_bf16x2(wa[i]);
-            xa[i] = pack_bf16x2(rbf(f.x * rinv) * g.x, rbf(f.y * rinv) * g.y);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(xa[e]), g = unpack_bf16x2(wa[e]);
+            xa[e] = pack_bf16x2(rbf(f.x * rinv) * g.x, rbf(f.y * rinv) * g.y);
           }
-          u = make_uint4(xa[0], xa[1], xa[2], xa[3]);
+          sts128(row + k8 * 16, make_uint4(xa[0], xa[1], xa[2], xa[3]));
         }
-        sts128(dst + k8 * 16, u);
       }
+      cons_bar();
     }
   }
 }
@@ -508,7 +552,7 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
       } else {
         const uint2* src = p.inbox[p.rank] + word_at(p, par, r, row, tp);
         uint2 x = ld_word(src);
-        if (x.y != call) {
+        if (x.y != call && !aborted(p)) {
           const uint64_t t0 = globaltimer_ns();
           uint32_t spins = 0;
           while ((x = ld_word(src)).y != call) {
@@ -779,22 +823,38 @@ __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, 
   if (*flag) {
     __threadfence();
     const float* pp = p.apart + (size_t)pair * ap.splits * kMaxG * (kHD + 2);
+    // the splits' (max, sum) of every head first, all loads in flight at once
+    // (the scratch after q_s is free again: sm_o was consumed above)
+    float* ml = sm_o;                    // [splits][G][2]: weight, sum
+    float* inv = sm_o + 2 * kMaxSplitsMerge * kMaxG;  // [G] 1 / total
+    for (int i = threadIdx.x; i < ap.splits * G; i += kCons * 32) {
+      const int sp = i / G, gg = i % G;
+      const float* q = pp + ((size_t)sp * kMaxG + gg) * (kHD + 2);
+      ml[i * 2] = __ldcg(q + kHD);
+      ml[i * 2 + 1] = __ldcg(q + kHD + 1);
+    }
+    cons_bar();
+    if (threadIdx.x < G) {
+      const int gg = threadIdx.x;
+      float M = -INFINITY;
+      for (int sp = 0; sp < ap.splits; ++sp) M = fmaxf(M, ml[(sp * G + gg) * 2]);
+      float lsum = 0.f;
+      for (int sp = 0; sp < ap.splits; ++sp) {
+        const float ms = ml[(sp * G + gg) * 2];
+        const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+        ml[(sp * G + gg) * 2] = f;  // now the split's weight
+        lsum = fmaf(f, ml[(sp * G + gg) * 2 + 1], lsum);
+      }
+      inv[gg] = lsum > 0.f ? 1.f / lsum : 0.f;
+    }
+    cons_bar();
     for (int idx = threadIdx.x; idx < G * kHD; idx += kCons * 32) {
       const int gg = idx / kHD, d = idx % kHD;
-      float M = -INFINITY;
-      for (int s = 0; s < ap.splits; ++s)
-        M = fmaxf(M, __ldcg(pp + ((size_t)s * kMaxG + gg) * (kHD + 2) + kHD));
-      float a = 0.f, lsum = 0.f;
-      for (int s = 0; s < ap.splits; ++s) {
-        const float* q = pp + ((size_t)s * kMaxG + gg) * (kHD + 2);
-        const float ms = __ldcg(q + kHD);
-        if (ms == -INFINITY) continue;
-        const float f = exp2f(ms - M);
-        a = fmaf(f, __ldcg(q + d), a);
-        lsum = fmaf(f, __ldcg(q + kHD + 1), lsum);
-      }
-      p.attn[(int64_t)b * p.Hq * kHD + (kvh * G + gg) * kHD + d] =
-          f2bf(lsum > 0.f ? a / lsum : 0.f);
+      float a = 0.f;
+#pragma unroll 8
+      for (int sp = 0; sp < ap.splits; ++sp)
+        a = fmaf(ml[(sp * G + gg) * 2], __ldcg(pp + ((size_t)sp * kMaxG + gg) * (kHD + 2) + d), a);
+      p.attn[(int64_t)b * p.Hq * kHD + (kvh * G + gg) * kHD + d] = f2bf(a * inv[gg]);
     }
     if (threadIdx.x == 0) p.pair_cnt[pair] = 0;  // next used after a grid barrier
   }
@@ -843,8 +903,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
     // QKV: rmsnorm(x) @ Wqkv -> qkv
     gran_range(proj_n(p, kQKV) / kGran, c, C, lo, hi);
     if (hi > lo) {
-      if (!aborted(p)) stage<1>(p, xs, p.X, p.H, lp.in_norm);
-      cons_bar();
+      stage<1>(p, xs, p.X, p.H, lp.in_norm);
       project(p, kQKV, ring_u, xs, full, empty, it, hi - lo, acc);
       reduce_warps(xs, hi - lo, acc, v);
       store_rows(p, p.qkv, proj_n(p, kQKV), lo, hi - lo, v);
@@ -856,19 +915,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
     // o_proj + all-reduce + residual -> x2
     gran_range(proj_n(p, kO) / kGran, c, C, lo, hi);
     if (hi > lo) {
-      if (!aborted(p)) stage<0>(p, xs, p.attn, proj_k(p, kO), nullptr);
-      cons_bar();
+      stage<0>(p, xs, p.attn, proj_k(p, kO), nullptr);
       project(p, kO, ring_u, xs, full, empty, it, hi - lo, acc);
       reduce_warps(xs, hi - lo, acc, v);
-      if (!aborted(p))
-        allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 1u, p.X, p.X2);
+      allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 1u, p.X, p.X2);
     }
     grid_sync(p, target);
     // gate/up: rmsnorm(x2) @ Wgate_up -> gu
     gran_range(proj_n(p, kGU) / kGran, c, C, lo, hi);
     if (hi > lo) {
-      if (!aborted(p)) stage<1>(p, xs, p.X2, p.H, lp.post_norm);
-      cons_bar();
+      stage<1>(p, xs, p.X2, p.H, lp.post_norm);
       project(p, kGU, ring_u, xs, full, empty, it, hi - lo, acc);
       reduce_warps(xs, hi - lo, acc, v);
       store_rows(p, p.gu, proj_n(p, kGU), lo, hi - lo, v);
@@ -877,12 +933,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
     // down: silu(gate) * up @ Wdown + all-reduce + residual -> x
     gran_range(proj_n(p, kDN) / kGran, c, C, lo, hi);
     if (hi > lo) {
-      if (!aborted(p)) stage<2>(p, xs, p.gu, p.I, nullptr);
-      cons_bar();
+      stage<2>(p, xs, p.gu, p.I, nullptr);
       project(p, kDN, ring_u, xs, full, empty, it, hi - lo, acc);
       reduce_warps(xs, hi - lo, acc, v);
-      if (!aborted(p))
-        allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 2u, p.X2, p.X);
+      allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 2u, p.X2, p.X);
     }
     grid_sync(p, target);
   }
