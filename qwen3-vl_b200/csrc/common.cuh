@@ -65,6 +65,12 @@ int* device_error_word();
 // `rows` in a plane read as zeros.
 int make_tmap_3d_rows128(CUtensorMap* map, const void* base, int64_t rows, int64_t planes,
                          int64_t plane_stride_elems, int box_rows);
+// 3-D view (64 elements, rows, 64-wide column blocks) of a bf16 [rows, cols]
+// matrix, boxes of box_rows rows x 64 x `depth` column blocks, laid out in
+// shared memory as depth consecutive [box_rows][64] tiles with the 128-byte
+// swizzle: one copy brings `depth` K blocks of a few weight rows.
+int make_tmap_wblocks(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                      int depth);
 int make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
                  int box_cols);
 int cached_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,

@@ -68,8 +68,11 @@ constexpr int kMaxSplitsMerge = 256;          // attention splits of one pair, a
 constexpr int kSmemLimit = 232448;
 enum { kQKV = 0, kATT = 1, kO = 2, kGU = 3, kDN = 4, kPhases = 5 };
 
+constexpr int kDepths = 4;                    // weight boxes of 1, 2, 4 or 8 K blocks
 struct alignas(64) LayerMaps {
-  CUtensorMap w[4];  // qkv, o, gate_up, down: [N, K] K-major, boxes of 8 rows x 64
+  // qkv, o, gate_up, down ([N, K] K-major) as 3-D (64, N, K / 64) views with
+  // boxes of 8 rows x 64 x 2^d K blocks (d = 0..3)
+  CUtensorMap w[4][kDepths];
   CUtensorMap k, v;  // caches [B * Hkv * max_seq, 128], boxes of 64 rows x 64
 };
 struct LayerPtrs {
@@ -123,11 +126,18 @@ __host__ __device__ inline void gran_range(int ng, int c, int C, int& lo, int& h
   lo = (int)((int64_t)ng * c / C);
   hi = (int)((int64_t)ng * (c + 1) / C);
 }
-// 64-wide K blocks per ring slot for g granules (one slot holds 16 KB)
+// 64-wide K blocks per ring slot for g granules (one slot holds 16 KB): a
+// power of two, so each granule's share of a slot is loaded by one or two
+// copies of 2^d blocks
 __host__ __device__ inline int kb_per_stage(int g, int nkb) {
-  int k = g > 0 ? 16 / g : 1;
-  if (k < 1) k = 1;
-  return k < nkb ? k : nkb;
+  int k = 1;
+  while (2 * k * g <= 16 && 2 * k <= nkb) k *= 2;
+  return k;
+}
+// blocks per copy (the box depth) for kbs blocks per stage, and its map index
+__host__ __device__ inline int box_depth(int kbs) { return kbs < 8 ? kbs : 8; }
+__host__ __device__ inline int depth_index(int depth) {
+  return depth >= 8 ? 3 : depth >= 4 ? 2 : depth >= 2 ? 1 : 0;
 }
 struct AttPlan {
   int splits, chunk;
@@ -285,20 +295,21 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
       gran_range(ng, c, C, lo, hi);
       const int g = hi - lo;
       if (g == 0) continue;
-      const int kbs = kb_per_stage(g, nkb);
-      const CUtensorMap* m = &mp->w[widx(ph)];
+      const int kbs = kb_per_stage(g, nkb), dep = box_depth(kbs);
+      const CUtensorMap* m = &mp->w[widx(ph)][depth_index(dep)];
       for (int kb0 = 0; kb0 < nkb; kb0 += kbs) {
         const int n = min(kbs, nkb - kb0);
+        const int ncp = (n + dep - 1) / dep;  // copies per granule (the last may run past K: zeros)
         const int s = (int)(it % ns);
         if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x803)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(g * n * 1024));
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(g * ncp * dep * 1024));
         for (int gi = 0; gi < g; ++gi)
-          for (int j = 0; j < n; ++j)
-            tma_load_2d(ring + s * kSlot + (gi * kbs + j) * 1024, m, &full[s], (kb0 + j) * 64,
-                        (lo + gi) * kGran, kCacheEvictFirst);
+          for (int q = 0; q < ncp; ++q)
+            tma_load_3d(ring + s * kSlot + (gi * kbs + q * dep) * 1024, m, &full[s], 0,
+                        (lo + gi) * kGran, kb0 + q * dep, kCacheEvictFirst);
         ++it;
       }
     }
@@ -1060,10 +1071,12 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
       rc = fail(Q3_ERR_INVALID, "q3_decode_tp_create: layer %d has a null pointer", i);
       break;
     }
-    rc = make_tmap_2d(&maps[i].w[0], L.w_qkv, (int64_t)nqkv, hidden, kGran, 64);
-    if (!rc) rc = make_tmap_2d(&maps[i].w[1], L.w_o, hidden, (int64_t)q_heads * 128, kGran, 64);
-    if (!rc) rc = make_tmap_2d(&maps[i].w[2], L.w_gate_up, 2 * (int64_t)inter, hidden, kGran, 64);
-    if (!rc) rc = make_tmap_2d(&maps[i].w[3], L.w_down, hidden, inter, kGran, 64);
+    const void* wp[4] = {L.w_qkv, L.w_o, L.w_gate_up, L.w_down};
+    const int64_t wn[4] = {(int64_t)nqkv, hidden, 2 * (int64_t)inter, hidden};
+    const int64_t wk[4] = {hidden, (int64_t)q_heads * 128, hidden, inter};
+    for (int w = 0; w < 4 && !rc; ++w)
+      for (int d = 0; d < kDepths && !rc; ++d)
+        rc = make_tmap_wblocks(&maps[i].w[w][d], wp[w], wn[w], wk[w], kGran, 1 << d);
     if (!rc)
       rc = make_tmap_2d(&maps[i].k, L.k_cache, (int64_t)batch * kv_heads * max_seq, kHD, kPos, 64);
     if (!rc)

@@ -65,6 +65,26 @@ int make_tmap_3d_rows128(CUtensorMap* map, const void* base, int64_t rows, int64
   return Q3_OK;
 }
 
+int make_tmap_wblocks(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows,
+                      int depth) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (cols % 64 != 0 || box_rows < 1 || box_rows > 256 || depth < 1 || depth > 256)
+    return fail(Q3_ERR_INVALID, "weight-block tensor map: bad shape");
+  if (!aligned(base, 16))
+    return fail(Q3_ERR_INVALID, "weight-block tensor map: base must be 16-byte aligned");
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)depth};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(Q3_ERR_CUDA, "cuTensorMapEncodeTiled (weight blocks) failed (%d)", (int)r);
+  return Q3_OK;
+}
+
 namespace {
 struct TmapKey {
   const void* p;

@@ -16,8 +16,14 @@ def gran_range(ng, c, C):
 
 
 def kb_per_stage(g, nkb):
-    k = max(1, 16 // g) if g > 0 else 1
-    return min(k, nkb)
+    k = 1
+    while 2 * k * g <= 16 and 2 * k <= nkb:
+        k *= 2
+    return k
+
+
+def box_depth(kbs):
+    return min(kbs, 8)
 
 
 def att_plan(pairs, L, C):
@@ -57,12 +63,21 @@ def schedule(c, C, H, Hq, Hkv, I, M, L, max_seq):
             continue
         nkb = K // 64
         kbs = kb_per_stage(g, nkb)
+        dep = box_depth(kbs)
+        assert kbs % dep == 0 and g * kbs * 1024 <= SLOT
         for kb0 in range(0, nkb, kbs):
             n = min(kbs, nkb - kb0)
-            boxes = [((kb0 + j) * 64, (lo + gi) * GRAN, GRAN) for gi in range(g) for j in range(n)]
-            offs = [(gi * kbs + j) * 1024 for gi in range(g) for j in range(n)]
-            assert max(offs) + 1024 <= SLOT and len(set(offs)) == len(offs)
-            out.append((name, g * n * 1024, boxes, N, K))
+            ncp = -(-n // dep)
+            # one copy per (granule, group of dep K blocks): x = first K block
+            boxes = [(kb0 + q * dep, (lo + gi) * GRAN, GRAN, dep)
+                     for gi in range(g) for q in range(ncp)]
+            spans = [((gi * kbs + q * dep) * 1024, (gi * kbs + q * dep + dep) * 1024)
+                     for gi in range(g) for q in range(ncp)]
+            for a, b in spans:      # inside the granule's share of the slot, no overlap
+                gi = a // 1024 // kbs
+                assert b <= (gi + 1) * kbs * 1024 <= SLOT
+            assert len({a for a, _ in spans}) == len(spans)
+            out.append((name, g * ncp * dep * 1024, boxes, N, K))
     return out
 
 
@@ -107,11 +122,13 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
     for c in range(C):
         for name, nbytes, boxes, rows, cols in schedule(c, C, H, Hq, Hkv, I, M, L, max_seq):
             assert 0 < nbytes <= SLOT
-            for x, y, r in boxes:
-                assert x % 64 == 0 and x + 64 <= cols
+            for box in boxes:
                 if name != "att":
-                    assert y + r <= rows
+                    kb, y, r, dep = box
+                    assert kb < cols // 64 and y + r <= rows   # past the last block: zeros
                 else:
+                    x, y, r = box
+                    assert x % 64 == 0 and x + 64 <= cols
                     assert y < rows   # a tile may run past the head: TMA fills zeros
 
 
