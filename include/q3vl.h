@@ -570,7 +570,7 @@ Q3_API int q3_decode_step_destroy(void* plan);
  * rank of the group must run the same steps in the same order.  A plan holds
  * workspaces for one step at a time: order its steps on one stream.  After a
  * Q3_ERR_TIMEOUT in the device error word (0x501: a peer never delivered;
- * 0x801-0x805: a barrier or ring wait ran out), destroy and recreate the
+ * 0x801-0x807: a barrier, ring or attention-pair wait ran out), destroy and recreate the
  * plan and the communicator. */
 Q3_API int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, int batch, int hidden,
                                int q_heads, int kv_heads, int inter, int64_t max_seq, float eps,

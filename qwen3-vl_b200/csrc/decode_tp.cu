@@ -15,8 +15,8 @@
 //            new k, KV write, attention over the cache; the split holding the
 //            last arrival merges the splits               -> attn
 //   O        attn @ Wo, all-reduce, + x                   -> x2
-//   GU       rmsnorm(x2) @ Wgate_up                       -> gu  (raw, bf16)
-//   DN       silu(gate) * up @ Wdown, all-reduce, + x2    -> x
+//   GU       rmsnorm(x2) @ Wgate_up, silu(gate) * up      -> h
+//   DN       h @ Wdown, all-reduce, + x2                  -> x
 // separated by grid-wide barriers (an arrival counter in global memory).
 //
 // Work split.  A projection's weight rows are cut into granules of 8 rows,
@@ -37,14 +37,16 @@
 // with every weight tile and old cache tile this CTA will read, across phase
 // and layer boundaries: none of them depends on the step's activations, so
 // HBM keeps streaming while the consumers sit at a barrier.  The activations
-// of a phase (x, attn, x2 or gu: at most 8 tokens) are staged once per phase
-// into shared memory by the consumers, with the RMSNorm or SwiGLU applied as
-// they are staged.
+// of a phase (x, attn, x2 or h: at most 8 tokens) are staged once per phase
+// into shared memory by the consumers, with the RMSNorm applied as they are
+// staged; the SwiGLU is applied once, by the gate/up CTA that owns both halves
+// of a feature.
 //
 // Every wait is bounded: a grid barrier or ring wait gives up after 2 s, a
 // peer word after the communicator's wait limit; the kernel then records the
 // code in the device error word, raises an abort flag that every later wait
 // checks, and unwinds.
+#include <cstdlib>
 #include <vector>
 
 #include "comm.h"
@@ -60,6 +62,7 @@ constexpr int kMaxSlots = 8;
 constexpr int kTok = 8;                       // tokens per step, at most
 constexpr int kGran = 8;                      // weight rows per granule
 constexpr int kMaxGran = 16;                  // granules per CTA in one phase
+constexpr int kMaxPairs = kMaxGran / 2;       // granule pairs (16-row MMA tiles)
 constexpr int kHD = 128;
 constexpr int kPos = 64;                      // cache positions per attention tile
 constexpr int kMaxG = 8;                      // query heads per KV head
@@ -71,8 +74,10 @@ enum { kQKV = 0, kATT = 1, kO = 2, kGU = 3, kDN = 4, kPhases = 5 };
 constexpr int kDepths = 4;                    // weight boxes of 1, 2, 4 or 8 K blocks
 struct alignas(64) LayerMaps {
   // qkv, o, gate_up, down ([N, K] K-major) as 3-D (64, N, K / 64) views with
-  // boxes of 8 rows x 64 x 2^d K blocks (d = 0..3)
-  CUtensorMap w[4][kDepths];
+  // boxes of all of a CTA's rows (8 g, for the phase's two granule counts g,
+  // the Params' gbox) x 64 x 2^d K blocks (d = 0..3): one copy moves a CTA's
+  // whole share of up to 8 K blocks, laid out [K block][row][64]
+  CUtensorMap w[4][2][kDepths];
   CUtensorMap k, v;  // caches [B * Hkv * max_seq, 128], boxes of 64 rows x 64
 };
 struct LayerPtrs {
@@ -98,9 +103,9 @@ struct Params {
   __nv_bfloat16* X2;          // [M, H]
   __nv_bfloat16* qkv;         // [M, (Hq + 2 Hkv) * 128]
   __nv_bfloat16* attn;        // [M, Hq * 128]
-  __nv_bfloat16* gu;          // [M, 2 I]
+  __nv_bfloat16* gu;          // h = silu(gate) * up [M, I]
   float* apart;               // [grid][kMaxG][kHD + 2] attention split partials
-  int* pair_cnt;              // [M * Hkv] split arrivals (zero, self-resetting)
+  int* pair_cnt;              // [M * Hkv] split arrivals (zeroed before each launch)
   unsigned* gbar;             // grid barrier arrivals (zeroed before each launch)
   unsigned* step_no;          // launches so far (exchange call numbers)
   uint2* inbox[kMaxRanks];    // every rank's exchange buffer (own included)
@@ -111,6 +116,9 @@ struct Params {
   int x_stride;               // bytes per staged-activation row
   int x_bytes;                // staged-activation buffer
   int nslots;
+  int gbox[4][2];             // granule counts the weight maps' boxes were made for
+  int inflight;               // producer: slots issued but not landed, at most
+  int prod_sleep, cons_sleep; // ring-wait back-off (ns) of the producer and the consumers
 };
 
 // --------------------------------------------------------- work geometry
@@ -125,6 +133,20 @@ __host__ __device__ inline int widx(int ph) { return ph == kQKV ? 0 : ph == kO ?
 __host__ __device__ inline void gran_range(int ng, int c, int C, int& lo, int& hi) {
   lo = (int)((int64_t)ng * c / C);
   hi = (int)((int64_t)ng * (c + 1) / C);
+}
+// this CTA's granules of a projection phase; gate/up is dealt in pairs of
+// granules (8 gate rows then the 8 up rows of the same 8 features), so the CTA
+// that computes a feature's gate also computes its up and applies the SwiGLU
+__host__ __device__ inline void phase_range(const Params& p, int ph, int c, int C, int& lo,
+                                            int& hi) {
+  const int ng = proj_n(p, ph) / kGran;
+  if (ph == kGU) {
+    gran_range(ng / 2, c, C, lo, hi);
+    lo *= 2;
+    hi *= 2;
+  } else {
+    gran_range(ng, c, C, lo, hi);
+  }
 }
 // 64-wide K blocks per ring slot for g granules (one slot holds 16 KB): a
 // power of two, so each granule's share of a slot is loaded by one or two
@@ -170,13 +192,16 @@ __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* q) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(q) : "memory");
   return v;
 }
-// mbarrier wait of one thread that also gives up once the kernel aborted
-__device__ __forceinline__ bool ring_wait(const Params& p, uint64_t* bar, uint32_t parity,
-                                          int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+// mbarrier wait of one thread that also gives up once the kernel aborted;
+// between polls it sleeps sleep_ns, so that a waiting warp leaves its
+// scheduler's issue slots to the warps that work.  The polling loop is out of
+// line: every call site then costs a few instructions of the step's text.
+__device__ __noinline__ bool ring_wait_slow(const Params& p, uint64_t* bar, uint32_t parity,
+                                            int code, int sleep_ns) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (!mbar_try_wait(bar, parity)) {
+    if (sleep_ns) __nanosleep(sleep_ns);
     if ((++spins & 255u) == 0) {
       if (aborted(p)) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -187,10 +212,14 @@ __device__ __forceinline__ bool ring_wait(const Params& p, uint64_t* bar, uint32
   }
   return true;
 }
+__device__ __forceinline__ bool ring_wait(const Params& p, uint64_t* bar, uint32_t parity,
+                                          int code, int sleep_ns = 0) {
+  return mbar_try_wait(bar, parity) || ring_wait_slow(p, bar, parity, code, sleep_ns);
+}
 // the same, with the outcome shared by the whole warp
 __device__ __forceinline__ bool ring_wait_warp(const Params& p, uint64_t* bar, uint32_t parity,
                                                int code) {
-  return __all_sync(0xffffffffu, ring_wait(p, bar, parity, code));
+  return __all_sync(0xffffffffu, ring_wait(p, bar, parity, code, p.cons_sleep));
 }
 // Grid-wide barrier of the consumer threads of every CTA.
 __device__ __forceinline__ void grid_sync(const Params& p, unsigned& target) {
@@ -257,6 +286,16 @@ __device__ __forceinline__ size_t word_at(const Params& p, int par, int src, int
 }
 
 // -------------------------------------------------------------- producer
+// Keeps at most p.inflight slots issued but not landed.  The HBM stream needs
+// only a few tens of KB in flight per SM to run at full bandwidth; more only
+// lengthens the memory system's queues, and every latency-bound access of the
+// step (activation staging from L2, the grid barrier, the peer exchange)
+// waits behind them.  Landed slots may still fill the whole ring.
+__device__ __forceinline__ bool throttle(const Params& p, uint64_t* full, uint32_t it) {
+  if (it < (uint32_t)p.inflight) return true;
+  const uint32_t k = it - (uint32_t)p.inflight;
+  return ring_wait(p, &full[k % p.nslots], (k / p.nslots) & 1, 0x806, p.prod_sleep);
+}
 // Issues every TMA load of this CTA's schedule in consumption order.
 __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_t* empty, int L,
                          AttPlan ap) {
@@ -265,6 +304,7 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
   bool ok = true;
   for (int l = 0; ok && l < p.n_layers && !aborted(p); ++l) {
     const LayerMaps* mp = p.maps + l;
+#pragma unroll 1
     for (int ph = 0; ok && ph < kPhases; ++ph) {
       if (ph == kATT) {
         const int pairs = p.M * p.Hkv;
@@ -276,7 +316,8 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
             const int row = (int)(((int64_t)b * p.Hkv + kvh) * p.max_seq + t0);
             for (int kv = 0; ok && kv < 2; ++kv) {
               const int s = (int)(it % ns);
-              if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x802)) {
+              if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x802, p.prod_sleep) ||
+                  !throttle(p, full, it)) {
                 ok = false;
                 break;
               }
@@ -290,26 +331,27 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
         }
         continue;
       }
-      const int ng = proj_n(p, ph) / kGran, nkb = proj_k(p, ph) / 64;
+      const int nkb = proj_k(p, ph) / 64;
       int lo, hi;
-      gran_range(ng, c, C, lo, hi);
+      phase_range(p, ph, c, C, lo, hi);
       const int g = hi - lo;
       if (g == 0) continue;
       const int kbs = kb_per_stage(g, nkb), dep = box_depth(kbs);
-      const CUtensorMap* m = &mp->w[widx(ph)][depth_index(dep)];
+      const int wi = widx(ph);
+      const CUtensorMap* m = &mp->w[wi][g == p.gbox[wi][1] ? 1 : 0][depth_index(dep)];
       for (int kb0 = 0; kb0 < nkb; kb0 += kbs) {
         const int n = min(kbs, nkb - kb0);
         const int ncp = (n + dep - 1) / dep;  // copies per granule (the last may run past K: zeros)
         const int s = (int)(it % ns);
-        if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x803)) {
+        if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x803, p.prod_sleep) ||
+            !throttle(p, full, it)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&full[s], (uint32_t)(g * ncp * dep * 1024));
-        for (int gi = 0; gi < g; ++gi)
-          for (int q = 0; q < ncp; ++q)
-            tma_load_3d(ring + s * kSlot + (gi * kbs + q * dep) * 1024, m, &full[s], 0,
-                        (lo + gi) * kGran, kb0 + q * dep, kCacheEvictFirst);
+        for (int q = 0; q < ncp; ++q)
+          tma_load_3d(ring + s * kSlot + q * dep * g * 1024, m, &full[s], 0, lo * kGran,
+                      kb0 + q * dep, kCacheEvictFirst);
         ++it;
       }
     }
@@ -321,6 +363,26 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
 }
 
 // ------------------------------------------------------------- staging
+// pin(x...) makes values opaque at this point of each call, so that the
+// address arithmetic derived from them stays inside the phase: left free, the
+// compiler hoists every phase's addresses out of the layer loop and keeps them
+// live across the whole step, which spills registers.
+__device__ __forceinline__ void pin1(int& a) { asm volatile("" : "+r"(a)); }
+__device__ __forceinline__ void pin1(uint32_t& a) { asm volatile("" : "+r"(a)); }
+template <class T>
+__device__ __forceinline__ void pin1(T*& a) {
+  asm volatile("" : "+l"(a));
+}
+template <class... T>
+__device__ __forceinline__ void pin(T&... a) {
+  (pin1(a), ...);
+}
+// the thread index, opaque (see pin)
+__device__ __forceinline__ int tid_pinned() {
+  int t = threadIdx.x;
+  pin1(t);
+  return t;
+}
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
                "r"(src_bytes)
@@ -331,118 +393,142 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // Rows 0..M-1 of a [M, K] activation into the staging buffer (row stride
-// x_stride bytes), rows M..7 zero.  MODE 0: as is; 1: RMSNorm with weight w
+// x_stride bytes), rows M..7 zero; with a weight w, RMSNorm
 // (model_fused.py:37-40: x * rsqrt(mean(x^2) + eps) rounded to bf16, times w
-// rounded to bf16); 2: SwiGLU of the interleaved gate/up rows (gu [M, 2K]:
-// 8 gate then 8 up columns per block of 8 features), silu(gate) * up with the
-// reference's bf16 rounding after each op (model_fused.py:169).
-// The activations come from L2 (written by other CTAs in this launch): modes
-// 0 and 1 copy them with cp.async.cg (every chunk in flight at once), then
-// mode 1 normalises in shared memory; mode 2 loads gate/up chunks four at a
-// time per thread.  Ends with the consumers' barrier.
-template <int MODE>
+// rounded to bf16).
+// The activations come from L2 (written by other CTAs in this launch) and are
+// copied with cp.async.cg, every chunk in flight at once, and w as a ninth
+// row.  The RMSNorm then works column-wise: thread t owns the 16-byte
+// chunks t, t + 128, ... of all eight rows, sums its squares per row, and the
+// four warps combine the row sums through `nscr` ([4][8] floats, then [8]
+// reciprocal RMS values) before the scaling pass.  Ends with the consumers'
+// barrier.
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 __device__ void stage(const Params& p, uint32_t xs, const __nv_bfloat16* src, int K,
-                      const __nv_bfloat16* w) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+                      const __nv_bfloat16* w, float* nscr) {
+  const int tid = tid_pinned();
+  pin(xs, src, w);
+  const int warp = tid >> 5, lane = tid & 31;
   constexpr int kT = kCons * 32;
   const int cpr = K / 8;  // 16-byte chunks per row
-  if constexpr (MODE == 2) {
-    const int n = kTok * cpr;
-    for (int i0 = tid; i0 < n; i0 += 4 * kT) {
-      uint4 gv[4], uv[4];
+  const int xst = p.x_stride;
+  // rows 0..7, then the norm weight as row 8; rows past M are zero-filled
+  const int nrows = w != nullptr ? kTok + 1 : kTok;
+#pragma unroll 1
+  for (int r = 0; r < nrows; ++r) {
+    const bool ok = r < p.M || r == kTok;
+    const __nv_bfloat16* row = r == kTok ? w : src + (ok ? (int64_t)r * K : 0);
+    const uint32_t dst = xs + r * xst;
+#pragma unroll 1
+    for (int k8 = tid; k8 < cpr; k8 += kT)
+      cp_async16(dst + k8 * 16, row + (ok ? k8 * 8 : 0), ok ? 16 : 0);
+  }
+  cp_async_wait_all();
+  cons_bar();
+  if (w == nullptr) return;
+  float ss[kTok];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * kT;
-        const int r = i / cpr, k8 = i % cpr;
-        if (i < n && r < p.M) {
-          const __nv_bfloat16* row = src + (int64_t)r * 2 * K;
-          gv[u] = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16));
-          uv[u] = __ldcg(reinterpret_cast<const uint4*>(row + k8 * 16 + 8));
-        } else {
-          gv[u] = uv[u] = make_uint4(0, 0, 0, 0);
-        }
+  for (int r = 0; r < kTok; ++r) ss[r] = 0.f;
+#pragma unroll 1
+  for (int k8 = tid; k8 < cpr; k8 += kT) {
+    uint4 u[kTok];
+#pragma unroll
+    for (int r = 0; r < kTok; ++r) u[r] = lds128(xs + r * xst + k8 * 16);
+#pragma unroll
+    for (int r = 0; r < kTok; ++r) {
+      const uint32_t ua[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(ua[e]);
+        ss[r] = fmaf(f.x, f.x, ss[r]);
+        ss[r] = fmaf(f.y, f.y, ss[r]);
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = i0 + u * kT;
-        if (i >= n) continue;
-        const int r = i / cpr, k8 = i % cpr;
-        const uint32_t ga[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
-        const uint32_t ua[4] = {uv[u].x, uv[u].y, uv[u].z, uv[u].w};
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 gg = unpack_bf16x2(ga[e]), uu = unpack_bf16x2(ua[e]);
-          o[e] = r < p.M ? pack_bf16x2(silu_ref(gg.x) * uu.x, silu_ref(gg.y) * uu.y) : 0u;
-        }
-        sts128(xs + r * p.x_stride + k8 * 16, make_uint4(o[0], o[1], o[2], o[3]));
-      }
-    }
-    cons_bar();
-    return;
-  } else {
-    for (int i = tid; i < kTok * cpr; i += kT) {
-      const int r = i / cpr, k8 = i % cpr;
-      const bool ok = r < p.M;
-      cp_async16(xs + r * p.x_stride + k8 * 16, ok ? src + (int64_t)r * K + k8 * 8 : src,
-                 ok ? 16 : 0);  // rows past M: zero-filled
-    }
-    cp_async_wait_all();
-    cons_bar();
-    if constexpr (MODE == 1) {
-      for (int r = warp; r < p.M; r += kCons) {
-        const uint32_t row = xs + r * p.x_stride;
-        float ss = 0.f;
-        for (int k8 = lane; k8 < cpr; k8 += 32) {
-          uint4 u;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
-                       : "r"(row + k8 * 16));
-          const uint32_t ua[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack_bf16x2(ua[e]);
-            ss = fmaf(f.x, f.x, ss);
-            ss = fmaf(f.y, f.y, ss);
-          }
-        }
-        ss = warp_sum(ss);
-        const float rinv = 1.0f / sqrtf(ss / (float)K + p.eps);
-#pragma unroll 4
-        for (int k8 = lane; k8 < cpr; k8 += 32) {
-          uint4 u;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
-                       : "r"(row + k8 * 16));
-          const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + k8 * 8));
-          uint32_t xa[4] = {u.x, u.y, u.z, u.w};
-          const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack_bf16x2(xa[e]), g = unpack_bf16x2(wa[e]);
-            xa[e] = pack_bf16x2(rbf(f.x * rinv) * g.x, rbf(f.y * rinv) * g.y);
-          }
-          sts128(row + k8 * 16, make_uint4(xa[0], xa[1], xa[2], xa[3]));
-        }
-      }
-      cons_bar();
     }
   }
+#pragma unroll
+  for (int r = 0; r < kTok; ++r) ss[r] = warp_sum(ss[r]);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < kTok; ++r) nscr[warp * kTok + r] = ss[r];
+  }
+  cons_bar();
+  if (tid < kTok) {  // one thread per row
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < kCons; ++q) t += nscr[q * kTok + tid];
+    nscr[kCons * kTok + tid] = 1.0f / sqrtf(t / (float)K + p.eps);
+  }
+  cons_bar();
+  float rinv[kTok];
+#pragma unroll
+  for (int r = 0; r < kTok; ++r) rinv[r] = nscr[kCons * kTok + r];
+  // bf16(bf16(x * rinv) * w): the bf16 product of two bf16 values is the
+  // rounded exact product, the same as rounding an fp32 product
+#pragma unroll 1
+  for (int k8 = tid; k8 < cpr; k8 += kT) {
+    const uint4 wv = lds128(xs + kTok * xst + k8 * 16);
+    const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint4 u[kTok];
+#pragma unroll
+    for (int r = 0; r < kTok; ++r) u[r] = lds128(xs + r * xst + k8 * 16);
+#pragma unroll
+    for (int r = 0; r < kTok; ++r) {
+      uint32_t xa[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(xa[e]);
+        xa[e] = mul_bf16x2(pack_bf16x2(f.x * rinv[r], f.y * rinv[r]), wa[e]);
+      }
+      sts128(xs + r * xst + k8 * 16, make_uint4(xa[0], xa[1], xa[2], xa[3]));
+    }
+  }
+  cons_bar();
 }
 
 // ---------------------------------------------------- projection phase
-// acc[gi] accumulates this warp's k16 steps (step `warp` of every 64-wide K
-// block) of granule gi; rows of the m16 tile are tokens (0..7 used), columns
-// the granule's 8 weight rows.
+// One mma.sync m16n8k16 multiplies a granule pair (16 weight rows, A) by the
+// staged tokens (8 columns, B) over 16 K: warp w takes the k16 step w of
+// every 64-wide K block, so the four warps' partial sums are added at the end.
+// A comes from the ring by ldmatrix.x4 (a stage holds [K block][row][64]:
+// granule gi of K block j at (j g + gi) KB, and the TMA's 128-byte swizzle
+// puts chunk c of row r at chunk c ^ r), B from the staging buffer by
+// ldmatrix.x2.  An
+// odd last granule is paired with itself (its second half is discarded).
+// A stage's (K block j, pair gp) items are taken eight at a time, item
+// i = j * P + gp with P the pair count rounded up to a power of two, into
+// accumulator i % 8: every group issues its loads first and then up to eight
+// independent MMAs, however few pairs the CTA has; accumulator v holds pair
+// v % P, and the P-way split is folded at the end.
+// acc[gp] ends as: [0], [1] = (row g8 of granule 2 gp, tokens 2 t4, 2 t4 + 1);
+// [2], [3] = (row g8 of granule 2 gp + 1, the same tokens).
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
 __device__ bool project(const Params& p, int ph, uint32_t ring_u, uint32_t xs, uint64_t* full,
-                        uint64_t* empty, uint32_t& it, int g, float (&acc)[kMaxGran][4]) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g8 = lane >> 2, t4 = lane & 3;
+                        uint64_t* empty, uint32_t& it, int g, float (&acc)[kMaxPairs][4]) {
+  const int tid = tid_pinned();
+  pin(xs, ring_u);
+  const int warp = tid >> 5, lane = tid & 31;
   const int ns = p.nslots;
   const int nkb = proj_k(p, ph) / 64;
   const int kbs = kb_per_stage(g, nkb);
+  const int np = (g + 1) >> 1;
+  const int lg = np <= 1 ? 0 : np <= 2 ? 1 : np <= 4 ? 2 : 3;  // P = 1 << lg
+  const int msk = (1 << lg) - 1;
+  // ldmatrix.x4 of A: lanes 8 m .. 8 m + 7 address matrix m = (granule 2 gp +
+  // (m & 1), chunk 2 warp + (m >> 1)), row lane & 7
+  const int rr = lane & 7, gsel = (lane >> 3) & 1;
+  const uint32_t a_off = rr * 128 + ((((2 * warp) + (lane >> 4)) ^ rr) << 4);
+  // ldmatrix.x2 of B: lanes 0-7 address token rows at K 16 warp, lanes 8-15 at + 8
+  const uint32_t b_base = xs + rr * p.x_stride + (warp * 16 + ((lane >> 3) & 1) * 8) * 2;
 #pragma unroll
-  for (int gi = 0; gi < kMaxGran; ++gi) acc[gi][0] = acc[gi][1] = acc[gi][2] = acc[gi][3] = 0.f;
+  for (int i = 0; i < kMaxPairs; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   bool ok = true;
   for (int kb0 = 0; kb0 < nkb; kb0 += kbs) {
     const int n = min(kbs, nkb - kb0);
@@ -450,17 +536,24 @@ __device__ bool project(const Params& p, int ph, uint32_t ring_u, uint32_t xs, u
     if (ok && !ring_wait_warp(p, &full[s], (it / ns) & 1, 0x804)) ok = false;
     if (ok) {
       const uint32_t slot = ring_u + s * kSlot;
-      for (int j = 0; j < n; ++j) {
-        const uint32_t xa = xs + g8 * p.x_stride + ((kb0 + j) * 64 + warp * 16 + 2 * t4) * 2;
-        const uint32_t a0 = lds32(xa), a2 = lds32(xa + 16);
-        const uint32_t c0 = (((2 * warp) ^ g8) << 4) + 4 * t4;
-        const uint32_t c1 = (((2 * warp + 1) ^ g8) << 4) + 4 * t4;
+      const int items = n << lg;
+#pragma unroll 1
+      for (int i0 = 0; i0 < items; i0 += kMaxPairs) {
+        uint32_t a[kMaxPairs][4], b[kMaxPairs][2];
 #pragma unroll
-        for (int gi = 0; gi < kMaxGran; ++gi) {
-          if (gi < g) {
-            const uint32_t wb = slot + (gi * kbs + j) * 1024 + g8 * 128;
-            mma_bf16_16816(acc[gi], a0, 0u, a2, 0u, lds32(wb + c0), lds32(wb + c1));
+        for (int v = 0; v < kMaxPairs; ++v) {
+          const int gp = v & msk, j = (i0 + v) >> lg;
+          if (gp < np && j < n) {
+            const int gi = min(2 * gp + gsel, g - 1);
+            ldsm_x2(b[v], b_base + (kb0 + j) * 128);
+            ldsm_x4(a[v], slot + (j * g + gi) * 1024 + a_off);
           }
+        }
+#pragma unroll
+        for (int v = 0; v < kMaxPairs; ++v) {
+          const int gp = v & msk, j = (i0 + v) >> lg;
+          if (gp < np && j < n)
+            mma_bf16_16816(acc[v], a[v][0], a[v][1], a[v][2], a[v][3], b[v][0], b[v][1]);
         }
       }
     }
@@ -468,35 +561,86 @@ __device__ bool project(const Params& p, int ph, uint32_t ring_u, uint32_t xs, u
     if (lane == 0) mbar_arrive(&empty[s]);  // released even after an abort
     ++it;
   }
+  // fold accumulator v into v % P
+#pragma unroll
+  for (int h = kMaxPairs / 2; h >= 1; h >>= 1) {
+    if ((1 << lg) <= h) {
+#pragma unroll
+      for (int v = 0; v < h; ++v)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[v][e] += acc[v + h][e];
+    }
+  }
   return ok;
+}
+
+// The four warps' partial sums into the reduction scratch at the start of the
+// staging buffer, red[warp][granule][row][token] (fp32); the caller then adds
+// the warps with red_sum.
+__device__ __forceinline__ float* red_scratch(uint32_t xs) {
+  return reinterpret_cast<float*>(__cvta_shared_to_generic(xs));
+}
+__device__ void spill_partials(uint32_t xs, int g, const float (&acc)[kMaxPairs][4]) {
+  const int tid = tid_pinned();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  float* red = red_scratch(xs);
+  cons_bar();  // every warp is done with the staged activations
+#pragma unroll
+  for (int gp = 0; gp < kMaxPairs; ++gp) {
+    if (2 * gp < g)
+      *reinterpret_cast<float2*>(red + ((warp * kMaxGran + 2 * gp) * kGran + g8) * kTok + 2 * t4) =
+          make_float2(acc[gp][0], acc[gp][1]);
+    if (2 * gp + 1 < g)
+      *reinterpret_cast<float2*>(red + ((warp * kMaxGran + 2 * gp + 1) * kGran + g8) * kTok +
+                                 2 * t4) = make_float2(acc[gp][2], acc[gp][3]);
+  }
+  cons_bar();
+}
+__device__ __forceinline__ float red_sum(const float* red, int gi, int r, int t) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCons; ++w) s += red[((w * kMaxGran + gi) * kGran + r) * kTok + t];
+  return s;
 }
 
 // Sum the four warps' partials; thread (warp w, lane) then holds, for
 // granules gi = w, w + 4, ..., the values of token g8 and rows 2 t4, 2 t4 + 1
 // of the granule in v[gi / 4][0..1].
-__device__ void reduce_warps(uint32_t xs, int g, const float (&acc)[kMaxGran][4],
+__device__ void reduce_warps(uint32_t xs, int g, const float (&acc)[kMaxPairs][4],
                              float (&v)[kMaxGran / kCons][2]) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* red = reinterpret_cast<float*>(__cvta_shared_to_generic(xs));
-  cons_bar();  // every warp is done with the staged activations
-#pragma unroll
-  for (int gi = 0; gi < kMaxGran; ++gi) {
-    if (gi < g) {
-      red[((warp * kMaxGran + gi) * 32 + lane) * 2 + 0] = acc[gi][0];
-      red[((warp * kMaxGran + gi) * 32 + lane) * 2 + 1] = acc[gi][1];
-    }
-  }
-  cons_bar();
+  const int tid = tid_pinned();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  spill_partials(xs, g, acc);
+  const float* red = red_scratch(xs);
 #pragma unroll
   for (int q = 0; q < kMaxGran / kCons; ++q) {
     const int gi = q * kCons + warp;
     v[q][0] = v[q][1] = 0.f;
     if (gi < g) {
-#pragma unroll
-      for (int w = 0; w < kCons; ++w) {
-        v[q][0] += red[((w * kMaxGran + gi) * 32 + lane) * 2 + 0];
-        v[q][1] += red[((w * kMaxGran + gi) * 32 + lane) * 2 + 1];
-      }
+      v[q][0] = red_sum(red, gi, 2 * t4, g8);
+      v[q][1] = red_sum(red, gi, 2 * t4 + 1, g8);
+    }
+  }
+}
+
+// Gate/up epilogue: gate and up are rounded to bf16 (the matmul's output),
+// then h = silu(gate) * up with the reference's rounding after each op
+// (model_fused.py:169), written to h [M, I] for the features of this CTA's
+// granule pairs [lo, lo + g) (g even).
+__device__ void store_swiglu(const Params& p, uint32_t xs, int lo, int g,
+                             const float (&acc)[kMaxPairs][4]) {
+  spill_partials(xs, g, acc);
+  const float* red = red_scratch(xs);
+  const int tid = tid_pinned();
+  const int nout = (g / 2) * kGran * kTok;
+  for (int idx = tid; idx < nout; idx += kCons * 32) {
+    const int k = idx / (kGran * kTok), t = (idx / kGran) % kTok, r = idx % kGran;
+    if (t < p.M) {
+      const float gate = rbf(red_sum(red, 2 * k, r, t));
+      const float up = rbf(red_sum(red, 2 * k + 1, r, t));
+      p.gu[(int64_t)t * p.I + (lo / 2 + k) * kGran + r] = f2bf(silu_ref(gate) * up);
     }
   }
 }
@@ -504,7 +648,8 @@ __device__ void reduce_warps(uint32_t xs, int g, const float (&acc)[kMaxGran][4]
 // Plain epilogue (QKV, gate/up): bf16 outputs [M, N] (the matmul's rounding).
 __device__ void store_rows(const Params& p, __nv_bfloat16* out, int N, int lo, int g,
                            const float (&v)[kMaxGran / kCons][2]) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = tid_pinned();
+  const int warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   if (g8 >= p.M) return;
 #pragma unroll
@@ -523,11 +668,12 @@ __device__ void store_rows(const Params& p, __nv_bfloat16* out, int N, int lo, i
 __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
                                const float (&v)[kMaxGran / kCons][2], uint32_t call,
                                const __nv_bfloat16* res, __nv_bfloat16* out) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = tid_pinned();
+  const int warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   // this rank's partials as bf16 [row][token] after the reduction scratch
-  __nv_bfloat16* part =
-      reinterpret_cast<__nv_bfloat16*>(__cvta_shared_to_generic(xs)) + 4 * kMaxGran * 32 * 2 * 2;
+  __nv_bfloat16* part = reinterpret_cast<__nv_bfloat16*>(red_scratch(xs) +
+                                                       kCons * kMaxGran * kGran * kTok);
 #pragma unroll
   for (int q = 0; q < kMaxGran / kCons; ++q) {
     const int gi = q * kCons + warp;
@@ -540,7 +686,7 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
   const int par = (int)(call & 1u);
   const int tps = (p.M + 1) / 2;
   const int nwords = g * kGran * tps;
-  for (int w = threadIdx.x; w < nwords; w += kCons * 32) {
+  for (int w = tid; w < nwords; w += kCons * 32) {
     const int rl = w / tps, tp = w % tps;
     const int row = lo * kGran + rl;
     const __nv_bfloat16 lo_v = part[rl * kTok + 2 * tp];
@@ -550,7 +696,7 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
     for (int r = 0; r < p.world; ++r)
       if (r != p.rank) st_word(p.inbox[r] + word_at(p, par, p.rank, row, tp), mine, call);
   }
-  for (int w = threadIdx.x; w < nwords; w += kCons * 32) {
+  for (int w = tid; w < nwords; w += kCons * 32) {
     const int rl = w / tps, tp = w % tps;
     const int row = lo * kGran + rl;
     float s0 = 0.f, s1 = 0.f;
@@ -597,8 +743,8 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
 // One head row of q or k (128 dims; lane owns dims 4 lane .. 4 lane + 3):
 // RMSNorm over the head (model_fused.py:113-119) then rotate-half RoPE
 // (:122-129), with the reference's bf16 rounding points.
-__device__ __forceinline__ void norm_rope_head(const __nv_bfloat16* x, const __nv_bfloat16* w,
-                                               const __nv_bfloat16* cs_cos,
+__device__ __noinline__ void norm_rope_head(const __nv_bfloat16* x, const __nv_bfloat16* w,
+                                            const __nv_bfloat16* cs_cos,
                                                const __nv_bfloat16* cs_sin, int64_t crow,
                                                float eps, int lane, float (&o)[4]) {
   const int d0 = lane * 4, j0 = d0 & 63;
@@ -631,11 +777,13 @@ __device__ __forceinline__ void norm_rope_head(const __nv_bfloat16* x, const __n
 
 // Attention of this CTA's (sequence, KV head, split) unit, if it has one.
 // Scratch in the staging buffer: q_s [G][128] bf16 | sm_o [4][G][128] f32 |
-// sm_ml [4][G][2] f32 | new_s [2][128] f32 | snew [G] f32 | flag.
+// sm_ml [4][G][2] f32 | new_s [2][128] f32 | snew [G] f32; the pair merge then
+// reuses sm_o as [splits][G][2] weights | [G] 1 / sum | [splits][slice] products.
 template <int G>
 __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, uint64_t* full,
                           uint64_t* empty, uint32_t& it, int L, AttPlan ap) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = tid_pinned();
+  const int warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int c = blockIdx.x, ns = p.nslots;
   const int pairs = p.M * p.Hkv;
@@ -653,10 +801,10 @@ __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, 
   float* sm_ml = sm_o + kCons * kMaxG * kHD;
   float* new_s = sm_ml + kCons * kMaxG * 2;
   float* snew = new_s + 2 * kHD;
-  int* flag = reinterpret_cast<int*>(snew + kMaxG);
   const int ld = (p.Hq + 2 * p.Hkv) * kHD;
   const __nv_bfloat16* qrow = p.qkv + (int64_t)b * ld;
 
+#pragma unroll 1
   for (int gg = warp; gg < G; gg += kCons) {
     float o4[4];
     norm_rope_head(qrow + (kvh * G + gg) * kHD, lp.q_norm, p.cos, p.sin, crow, p.eps, lane, o4);
@@ -793,7 +941,8 @@ __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, 
   cons_bar();
   // merge the warps (and the new row): one split's partial, or the output
   float* apart = p.apart + (size_t)c * kMaxG * (kHD + 2);
-  for (int idx = threadIdx.x; idx < G * kHD; idx += kCons * 32) {
+#pragma unroll 1
+  for (int idx = tid; idx < G * kHD; idx += kCons * 32) {
     const int gg = idx / kHD, d = idx % kHD;
     float M = -INFINITY;
 #pragma unroll
@@ -823,58 +972,83 @@ __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, 
     }
   }
   if (ap.splits == 1) return ok;
-  // the split that arrives last merges the pair's splits
+  // Every split of the pair merges a slice of the pair's G x 128 outputs once
+  // all the pair's splits have published their partials: the arrivals count
+  // up by one per split and layer (the counter is zeroed before each launch).
   cons_bar();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     __threadfence();
-    const int prev = atomicAdd(&p.pair_cnt[pair], 1);
-    *flag = (prev == ap.splits - 1) ? 1 : 0;
+    atomicAdd(&p.pair_cnt[pair], 1);
+    const int target = ap.splits * (l + 1);
+    if (ld_acquire_gpu_u32(reinterpret_cast<const unsigned*>(&p.pair_cnt[pair])) < (unsigned)target &&
+        !aborted(p)) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_gpu_u32(reinterpret_cast<const unsigned*>(&p.pair_cnt[pair])) <
+             (unsigned)target) {
+        __nanosleep(20);
+        if ((++spins & 63u) == 0) {
+          if (aborted(p)) break;
+          if (globaltimer_ns() - t0 > p.wait_ns) {
+            raise_abort(p, 0x807);
+            break;
+          }
+        }
+      }
+    }
   }
   cons_bar();
-  if (*flag) {
-    __threadfence();
-    const float* pp = p.apart + (size_t)pair * ap.splits * kMaxG * (kHD + 2);
-    // the splits' (max, sum) of every head first, all loads in flight at once
-    // (the scratch after q_s is free again: sm_o was consumed above)
-    float* ml = sm_o;                    // [splits][G][2]: weight, sum
-    float* inv = sm_o + 2 * kMaxSplitsMerge * kMaxG;  // [G] 1 / total
-    for (int i = threadIdx.x; i < ap.splits * G; i += kCons * 32) {
-      const int sp = i / G, gg = i % G;
-      const float* q = pp + ((size_t)sp * kMaxG + gg) * (kHD + 2);
-      ml[i * 2] = __ldcg(q + kHD);
-      ml[i * 2 + 1] = __ldcg(q + kHD + 1);
+  const float* pp = p.apart + (size_t)pair * ap.splits * kMaxG * (kHD + 2);
+  // per split and head: (max, sum) -> (weight, sum); scratch after q_s
+  float* ml = sm_o;                                  // [splits][G][2]
+  float* inv = sm_o + 2 * kMaxSplitsMerge * kMaxG;  // [G]
+  float* prod = inv + kMaxG;                        // [splits][per]
+#pragma unroll 1
+  for (int i = tid; i < ap.splits * G; i += kCons * 32) {
+    const int sp = i / G, gg = i % G;
+    const float* q = pp + ((size_t)sp * kMaxG + gg) * (kHD + 2);
+    ml[i * 2] = __ldcg(q + kHD);
+    ml[i * 2 + 1] = __ldcg(q + kHD + 1);
+  }
+  cons_bar();
+#pragma unroll 1
+  for (int gg = warp; gg < G; gg += kCons) {  // one warp per head, lanes over splits
+    float M = -INFINITY;
+    for (int sp = lane; sp < ap.splits; sp += 32) M = fmaxf(M, ml[(sp * G + gg) * 2]);
+    M = warp_max(M);
+    float lsum = 0.f;
+    for (int sp = lane; sp < ap.splits; sp += 32) {
+      const float ms = ml[(sp * G + gg) * 2];
+      const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+      ml[(sp * G + gg) * 2] = f;  // now the split's weight
+      lsum = fmaf(f, ml[(sp * G + gg) * 2 + 1], lsum);
     }
-    cons_bar();
-    if (threadIdx.x < G) {
-      const int gg = threadIdx.x;
-      float M = -INFINITY;
-      for (int sp = 0; sp < ap.splits; ++sp) M = fmaxf(M, ml[(sp * G + gg) * 2]);
-      float lsum = 0.f;
-      for (int sp = 0; sp < ap.splits; ++sp) {
-        const float ms = ml[(sp * G + gg) * 2];
-        const float f = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-        ml[(sp * G + gg) * 2] = f;  // now the split's weight
-        lsum = fmaf(f, ml[(sp * G + gg) * 2 + 1], lsum);
-      }
-      inv[gg] = lsum > 0.f ? 1.f / lsum : 0.f;
-    }
-    cons_bar();
-    for (int idx = threadIdx.x; idx < G * kHD; idx += kCons * 32) {
-      const int gg = idx / kHD, d = idx % kHD;
-      float a = 0.f;
-#pragma unroll 8
-      for (int sp = 0; sp < ap.splits; ++sp)
-        a = fmaf(ml[(sp * G + gg) * 2], __ldcg(pp + ((size_t)sp * kMaxG + gg) * (kHD + 2) + d), a);
-      p.attn[(int64_t)b * p.Hq * kHD + (kvh * G + gg) * kHD + d] = f2bf(a * inv[gg]);
-    }
-    if (threadIdx.x == 0) p.pair_cnt[pair] = 0;  // next used after a grid barrier
+    lsum = warp_sum(lsum);
+    if (lane == 0) inv[gg] = lsum > 0.f ? 1.f / lsum : 0.f;
+  }
+  cons_bar();
+  // this split's slice of outputs: every (split, output) product loaded at once
+  const int per = (G * kHD + ap.splits - 1) / ap.splits;
+  const int o0 = split * per, n_out = max(0, min(per, G * kHD - o0));
+#pragma unroll 4
+  for (int i = tid; i < ap.splits * n_out; i += kCons * 32) {
+    const int sp = i / n_out, k = i % n_out;
+    const int gg = (o0 + k) / kHD, d = (o0 + k) % kHD;
+    prod[i] = ml[(sp * G + gg) * 2] * __ldcg(pp + ((size_t)sp * kMaxG + gg) * (kHD + 2) + d);
+  }
+  cons_bar();
+  for (int k = tid; k < n_out; k += kCons * 32) {
+    const int gg = (o0 + k) / kHD, d = (o0 + k) % kHD;
+    float a = 0.f;
+    for (int sp = 0; sp < ap.splits; ++sp) a += prod[sp * n_out + k];
+    p.attn[(int64_t)b * p.Hq * kHD + (kvh * G + gg) * kHD + d] = f2bf(a * inv[gg]);
   }
   return ok;
 }
 
 // ---------------------------------------------------------------- kernel
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
+__global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -883,6 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
   const uint32_t xs = ring_u + p.nslots * kSlot;
   uint64_t* full = reinterpret_cast<uint64_t*>(base + p.nslots * kSlot + p.x_bytes);
   uint64_t* empty = full + kMaxSlots;
+  float* nscr = reinterpret_cast<float*>(empty + kMaxSlots);  // RMSNorm: [4][8] sums, [8] 1/rms
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -906,50 +1081,45 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(Params p) {
   const int C = gridDim.x, c = blockIdx.x;
   uint32_t it = 0;
   unsigned target = 0;
-  float acc[kMaxGran][4];
+  float acc[kMaxPairs][4];
   float v[kMaxGran / kCons][2];
+  // The layer's five phases run through one copy of the code: the step kernel
+  // executes its whole text once per layer, and a text larger than the SM's
+  // instruction cache is refetched from the (busy) L2 every layer.
   for (int l = 0; l < p.n_layers; ++l) {
-    const LayerPtrs lp = p.lp[l];
-    int lo, hi;
-    // QKV: rmsnorm(x) @ Wqkv -> qkv
-    gran_range(proj_n(p, kQKV) / kGran, c, C, lo, hi);
-    if (hi > lo) {
-      stage<1>(p, xs, p.X, p.H, lp.in_norm);
-      project(p, kQKV, ring_u, xs, full, empty, it, hi - lo, acc);
-      reduce_warps(xs, hi - lo, acc, v);
-      store_rows(p, p.qkv, proj_n(p, kQKV), lo, hi - lo, v);
+#pragma unroll 1
+    for (int ph0 = 0; ph0 < kPhases; ++ph0) {
+      int ph = ph0;
+      pin(ph);
+      if (ph == kATT) {
+        attention<G>(p, l, ring_u, xs, full, empty, it, L, ap);  // -> attn
+      } else {
+        int lo, hi;
+        phase_range(p, ph, c, C, lo, hi);
+        if (hi > lo) {
+          // QKV: rmsnorm(x) @ Wqkv -> qkv; O: attn @ Wo + all-reduce + x -> x2;
+          // GU: rmsnorm(x2) @ Wgate_up, silu(gate) * up -> h;
+          // DN: h @ Wdown + all-reduce + x2 -> x
+          const __nv_bfloat16* src = ph == kQKV ? p.X : ph == kO ? p.attn : ph == kGU ? p.X2 : p.gu;
+          const __nv_bfloat16* nw = ph == kQKV ? p.lp[l].in_norm
+                                   : ph == kGU ? p.lp[l].post_norm
+                                               : nullptr;
+          stage(p, xs, src, proj_k(p, ph), nw, nscr);
+          project(p, ph, ring_u, xs, full, empty, it, hi - lo, acc);
+          if (ph == kGU) {
+            store_swiglu(p, xs, lo, hi - lo, acc);
+          } else {
+            reduce_warps(xs, hi - lo, acc, v);
+            if (ph == kQKV)
+              store_rows(p, p.qkv, proj_n(p, kQKV), lo, hi - lo, v);
+            else
+              allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + (ph == kO ? 1u : 2u),
+                             ph == kO ? p.X : p.X2, ph == kO ? p.X2 : p.X);
+          }
+        }
+      }
+      grid_sync(p, target);
     }
-    grid_sync(p, target);
-    // attention -> attn
-    attention<G>(p, l, ring_u, xs, full, empty, it, L, ap);
-    grid_sync(p, target);
-    // o_proj + all-reduce + residual -> x2
-    gran_range(proj_n(p, kO) / kGran, c, C, lo, hi);
-    if (hi > lo) {
-      stage<0>(p, xs, p.attn, proj_k(p, kO), nullptr);
-      project(p, kO, ring_u, xs, full, empty, it, hi - lo, acc);
-      reduce_warps(xs, hi - lo, acc, v);
-      allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 1u, p.X, p.X2);
-    }
-    grid_sync(p, target);
-    // gate/up: rmsnorm(x2) @ Wgate_up -> gu
-    gran_range(proj_n(p, kGU) / kGran, c, C, lo, hi);
-    if (hi > lo) {
-      stage<1>(p, xs, p.X2, p.H, lp.post_norm);
-      project(p, kGU, ring_u, xs, full, empty, it, hi - lo, acc);
-      reduce_warps(xs, hi - lo, acc, v);
-      store_rows(p, p.gu, proj_n(p, kGU), lo, hi - lo, v);
-    }
-    grid_sync(p, target);
-    // down: silu(gate) * up @ Wdown + all-reduce + residual -> x
-    gran_range(proj_n(p, kDN) / kGran, c, C, lo, hi);
-    if (hi > lo) {
-      stage<2>(p, xs, p.gu, p.I, nullptr);
-      project(p, kDN, ring_u, xs, full, empty, it, hi - lo, acc);
-      reduce_warps(xs, hi - lo, acc, v);
-      allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + 2u, p.X2, p.X);
-    }
-    grid_sync(p, target);
   }
   // every CTA has read step_no (at its start) and finished: advance it
   if (c == 0 && threadIdx.x == 0) *p.step_no += 1u;
@@ -998,21 +1168,24 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   int dev = 0;
   Q3_CUDA_CHECK(cudaGetDevice(&dev));
   const int C = num_sms();
-  // every phase's granules must fit kMaxGran per CTA
-  const int nmax = max(max((q_heads + 2 * kv_heads) * 128, 2 * inter), hidden);
-  Q3_REQUIRE((nmax / kGran + C - 1) / C <= kMaxGran,
-             "q3_decode_tp_create: %d output rows need more than %d granules per SM (a "
+  // every phase's granules must fit kMaxGran per CTA (gate/up: whole pairs)
+  const int nmax = max((q_heads + 2 * kv_heads) * 128, hidden);
+  Q3_REQUIRE((nmax / kGran + C - 1) / C <= kMaxGran &&
+                 2 * ((inter / kGran + C - 1) / C) <= kMaxGran,
+             "q3_decode_tp_create: %d / %d output rows need more than %d granules per SM (a "
              "larger tensor-parallel degree fits)",
-             nmax, kMaxGran);
+             nmax, 2 * inter, kMaxGran);
   const int kmax = max(max(hidden, q_heads * 128), inter);
   const int x_stride = kmax * 2 + 16;
   // staged activations, or the reduction scratch, or the attention scratch
-  const int red_bytes = kCons * kMaxGran * 32 * 2 * 4 + kMaxGran * kGran * kTok * 2;
-  const int att_bytes = kMaxG * kHD * 2 + (kCons * kMaxG * kHD + kCons * kMaxG * 2 + 2 * kHD +
-                                           kMaxG + 1) * 4;
-  int x_bytes = max(max(kTok * x_stride, red_bytes), att_bytes);
+  const int red_bytes = kCons * kMaxGran * kGran * kTok * 4 + kMaxGran * kGran * kTok * 2;
+  const int att_bytes = kMaxG * kHD * 2 +
+                        max(kCons * kMaxG * kHD + kCons * kMaxG * 2 + 2 * kHD + kMaxG + 1,
+                            2 * kMaxSplitsMerge * kMaxG + kMaxG + kMaxG * kHD + kMaxSplitsMerge) *
+                            4;
+  int x_bytes = max(max((kTok + 1) * x_stride, red_bytes), att_bytes);  // + the norm weight row
   x_bytes = (x_bytes + 1023) / 1024 * 1024;
-  const int fixed = x_bytes + 1024 /*align*/ + 2 * kMaxSlots * 8;
+  const int fixed = x_bytes + 1024 /*align*/ + 2 * kMaxSlots * 8 + (kCons + 1) * kTok * 4;
   const int nslots = min(kMaxSlots, (kSmemLimit - fixed) / kSlot);
   Q3_REQUIRE(nslots >= 3,
              "q3_decode_tp_create: reduction length %d leaves no room for the weight ring", kmax);
@@ -1037,6 +1210,12 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   p.x_stride = x_stride;
   p.x_bytes = x_bytes;
   p.nslots = nslots;
+  p.inflight = nslots;
+  if (const char* e = getenv("Q3VL_TP_INFLIGHT")) p.inflight = max(1, min(nslots, atoi(e)));
+  p.prod_sleep = 0;
+  p.cons_sleep = 0;
+  if (const char* e = getenv("Q3VL_TP_PSLEEP")) p.prod_sleep = max(0, min(1000, atoi(e)));
+  if (const char* e = getenv("Q3VL_TP_CSLEEP")) p.cons_sleep = max(0, min(1000, atoi(e)));
   p.err = device_error_word();
 
   // device memory: maps | layer pointers | x2 | qkv | attn | gu | apart | pair_cnt | gbar,
@@ -1061,6 +1240,19 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   }
   char* d = static_cast<char*>(pl->dmem);
   e = cudaMemset(d, 0, off);
+  // every CTA owns g = floor or ceil(granules / CTAs) granules of a phase
+  // (gate/up: twice the pairs), one weight-map box height each
+  int gbox[4][2];
+  {
+    const int ng[4] = {(int)(nqkv / kGran), hidden / kGran, inter / kGran, hidden / kGran};
+    for (int w = 0; w < 4; ++w) {
+      const int mul = w == 2 ? 2 : 1;
+      gbox[w][0] = mul * (ng[w] / C);
+      gbox[w][1] = mul * ((ng[w] + C - 1) / C);
+      pl->p.gbox[w][0] = gbox[w][0];
+      pl->p.gbox[w][1] = gbox[w][1];
+    }
+  }
   std::vector<LayerMaps> maps(n_layers);
   std::vector<LayerPtrs> ptrs(n_layers);
   int rc = Q3_OK;
@@ -1075,8 +1267,10 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
     const int64_t wn[4] = {(int64_t)nqkv, hidden, 2 * (int64_t)inter, hidden};
     const int64_t wk[4] = {hidden, (int64_t)q_heads * 128, hidden, inter};
     for (int w = 0; w < 4 && !rc; ++w)
-      for (int d = 0; d < kDepths && !rc; ++d)
-        rc = make_tmap_wblocks(&maps[i].w[w][d], wp[w], wn[w], wk[w], kGran, 1 << d);
+      for (int gc = 0; gc < 2 && !rc; ++gc)
+        for (int d = 0; d < kDepths && !rc && gbox[w][gc] > 0; ++d)
+          rc = make_tmap_wblocks(&maps[i].w[w][gc][d], wp[w], wn[w], wk[w], kGran * gbox[w][gc],
+                                 1 << d);
     if (!rc)
       rc = make_tmap_2d(&maps[i].k, L.k_cache, (int64_t)batch * kv_heads * max_seq, kHD, kPos, 64);
     if (!rc)
@@ -1126,7 +1320,11 @@ extern "C" int q3_decode_tp(void* plan, void* x, const int32_t* kv_len_dev, int6
   p.kv_len_dev = kv_len_dev;
   p.rope_delta = rope_delta;
   cudaStream_t s = (cudaStream_t)stream;
-  Q3_CUDA_CHECK(cudaMemsetAsync(p.gbar, 0, sizeof(unsigned), s));
+  // the grid barrier's and the attention pairs' arrival counters
+  Q3_CUDA_CHECK(cudaMemsetAsync(p.pair_cnt, 0,
+                                reinterpret_cast<char*>(p.gbar + 1) -
+                                    reinterpret_cast<char*>(p.pair_cnt),
+                                s));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl->grid);
   cfg.blockDim = dim3(kThreads);

@@ -15,6 +15,14 @@ def gran_range(ng, c, C):
     return ng * c // C, ng * (c + 1) // C
 
 
+def phase_range(name, N, c, C):
+    """Granules of CTA c; gate/up is dealt in whole (gate, up) granule pairs."""
+    if name == "gu":
+        lo, hi = gran_range(N // GRAN // 2, c, C)
+        return 2 * lo, 2 * hi
+    return gran_range(N // GRAN, c, C)
+
+
 def kb_per_stage(g, nkb):
     k = 1
     while 2 * k * g <= 16 and 2 * k <= nkb:
@@ -57,7 +65,7 @@ def schedule(c, C, H, Hq, Hkv, I, M, L, max_seq):
                         out.append((name, SLOT, [(0, row, POS), (64, row, POS)],
                                     M * Hkv * max_seq, 128))
             continue
-        lo, hi = gran_range(N // GRAN, c, C)
+        lo, hi = phase_range(name, N, c, C)
         g = hi - lo
         if g == 0:
             continue
@@ -68,15 +76,18 @@ def schedule(c, C, H, Hq, Hkv, I, M, L, max_seq):
         for kb0 in range(0, nkb, kbs):
             n = min(kbs, nkb - kb0)
             ncp = -(-n // dep)
-            # one copy per (granule, group of dep K blocks): x = first K block
-            boxes = [(kb0 + q * dep, (lo + gi) * GRAN, GRAN, dep)
-                     for gi in range(g) for q in range(ncp)]
-            spans = [((gi * kbs + q * dep) * 1024, (gi * kbs + q * dep + dep) * 1024)
-                     for gi in range(g) for q in range(ncp)]
-            for a, b in spans:      # inside the granule's share of the slot, no overlap
-                gi = a // 1024 // kbs
-                assert b <= (gi + 1) * kbs * 1024 <= SLOT
-            assert len({a for a, _ in spans}) == len(spans)
+            # one copy per group of dep K blocks, all g granules: x = first K block
+            boxes = [(kb0 + q * dep, lo * GRAN, g * GRAN, dep) for q in range(ncp)]
+            spans = [(q * dep * g * 1024, (q + 1) * dep * g * 1024) for q in range(ncp)]
+            for a, b in spans:      # inside the slot, no overlap, [K block][row] order
+                assert b <= SLOT
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(len(spans) - 1))
+            # the consumer's address of (K block j, granule gi) lies in copy j // dep
+            for j in range(n):
+                for gi in range(g):
+                    off = (j * g + gi) * 1024
+                    q = j // dep
+                    assert spans[q][0] <= off < spans[q][1]
             out.append((name, g * ncp * dep * 1024, boxes, N, K))
     return out
 
@@ -101,8 +112,10 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
         ng = N // GRAN
         owned = []
         for c in range(C):
-            lo, hi = gran_range(ng, c, C)
+            lo, hi = phase_range(name, N, c, C)
             assert hi - lo <= MAX_GRAN, (label, name, hi - lo)
+            if name == "gu":   # whole pairs: a feature's gate and up in one CTA
+                assert lo % 2 == 0 and hi % 2 == 0
             owned.extend(range(lo, hi))
         assert owned == list(range(ng)), (label, name)
         assert K % 64 == 0 and N % GRAN == 0
@@ -126,6 +139,7 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
                 if name != "att":
                     kb, y, r, dep = box
                     assert kb < cols // 64 and y + r <= rows   # past the last block: zeros
+                    assert r <= 256 and dep <= 256             # TMA box limits
                 else:
                     x, y, r = box
                     assert x % 64 == 0 and x + 64 <= cols
@@ -136,10 +150,20 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
 def test_shared_memory_and_exchange_sizes(label, H, Hq, Hkv, I, M, L, max_seq):
     kmax = max(H, Hq * HD, I)
     x_stride = kmax * 2 + 16
-    red = 4 * MAX_GRAN * 32 * 2 * 4 + MAX_GRAN * GRAN * TOK * 2
-    att = MAXG * HD * 2 + (4 * MAXG * HD + 4 * MAXG * 2 + 2 * HD + MAXG + 1) * 4
-    x_bytes = -(-max(TOK * x_stride, red, att) // 1024) * 1024
-    fixed = x_bytes + 1024 + 2 * MAX_SLOTS * 8
+    red = 4 * MAX_GRAN * GRAN * TOK * 4 + MAX_GRAN * GRAN * TOK * 2
+    # attention scratch, and the per-pair merge's weights and products after q
+    MAX_SPLITS = 256
+    att = MAXG * HD * 2 + max(4 * MAXG * HD + 4 * MAXG * 2 + 2 * HD + MAXG + 1,
+                              2 * MAX_SPLITS * MAXG + MAXG + MAXG * HD + MAX_SPLITS) * 4
+    sp, ch = att_plan(M * Hkv, L, SMS)
+    assert sp <= MAX_SPLITS
+    # a split's slice of the merge: splits x slice products fit the scratch
+    G = Hq // Hkv
+    per = -(-G * HD // sp)
+    assert sp * per <= MAXG * HD + MAX_SPLITS
+    # eight token rows plus the RMSNorm weight row
+    x_bytes = -(-max((TOK + 1) * x_stride, red, att) // 1024) * 1024
+    fixed = x_bytes + 1024 + 2 * MAX_SLOTS * 8 + 4 * TOK * 4
     nslots = min(MAX_SLOTS, (SMEM_LIMIT - fixed) // SLOT)
     assert nslots >= 3, label
     assert nslots * SLOT + fixed <= SMEM_LIMIT
@@ -170,7 +194,7 @@ def test_producer_and_consumers_walk_the_same_slots():
                     start, end = split * ch, min(split * ch + ch, L - 1)
                     cons += 2 * len(range(start, end, POS))
                 continue
-            lo, hi = gran_range(N // GRAN, c, C)
+            lo, hi = phase_range(name, N, c, C)
             if hi > lo:
                 nkb = K // 64
                 cons += -(-nkb // kb_per_stage(hi - lo, nkb))
