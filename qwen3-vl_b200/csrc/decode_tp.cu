@@ -105,6 +105,8 @@ struct Params {
   __nv_bfloat16* attn;        // [M, Hq * 128]
   __nv_bfloat16* gu;          // h = silu(gate) * up [M, I]
   float* apart;               // [grid][kMaxG][kHD + 2] attention split partials
+  float* ssx;                 // [grid][8] per-CTA sums of squares of x's rows (down epilogue)
+  float* ssx2;                // [grid][8] the same for x2 (o_proj epilogue)
   int* pair_cnt;              // [M * Hkv] split arrivals (zeroed before each launch)
   unsigned* gbar;             // grid barrier arrivals (zeroed before each launch)
   unsigned* step_no;          // launches so far (exchange call numbers)
@@ -297,6 +299,8 @@ __device__ __forceinline__ bool throttle(const Params& p, uint64_t* full, uint32
   return ring_wait(p, &full[k % p.nslots], (k / p.nslots) & 1, 0x806, p.prod_sleep);
 }
 // Issues every TMA load of this CTA's schedule in consumption order.
+// Issues every TMA load of this CTA's schedule in consumption order.
+// Issues every TMA load of this CTA's schedule in consumption order.
 __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_t* empty, int L,
                          AttPlan ap) {
   const int C = gridDim.x, c = blockIdx.x, ns = p.nslots;
@@ -396,64 +400,87 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // x_stride bytes), rows M..7 zero; with a weight w, RMSNorm
 // (model_fused.py:37-40: x * rsqrt(mean(x^2) + eps) rounded to bf16, times w
 // rounded to bf16).
-// The activations come from L2 (written by other CTAs in this launch) and are
-// copied with cp.async.cg, every chunk in flight at once, and w as a ninth
-// row.  The RMSNorm then works column-wise: thread t owns the 16-byte
-// chunks t, t + 128, ... of all eight rows, sums its squares per row, and the
-// four warps combine the row sums through `nscr` ([4][8] floats, then [8]
-// reciprocal RMS values) before the scaling pass.  Ends with the consumers'
-// barrier.
+// The activations come from L2 (written by other CTAs in this launch): one
+// thread issues a bulk copy per row (and one for w, as a ninth row) onto the
+// stage barrier `sbar`.  The RMSNorm needs the rows' sums of squares: with
+// `ssp` ([CTAs][8], the per-CTA partials that the producing all-reduce
+// epilogue wrote) they arrive with the rows; without it (the first layer's
+// input) thread t sums its 16-byte chunks t, t + 128, ... of every row.  The
+// four warps' sums meet in `nscr` ([4][8] floats, then the [8] reciprocal
+// RMS values) before the scaling pass.  Ends with the consumers' barrier.
 __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ void stage(const Params& p, uint32_t xs, const __nv_bfloat16* src, int K,
-                      const __nv_bfloat16* w, float* nscr) {
+                      const __nv_bfloat16* w, const float* ssp, float* nscr, uint64_t* sbar,
+                      uint32_t& sphase) {
   const int tid = tid_pinned();
   pin(xs, src, w);
   const int warp = tid >> 5, lane = tid & 31;
   constexpr int kT = kCons * 32;
   const int cpr = K / 8;  // 16-byte chunks per row
   const int xst = p.x_stride;
-  // rows 0..7, then the norm weight as row 8; rows past M are zero-filled
-  const int nrows = w != nullptr ? kTok + 1 : kTok;
-#pragma unroll 1
-  for (int r = 0; r < nrows; ++r) {
-    const bool ok = r < p.M || r == kTok;
-    const __nv_bfloat16* row = r == kTok ? w : src + (ok ? (int64_t)r * K : 0);
-    const uint32_t dst = xs + r * xst;
-#pragma unroll 1
-    for (int k8 = tid; k8 < cpr; k8 += kT)
-      cp_async16(dst + k8 * 16, row + (ok ? k8 * 8 : 0), ok ? 16 : 0);
+  const uint32_t ss_buf = xs + (kTok + 1) * xst;  // [CTAs][8] partial sums
+  if (tid == 0) {
+    const uint32_t rowb = (uint32_t)K * 2;
+    const int nr = min(p.M, kTok);
+    mbar_arrive_expect_tx(sbar, rowb * (nr + (w ? 1 : 0)) +
+                                    (ssp ? (uint32_t)gridDim.x * kTok * 4 : 0u));
+    for (int r = 0; r < nr; ++r) bulk_g2s(xs + r * xst, src + (int64_t)r * K, rowb, sbar);
+    if (w) bulk_g2s(xs + kTok * xst, w, rowb, sbar);
+    if (ssp) bulk_g2s(ss_buf, ssp, gridDim.x * kTok * 4, sbar);
   }
-  cp_async_wait_all();
+  for (int i = p.M * cpr + tid; i < kTok * cpr; i += kT)  // rows past M: zeros
+    sts128(xs + (i / cpr) * xst + (i % cpr) * 16, make_uint4(0, 0, 0, 0));
+  ring_wait(p, sbar, sphase, 0x808);  // after an abort the rows are not used
+  sphase ^= 1u;
   cons_bar();
   if (w == nullptr) return;
   float ss[kTok];
 #pragma unroll
   for (int r = 0; r < kTok; ++r) ss[r] = 0.f;
+  if (ssp) {
+    // thread (warp, lane): token lane & 7, CTAs (lane >> 3) + 4 warp + 16 i
+    const float* sb = reinterpret_cast<const float*>(__cvta_shared_to_generic(ss_buf));
+    float t = 0.f;
 #pragma unroll 1
-  for (int k8 = tid; k8 < cpr; k8 += kT) {
-    uint4 u[kTok];
+    for (int c = (lane >> 3) + 4 * warp; c < (int)gridDim.x; c += 16) t += sb[c * kTok + (lane & 7)];
+    t += __shfl_xor_sync(0xffffffffu, t, 8);
+    t += __shfl_xor_sync(0xffffffffu, t, 16);
+    if (lane < kTok) nscr[warp * kTok + lane] = t;
+  } else {
+#pragma unroll 1
+    for (int k8 = tid; k8 < cpr; k8 += kT) {
+      uint4 u[kTok];
 #pragma unroll
-    for (int r = 0; r < kTok; ++r) u[r] = lds128(xs + r * xst + k8 * 16);
+      for (int r = 0; r < kTok; ++r) u[r] = lds128(xs + r * xst + k8 * 16);
 #pragma unroll
-    for (int r = 0; r < kTok; ++r) {
-      const uint32_t ua[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+      for (int r = 0; r < kTok; ++r) {
+        const uint32_t ua[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = unpack_bf16x2(ua[e]);
-        ss[r] = fmaf(f.x, f.x, ss[r]);
-        ss[r] = fmaf(f.y, f.y, ss[r]);
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(ua[e]);
+          ss[r] = fmaf(f.x, f.x, ss[r]);
+          ss[r] = fmaf(f.y, f.y, ss[r]);
+        }
       }
     }
-  }
 #pragma unroll
-  for (int r = 0; r < kTok; ++r) ss[r] = warp_sum(ss[r]);
-  if (lane == 0) {
+    for (int r = 0; r < kTok; ++r) ss[r] = warp_sum(ss[r]);
+    if (lane == 0) {
 #pragma unroll
-    for (int r = 0; r < kTok; ++r) nscr[warp * kTok + r] = ss[r];
+      for (int r = 0; r < kTok; ++r) nscr[warp * kTok + r] = ss[r];
+    }
   }
   cons_bar();
   if (tid < kTok) {  // one thread per row
@@ -664,16 +691,22 @@ __device__ void store_rows(const Params& p, __nv_bfloat16* out, int N, int lo, i
 
 // All-reduce epilogue (o_proj, down): out = bf16(res + bf16(sum over ranks of
 // the bf16 partials)), for this CTA's rows; the rows are the same on every
-// rank, so the exchange is between the CTAs of one index on every GPU.
+// rank, so the exchange is between the CTAs of one index on every GPU.  Each
+// thread loads its residuals and all the peers' words of a row at once (one
+// round trip, then polls only what had not arrived), and the CTA leaves the
+// per-token sums of squares of its outputs in ssp_out[CTA][8] for the next
+// RMSNorm.
 __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
                                const float (&v)[kMaxGran / kCons][2], uint32_t call,
-                               const __nv_bfloat16* res, __nv_bfloat16* out) {
+                               const __nv_bfloat16* res, __nv_bfloat16* out, float* ssp_out) {
   const int tid = tid_pinned();
   const int warp = tid >> 5, lane = tid & 31;
   const int g8 = lane >> 2, t4 = lane & 3;
-  // this rank's partials as bf16 [row][token] after the reduction scratch
+  // this rank's partials as bf16 [row][token] after the reduction scratch,
+  // then the outputs' squares [row][token]
   __nv_bfloat16* part = reinterpret_cast<__nv_bfloat16*>(red_scratch(xs) +
                                                        kCons * kMaxGran * kGran * kTok);
+  float* sq = red_scratch(xs) + kCons * kMaxGran * kGran * kTok + kMaxGran * kGran * kTok / 2;
 #pragma unroll
   for (int q = 0; q < kMaxGran / kCons; ++q) {
     const int gi = q * kCons + warp;
@@ -682,6 +715,7 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
       part[(gi * kGran + 2 * t4 + 1) * kTok + g8] = f2bf(v[q][1]);
     }
   }
+  for (int i = tid; i < g * kGran * kTok; i += kCons * 32) sq[i] = 0.f;
   cons_bar();
   const int par = (int)(call & 1u);
   const int tps = (p.M + 1) / 2;
@@ -696,23 +730,30 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
     for (int r = 0; r < p.world; ++r)
       if (r != p.rank) st_word(p.inbox[r] + word_at(p, par, p.rank, row, tp), mine, call);
   }
+#pragma unroll 1
   for (int w = tid; w < nwords; w += kCons * 32) {
     const int rl = w / tps, tp = w % tps;
     const int row = lo * kGran + rl;
+    const bool two = 2 * tp + 1 < p.M;
+    const float r0 = bf2f(__ldcg(res + (int64_t)(2 * tp) * p.H + row));
+    const float r1 = two ? bf2f(__ldcg(res + (int64_t)(2 * tp + 1) * p.H + row)) : 0.f;
+    uint2 x[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < p.world && r != p.rank) x[r] = ld_word(p.inbox[p.rank] + word_at(p, par, r, row, tp));
     float s0 = 0.f, s1 = 0.f;
+#pragma unroll 1
     for (int r = 0; r < p.world; ++r) {
       uint32_t d;
       if (r == p.rank) {
         d = (uint32_t)__bfloat16_as_ushort(part[rl * kTok + 2 * tp]) |
-            ((2 * tp + 1 < p.M) ? (uint32_t)__bfloat16_as_ushort(part[rl * kTok + 2 * tp + 1]) << 16
-                                : 0u);
+            (two ? (uint32_t)__bfloat16_as_ushort(part[rl * kTok + 2 * tp + 1]) << 16 : 0u);
       } else {
-        const uint2* src = p.inbox[p.rank] + word_at(p, par, r, row, tp);
-        uint2 x = ld_word(src);
-        if (x.y != call && !aborted(p)) {
+        if (x[r].y != call && !aborted(p)) {
+          const uint2* src = p.inbox[p.rank] + word_at(p, par, r, row, tp);
           const uint64_t t0 = globaltimer_ns();
           uint32_t spins = 0;
-          while ((x = ld_word(src)).y != call) {
+          while ((x[r] = ld_word(src)).y != call) {
             if ((++spins & 255u) == 0) {
               if (aborted(p)) break;
               if (globaltimer_ns() - t0 > p.wait_ns) {
@@ -722,20 +763,29 @@ __device__ void allreduce_rows(const Params& p, uint32_t xs, int lo, int g,
             }
           }
         }
-        d = x.x;
+        d = x[r].x;
       }
       const float2 f = unpack_bf16x2(d);
       s0 += f.x;
       s1 += f.y;
     }
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int tok = 2 * tp + e;
-      if (tok < p.M) {
-        const float r0 = bf2f(__ldcg(res + (int64_t)tok * p.H + row));
-        out[(int64_t)tok * p.H + row] = f2bf(r0 + rbf(e ? s1 : s0));
-      }
+    const __nv_bfloat16 o0 = f2bf(r0 + rbf(s0));
+    out[(int64_t)(2 * tp) * p.H + row] = o0;
+    sq[rl * kTok + 2 * tp] = bf2f(o0) * bf2f(o0);
+    if (two) {
+      const __nv_bfloat16 o1 = f2bf(r1 + rbf(s1));
+      out[(int64_t)(2 * tp + 1) * p.H + row] = o1;
+      sq[rl * kTok + 2 * tp + 1] = bf2f(o1) * bf2f(o1);
     }
+  }
+  cons_bar();
+  // per-token sums over this CTA's rows, in row order: warp w sums tokens w, w + 4
+#pragma unroll 1
+  for (int t = warp; t < kTok; t += kCons) {
+    float a = 0.f;
+    for (int rl = lane; rl < g * kGran; rl += 32) a += sq[rl * kTok + t];
+    a = warp_sum(a);
+    if (lane == 0) ssp_out[blockIdx.x * kTok + t] = a;
   }
 }
 
@@ -1058,6 +1108,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
   uint64_t* full = reinterpret_cast<uint64_t*>(base + p.nslots * kSlot + p.x_bytes);
   uint64_t* empty = full + kMaxSlots;
   float* nscr = reinterpret_cast<float*>(empty + kMaxSlots);  // RMSNorm: [4][8] sums, [8] 1/rms
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(nscr + (kCons + 1) * kTok);  // staging copies
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -1065,6 +1116,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kCons);
     }
+    mbar_init(sbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -1081,6 +1133,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
   const int C = gridDim.x, c = blockIdx.x;
   uint32_t it = 0;
   unsigned target = 0;
+  uint32_t sphase = 0;
   float acc[kMaxPairs][4];
   float v[kMaxGran / kCons][2];
   // The layer's five phases run through one copy of the code: the step kernel
@@ -1104,7 +1157,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
           const __nv_bfloat16* nw = ph == kQKV ? p.lp[l].in_norm
                                    : ph == kGU ? p.lp[l].post_norm
                                                : nullptr;
-          stage(p, xs, src, proj_k(p, ph), nw, nscr);
+          const float* ssp = ph == kGU ? p.ssx2 : (ph == kQKV && l > 0) ? p.ssx : nullptr;
+          stage(p, xs, src, proj_k(p, ph), nw, ssp, nscr, sbar, sphase);
           project(p, ph, ring_u, xs, full, empty, it, hi - lo, acc);
           if (ph == kGU) {
             store_swiglu(p, xs, lo, hi - lo, acc);
@@ -1114,8 +1168,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
               store_rows(p, p.qkv, proj_n(p, kQKV), lo, hi - lo, v);
             else
               allreduce_rows(p, xs, lo, hi - lo, v, call0 + 2u * l + (ph == kO ? 1u : 2u),
-                             ph == kO ? p.X : p.X2, ph == kO ? p.X2 : p.X);
+                             ph == kO ? p.X : p.X2, ph == kO ? p.X2 : p.X,
+                             ph == kO ? p.ssx2 : p.ssx);
           }
+        } else if ((ph == kO || ph == kDN) && threadIdx.x < kTok) {
+          (ph == kO ? p.ssx2 : p.ssx)[c * kTok + threadIdx.x] = 0.f;  // no rows here
         }
       }
       grid_sync(p, target);
@@ -1178,14 +1235,16 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   const int kmax = max(max(hidden, q_heads * 128), inter);
   const int x_stride = kmax * 2 + 16;
   // staged activations, or the reduction scratch, or the attention scratch
-  const int red_bytes = kCons * kMaxGran * kGran * kTok * 4 + kMaxGran * kGran * kTok * 2;
+  const int red_bytes = kCons * kMaxGran * kGran * kTok * 4 + kMaxGran * kGran * kTok * 2 +
+                        kMaxGran * kGran * kTok * 4;
   const int att_bytes = kMaxG * kHD * 2 +
                         max(kCons * kMaxG * kHD + kCons * kMaxG * 2 + 2 * kHD + kMaxG + 1,
                             2 * kMaxSplitsMerge * kMaxG + kMaxG + kMaxG * kHD + kMaxSplitsMerge) *
                             4;
-  int x_bytes = max(max((kTok + 1) * x_stride, red_bytes), att_bytes);  // + the norm weight row
+  // eight rows, the norm weight row, the per-CTA sums of squares
+  int x_bytes = max(max((kTok + 1) * x_stride + C * kTok * 4, red_bytes), att_bytes);
   x_bytes = (x_bytes + 1023) / 1024 * 1024;
-  const int fixed = x_bytes + 1024 /*align*/ + 2 * kMaxSlots * 8 + (kCons + 1) * kTok * 4;
+  const int fixed = x_bytes + 1024 /*align*/ + 2 * kMaxSlots * 8 + (kCons + 1) * kTok * 4 + 8;
   const int nslots = min(kMaxSlots, (kSmemLimit - fixed) / kSlot);
   Q3_REQUIRE(nslots >= 3,
              "q3_decode_tp_create: reduction length %d leaves no room for the weight ring", kmax);
@@ -1230,6 +1289,7 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   const size_t o_attn = off; off = al(off + (size_t)batch * q_heads * 128 * 2);
   const size_t o_gu = off; off = al(off + (size_t)batch * 2 * inter * 2);
   const size_t o_ap = off; off = al(off + (size_t)C * kMaxG * (kHD + 2) * 4);
+  const size_t o_ss = off; off = al(off + (size_t)2 * C * kTok * 4);
   const size_t o_cnt = off; off = al(off + (size_t)batch * kv_heads * 4);
   const size_t o_ctr = off; off = al(off + 3 * 4);
   cudaError_t e = cudaMalloc(&pl->dmem, off);
@@ -1299,6 +1359,8 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   p.attn = reinterpret_cast<__nv_bfloat16*>(d + o_attn);
   p.gu = reinterpret_cast<__nv_bfloat16*>(d + o_gu);
   p.apart = reinterpret_cast<float*>(d + o_ap);
+  p.ssx = reinterpret_cast<float*>(d + o_ss);
+  p.ssx2 = p.ssx + C * kTok;
   p.pair_cnt = reinterpret_cast<int*>(d + o_cnt);
   p.gbar = reinterpret_cast<unsigned*>(d + o_ctr);
   p.step_no = p.gbar + 1;

@@ -150,7 +150,8 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
 def test_shared_memory_and_exchange_sizes(label, H, Hq, Hkv, I, M, L, max_seq):
     kmax = max(H, Hq * HD, I)
     x_stride = kmax * 2 + 16
-    red = 4 * MAX_GRAN * GRAN * TOK * 4 + MAX_GRAN * GRAN * TOK * 2
+    # warp partials, bf16 exchange partials, the outputs' squares
+    red = 4 * MAX_GRAN * GRAN * TOK * 4 + MAX_GRAN * GRAN * TOK * 2 + MAX_GRAN * GRAN * TOK * 4
     # attention scratch, and the per-pair merge's weights and products after q
     MAX_SPLITS = 256
     att = MAXG * HD * 2 + max(4 * MAXG * HD + 4 * MAXG * 2 + 2 * HD + MAXG + 1,
@@ -161,9 +162,13 @@ def test_shared_memory_and_exchange_sizes(label, H, Hq, Hkv, I, M, L, max_seq):
     G = Hq // Hkv
     per = -(-G * HD // sp)
     assert sp * per <= MAXG * HD + MAX_SPLITS
-    # eight token rows plus the RMSNorm weight row
-    x_bytes = -(-max((TOK + 1) * x_stride, red, att) // 1024) * 1024
-    fixed = x_bytes + 1024 + 2 * MAX_SLOTS * 8 + 4 * TOK * 4
+    # eight token rows, the RMSNorm weight row, the per-CTA sums of squares
+    x_bytes = -(-max((TOK + 1) * x_stride + SMS * TOK * 4, red, att) // 1024) * 1024
+    fixed = x_bytes + 1024 + 2 * MAX_SLOTS * 8 + 5 * TOK * 4 + 8
+    # bulk copies: 16-byte aligned rows and sizes
+    assert x_stride % 16 == 0 and ((TOK + 1) * x_stride) % 16 == 0
+    for K in (H, Hq * HD, I):
+        assert (K * 2) % 16 == 0
     nslots = min(MAX_SLOTS, (SMEM_LIMIT - fixed) // SLOT)
     assert nslots >= 3, label
     assert nslots * SLOT + fixed <= SMEM_LIMIT
