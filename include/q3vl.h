@@ -570,12 +570,27 @@ Q3_API int q3_decode_step_destroy(void* plan);
  * rank of the group must run the same steps in the same order.  A plan holds
  * workspaces for one step at a time: order its steps on one stream.  After a
  * Q3_ERR_TIMEOUT in the device error word (0x501: a peer never delivered;
- * 0x801-0x807: a barrier, ring or attention-pair wait ran out), destroy and recreate the
+ * 0x801-0x808: a barrier, ring, attention-pair or staging wait ran out;
+ * 0x80a: *kv_len_dev outside 1..max_seq, nothing ran), destroy and recreate the
  * plan and the communicator. */
 Q3_API int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, int batch, int hidden,
                                int q_heads, int kv_heads, int inter, int64_t max_seq, float eps,
                                const void* rope_cos, const void* rope_sin, int64_t rope_rows,
                                void* comm, void** plan_out);
+/* q3_decode_tp_create_paged: the same step over a paged KV cache (the
+ * bucketed cache of model_fused.py:224-232, :244-246 kept in pages): every
+ * layer's k_cache / v_cache is a page pool [num_pages, kv_heads, page_tokens,
+ * 128] with page_tokens a multiple of 64, and sequence b's position t lives in
+ * page block_table[b * table_stride + t / page_tokens] (device int32 [batch,
+ * table_stride], read at every launch, so its entries may change between
+ * steps; table_stride * page_tokens >= max_seq).  A table entry outside the
+ * pool records 0x809 and abandons the step. */
+Q3_API int q3_decode_tp_create_paged(const q3_step_layer* layers, int n_layers, int batch,
+                                     int hidden, int q_heads, int kv_heads, int inter,
+                                     int64_t max_seq, float eps, const void* rope_cos,
+                                     const void* rope_sin, int64_t rope_rows, void* comm,
+                                     const int32_t* block_table, int table_stride,
+                                     int page_tokens, int64_t num_pages, void** plan_out);
 Q3_API int q3_decode_tp(void* plan, void* x, const int32_t* kv_len_dev, int64_t rope_delta,
                         q3_stream_t stream);
 Q3_API int q3_decode_tp_destroy(void* plan);

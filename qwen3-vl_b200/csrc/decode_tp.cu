@@ -99,6 +99,12 @@ struct Params {
   const __nv_bfloat16* sin;
   int64_t rope_rows, rope_delta;
   const int32_t* kv_len_dev;  // new position + 1
+  // paged caches (table != nullptr): the caches are page pools [num_pages,
+  // Hkv, page_tokens, 128] and sequence b's position t lives in page
+  // table[b * table_stride + t / page_tokens]
+  const int32_t* table;
+  int table_stride, page_tokens;
+  int64_t num_pages;
   __nv_bfloat16* X;           // [M, H] residual stream (in: embedded tokens, out: last layer)
   __nv_bfloat16* X2;          // [M, H]
   __nv_bfloat16* qkv;         // [M, (Hq + 2 Hkv) * 128]
@@ -185,6 +191,14 @@ __device__ __forceinline__ bool aborted(const Params& p) {
 __device__ __forceinline__ void raise_abort(const Params& p, int code) {
   report_timeout(p.err, code);
   atomicExch(p.abort, 1);
+}
+// cache row ([rows, 128] view) of sequence b, KV head kvh, position t; -1 for
+// a table entry outside the pool
+__device__ __forceinline__ int64_t kv_row(const Params& p, int b, int kvh, int t) {
+  if (p.table == nullptr) return ((int64_t)b * p.Hkv + kvh) * p.max_seq + t;
+  const int pg = p.table[(int64_t)b * p.table_stride + t / p.page_tokens];
+  if (pg < 0 || pg >= p.num_pages) return -1;
+  return ((int64_t)pg * p.Hkv + kvh) * p.page_tokens + t % p.page_tokens;
 }
 __device__ __forceinline__ void cons_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
@@ -317,7 +331,12 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
           const int b = pair / p.Hkv, kvh = pair % p.Hkv;
           const int start = split * ap.chunk, end = min(start + ap.chunk, L - 1);
           for (int t0 = start; ok && t0 < end; t0 += kPos) {
-            const int row = (int)(((int64_t)b * p.Hkv + kvh) * p.max_seq + t0);
+            int64_t r64 = kv_row(p, b, kvh, t0);  // a tile never straddles two pages
+            if (r64 < 0) {
+              raise_abort(p, 0x809);
+              r64 = 0;
+            }
+            const int row = (int)r64;
             for (int kv = 0; ok && kv < 2; ++kv) {
               const int s = (int)(it % ns);
               if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x802, p.prod_sleep) ||
@@ -961,8 +980,12 @@ __device__ bool attention(const Params& p, int l, uint32_t ring_u, uint32_t xs, 
   if (with_new) {
     // the new token's k (normed, rotated) and v rows: into the caches and into
     // this split's merge
-    const int64_t off = (((int64_t)b * p.Hkv + kvh) * p.max_seq + (L - 1)) * kHD;
-    if (warp == 0) {
+    const int64_t row = kv_row(p, b, kvh, L - 1);
+    const int64_t off = (row < 0 ? 0 : row) * kHD;
+    if (row < 0 && tid == 0) raise_abort(p, 0x809);
+    if (row < 0) {
+      // no cache row to write: the step is abandoned (the abort stops every CTA)
+    } else if (warp == 0) {
       float o4[4];
       norm_rope_head(qrow + (p.Hq + kvh) * kHD, lp.k_norm, p.cos, p.sin, crow, p.eps, lane, o4);
       const uint2 pk = make_uint2(pack_bf16x2(o4[0], o4[1]), pack_bf16x2(o4[2], o4[3]));
@@ -1121,6 +1144,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tp_kernel(const __grid_con
   }
   __syncthreads();
   const int L = *p.kv_len_dev;
+  {  // the new position must have a cache row: otherwise no CTA runs the step
+    const int64_t cap = p.table ? (int64_t)p.table_stride * p.page_tokens : p.max_seq;
+    if (L < 1 || L > cap) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) raise_abort(p, 0x80a);
+      return;
+    }
+  }
   const AttPlan ap = att_plan(p.M * p.Hkv, L, gridDim.x);
 
   if (warp == kCons) {
@@ -1195,14 +1225,23 @@ struct Plan {
 }  // namespace tp
 }  // namespace q3
 
-extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, int batch,
-                                   int hidden, int q_heads, int kv_heads, int inter,
-                                   int64_t max_seq, float eps, const void* rope_cos,
-                                   const void* rope_sin, int64_t rope_rows, void* comm,
-                                   void** plan_out) {
+namespace {
+int decode_tp_create_impl(const q3_step_layer* layers, int n_layers, int batch, int hidden,
+                          int q_heads, int kv_heads, int inter, int64_t max_seq, float eps,
+                          const void* rope_cos, const void* rope_sin, int64_t rope_rows,
+                          void* comm, const int32_t* table, int table_stride, int page_tokens,
+                          int64_t num_pages, void** plan_out) {
   using namespace q3;
   using namespace q3::tp;
   Q3_REQUIRE(layers && rope_cos && rope_sin && comm && plan_out, "q3_decode_tp_create: null pointer");
+  if (table) {
+    Q3_REQUIRE(page_tokens > 0 && page_tokens % kPos == 0 && table_stride > 0 && num_pages > 0 &&
+                   num_pages * kv_heads * page_tokens < (1ll << 31) &&
+                   (int64_t)table_stride * page_tokens >= max_seq,
+               "q3_decode_tp_create_paged: pages of %d tokens (a multiple of %d), %d table "
+               "columns covering max_seq %lld, %lld pages",
+               page_tokens, kPos, table_stride, (long long)max_seq, (long long)num_pages);
+  }
   Q3_REQUIRE(n_layers > 0 && batch >= 1 && batch <= kTok,
              "q3_decode_tp_create: %d layers, batch %d (1..%d)", n_layers, batch, kTok);
   Q3_REQUIRE(q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
@@ -1213,7 +1252,7 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   Q3_REQUIRE(hidden > 0 && hidden % 64 == 0 && inter > 0 && inter % 64 == 0 &&
                  (q_heads * 128) % 64 == 0,
              "q3_decode_tp_create: hidden %d and inter %d must be multiples of 64", hidden, inter);
-  Q3_REQUIRE(max_seq > 0 && batch * kv_heads * max_seq < (1ll << 31) && rope_rows > 0,
+  Q3_REQUIRE(max_seq > 0 && (table || batch * kv_heads * max_seq < (1ll << 31)) && rope_rows > 0,
              "q3_decode_tp_create: bad max_seq / rope_rows");
   Comm* cm = static_cast<Comm*>(comm);
   Q3_REQUIRE(cm->open || cm->world == 1, "q3_decode_tp_create: communicator peers not opened");
@@ -1261,6 +1300,10 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   p.scale_log2 = (1.0f / sqrtf(128.0f)) * 1.4426950408889634f;
   p.cos = (const __nv_bfloat16*)rope_cos; p.sin = (const __nv_bfloat16*)rope_sin;
   p.rope_rows = rope_rows;
+  p.table = table;
+  p.table_stride = table_stride;
+  p.page_tokens = page_tokens;
+  p.num_pages = num_pages;
   p.rank = cm->rank; p.world = cm->world;
   p.wait_ns = cm->wait_ns;
   for (int r = 0; r < kMaxRanks; ++r)
@@ -1313,6 +1356,8 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
       pl->p.gbox[w][1] = gbox[w][1];
     }
   }
+  const int64_t kv_rows = table ? num_pages * kv_heads * page_tokens
+                                : (int64_t)batch * kv_heads * max_seq;
   std::vector<LayerMaps> maps(n_layers);
   std::vector<LayerPtrs> ptrs(n_layers);
   int rc = Q3_OK;
@@ -1332,9 +1377,9 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
           rc = make_tmap_wblocks(&maps[i].w[w][gc][d], wp[w], wn[w], wk[w], kGran * gbox[w][gc],
                                  1 << d);
     if (!rc)
-      rc = make_tmap_2d(&maps[i].k, L.k_cache, (int64_t)batch * kv_heads * max_seq, kHD, kPos, 64);
+      rc = make_tmap_2d(&maps[i].k, L.k_cache, kv_rows, kHD, kPos, 64);
     if (!rc)
-      rc = make_tmap_2d(&maps[i].v, L.v_cache, (int64_t)batch * kv_heads * max_seq, kHD, kPos, 64);
+      rc = make_tmap_2d(&maps[i].v, L.v_cache, kv_rows, kHD, kPos, 64);
     ptrs[i] = LayerPtrs{(const __nv_bfloat16*)L.input_norm, (const __nv_bfloat16*)L.post_norm,
                         (const __nv_bfloat16*)L.q_norm, (const __nv_bfloat16*)L.k_norm,
                         (__nv_bfloat16*)L.k_cache, (__nv_bfloat16*)L.v_cache};
@@ -1367,6 +1412,30 @@ extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, in
   p.abort = reinterpret_cast<int*>(p.gbar + 2);
   *plan_out = pl;
   return Q3_OK;
+}
+}  // namespace
+
+extern "C" int q3_decode_tp_create(const q3_step_layer* layers, int n_layers, int batch,
+                                   int hidden, int q_heads, int kv_heads, int inter,
+                                   int64_t max_seq, float eps, const void* rope_cos,
+                                   const void* rope_sin, int64_t rope_rows, void* comm,
+                                   void** plan_out) {
+  return decode_tp_create_impl(layers, n_layers, batch, hidden, q_heads, kv_heads, inter, max_seq,
+                               eps, rope_cos, rope_sin, rope_rows, comm, nullptr, 0, 0, 0,
+                               plan_out);
+}
+
+extern "C" int q3_decode_tp_create_paged(const q3_step_layer* layers, int n_layers, int batch,
+                                         int hidden, int q_heads, int kv_heads, int inter,
+                                         int64_t max_seq, float eps, const void* rope_cos,
+                                         const void* rope_sin, int64_t rope_rows, void* comm,
+                                         const int32_t* block_table, int table_stride,
+                                         int page_tokens, int64_t num_pages, void** plan_out) {
+  using namespace q3;
+  Q3_REQUIRE(block_table, "q3_decode_tp_create_paged: null block table");
+  return decode_tp_create_impl(layers, n_layers, batch, hidden, q_heads, kv_heads, inter, max_seq,
+                               eps, rope_cos, rope_sin, rope_rows, comm, block_table,
+                               table_stride, page_tokens, num_pages, plan_out);
 }
 
 extern "C" int q3_decode_tp(void* plan, void* x, const int32_t* kv_len_dev, int64_t rope_delta,

@@ -690,7 +690,8 @@ class Qwen3VLDecoderFused:
                 all(L.attn_block.qkv_bias is None for L in self.layers))
 
     def _step_plan(self, B, kv_cache):
-        key = (B, kv_cache[0][0].data_ptr())
+        paged = isinstance(kv_cache[0], PagedLayer)
+        key = (B, kv_cache[0][0].data_ptr(), kv_cache[0].table.data_ptr() if paged else 0)
         plan = self._step_plans.get(key)
         if plan is None:
             layers = []
@@ -729,10 +730,13 @@ class Qwen3VLDecoderFused:
     # ------------------------------------------- tensor-parallel step kernel
     def _tp_ok(self, B: int, kv_cache, rope_delta) -> bool:
         """The step kernel covers up to 8 sequences, head_dim 128, no QKV bias,
-        contiguous caches and one RoPE delta for the batch; at TP > 1 it needs
+        contiguous caches or pages of a multiple of 64 tokens, and one RoPE
+        delta for the batch; at TP > 1 it needs
         its communicator (enable_peer_allreduce with Q3VL_TP_KERNEL=1)."""
+        paged_ok = (not isinstance(kv_cache[0], PagedLayer) or
+                    kv_cache[0][0].shape[2] % 64 == 0)
         return (self.use_tp_kernel and self.num_layers > 0 and 1 <= B <= 8 and
-                self.head_dim == 128 and not isinstance(kv_cache[0], PagedLayer) and
+                self.head_dim == 128 and paged_ok and
                 not isinstance(rope_delta, RowRope) and
                 all(L.attn_block.qkv_bias is None for L in self.layers) and
                 (self.tp_size == 1 or self.mk_comm is not None))
@@ -740,7 +744,8 @@ class Qwen3VLDecoderFused:
     def _tp_plan(self, B, kv_cache):
         """The step kernel's plan for this batch and cache, or None when the
         library rejects the shapes (then the per-kernel step runs)."""
-        key = (B, kv_cache[0][0].data_ptr())
+        paged = isinstance(kv_cache[0], PagedLayer)
+        key = (B, kv_cache[0][0].data_ptr(), kv_cache[0].table.data_ptr() if paged else 0)
         if key in self._tp_plans:
             return self._tp_plans[key]
         if self.tp_size == 1 and self.mk_comm is None:
@@ -761,8 +766,11 @@ class Qwen3VLDecoderFused:
             plan = ops.DecodeTPPlan(
                 layers, batch=B, hidden=self.layers[0].attn_block.input_norm_weight.numel(),
                 q_heads=self.num_q_heads, kv_heads=self.num_kv_heads,
-                inter=mlp0.down_weight_km.shape[1], max_seq=kv_cache[0][0].shape[2],
-                eps=self._eps, cos=cos, sin=sin, comm=self.mk_comm)
+                inter=mlp0.down_weight_km.shape[1],
+                max_seq=(kv_cache[0].table.shape[1] * kv_cache[0][0].shape[2] if paged
+                         else kv_cache[0][0].shape[2]),
+                eps=self._eps, cos=cos, sin=sin, comm=self.mk_comm,
+                block_table=kv_cache[0].table if paged else None)
         except Q3Error:
             plan = None
         self._tp_plans[key] = plan

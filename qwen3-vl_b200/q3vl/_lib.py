@@ -110,6 +110,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_decode_step_destroy": (I32, [P]),
     "q3_decode_tp_create": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64, P,
                                   ctypes.POINTER(P)]),
+    "q3_decode_tp_create_paged": (I32, [P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, I64, P,
+                                        P, I32, I32, I64, ctypes.POINTER(P)]),
     "q3_decode_tp": (I32, [P, P, P, I64, P]),
     "q3_decode_tp_destroy": (I32, [P]),
     "q3_embed": (I32, [P, P, P, I64, I64, I64, P]),

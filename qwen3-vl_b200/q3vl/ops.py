@@ -737,7 +737,9 @@ class DecodeStepPlan:
 
 class DecodeTPPlan:
     """One decode step of every layer, with the tensor-parallel all-reduce
-    inside, as one persistent kernel per GPU (q3_decode_tp).
+    inside, as one persistent kernel per GPU (q3_decode_tp).  With
+    `block_table` the layers' k_cache / v_cache are page pools and the table
+    maps each sequence's positions to pages (q3_decode_tp_create_paged).
 
     `layers` as for DecodeStepPlan (this rank's shards); `comm` an object with
     a `.handle` to a q3_comm_create communicator of this rank's group, opened,
@@ -746,7 +748,7 @@ class DecodeTPPlan:
 
     def __init__(self, layers, *, batch: int, hidden: int, q_heads: int, kv_heads: int,
                  inter: int, max_seq: int, eps: float, cos: torch.Tensor, sin: torch.Tensor,
-                 comm):
+                 comm, block_table: torch.Tensor = None):
         from ._lib import StepLayer
         arr = (StepLayer * len(layers))()
         keep = []
@@ -761,9 +763,23 @@ class DecodeTPPlan:
         _cuda("decode_tp", cos, sin)
         _bf16("decode_tp", cos, sin)
         handle = ctypes.c_void_p()
-        call("q3_decode_tp_create", ctypes.cast(arr, ctypes.c_void_p), len(layers), batch,
-             hidden, q_heads, kv_heads, inter, int(max_seq), float(eps), _p(cos), _p(sin),
-             cos.shape[0], comm.handle, ctypes.byref(handle))
+        if block_table is None:
+            call("q3_decode_tp_create", ctypes.cast(arr, ctypes.c_void_p), len(layers), batch,
+                 hidden, q_heads, kv_heads, inter, int(max_seq), float(eps), _p(cos), _p(sin),
+                 cos.shape[0], comm.handle, ctypes.byref(handle))
+        else:
+            # paged caches: k_cache / v_cache are page pools [pages, kv_heads, page_tokens, 128]
+            if not (block_table.is_cuda and block_table.dtype == torch.int32 and
+                    block_table.dim() == 2 and block_table.is_contiguous() and
+                    block_table.shape[0] >= batch):
+                raise ValueError("DecodeTPPlan: block_table must be contiguous int32 "
+                                 "[>= batch, width] on the GPU")
+            pool = layers[0]["k_cache"]
+            call("q3_decode_tp_create_paged", ctypes.cast(arr, ctypes.c_void_p), len(layers),
+                 batch, hidden, q_heads, kv_heads, inter, int(max_seq), float(eps), _p(cos),
+                 _p(sin), cos.shape[0], comm.handle, _p(block_table), block_table.shape[1],
+                 pool.shape[2], pool.shape[0], ctypes.byref(handle))
+            keep.append(block_table)
         self.handle = handle
         self.batch, self.hidden = batch, hidden
         self._keep = keep + [cos, sin, comm]
