@@ -751,10 +751,11 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   int64_t slots = (int64_t)per_sm * num_sms();
   if (slots > 2 * (int64_t)num_sms()) slots = 2 * (int64_t)num_sms();
   const int64_t pairs = (int64_t)p.B * p.Hkv;
-  // few (sequence, KV head) pairs (a TP8 rank: one KV head per sequence): one
-  // CTA per SM streams as fast and leaves fewer partials to merge (B200, 8
-  // pairs at L = 1152: 7.6 us against 11.6 us at two per SM)
-  if (pairs <= 16) slots = num_sms();
+  // one CTA per SM: its ring keeps the SM's stream at full rate, and the
+  // splits come out more even and leave fewer partials to merge (B200, L =
+  // 1152: 8 pairs 7.6 us against 11.6 us at two CTAs per SM; 64 pairs 17.4
+  // against 19.5 us per call)
+  slots = num_sms();
   if (decode_slots_per_sm() > 0 && decode_slots_per_sm() <= per_sm)
     slots = (int64_t)decode_slots_per_sm() * num_sms();
   const int64_t L = p.kv_len < 1 ? 1 : p.kv_len;

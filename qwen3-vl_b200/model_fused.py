@@ -207,10 +207,14 @@ class RowRope:
 
 
 class _DecodeGraph:
-    """One captured decode step for a fixed batch, KV bucket and cache storage."""
+    """Captured decode steps for a fixed batch, KV bucket and cache storage:
+    `graph` one step (the next tokens land in `tok`), `multi` `steps` steps
+    in a row, each writing its tokens to hist[j] and advancing the device
+    position counters itself, so the host replays once per `steps` tokens."""
 
-    def __init__(self, graph, tok, pos, kv_len):
+    def __init__(self, graph, tok, pos, kv_len, multi=None, hist=None, steps=1):
         self.graph, self.tok, self.pos, self.kv_len = graph, tok, pos, kv_len
+        self.multi, self.hist, self.steps = multi, hist, steps
 
 
 class Qwen3VLDecoderFused:
@@ -251,6 +255,9 @@ class Qwen3VLDecoderFused:
         self.use_tp_kernel = (tpk == "1") if tpk in ("0", "1") else self.tp_size >= 4
         self.mk_comm = None
         self._tp_plans = {}
+        # decode graphs replay this many steps per launch from the host (the
+        # position counters advance inside the graph); 1 replays step by step
+        self.graph_steps = max(1, int(os.environ.get("Q3VL_DECODE_GRAPH_STEPS", "8")))
         # prefill: QK-norm, RoPE and the KV write in the QKV GEMM's epilogue
         self.fuse_qkv = os.environ.get("Q3VL_FUSE_QKV", "1") != "0"
         # decode: QK-norm, RoPE and the KV write inside the attention kernel
@@ -821,7 +828,18 @@ class Qwen3VLDecoderFused:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step()
-        g = _DecodeGraph(graph, tok, pos, kv_len)
+        multi, hist = None, None
+        steps = self.graph_steps
+        if steps > 1:
+            hist = torch.zeros(steps, B, dtype=torch.int64, device=dev)
+            multi = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(multi):
+                for j in range(steps):
+                    step()
+                    hist[j].copy_(tok)
+                    pos.add_(1)
+                    kv_len.add_(1)
+        g = _DecodeGraph(graph, tok, pos, kv_len, multi, hist, steps if multi is not None else 1)
         self._graphs[key] = g
         return g
 
@@ -942,18 +960,27 @@ class Qwen3VLDecoderFused:
             g.pos.fill_(P)
             g.kv_len.fill_(P + 1)
             done_at = max_new_tokens
-            for i in range(1, max_new_tokens):
-                g.graph.replay()
-                out[:, i].copy_(g.tok)
-                g.pos.add_(1)
-                g.kv_len.add_(1)
-                if i % eos_check_every == 0:
+            i = 1                                   # tokens 0 .. i-1 are in `out`
+            next_check = 1 + eos_check_every
+            while i < max_new_tokens:
+                if g.multi is not None and max_new_tokens - i >= g.steps:
+                    g.multi.replay()                # steps tokens, counters advanced inside
+                    out[:, i:i + g.steps].copy_(g.hist.t())
+                    i += g.steps
+                else:
+                    g.graph.replay()
+                    out[:, i].copy_(g.tok)
+                    g.pos.add_(1)
+                    g.kv_len.add_(1)
+                    i += 1
+                if i >= next_check:
+                    next_check = i + eos_check_every
                     if health is not None:
                         torch.cuda.current_stream(self.device).synchronize()
                         health.wait_for_peers(health.tick())
                     if eos_token_id is not None and \
-                            bool((out[:, :i + 1] == eos_token_id).any(dim=1).all()):
-                        done_at = i + 1
+                            bool((out[:, :i] == eos_token_id).any(dim=1).all()):
+                        done_at = i
                         break
             return out[:, :done_at]
         tok = out[:, 0]
