@@ -268,8 +268,8 @@ class Qwen3VLDecoderFused:
         # instead of the all_gather of every rank's logits
         self.dist_argmax = os.environ.get("Q3VL_DIST_ARGMAX", "1") != "0"
         # prefill attention on the tcgen05 tensor cores (measured on B200, config
-        # 2: 258 TFLOP/s against 147 for the mma.sync kernel); Q3VL_PREFILL_TC=0
-        # selects the mma.sync kernel
+        # 2: 578 TFLOP/s for the persistent variant against 147 for the mma.sync
+        # kernel); Q3VL_PREFILL_TC=0 selects the mma.sync kernel
         self.prefill_tc = os.environ.get("Q3VL_PREFILL_TC", "1") == "1"
         # decode: weights brought into L2 while the attention kernel, which
         # leaves HBM bandwidth idle, runs (opt-in until measured):
