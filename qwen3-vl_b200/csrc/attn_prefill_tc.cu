@@ -695,6 +695,12 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 // The kernel is persistent: min(items, SMs) CTAs, where an item is one
 // (query row block, head pair, sequence).  Items run longest first (the
@@ -948,30 +954,29 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
         if (!warp_wait(&s_full[t], Tj & 1, p.err, 0x638)) { ok = false; break; }
         tc_fence_after();
-        float sc[kPpN];
-        {
-          uint32_t rr[kPpN];
+        // raw scores S (fp32); the softmax works on S * scale_log2, and as the
+        // scale is positive the row max of the raw scores scales to the max of
+        // the scaled ones (rounding is monotonic), so the scaling is folded into
+        // one packed FMA with the subtraction of the base: p = 2^(s * scale - m)
+        uint32_t rr[kPpN];
 #pragma unroll
-          for (int c = 0; c < kPpN / 32; ++c) {
-            uint32_t(&r32)[32] = *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]);
-            tmem_ld_32cols(s_col + c * 32, r32);
-          }
-          tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < kPpN; ++i) sc[i] = __uint_as_float(rr[i]) * p.scale_log2;
+        for (int c = 0; c < kPpN / 32; ++c) {
+          uint32_t(&r32)[32] = *reinterpret_cast<uint32_t(*)[32]>(&rr[c * 32]);
+          tmem_ld_32cols(s_col + c * 32, r32);
         }
+        tc_wait_ld();
         const int kbase = j * kPpN;
         // masks only where a key can lie past a row's position or past the end
         if (kbase + kPpN - 1 > qpos_min || kbase + kPpN > kv_total) {
           const int lim = (int)min64(kv_total - 1, p.causal ? qpos : kv_total - 1) - kbase;
 #pragma unroll
           for (int c = 0; c < kPpN; ++c)
-            if (c > lim) sc[c] = -INFINITY;
+            if (c > lim) rr[c] = __float_as_uint(-INFINITY);
         }
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kPpN; ++c) mx = fmaxf(mx, sc[c]);
-        const float m_new = fmaxf(m_used, mx);
+        for (int c = 0; c < kPpN; c += 2) mx = max3f(mx, __uint_as_float(rr[c]), __uint_as_float(rr[c + 1]));
+        const float m_new = fmaxf(m_used, mx * p.scale_log2);
         const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
         const bool rescale = move && j > 0 && m_used != -INFINITY;
         const float corr = rescale ? ex2_approx(m_used - m_new) : 1.f;
@@ -980,19 +985,23 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           m_used = m_new;
         }
         const float base = (m_used == -INFINITY) ? 0.f : m_used;
-        float rs = 0.f;
+        const float nbase = -base;
+        float rs0 = 0.f, rs1 = 0.f;  // even and odd keys
 #pragma unroll
         for (int c = 0; c < kPpN / 32; ++c) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2_approx(sc[c * 32 + 2 * i] - base);
-            const float p1 = ex2_approx(sc[c * 32 + 2 * i + 1] - base);
-            rs += p0 + p1;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i]), p.scale_log2, nbase));
+            const float p1 =
+                ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i + 1]), p.scale_log2, nbase));
+            rs0 += p0;
+            rs1 += p1;
             w[i] = pack_bf16x2(p0, p1);
           }
           tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
         }
+        const float rs = rs0 + rs1;
         if (__any_sync(0xffffffffu, rescale)) {
           // O[t] holds tiles 0..j-1 of this item, complete (covered by the
           // commit of S_j(t)): rescale it to the new base before PV_j adds to it
