@@ -973,9 +973,14 @@ __global__ void __launch_bounds__(kPpThreads, 1)
           for (int c = 0; c < kPpN; ++c)
             if (c > lim) rr[c] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
+        // four independent max chains (a single chain would serialise 64 maxes)
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int c = 0; c < kPpN; c += 2) mx = max3f(mx, __uint_as_float(rr[c]), __uint_as_float(rr[c + 1]));
+        for (int c = 0; c < kPpN; c += 8)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            mq[q] = max3f(mq[q], __uint_as_float(rr[c + 2 * q]), __uint_as_float(rr[c + 2 * q + 1]));
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         const float m_new = fmaxf(m_used, mx * p.scale_log2);
         const bool move = m_new > m_used + kRescaleLog2;   // -inf + 8 = -inf
         const bool rescale = move && j > 0 && m_used != -INFINITY;
@@ -986,7 +991,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         }
         const float base = (m_used == -INFINITY) ? 0.f : m_used;
         const float nbase = -base;
-        float rs0 = 0.f, rs1 = 0.f;  // even and odd keys
+        float rsq[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
 #pragma unroll
         for (int c = 0; c < kPpN / 32; ++c) {
           uint32_t w[16];
@@ -995,13 +1000,12 @@ __global__ void __launch_bounds__(kPpThreads, 1)
             const float p0 = ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i]), p.scale_log2, nbase));
             const float p1 =
                 ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i + 1]), p.scale_log2, nbase));
-            rs0 += p0;
-            rs1 += p1;
+            rsq[i & 3] += p0 + p1;
             w[i] = pack_bf16x2(p0, p1);
           }
           tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
         }
-        const float rs = rs0 + rs1;
+        const float rs = (rsq[0] + rsq[1]) + (rsq[2] + rsq[3]);
         if (__any_sync(0xffffffffu, rescale)) {
           // O[t] holds tiles 0..j-1 of this item, complete (covered by the
           // commit of S_j(t)): rescale it to the new base before PV_j adds to it
