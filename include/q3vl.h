@@ -552,7 +552,10 @@ Q3_API int q3_decode_step_destroy(void* plan);
  * Replaces forward_layer (model_fused.py:234-277) at S = 1 for every layer,
  * with its two dist.all_reduce calls per layer (:267, :274), on one rank of a
  * tensor-parallel group (layers: this rank's shards, as q3_step_layer gives
- * them; q_heads, kv_heads and inter per rank).  One persistent kernel per GPU
+ * them, except w_gate_up: its rows come in granules of 8, the 4 gate rows of
+ * 4 consecutive features then their 4 up rows, so every granule holds whole
+ * features (ops.gate_up_granules4 builds it from q3_gemm's 8-row interleave);
+ * q_heads, kv_heads and inter per rank).  One persistent kernel per GPU
  * (one CTA per SM, cooperative launch) runs every phase of every layer,
  * separated by grid-wide barriers; weight tiles stream through a TMA ring
  * across phase boundaries; o_proj and down reduce over the ranks inside the

@@ -58,7 +58,7 @@ namespace tp {
 constexpr int kCons = 4;                      // consumer warps
 constexpr int kThreads = (kCons + 1) * 32;    // + the TMA producer warp
 constexpr int kSlot = 16384;                  // ring slot
-constexpr int kMaxSlots = 8;
+constexpr int kMaxSlots = 12;
 constexpr int kTok = 8;                       // tokens per step, at most
 constexpr int kGran = 8;                      // weight rows per granule
 constexpr int kMaxGran = 16;                  // granules per CTA in one phase
@@ -142,30 +142,23 @@ __host__ __device__ inline void gran_range(int ng, int c, int C, int& lo, int& h
   lo = (int)((int64_t)ng * c / C);
   hi = (int)((int64_t)ng * (c + 1) / C);
 }
-// this CTA's granules of a projection phase; gate/up is dealt in pairs of
-// granules (8 gate rows then the 8 up rows of the same 8 features), so the CTA
-// that computes a feature's gate also computes its up and applies the SwiGLU
+// this CTA's granules of a projection phase (the step kernel's gate/up rows
+// come in granules of 4 gate rows then the 4 up rows of the same 4 features,
+// so every granule holds whole features and the CTA that owns it applies the
+// SwiGLU)
 __host__ __device__ inline void phase_range(const Params& p, int ph, int c, int C, int& lo,
                                             int& hi) {
-  const int ng = proj_n(p, ph) / kGran;
-  if (ph == kGU) {
-    gran_range(ng / 2, c, C, lo, hi);
-    lo *= 2;
-    hi *= 2;
-  } else {
-    gran_range(ng, c, C, lo, hi);
-  }
+  gran_range(proj_n(p, ph) / kGran, c, C, lo, hi);
 }
-// 64-wide K blocks per ring slot for g granules (one slot holds 16 KB): a
-// power of two, so each granule's share of a slot is loaded by one or two
-// copies of 2^d blocks
+// 64-wide K blocks per ring slot for g granules: as many as fill the 16 KB
+// slot (a stage of n blocks is loaded by one copy per set bit of n, boxes of
+// 8, 4, 2 and 1 blocks): the bytes in flight per SM, not the copies, bound
+// the stream
 __host__ __device__ inline int kb_per_stage(int g, int nkb) {
-  int k = 1;
-  while (2 * k * g <= 16 && 2 * k <= nkb) k *= 2;
-  return k;
+  const int k = 16 / g;
+  return k < nkb ? k : nkb;
 }
-// blocks per copy (the box depth) for kbs blocks per stage, and its map index
-__host__ __device__ inline int box_depth(int kbs) { return kbs < 8 ? kbs : 8; }
+// map index of a box of 2^d blocks
 __host__ __device__ inline int depth_index(int depth) {
   return depth >= 8 ? 3 : depth >= 4 ? 2 : depth >= 2 ? 1 : 0;
 }
@@ -359,22 +352,29 @@ __device__ void producer(const Params& p, uint8_t* ring, uint64_t* full, uint64_
       phase_range(p, ph, c, C, lo, hi);
       const int g = hi - lo;
       if (g == 0) continue;
-      const int kbs = kb_per_stage(g, nkb), dep = box_depth(kbs);
+      const int kbs = kb_per_stage(g, nkb);
       const int wi = widx(ph);
-      const CUtensorMap* m = &mp->w[wi][g == p.gbox[wi][1] ? 1 : 0][depth_index(dep)];
+      const CUtensorMap* mg = &mp->w[wi][g == p.gbox[wi][1] ? 1 : 0][0];
       for (int kb0 = 0; kb0 < nkb; kb0 += kbs) {
         const int n = min(kbs, nkb - kb0);
-        const int ncp = (n + dep - 1) / dep;  // copies per granule (the last may run past K: zeros)
         const int s = (int)(it % ns);
         if (!ring_wait(p, &empty[s], ((it / ns) & 1) ^ 1, 0x803, p.prod_sleep) ||
             !throttle(p, full, it)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(g * ncp * dep * 1024));
-        for (int q = 0; q < ncp; ++q)
-          tma_load_3d(ring + s * kSlot + q * dep * g * 1024, m, &full[s], 0, lo * kGran,
-                      kb0 + q * dep, kCacheEvictFirst);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(g * n * 1024));
+        // copies of 8, 4, 2 and 1 K blocks, largest first (16 blocks: two of
+        // 8): blocks [q, q + 2^d) land at q * g KB, the consumers' [K block][row]
+        // order
+#pragma unroll 1
+        for (int q = 0; q < n;) {
+          const int r = n - q;
+          const int d = r >= 8 ? 3 : r >= 4 ? 2 : r >= 2 ? 1 : 0;
+          tma_load_3d(ring + s * kSlot + q * g * 1024, mg + d, &full[s], 0, lo * kGran, kb0 + q,
+                      kCacheEvictFirst);
+          q += 1 << d;
+        }
         ++it;
       }
     }
@@ -673,20 +673,21 @@ __device__ void reduce_warps(uint32_t xs, int g, const float (&acc)[kMaxPairs][4
 
 // Gate/up epilogue: gate and up are rounded to bf16 (the matmul's output),
 // then h = silu(gate) * up with the reference's rounding after each op
-// (model_fused.py:169), written to h [M, I] for the features of this CTA's
-// granule pairs [lo, lo + g) (g even).
+// (model_fused.py:169), written to h [M, I] for the 4 features of each of this
+// CTA's granules [lo, lo + g) (rows 0-3 gate, rows 4-7 up).
 __device__ void store_swiglu(const Params& p, uint32_t xs, int lo, int g,
                              const float (&acc)[kMaxPairs][4]) {
+  constexpr int kF = kGran / 2;  // features per granule
   spill_partials(xs, g, acc);
   const float* red = red_scratch(xs);
   const int tid = tid_pinned();
-  const int nout = (g / 2) * kGran * kTok;
+  const int nout = g * kF * kTok;
   for (int idx = tid; idx < nout; idx += kCons * 32) {
-    const int k = idx / (kGran * kTok), t = (idx / kGran) % kTok, r = idx % kGran;
+    const int gi = idx / (kF * kTok), t = (idx / kF) % kTok, r = idx % kF;
     if (t < p.M) {
-      const float gate = rbf(red_sum(red, 2 * k, r, t));
-      const float up = rbf(red_sum(red, 2 * k + 1, r, t));
-      p.gu[(int64_t)t * p.I + (lo / 2 + k) * kGran + r] = f2bf(silu_ref(gate) * up);
+      const float gate = rbf(red_sum(red, gi, r, t));
+      const float up = rbf(red_sum(red, gi, r + kF, t));
+      p.gu[(int64_t)t * p.I + (lo + gi) * kF + r] = f2bf(silu_ref(gate) * up);
     }
   }
 }
@@ -1264,13 +1265,12 @@ int decode_tp_create_impl(const q3_step_layer* layers, int n_layers, int batch, 
   int dev = 0;
   Q3_CUDA_CHECK(cudaGetDevice(&dev));
   const int C = num_sms();
-  // every phase's granules must fit kMaxGran per CTA (gate/up: whole pairs)
-  const int nmax = max((q_heads + 2 * kv_heads) * 128, hidden);
-  Q3_REQUIRE((nmax / kGran + C - 1) / C <= kMaxGran &&
-                 2 * ((inter / kGran + C - 1) / C) <= kMaxGran,
-             "q3_decode_tp_create: %d / %d output rows need more than %d granules per SM (a "
+  // every phase's granules must fit kMaxGran per CTA
+  const int nmax = max(max((q_heads + 2 * kv_heads) * 128, hidden), 2 * inter);
+  Q3_REQUIRE((nmax / kGran + C - 1) / C <= kMaxGran,
+             "q3_decode_tp_create: %d output rows need more than %d granules per SM (a "
              "larger tensor-parallel degree fits)",
-             nmax, 2 * inter, kMaxGran);
+             nmax, kMaxGran);
   const int kmax = max(max(hidden, q_heads * 128), inter);
   const int x_stride = kmax * 2 + 16;
   // staged activations, or the reduction scratch, or the attention scratch
@@ -1343,15 +1343,14 @@ int decode_tp_create_impl(const q3_step_layer* layers, int n_layers, int batch, 
   }
   char* d = static_cast<char*>(pl->dmem);
   e = cudaMemset(d, 0, off);
-  // every CTA owns g = floor or ceil(granules / CTAs) granules of a phase
-  // (gate/up: twice the pairs), one weight-map box height each
+  // every CTA owns g = floor or ceil(granules / CTAs) granules of a phase, one
+  // weight-map box height each
   int gbox[4][2];
   {
-    const int ng[4] = {(int)(nqkv / kGran), hidden / kGran, inter / kGran, hidden / kGran};
+    const int ng[4] = {(int)(nqkv / kGran), hidden / kGran, 2 * inter / kGran, hidden / kGran};
     for (int w = 0; w < 4; ++w) {
-      const int mul = w == 2 ? 2 : 1;
-      gbox[w][0] = mul * (ng[w] / C);
-      gbox[w][1] = mul * ((ng[w] + C - 1) / C);
+      gbox[w][0] = ng[w] / C;
+      gbox[w][1] = (ng[w] + C - 1) / C;
       pl->p.gbox[w][0] = gbox[w][0];
       pl->p.gbox[w][1] = gbox[w][1];
     }

@@ -735,6 +735,19 @@ class DecodeStepPlan:
             pass
 
 
+def gate_up_granules4(w_il: torch.Tensor) -> torch.Tensor:
+    """The step kernel's gate/up row order from the 8-row interleave of
+    q3_gemm (rows 16j..16j+7 gate of features 8j.., 16j+8.. up): granules of 8
+    rows holding 4 gate rows then the 4 up rows of the same 4 features, so
+    every granule a CTA owns carries whole features.  A new tensor."""
+    n2 = w_il.shape[0]
+    n = torch.arange(n2, device=w_il.device)
+    f = (n // 8) * 4 + (n % 4)                     # feature of new row n
+    up = (n % 8) >= 4
+    src = (f // 8) * 16 + (f % 8) + up.to(torch.long) * 8
+    return w_il.index_select(0, src).contiguous()
+
+
 class DecodeTPPlan:
     """One decode step of every layer, with the tensor-parallel all-reduce
     inside, as one persistent kernel per GPU (q3_decode_tp).  With
@@ -753,6 +766,8 @@ class DecodeTPPlan:
         arr = (StepLayer * len(layers))()
         keep = []
         for i, d in enumerate(layers):
+            d = dict(d)
+            d["w_gate_up"] = gate_up_granules4(d["w_gate_up"])   # the kernel's row order
             for name, _ in StepLayer._fields_:
                 t = d[name]
                 if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):

@@ -7,7 +7,7 @@ cache position once, and the scratch regions fit the staging buffer.  CPU only."
 import pytest
 
 SMS = 148
-SLOT, MAX_SLOTS, TOK, GRAN, MAX_GRAN, HD, POS, MAXG = 16384, 8, 8, 8, 16, 128, 64, 8
+SLOT, MAX_SLOTS, TOK, GRAN, MAX_GRAN, HD, POS, MAXG = 16384, 12, 8, 8, 16, 128, 64, 8
 SMEM_LIMIT = 232448
 
 
@@ -16,22 +16,24 @@ def gran_range(ng, c, C):
 
 
 def phase_range(name, N, c, C):
-    """Granules of CTA c; gate/up is dealt in whole (gate, up) granule pairs."""
-    if name == "gu":
-        lo, hi = gran_range(N // GRAN // 2, c, C)
-        return 2 * lo, 2 * hi
+    """Granules of CTA c (the step kernel's gate/up granules hold 4 gate rows
+    and the 4 up rows of the same features, so any granule split works)."""
     return gran_range(N // GRAN, c, C)
 
 
 def kb_per_stage(g, nkb):
-    k = 1
-    while 2 * k * g <= 16 and 2 * k <= nkb:
-        k *= 2
-    return k
+    return min(16 // g, nkb)
 
 
-def box_depth(kbs):
-    return min(kbs, 8)
+def copies(n):
+    """(first block, depth) of the copies of an n-block stage: 8, 4, 2, 1 blocks, largest first."""
+    out, q = [], 0
+    while q < n:
+        r = n - q
+        d = 8 if r >= 8 else 4 if r >= 4 else 2 if r >= 2 else 1
+        out.append((q, d))
+        q += d
+    return out
 
 
 def att_plan(pairs, L, C):
@@ -71,24 +73,25 @@ def schedule(c, C, H, Hq, Hkv, I, M, L, max_seq):
             continue
         nkb = K // 64
         kbs = kb_per_stage(g, nkb)
-        dep = box_depth(kbs)
-        assert kbs % dep == 0 and g * kbs * 1024 <= SLOT
+        assert g * kbs * 1024 <= SLOT
         for kb0 in range(0, nkb, kbs):
             n = min(kbs, nkb - kb0)
-            ncp = -(-n // dep)
-            # one copy per group of dep K blocks, all g granules: x = first K block
-            boxes = [(kb0 + q * dep, lo * GRAN, g * GRAN, dep) for q in range(ncp)]
-            spans = [(q * dep * g * 1024, (q + 1) * dep * g * 1024) for q in range(ncp)]
+            cps = copies(n)
+            # copies of 8/4/2/1 K blocks, all g granules: x = first K block of the copy
+            boxes = [(kb0 + q, lo * GRAN, g * GRAN, d) for q, d in cps]
+            spans = [(q * g * 1024, (q + d) * g * 1024) for q, d in cps]
+            assert sum(d for _, d in cps) == n and all(d in (1, 2, 4, 8) for _, d in cps)
             for a, b in spans:      # inside the slot, no overlap, [K block][row] order
                 assert b <= SLOT
+            assert spans[0][0] == 0
             assert all(spans[i][1] == spans[i + 1][0] for i in range(len(spans) - 1))
-            # the consumer's address of (K block j, granule gi) lies in copy j // dep
+            # the consumer's address of (K block j, granule gi) lies in the copy holding j
             for j in range(n):
                 for gi in range(g):
                     off = (j * g + gi) * 1024
-                    q = j // dep
-                    assert spans[q][0] <= off < spans[q][1]
-            out.append((name, g * ncp * dep * 1024, boxes, N, K))
+                    q, d = next((q, d) for q, d in cps if q <= j < q + d)
+                    assert spans[cps.index((q, d))][0] <= off < spans[cps.index((q, d))][1]
+            out.append((name, g * n * 1024, boxes, N, K))
     return out
 
 
@@ -114,8 +117,6 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
         for c in range(C):
             lo, hi = phase_range(name, N, c, C)
             assert hi - lo <= MAX_GRAN, (label, name, hi - lo)
-            if name == "gu":   # whole pairs: a feature's gate and up in one CTA
-                assert lo % 2 == 0 and hi % 2 == 0
             owned.extend(range(lo, hi))
         assert owned == list(range(ng)), (label, name)
         assert K % 64 == 0 and N % GRAN == 0
@@ -138,8 +139,8 @@ def test_plan_covers_rows_once_and_stays_in_bounds(label, H, Hq, Hkv, I, M, L, m
             for box in boxes:
                 if name != "att":
                     kb, y, r, dep = box
-                    assert kb < cols // 64 and y + r <= rows   # past the last block: zeros
-                    assert r <= 256 and dep <= 256             # TMA box limits
+                    assert kb + dep <= cols // 64 and y + r <= rows   # exact, no overrun
+                    assert r <= 256 and dep <= 256                   # TMA box limits
                 else:
                     x, y, r = box
                     assert x % 64 == 0 and x + 64 <= cols
@@ -204,3 +205,19 @@ def test_producer_and_consumers_walk_the_same_slots():
                 nkb = K // 64
                 cons += -(-nkb // kb_per_stage(hi - lo, nkb))
         assert prod == cons * 36
+
+
+def test_gate_up_granules_hold_whole_features():
+    """ops.gate_up_granules4: from q3_gemm's 8-row gate/up interleave to the step
+    kernel's granules of 4 gate rows then the same 4 features' up rows."""
+    import torch
+    from q3vl import layout
+    from q3vl.ops import gate_up_granules4
+    I, H = 96, 3
+    gate = torch.randn(I, H)
+    up = torch.randn(I, H)
+    w4 = gate_up_granules4(layout.interleave_gate_up(gate, up))
+    assert w4.shape == (2 * I, H)
+    for j in range(2 * I // GRAN):
+        assert torch.equal(w4[8 * j:8 * j + 4], gate[4 * j:4 * j + 4])
+        assert torch.equal(w4[8 * j + 4:8 * j + 8], up[4 * j:4 * j + 4])
