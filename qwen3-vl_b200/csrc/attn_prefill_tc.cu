@@ -862,22 +862,31 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(kFM, kPpN);
       constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(kFM, kFD);
+      // The MMA loops are unrolled with every descriptor a base plus a
+      // constant: a tcgen05.mma of 128 x 128 x 16 takes 64 cycles, and an
+      // issue loop that recomputes descriptors per step measured 75-140
+      // cycles per MMA on B200, which left the tensor pipe idle half the time.
+      // Descriptor start addresses are in 16-byte units (14 bits cover the
+      // 256 KB of shared memory), so adding byte offset / 16 to a descriptor
+      // is exact.
       auto issue_s = [&](int T, int t) {
-        const uint32_t kb = s_base + kPpOffK + (T & 1) * kPpKVBytes;
-        const uint32_t qa = s_base + t * kPpQBytes;
-#pragma unroll 1
+        const uint64_t dq = umma_desc_k_sw128(s_base + t * kPpQBytes);
+        const uint64_t dk = umma_desc_k_sw128(s_base + kPpOffK + (T & 1) * kPpKVBytes);
+        const uint32_t ds = tmem + t * kPpN;
+#pragma unroll
         for (int ks = 0; ks < kFD / 16; ++ks)
-          tc_mma_bf16(tmem + t * kPpN, umma_desc_k_sw128(qa + (ks >> 2) * (kPpQBytes / 2)) + 2 * (ks & 3),
-                      umma_desc_k_sw128(kb + (ks >> 2) * kPpHalf) + 2 * (ks & 3), idesc_s, ks != 0);
+          tc_mma_bf16(ds, dq + (uint64_t)(((ks >> 2) * (kPpQBytes / 2)) >> 4) + 2 * (ks & 3),
+                      dk + (uint64_t)(((ks >> 2) * kPpHalf) >> 4) + 2 * (ks & 3), idesc_s, ks != 0);
         tc_commit(&s_full[t]);
       };
       auto issue_pv = [&](int T, int t, bool first) {
-        const uint32_t vb = s_base + kPpOffV + (T & 1) * kPpKVBytes;
-#pragma unroll 1
-        for (int ks = 0; ks < kPpN / 16; ++ks)
-          tc_mma_bf16_ts(tmem + 2 * kPpN + t * kFD, tmem + t * kPpN + ks * 8,
-                         umma_desc_mn_sw128(vb + ks * 2048, kPpHalf, 1024u), idesc_o,
-                         !first || ks > 0);
+        const uint64_t dv =
+            umma_desc_mn_sw128(s_base + kPpOffV + (T & 1) * kPpKVBytes, kPpHalf, 1024u);
+        const uint32_t dO = tmem + 2 * kPpN + t * kFD, dp = tmem + t * kPpN;
+        tc_mma_bf16_ts(dO, dp, dv, idesc_o, first ? 0u : 1u);
+#pragma unroll
+        for (int ks = 1; ks < kPpN / 16; ++ks)
+          tc_mma_bf16_ts(dO, dp + ks * 8, dv + (uint64_t)((ks * 2048) >> 4), idesc_o, 1u);
       };
       bool ok = true;
       int T = 0, ic = 0;
