@@ -701,6 +701,54 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+// Packed fp32 pairs (one instruction per pair on sm_100).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// 2^x for a pair on the FMA pipe, so that part of the softmax's exponentials
+// leave the MUFU pipe (the MUFU pipe bounds the softmax of a 128-key tile).
+// Cody-Waite range reduction, 2^x = 2^j * 2^f with j = round(x) (the 1.5 *
+// 2^23 shifter) and f in [-0.5, 0.5], then a cubic for 2^f whose coefficients
+// were fitted here by iteratively reweighted least squares for the smallest
+// maximum relative error on [-0.5, 0.5] with p(0) = 1: 1.02e-4, a twentieth of
+// bf16's half-ulp (P is stored as bf16).  2^j is added to the exponent field:
+// the shifter's low mantissa bits hold j, and shifting its bits left by 23
+// leaves exactly j << 23.  x is clamped to -127, where the result is exactly
+// 0 (masked keys, x = -inf); results below 2^-126 are flushed towards zero
+// as with ex2.approx.ftz.  Inputs above 0 stay exact up to 2^127 (the lazy
+// rescale lets x reach +8).
+constexpr int kExpPolyLane = 3;  // i % 4 of the key pairs that take the polynomial
+constexpr float kExp2C1 = 0.6932828426361084f;
+constexpr float kExp2C2 = 0.24220985174179077f;
+constexpr float kExp2C3 = 0.05500836670398712f;
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = fadd2(x, make_float2(kShift, kShift));
+  const float2 r = fadd2(t, make_float2(-kShift, -kShift));  // round(x), exact
+  const float2 f = ffma2(r, make_float2(-1.f, -1.f), x);     // x - round(x), exact
+  float2 q = ffma2(f, make_float2(kExp2C3, kExp2C3), make_float2(kExp2C2, kExp2C2));
+  q = ffma2(q, f, make_float2(kExp2C1, kExp2C1));
+  q = ffma2(q, f, make_float2(1.f, 1.f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
 
 // The kernel is persistent: min(items, SMs) CTAs, where an item is one
 // (query row block, head pair, sequence).  Items run longest first (the
@@ -1000,21 +1048,27 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         }
         const float base = (m_used == -INFINITY) ? 0.f : m_used;
         const float nbase = -base;
-        float rsq[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nb2 = make_float2(nbase, nbase);
+        float2 rsq[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // sum chains
 #pragma unroll
         for (int c = 0; c < kPpN / 32; ++c) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i]), p.scale_log2, nbase));
-            const float p1 =
-                ex2_approx(fmaf(__uint_as_float(rr[c * 32 + 2 * i + 1]), p.scale_log2, nbase));
-            rsq[i & 3] += p0 + p1;
-            w[i] = pack_bf16x2(p0, p1);
+            const float2 x = ffma2(make_float2(__uint_as_float(rr[c * 32 + 2 * i]),
+                                               __uint_as_float(rr[c * 32 + 2 * i + 1])),
+                                   sc2, nb2);
+            // one key pair in four on the FMA pipe, the rest on MUFU
+            const float2 e = (i & 3) == kExpPolyLane
+                                 ? exp2_poly2(x)
+                                 : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            rsq[i & 1] = fadd2(rsq[i & 1], e);
+            w[i] = pack_bf16x2(e.x, e.y);
           }
           tmem_st_16cols(s_col + c * 16, w);  // P: 32 keys per 16 columns
         }
-        const float rs = (rsq[0] + rsq[1]) + (rsq[2] + rsq[3]);
+        const float rs = (rsq[0].x + rsq[1].x) + (rsq[0].y + rsq[1].y);
         if (__any_sync(0xffffffffu, rescale)) {
           // O[t] holds tiles 0..j-1 of this item, complete (covered by the
           // commit of S_j(t)): rescale it to the new base before PV_j adds to it
