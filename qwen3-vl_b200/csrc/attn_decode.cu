@@ -282,8 +282,10 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(DecodeParam
 // One warp per (b, h): merge the split partials.
 template <typename T>
 __global__ void attn_decode_combine(DecodeParams p) {
-  pdl_wait();
+  // dependents first: the projection that follows prefetches its weights
+  // before its own wait, which covers this kernel's outputs
   pdl_launch();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t bh = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (bh >= (int64_t)p.B * p.Hq) return;

@@ -126,8 +126,11 @@ __global__ void qkv_norm_rope_kernel(
     __nv_bfloat16* __restrict__ v_out, __nv_bfloat16* __restrict__ k_cache,
     __nv_bfloat16* __restrict__ v_cache, int B, int S, int Hq, int Hkv, int64_t start_pos,
     const int32_t* __restrict__ pos_dev, int64_t max_seq, float eps, PageRef pr) {
-  pdl_wait();
+  // dependents first: decode attention streams the cache rows of earlier
+  // steps before its own wait, and waits for this kernel before it reads q
+  // or the newest row
   pdl_launch();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int heads = Hq + 2 * Hkv;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
