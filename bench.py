@@ -178,30 +178,16 @@ def run_ours(args):
     for _ in range(args.warmup):
         dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, **gen_kw)
 
-    # launch accounting: one step run eagerly (graphs replay exactly these kernels);
-    # q3_attn_decode adds a split-K combine kernel whenever it splits
-    import q3vl.ops as ops_mod
-    counts = {"n": 0}
-    orig_call = ops_mod.call
-
-    ws_bytes = _lib.raw("q3_attn_decode_workspace_bytes")
-
-    def counting_call(name, *a):
-        n = 1
-        if name in ("q3_attn_decode", "q3_attn_decode_paged") and ws_bytes(*a[4:9]) > 0:
-            # split-K: + combine kernel
-            n = 2
-        elif name == "q3_gemm_allreduce":
-            n = 2  # the pushing GEMM + the reduce/gather kernel
-        counts["n"] += n
-        return orig_call(name, *a)
-
-    ops_mod.call = counting_call
+    # launch accounting: one step run eagerly (graphs replay exactly these
+    # kernels), counted by the library itself (q3_launch_count: every kernel
+    # launch of every entry point, the split-K merge of decode attention
+    # included when it runs as its own kernel)
+    launch_count = _lib.raw("q3_launch_count")
+    n0 = int(launch_count())
     dec.use_graphs = False
     dec.generate_tokens(prompt, NEW_TOKENS, eos_token_id=None, **gen_kw)
     dec.use_graphs = True
-    ops_mod.call = orig_call
-    launches_per_step = counts["n"]
+    launches_per_step = int(launch_count()) - n0
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream(dev)

@@ -64,6 +64,10 @@ Q3_API const char* q3_last_error(void);
 /* Reads (and with clear!=0 resets) the device error word that kernels set
  * when a bounded wait times out; 0 means no error was recorded. */
 Q3_API int q3_device_error(int clear);
+/* Kernels this library has launched in this process (every entry point
+ * counts the launches it makes, including the split-K merge of decode
+ * attention when it runs as a separate kernel); for launch accounting. */
+Q3_API uint64_t q3_launch_count(void);
 
 /* ---- a1: RMSNorm -------------------------------------------------------
  * Replaces RMSNorm.forward (model_fused.py:37-40; model.py:44-47) and the

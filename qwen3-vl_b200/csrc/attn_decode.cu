@@ -130,6 +130,10 @@ struct DecodeParams {
   const int32_t* pages;
   int64_t pages_stride;
   int page_tokens, num_pages;
+  // tensor-core kernel, splits > 1: the splits of one (sequence, KV head) run
+  // as one thread-block cluster and cluster rank 0 merges them through
+  // distributed shared memory (no workspace, no combine kernel)
+  int cluster_merge;
 };
 
 // Positions per split.  The grid's split count is planned on the host from
@@ -445,6 +449,7 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
   __shared__ __align__(16) __nv_bfloat16 q_s[FQ ? G : 1][kHD];  // FQ: normed, rotated q
   __shared__ float new_s[FQ ? 2 : 1][kHD];                       // FQ: new k and v rows
   __shared__ float snew_s[FQ ? G : 1];                           // FQ: new row's scores
+  __shared__ float cl_ml[G][2];  // cluster merge: this split's (max, sum) per head
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -686,6 +691,14 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
     if (p.splits == 1) {
       __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + ((int64_t)b * p.Hq + h) * kHD;
       out[d] = f2bf(l > 0.f ? a / l : 0.f);
+    } else if (p.cluster_merge) {
+      // only this thread reads sm_o[*][gg][d]: its warp-0 slot takes the
+      // split's sum; (max, sum) go to cl_ml, which no thread reads yet
+      sm_o[0][gg][d] = a;
+      if (d == 0) {
+        cl_ml[gg][0] = M;  // log2 units
+        cl_ml[gg][1] = l;
+      }
     } else {
       const int64_t slot = ((int64_t)b * p.Hq + h) * p.splits + split;
       p.ws_acc[slot * kHD + d] = a;
@@ -695,6 +708,36 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
         p.ws_ml[slot * 2 + 1] = l;
       }
     }
+  }
+  if (p.splits > 1 && p.cluster_merge) {
+    // every split of this (sequence, KV head) left (max, sum, O) in its own
+    // shared memory; rank 0 reads them in rank order and writes the output,
+    // and the second barrier keeps the peers resident until it has read
+    cluster_sync_all();
+    if (cluster_ctarank() == 0) {
+      const uint32_t nr = cluster_nctarank();
+      for (int idx = threadIdx.x; idx < G * kHD; idx += blockDim.x) {
+        const int gg = idx / kHD, d = idx % kHD;
+        const uint32_t a_loc = smem_u32(&sm_o[0][gg][d]);
+        const uint32_t m_loc = smem_u32(&cl_ml[gg][0]);
+        float M = -INFINITY;
+        for (uint32_t r = 0; r < nr; ++r)
+          M = fmaxf(M, ld_shared_cluster_f32(map_shared_rank(m_loc, r)));
+        float a = 0.f, l = 0.f;
+        for (uint32_t r = 0; r < nr; ++r) {
+          const uint32_t mr = map_shared_rank(m_loc, r);
+          const float mw = ld_shared_cluster_f32(mr);
+          if (mw == -INFINITY) continue;
+          const float f = exp2f(mw - M);
+          a = fmaf(f, ld_shared_cluster_f32(map_shared_rank(a_loc, r)), a);
+          l = fmaf(f, ld_shared_cluster_f32(mr + 4), l);
+        }
+        __nv_bfloat16* out =
+            reinterpret_cast<__nv_bfloat16*>(p.out) + ((int64_t)b * p.Hq + kvh * G + gg) * kHD;
+        out[d] = f2bf(l > 0.f ? a / l : 0.f);
+      }
+    }
+    cluster_sync_all();
   }
 }
 
@@ -711,6 +754,18 @@ static int decode_slots_per_sm() {
     return (x == 1 || x == 2) ? x : 0;
   }();
   return v;
+}
+
+// Whether the tensor-core kernel merges 2-8 splits inside a thread-block
+// cluster (Q3VL_DECODE_CLUSTER_MERGE=1) instead of through the workspace and
+// the combine kernel (the default).  Measured on B200, B = 8, L = 1152 in a
+// CUDA graph: 11.7 us per call with the cluster merge against 10.1 us with
+// the combine kernel, whose launch overlaps the next kernel's start; clusters
+// must be co-scheduled in one GPC, and the next launch's CTAs lose their
+// early start.  Read per call so a process can compare both.
+static bool decode_cluster_merge() {
+  const char* e = getenv("Q3VL_DECODE_CLUSTER_MERGE");
+  return e && e[0] == '1';
 }
 
 static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_qkv = false,
@@ -773,6 +828,9 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   p.splits = (int)sp;
   p.chunk = (int)ch;
   if (sp > 1) p.ws_ml = p.ws_acc + (size_t)p.B * p.Hq * sp * kHD;
+  // 2-8 splits: one cluster per (sequence, KV head), merged in shared memory
+  const bool cl = sp > 1 && sp <= 8 && decode_cluster_merge();
+  p.cluster_merge = cl ? 1 : 0;
   CUtensorMap tk, tv;
   const int64_t rows = paged ? (int64_t)p.num_pages * p.Hkv * p.page_tokens
                              : (int64_t)p.B * p.Hkv * p.max_seq;
@@ -781,9 +839,10 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   rc = cached_tmap_2d(&tv, p.v, rows, kHD, kTcTile, 64);
   if (rc) return rc;
   DecodeTcParams prm{p, device_error_word()};
-  rc = launch_ex(kern, dim3(p.splits, p.Hkv, p.B), dim3(kTcThreads), kTcSmem, s, 1, tk, tv, prm);
+  rc = launch_ex_cluster(kern, dim3(p.splits, p.Hkv, p.B), dim3(kTcThreads), kTcSmem, s,
+                         dim3(cl ? p.splits : 1, 1, 1), tk, tv, prm);
   if (rc) return rc;
-  if (p.splits > 1) {
+  if (p.splits > 1 && !cl) {
     const int warps = 4;
     const int64_t n = (int64_t)p.B * p.Hq;
     rc = launch_ex(attn_decode_combine<__nv_bfloat16>, dim3((unsigned)((n + warps - 1) / warps)),

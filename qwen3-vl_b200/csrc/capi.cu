@@ -1,6 +1,7 @@
 // Library-level C ABI: version, error strings, device error word.
 #include <stdarg.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -56,6 +57,9 @@ int* device_error_word() {
   return words[dev];
 }
 
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = getenv("Q3VL_PDL");
@@ -67,6 +71,10 @@ bool pdl_enabled() {
 }  // namespace q3
 
 extern "C" int q3_version(void) { return 100; }
+
+extern "C" uint64_t q3_launch_count(void) {
+  return q3::g_launches.load(std::memory_order_relaxed);
+}
 
 extern "C" const char* q3_last_error(void) { return q3::g_last_error; }
 

@@ -84,10 +84,13 @@ int cached_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 // kernel waits before it completes, completion is transitive along the
 // stream), and pdl_launch() to let the next kernel start its prologue.
 bool pdl_enabled();
+// Adds one to the count q3_launch_count reports (after each kernel launch).
+void count_launch();
 
+// Launch with a thread-block cluster of shape `cluster` (1 x 1 x 1: none).
 template <typename... KArgs, typename... Args>
-int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-              int cluster_y, Args&&... args) {
+int launch_ex_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t s, dim3 cluster, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -95,11 +98,11 @@ int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
-  if (cluster_y > 1) {
+  if (cluster.x * cluster.y * cluster.z > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = 1;
-    attr[n].val.clusterDim.y = cluster_y;
-    attr[n].val.clusterDim.z = 1;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
     ++n;
   }
   if (pdl_enabled()) {
@@ -112,7 +115,15 @@ int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
   if (e != cudaSuccess)
     return fail(Q3_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  count_launch();
   return Q3_OK;
+}
+// ... with `cluster_y` CTAs per cluster along y (1: no cluster).
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+              int cluster_y, Args&&... args) {
+  return launch_ex_cluster(kernel, grid, block, smem, s, dim3(1, cluster_y > 1 ? cluster_y : 1, 1),
+                           static_cast<Args&&>(args)...);
 }
 
 // Decode-shaped (M <= 16) projection, defined in gemv.cu.  Options: a fused

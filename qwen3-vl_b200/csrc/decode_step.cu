@@ -1043,6 +1043,7 @@ static int launch(const Plan& pl, const Params& prm, cudaStream_t s) {
   cfg.attrs = at;
   cfg.numAttrs = 1;
   Q3_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, prm));
+  count_launch();
   return Q3_OK;
 }
 

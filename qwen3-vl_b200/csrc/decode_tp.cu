@@ -1468,6 +1468,7 @@ extern "C" int q3_decode_tp(void* plan, void* x, const int32_t* kv_len_dev, int6
   void (*kern)(Params) = pl->G == 1 ? decode_tp_kernel<1> : pl->G == 2 ? decode_tp_kernel<2>
                          : pl->G == 4 ? decode_tp_kernel<4> : decode_tp_kernel<8>;
   Q3_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, p));
+  count_launch();
   return Q3_OK;
 }
 

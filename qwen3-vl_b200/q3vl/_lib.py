@@ -45,6 +45,7 @@ SZ = ctypes.c_size_t
 SIGNATURES: dict[str, tuple] = {
     "q3_version": (I32, []),
     "q3_last_error": (ctypes.c_char_p, []),
+    "q3_launch_count": (ctypes.c_uint64, []),
     "q3_device_error": (I32, [I32]),
     "q3_rmsnorm": (I32, [P, P, P, P, P, I64, I64, F32, P]),
     "q3_rope": (I32, [P, P, P, I64, I32, I32, P]),
