@@ -268,6 +268,21 @@ Q3_API int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const void*
                               int64_t kv_len, const int32_t* kv_len_dev, int64_t max_seq,
                               float scale, float eps, void* workspace, size_t workspace_bytes,
                               q3_stream_t stream);
+/* q3_attn_decode_qkv over a page pool, as q3_attn_decode_paged reads one:
+ * k_pages / v_pages bf16 [num_pages, Hkv, page_tokens, 128], block_table int32
+ * [B, table_stride] on the device.  The new token's k and v rows go to page
+ * block_table[b, (kv_len-1) / page_tokens] (the caller has grown the table to
+ * hold it; a table entry outside [0, num_pages) skips the write and sets the
+ * device error word to 0x402).  Replaces q3_qkv_norm_rope_paged followed by
+ * q3_attn_decode_paged at decode time (model_fused.py:244-262). */
+Q3_API int q3_attn_decode_qkv_paged(const void* qkv, const void* q_norm_w, const void* k_norm_w,
+                                    const void* cos, const void* sin, int64_t cs_offset,
+                                    void* k_pages, void* v_pages, void* out, int B, int Hq,
+                                    int Hkv, int head_dim, int64_t kv_len,
+                                    const int32_t* kv_len_dev, const int32_t* block_table,
+                                    int64_t table_stride, int page_tokens, int num_pages,
+                                    float scale, float eps, void* workspace,
+                                    size_t workspace_bytes, q3_stream_t stream);
 
 /* Same computation as q3_attn_decode, for callers that cannot allocate device
  * memory at call time (a runtime whose free HBM is already committed to its

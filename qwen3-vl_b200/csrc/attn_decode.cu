@@ -636,20 +636,31 @@ __global__ void __launch_bounds__(kTcThreads) attn_decode_tc_kernel(
       const int ld = (p.Hq + 2 * p.Hkv) * kHD;
       const int64_t pos = L - 1;
       const int64_t crow = pos + p.cs_offset;
-      const int64_t crow_off = (((int64_t)b * p.Hkv + kvh) * p.max_seq + pos) * kHD;
+      int64_t crow_off;
+      bool row_ok = true;
+      if constexpr (PAGED) {
+        // the new row's page (the caller grew the table to hold it)
+        const int pg = p.pages[(int64_t)b * p.pages_stride + pos / p.page_tokens];
+        row_ok = pg >= 0 && pg < p.num_pages;
+        if (!row_ok && threadIdx.x == 0) report_timeout(prm.err, 0x402);
+        crow_off = ((row_ok ? (int64_t)pg * p.Hkv + kvh : 0) * p.page_tokens +
+                    pos % p.page_tokens) * kHD;
+      } else {
+        crow_off = (((int64_t)b * p.Hkv + kvh) * p.max_seq + pos) * kHD;
+      }
       if (warp == 0) {
         float o4[4];
         head_norm_rope(p.qkv + (int64_t)b * ld + (p.Hq + kvh) * kHD,
                        head_tabs(p.k_norm, p.cos, p.sin, crow, lane), p.eps, lane, o4);
         const uint2 pk = make_uint2(pack_bf16x2(o4[0], o4[1]), pack_bf16x2(o4[2], o4[3]));
-        *reinterpret_cast<uint2*>(p.k_cache_w + crow_off + lane * 4) = pk;
+        if (row_ok) *reinterpret_cast<uint2*>(p.k_cache_w + crow_off + lane * 4) = pk;
         const float2 a0 = unpack_bf16x2(pk.x), a1 = unpack_bf16x2(pk.y);
         new_s[0][lane * 4 + 0] = a0.x; new_s[0][lane * 4 + 1] = a0.y;
         new_s[0][lane * 4 + 2] = a1.x; new_s[0][lane * 4 + 3] = a1.y;
       } else if (warp == 1) {
         const uint2 pv = *reinterpret_cast<const uint2*>(
             p.qkv + (int64_t)b * ld + (p.Hq + p.Hkv + kvh) * kHD + lane * 4);
-        *reinterpret_cast<uint2*>(p.v_cache_w + crow_off + lane * 4) = pv;
+        if (row_ok) *reinterpret_cast<uint2*>(p.v_cache_w + crow_off + lane * 4) = pv;
         const float2 a0 = unpack_bf16x2(pv.x), a1 = unpack_bf16x2(pv.y);
         new_s[1][lane * 4 + 0] = a0.x; new_s[1][lane * 4 + 1] = a0.y;
         new_s[1][lane * 4 + 2] = a1.x; new_s[1][lane * 4 + 3] = a1.y;
@@ -774,12 +785,13 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
   int gi = 0;
   if (paged) {
     switch (G) {
-      case 1: kern = attn_decode_tc_kernel<1, false, true>; gi = 8; break;
-      case 2: kern = attn_decode_tc_kernel<2, false, true>; gi = 9; break;
-      case 4: kern = attn_decode_tc_kernel<4, false, true>; gi = 10; break;
-      case 8: kern = attn_decode_tc_kernel<8, false, true>; gi = 11; break;
+      case 1: kern = fused_qkv ? attn_decode_tc_kernel<1, true, true> : attn_decode_tc_kernel<1, false, true>; gi = 8; break;
+      case 2: kern = fused_qkv ? attn_decode_tc_kernel<2, true, true> : attn_decode_tc_kernel<2, false, true>; gi = 9; break;
+      case 4: kern = fused_qkv ? attn_decode_tc_kernel<4, true, true> : attn_decode_tc_kernel<4, false, true>; gi = 10; break;
+      case 8: kern = fused_qkv ? attn_decode_tc_kernel<8, true, true> : attn_decode_tc_kernel<8, false, true>; gi = 11; break;
       default: return fail(Q3_ERR_UNSUPPORTED, "q3_attn_decode: Hq/Hkv=%d not in {1,2,4,8}", G);
     }
+    if (fused_qkv) gi += 4;
   } else {
     switch (G) {
       case 1: kern = fused_qkv ? attn_decode_tc_kernel<1, true> : attn_decode_tc_kernel<1, false>; gi = 0; break;
@@ -790,7 +802,7 @@ static int launch_decode_tc(DecodeParams& p, int G, cudaStream_t s, bool fused_q
     }
     if (fused_qkv) gi += 4;
   }
-  static int per_sm_cache[64][12] = {{0}};
+  static int per_sm_cache[64][16] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
   const bool cacheable = dev >= 0 && dev < 64;
@@ -962,6 +974,66 @@ extern "C" int q3_attn_decode_qkv(const void* qkv, const void* q_norm_w, const v
     p.ws_ml = p.ws_acc + (size_t)B * Hq * p.splits * kHD;
   }
   return launch_decode_tc(p, Hq / Hkv, (cudaStream_t)stream, true);
+}
+
+// The fused variant over a page pool: the new token's K/V row goes to its page
+// (block_table[b, (kv_len - 1) / page_tokens]), the older rows are read
+// through the table.
+extern "C" int q3_attn_decode_qkv_paged(const void* qkv, const void* q_norm_w,
+                                        const void* k_norm_w, const void* cos, const void* sin,
+                                        int64_t cs_offset, void* k_pages, void* v_pages, void* out,
+                                        int B, int Hq, int Hkv, int head_dim, int64_t kv_len,
+                                        const int32_t* kv_len_dev, const int32_t* block_table,
+                                        int64_t table_stride, int page_tokens, int num_pages,
+                                        float scale, float eps, void* workspace,
+                                        size_t workspace_bytes, q3_stream_t stream) {
+  using namespace q3;
+  Q3_REQUIRE(qkv && q_norm_w && k_norm_w && cos && sin && k_pages && v_pages && out && block_table,
+             "q3_attn_decode_qkv_paged: null pointer");
+  Q3_REQUIRE(head_dim == kHD, "q3_attn_decode_qkv_paged: head_dim must be 128 (got %d)",
+             head_dim);
+  Q3_REQUIRE(B > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+             "q3_attn_decode_qkv_paged: bad heads Hq=%d Hkv=%d", Hq, Hkv);
+  Q3_REQUIRE(page_tokens > 0 && page_tokens % kTcTile == 0 && num_pages > 0,
+             "q3_attn_decode_qkv_paged: page_tokens=%d must be a positive multiple of %d",
+             page_tokens, kTcTile);
+  Q3_REQUIRE((int64_t)num_pages * Hkv * page_tokens < (1ll << 31),
+             "q3_attn_decode_qkv_paged: pool of %d pages too large for 32-bit rows", num_pages);
+  Q3_REQUIRE(table_stride > 0 && kv_len >= 1 && kv_len <= table_stride * page_tokens,
+             "q3_attn_decode_qkv_paged: kv_len=%lld beyond the table width (%lld pages of %d)",
+             (long long)kv_len, (long long)table_stride, page_tokens);
+  Q3_REQUIRE(aligned(qkv, 8) && aligned(q_norm_w, 8) && aligned(k_norm_w, 8) && aligned(cos, 8) &&
+                 aligned(sin, 8) && aligned(k_pages, 16) && aligned(v_pages, 16) &&
+                 aligned(out, 8) && aligned(block_table, 4),
+             "q3_attn_decode_qkv_paged: misaligned pointer");
+  DecodeParams p{};
+  p.q = nullptr; p.k = k_pages; p.v = v_pages; p.out = out;
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv;
+  p.kv_len = kv_len; p.kv_len_dev = kv_len_dev; p.max_seq = table_stride * page_tokens;
+  p.scale = scale;
+  p.qkv = (const __nv_bfloat16*)qkv;
+  p.q_norm = (const __nv_bfloat16*)q_norm_w;
+  p.k_norm = (const __nv_bfloat16*)k_norm_w;
+  p.cos = (const __nv_bfloat16*)cos;
+  p.sin = (const __nv_bfloat16*)sin;
+  p.cs_offset = cs_offset;
+  p.eps = eps;
+  p.k_cache_w = (__nv_bfloat16*)k_pages;
+  p.v_cache_w = (__nv_bfloat16*)v_pages;
+  p.pages = block_table;
+  p.pages_stride = table_stride;
+  p.page_tokens = page_tokens;
+  p.num_pages = num_pages;
+  decode_split_plan(B, Hkv, kv_len, &p.splits, &p.chunk);
+  if (p.splits > 1) {
+    const size_t need = (size_t)B * Hq * p.splits * (kHD + 2) * sizeof(float);
+    Q3_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+               "q3_attn_decode_qkv_paged: workspace of %zu bytes needed (got %zu)", need,
+               workspace_bytes);
+    p.ws_acc = reinterpret_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + (size_t)B * Hq * p.splits * kHD;
+  }
+  return launch_decode_tc(p, Hq / Hkv, (cudaStream_t)stream, true, true);
 }
 
 // ---------------------------------------------------------------------------

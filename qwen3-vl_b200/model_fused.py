@@ -424,8 +424,7 @@ class Qwen3VLDecoderFused:
             cos, sin = rope
             cs_use_pos, cs_stride_b, cs_offset = False, S, 0
         fused_attn = (S == 1 and rope is None and qkv is not None and self.fuse_attn_qkv and
-                      cos.dtype == torch.bfloat16 and not paged and
-                      not isinstance(rope_delta, RowRope))
+                      cos.dtype == torch.bfloat16 and not isinstance(rope_delta, RowRope))
         if paged and fused_qkv:
             q = ops.gemm_qkv_rope_paged(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
                                         ab.k_norm_weight, cos, sin, B=B, S=S,
@@ -434,6 +433,8 @@ class Qwen3VLDecoderFused:
                                         start_pos=start_pos, cs_use_pos=cs_use_pos,
                                         cs_offset=cs_offset, cs_stride_b=cs_stride_b,
                                         eps=ab.eps)
+        elif fused_attn:
+            q = None  # computed inside the attention kernel from qkv
         elif paged:
             # K/V rows go straight into their pages (no dense copy)
             q = ops.qkv_norm_rope_paged(qkv, ab.q_norm_weight, ab.k_norm_weight, cos, sin, B=B,
@@ -442,8 +443,6 @@ class Qwen3VLDecoderFused:
                                         start_pos=start_pos, pos_dev=pos_dev,
                                         cs_use_pos=cs_use_pos, cs_offset=cs_offset,
                                         cs_stride_b=cs_stride_b, eps=ab.eps)
-        elif fused_attn:
-            q = None  # computed inside the attention kernel from qkv
         elif fused_qkv:
             q = ops.gemm_qkv_rope(h.view(T, H), ab.qkv_weight_km, ab.q_norm_weight,
                                   ab.k_norm_weight, cos, sin, B=B, S=S, Hq=ab.num_q_heads,
@@ -463,7 +462,14 @@ class Qwen3VLDecoderFused:
                 ops.l2_prefetch(L.o_proj.weight_km)
             if self.l2_prefetch_qkv and layer_idx + 1 < self.num_layers:
                 ops.l2_prefetch(self.layers[layer_idx + 1].attn_block.qkv_weight_km)
-            if paged:
+            if paged and fused_attn:
+                attn = ops.attn_decode_qkv_paged(qkv, ab.q_norm_weight, ab.k_norm_weight, cos,
+                                                 sin, kc, vc, kv_cache[layer_idx].table,
+                                                 Hq=ab.num_q_heads, Hkv=ab.num_kv_heads,
+                                                 kv_len=bound, kv_len_dev=kv_len_dev,
+                                                 cs_offset=cs_offset, scale=self.scale,
+                                                 eps=ab.eps)
+            elif paged:
                 attn = ops.attn_decode_paged(q.view(B, ab.num_q_heads, self.head_dim), kc, vc,
                                              kv_cache[layer_idx].table, kv_len=bound,
                                              kv_len_dev=kv_len_dev, scale=self.scale)

@@ -81,6 +81,8 @@ SIGNATURES: dict[str, tuple] = {
     "q3_attn_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I64, P, I64, F32, I32, P, SZ, P]),
     "q3_attn_decode_qkv": (I32, [P, P, P, P, P, I64, P, P, P, I32, I32, I32, I32, I64, P, I64,
                                  F32, F32, P, SZ, P]),
+    "q3_attn_decode_qkv_paged": (I32, [P, P, P, P, P, I64, P, P, P, I32, I32, I32, I32, I64, P,
+                                       P, I64, I32, I32, F32, F32, P, SZ, P]),
     "q3_attn_decode_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I64, P, I64, F32, I32, P]),
     "q3_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I64, I32, F32, P, P, P, P]),
     "q3_gemm": (I32, [P, P, P, I64, I64, I64, I32, P, P]),

@@ -418,6 +418,38 @@ def attn_decode_qkv(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin, k_cache: to
     return o
 
 
+def attn_decode_qkv_paged(qkv: torch.Tensor, q_norm_w, k_norm_w, cos, sin,
+                          k_pages: torch.Tensor, v_pages: torch.Tensor,
+                          block_table: torch.Tensor, *, Hq: int, Hkv: int, kv_len: int,
+                          kv_len_dev: torch.Tensor = None, cs_offset: int = 0,
+                          scale: float = None, eps: float = 1e-6,
+                          out: torch.Tensor = None) -> torch.Tensor:
+    """attn_decode_qkv over a page pool (q3_attn_decode_qkv_paged): k_pages /
+    v_pages bf16 [num_pages, Hkv, page_tokens, 128]; block_table int32 [B, width]
+    on the device, already holding the page of position kv_len - 1."""
+    _cuda("attn_decode_qkv_paged", qkv, q_norm_w, k_norm_w, cos, sin, k_pages, v_pages,
+          block_table, kv_len_dev)
+    _bf16("attn_decode_qkv_paged", qkv, q_norm_w, k_norm_w, cos, sin, k_pages, v_pages)
+    _contig("attn_decode_qkv_paged", qkv, cos, sin, k_pages, v_pages, block_table)
+    if block_table.dtype != torch.int32:
+        raise TypeError("attn_decode_qkv_paged: block_table must be int32")
+    B = qkv.shape[0]
+    if qkv.numel() != B * (Hq + 2 * Hkv) * HEAD_DIM:
+        raise ValueError("attn_decode_qkv_paged: qkv must be [B, (Hq+2Hkv)*128]")
+    if kv_len_dev is not None and kv_len_dev.dtype != torch.int32:
+        raise TypeError("attn_decode_qkv_paged: kv_len_dev must be int32")
+    num_pages, _, page_tokens, _ = k_pages.shape
+    scale = 1.0 / math.sqrt(HEAD_DIM) if scale is None else scale
+    o = torch.empty(B, Hq, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device) if out is None \
+        else out
+    ws = decode_workspace(B, Hq, Hkv, qkv.device)
+    call("q3_attn_decode_qkv_paged", _p(qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin),
+         int(cs_offset), _p(k_pages), _p(v_pages), _p(o), B, Hq, Hkv, HEAD_DIM, int(kv_len),
+         _p(kv_len_dev), _p(block_table), block_table.stride(0), page_tokens, num_pages,
+         float(scale), float(eps), _p(ws), 0 if ws is None else ws.numel(), _stream())
+    return o
+
+
 # ----------------------------------------------------------------------------
 # a6/a7: prefill attention
 # ----------------------------------------------------------------------------

@@ -214,6 +214,43 @@ def test_decode_attention_from_qkv_matches_norm_rope_then_attention(B, Hq, Hkv, 
             min_cos=0.9999)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,L,page,offset", [(8, 32, 8, 1152, 256, 0),
+                                                     (4, 32, 8, 257, 128, 2),
+                                                     (3, 8, 1, 64, 64, 0),
+                                                     (2, 16, 4, 2048, 512, 1)])
+def test_paged_decode_attention_from_qkv_matches_norm_rope_then_attention(B, Hq, Hkv, L, page,
+                                                                           offset):
+    """q3_attn_decode_qkv_paged == q3_qkv_norm_rope_paged (new row into its
+    page) followed by q3_attn_decode_paged, over pages dealt in a shuffled
+    order: both pools bit-identical after the call (the new rows land in the
+    same page slots), the outputs within the tolerance of the contiguous case."""
+    D, S = 128, 2048
+    per = S // page
+    qkv = rnd(B, (Hq + 2 * Hkv) * D, seed=90)
+    qn = (1 + rnd(D, seed=91, std=0.1)).to(BF16)
+    kn = (1 + rnd(D, seed=92, std=0.1)).to(BF16)
+    cos, sin = oref.rotary_tables(D, S + 16, 5e6)
+    kp = rnd(B * per + 3, Hkv, page, D, seed=93)
+    vp = rnd(B * per + 3, Hkv, page, D, seed=94)
+    perm = torch.randperm(B * per + 3, generator=torch.Generator().manual_seed(5))[:B * per]
+    table = perm.view(B, per).to(torch.int32).to(DEV)
+    kp1, vp1, kp2, vp2 = kp.to(DEV), vp.to(DEV), kp.to(DEV), vp.to(DEV)
+    qkvd, qnd, knd, cd, sd = qkv.to(DEV), qn.to(DEV), kn.to(DEV), cos.to(DEV), sin.to(DEV)
+    pos = L - 1
+    Ld = torch.tensor([L], dtype=torch.int32, device=DEV)
+    Pd = torch.tensor([pos], dtype=torch.int32, device=DEV)
+    got = ops.attn_decode_qkv_paged(qkvd, qnd, knd, cd, sd, kp1, vp1, table, Hq=Hq, Hkv=Hkv,
+                                    kv_len=S, kv_len_dev=Ld, cs_offset=offset)
+    q = ops.qkv_norm_rope_paged(qkvd, qnd, knd, cd, sd, B=B, S=1, Hq=Hq, Hkv=Hkv, k_pages=kp2,
+                                v_pages=vp2, block_table=table, start_pos=0, pos_dev=Pd,
+                                cs_offset=offset)
+    want = ops.attn_decode_paged(q.view(B, Hq, D), kp2, vp2, table, kv_len=S, kv_len_dev=Ld)
+    torch.cuda.synchronize()
+    assert torch.equal(kp1.cpu(), kp2.cpu()) and torch.equal(vp1.cpu(), vp2.cpu())
+    compare(f"paged attn from qkv B={B} L={L}", got.cpu(), want.cpu(), max_abs=2e-2,
+            rel_scale=True, min_cos=0.9999)
+
+
 # --------------------------------------------------------------------------- a6/a7 prefill
 def test_prefill_kat_vs_reference_attention_ref():
     """kernels/prefill_attention.py layouts (q [Hq,D,S], k [Hkv,D,S], v [Hkv,S,D])."""
