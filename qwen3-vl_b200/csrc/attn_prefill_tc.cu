@@ -723,19 +723,25 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 // 2^x for a pair on the FMA pipe, so that part of the softmax's exponentials
 // leave the MUFU pipe (the MUFU pipe bounds the softmax of a 128-key tile).
 // Cody-Waite range reduction, 2^x = 2^j * 2^f with j = round(x) (the 1.5 *
-// 2^23 shifter) and f in [-0.5, 0.5], then a cubic for 2^f whose coefficients
-// were fitted here by iteratively reweighted least squares for the smallest
-// maximum relative error on [-0.5, 0.5] with p(0) = 1: 1.02e-4, a twentieth of
-// bf16's half-ulp (P is stored as bf16).  2^j is added to the exponent field:
+// 2^23 shifter) and f in [-0.5, 0.5], then a degree-5 polynomial for 2^f whose
+// coefficients were fitted here by iteratively reweighted least squares for
+// the smallest maximum relative error on [-0.5, 0.5] with p(0) = 1: 1.9e-7
+// through the fp32 evaluation, the size of ex2.approx's own error, so the bf16
+// P of nearly every key (all but about 2 in 10^6) rounds as it does from the
+// exact exponential.  (A cubic, 1.0e-4, changed the bf16 rounding of 5 % of
+// its keys, enough to flip near-tie greedy tokens downstream.)  2^j is added
+// to the exponent field:
 // the shifter's low mantissa bits hold j, and shifting its bits left by 23
 // leaves exactly j << 23.  x is clamped to -127, where the result is exactly
 // 0 (masked keys, x = -inf); results below 2^-126 are flushed towards zero
 // as with ex2.approx.ftz.  Inputs above 0 stay exact up to 2^127 (the lazy
 // rescale lets x reach +8).
 constexpr int kExpPolyLane = 3;  // i % 4 of the key pairs that take the polynomial
-constexpr float kExp2C1 = 0.6932828426361084f;
-constexpr float kExp2C2 = 0.24220985174179077f;
-constexpr float kExp2C3 = 0.05500836670398712f;
+constexpr float kExp2C1 = 0.6931470036506653f;
+constexpr float kExp2C2 = 0.24022242426872253f;
+constexpr float kExp2C3 = 0.05550733581185341f;
+constexpr float kExp2C4 = 0.00967150554060936f;
+constexpr float kExp2C5 = 0.0013264697045087814f;
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   x.x = fmaxf(x.x, -127.f);
@@ -743,7 +749,9 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   const float2 t = fadd2(x, make_float2(kShift, kShift));
   const float2 r = fadd2(t, make_float2(-kShift, -kShift));  // round(x), exact
   const float2 f = ffma2(r, make_float2(-1.f, -1.f), x);     // x - round(x), exact
-  float2 q = ffma2(f, make_float2(kExp2C3, kExp2C3), make_float2(kExp2C2, kExp2C2));
+  float2 q = ffma2(f, make_float2(kExp2C5, kExp2C5), make_float2(kExp2C4, kExp2C4));
+  q = ffma2(q, f, make_float2(kExp2C3, kExp2C3));
+  q = ffma2(q, f, make_float2(kExp2C2, kExp2C2));
   q = ffma2(q, f, make_float2(kExp2C1, kExp2C1));
   q = ffma2(q, f, make_float2(1.f, 1.f));
   return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
